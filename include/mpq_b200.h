@@ -1,0 +1,149 @@
+/*
+ * mpq_b200.h — C ABI of libmpq_b200.so, the sm_100a kernels of MPQ's per-layer quantization solve.
+ *
+ * Conventions (all entry points):
+ *   - plain device pointers and sizes; row-major float32 matrices with an explicit leading
+ *     dimension (elements); `stream` is a cudaStream_t (NULL = legacy default stream);
+ *   - work is enqueued on `stream` and the call returns without synchronizing;
+ *   - return 0 on success, 10001 for an invalid argument, or a cudaError_t from the launch;
+ *     mpq_last_error() gives a message for the calling thread's last failure;
+ *   - grouped quantizer parameters (scale, zero) are addressed p[row * ld_p + (col >> gshift)]:
+ *     gshift = 0 for group-expanded (B x n) tensors, log2(group) for per-group (B x n/group).
+ *
+ * The reference (poseidonchan/MPQ) is a Python package; the functions below replace the device
+ * work behind its Python plugin points.  Each declaration names the reference code it replaces
+ * (path:line within the reference project).
+ */
+#ifndef MPQ_B200_H
+#define MPQ_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- library ---- */
+const char* mpq_last_error(void);
+int mpq_abi_version(void);
+
+/* ---- grouped-scalar prior (K1) ----
+ * Exact discrete posterior over the maxq+1 grid atoms with a Gaussian prior centred on W:
+ * outputs the posterior mean (and optionally var, MAP value, MAP index), plus the per-row
+ * variance sum (alpha1 = gamma * var_rowsum / n).  prior_tau <= 0 disables the prior.
+ * Replaces mpq/priors/uniform.py:99-213 (discrete_uniform_mmse) and
+ * mpq/priors/triton_vamp.py:24-102,446-517 (_uniform_mmse_kernel / uniform_mmse_triton). */
+int mpq_uniform_mmse(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* scale,
+                     const float* zero, int64_t ld_p, int gshift, const float* gamma, int B, int n, int maxq,
+                     float prior_tau, float* mean_out, int64_t ld_out, float* var_out, float* map_value_out,
+                     uint8_t* map_idx_out, float* var_rowsum, void* stream);
+
+/* MAP hard decision: argmax atom re-rounded through nearest_atom_idx, codes (u8) and dequantized values.
+ * Replaces mpq/solver.py:513-541 (_current_hard_state) + :833-850 (_uniform_hard_decision, 'map'). */
+int mpq_uniform_map_decision(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* scale,
+                             const float* zero, int64_t ld_p, int gshift, const float* gamma, int B, int n, int maxq,
+                             float prior_tau, uint8_t* q_out, float* x_out, int64_t ld_out, void* stream);
+
+/* q = clamp(rint(x / max(s,1e-12) + z), 0, maxq); x_out = s (q - z).
+ * Replaces mpq/priors/uniform.py:287-309 (nearest_atom_idx, dequant_from_q). */
+int mpq_uniform_nearest(const float* x, int64_t ld_x, const float* scale, const float* zero, int64_t ld_p, int gshift,
+                        int B, int n, int maxq, uint8_t* q_out, float* x_out, int64_t ld_out, void* stream);
+
+/* Per-(row, group) asymmetric min-max grid (scale, zero); the restated GPTQ quantizer called at
+ * mpq/adapters/gptqmodel.py:899-909 (GPTQModel Quantizer.find_params, not vendored). */
+int mpq_group_minmax(const float* W, int64_t ldw, int rows, int cols, int group, int maxq, float* scale, float* zero,
+                     int64_t ldp, void* stream);
+
+/* RTN init q = clamp(rint(W / s) + z, 0, maxq); x = s (q - z).  Replaces mpq/adapters/gptqmodel.py:928-931,968-969. */
+int mpq_uniform_rtn(const float* W, int64_t ldw, const float* scale, const float* zero, int64_t ld_p, int gshift,
+                    int B, int n, int maxq, uint8_t* q_out, float* x_out, int64_t ld_out, void* stream);
+
+/* ---- VAMP message algebra (mpq/solver.py:553-699, mpq/linear.py:10-94) ---- */
+
+/* Per-row scalar stage of one iteration: alpha1 from the variance sums, gamma2 (damped), the
+ * gamma-only terms of linear_mmse_exact (alpha2, eta2, gamma1_new, damped gamma1) and the EM
+ * trace term.  flags[0..4] count invalid alpha1 / non-finite alpha1 / invalid gamma2_new /
+ * invalid gamma2 / clipped alpha2 rows.  final_retry != 0 clips alpha1 instead of failing.
+ * Replaces mpq/solver.py:559-653 (scalar parts), mpq/linear.py:44-54,74-75. */
+int mpq_vamp_rows(const float* var_rowsum, float* gamma1, float* gamma1_work, float* alpha1, float* eta1,
+                  float* gamma2_new, float* gamma2, const float* gamma2_prev, float* alpha2, float* eta2,
+                  float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int B, int n,
+                  int R, float obs, float damping, int final_retry, void* stream);
+
+/* gamma retry of rows with alpha1 outside (1e-7, 1-1e-7).  Replaces mpq/solver.py:593-596. */
+int mpq_gamma_retry(float* gamma1_work, const float* var_rowsum, int B, int n, float factor, void* stream);
+
+/* r2 = damp(r2_prev, (eta1 x1 - gamma1w r1) / gamma2_new); r2_prev NULL = undamped.  mpq/solver.py:605-612. */
+int mpq_vamp_r2(const float* x1, const float* r1, const float* r2_prev, float* r2, const float* eta1,
+                const float* gamma1_work, const float* gamma2_new, int B, int n, int64_t ld, float damping,
+                void* stream);
+
+/* Linear-module epilogue over P = r2 V: u = (Y_u - P s) obs s / denom and rowsum(residual_after^2).
+ * Replaces mpq/linear.py:46-55 and the residual term of mpq/linear.py:76. */
+int mpq_linear_epilogue(const float* P, const float* Y_u, const float* S, const float* gamma2, float obs, int B, int R,
+                        int64_t ld, float* u, float* resid_rowsum, void* stream);
+
+/* r1 = damp(r1, (eta2 (r2 + D) - gamma2 r2) / gamma1_new) with D = u V^T.  mpq/linear.py:51-52, mpq/solver.py:645-653. */
+int mpq_vamp_r1(const float* D, const float* r2, float* r1, const float* eta2, const float* gamma2,
+                const float* gamma1_new, int B, int n, int64_t ld, float damping, void* stream);
+
+/* out[b] = sum_r (Y[b,r] - C[b,r])^2.  Replaces mpq/linear.py:85-94 (vamp_rankspace_error) after C = x Vs. */
+int mpq_row_sqerr(const float* Y, const float* C, int B, int R, int64_t ldy, int64_t ldc, float* out, void* stream);
+
+/* C <- Y - C and rowsum(C^2).  Replaces mpq/polish/triton_scalar_cd.py:195-197 (residual_u, residual_norm). */
+int mpq_residual(const float* Y, float* C, int B, int R, int64_t ld, float* rowsum, void* stream);
+
+/* out = mean_b (a[b] + c[b]) (c may be NULL), fixed-order reduction.  mpq/linear.py:77, mpq/solver.py:679. */
+int mpq_mean_rows(const float* a, const float* c, int B, float* out, void* stream);
+
+/* Row-wise polish merge where err_after + 1e-12 < err_before.  Replaces mpq/solver.py:749-754. */
+int mpq_polish_merge(const float* err_after, float* err_final, const float* err_before, const float* x_src,
+                     float* x_dst, const uint8_t* q_src, uint8_t* q_dst, int B, int n, int64_t ld,
+                     int* improved_count, void* stream);
+
+/* gamma1 = gamma_start * 0.25 / max(mean_j (W - x)^2, 1e-12).  Replaces mpq/solver.py:86-87,481. */
+int mpq_gamma_init(const float* W, const float* x, int B, int n, int64_t ld, float gamma_start, float* gamma1,
+                   void* stream);
+
+/* out[b] = sum_j A[b,j] C[b,j].  The raw-Hessian audit of mpq/adapters/gptqmodel.py:1048-1056. */
+int mpq_row_dot(const float* A, int64_t lda, const float* C, int64_t ldc, int B, int n, float* out, void* stream);
+
+/* D = A - C (same leading dimension).  mpq/adapters/gptqmodel.py:932, :1049. */
+int mpq_sub(const float* A, const float* C, float* D, int B, int n, int64_t ld, void* stream);
+
+/* ---- dense products (K7/K8, scalar-CD block updates) ----
+ * C = alpha A op(B) + beta C with A: M x K row-major; layout 0: B is N x K ("NT"), layout 1: B is K x N ("NN").
+ * Replaces the torch matmuls of mpq/linear.py:48,51,94, mpq/solver.py:485 and
+ * mpq/polish/triton_scalar_cd.py:195-196,286-288. */
+int mpq_gemm_f32(int layout, int M, int N, int K, float alpha, const float* A, int64_t lda, const float* B,
+                 int64_t ldb, float beta, float* C, int64_t ldc, void* stream);
+
+/* ---- scalar greedy CD (K2): mpq/polish/triton_scalar_cd.py:164-307 ---- */
+/* diag = max(rowsum(Vs^2), 1e-12), diag_inv = 1/diag.  :198-199 */
+int mpq_cd_diag(const float* Vs, int n, int R, int64_t ld, float* diag, float* diag_inv, void* stream);
+/* gain[j] = sum_b rhs[b,j]^2 diag_inv[j] / B.  :242 */
+int mpq_cd_gain(const float* rhs, int B, int n, int64_t ld, const float* diag_inv, float* gain, void* stream);
+/* order = argsort(key, descending), ties by ascending index; n <= 16384.  :243 */
+int mpq_argsort_desc(const float* key, int n, int* order, void* stream);
+/* HJ[k,:] = H[order[c0+k],:], Hsub[k,l] = H[order[c0+k], order[c0+l]] (Hsub is 128 x 128). */
+int mpq_cd_gather(const float* H, int64_t ldh, int n, const int* order, int c0, int K, float* HJ, float* Hsub,
+                  void* stream);
+/* Sequential greedy decisions of the columns order[c0 : c0+K] (K <= 128) for every row; writes x, the
+ * residual norms, the accepted steps delta (B x 128) and the accepted count.  Replaces the column loop
+ * of the persistent Triton sweep :59-107 for one block of columns. */
+int mpq_cd_block(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* scale, const float* zero,
+                 int64_t ld_p, int gshift, const float* diag, const float* diag_inv, const int* order, int c0, int K,
+                 const float* Hsub, float* res, float* delta, int* accepted, int B, int maxq, float accept_tol,
+                 void* stream);
+
+/* ---- rotation ----
+ * Block Walsh-Hadamard of the last dim, blocks of `had` (power of two <= 16384), normalized by sqrt(had);
+ * mode 0: y = H(x * signs) (right rotation), mode 1: y = H(x) * signs (inverse).  signs may be NULL.
+ * Replaces mpq/rotation.py:404-441 (apply_block_hadamard, apply_right_block_hadamard[_inverse]). */
+int mpq_block_hadamard(const float* x, int64_t ldx, float* y, int64_t ldy, int rows, int n, int had,
+                       const float* signs, int mode, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MPQ_B200_H */

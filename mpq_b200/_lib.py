@@ -1,0 +1,94 @@
+"""ctypes binding of ``libmpq_b200.so`` (the C-ABI declared in ``include/mpq_b200.h``).
+
+The library is the product: there is no CPU or library fallback.  Importing a kernel entry
+point when the shared object is missing raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Any, Dict, Tuple
+
+import torch
+
+from . import trace as _trace
+
+LIB_PATH = Path(__file__).resolve().parent / "libmpq_b200.so"
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+L = ctypes.c_int64
+F = ctypes.c_float
+
+# name -> argtypes (every entry returns int status; `stream` is the trailing c_void_p)
+SIGNATURES: Dict[str, Tuple[Any, ...]] = {
+    "mpq_uniform_mmse": (P, L, P, L, P, P, L, I, P, I, I, I, F, P, L, P, P, P, P, P),
+    "mpq_uniform_map_decision": (P, L, P, L, P, P, L, I, P, I, I, I, F, P, P, L, P),
+    "mpq_uniform_nearest": (P, L, P, P, L, I, I, I, I, P, P, L, P),
+    "mpq_group_minmax": (P, L, I, I, I, I, P, P, L, P),
+    "mpq_uniform_rtn": (P, L, P, P, L, I, I, I, I, P, P, L, P),
+    "mpq_block_hadamard": (P, L, P, L, I, I, I, P, I, P),
+    "mpq_vamp_rows": (P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, F, F, I, P),
+    "mpq_gamma_retry": (P, P, I, I, F, P),
+    "mpq_vamp_r2": (P, P, P, P, P, P, P, I, I, L, F, P),
+    "mpq_linear_epilogue": (P, P, P, P, F, I, I, L, P, P, P),
+    "mpq_vamp_r1": (P, P, P, P, P, P, I, I, L, F, P),
+    "mpq_row_sqerr": (P, P, I, I, L, L, P, P),
+    "mpq_residual": (P, P, I, I, L, P, P),
+    "mpq_mean_rows": (P, P, I, P, P),
+    "mpq_polish_merge": (P, P, P, P, P, P, P, I, I, L, P, P),
+    "mpq_gamma_init": (P, P, I, I, L, F, P, P),
+    "mpq_row_dot": (P, L, P, L, I, I, P, P),
+    "mpq_sub": (P, P, P, I, I, L, P),
+    "mpq_gemm_f32": (I, I, I, I, F, P, L, P, L, F, P, L, P),
+    "mpq_cd_diag": (P, I, I, L, P, P, P),
+    "mpq_cd_gain": (P, I, I, L, P, P, P),
+    "mpq_argsort_desc": (P, I, P, P),
+    "mpq_cd_gather": (P, L, I, P, I, I, P, P, P),
+    "mpq_cd_block": (P, L, P, L, P, P, L, I, P, P, P, I, I, P, P, P, P, I, I, F, P),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the CUDA library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"libmpq_b200.so not found at {LIB_PATH}; build it with `python -m mpq_b200.build` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = list(argtypes)
+        fn.restype = ctypes.c_int
+    lib.mpq_last_error.restype = ctypes.c_char_p
+    lib.mpq_last_error.argtypes = []
+    lib.mpq_abi_version.restype = ctypes.c_int
+    _lib = lib
+    return lib
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def stream_ptr(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def call(name: str, *args) -> None:
+    """Invoke a C-ABI entry point on the current torch stream; raise RuntimeError on failure."""
+    lib = load()
+    fn = getattr(lib, name)
+    status = fn(*args, stream_ptr())
+    _trace.count_launch()
+    if status != 0:
+        msg = lib.mpq_last_error().decode(errors="replace")
+        raise RuntimeError(f"{name} failed with status {status}: {msg}")

@@ -1,0 +1,270 @@
+"""Per-linear grouped-scalar driver (the GPTQModel hook point).
+
+Reference: mpq/adapters/gptqmodel.py:650-1163 (run_mpq_quantization), :276-310
+(_vamp_hessian_eigen), :313-327 (_resolve_block_rows), :46-118 (_resolve_internal_rotation).
+
+Only the default ``vamp`` solver is on this path; the research baselines (cdquant, quantease,
+ojbkq) and ``desc_act`` column permutation raise ``ValueError``.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+from typing import Any, Dict, List, Optional, Tuple
+
+import torch
+
+from .. import ops
+from .._lib import call, ptr
+from ..rotation import (apply_right_block_hadamard, apply_right_block_hadamard_inverse, resolve_block_hadamard_plan,
+                        sample_rademacher_signs)
+from ..solver import UniformVampConfig, solve_uniform_rankspace_vamp
+
+
+@dataclass(frozen=True)
+class GPTQAdapterConfig:
+    hessian_scale: float = 0.5  # GPTQModel stores H = 2/m X^T X; 0.5 gives X^T X / m
+    block_rows: int = 128
+    jitter_base: float = 1e-6
+    eigen_floor_scale: float = 1e-6
+    rotation_seed: int = 0
+    # True: grow block_rows to the memory budget as the reference does on CUDA
+    # (mpq/adapters/gptqmodel.py:313-327).  False: use block_rows as given (parity pinning).
+    grow_block_rows: bool = True
+
+
+@torch.inference_mode()
+def vamp_hessian_eigen(H: torch.Tensor, *, jitter_base: float = 1e-6, floor_scale: float = 1e-6,
+                       fp64: bool = False) -> Tuple[torch.Tensor, torch.Tensor, float]:
+    """Floored, descending eigendecomposition (cuSOLVER through torch.linalg.eigh).
+
+    mpq/adapters/gptqmodel.py:276-310 (fp32) and mpq/adapters/quip_sharp.py:33-67 (fp64).
+    """
+    Hd = H.to(torch.float64 if fp64 else torch.float32)
+    Hd = 0.5 * (Hd + Hd.T)
+    if not torch.isfinite(Hd).all():
+        Hd = torch.nan_to_num(Hd, nan=0.0, posinf=0.0, neginf=0.0)
+    lam, V = torch.linalg.eigh(Hd)
+    lam = lam.to(torch.float32)
+    V = V.to(torch.float32)
+    max_lam = float(lam.max().item()) if lam.numel() else 0.0
+    diag_mean = float(torch.diagonal(Hd).mean().abs().item()) if Hd.numel() else 0.0
+    floor = max(float(jitter_base), float(floor_scale) * max(diag_mean, max_lam, 1e-12))
+    lam = lam.clamp_min_(floor).flip(0).contiguous()
+    V = V.flip(1).contiguous()
+    return lam, V, float(floor)
+
+
+def resolve_block_rows(rows: int, cols: int, maxq: int, requested: int, device: torch.device, grow: bool = True) -> int:
+    """mpq/adapters/gptqmodel.py:313-327."""
+    block_rows = min(int(rows), max(int(requested), 1))
+    if not grow or device.type != "cuda":
+        return block_rows
+    with torch.cuda.device(device):
+        free_bytes, _ = torch.cuda.mem_get_info()
+    bytes_per_row = 4 * (8 * int(cols) + 4 * int(cols) * (int(maxq) + 1))
+    budget = min(4 * 1024**3, int(free_bytes) // 2)
+    auto = max(8, min(int(rows), int(budget // max(bytes_per_row, 1))))
+    return min(int(rows), max(block_rows, int(auto)))
+
+
+def group_params(W: torch.Tensor, group_size: int, maxq: int, quantizer: Any = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-(row, group) scale/zero.  With ``quantizer`` (a GPTQModel ``Quantizer``) its
+    ``find_params`` is called per group as the reference does (:899-909); otherwise the CUDA
+    min-max kernel (the restated asymmetric GPTQ grid) computes them."""
+    rows, cols = W.shape
+    ng = (cols + group_size - 1) // group_size
+    if quantizer is not None and hasattr(quantizer, "find_params"):
+        sc, zc = [], []
+        for g in range(ng):
+            quantizer.find_params(W[:, g * group_size:(g + 1) * group_size].contiguous(), weight=True)
+            sc.append(quantizer.scale.to(torch.float32).reshape(rows, 1).clone())
+            zc.append(quantizer.zero.to(torch.float32).reshape(rows, 1).clone())
+        return torch.cat(sc, 1).contiguous(), torch.cat(zc, 1).contiguous()
+    scale = torch.empty(rows, ng, device=W.device, dtype=torch.float32)
+    zero = torch.empty(rows, ng, device=W.device, dtype=torch.float32)
+    call("mpq_group_minmax", ptr(W), W.stride(0), rows, cols, int(group_size), int(maxq), ptr(scale), ptr(zero),
+         scale.stride(0))
+    return scale, zero
+
+
+def _expand(g: torch.Tensor, group_size: int, cols: int) -> torch.Tensor:
+    return torch.repeat_interleave(g, group_size, dim=1)[:, :cols].contiguous()
+
+
+@torch.inference_mode()
+def run_mpq_quantization(
+    *,
+    W: torch.Tensor,
+    H: torch.Tensor,
+    quantizer: Any,
+    qcfg: Any,
+    module_name: str,
+    vamp_cfg: UniformVampConfig,
+    adapter_cfg: GPTQAdapterConfig = GPTQAdapterConfig(),
+) -> Tuple[torch.Tensor, Optional[torch.Tensor], Optional[torch.Tensor], Optional[torch.Tensor],
+           Optional[torch.Tensor], float, Dict[str, Any]]:
+    """Run MPQ on one linear layer given its weights and accumulated Hessian.
+
+    Returns (Q dense float32 in the original basis, q_int uint8 in the solver basis,
+    scale_groups, zero_groups, g_idx int32, quant_time_s, stats).
+    """
+    start = time.time()
+    if not W.is_cuda:
+        raise ValueError("run_mpq_quantization requires CUDA tensors (there is no CPU path)")
+    device = W.device
+    W = W.to(torch.float32).contiguous()
+    H = H.to(device=device, dtype=torch.float32).contiguous()
+    rows, cols = W.shape
+    bits = int(getattr(qcfg, "bits"))
+    maxq = int(2**bits - 1)
+    group_size = int(getattr(qcfg, "group_size", cols))
+    if group_size == -1:
+        group_size = cols
+    mpq_cfg = getattr(qcfg, "mpq", None)
+    solver_name = str(getattr(mpq_cfg, "dispatch_solver", getattr(mpq_cfg, "solver", "vamp")) or "vamp").lower()
+    if solver_name != "vamp":
+        raise ValueError(f"unsupported GPTQModel MPQ solver={solver_name!r} (only 'vamp' is on the CUDA path).")
+    if bool(getattr(qcfg, "desc_act", False)):
+        raise ValueError("desc_act column ordering is not supported by the CUDA path.")
+    rotation = str(getattr(mpq_cfg, "rotation_mode", getattr(qcfg, "rotation", None) or "none") or "none").lower()
+    if rotation not in {"none", "internal_hadamard", "model_hadamard", "model_random"}:
+        raise ValueError("mpq only supports rotation in {none, model_hadamard, model_random, internal_hadamard}; "
+                         f"got rotation={rotation!r}.")
+
+    H_work = float(adapter_cfg.hessian_scale) * H
+    lam, V, eigen_floor = vamp_hessian_eigen(H_work, jitter_base=adapter_cfg.jitter_base,
+                                             floor_scale=adapter_cfg.eigen_floor_scale)
+    signs = None
+    had_dim = 1
+    effective = rotation
+    if rotation == "internal_hadamard":
+        mode, had_dim = resolve_block_hadamard_plan(cols)
+        if mode == "block":
+            signs = sample_rademacher_signs(width=cols, key=f"{module_name}:full", seed=int(adapter_cfg.rotation_seed),
+                                            device=device)
+            effective = "internal_block_hadamard"
+        else:
+            effective = "none"
+    if signs is not None:
+        W_work = apply_right_block_hadamard(W, signs=signs, had_dim=had_dim)
+        H_metric = apply_right_block_hadamard(H_work.T.contiguous(), signs=signs, had_dim=had_dim).T.contiguous()
+        H_metric = apply_right_block_hadamard(H_metric, signs=signs, had_dim=had_dim)
+        V = apply_right_block_hadamard(V.T.contiguous(), signs=signs, had_dim=had_dim).T.contiguous()
+    else:
+        W_work, H_metric = W, H_work.contiguous()
+    dead = torch.diagonal(H_metric) == 0
+    if bool(dead.any().item()):
+        # mpq/adapters/gptqmodel.py:743-749 then a re-decomposition in the solver basis (:885-892)
+        H_metric = H_metric.clone()
+        W_work = W_work.clone()
+        H_metric[dead, dead] = 1
+        W_work[:, dead] = 0
+        lam, V, eigen_floor = vamp_hessian_eigen(H_metric, jitter_base=adapter_cfg.jitter_base,
+                                                 floor_scale=adapter_cfg.eigen_floor_scale)
+    V = V.contiguous()
+    Vh = V.T.contiguous()
+    S = torch.sqrt(lam).contiguous()
+    Vs = (V * S.unsqueeze(0)).contiguous()
+    R = int(S.numel())
+
+    scale_groups, zero_groups = group_params(W_work, group_size, maxq, quantizer)
+    block_rows = resolve_block_rows(rows, cols, maxq, int(adapter_cfg.block_rows), device,
+                                    grow=bool(adapter_cfg.grow_block_rows))
+
+    def block_params(rb):
+        sg, zg = scale_groups[rb], zero_groups[rb]
+        if cols % group_size == 0 and (group_size & (group_size - 1)) == 0:
+            return sg.contiguous(), zg.contiguous()
+        return _expand(sg, group_size, cols), _expand(zg, group_size, cols)
+
+    def rtn(rb, sb, zb):
+        Wb = W_work[rb]
+        ld_p, gshift = ops.group_layout(sb, cols)
+        x = torch.empty_like(Wb)
+        call("mpq_uniform_rtn", ptr(Wb), Wb.stride(0), ptr(sb), ptr(zb), ld_p, gshift, Wb.shape[0], cols, maxq, None,
+             ptr(x), x.stride(0))
+        return x
+
+    VsT = Vs.T.contiguous()
+    if float(getattr(vamp_cfg, "obs_precision", 0.0)) > 0.0:
+        obs_precision = float(vamp_cfg.obs_precision)
+    else:
+        sum_sq = 0.0
+        count = 0
+        for r0 in range(0, rows, block_rows):
+            rb = slice(r0, min(r0 + block_rows, rows))
+            sb, zb = block_params(rb)
+            x_rtn = rtn(rb, sb, zb)
+            delta = torch.empty_like(x_rtn)
+            call("mpq_sub", ptr(W_work[rb]), ptr(x_rtn), ptr(delta), delta.shape[0], cols, delta.stride(0))
+            diff_u = ops.gemm_nt(delta, VsT)
+            zeros = torch.zeros_like(diff_u)
+            e = torch.empty(diff_u.shape[0], device=device, dtype=torch.float32)
+            call("mpq_row_sqerr", ptr(diff_u), ptr(zeros), diff_u.shape[0], R, diff_u.stride(0), zeros.stride(0), ptr(e))
+            sum_sq += float(e.double().sum().item())
+            count += int(diff_u.numel())
+        obs_precision = 1.0 / float(max(sum_sq / max(count, 1), 1e-12))
+
+    Q_work = torch.empty_like(W_work)
+    q_int_work = torch.empty((rows, cols), dtype=torch.uint8, device=device)
+    obs_block = float(obs_precision)
+    layer_err_sum = 0.0
+    raw_err_sum = 0.0
+    rtn_err_sum = 0.0
+    block_stats: List[Dict[str, Any]] = []
+    gamma_sum, gamma_count = 0.0, 0
+    for r0 in range(0, rows, block_rows):
+        rb = slice(r0, min(r0 + block_rows, rows))
+        sb, zb = block_params(rb)
+        x_rtn = rtn(rb, sb, zb)
+        dbg: Dict[str, Any] = {"summary_only": True}
+        q_int, x_final, final_err, rtn_err, st = solve_uniform_rankspace_vamp(
+            W=W_work[rb], x_rtn=x_rtn, scale_full=sb, zero_full=zb, maxq=maxq, V=V, Vh=Vh, S=S, Vs=Vs, cfg=vamp_cfg,
+            gram_full=H_metric, obs_precision_init=obs_block, log_stats=False, debug_out=dbg)
+        Q_work[rb] = x_final
+        q_int_work[rb] = q_int.to(torch.uint8)
+        layer_err_sum += float(final_err.double().sum().item())
+        # raw Hessian audit (:1048-1056): (W - Q) H (W - Q)^T per row
+        delta = torch.empty_like(x_final)
+        call("mpq_sub", ptr(W_work[rb]), ptr(x_final), ptr(delta), delta.shape[0], cols, delta.stride(0))
+        dH = ops.gemm_nn(delta, H_metric)
+        raw = torch.empty(delta.shape[0], device=device, dtype=torch.float32)
+        call("mpq_row_dot", ptr(dH), dH.stride(0), ptr(delta), delta.stride(0), delta.shape[0], cols, ptr(raw))
+        raw_err_sum += float(raw.double().sum().item())
+        rtn_err_sum += float(rtn_err.double().sum().item())
+        if bool(getattr(vamp_cfg, "em_obs_precision", True)):
+            obs_block = float(st.get("obs_precision_final", obs_block))
+        gamma_sum += float(dbg.get("gamma1_sum", 0.0))
+        gamma_count += int(dbg.get("gamma1_count", 0))
+        block_stats.append(st)
+
+    g_idx = torch.arange(cols, device=device, dtype=torch.int32) // int(group_size)
+    Q = apply_right_block_hadamard_inverse(Q_work, signs=signs, had_dim=had_dim) if signs is not None else Q_work
+    stats: Dict[str, Any] = {
+        "method": "mpq",
+        "solver": solver_name,
+        "module": str(module_name),
+        "bits": bits,
+        "group_size": group_size,
+        "rotation_requested": rotation,
+        "rotation_effective": effective,
+        "rotation_internal": signs is not None,
+        "rotation_block_dim": int(had_dim),
+        "rows": int(rows),
+        "cols": int(cols),
+        "rank": R,
+        "eigen_floor": float(eigen_floor),
+        "block_rows": int(block_rows),
+        "block_cd_backend": "cuda",
+        "obs_precision_initial": float(obs_precision),
+        "obs_precision_final": float(obs_block),
+        "layer_error_sum": float(layer_err_sum),
+        "stabilized_objective_mean_final": float(layer_err_sum / max(rows, 1)),
+        "raw_objective_mean_final": float(raw_err_sum / max(rows, 1)),
+        "rtn_error_sum": float(rtn_err_sum),
+        "block_stats": block_stats,
+        "quant_time_s": float(time.time() - start),
+        "stage1_gamma1_mean": float(gamma_sum / max(gamma_count, 1)),
+    }
+    return Q, q_int_work, scale_groups, zero_groups, g_idx, float(time.time() - start), stats

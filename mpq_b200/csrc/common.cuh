@@ -1,0 +1,81 @@
+// Shared helpers for the MPQ B200 kernels (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <math.h>
+
+#define MPQ_API extern "C" __attribute__((visibility("default")))
+
+// Status codes returned by every C-ABI entry point (0 = success; >0 = cudaError_t).
+enum MpqStatus {
+  MPQ_OK = 0,
+  MPQ_ERR_ARG = 10001,        // invalid argument (shape, null pointer, unsupported size)
+  MPQ_ERR_UNSUPPORTED = 10002,
+};
+
+namespace mpq {
+
+void set_last_error(const char* fmt, ...);
+
+inline int launch_status(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error("%s: %s", what, cudaGetErrorString(e));
+    return (int)e;
+  }
+  return MPQ_OK;
+}
+
+#define MPQ_CHECK_ARG(cond, ...)          \
+  do {                                    \
+    if (!(cond)) {                        \
+      ::mpq::set_last_error(__VA_ARGS__); \
+      return MPQ_ERR_ARG;                 \
+    }                                     \
+  } while (0)
+
+// ---- exact float32 arithmetic (no FMA contraction): mirrors the reference op order ----
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+
+// torch.nan_to_num(x, nan, posinf, neginf)
+__device__ __forceinline__ float nan_to_num(float x, float nan_v, float pinf, float ninf) {
+  if (isnan(x)) return nan_v;
+  if (isinf(x)) return x > 0.f ? pinf : ninf;
+  return x;
+}
+
+// mpq/utils.py log_damp_positive: exp((1-d) ln max(p,1e-12) + d ln max(n,1e-12)), float32.
+__device__ __forceinline__ float log_damp(float prev, float nw, float one_minus_d, float d) {
+  prev = fmaxf(prev, 1e-12f);
+  nw = fmaxf(nw, 1e-12f);
+  return expf(fadd(fmul(one_minus_d, logf(prev)), fmul(d, logf(nw))));
+}
+
+// Deterministic block-wide sum (fixed tree order). `red` must hold blockDim.x/32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = 0.f;
+  if (wid == 0) {
+    t = lane < nw ? red[lane] : 0.f;
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  }
+  return t;  // valid in warp 0
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace mpq

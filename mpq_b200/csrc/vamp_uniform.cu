@@ -1,0 +1,379 @@
+// VAMP message updates in rank space: the per-row scalar algebra and the fused element-wise
+// passes around the three rank-space GEMMs of each iteration.
+//
+// Reference: mpq/solver.py:553-699 (the scalar VAMP loop; the E8P12 loop :961-1122 shares
+// the algebra), mpq/linear.py:10-82 (linear_mmse_exact, em_update_obs_precision_rankspace),
+// mpq/linear.py:85-94 (vamp_rankspace_error), mpq/utils.py:24-57 (damping, validity masks).
+//
+// Row state lives in small device vectors of length B.  Flags that steer the host control
+// flow (retry / skip / best-iterate) are counted with integer atomics (order independent).
+#include "common.cuh"
+
+namespace mpq {
+
+constexpr float kAlphaEps = 1e-7f;
+// float32(1.0 - 1e-7), the comparison constant torch uses for `1.0 - alpha_eps`
+constexpr float kOneMinusAlphaEps = 0.99999988079071044921875f;
+
+__device__ __forceinline__ bool alpha_valid(float a) { return isfinite(a) && a > kAlphaEps && a < kOneMinusAlphaEps; }
+__device__ __forceinline__ bool precision_valid(float g) { return isfinite(g) && g > 1e-12f; }
+__device__ __forceinline__ float clip_alpha(float a) {
+  a = nan_to_num(a, 0.5f, kOneMinusAlphaEps, kAlphaEps);
+  return fminf(fmaxf(a, kAlphaEps), kOneMinusAlphaEps);
+}
+
+// flags[0] = #rows with invalid alpha1, flags[1] = #rows non-finite alpha1,
+// flags[2] = #rows invalid gamma2_new, flags[3] = #rows invalid damped gamma2, flags[4] = #alpha2 clipped
+struct RowState {
+  const float* var_rowsum;  // (B) sum_j var1
+  float* gamma1;            // (B) committed gamma1
+  float* gamma1_work;       // (B) gamma1 used by the current denoiser call
+  float* alpha1;            // (B)
+  float* eta1;              // (B)
+  float* gamma2_new;        // (B)
+  float* gamma2;            // (B) damped (current)
+  const float* gamma2_prev; // (B) previous damped gamma2 or null
+  float* alpha2;            // (B) clipped
+  float* eta2;              // (B)
+  float* gamma1_new;        // (B)
+  float* gamma1_next;       // (B) damped gamma1 for the next iteration
+  float* trace;             // (B) sum_r s^2 / (obs s^2 + gamma2)
+  int* flags;               // (8)
+};
+
+// Stage A+B of one VAMP iteration (mpq/solver.py:559-631 up to the linear module, plus the
+// gamma-only parts of linear_mmse_exact and the EM trace term).  One warp per row; the
+// rank-space sums over S run in a fixed lane-strided order.
+__global__ void k_vamp_rows(RowState st, const float* __restrict__ S, int B, int n, int R, float obs, float damping,
+                            int final_retry) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= B) return;
+  const int b = warp;
+  const float g1w = st.gamma1_work[b];
+  const float a1_raw = fmul(g1w, fdiv(st.var_rowsum[b], (float)n));  // gamma1 * var.mean(dim=1)
+  float a1 = a1_raw;
+  if (!alpha_valid(a1_raw)) {
+    if (lane == 0) {
+      atomicAdd(&st.flags[0], 1);
+      if (!isfinite(a1_raw)) atomicAdd(&st.flags[1], 1);
+    }
+    if (final_retry) a1 = clip_alpha(a1_raw);
+  }
+  const float eta1 = fdiv(g1w, a1);
+  const float g2n = fmaxf(nan_to_num(fsub(eta1, g1w), 1e-12f, 1e12f, 1e-12f), 1e-12f);
+  float g2 = g2n;
+  const bool damp = (st.gamma2_prev != nullptr) && damping < 1.f;
+  if (damp) g2 = log_damp(st.gamma2_prev[b], g2n, (float)(1.0 - (double)damping), damping);
+  // gamma-only parts of linear_mmse_exact: sum_r 1/denom and sum_r s^2/denom, denom = obs*s^2 + gamma2
+  float inv_sum = 0.f, tr_sum = 0.f;
+  for (int r = lane; r < R; r += 32) {
+    const float s = S[r];
+    const float s2 = fmul(s, s);
+    const float den = fadd(fmul(obs, s2), g2);
+    inv_sum += fdiv(1.f, den);
+    tr_sum += fdiv(s2, den);
+  }
+  inv_sum = warp_sum(inv_sum);
+  tr_sum = warp_sum(tr_sum);
+  const float c0 = (float)(1.0 - (double)R / (double)n);
+  const float a2_raw = fadd(c0, fmul(fdiv(g2, (float)n), inv_sum));
+  const float a2 = clip_alpha(a2_raw);
+  const float eta2 = fdiv(g2, a2);
+  const float g1n = fmaxf(nan_to_num(fsub(eta2, g2), 1e-12f, 1e12f, 1e-12f), 1e-12f);
+  const float g1c = st.gamma1[b];
+  const float g1next = damping >= 1.f ? g1n : log_damp(g1c, g1n, (float)(1.0 - (double)damping), damping);
+  if (lane == 0) {
+    st.alpha1[b] = a1;
+    st.eta1[b] = eta1;
+    st.gamma2_new[b] = g2n;
+    st.gamma2[b] = g2;
+    st.alpha2[b] = a2;
+    st.eta2[b] = eta2;
+    st.gamma1_new[b] = g1n;
+    st.gamma1_next[b] = g1next;
+    st.trace[b] = tr_sum;
+    if (!precision_valid(g2n)) atomicAdd(&st.flags[2], 1);
+    if (!precision_valid(g2)) atomicAdd(&st.flags[3], 1);
+    if (!alpha_valid(a2_raw)) atomicAdd(&st.flags[4], 1);
+  }
+}
+
+// gamma retry (mpq/solver.py:593-596): divide/multiply the work precision of invalid rows.
+__global__ void k_gamma_retry(float* gamma1_work, const float* alpha1_raw_src_var, const float* var_rowsum, int B,
+                              int n, float factor) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  float g = gamma1_work[b];
+  const float a = fmul(g, fdiv(var_rowsum[b], (float)n));
+  if (a <= kAlphaEps) g = fdiv(g, factor);
+  if (a >= kOneMinusAlphaEps) g = fmul(g, factor);
+  gamma1_work[b] = fmaxf(g, 1e-12f);
+}
+
+// r2 = damp(r2_prev, (eta1*x1 - gamma1w*r1)/gamma2_new)          (mpq/solver.py:605-612)
+__global__ void k_vamp_r2(const float* __restrict__ x1, const float* __restrict__ r1, const float* __restrict__ r2_prev,
+                          float* __restrict__ r2, const float* __restrict__ eta1, const float* __restrict__ g1w,
+                          const float* __restrict__ g2n, int B, int n, int64_t ld, float damping) {
+  const int64_t total = (int64_t)B * n;
+  const float omd = (float)(1.0 - (double)damping);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i / n), j = (int)(i % n);
+    const int64_t o = b * ld + j;
+    const float rn = fdiv(fsub(fmul(eta1[b], x1[o]), fmul(g1w[b], r1[o])), g2n[b]);
+    r2[o] = r2_prev ? fadd(fmul(omd, r2_prev[o]), fmul(damping, rn)) : rn;
+  }
+}
+
+// Linear-module epilogue over P = r2 @ V  (mpq/linear.py:46-55):
+//   rb = Y_u - P*s;  u = rb * (obs*s/denom);  rowsum((rb*gamma2/denom)^2)
+// One CTA per row; the row sum is reduced in a fixed order.
+__global__ void __launch_bounds__(256) k_linear_epilogue(const float* __restrict__ P, const float* __restrict__ Y_u,
+                                                         const float* __restrict__ S, const float* __restrict__ g2,
+                                                         float obs, int R, int64_t ld, float* __restrict__ u,
+                                                         float* __restrict__ resid_rowsum) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const float gb = g2[b];
+  float acc = 0.f;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const float s = S[r];
+    const float den = fadd(fmul(obs, fmul(s, s)), gb);
+    const float rb = fsub(Y_u[b * ld + r], fmul(P[b * ld + r], s));
+    const float coeff = fdiv(fmul(obs, s), den);
+    u[b * ld + r] = fmul(rb, coeff);
+    const float ra = fmul(rb, fdiv(gb, den));
+    acc += ra * ra;
+  }
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) resid_rowsum[b] = t;
+}
+
+// r1 update from D = u @ V^T  (mpq/linear.py:51-52, mpq/solver.py:645-653):
+//   x2 = r2 + D;  r1_new = (eta2*x2 - gamma2*r2)/gamma1_new;  r1 = (1-d) r1 + d r1_new
+__global__ void k_vamp_r1(const float* __restrict__ D, const float* __restrict__ r2, float* __restrict__ r1,
+                          const float* __restrict__ eta2, const float* __restrict__ g2, const float* __restrict__ g1n,
+                          int B, int n, int64_t ld, float damping) {
+  const int64_t total = (int64_t)B * n;
+  const float omd = (float)(1.0 - (double)damping);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i / n), j = (int)(i % n);
+    const int64_t o = b * ld + j;
+    const float x2 = fadd(r2[o], D[o]);
+    const float rn = fdiv(fsub(fmul(eta2[b], x2), fmul(g2[b], r2[o])), g1n[b]);
+    r1[o] = damping >= 1.f ? rn : fadd(fmul(omd, r1[o]), fmul(damping, rn));
+  }
+}
+
+// rowsum((Y - C)^2) (vamp_rankspace_error), optionally rowsum((Y - C)^2) + add[b]; one CTA per row.
+__global__ void __launch_bounds__(256) k_row_sqerr(const float* __restrict__ Y, const float* __restrict__ C, int R,
+                                                   int64_t ldy, int64_t ldc, float* __restrict__ out) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  float acc = 0.f;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const float d = fsub(Y[b * ldy + r], C[b * ldc + r]);
+    acc += d * d;
+  }
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) out[b] = t;
+}
+
+// residual = Y - C (in place into C), and rowsum(residual^2)
+__global__ void __launch_bounds__(256) k_residual(const float* __restrict__ Y, float* __restrict__ C, int R,
+                                                  int64_t ld, float* __restrict__ rowsum) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  float acc = 0.f;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const float d = fsub(Y[b * ld + r], C[b * ld + r]);
+    C[b * ld + r] = d;
+    acc += d * d;
+  }
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0 && rowsum) rowsum[b] = t;
+}
+
+// mean over B of (a[b] + (c ? c[b] : 0)) in a fixed order (single CTA).
+__global__ void __launch_bounds__(1024) k_mean_rows(const float* __restrict__ a, const float* __restrict__ c, int B,
+                                                    float* __restrict__ out) {
+  __shared__ float red[32];
+  float acc = 0.f;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) acc += c ? fadd(a[b], c[b]) : a[b];
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) *out = B > 0 ? t / (float)B : 0.f;
+}
+
+// Row-wise selection:  dst[b,:] = mask[b] ? src[b,:] : dst[b,:]  for f32 and u8 payloads, and
+// the polish merge mask improve = err_after + 1e-12 < err_before (mpq/solver.py:749-754).
+__global__ void k_polish_merge(const float* __restrict__ err_after, float* __restrict__ err_final,
+                               const float* __restrict__ err_before, const float* __restrict__ x_src,
+                               float* __restrict__ x_dst, const uint8_t* __restrict__ q_src, uint8_t* __restrict__ q_dst,
+                               int B, int n, int64_t ld, int* improved_count) {
+  const int b = blockIdx.x;
+  const bool imp = fadd(err_after[b], 1e-12f) < err_before[b];
+  if (!imp) return;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    x_dst[b * ld + j] = x_src[b * ld + j];
+    q_dst[b * ld + j] = q_src[b * ld + j];
+  }
+  if (threadIdx.x == 0) {
+    err_final[b] = err_after[b];
+    atomicAdd(improved_count, 1);
+  }
+}
+
+// gamma1 = 0.25 * gamma_start / max(mean_j (W - x_rtn)^2, 1e-12)  (mpq/solver.py:481, :86-87)
+__global__ void __launch_bounds__(256) k_gamma_init(const float* __restrict__ W, const float* __restrict__ x, int n,
+                                                    int64_t ld, float gamma_start, float* __restrict__ gamma1) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  float acc = 0.f;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float d = fsub(W[b * ld + j], x[b * ld + j]);
+    acc += d * d;
+  }
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) {
+    const float mse = fmaxf(t / (float)n, 1e-12f);
+    gamma1[b] = fmul(gamma_start, fdiv(0.25f, mse));
+  }
+}
+
+static inline int ew_grid(int64_t total) {
+  int64_t g = (total + 255) / 256;
+  if (g > 148 * 16) g = 148 * 16;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace mpq
+
+using namespace mpq;
+
+MPQ_API int mpq_vamp_rows(const float* var_rowsum, float* gamma1, float* gamma1_work, float* alpha1, float* eta1,
+                          float* gamma2_new, float* gamma2, const float* gamma2_prev, float* alpha2, float* eta2,
+                          float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int B,
+                          int n, int R, float obs, float damping, int final_retry, void* stream) {
+  MPQ_CHECK_ARG(var_rowsum && gamma1 && gamma1_work && alpha1 && eta1 && gamma2_new && gamma2 && alpha2 && eta2 &&
+                    gamma1_new && gamma1_next && trace && flags && S,
+                "mpq_vamp_rows: null pointer");
+  if (B == 0) return MPQ_OK;
+  RowState st{var_rowsum, gamma1, gamma1_work, alpha1, eta1, gamma2_new, gamma2, gamma2_prev,
+              alpha2, eta2, gamma1_new, gamma1_next, trace, flags};
+  const int threads = 256;
+  const int blocks = (B * 32 + threads - 1) / threads;
+  k_vamp_rows<<<blocks, threads, 0, (cudaStream_t)stream>>>(st, S, B, n, R, obs, damping, final_retry);
+  return launch_status("mpq_vamp_rows");
+}
+
+MPQ_API int mpq_gamma_retry(float* gamma1_work, const float* var_rowsum, int B, int n, float factor, void* stream) {
+  MPQ_CHECK_ARG(gamma1_work && var_rowsum, "mpq_gamma_retry: null pointer");
+  if (B == 0) return MPQ_OK;
+  k_gamma_retry<<<(B + 255) / 256, 256, 0, (cudaStream_t)stream>>>(gamma1_work, nullptr, var_rowsum, B, n, factor);
+  return launch_status("mpq_gamma_retry");
+}
+
+MPQ_API int mpq_vamp_r2(const float* x1, const float* r1, const float* r2_prev, float* r2, const float* eta1,
+                        const float* gamma1_work, const float* gamma2_new, int B, int n, int64_t ld, float damping,
+                        void* stream) {
+  MPQ_CHECK_ARG(x1 && r1 && r2 && eta1 && gamma1_work && gamma2_new, "mpq_vamp_r2: null pointer");
+  if ((int64_t)B * n == 0) return MPQ_OK;
+  k_vamp_r2<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(x1, r1, r2_prev, r2, eta1, gamma1_work,
+                                                                       gamma2_new, B, n, ld, damping);
+  return launch_status("mpq_vamp_r2");
+}
+
+MPQ_API int mpq_linear_epilogue(const float* P, const float* Y_u, const float* S, const float* gamma2, float obs,
+                                int B, int R, int64_t ld, float* u, float* resid_rowsum, void* stream) {
+  MPQ_CHECK_ARG(P && Y_u && S && gamma2 && u && resid_rowsum, "mpq_linear_epilogue: null pointer");
+  if (B == 0) return MPQ_OK;
+  k_linear_epilogue<<<B, 256, 0, (cudaStream_t)stream>>>(P, Y_u, S, gamma2, obs, R, ld, u, resid_rowsum);
+  return launch_status("mpq_linear_epilogue");
+}
+
+MPQ_API int mpq_vamp_r1(const float* D, const float* r2, float* r1, const float* eta2, const float* gamma2,
+                        const float* gamma1_new, int B, int n, int64_t ld, float damping, void* stream) {
+  MPQ_CHECK_ARG(D && r2 && r1 && eta2 && gamma2 && gamma1_new, "mpq_vamp_r1: null pointer");
+  if ((int64_t)B * n == 0) return MPQ_OK;
+  k_vamp_r1<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(D, r2, r1, eta2, gamma2, gamma1_new, B, n, ld,
+                                                                       damping);
+  return launch_status("mpq_vamp_r1");
+}
+
+MPQ_API int mpq_row_sqerr(const float* Y, const float* C, int B, int R, int64_t ldy, int64_t ldc, float* out,
+                          void* stream) {
+  MPQ_CHECK_ARG(Y && C && out, "mpq_row_sqerr: null pointer");
+  if (B == 0) return MPQ_OK;
+  k_row_sqerr<<<B, 256, 0, (cudaStream_t)stream>>>(Y, C, R, ldy, ldc, out);
+  return launch_status("mpq_row_sqerr");
+}
+
+MPQ_API int mpq_residual(const float* Y, float* C, int B, int R, int64_t ld, float* rowsum, void* stream) {
+  MPQ_CHECK_ARG(Y && C, "mpq_residual: null pointer");
+  if (B == 0) return MPQ_OK;
+  k_residual<<<B, 256, 0, (cudaStream_t)stream>>>(Y, C, R, ld, rowsum);
+  return launch_status("mpq_residual");
+}
+
+MPQ_API int mpq_mean_rows(const float* a, const float* c, int B, float* out, void* stream) {
+  MPQ_CHECK_ARG(a && out, "mpq_mean_rows: null pointer");
+  k_mean_rows<<<1, 1024, 0, (cudaStream_t)stream>>>(a, c, B, out);
+  return launch_status("mpq_mean_rows");
+}
+
+MPQ_API int mpq_polish_merge(const float* err_after, float* err_final, const float* err_before, const float* x_src,
+                             float* x_dst, const uint8_t* q_src, uint8_t* q_dst, int B, int n, int64_t ld,
+                             int* improved_count, void* stream) {
+  MPQ_CHECK_ARG(err_after && err_final && err_before && x_src && x_dst && q_src && q_dst && improved_count,
+                "mpq_polish_merge: null pointer");
+  if (B == 0) return MPQ_OK;
+  k_polish_merge<<<B, 256, 0, (cudaStream_t)stream>>>(err_after, err_final, err_before, x_src, x_dst, q_src, q_dst, B,
+                                                      n, ld, improved_count);
+  return launch_status("mpq_polish_merge");
+}
+
+MPQ_API int mpq_gamma_init(const float* W, const float* x, int B, int n, int64_t ld, float gamma_start, float* gamma1,
+                           void* stream) {
+  MPQ_CHECK_ARG(W && x && gamma1, "mpq_gamma_init: null pointer");
+  if (B == 0) return MPQ_OK;
+  k_gamma_init<<<B, 256, 0, (cudaStream_t)stream>>>(W, x, n, ld, gamma_start, gamma1);
+  return launch_status("mpq_gamma_init");
+}
+
+// out[b] = sum_j A[b,j] * C[b,j]   (row-wise dot, e.g. the raw Hessian audit (d H) . d)
+namespace mpq {
+__global__ void __launch_bounds__(256) k_row_dot(const float* __restrict__ A, int64_t lda, const float* __restrict__ C,
+                                                 int64_t ldc, int n, float* __restrict__ out) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  float acc = 0.f;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) acc += A[b * lda + j] * C[b * ldc + j];
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) out[b] = t;
+}
+
+// D = A - C  (elementwise, e.g. delta = W - x)
+__global__ void k_sub(const float* __restrict__ A, const float* __restrict__ C, float* __restrict__ D, int B, int n,
+                      int64_t ld) {
+  const int64_t total = (int64_t)B * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i / n), j = (int)(i % n);
+    D[b * ld + j] = fsub(A[b * ld + j], C[b * ld + j]);
+  }
+}
+}  // namespace mpq
+
+MPQ_API int mpq_row_dot(const float* A, int64_t lda, const float* C, int64_t ldc, int B, int n, float* out,
+                        void* stream) {
+  MPQ_CHECK_ARG(A && C && out, "mpq_row_dot: null pointer");
+  if (B == 0) return MPQ_OK;
+  k_row_dot<<<B, 256, 0, (cudaStream_t)stream>>>(A, lda, C, ldc, n, out);
+  return launch_status("mpq_row_dot");
+}
+
+MPQ_API int mpq_sub(const float* A, const float* C, float* D, int B, int n, int64_t ld, void* stream) {
+  MPQ_CHECK_ARG(A && C && D, "mpq_sub: null pointer");
+  if ((int64_t)B * n == 0) return MPQ_OK;
+  k_sub<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(A, C, D, B, n, ld);
+  return launch_status("mpq_sub");
+}

@@ -1,0 +1,467 @@
+"""Rank-space VAMP solvers: the public plugin interface of the reference, on sm_100a kernels.
+
+Reference: mpq/solver.py (UniformVampConfig :35-55, E8P12VampConfig :58-82,
+polish_uniform_rankspace :260-366, solve_uniform_rankspace_vamp :426-830,
+_uniform_hard_decision :833-850).
+
+Signatures, argument meaning, return values and error behaviour follow the reference:
+keyword-only, pure (fresh outputs), ``ValueError`` for bad configuration or shapes,
+``RuntimeError`` for numerical invalidity.  All tensors must live on one CUDA device; the
+computation runs on the current torch stream through ``libmpq_b200.so``.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Any, Dict, Optional, Tuple
+
+import torch
+
+from . import ops
+from ._lib import call, ptr
+
+ALPHA_EPS = 1e-7
+
+
+@dataclass(frozen=True)
+class UniformVampConfig:
+    iters: int = 10
+    damping: float = 0.5
+    final_decision: str = "map"  # "map" | "round_mean"
+    init_from: str = "rtn"  # "rtn" | "float" | "zero"
+    gamma_start: float = 1.0
+    gamma_retry_factor: float = 4.0
+    gamma_retry_steps: int = 3
+    prior_tau: float = 0.2
+    obs_precision: float = 0.0
+    em_obs_precision: bool = True
+    em_obs_precision_damping: float = 0.3
+    em_obs_precision_min: float = 1e-4
+    em_obs_precision_max: float = 1e8
+    polish_sweeps: int = 3
+    polish_mode: str = "block_cd"  # "none" | "block_cd" | "topk_block_cd"
+    topk_k: int = 16
+    vamp_backend: str = "auto"  # accepted for interface compatibility; always the CUDA kernels
+    compile_block_cd: bool = True
+    block_cd_backend: str = "eager"
+
+
+@dataclass(frozen=True)
+class E8P12VampConfig:
+    """Scalar-precision VAMP config for QUIP E8P12 (mpq/solver.py:58-82)."""
+
+    iters: int = 16
+    damping: float = 0.5
+    gamma_start: float = 1.0
+    gamma_retry_factor: float = 4.0
+    gamma_retry_steps: int = 3
+    prior_tau: float = 0.25
+    prior_tau_scale_mode: str = "absmax"
+    compile_prior: bool = True
+    obs_precision: float = 0.0
+    em_obs_precision: bool = True
+    em_obs_precision_damping: float = 0.3
+    em_obs_precision_min: float = 1e-4
+    em_obs_precision_max: float = 1e8
+    blocks_per_chunk: int = 16
+    polish_sweeps: int = 3
+    polish_mode: str = "block_cd"
+    polish_metric: str = "gram"
+    polish_metric_rows_per_chunk: int = 0
+    polish_max_blocks: int = 0
+    topk_k: int = 16
+    best_iterate: bool = False
+
+
+def _resolve_polish_mode(*, sweeps: int, mode: str) -> str:
+    """mpq/solver.py:164-175."""
+    if int(sweeps) <= 0:
+        return "none"
+    mode_norm = str(mode or "block_cd").strip().lower()
+    if mode_norm in {"none", "off"}:
+        return "none"
+    if mode_norm in {"block_cd", "cd", "full_cd"}:
+        return "block_cd"
+    if mode_norm in {"topk_block_cd", "topk_cd", "topk", "vamp_topk"}:
+        return "topk_block_cd"
+    raise ValueError(f"unsupported polish_mode={mode!r}; expected none|block_cd|topk_block_cd.")
+
+
+def _log_damp_scalar(prev: float, new: float, damping: float) -> float:
+    """mpq/utils.py:36-45."""
+    if damping >= 1.0:
+        return float(new)
+    if damping <= 0.0:
+        return float(prev)
+    prev = max(float(prev), 1e-12)
+    new = max(float(new), 1e-12)
+    return float(math.exp((1.0 - damping) * math.log(prev) + damping * math.log(new)))
+
+
+class _UniformCtx:
+    """Device-side operands of one grouped-scalar solve (shared by VAMP and polish)."""
+
+    def __init__(self, W, scale_full, zero_full, maxq, V, Vh, S, Vs):
+        self.dev = W.device
+        self.W = W
+        self.B, self.n = W.shape
+        self.R = int(S.numel())
+        self.scale = scale_full
+        self.zero = zero_full
+        self.ld_p, self.gshift = ops.group_layout(scale_full, self.n)
+        if zero_full.shape != scale_full.shape or zero_full.stride(0) != self.ld_p:
+            raise ValueError("scale_full and zero_full must have the same shape and layout")
+        self.maxq = int(maxq)
+        self.V = V
+        self.Vh = Vh
+        self.S = S
+        self.Vs = Vs
+        self.VsT = Vs.t().contiguous()
+        self.Y_u = ops.gemm_nt(W, self.VsT)
+
+    def err(self, x, out=None, tmp=None):
+        return ops.rankspace_error(self.Y_u, x, self.VsT, tmp=tmp, out=out)
+
+    def nearest(self, x, q_out, x_out):
+        call("mpq_uniform_nearest", ptr(x), x.stride(0), ptr(self.scale), ptr(self.zero), self.ld_p, self.gshift,
+             self.B, self.n, self.maxq, ptr(q_out), ptr(x_out), x_out.stride(0))
+
+
+def _f32c(t: torch.Tensor, device) -> torch.Tensor:
+    return t.to(device=device, dtype=torch.float32).contiguous()
+
+
+@torch.inference_mode()
+def scalar_greedy_cd(ctx: _UniformCtx, x_init: torch.Tensor, gram_full: torch.Tensor, *, sweeps: int,
+                     accept_tol: float = 0.0) -> Tuple[torch.Tensor, Dict[str, Any]]:
+    """Raw-Hessian scalar greedy CD (mpq/polish/triton_scalar_cd.py:164-307) in 128-column blocks.
+
+    Returns (x_polished, stats).  Each sweep orders columns by the greedy gain, then for every
+    block of 128 columns runs the per-row sequential decisions (mpq_cd_block) and applies the
+    block's accepted steps to the right-hand side with one GEMM.
+    """
+    dev, B, n, R = ctx.dev, ctx.B, ctx.n, ctx.R
+    x_work = x_init.clone()
+    res_u = ops.gemm_nt(x_work, ctx.VsT)
+    res_norm = torch.empty(B, device=dev, dtype=torch.float32)
+    call("mpq_residual", ptr(ctx.Y_u), ptr(res_u), B, R, res_u.stride(0), ptr(res_norm))
+    rhs = ops.gemm_nt(res_u, ctx.Vs)  # residual_u @ Vs^T  (B x n)
+    del res_u
+    diag = torch.empty(n, device=dev, dtype=torch.float32)
+    diag_inv = torch.empty(n, device=dev, dtype=torch.float32)
+    call("mpq_cd_diag", ptr(ctx.Vs), n, R, ctx.Vs.stride(0), ptr(diag), ptr(diag_inv))
+    gain = torch.empty(n, device=dev, dtype=torch.float32)
+    order = torch.empty(n, device=dev, dtype=torch.int32)
+    HJ = torch.empty(128, n, device=dev, dtype=torch.float32)
+    Hsub = torch.empty(128, 128, device=dev, dtype=torch.float32)
+    delta = torch.empty(B, 128, device=dev, dtype=torch.float32)
+    accepted = torch.zeros(1, device=dev, dtype=torch.int32)
+    H = gram_full
+    for _ in range(max(int(sweeps), 0)):
+        call("mpq_cd_gain", ptr(rhs), B, n, rhs.stride(0), ptr(diag_inv), ptr(gain))
+        call("mpq_argsort_desc", ptr(gain), n, ptr(order))
+        for c0 in range(0, n, 128):
+            K = min(128, n - c0)
+            call("mpq_cd_gather", ptr(H), H.stride(0), n, ptr(order), c0, K, ptr(HJ), ptr(Hsub))
+            call("mpq_cd_block", ptr(x_work), x_work.stride(0), ptr(rhs), rhs.stride(0), ptr(ctx.scale),
+                 ptr(ctx.zero), ctx.ld_p, ctx.gshift, ptr(diag), ptr(diag_inv), ptr(order), c0, K, ptr(Hsub),
+                 ptr(res_norm), ptr(delta), ptr(accepted), B, ctx.maxq, float(accept_tol))
+            ops.gemm_nn(delta[:, :K], HJ[:K], out=rhs, alpha=-1.0, beta=1.0)
+    return x_work, {"accepted_updates": float(accepted.item())}
+
+
+@torch.inference_mode()
+def polish_uniform_rankspace(
+    *,
+    x_init: torch.Tensor,
+    Y_u: torch.Tensor,
+    Vs: torch.Tensor,
+    scale_full: torch.Tensor,
+    zero_full: torch.Tensor,
+    maxq: int,
+    sweeps: int,
+    polish_mode: str,
+    topk_values: Optional[torch.Tensor] = None,
+    topk_q: Optional[torch.Tensor] = None,
+    compile_block_cd: bool = True,
+    block_cd_backend: Optional[str] = None,
+    gram_full: Optional[torch.Tensor] = None,
+    order_mode: str = "greedy_gain",
+    raw_target: Optional[torch.Tensor] = None,
+    raw_gram: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Dict[str, Any]]:
+    """mpq/solver.py:260-366 on CUDA: the raw-Hessian greedy scalar CD, then re-rounding."""
+    mode = _resolve_polish_mode(sweeps=int(sweeps), mode=str(polish_mode))
+    dev = x_init.device
+    x_work = _f32c(x_init, dev)
+    B, n = x_work.shape
+    R = int(Vs.shape[1])
+    scale_full = _f32c(scale_full, dev)
+    zero_full = _f32c(zero_full, dev)
+    Vs = _f32c(Vs, dev)
+    VsT = Vs.t().contiguous()
+    Y_u = _f32c(Y_u, dev)
+    ld_p, gshift = ops.group_layout(scale_full, n)
+    q_out = torch.empty(B, n, device=dev, dtype=torch.uint8)
+    x_out = torch.empty(B, n, device=dev, dtype=torch.float32)
+
+    def finish(x, stats):
+        call("mpq_uniform_nearest", ptr(x), x.stride(0), ptr(scale_full), ptr(zero_full), ld_p, gshift, B, n,
+             int(maxq), ptr(q_out), ptr(x_out), x_out.stride(0))
+        err = ops.rankspace_error(Y_u, x_out, VsT)
+        return q_out.to(torch.int32), x_out, err, stats
+
+    if mode == "none" or Vs.numel() == 0:
+        return finish(x_work, {"accepted_updates": 0.0})
+    if mode == "topk_block_cd":
+        raise NotImplementedError("topk_block_cd uniform polish is not built yet")
+    if gram_full is None:
+        raise NotImplementedError("the uniform polish needs gram_full (the raw Hessian)")
+    ctx = _UniformCtx.__new__(_UniformCtx)
+    ctx.dev, ctx.B, ctx.n, ctx.R = dev, B, n, R
+    ctx.scale, ctx.zero, ctx.ld_p, ctx.gshift, ctx.maxq = scale_full, zero_full, ld_p, gshift, int(maxq)
+    ctx.Vs, ctx.VsT, ctx.Y_u = Vs, VsT, Y_u
+    x_pol, st = scalar_greedy_cd(ctx, x_work, _f32c(gram_full, dev), sweeps=int(sweeps))
+    st = dict(st)
+    st["block_cd_backend"] = "cuda"
+    return finish(x_pol, st)
+
+
+@torch.inference_mode()
+def solve_uniform_rankspace_vamp(
+    *,
+    W: torch.Tensor,
+    x_rtn: torch.Tensor,
+    scale_full: torch.Tensor,
+    zero_full: torch.Tensor,
+    maxq: int,
+    V: torch.Tensor,
+    Vh: torch.Tensor,
+    S: torch.Tensor,
+    Vs: torch.Tensor,
+    cfg: UniformVampConfig,
+    gram_full: Optional[torch.Tensor] = None,
+    obs_precision_init: Optional[float] = None,
+    log_stats: bool = True,
+    debug_out: Optional[Dict[str, Any]] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, Dict[str, Any]]:
+    """Scalar uniform exact-full VAMP in rank space (MMSE x1) with the greedy CD polish.
+
+    mpq/solver.py:426-830.  Returns (q_int int32 (B, n), x_final (B, n), final_err (B,),
+    rtn_err (B,), stats).
+    """
+    if not W.is_cuda:
+        raise ValueError("solve_uniform_rankspace_vamp requires CUDA tensors (there is no CPU path)")
+    dev = W.device
+    W = _f32c(W, dev)
+    x_rtn = _f32c(x_rtn, dev)
+    scale_full = _f32c(scale_full, dev)
+    zero_full = _f32c(zero_full, dev)
+    V, Vh, S, Vs = (_f32c(t, dev) for t in (V, Vh, S, Vs))
+    maxq = int(maxq)
+    iters = max(int(cfg.iters), 0)
+    damping = float(cfg.damping)
+    prior_tau = float(cfg.prior_tau)
+    final_decision = str(cfg.final_decision or "map").strip().lower()
+    init_from = str(cfg.init_from or "rtn").strip().lower()
+    if final_decision != "map":
+        raise ValueError(f"unsupported final_decision={cfg.final_decision!r} (the CUDA path implements 'map')")
+    B, n = W.shape
+    R = int(S.numel())
+    if R == 0:
+        raise ValueError("rank-0 spectra are not supported by the CUDA solver")
+    ctx = _UniformCtx(W, scale_full, zero_full, maxq, V, Vh, S, Vs)
+    f32 = dict(device=dev, dtype=torch.float32)
+
+    if init_from == "zero":
+        r1 = torch.zeros(B, n, **f32)
+    elif init_from == "float":
+        r1 = W.clone()
+    elif init_from == "rtn":
+        r1 = x_rtn.clone()
+    else:
+        raise ValueError(f"unknown init_from={init_from!r} (expected 'rtn', 'float', or 'zero').")
+
+    gamma1 = torch.empty(B, **f32)
+    call("mpq_gamma_init", ptr(W), ptr(x_rtn), B, n, W.stride(0), float(cfg.gamma_start), ptr(gamma1))
+    tmpBR = torch.empty(B, R, **f32)
+    if obs_precision_init is not None and float(obs_precision_init) > 0.0:
+        obs_initial = float(obs_precision_init)
+    elif float(cfg.obs_precision) > 0.0:
+        obs_initial = float(cfg.obs_precision)
+    else:
+        e = ctx.err(x_rtn, tmp=tmpBR)
+        obs_initial = 1.0 / max(float(ops.mean_rows(e).item()) / R, 1e-12)
+    obs = float(obs_initial)
+    em_active = bool(cfg.em_obs_precision) and float(cfg.obs_precision) <= 0.0
+
+    def args_uniform(r, g):
+        return (ptr(r), r.stride(0), ptr(W), W.stride(0), ptr(scale_full), ptr(zero_full), ctx.ld_p, ctx.gshift,
+                ptr(g), B, n, maxq, prior_tau)
+
+    def hard_state(r, g, q_out, x_out, err_out):
+        call("mpq_uniform_map_decision", *args_uniform(r, g), ptr(q_out), ptr(x_out), x_out.stride(0))
+        ctx.err(x_out, out=err_out, tmp=tmpBR)
+
+    best_q = torch.empty(B, n, device=dev, dtype=torch.uint8)
+    best_x = torch.empty(B, n, **f32)
+    best_err = torch.empty(B, **f32)
+    cur_q = torch.empty_like(best_q)
+    cur_x = torch.empty_like(best_x)
+    cur_err = torch.empty_like(best_err)
+    hard_state(r1, gamma1, best_q, best_x, best_err)
+    best_err_mean = float(ops.mean_rows(best_err).item())
+    best_r1 = r1.clone()
+    best_g1 = gamma1.clone()
+    best_obs = obs
+
+    x1 = torch.empty(B, n, **f32)  # posterior mean, later reused for the linear-module delta
+    r2 = torch.empty(B, n, **f32)
+    r2_prev = torch.empty(B, n, **f32)
+    have_prev = False
+    u = torch.empty(B, R, **f32)
+    rows = {k: torch.empty(B, **f32) for k in ("var", "g1w", "a1", "eta1", "g2n", "g2", "g2p", "a2", "eta2", "g1n",
+                                               "g1next", "trace", "resid")}
+    flags = torch.zeros(8, device=dev, dtype=torch.int32)
+    means = torch.zeros(2, **f32)
+    factor = max(float(cfg.gamma_retry_factor), 1.000001)
+    retry_steps = max(int(cfg.gamma_retry_steps), 0)
+    alpha1_retry_count = 0
+    alpha2_clip_count = 0
+    gamma2_invalid_count = 0
+    obs_values = []
+    best_iter_idx = -1
+    stop_iter_idx = -1
+
+    for it in range(iters):
+        rows["g1w"].copy_(gamma1)
+        for retry_idx in range(retry_steps + 1):
+            final = retry_idx >= retry_steps
+            call("mpq_uniform_mmse", *args_uniform(r1, rows["g1w"]), ptr(x1), x1.stride(0), None, None, None,
+                 ptr(rows["var"]))
+            flags.zero_()
+            call("mpq_vamp_rows", ptr(rows["var"]), ptr(gamma1), ptr(rows["g1w"]), ptr(rows["a1"]), ptr(rows["eta1"]),
+                 ptr(rows["g2n"]), ptr(rows["g2"]), ptr(rows["g2p"]) if (have_prev and damping < 1.0) else None,
+                 ptr(rows["a2"]), ptr(rows["eta2"]), ptr(rows["g1n"]), ptr(rows["g1next"]), ptr(rows["trace"]),
+                 ptr(flags), ptr(S), B, n, R, obs, damping, int(final))
+            fl = flags.tolist()
+            if fl[0] == 0:
+                break
+            if final:
+                if fl[1] > 0:
+                    raise RuntimeError(f"alpha1 invalid: expected all in ({ALPHA_EPS}, 1-{ALPHA_EPS}).")
+                break
+            alpha1_retry_count += int(fl[0])
+            call("mpq_gamma_retry", ptr(rows["g1w"]), ptr(rows["var"]), B, n, factor)
+        if fl[2] > 0 or fl[3] > 0:
+            gamma2_invalid_count += 1
+            continue
+        alpha2_clip_count += int(fl[4])
+        call("mpq_vamp_r2", ptr(x1), ptr(r1), ptr(r2_prev) if (have_prev and damping < 1.0) else None, ptr(r2),
+             ptr(rows["eta1"]), ptr(rows["g1w"]), ptr(rows["g2n"]), B, n, r2.stride(0), damping)
+        P = ops.gemm_nt(r2, Vh, tmpBR)  # r2 @ V
+        call("mpq_linear_epilogue", ptr(P), ptr(ctx.Y_u), ptr(S), ptr(rows["g2"]), obs, B, R, P.stride(0), ptr(u),
+             ptr(rows["resid"]))
+        D = ops.gemm_nt(u, V, x1)  # (resid * coeff) @ Vh
+        call("mpq_vamp_r1", ptr(D), ptr(r2), ptr(r1), ptr(rows["eta2"]), ptr(rows["g2"]), ptr(rows["g1n"]), B, n,
+             r1.stride(0), damping)
+        gamma1.copy_(rows["g1next"])
+        r2, r2_prev = r2_prev, r2
+        rows["g2p"].copy_(rows["g2"])
+        have_prev = True
+        if em_active:
+            ops.mean_rows(rows["resid"], rows["trace"], out=means[0:1])
+        hard_state(r1, gamma1, cur_q, cur_x, cur_err)
+        ops.mean_rows(cur_err, out=means[1:2])
+        em_mean, cur_err_mean = means.tolist()
+        if em_active:
+            beta_new = float(R / max(em_mean, 1e-12))
+            beta = _log_damp_scalar(max(obs, 1e-12), beta_new, float(cfg.em_obs_precision_damping))
+            obs = float(min(max(beta, float(cfg.em_obs_precision_min)), float(cfg.em_obs_precision_max)))
+        obs_values.append(obs)
+        tol = max(1e-10, abs(best_err_mean) * 1e-8)
+        if cur_err_mean + tol < best_err_mean:
+            best_q, cur_q = cur_q, best_q
+            best_x, cur_x = cur_x, best_x
+            best_err, cur_err = cur_err, best_err
+            best_err_mean = cur_err_mean
+            best_r1.copy_(r1)
+            best_g1.copy_(gamma1)
+            best_obs = obs
+            best_iter_idx = it
+        else:
+            r1.copy_(best_r1)
+            gamma1.copy_(best_g1)
+            obs = float(best_obs)
+            stop_iter_idx = it
+            break
+
+    q_final, x_final, err_final = best_q, best_x, best_err
+    polish_sweeps = max(int(cfg.polish_sweeps), 0)
+    polish_mode = _resolve_polish_mode(sweeps=polish_sweeps, mode=str(getattr(cfg, "polish_mode", "block_cd")))
+    polish_stats: Dict[str, Any] = {}
+    polish_updates = 0.0
+    polish_gain = 0.0
+    if polish_mode != "none":
+        if polish_mode != "block_cd":
+            raise NotImplementedError("topk_block_cd uniform polish is not built yet")
+        if gram_full is None:
+            raise NotImplementedError("the uniform polish needs gram_full (the raw Hessian)")
+        x_pol, polish_stats = scalar_greedy_cd(ctx, x_final, _f32c(gram_full, dev), sweeps=polish_sweeps)
+        q_pol = torch.empty_like(q_final)
+        x_out = torch.empty_like(x_final)
+        ctx.nearest(x_pol, q_pol, x_out)
+        err_after = ctx.err(x_out, tmp=tmpBR)
+        err_before = err_final.clone()
+        improved = torch.zeros(1, device=dev, dtype=torch.int32)
+        call("mpq_polish_merge", ptr(err_after), ptr(err_final), ptr(err_before), ptr(x_out), ptr(x_final),
+             ptr(q_pol), ptr(q_final), B, n, x_final.stride(0), ptr(improved))
+        polish_updates = float(polish_stats.get("accepted_updates", 0.0))
+        polish_stats = dict(polish_stats)
+        polish_stats["block_cd_backend"] = "cuda"
+        polish_stats["rows_improved"] = int(improved.item())
+
+    rtn_err = ctx.err(x_rtn, tmp=tmpBR)
+    if debug_out is not None:
+        debug_out["solver"] = "uniform_exact_vamp"
+        g64 = gamma1.double()
+        debug_out["gamma1_sum"] = float(g64.sum())
+        debug_out["gamma1_count"] = int(g64.numel())
+        debug_out["gamma1_min"] = float(g64.min()) if B else 0.0
+        debug_out["gamma1_max"] = float(g64.max()) if B else 0.0
+        if bool(debug_out.get("capture_r1", False)):
+            debug_out["r1"] = r1.detach().cpu()
+        debug_out["gamma1"] = gamma1.detach().cpu()
+    stats: Dict[str, Any] = {
+        "solver": "uniform_exact_vamp",
+        "iters": int(iters),
+        "rank": int(R),
+        "init_from": init_from,
+        "damping": damping,
+        "prior_tau": prior_tau,
+        "vamp_backend": "cuda",
+        "vamp_backend_used": "cuda",
+        "gamma_start": float(cfg.gamma_start),
+        "gamma_retry_factor": float(factor),
+        "gamma_retry_steps": int(retry_steps),
+        "obs_precision_initial": float(obs_initial),
+        "obs_precision_final": float(obs),
+        "obs_precision_mean": float(sum(obs_values) / len(obs_values)) if obs_values else float(obs),
+        "alpha1_retry_count": int(alpha1_retry_count),
+        "alpha2_clip_count": int(alpha2_clip_count),
+        "gamma2_invalid_count": int(gamma2_invalid_count),
+        "final_decision": final_decision,
+        "best_iterate_enabled": True,
+        "best_iter": int(best_iter_idx),
+        "stop_iter": int(stop_iter_idx),
+        "best_rankspace_error_mean": float(best_err_mean),
+        "polish_sweeps": int(polish_sweeps),
+        "polish_mode": polish_mode,
+        "polish_gain": float(polish_gain),
+        "polish_updates": float(polish_updates),
+        "polish_trace": polish_stats,
+        "block_cd_backend": "cuda",
+        "rankspace_error_mean": float(ops.mean_rows(err_final).item()),
+        "rtn_rankspace_error_mean": float(ops.mean_rows(rtn_err).item()),
+    }
+    return q_final.to(torch.int32), x_final, err_final, rtn_err, stats

@@ -1,0 +1,206 @@
+"""Generate golden input/output vectors by running the REFERENCE implementation (poseidonchan/MPQ).
+
+Run in a container where the reference source tree is importable (pass its path with
+``--reference``).  The outputs are small ``.npz`` fixtures committed next to this script;
+tests read only the fixtures, never the reference tree.
+
+Where the reference calls into third-party code that is not vendored (GPTQModel's
+``Quantizer.find_params``; the CUDA dispatch of the uniform polish), this script passes the
+same restatements the oracle and the product use, and says so in the fixture metadata.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+class MinMaxQuantizer:
+    """Asymmetric per-row min-max grid: the restatement of GPTQModel's find_params."""
+
+    def __init__(self, bits: int):
+        self.maxq = 2 ** bits - 1
+
+    def find_params(self, x, weight=True):
+        zero = torch.zeros(x.shape[0], dtype=x.dtype)
+        xmin = torch.minimum(x.min(1)[0], zero)
+        xmax = torch.maximum(x.max(1)[0], zero)
+        tmp = (xmin == 0) & (xmax == 0)
+        xmin[tmp] = -1
+        xmax[tmp] = 1
+        self.scale = ((xmax - xmin) / self.maxq).unsqueeze(1)
+        self.zero = torch.round(-xmin / self.scale.squeeze(1)).unsqueeze(1)
+
+
+def synth_layer(m, n, seed, calib_mult=4):
+    g = torch.Generator().manual_seed(seed)
+    W = torch.randn(m, n, generator=g) * 0.02
+    s = torch.exp(torch.randn(n, generator=g))
+    X = torch.randn(calib_mult * n, n, generator=g) * s.sqrt()
+    H = X.T @ X / X.shape[0]
+    H = H + 0.01 * H.diagonal().mean() * torch.eye(n)
+    return W, H
+
+
+def gen_uniform_denoise(out):
+    from mpq.priors.uniform import discrete_uniform_mmse, nearest_atom_idx, dequant_from_q
+    g = torch.Generator().manual_seed(11)
+    cases = {}
+    for name, (B, n, maxq, tau) in {"q4": (6, 256, 15, 0.2), "q3": (5, 128, 7, 0.25), "q4_noprior": (4, 128, 15, 0.0)}.items():
+        W = torch.randn(B, n, generator=g) * 0.02
+        scale = (torch.rand(B, n // 64, generator=g) * 0.01 + 0.002).repeat_interleave(64, 1)
+        zero = torch.randint(0, maxq + 1, (B, n // 64), generator=g).float().repeat_interleave(64, 1)
+        r1 = W + torch.randn(B, n, generator=g) * 0.01
+        # exact ties: r1 halfway between two atoms, center far away
+        r1[0, :16] = scale[0, :16] * (torch.arange(16).float() % maxq + 0.5 - zero[0, :16])
+        gamma = torch.rand(B, 1, generator=g) * 2e4 + 1e3
+        post = discrete_uniform_mmse(r1=r1, gamma1=gamma, scale_full=scale, zero_full=zero, maxq=maxq,
+                                     prior_center=W, prior_tau=tau, need_stats=False, vamp_backend="eager")
+        q = nearest_atom_idx(x=post["map_value"], scale_full=scale, zero_full=zero, maxq=maxq)
+        x = dequant_from_q(q_int=q, scale_full=scale, zero_full=zero)
+        for k, v in dict(r1=r1, W=W, scale=scale, zero=zero, gamma=gamma, mean=post["mean"], var=post["var"],
+                         map_idx=post["map_idx"], map_value=post["map_value"], alpha1=post["alpha1"], q=q, x=x).items():
+            cases[f"{name}/{k}"] = _np(v)
+        cases[f"{name}/maxq"] = np.array(maxq)
+        cases[f"{name}/tau"] = np.array(tau, dtype=np.float64)
+    # rounding ties of nearest_atom_idx: x/scale + zero exactly k + 0.5
+    scale = torch.full((2, 32), 0.5)
+    zero = torch.full((2, 32), 3.0)
+    x = (torch.arange(64).float().view(2, 32) * 0.25 - 4.0)
+    cases["ties/x"] = _np(x)
+    cases["ties/scale"] = _np(scale)
+    cases["ties/zero"] = _np(zero)
+    cases["ties/q"] = _np(nearest_atom_idx(x=x, scale_full=scale, zero_full=zero, maxq=7))
+    np.savez_compressed(out / "uniform_denoise.npz", **cases)
+
+
+def gen_linear(out):
+    from mpq.linear import linear_mmse_exact, em_update_obs_precision_rankspace, vamp_rankspace_error
+    W, H = synth_layer(8, 64, 3)
+    lam, V = torch.linalg.eigh(H)
+    lam = lam.flip(0).clamp_min(1e-6 * float(lam.max()))
+    V = V.flip(1).contiguous()
+    S = lam.sqrt()
+    Vs = V * S
+    g = torch.Generator().manual_seed(5)
+    r2 = W + torch.randn(W.shape, generator=g) * 0.005
+    gamma2 = torch.rand(8, 1, generator=g) * 1e4 + 1e3
+    Y_u = W @ Vs
+    obs = 1234.5
+    x2, a2, res = linear_mmse_exact(r2, gamma2, Y_u=Y_u, V=V, Vh=V.T.contiguous(), S=S, obs_precision=obs)
+    beta = em_update_obs_precision_rankspace(residual_u=res, gamma2=gamma2, S=S, obs_precision=obs, num_obs=64)
+    err = vamp_rankspace_error(Y_u=Y_u, x=r2, Vs=Vs)
+    np.savez_compressed(out / "linear_mmse.npz", r2=_np(r2), gamma2=_np(gamma2), Y_u=_np(Y_u), V=_np(V), S=_np(S),
+                        Vs=_np(Vs), obs=np.array(obs), x2=_np(x2), alpha2=_np(a2), residual=_np(res),
+                        beta=np.array(beta), err=_np(err))
+
+
+def gen_scalar_cd(out):
+    from mpq.polish.triton_scalar_cd import uniform_scalar_diag_greedy_cd
+    W, H = synth_layer(12, 128, 7)
+    lam, V = torch.linalg.eigh(H)
+    lam = lam.flip(0).clamp_min(1e-6 * float(lam.max()))
+    V = V.flip(1).contiguous()
+    Vs = V * lam.sqrt()
+    maxq = 15
+    Wg = W.view(12, 2, 64)
+    mn, mx = Wg.amin(-1).clamp(max=0), Wg.amax(-1).clamp(min=0)
+    scale = ((mx - mn) / maxq).repeat_interleave(64, 1)
+    zero = torch.round(-mn / ((mx - mn) / maxq)).repeat_interleave(64, 1)
+    q = torch.clamp(torch.round(W / scale) + zero, 0, maxq)
+    x = scale * (q - zero)
+    Y_u = W @ Vs
+    xp, st = uniform_scalar_diag_greedy_cd(x=x, Y_u=Y_u, Vs=Vs, gram_full=H, scale=scale, zero=zero, maxq=maxq,
+                                           sweeps=3, update_backend="torch")
+    np.savez_compressed(out / "scalar_cd.npz", x=_np(x), Y_u=_np(Y_u), Vs=_np(Vs), H=_np(H), scale=_np(scale),
+                        zero=_np(zero), x_out=_np(xp), accepted=np.array(st["accepted_updates"]))
+
+
+def _install_gpu_polish_semantics():
+    """Route the uniform polish through the raw-H greedy CD (the reference's CUDA dispatch,
+    mpq/solver.py:299-333) with the torch twin, since CUDA is absent in this container."""
+    import mpq.solver as S
+    from mpq.polish.triton_scalar_cd import uniform_scalar_diag_greedy_cd
+    from mpq.priors.uniform import nearest_atom_idx, dequant_from_q
+    from mpq.linear import vamp_rankspace_error
+
+    def polish(*, x_init, Y_u, Vs, scale_full, zero_full, maxq, sweeps, polish_mode, gram_full=None, **kw):
+        xp, st = uniform_scalar_diag_greedy_cd(x=x_init.float(), Y_u=Y_u, Vs=Vs, gram_full=gram_full,
+                                               scale=scale_full, zero=zero_full, maxq=maxq, sweeps=int(sweeps),
+                                               accept_tol=0.0, update_backend="torch")
+        q = nearest_atom_idx(x=xp, scale_full=scale_full, zero_full=zero_full, maxq=maxq).to(torch.int32)
+        xo = dequant_from_q(q_int=q, scale_full=scale_full, zero_full=zero_full)
+        return q, xo, vamp_rankspace_error(Y_u=Y_u, x=xo, Vs=Vs), dict(st, block_cd_backend="triton")
+
+    S.polish_uniform_rankspace = polish
+
+
+def gen_scalar_layer(out):
+    _install_gpu_polish_semantics()
+    from mpq.adapters.gptqmodel import run_mpq_quantization, GPTQAdapterConfig
+    from mpq.solver import UniformVampConfig
+    cases = {}
+    for name, (m, n, bits, block_rows, iters) in {"a": (48, 256, 4, 16, 20), "b": (32, 128, 3, 32, 16)}.items():
+        W, H = synth_layer(m, n, 100 + m)
+        qcfg = types.SimpleNamespace(bits=bits, group_size=64, desc_act=False,
+                                     mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
+        cfg = UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto")
+        acfg = GPTQAdapterConfig(block_rows=block_rows)
+        Q, q_int, scale, zero, g_idx, _, st = run_mpq_quantization(
+            W=W, H=2.0 * H, quantizer=MinMaxQuantizer(bits), qcfg=qcfg, module_name=f"golden.{name}",
+            vamp_cfg=cfg, adapter_cfg=acfg)
+        for k, v in dict(W=W, H=H, Q=Q, q_int=q_int, scale=scale, zero=zero).items():
+            cases[f"{name}/{k}"] = _np(v)
+        cases[f"{name}/meta"] = np.array(json.dumps(dict(bits=bits, group_size=64, block_rows=block_rows, iters=iters,
+                                                          obs_init=st["obs_precision_initial"],
+                                                          obs_final=st["obs_precision_final"],
+                                                          raw_objective=st["raw_objective_mean_final"],
+                                                          best_iters=[b["best_iter"] for b in st["block_stats"]],
+                                                          stop_iters=[b["stop_iter"] for b in st["block_stats"]],
+                                                          polish_updates=[b["polish_updates"] for b in st["block_stats"]])))
+    np.savez_compressed(out / "scalar_layer.npz", **cases)
+
+
+def gen_rotation(out):
+    from mpq.rotation import apply_right_block_hadamard, apply_right_block_hadamard_inverse, sample_rademacher_signs
+    from mpq.utils import stable_seed
+    g = torch.Generator().manual_seed(9)
+    M = torch.randn(6, 256, generator=g)
+    signs = sample_rademacher_signs(width=256, key="golden.rot:full", seed=0, device=torch.device("cpu"))
+    R = apply_right_block_hadamard(M, signs=signs, had_dim=64)
+    Ri = apply_right_block_hadamard_inverse(R, signs=signs, had_dim=64)
+    seeds = np.array([stable_seed(k, base_seed=b) for k, b in [("a", 0), ("model.layers.0.q_proj:full", 0), ("x", 7)]])
+    np.savez_compressed(out / "rotation.npz", M=_np(M), signs=_np(signs), R=_np(R), Ri=_np(Ri), seeds=seeds)
+
+
+GENERATORS = {"uniform_denoise": gen_uniform_denoise, "linear": gen_linear, "scalar_cd": gen_scalar_cd,
+              "scalar_layer": gen_scalar_layer, "rotation": gen_rotation}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the reference source tree (poseidonchan/MPQ)")
+    ap.add_argument("--only", default="")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    torch.set_num_threads(8)
+    for name, fn in GENERATORS.items():
+        if args.only and name not in args.only.split(","):
+            continue
+        fn(HERE)
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    main()

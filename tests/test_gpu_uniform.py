@@ -1,0 +1,239 @@
+"""GPU parity of the grouped-scalar kernels against the CPU oracle (all calls go through the C-ABI)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import layer as OL
+from oracle import uniform_vamp as OU
+
+pytestmark = pytest.mark.gpu
+
+
+def _rng(seed):
+    return np.random.default_rng(seed)
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _uniform_case(seed, B, n, maxq, group):
+    r = _rng(seed)
+    W = (r.standard_normal((B, n)) * 0.02).astype(np.float32)
+    G = n // group
+    scale_g = (r.random((B, G)) * 0.01 + 0.002).astype(np.float32)
+    zero_g = r.integers(0, maxq + 1, (B, G)).astype(np.float32)
+    r1 = (W + r.standard_normal((B, n)).astype(np.float32) * 0.01).astype(np.float32)
+    sf = np.repeat(scale_g, group, 1)
+    zf = np.repeat(zero_g, group, 1)
+    # exact ties between neighbouring atoms
+    r1[0, :16] = sf[0, :16] * (np.arange(16, dtype=np.float32) % maxq + np.float32(0.5) - zf[0, :16])
+    gamma = (r.random((B, 1)) * 2e4 + 1e3).astype(np.float32)
+    return W, scale_g, zero_g, sf, zf, r1, gamma
+
+
+@pytest.mark.parametrize("maxq,tau,grouped", [(15, 0.2, True), (15, 0.2, False), (7, 0.25, True), (3, 0.0, True),
+                                              (1, 0.2, True), (31, 0.2, True)])
+def test_uniform_mmse_matches_oracle(cuda_dev, maxq, tau, grouped):
+    from mpq_b200._lib import call, ptr
+    B, n, group = 9, 384, 64
+    W, sg, zg, sf, zf, r1, gamma = _uniform_case(1 + maxq, B, n, maxq, group)
+    ref = OU.discrete_uniform_mmse(r1=r1, gamma1=gamma, scale_full=sf, zero_full=zf, maxq=maxq, prior_center=W,
+                                   prior_tau=tau)
+    d = lambda a: _t(a, cuda_dev)
+    s_in, z_in = (d(sg), d(zg)) if grouped else (d(sf), d(zf))
+    gshift = 6 if grouped else 0
+    mean = torch.empty(B, n, device=cuda_dev)
+    var = torch.empty(B, n, device=cuda_dev)
+    mapv = torch.empty(B, n, device=cuda_dev)
+    mapi = torch.empty(B, n, device=cuda_dev, dtype=torch.uint8)
+    vsum = torch.empty(B, device=cuda_dev)
+    r1d, Wd, gd = d(r1), d(W), d(gamma[:, 0])
+    call("mpq_uniform_mmse", ptr(r1d), n, ptr(Wd), n, ptr(s_in), ptr(z_in), s_in.stride(0), gshift, ptr(gd), B, n,
+         maxq, tau, ptr(mean), n, ptr(var), ptr(mapv), ptr(mapi), ptr(vsum))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(mapi.cpu().numpy(), ref["map_idx"])          # bit-exact codes
+    np.testing.assert_array_equal(mapv.cpu().numpy(), ref["map_value"])
+    np.testing.assert_allclose(mean.cpu().numpy(), ref["mean"], rtol=2e-5, atol=1e-8)
+    np.testing.assert_allclose(var.cpu().numpy(), ref["var"], rtol=2e-3, atol=1e-10)
+    np.testing.assert_allclose(gamma[:, 0] * vsum.cpu().numpy() / n, ref["alpha1"][:, 0], rtol=1e-4)
+    # the MAP hard decision
+    q = torch.empty(B, n, device=cuda_dev, dtype=torch.uint8)
+    x = torch.empty(B, n, device=cuda_dev)
+    call("mpq_uniform_map_decision", ptr(r1d), n, ptr(Wd), n, ptr(s_in), ptr(z_in), s_in.stride(0), gshift, ptr(gd),
+         B, n, maxq, tau, ptr(q), ptr(x), n)
+    rq, rx = OU.uniform_hard_decision(x_mean=ref["mean"], x_map=ref["map_value"], scale_full=sf, zero_full=zf,
+                                      maxq=maxq)
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+    np.testing.assert_array_equal(x.cpu().numpy(), rx)
+
+
+def test_uniform_mmse_golden_reference_vectors(cuda_dev, golden_dir):
+    """The kernel against vectors produced by the reference itself."""
+    from mpq_b200._lib import call, ptr
+    z = np.load(golden_dir / "uniform_denoise.npz")
+    for case in ("q4", "q3", "q4_noprior"):
+        g = lambda k: z[f"{case}/{k}"]
+        B, n = g("r1").shape
+        d = lambda a: _t(a.astype(np.float32), cuda_dev)
+        mean = torch.empty(B, n, device=cuda_dev)
+        mapi = torch.empty(B, n, device=cuda_dev, dtype=torch.uint8)
+        vsum = torch.empty(B, device=cuda_dev)
+        sc, ze = d(g("scale")), d(g("zero"))
+        call("mpq_uniform_mmse", ptr(d(g("r1"))), n, ptr(d(g("W"))), n, ptr(sc), ptr(ze), n, 0,
+             ptr(d(g("gamma")[:, 0])), B, n, int(g("maxq")), float(g("tau")), ptr(mean), n, None, None, ptr(mapi),
+             ptr(vsum))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(mapi.cpu().numpy().astype(np.int64), g("map_idx"))
+        np.testing.assert_allclose(mean.cpu().numpy(), g("mean"), rtol=2e-5, atol=1e-8)
+
+
+def test_nearest_rtn_minmax_hadamard_bit_exact(cuda_dev):
+    from mpq_b200._lib import call, ptr
+    r = _rng(5)
+    B, n, group, maxq = 7, 512, 128, 15
+    W = (r.standard_normal((B, n)) * 0.03).astype(np.float32)
+    W[2, :128] = 0.0  # all-zero group -> [-1, 1] grid
+    sg_ref = np.empty((B, n // group), np.float32)
+    zg_ref = np.empty_like(sg_ref)
+    for g in range(n // group):
+        s, z = OL.find_params_minmax(W[:, g * group:(g + 1) * group], maxq)
+        sg_ref[:, g], zg_ref[:, g] = s[:, 0], z[:, 0]
+    Wd = _t(W, cuda_dev)
+    sg = torch.empty(B, n // group, device=cuda_dev)
+    zg = torch.empty_like(sg)
+    call("mpq_group_minmax", ptr(Wd), n, B, n, group, maxq, ptr(sg), ptr(zg), sg.stride(0))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(sg.cpu().numpy(), sg_ref)
+    np.testing.assert_array_equal(zg.cpu().numpy(), zg_ref)
+    sf, zf = np.repeat(sg_ref, group, 1), np.repeat(zg_ref, group, 1)
+    # RTN: round(W/s) + z
+    x = torch.empty(B, n, device=cuda_dev)
+    q = torch.empty(B, n, device=cuda_dev, dtype=torch.uint8)
+    call("mpq_uniform_rtn", ptr(Wd), n, ptr(sg), ptr(zg), sg.stride(0), 7, B, n, maxq, ptr(q), ptr(x), n)
+    qr = np.clip(np.round(W / sf) + zf, 0, maxq).astype(np.float32)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(q.cpu().numpy(), qr.astype(np.uint8))
+    np.testing.assert_array_equal(x.cpu().numpy(), (sf * (qr - zf)).astype(np.float32))
+    # nearest_atom_idx with round-half-even ties
+    xt = (np.arange(B * n, dtype=np.float32).reshape(B, n) % 37 - 18) * np.float32(0.25) * sf
+    call("mpq_uniform_nearest", ptr(_t(xt, cuda_dev)), n, ptr(sg), ptr(zg), sg.stride(0), 7, B, n, maxq, ptr(q),
+         ptr(x), n)
+    rq = OU.nearest_atom_idx(x=xt, scale_full=sf, zero_full=zf, maxq=maxq)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(q.cpu().numpy(), rq.astype(np.uint8))
+    # block Hadamard rotation and its inverse (bit-exact against the reference butterfly order)
+    from mpq_b200.rotation import apply_right_block_hadamard, apply_right_block_hadamard_inverse
+    signs = OL.rademacher_signs_torch(n, "test:full", 0)
+    for had in (64, 512):
+        R = apply_right_block_hadamard(Wd, signs=_t(signs, cuda_dev), had_dim=had)
+        np.testing.assert_array_equal(R.cpu().numpy(), OL.right_block_hadamard(W, signs, had))
+        Ri = apply_right_block_hadamard_inverse(R, signs=_t(signs, cuda_dev), had_dim=had)
+        np.testing.assert_array_equal(Ri.cpu().numpy(), OL.right_block_hadamard_inverse(R.cpu().numpy(), signs, had))
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 512), (37, 91, 300), (1, 5, 7)])
+def test_gemm_f32(cuda_dev, M, N, K):
+    from mpq_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(M + N + K)
+    A = torch.randn(M, K, generator=g)
+    Bt = torch.randn(N, K, generator=g)
+    Bn = torch.randn(K, N, generator=g)
+    C = ops.gemm_nt(A.to(cuda_dev), Bt.to(cuda_dev)).cpu()
+    torch.testing.assert_close(C, A.double().matmul(Bt.double().T).float(), rtol=1e-5, atol=1e-4)
+    C0 = torch.randn(M, N, generator=g)
+    C2 = ops.gemm_nn(A.to(cuda_dev), Bn.to(cuda_dev), out=C0.clone().to(cuda_dev), alpha=-1.0, beta=1.0).cpu()
+    torch.testing.assert_close(C2, (C0.double() - A.double() @ Bn.double()).float(), rtol=1e-5, atol=1e-4)
+
+
+def _layer_fixture(m, n, seed):
+    r = _rng(seed)
+    W = (r.standard_normal((m, n)) * 0.02).astype(np.float32)
+    s = np.exp(r.standard_normal(n)).astype(np.float32)
+    X = (r.standard_normal((4 * n, n)) * np.sqrt(s)).astype(np.float32)
+    H = OL.hessian_from_calibration(X)
+    return W, H
+
+
+def _eig(H):
+    lam, V, _ = OL.vamp_hessian_eigen(H)
+    S = np.sqrt(lam).astype(np.float32)
+    return V, S, (V * S[None, :]).astype(np.float32)
+
+
+def _rtn(W, maxq, group):
+    sg = np.empty((W.shape[0], W.shape[1] // group), np.float32)
+    zg = np.empty_like(sg)
+    for g in range(W.shape[1] // group):
+        s, z = OL.find_params_minmax(W[:, g * group:(g + 1) * group], maxq)
+        sg[:, g], zg[:, g] = s[:, 0], z[:, 0]
+    sf, zf = np.repeat(sg, group, 1), np.repeat(zg, group, 1)
+    q = np.clip(np.round(W / sf) + zf, 0, maxq).astype(np.float32)
+    return sg, zg, sf, zf, (sf * (q - zf)).astype(np.float32)
+
+
+def test_scalar_cd_matches_oracle(cuda_dev):
+    from mpq_b200 import solver as S
+    W, H = _layer_fixture(24, 320, 21)
+    V, Sv, Vs = _eig(H)
+    maxq, group = 15, 64
+    sg, zg, sf, zf, x0 = _rtn(W, maxq, group)
+    Y_u = W @ Vs
+    ref_x, ref_st = OU.uniform_scalar_diag_greedy_cd(x=x0, Y_u=Y_u, Vs=Vs, gram_full=H, scale=sf, zero=zf, maxq=maxq,
+                                                     sweeps=3)
+    d = lambda a: _t(a, cuda_dev)
+    q, x, err, st = S.polish_uniform_rankspace(x_init=d(x0), Y_u=d(Y_u), Vs=d(Vs), scale_full=d(sg), zero_full=d(zg),
+                                               maxq=maxq, sweeps=3, polish_mode="block_cd", gram_full=d(H))
+    ref_q = OU.nearest_atom_idx(x=ref_x, scale_full=sf, zero_full=zf, maxq=maxq)
+    agree = (q.cpu().numpy() == ref_q).mean()
+    assert agree >= 0.999, agree
+    assert abs(st["accepted_updates"] - ref_st["accepted_updates"]) <= 0.01 * ref_st["accepted_updates"] + 2
+
+
+@pytest.mark.parametrize("m,n,iters,maxq,group", [(64, 256, 20, 15, 64), (40, 192, 16, 7, 64), (1, 128, 10, 15, 128)])
+def test_solve_uniform_vamp_matches_oracle(cuda_dev, m, n, iters, maxq, group):
+    from mpq_b200 import solver as S
+    W, H = _layer_fixture(m, n, 3 + m)
+    V, Sv, Vs = _eig(H)
+    sg, zg, sf, zf, x_rtn = _rtn(W, maxq, group)
+    ocfg = OU.UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=3)
+    rq, rx, rerr, rrtn, rst = OU.solve_uniform_rankspace_vamp(W=W, x_rtn=x_rtn, scale_full=sf, zero_full=zf,
+                                                              maxq=maxq, V=V, Vh=V.T.copy(), S=Sv, Vs=Vs, cfg=ocfg,
+                                                              gram_full=H)
+    d = lambda a: _t(a, cuda_dev)
+    cfg = S.UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=3)
+    q, x, err, rtn_err, st = S.solve_uniform_rankspace_vamp(W=d(W), x_rtn=d(x_rtn), scale_full=d(sg), zero_full=d(zg),
+                                                            maxq=maxq, V=d(V), Vh=d(V.T.copy()), S=d(Sv), Vs=d(Vs),
+                                                            cfg=cfg, gram_full=d(H))
+    agree = (q.cpu().numpy() == rq).mean()
+    assert agree >= 0.999, (agree, st["best_iter"], rst["best_iter"])
+    loss = OL.proxy_loss(W, x.cpu().numpy(), H)
+    rloss = OL.proxy_loss(W, rx, H)
+    assert abs(loss - rloss) <= 0.005 * rloss
+    np.testing.assert_allclose(rtn_err.cpu().numpy(), rrtn, rtol=1e-3)
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_run_mpq_quantization_matches_reference_golden(cuda_dev, golden_dir, case):
+    """The full per-linear driver against the reference's own output (tests/golden/scalar_layer.npz)."""
+    import json
+    import types
+    from mpq_b200.adapters.gptqmodel import GPTQAdapterConfig, run_mpq_quantization
+    from mpq_b200.solver import UniformVampConfig
+    z = np.load(golden_dir / "scalar_layer.npz")
+    g = lambda k: z[f"{case}/{k}"]
+    meta = json.loads(str(g("meta")))
+    qcfg = types.SimpleNamespace(bits=meta["bits"], group_size=meta["group_size"], desc_act=False,
+                                 mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
+    cfg = UniformVampConfig(iters=meta["iters"], prior_tau=0.2, damping=0.5, polish_sweeps=3)
+    acfg = GPTQAdapterConfig(block_rows=meta["block_rows"], grow_block_rows=False)
+    Q, q_int, scale, zero, g_idx, _, st = run_mpq_quantization(
+        W=_t(g("W"), cuda_dev), H=_t(2.0 * g("H"), cuda_dev), quantizer=None, qcfg=qcfg, module_name=f"golden.{case}",
+        vamp_cfg=cfg, adapter_cfg=acfg)
+    np.testing.assert_allclose(scale.cpu().numpy(), g("scale"), rtol=1e-6)
+    np.testing.assert_array_equal(zero.cpu().numpy(), g("zero"))
+    agree = (q_int.cpu().numpy() == g("q_int")).mean()
+    assert agree >= 0.999, agree
+    rel = abs(st["raw_objective_mean_final"] - meta["raw_objective"]) / meta["raw_objective"]
+    assert rel <= 0.005, rel
+    np.testing.assert_allclose(Q.cpu().numpy(), g("Q"), rtol=0, atol=2e-3 * np.abs(g("Q")).max())

@@ -1,0 +1,87 @@
+"""Pin the CPU oracle against golden vectors produced by the reference itself."""
+import json
+
+import numpy as np
+import pytest
+
+from oracle import uniform_vamp as U
+from oracle import layer as L
+
+
+def _load(golden_dir, name):
+    return np.load(golden_dir / f"{name}.npz")
+
+
+@pytest.mark.parametrize("case", ["q4", "q3", "q4_noprior"])
+def test_uniform_denoise_matches_reference(golden_dir, case):
+    z = _load(golden_dir, "uniform_denoise")
+    g = lambda k: z[f"{case}/{k}"]
+    post = U.discrete_uniform_mmse(r1=g("r1"), gamma1=g("gamma"), scale_full=g("scale"), zero_full=g("zero"),
+                                   maxq=int(g("maxq")), prior_center=g("W"), prior_tau=float(g("tau")))
+    # discrete decisions: bit-exact
+    np.testing.assert_array_equal(post["map_idx"], g("map_idx"))
+    np.testing.assert_array_equal(post["map_value"], g("map_value"))
+    q = U.nearest_atom_idx(x=post["map_value"], scale_full=g("scale"), zero_full=g("zero"), maxq=int(g("maxq")))
+    np.testing.assert_array_equal(q, g("q"))
+    np.testing.assert_array_equal(U.dequant_from_q(q_int=q, scale_full=g("scale"), zero_full=g("zero")), g("x"))
+    # moments: float32 summation-order tolerance
+    np.testing.assert_allclose(post["mean"], g("mean"), rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(post["var"], g("var"), rtol=1e-3, atol=1e-9)
+    np.testing.assert_allclose(post["alpha1"], g("alpha1"), rtol=1e-4)
+
+
+def test_nearest_atom_round_half_even(golden_dir):
+    z = _load(golden_dir, "uniform_denoise")
+    q = U.nearest_atom_idx(x=z["ties/x"], scale_full=z["ties/scale"], zero_full=z["ties/zero"], maxq=7)
+    np.testing.assert_array_equal(q, z["ties/q"])
+
+
+def test_linear_mmse_and_em(golden_dir):
+    z = _load(golden_dir, "linear_mmse")
+    V = z["V"]
+    x2, a2, res = U.linear_mmse_exact(z["r2"], z["gamma2"], Y_u=z["Y_u"], V=V, Vh=np.ascontiguousarray(V.T),
+                                      S=z["S"], obs_precision=float(z["obs"]))
+    np.testing.assert_allclose(x2, z["x2"], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(a2, z["alpha2"], rtol=1e-5)
+    np.testing.assert_allclose(res, z["residual"], rtol=1e-4, atol=1e-8)
+    beta = U.em_update_obs_precision_rankspace(residual_u=z["residual"], gamma2=z["gamma2"], S=z["S"],
+                                               obs_precision=float(z["obs"]), num_obs=64)
+    assert beta == pytest.approx(float(z["beta"]), rel=1e-5)
+    err = U.vamp_rankspace_error(Y_u=z["Y_u"], x=z["r2"], Vs=z["Vs"])
+    np.testing.assert_allclose(err, z["err"], rtol=1e-4)
+
+
+def test_scalar_cd_matches_reference_torch_twin(golden_dir):
+    z = _load(golden_dir, "scalar_cd")
+    xo, st = U.uniform_scalar_diag_greedy_cd(x=z["x"], Y_u=z["Y_u"], Vs=z["Vs"], gram_full=z["H"], scale=z["scale"],
+                                             zero=z["zero"], maxq=15, sweeps=3)
+    agree = (xo == z["x_out"]).mean()
+    assert agree >= 0.999, agree
+    assert abs(st["accepted_updates"] - float(z["accepted"])) <= 0.01 * float(z["accepted"]) + 2
+
+
+def test_rotation_and_seeds(golden_dir):
+    z = _load(golden_dir, "rotation")
+    assert [L.stable_seed(k, b) for k, b in [("a", 0), ("model.layers.0.q_proj:full", 0), ("x", 7)]] == list(z["seeds"])
+    signs = L.rademacher_signs_torch(256, "golden.rot:full", 0)
+    np.testing.assert_array_equal(signs, z["signs"])
+    R = L.right_block_hadamard(z["M"], signs, 64)
+    np.testing.assert_array_equal(R, z["R"])
+    np.testing.assert_allclose(L.right_block_hadamard_inverse(R, signs, 64), z["Ri"], rtol=0, atol=1e-6)
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_scalar_layer_matches_reference(golden_dir, case):
+    z = _load(golden_dir, "scalar_layer")
+    g = lambda k: z[f"{case}/{k}"]
+    meta = json.loads(str(g("meta")))
+    cfg = U.UniformVampConfig(iters=meta["iters"], prior_tau=0.2, damping=0.5, polish_sweeps=3)
+    out = L.run_scalar_layer(W=g("W"), H=2.0 * g("H"), bits=meta["bits"], group_size=meta["group_size"],
+                             vamp_cfg=cfg, block_rows=meta["block_rows"], module_name=f"golden.{case}")
+    np.testing.assert_allclose(out["scale"], g("scale"), rtol=1e-6)
+    np.testing.assert_array_equal(out["zero"], g("zero"))
+    agree = (out["q_int"] == g("q_int")).mean()
+    assert agree >= 0.999, agree
+    ref_loss = L.proxy_loss(out["W_work"], L.right_block_hadamard(g("Q"), out["signs"], out["had_dim"]), out["H_metric"])
+    my_loss = L.proxy_loss(out["W_work"], out["Q_work"], out["H_metric"])
+    assert abs(my_loss - ref_loss) <= 0.005 * ref_loss
