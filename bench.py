@@ -46,7 +46,12 @@ def parse():
     ap.add_argument("--cpu-sample-rows", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--profile", action="store_true",
+                    help="one warm-up + one timed step, no e2e / CPU legs (for an ncu launch list)")
+    a = ap.parse_args()
+    if a.profile:
+        a.steps, a.warmup, a.no_cpu_baseline, a.no_clocks = 1, 1, True, True
+    return a
 
 
 # ----------------------------------------------------------------------------------------------
@@ -197,7 +202,9 @@ def run_mpq(args):
             s = torch.cuda.Event(enable_timing=True)
             e = torch.cuda.Event(enable_timing=True)
             s.record()
+            torch.cuda.nvtx.range_push("timed_step")
             out = solve_step(Wr, H2, block_rows)
+            torch.cuda.nvtx.range_pop()
             e.record()
             torch.cuda.synchronize()
             step_ms.append(s.elapsed_time(e))
@@ -209,6 +216,11 @@ def run_mpq(args):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+
+    if args.profile:
+        if world > 1:
+            dist.destroy_process_group()
+        return {"profile": True, "ms_per_step": ms, "gpu_launches": launches}
 
     # ---- e2e through the public API with host buffers ----
     W_host = Wr.cpu().pin_memory()

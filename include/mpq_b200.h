@@ -125,8 +125,9 @@ int mpq_cd_diag(const float* Vs, int n, int R, int64_t ld, float* diag, float* d
 int mpq_cd_gain(const float* rhs, int B, int n, int64_t ld, const float* diag_inv, float* gain, void* stream);
 /* order = argsort(key, descending), ties by ascending index; n <= 16384.  :243 */
 int mpq_argsort_desc(const float* key, int n, int* order, void* stream);
-/* HJ[k,:] = H[order[c0+k],:], Hsub[k,l] = H[order[c0+k], order[c0+l]] (Hsub is 128 x 128). */
-int mpq_cd_gather(const float* H, int64_t ldh, int n, const int* order, int c0, int K, float* HJ, float* Hsub,
+/* HJT[j,k] = H[order[c0+k], j] (n x 128, leading dimension 128), Hsub[k,l] = H[order[c0+k], order[c0+l]]
+ * (128 x 128); the block's rows of the raw Hessian in the layouts of the update GEMM and of mpq_cd_block. */
+int mpq_cd_gather(const float* H, int64_t ldh, int n, const int* order, int c0, int K, float* HJT, float* Hsub,
                   void* stream);
 /* Sequential greedy decisions of the columns order[c0 : c0+K] (K <= 128) for every row; writes x, the
  * residual norms, the accepted steps delta (B x 128) and the accepted count.  Replaces the column loop
@@ -135,6 +136,17 @@ int mpq_cd_block(float* x, int64_t ldx, const float* rhs, int64_t ldr, const flo
                  int64_t ld_p, int gshift, const float* diag, const float* diag_inv, const int* order, int c0, int K,
                  const float* Hsub, float* res, float* delta, int* accepted, int B, int maxq, float accept_tol,
                  void* stream);
+
+/* ---- tensor-core products (tcgen05 + TMEM + TMA, sm_100a) ----
+ * C = alpha * sum_{r < nreg} A[r] B[r]^T + beta C, TF32 operands with FP32 accumulation; A[r]: M x K row-major,
+ * B[r]: N x K row-major (host arrays of device pointers); nreg = 3 with (A_hi,B_hi),(A_hi,B_lo),(A_lo,B_hi) is the
+ * FP32-faithful 3xTF32 product.  16-byte aligned operands, lda/ldb multiples of 4.  `status` (device int) records a
+ * pipeline-wait timeout.  Replaces the FP32 torch matmuls of mpq/linear.py:48,51,94, mpq/solver.py:485 and
+ * mpq/polish/triton_scalar_cd.py:195-196,286-288. */
+int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float* const* A, int64_t lda, const float* const* B,
+                int64_t ldb, float beta, float* C, int64_t ldc, int* status, void* stream);
+/* hi = TF32 round-to-nearest of x, lo = x - hi (the operand split of the 3xTF32 product). */
+int mpq_split_tf32(const float* x, int64_t ldx, float* hi, float* lo, int64_t ldo, int rows, int cols, void* stream);
 
 /* ---- rotation ----
  * Block Walsh-Hadamard of the last dim, blocks of `had` (power of two <= 16384), normalized by sqrt(had);

@@ -186,7 +186,7 @@ def run_mpq_quantization(
              ptr(x), x.stride(0))
         return x
 
-    VsT = Vs.T.contiguous()
+    opVsT = ops.Operand(Vs.T.contiguous())
     if float(getattr(vamp_cfg, "obs_precision", 0.0)) > 0.0:
         obs_precision = float(vamp_cfg.obs_precision)
     else:
@@ -198,7 +198,7 @@ def run_mpq_quantization(
             x_rtn = rtn(rb, sb, zb)
             delta = torch.empty_like(x_rtn)
             call("mpq_sub", ptr(W_work[rb]), ptr(x_rtn), ptr(delta), delta.shape[0], cols, delta.stride(0))
-            diff_u = ops.gemm_nt(delta, VsT)
+            diff_u = ops.mm_nt(delta, opVsT)
             zeros = torch.zeros_like(diff_u)
             e = torch.empty(diff_u.shape[0], device=device, dtype=torch.float32)
             call("mpq_row_sqerr", ptr(diff_u), ptr(zeros), diff_u.shape[0], R, diff_u.stride(0), zeros.stride(0), ptr(e))
@@ -206,6 +206,7 @@ def run_mpq_quantization(
             count += int(diff_u.numel())
         obs_precision = 1.0 / float(max(sum_sq / max(count, 1), 1e-12))
 
+    opHT = ops.Operand(H_metric.T.contiguous())  # (W - Q) @ H for the raw audit
     Q_work = torch.empty_like(W_work)
     q_int_work = torch.empty((rows, cols), dtype=torch.uint8, device=device)
     obs_block = float(obs_precision)
@@ -228,7 +229,7 @@ def run_mpq_quantization(
         # raw Hessian audit (:1048-1056): (W - Q) H (W - Q)^T per row
         delta = torch.empty_like(x_final)
         call("mpq_sub", ptr(W_work[rb]), ptr(x_final), ptr(delta), delta.shape[0], cols, delta.stride(0))
-        dH = ops.gemm_nn(delta, H_metric)
+        dH = ops.mm_nt(delta, opHT)
         raw = torch.empty(delta.shape[0], device=device, dtype=torch.float32)
         call("mpq_row_dot", ptr(dH), dH.stride(0), ptr(delta), delta.stride(0), delta.shape[0], cols, ptr(raw))
         raw_err_sum += float(raw.double().sum().item())

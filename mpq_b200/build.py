@@ -11,7 +11,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OUT = HERE / "libmpq_b200.so"
 
-SOURCES = ["capi.cu", "uniform_prior.cu", "vamp_uniform.cu", "gemm_simt.cu", "scalar_cd.cu", "hadamard.cu"]
+SOURCES = ["capi.cu", "uniform_prior.cu", "vamp_uniform.cu", "gemm_simt.cu", "scalar_cd.cu", "hadamard.cu", "gemm_tc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

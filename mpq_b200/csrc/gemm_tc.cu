@@ -1,0 +1,365 @@
+// tcgen05 tensor-core GEMM for sm_100a (TF32 operands, FP32 accumulation in TMEM).
+//
+//   C[M, N] = alpha * sum_r A_r[M, K] * B_r[N, K]^T + beta * C        (r = 0 .. nreg-1, nreg <= 3)
+//
+// With (A_hi, B_hi), (A_hi, B_lo), (A_lo, B_hi) this is the 3xTF32 split product, which keeps the
+// rank-space VAMP products at FP32 accuracy (plain TF32 flips ~6% of the VAMP codes); with one
+// region it is a plain TF32 GEMM.  The regions are concatenated along K, so one accumulator and
+// one pipeline serve both.
+//
+// Structure (one 128 x BN output tile per CTA, 192 threads):
+//   warp 0      TMA producer: 2-D tiled loads (128B swizzle) of A and B k-blocks into a STAGES-deep
+//               shared-memory ring, completion signalled on per-stage mbarriers (expect_tx);
+//   warp 1      allocates BN TMEM columns, issues tcgen05.mma (M=128, N=BN, K=8) from one thread,
+//               frees ring slots with tcgen05.commit, and finally commits the accumulator;
+//   warps 2..5  epilogue: tcgen05.ld 32x32b of the accumulator (one row per thread) -> global.
+// Every mbarrier wait is bounded (globaltimer); on timeout the kernel records an error code in
+// `status`, drains its own in-flight copies / MMAs (bounded), frees TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include "common.cuh"
+
+namespace mpq {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // fp32 elements per k-block = 128 bytes = one 128B swizzle row
+constexpr int kThreads = 192;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false when the deadline passes first.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, K-major operand in the 128B-swizzled canonical layout:
+// rows of 128 B, 8-row swizzle atoms 1024 B apart (SBO), version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+  d |= (uint64_t)(16 >> 4) << 16;    // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // SBO: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::tf32, D = F32, A = B = TF32, both K-major, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+struct Maps {
+  CUtensorMap a[3];
+  CUtensorMap b[3];
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ Maps maps, int nreg, int M, int N, int K, float alpha, float beta,
+              float* __restrict__ C, int64_t ldc, int* __restrict__ status) {
+  constexpr uint32_t kStageA = BM * BK * 4;
+  constexpr uint32_t kStageB = BN * BK * 4;
+  constexpr uint32_t kIdesc = idesc_tf32(BM, BN);
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte aligned ring (swizzle atoms need 1024 B alignment)
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = base;
+  unsigned char* sB = base + STAGES * kStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kStageB);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_bar = empty + STAGES;
+  uint64_t* drain_bar = acc_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int kb_per_reg = (K + BK - 1) / BK;
+  const int total_kb = kb_per_reg * nreg;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_bar, 1);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < total_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int r = kb / kb_per_reg;
+        const int k0 = (kb % kb_per_reg) * BK;
+        mbar_expect_tx(&full[s], kStageA + kStageB);
+        tma_load_2d(sA + s * kStageA, &maps.a[r], &full[s], k0, m0);
+        tma_load_2d(sB + s * kStageB, &maps.b[r], &full[s], k0, n0);
+        issued = kb + 1;
+      }
+      if (*abort_flag) {
+        // drain: wait (bounded) for every copy this thread issued into the ring
+        for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb)
+          mbar_wait(&full[kb % STAGES], (uint32_t)(kb / STAGES) & 1u);
+        atomicCAS(status, 0, 2);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int kb = 0; kb < total_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        if (*abort_flag || !mbar_wait(&full[s], ph)) {
+          ok = false;
+          *abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_addr = smem_u32(sA + s * kStageA);
+        const uint32_t b_addr = smem_u32(sB + s * kStageB);
+        #pragma unroll
+        for (int j = 0; j < BK / 8; ++j) {
+          const uint64_t da = smem_desc_k_sw128(a_addr + j * 32);
+          const uint64_t db = smem_desc_k_sw128(b_addr + j * 32);
+          const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+          asm volatile(
+              "{\n\t.reg .pred p;\n\t"
+              "setp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+              "l"(da), "l"(db), "r"(kIdesc), "r"(acc)
+              : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&empty[s]))
+                     : "memory");
+      }
+      // accumulator ready (or, after an abort, all issued MMAs retired) -> epilogue / teardown
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(acc_bar))
+                   : "memory");
+      if (!ok) atomicCAS(status, 0, 3);
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+    const int quad = warp & 3;
+    const int row = m0 + quad * 32 + lane;
+    const bool ready = mbar_wait(acc_bar, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (!ready) {
+      *abort_flag = 1;
+      atomicCAS(status, 0, 4);
+    } else if (!*abort_flag) {
+      #pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+            "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+              "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < M) {
+          float* crow = C + (int64_t)row * ldc + n0 + c0;
+          const int ncol = min(32, N - (n0 + c0));
+          if (ncol == 32 && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
+            #pragma unroll
+            for (int t = 0; t < 32; t += 4) {
+              float4 o;
+              o.x = alpha * __uint_as_float(v[t]);
+              o.y = alpha * __uint_as_float(v[t + 1]);
+              o.z = alpha * __uint_as_float(v[t + 2]);
+              o.w = alpha * __uint_as_float(v[t + 3]);
+              float4* dst = reinterpret_cast<float4*>(crow + t);
+              if (beta != 0.f) {
+                const float4 c = *dst;
+                o.x += beta * c.x; o.y += beta * c.y; o.z += beta * c.z; o.w += beta * c.w;
+              }
+              *dst = o;
+            }
+          } else {
+            #pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              if (t < ncol) {
+                float o = alpha * __uint_as_float(v[t]);
+                if (beta != 0.f) o += beta * crow[t];
+                crow[t] = o;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN) : "memory");
+  }
+}
+
+// ---- host: tensor maps through the driver entry point (no libcuda link dependency) ----
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encoder() {
+  if (g_encode) return MPQ_OK;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+    set_last_error("cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(e));
+    return MPQ_ERR_UNSUPPORTED;
+  }
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return MPQ_OK;
+}
+
+// rows x K row-major fp32 (leading dimension ld), box = box_rows x 32, 128B swizzle
+static int make_map(CUtensorMap* m, const float* p, int rows, int K, int64_t ld, int box_rows) {
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled failed (%d) rows=%d K=%d ld=%lld", (int)r, rows, K, (long long)ld);
+    return MPQ_ERR_ARG;
+  }
+  return MPQ_OK;
+}
+
+template <int BN, int STAGES>
+static int launch(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
+                  int* status, cudaStream_t stream) {
+  const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * BK * 4 + 256;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm_tc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  k_gemm_tc<BN, STAGES><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status);
+  return launch_status("mpq_gemm_tc");
+}
+
+}  // namespace tc
+}  // namespace mpq
+
+using namespace mpq;
+
+// C = alpha * sum_{r < nreg} A_r B_r^T + beta * C.  A_r: M x K row-major (lda), B_r: N x K row-major (ldb).
+// Requirements (TMA): 16-byte aligned base pointers, lda/ldb multiples of 4 elements.  `status` (device int,
+// required) receives a non-zero code if a pipeline wait timed out (2: producer, 3: MMA, 4: epilogue).
+MPQ_API int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float* const* A, int64_t lda,
+                        const float* const* B, int64_t ldb, float beta, float* C, int64_t ldc, int* status,
+                        void* stream) {
+  MPQ_CHECK_ARG(nreg >= 1 && nreg <= 3, "mpq_gemm_tc: nreg must be 1..3");
+  MPQ_CHECK_ARG(A && B && C, "mpq_gemm_tc: null pointer");
+  MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 1, "mpq_gemm_tc: bad shape");
+  MPQ_CHECK_ARG(lda % 4 == 0 && ldb % 4 == 0 && lda >= K && ldb >= K, "mpq_gemm_tc: lda/ldb must be multiples of 4 and >= K");
+  if (M == 0 || N == 0) return MPQ_OK;
+  int st = tc::get_encoder();
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  for (int r = 0; r < nreg; ++r) {
+    MPQ_CHECK_ARG(A[r] && B[r], "mpq_gemm_tc: null operand %d", r);
+    MPQ_CHECK_ARG(((uintptr_t)A[r] & 15) == 0 && ((uintptr_t)B[r] & 15) == 0, "mpq_gemm_tc: operands must be 16-byte aligned");
+    st = tc::make_map(&maps.a[r], A[r], M, K, lda, tc::BM);
+    if (st) return st;
+    st = tc::make_map(&maps.b[r], B[r], N, K, ldb, 256);
+    if (st) return st;
+  }
+  MPQ_CHECK_ARG(status, "mpq_gemm_tc: status word required");
+  return tc::launch<256, 4>(maps, nreg, M, N, K, alpha, beta, C, ldc, status, (cudaStream_t)stream);
+}
+
+// hi = tf32 round-to-nearest of x (low 13 mantissa bits cleared), lo = x - hi (exact in fp32).
+namespace mpq {
+__global__ void k_split_tf32(const float* __restrict__ x, int64_t ldx, float* __restrict__ hi, float* __restrict__ lo,
+                             int64_t ldo, int rows, int cols) {
+  const int64_t total = (int64_t)rows * cols;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    const float v = x[r * ldx + c];
+    uint32_t h;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+    const float hv = __uint_as_float(h);
+    hi[r * ldo + c] = hv;
+    lo[r * ldo + c] = fsub(v, hv);
+  }
+}
+}  // namespace mpq
+
+MPQ_API int mpq_split_tf32(const float* x, int64_t ldx, float* hi, float* lo, int64_t ldo, int rows, int cols,
+                           void* stream) {
+  MPQ_CHECK_ARG(x && hi && lo, "mpq_split_tf32: null pointer");
+  const int64_t total = (int64_t)rows * cols;
+  if (total == 0) return MPQ_OK;
+  int64_t g = (total + 255) / 256;
+  if (g > 148 * 16) g = 148 * 16;
+  k_split_tf32<<<(int)g, 256, 0, (cudaStream_t)stream>>>(x, ldx, hi, lo, ldo, rows, cols);
+  return launch_status("mpq_split_tf32");
+}

@@ -82,16 +82,31 @@ __global__ void __launch_bounds__(1024) k_argsort_desc(const float* __restrict__
   for (int i = threadIdx.x; i < n; i += blockDim.x) order[i] = v[i];
 }
 
-// HJ[k, :] = H[J[k], :] and Hsub[k, l] = H[J[k], J[l]] for the block J = order[c0 : c0 + K]
-__global__ void k_cd_gather(const float* __restrict__ H, int64_t ldh, int n, const int* __restrict__ order, int c0,
-                            int K, float* __restrict__ HJ, float* __restrict__ Hsub) {
-  const int k = blockIdx.y;
-  const int row = order[c0 + k];
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
-    HJ[(int64_t)k * n + j] = H[(int64_t)row * ldh + j];
-  if (blockIdx.x == 0)
-    for (int l = threadIdx.x; l < kCdBlock; l += blockDim.x)
-      Hsub[k * kCdBlock + l] = l < K ? H[(int64_t)row * ldh + order[c0 + l]] : 0.f;
+// HJT[j, k] = H[J[k], j] (n x 128, transposed through shared-memory tiles so both the read of
+// H's rows and the write are coalesced) and Hsub[k, l] = H[J[k], J[l]] for J = order[c0 : c0 + K].
+__global__ void __launch_bounds__(256) k_cd_gather(const float* __restrict__ H, int64_t ldh, int n,
+                                                   const int* __restrict__ order, int c0, int K,
+                                                   float* __restrict__ HJT, float* __restrict__ Hsub) {
+  __shared__ float tile[32][33];
+  const int j0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  for (int kk = ty; kk < 32; kk += 8) {
+    const int k = k0 + kk, j = j0 + tx;
+    float v = 0.f;
+    if (k < K && j < n) v = H[(int64_t)order[c0 + k] * ldh + j];
+    tile[kk][tx] = v;
+  }
+  __syncthreads();
+  for (int jj = ty; jj < 32; jj += 8) {
+    const int j = j0 + jj, k = k0 + tx;
+    if (j < n) HJT[(int64_t)j * kCdBlock + k] = tile[tx][jj];
+  }
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < 32 * kCdBlock; i += blockDim.x) {
+      const int k = k0 + i / kCdBlock, l = i % kCdBlock;
+      if (k < kCdBlock) Hsub[k * kCdBlock + l] = (k < K && l < K) ? H[(int64_t)order[c0 + k] * ldh + order[c0 + l]] : 0.f;
+    }
+  }
 }
 
 struct CdArgs {
@@ -209,12 +224,12 @@ MPQ_API int mpq_argsort_desc(const float* key, int n, int* order, void* stream) 
   return launch_status("mpq_argsort_desc");
 }
 
-MPQ_API int mpq_cd_gather(const float* H, int64_t ldh, int n, const int* order, int c0, int K, float* HJ, float* Hsub,
+MPQ_API int mpq_cd_gather(const float* H, int64_t ldh, int n, const int* order, int c0, int K, float* HJT, float* Hsub,
                           void* stream) {
-  MPQ_CHECK_ARG(H && order && HJ && Hsub, "mpq_cd_gather: null pointer");
+  MPQ_CHECK_ARG(H && order && HJT && Hsub, "mpq_cd_gather: null pointer");
   MPQ_CHECK_ARG(K >= 1 && K <= kCdBlock && c0 >= 0 && c0 + K <= n, "mpq_cd_gather: bad block [%d, %d)", c0, c0 + K);
-  dim3 grid((n + 255) / 256 < 16 ? (n + 255) / 256 : 16, K);
-  k_cd_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(H, ldh, n, order, c0, K, HJ, Hsub);
+  dim3 grid((n + 31) / 32, kCdBlock / 32);
+  k_cd_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(H, ldh, n, order, c0, K, HJT, Hsub);
   return launch_status("mpq_cd_gather");
 }
 

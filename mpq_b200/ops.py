@@ -80,3 +80,118 @@ def mean_rows(a: torch.Tensor, c: Optional[torch.Tensor] = None, out: Optional[t
         out = torch.empty(1, device=a.device, dtype=torch.float32)
     call("mpq_mean_rows", ptr(a), ptr(c), int(a.numel()), ptr(out))
     return out
+
+
+# ------------------------------------------------------------------------------------------------
+# tcgen05 tensor-core products (3xTF32 by default)
+# ------------------------------------------------------------------------------------------------
+
+import ctypes as _ct
+
+_PRECISION = "tf32x3"
+_scratch = {}
+_status = {}
+
+
+def set_gemm_precision(mode: str) -> None:
+    """'tf32x3' (FP32-faithful split products, default), 'tf32' (single TF32 product) or 'fp32'
+    (CUDA-core FP32 kernel)."""
+    global _PRECISION
+    if mode not in ("tf32x3", "tf32", "fp32"):
+        raise ValueError(f"unknown GEMM precision {mode!r}")
+    _PRECISION = mode
+
+
+def gemm_precision() -> str:
+    return _PRECISION
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    key = (device.type, device.index)
+    t = _status.get(key)
+    if t is None:
+        t = torch.zeros(1, device=device, dtype=torch.int32)
+        _status[key] = t
+    return t
+
+
+def check_status(device: torch.device) -> None:
+    """Raise if a tensor-core pipeline wait timed out since the last check (host sync)."""
+    t = status_word(device)
+    v = int(t.item())
+    if v:
+        t.zero_()
+        raise RuntimeError(f"mpq_gemm_tc: pipeline wait timed out (code {v})")
+
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    return t.stride(-1) == 1 and t.stride(0) % 4 == 0 and t.data_ptr() % 16 == 0
+
+
+def split_tf32(x: torch.Tensor, hi: Optional[torch.Tensor] = None, lo: Optional[torch.Tensor] = None):
+    """hi = round-to-nearest TF32 of x, lo = x - hi (exact)."""
+    rows, cols = x.shape
+    if hi is None:
+        hi = torch.empty(rows, cols, device=x.device, dtype=torch.float32)
+    if lo is None:
+        lo = torch.empty_like(hi)
+    call("mpq_split_tf32", ptr(x), x.stride(0), ptr(hi), ptr(lo), hi.stride(0), rows, cols)
+    return hi, lo
+
+
+class Operand:
+    """A row-major K-major matrix used as the B side of repeated products, with its TF32 split."""
+
+    def __init__(self, t: torch.Tensor, precision: Optional[str] = None):
+        self.full = t
+        self.precision = precision or _PRECISION
+        self.hi = self.lo = None
+        if self.precision == "tf32x3" and _tma_ok(t):
+            self.hi, self.lo = split_tf32(t)
+
+    @property
+    def shape(self):
+        return self.full.shape
+
+
+def _scratch_split(A: torch.Tensor):
+    key = (A.device.index, tuple(A.shape))
+    buf = _scratch.get(key)
+    if buf is None:
+        buf = (torch.empty(A.shape, device=A.device, dtype=torch.float32),
+               torch.empty(A.shape, device=A.device, dtype=torch.float32))
+        _scratch[key] = buf
+    return split_tf32(A, buf[0], buf[1])
+
+
+def mm_nt(A: torch.Tensor, B, out: Optional[torch.Tensor] = None, *, alpha: float = 1.0, beta: float = 0.0,
+          precision: Optional[str] = None) -> torch.Tensor:
+    """C = alpha * A @ B^T + beta * C on the tensor cores.  B: Operand or (N x K) tensor."""
+    if not isinstance(B, Operand):
+        B = Operand(B, precision)
+    prec = precision or B.precision
+    M, K = A.shape
+    N = B.full.shape[0]
+    if B.full.shape[1] != K:
+        raise ValueError(f"mm_nt shape mismatch {tuple(A.shape)} x {tuple(B.full.shape)}^T")
+    if out is None:
+        out = torch.empty(M, N, device=A.device, dtype=torch.float32)
+    if prec == "fp32" or not (_tma_ok(A) and _tma_ok(B.full) and (prec != "tf32x3" or B.hi is not None)):
+        return gemm_nt(A, B.full, out, alpha=alpha, beta=beta)
+    if prec == "tf32x3":
+        Ah, Al = _scratch_split(A)
+        As = [Ah, Ah, Al]
+        Bs = [B.hi, B.lo, B.hi]
+        lda = Ah.stride(0)
+        ldb = B.hi.stride(0)
+    else:
+        As, Bs = [A], [B.full]
+        lda, ldb = A.stride(0), B.full.stride(0)
+    arrA = (_ct.c_void_p * 3)(*[t.data_ptr() for t in As])
+    arrB = (_ct.c_void_p * 3)(*[t.data_ptr() for t in Bs])
+    st = status_word(A.device)
+    tok = trace.begin_timing("gemm")
+    call("mpq_gemm_tc", len(As), M, N, K, float(alpha), arrA, lda, arrB, ldb, float(beta), ptr(out), out.stride(0),
+         ptr(st))
+    trace.end_timing("gemm", tok, 2.0 * M * N * K)
+    return out

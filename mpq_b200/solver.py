@@ -117,10 +117,19 @@ class _UniformCtx:
         self.S = S
         self.Vs = Vs
         self.VsT = Vs.t().contiguous()
-        self.Y_u = ops.gemm_nt(W, self.VsT)
+        # B-side operands of the rank-space products, split once for the 3xTF32 tensor-core GEMM
+        self.opV = ops.Operand(V)        # (resid * coeff) @ Vh  ==  u @ V^T
+        self.opVh = ops.Operand(Vh)      # r2 @ V                ==  r2 @ Vh^T
+        self.opVsT = ops.Operand(self.VsT)  # x @ Vs
+        self.opVs = ops.Operand(Vs)      # residual_u @ Vs^T
+        self.Y_u = ops.mm_nt(W, self.opVsT)
 
     def err(self, x, out=None, tmp=None):
-        return ops.rankspace_error(self.Y_u, x, self.VsT, tmp=tmp, out=out)
+        C = ops.mm_nt(x, self.opVsT, tmp)
+        if out is None:
+            out = torch.empty(x.shape[0], device=x.device, dtype=torch.float32)
+        call("mpq_row_sqerr", ptr(self.Y_u), ptr(C), x.shape[0], C.shape[1], self.Y_u.stride(0), C.stride(0), ptr(out))
+        return out
 
     def nearest(self, x, q_out, x_out):
         call("mpq_uniform_nearest", ptr(x), x.stride(0), ptr(self.scale), ptr(self.zero), self.ld_p, self.gshift,
@@ -142,17 +151,17 @@ def scalar_greedy_cd(ctx: _UniformCtx, x_init: torch.Tensor, gram_full: torch.Te
     """
     dev, B, n, R = ctx.dev, ctx.B, ctx.n, ctx.R
     x_work = x_init.clone()
-    res_u = ops.gemm_nt(x_work, ctx.VsT)
+    res_u = ops.mm_nt(x_work, ctx.opVsT)
     res_norm = torch.empty(B, device=dev, dtype=torch.float32)
     call("mpq_residual", ptr(ctx.Y_u), ptr(res_u), B, R, res_u.stride(0), ptr(res_norm))
-    rhs = ops.gemm_nt(res_u, ctx.Vs)  # residual_u @ Vs^T  (B x n)
+    rhs = ops.mm_nt(res_u, ctx.opVs)  # residual_u @ Vs^T  (B x n)
     del res_u
     diag = torch.empty(n, device=dev, dtype=torch.float32)
     diag_inv = torch.empty(n, device=dev, dtype=torch.float32)
     call("mpq_cd_diag", ptr(ctx.Vs), n, R, ctx.Vs.stride(0), ptr(diag), ptr(diag_inv))
     gain = torch.empty(n, device=dev, dtype=torch.float32)
     order = torch.empty(n, device=dev, dtype=torch.int32)
-    HJ = torch.empty(128, n, device=dev, dtype=torch.float32)
+    HJT = torch.empty(n, 128, device=dev, dtype=torch.float32)
     Hsub = torch.empty(128, 128, device=dev, dtype=torch.float32)
     delta = torch.empty(B, 128, device=dev, dtype=torch.float32)
     accepted = torch.zeros(1, device=dev, dtype=torch.int32)
@@ -162,11 +171,11 @@ def scalar_greedy_cd(ctx: _UniformCtx, x_init: torch.Tensor, gram_full: torch.Te
         call("mpq_argsort_desc", ptr(gain), n, ptr(order))
         for c0 in range(0, n, 128):
             K = min(128, n - c0)
-            call("mpq_cd_gather", ptr(H), H.stride(0), n, ptr(order), c0, K, ptr(HJ), ptr(Hsub))
+            call("mpq_cd_gather", ptr(H), H.stride(0), n, ptr(order), c0, K, ptr(HJT), ptr(Hsub))
             call("mpq_cd_block", ptr(x_work), x_work.stride(0), ptr(rhs), rhs.stride(0), ptr(ctx.scale),
                  ptr(ctx.zero), ctx.ld_p, ctx.gshift, ptr(diag), ptr(diag_inv), ptr(order), c0, K, ptr(Hsub),
                  ptr(res_norm), ptr(delta), ptr(accepted), B, ctx.maxq, float(accept_tol))
-            ops.gemm_nn(delta[:, :K], HJ[:K], out=rhs, alpha=-1.0, beta=1.0)
+            ops.mm_nt(delta[:, :K], HJT[:, :K], out=rhs, alpha=-1.0, beta=1.0)
     return x_work, {"accepted_updates": float(accepted.item())}
 
 
@@ -208,7 +217,9 @@ def polish_uniform_rankspace(
     def finish(x, stats):
         call("mpq_uniform_nearest", ptr(x), x.stride(0), ptr(scale_full), ptr(zero_full), ld_p, gshift, B, n,
              int(maxq), ptr(q_out), ptr(x_out), x_out.stride(0))
-        err = ops.rankspace_error(Y_u, x_out, VsT)
+        C = ops.mm_nt(x_out, ops.Operand(VsT))
+        err = torch.empty(B, device=dev, dtype=torch.float32)
+        call("mpq_row_sqerr", ptr(Y_u), ptr(C), B, C.shape[1], Y_u.stride(0), C.stride(0), ptr(err))
         return q_out.to(torch.int32), x_out, err, stats
 
     if mode == "none" or Vs.numel() == 0:
@@ -221,6 +232,7 @@ def polish_uniform_rankspace(
     ctx.dev, ctx.B, ctx.n, ctx.R = dev, B, n, R
     ctx.scale, ctx.zero, ctx.ld_p, ctx.gshift, ctx.maxq = scale_full, zero_full, ld_p, gshift, int(maxq)
     ctx.Vs, ctx.VsT, ctx.Y_u = Vs, VsT, Y_u
+    ctx.opVs, ctx.opVsT = ops.Operand(Vs), ops.Operand(VsT)
     x_pol, st = scalar_greedy_cd(ctx, x_work, _f32c(gram_full, dev), sweeps=int(sweeps))
     st = dict(st)
     st["block_cd_backend"] = "cuda"
@@ -359,10 +371,10 @@ def solve_uniform_rankspace_vamp(
         alpha2_clip_count += int(fl[4])
         call("mpq_vamp_r2", ptr(x1), ptr(r1), ptr(r2_prev) if (have_prev and damping < 1.0) else None, ptr(r2),
              ptr(rows["eta1"]), ptr(rows["g1w"]), ptr(rows["g2n"]), B, n, r2.stride(0), damping)
-        P = ops.gemm_nt(r2, Vh, tmpBR)  # r2 @ V
+        P = ops.mm_nt(r2, ctx.opVh, tmpBR)  # r2 @ V
         call("mpq_linear_epilogue", ptr(P), ptr(ctx.Y_u), ptr(S), ptr(rows["g2"]), obs, B, R, P.stride(0), ptr(u),
              ptr(rows["resid"]))
-        D = ops.gemm_nt(u, V, x1)  # (resid * coeff) @ Vh
+        D = ops.mm_nt(u, ctx.opV, x1)  # (resid * coeff) @ Vh
         call("mpq_vamp_r1", ptr(D), ptr(r2), ptr(r1), ptr(rows["eta2"]), ptr(rows["g2"]), ptr(rows["g1n"]), B, n,
              r1.stride(0), damping)
         gamma1.copy_(rows["g1next"])
@@ -422,6 +434,7 @@ def solve_uniform_rankspace_vamp(
         polish_stats["rows_improved"] = int(improved.item())
 
     rtn_err = ctx.err(x_rtn, tmp=tmpBR)
+    ops.check_status(dev)
     if debug_out is not None:
         debug_out["solver"] = "uniform_exact_vamp"
         g64 = gamma1.double()
