@@ -184,8 +184,105 @@ def gen_rotation(out):
     np.savez_compressed(out / "rotation.npz", M=_np(M), signs=_np(signs), R=_np(R), Ri=_np(Ri), seeds=seeds)
 
 
+def _reference_codebook():
+    """Torch wrapper of the restated E8P12 grid with the attributes the reference reads; its quantize()
+    is the reference's own factorized MAP at unit precision (nearest codeword)."""
+    sys.path.insert(0, str(HERE.parents[1]))
+    from oracle.e8p12 import E8P12_codebook as NpCB
+    from mpq.priors.e8p12 import vamp_vector_map_e8p12
+
+    class E8P12_codebook:
+        codesz = 8
+        idx_dtype = torch.int64
+
+        def __init__(self):
+            self.grid = torch.from_numpy(NpCB().grid.copy())
+            self.grid_packed_abs = torch.arange(256, dtype=torch.int64)
+
+        def quantize(self, X, return_idx=True, **kw):
+            X = X.reshape(-1, 8).float()
+            out = vamp_vector_map_e8p12(r1_blocks=X.view(1, -1, 8), gamma1=torch.ones(1, 1), cb=self,
+                                        blocks_per_chunk=1 << 30)
+            idx = out["map_idxs"].view(-1)
+            vals = self.grid.index_select(0, idx)
+            return (vals, idx) if return_idx else vals
+
+    return E8P12_codebook()
+
+
+def gen_e8p12(out):
+    from mpq.priors.e8p12 import vamp_vector_discrete_mmse_e8p12, vamp_vector_map_e8p12, prior_scale_from_center
+    from mpq.polish.block_cd import _cd_gram_step_impl
+    from mpq.linear import stabilize_cholesky
+    cb = _reference_codebook()
+    g = torch.Generator().manual_seed(21)
+    cases = {}
+    B, nb = 12, 40
+    W = torch.randn(B, nb, 8, generator=g) * 0.8
+    r1 = W + torch.randn(B, nb, 8, generator=g) * 0.3
+    ps = prior_scale_from_center(W, "absmax")
+    for name, gam in {"lo": torch.rand(B, 1, generator=g) * 4 + 1, "hi": torch.rand(B, 1, generator=g) * 40 + 10,
+                      "snap": torch.full((B, 1), 1500.0)}.items():
+        post = vamp_vector_discrete_mmse_e8p12(r1_blocks=r1, gamma1=gam, cb=cb, blocks_per_chunk=nb,
+                                               prior_center_blocks=W, prior_scale_blocks=ps, prior_tau=0.25,
+                                               compile_prior=False)
+        mp = vamp_vector_map_e8p12(r1_blocks=r1, gamma1=gam, cb=cb, blocks_per_chunk=nb, prior_center_blocks=W,
+                                   prior_scale_blocks=ps, prior_tau=0.25)
+        for k in ("x1_blocks", "var1", "map_idxs", "alpha1"):
+            cases[f"{name}/{k}"] = _np(post[k])
+        cases[f"{name}/map_only_idxs"] = _np(mp["map_idxs"])
+        cases[f"{name}/gamma"] = _np(gam)
+    cases["r1"] = _np(r1)
+    cases["W"] = _np(W)
+    # nearest codeword (RTN) of unscaled Gaussian blocks
+    X = torch.randn(2048, 8, generator=g)
+    _, qi = cb.quantize(X)
+    cases["rtn/X"] = _np(X)
+    cases["rtn/idx"] = _np(qi)
+    # one gram-metric CD step (mpq/polish/block_cd.py:212-246)
+    n, R, Bc = 64, 64, 48
+    Vs = torch.randn(n, R, generator=g) / 8
+    resid = torch.randn(Bc, R, generator=g) * 0.5
+    xb = cb.grid[torch.randint(0, 65536, (Bc,), generator=g)]
+    vb = Vs[8:16]
+    gram = vb @ vb.T
+    chol = stabilize_cholesky(gram)
+    ginv = torch.cholesky_inverse(chol)
+    rn = resid.square().sum(1)
+    new_x, best, acc, rupd, nn_, na = _cd_gram_step_impl(resid, xb, vb.T.contiguous(), ginv, chol, cb.grid, gram, vb,
+                                                         rn, 0.0)
+    for k, v in dict(Vs=Vs, resid=resid, xb=xb, chol=chol, ginv=ginv, best=best, accept=acc, new_x=new_x).items():
+        cases[f"gram/{k}"] = _np(v)
+    np.savez_compressed(out / "e8p12_prior.npz", **cases)
+
+
+def gen_e8p12_layer(out):
+    from mpq.adapters.quip_sharp import mpq_refine_codebook
+    cb = _reference_codebook()
+    cases = {}
+    for name, (m, n, block_rows, iters) in {"a": (32, 256, 16, 16), "b": (24, 128, 24, 8)}.items():
+        W, H = synth_layer(m, n, 300 + m)
+        Wr = W / W.square().mean().sqrt() * 0.9  # unit-scale weights as QUIP# feeds the codebook
+        args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=iters, mpq_prior_tau=0.25, mpq_polish_sweeps=3,
+                                     mpq_block_rows=block_rows, mpq_blocks_per_chunk=1 << 20, mpq_compile_prior=False,
+                                     quant_solver="vamp", quant_polish_mode="block_cd", mpq_polish_metric="gram")
+        hat0, q0 = cb.quantize(Wr.reshape(-1, 8))
+        hatWr, Qidxs, st = mpq_refine_codebook(Wr, H, hat0.view(m, n), q0.view(m, n // 8), cb, args,
+                                               module_name=f"golden.e8.{name}")
+        for k, v in dict(Wr=Wr, H=H, hatWr=hatWr, Qidxs=Qidxs).items():
+            cases[f"{name}/{k}"] = _np(v)
+        cases[f"{name}/meta"] = np.array(json.dumps(dict(block_rows=block_rows, iters=iters,
+                                                          obs_init=st["obs_precision_initial"],
+                                                          obs_final=st["obs_precision_final"],
+                                                          surrogate_before=st["exact_surrogate_before_mean"],
+                                                          surrogate_after=st["exact_surrogate_after_mean"],
+                                                          changed=st["mechanism"]["cleanup_changed_count"])))
+    np.savez_compressed(out / "e8p12_layer.npz", **cases)
+
+
 GENERATORS = {"uniform_denoise": gen_uniform_denoise, "linear": gen_linear, "scalar_cd": gen_scalar_cd,
-              "scalar_layer": gen_scalar_layer, "rotation": gen_rotation}
+              "scalar_layer": gen_scalar_layer, "rotation": gen_rotation, "e8p12": gen_e8p12,
+              "e8p12_layer": gen_e8p12_layer}
 
 
 def main():

@@ -1,0 +1,95 @@
+"""Pin the E8P12 part of the CPU oracle against vectors produced by the reference's own E8P12 code
+(run on the restated codebook, see tests/golden/make_golden.py)."""
+import json
+
+import numpy as np
+import pytest
+
+from oracle import e8p12 as E
+from oracle import layer as OL
+
+
+@pytest.fixture(scope="module")
+def cb():
+    return E.E8P12_codebook()
+
+
+def test_codebook_is_e8_plus_quarter(cb):
+    g = cb.grid.astype(np.float64)
+    assert g.shape == (65536, 8)
+    assert len(np.unique(g, axis=0)) == 65536
+    y = g - 0.25
+    integer = np.all(np.abs(y - np.round(y)) < 1e-9, axis=1)
+    half = np.all(np.abs(y - np.round(y - 0.5) - 0.5) < 1e-9, axis=1)
+    assert np.all(integer | half)
+    assert np.all(np.round(y.sum(axis=1)).astype(np.int64) % 2 == 0)  # even coordinate sum: E8
+    c = E.factor_cache(cb)  # the reference's structural assertions
+    assert c["idx_lut"].shape == (2, 256, 256)
+    norms = np.sort(np.unique((cb.base_signed.astype(np.float64) ** 2).sum(axis=1)))
+    assert norms.max() == 12.0
+
+
+def test_nearest_codeword_matches_reference(golden_dir, cb):
+    z = np.load(golden_dir / "e8p12_prior.npz")
+    _, idx = cb.quantize(z["rtn/X"])
+    agree = idx == z["rtn/idx"]
+    assert agree.mean() >= 0.999
+    X = z["rtn/X"].astype(np.float64)
+    d = lambda i: ((X - cb.grid[i]) ** 2).sum(axis=1)
+    np.testing.assert_allclose(d(idx)[~agree], d(z["rtn/idx"])[~agree], rtol=1e-6)  # only exact ties differ
+
+
+@pytest.mark.parametrize("case", ["lo", "hi", "snap"])
+def test_factorized_posterior_matches_reference(golden_dir, cb, case):
+    z = np.load(golden_dir / "e8p12_prior.npz")
+    W, r1 = z["W"], z["r1"]
+    gam = z[f"{case}/gamma"]
+    ps = E.prior_scale_from_center(W, "absmax")
+    post = E.vamp_vector_discrete_mmse_e8p12(r1_blocks=r1, gamma1=gam, cb=cb, prior_center_blocks=W,
+                                             prior_scale_blocks=ps, prior_tau=0.25)
+    assert (post["map_idxs"] == z[f"{case}/map_idxs"]).mean() >= 0.999
+    mp = E.vamp_vector_map_e8p12(r1_blocks=r1, gamma1=gam, cb=cb, prior_center_blocks=W, prior_scale_blocks=ps,
+                                 prior_tau=0.25)
+    assert (mp["map_idxs"] == z[f"{case}/map_only_idxs"]).mean() >= 0.999
+    # Components whose sign product is within ~1e-6 of +-1 divide by (1 +- prod): a 1-ulp tanh difference
+    # moves their sign means by up to ~1e-2.  Require tight agreement almost everywhere, bounded elsewhere.
+    x1, rx1 = post["x1_blocks"], z[f"{case}/x1_blocks"]
+    close = np.isclose(x1, rx1, rtol=1e-4, atol=2e-5)
+    assert close.mean() >= 0.99, close.mean()
+    assert np.abs(x1 - rx1).max() <= 2e-2
+    # Where all |tanh(a_k)| saturate at the 1 - 1e-7 clamp, log(1 - prod) depends on 1-ulp tanh rounding
+    # (torch vs numpy vs CUDA), which moves that component's weight by a few percent: variances (and their
+    # row means, alpha1) agree tightly except on such items.
+    v, rv = post["var1"], z[f"{case}/var1"]
+    assert np.isclose(v, rv, rtol=2e-3, atol=2e-6).mean() >= 0.97
+    np.testing.assert_allclose(post["alpha1"], z[f"{case}/alpha1"], rtol=2e-2)
+
+
+def test_gram_cd_step_matches_reference(golden_dir, cb):
+    z = np.load(golden_dir / "e8p12_prior.npz")
+    g = lambda k: z[f"gram/{k}"]
+    Vs, resid, xb, chol, ginv = g("Vs"), g("resid"), g("xb"), g("chol"), g("ginv")
+    vb = Vs[8:16]
+    rhs = resid @ vb.T
+    target = (xb + rhs @ ginv).astype(np.float32)
+    best = E.gram_search(target, chol, cb.grid)
+    assert (best == g("best")).mean() >= 0.98
+    # any disagreement must be a near-tie of the metric distance
+    L = chol.astype(np.float64)
+    dist = lambda i: ((((cb.grid[i] - target) @ L)) ** 2).sum(axis=1)
+    np.testing.assert_allclose(dist(best), dist(g("best")), rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_e8p12_layer_matches_reference(golden_dir, cb, case):
+    z = np.load(golden_dir / "e8p12_layer.npz")
+    g = lambda k: z[f"{case}/{k}"]
+    meta = json.loads(str(g("meta")))
+    cfg = E.E8P12VampConfig(iters=meta["iters"], prior_tau=0.25, polish_sweeps=3)
+    out = E.refine_codebook(Wr=g("Wr"), Hr=g("H"), cb=cb, cfg=cfg, block_rows=meta["block_rows"])
+    agree = (out["Qidxs"] == g("Qidxs")).mean()
+    assert agree >= 0.999, agree
+    H = g("H")
+    ref_loss = OL.proxy_loss(g("Wr"), g("hatWr"), H)
+    my_loss = OL.proxy_loss(g("Wr"), out["hatWr"], H)
+    assert abs(my_loss - ref_loss) <= 0.005 * ref_loss
