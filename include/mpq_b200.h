@@ -60,7 +60,8 @@ int mpq_uniform_rtn(const float* W, int64_t ldw, const float* scale, const float
 
 /* ---- VAMP message algebra (mpq/solver.py:553-699, mpq/linear.py:10-94) ---- */
 
-/* Per-row scalar stage of one iteration: alpha1 from the variance sums, gamma2 (damped), the
+/* Per-row scalar stage of one iteration: alpha1 = gamma1_work * var_rowsum / n_var (n_var = n for the scalar
+ * grid, n/8 for E8P12 blocks), gamma2 (damped), the
  * gamma-only terms of linear_mmse_exact (alpha2, eta2, gamma1_new, damped gamma1) and the EM
  * trace term.  flags[0..4] count invalid alpha1 / non-finite alpha1 / invalid gamma2_new /
  * invalid gamma2 / clipped alpha2 rows.  final_retry != 0 clips alpha1 instead of failing.
@@ -70,8 +71,9 @@ int mpq_vamp_rows(const float* var_rowsum, float* gamma1, float* gamma1_work, fl
                   float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int B, int n,
                   int R, float obs, float damping, int final_retry, void* stream);
 
-/* gamma retry of rows with alpha1 outside (1e-7, 1-1e-7).  Replaces mpq/solver.py:593-596. */
-int mpq_gamma_retry(float* gamma1_work, const float* var_rowsum, int B, int n, float factor, void* stream);
+/* gamma retry of rows with alpha1 = gamma1_work * var_rowsum / n_var outside (1e-7, 1-1e-7).
+ * Replaces mpq/solver.py:593-596 (and :998-1001). */
+int mpq_gamma_retry(float* gamma1_work, const float* var_rowsum, int B, int n_var, float factor, void* stream);
 
 /* r2 = damp(r2_prev, (eta1 x1 - gamma1w r1) / gamma2_new); r2_prev NULL = undamped.  mpq/solver.py:605-612. */
 int mpq_vamp_r2(const float* x1, const float* r1, const float* r2_prev, float* r2, const float* eta1,
@@ -147,6 +149,48 @@ int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float* const* 
                 int64_t ldb, float beta, float* C, int64_t ldc, int* status, void* stream);
 /* hi = TF32 round-to-nearest of x, lo = x - hi (the operand split of the 3xTF32 product). */
 int mpq_split_tf32(const float* x, int64_t ldx, float* hi, float* lo, int64_t ldo, int rows, int cols, void* stream);
+
+/* ---- E8P12 (K3, K4, K6): mpq/priors/e8p12.py ----
+ * Tables (from the codebook grid, as mpq/priors/e8p12.py:83-151 derives them): base_abs 256x8, base_sqnorm 256,
+ * base_parity 256, idx_lut 2x256x256 (branch, abs, sign id) -> index, grid 65536x8, sign_id 65536 (u8).
+ * Items are the nb = n/8 consecutive 8-blocks of each of B rows; the prior (tau > 0, centre W) is folded
+ * per block with scale = absmax of the centre block unless pscale (B x nb) is given. */
+/* Factorized posterior mean x1 (B x n), per-block variance, MAP index / values and the per-row variance sum.
+ * Replaces mpq/priors/e8p12.py:815-968 (vamp_vector_discrete_mmse_e8p12, _branch_factorized_stats :169-308). */
+int mpq_e8p12_mmse(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                   int64_t ld_s, const float* gamma, float prior_tau, int B, int nb, const float* base_abs,
+                   const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,
+                   float* x1_out, int64_t ld_x, float* var_out, int64_t ld_v, int* idx_out, int64_t ld_i,
+                   float* map_out, int64_t ld_m, float* var_rowsum, void* stream);
+/* MAP codeword (bit-exact first maximum); fixed_gamma > 0 with prior_tau <= 0 is the nearest codeword (RTN).
+ * Replaces mpq/priors/e8p12.py:541-631 (vamp_vector_map_e8p12, _branch_factorized_map :367-449) and the
+ * nearest-codeword cb.quantize of mpq/adapters/quip_sharp.py:212-241. */
+int mpq_e8p12_map(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                  int64_t ld_s, const float* gamma, float fixed_gamma, float prior_tau, int B, int nb,
+                  const float* base_abs, const float* base_sqnorm, const int* base_parity, const int* idx_lut,
+                  const float* grid, int* idx_out, int64_t ld_i, float* map_out, int64_t ld_m, void* stream);
+
+/* ---- gram-metric block CD (K5, K10): mpq/polish/block_cd.py:332-625 ----
+ * meta per block (196 floats): gram Vs_blk Vs_blk^T | L = stabilize_cholesky(gram) | (L L^T)^-1 | eigenvalue
+ * bounds of L L^T.  Replaces mpq/polish/block_cd.py:383-404 and mpq/linear.py:121-141. */
+int mpq_gram_meta(const float* Vs, int64_t ld, int R, int nb, float* meta, int* fail_count, void* stream);
+/* greedy block gain mean_b rhs_bk Ginv_k rhs_bk^T.  Replaces mpq/polish/block_cd.py:286-306. */
+int mpq_gram_gain(const float* rhs, int64_t ld, int B, int nb, const float* meta, float* gain, void* stream);
+/* chunk operands for blocks order[c0:c0+Kb] (Kb <= 16): VsJ 128 x R, VsJT R x 128, Hsub 128 x 128 of Hf = Vs Vs^T. */
+int mpq_gram_gather(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order, int c0,
+                    int Kb, float* VsJ, float* VsJT, float* Hsub, void* stream);
+/* Sequential block decisions of one chunk per row: target = x + rhs Ginv, exact first-minimum gram search,
+ * accept test, x / idx / residual-norm updates, accepted steps delta (B x 128).  Replaces the block loop of
+ * mpq/polish/block_cd.py:534-547 with _cd_gram_step_impl :212-246. */
+int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* Hsub, const float* meta,
+                   const int* order, int c0, int Kb, const float* base_abs, const int* base_parity, const float* grid,
+                   const uint8_t* sign_id, float* res, int* idx, int64_t ldi, float* delta, int* accepted,
+                   long long* evals, int B, float accept_tol, void* stream);
+/* Standalone exact gram-metric search for N targets sharing one factor L (first minimum of
+ * |tL|^2 + |cL|^2 - 2 (tL).(cL) over the grid).  Replaces E8P12Provider._metric_map_assign
+ * (mpq/polish/block_cd.py:702-739) and the Triton search mpq/polish/triton_e8p12_cd.py:83-180. */
+int mpq_gram_search(const float* targets, int N, const float* L, float lam_lo, float lam_hi, const float* base_abs,
+                    const int* base_parity, const float* grid, const uint8_t* sign_id, int* out_idx, void* stream);
 
 /* ---- rotation ----
  * Block Walsh-Hadamard of the last dim, blocks of `had` (power of two <= 16384), normalized by sqrt(had);

@@ -29,7 +29,14 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_group_minmax": (P, L, I, I, I, I, P, P, L, P),
     "mpq_uniform_rtn": (P, L, P, P, L, I, I, I, I, P, P, L, P),
     "mpq_block_hadamard": (P, L, P, L, I, I, I, P, I, P),
-    "mpq_vamp_rows": (P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, F, F, I, P),
+    "mpq_e8p12_mmse": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, L, P, L, P, L, P, P),
+    "mpq_e8p12_map": (P, L, P, L, P, L, P, F, F, I, I, P, P, P, P, P, P, L, P, L, P),
+    "mpq_gram_meta": (P, L, I, I, P, P, P),
+    "mpq_gram_gain": (P, L, I, I, P, P, P),
+    "mpq_gram_gather": (P, L, I, P, L, P, I, I, P, P, P, P),
+    "mpq_gram_chunk": (P, L, P, L, P, P, P, I, I, P, P, P, P, P, P, L, P, P, P, I, F, P),
+    "mpq_gram_search": (P, I, P, F, F, P, P, P, P, P, P),
+    "mpq_vamp_rows": (P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, F, F, I, P),
     "mpq_gamma_retry": (P, P, I, I, F, P),
     "mpq_vamp_r2": (P, P, P, P, P, P, P, I, I, L, F, P),
     "mpq_linear_epilogue": (P, P, P, P, F, I, I, L, P, P, P),

@@ -47,11 +47,13 @@ __device__ __forceinline__ float nan_to_num(float x, float nan_v, float pinf, fl
   return x;
 }
 
-// mpq/utils.py log_damp_positive: exp((1-d) ln max(p,1e-12) + d ln max(n,1e-12)), float32.
+// mpq/utils.py log_damp_positive: exp((1-d) ln max(p,1e-12) + d ln max(n,1e-12)) in float32 steps, with
+// correctly rounded log/exp (double evaluation, one rounding), as torch's CPU float32 kernels return.
 __device__ __forceinline__ float log_damp(float prev, float nw, float one_minus_d, float d) {
   prev = fmaxf(prev, 1e-12f);
   nw = fmaxf(nw, 1e-12f);
-  return expf(fadd(fmul(one_minus_d, logf(prev)), fmul(d, logf(nw))));
+  const float lp = (float)log((double)prev), ln = (float)log((double)nw);
+  return (float)exp((double)fadd(fmul(one_minus_d, lp), fmul(d, ln)));
 }
 
 // Deterministic block-wide sum (fixed tree order). `red` must hold blockDim.x/32 floats.

@@ -1,0 +1,563 @@
+// Gram-metric block coordinate descent over E8P12 8-blocks (the E8P12 polish).
+//
+// Reference: mpq/polish/block_cd.py:332-625 (block_coordinate_descent_rankspace) with the E8P12
+// provider's full-grid search (_cd_gram_step_impl :212-246, E8P12Provider._metric_map_assign :702-739),
+// per-block metadata :383-404 (Vs_blk Vs_blk^T, stabilize_cholesky mpq/linear.py:121-141,
+// cholesky_inverse) and the greedy block order _batched_greedy_gain :286-306.
+//
+// Search.  For target t and Cholesky factor L of the block gram, the reference scores every codeword c
+// by  |tL|^2 + |cL|^2 - 2 (tL).(cL)  and takes the first minimum.  Here the same float32 score (products
+// and sums in index order, no FMA contraction) decides, but codewords are skipped when a lower bound
+// proves they cannot reach the running minimum:  score(c) >= lam_min(L L^T) |c - t|^2, and the Euclidean
+// distance of every codeword of a (branch, abs) component is  sum_k (|y_k| - |b_k|)^2 + 4 sum_{k flipped}
+// |y_k||b_k|  (y = t - offset) in closed form.  The bound carries a relative safety factor and an
+// absolute margin far above the float32 rounding of the score, so the result equals the exhaustive
+// first-minimum search.
+//
+// Blocks are visited in the greedy order in chunks of up to 16 blocks (128 columns): one warp per row
+// runs the chunk's sequential block decisions with the chunk's cross-block grams in shared memory, and
+// the accepted steps are applied to the rank-space residual by one tensor-core GEMM per chunk.
+#include "common.cuh"
+
+namespace mpq {
+
+constexpr int kChunkBlocks = 16;
+constexpr int kChunkCols = kChunkBlocks * 8;
+
+// ---------------------------------------------------------------------------------------------
+// per-block metadata
+// ---------------------------------------------------------------------------------------------
+
+// Cholesky of an 8x8 SPD matrix (float32, lower), column-by-column as LAPACK's unblocked potf2.
+__device__ bool chol8(const float A[64], float L[64]) {
+  for (int i = 0; i < 64; ++i) L[i] = 0.f;
+  for (int j = 0; j < 8; ++j) {
+    float s = A[j * 8 + j];
+    for (int k = 0; k < j; ++k) s -= L[j * 8 + k] * L[j * 8 + k];
+    if (!(s > 0.f) || !isfinite(s)) return false;
+    const float d = sqrtf(s);
+    L[j * 8 + j] = d;
+    for (int i = j + 1; i < 8; ++i) {
+      float t = A[i * 8 + j];
+      for (int k = 0; k < j; ++k) t -= L[i * 8 + k] * L[j * 8 + k];
+      L[i * 8 + j] = t / d;
+    }
+  }
+  return true;
+}
+
+// Symmetric 8x8 eigenvalue bounds by cyclic Jacobi in double.
+__device__ void eig8_bounds(const double S[64], double& lo, double& hi) {
+  double A[64];
+  for (int i = 0; i < 64; ++i) A[i] = S[i];
+  for (int sweep = 0; sweep < 30; ++sweep) {
+    double off = 0.0;
+    for (int p = 0; p < 8; ++p)
+      for (int q = p + 1; q < 8; ++q) off += A[p * 8 + q] * A[p * 8 + q];
+    if (off < 1e-30) break;
+    for (int p = 0; p < 8; ++p)
+      for (int q = p + 1; q < 8; ++q) {
+        const double apq = A[p * 8 + q];
+        if (fabs(apq) < 1e-300) continue;
+        const double theta = (A[q * 8 + q] - A[p * 8 + p]) / (2.0 * apq);
+        const double t = (theta >= 0 ? 1.0 : -1.0) / (fabs(theta) + sqrt(theta * theta + 1.0));
+        const double c = 1.0 / sqrt(t * t + 1.0), s = t * c;
+        for (int k = 0; k < 8; ++k) {
+          const double akp = A[k * 8 + p], akq = A[k * 8 + q];
+          A[k * 8 + p] = c * akp - s * akq;
+          A[k * 8 + q] = s * akp + c * akq;
+        }
+        for (int k = 0; k < 8; ++k) {
+          const double apk = A[p * 8 + k], aqk = A[q * 8 + k];
+          A[p * 8 + k] = c * apk - s * aqk;
+          A[q * 8 + k] = s * apk + c * aqk;
+        }
+      }
+  }
+  double off = 0.0;
+  for (int p = 0; p < 8; ++p)
+    for (int q = 0; q < 8; ++q)
+      if (p != q) off += A[p * 8 + q] * A[p * 8 + q];
+  const double r = sqrt(off);  // Gershgorin-style slack for the residual off-diagonal mass
+  lo = 1e300;
+  hi = -1e300;
+  for (int i = 0; i < 8; ++i) {
+    lo = fmin(lo, A[i * 8 + i]);
+    hi = fmax(hi, A[i * 8 + i]);
+  }
+  lo -= r;
+  hi += r;
+}
+
+// One warp per block: gram = Vs_blk Vs_blk^T, L = stabilize_cholesky(gram), ginv = (L L^T)^-1 and
+// eigenvalue bounds of L L^T.  meta layout per block: [gram 64 | L 64 | ginv 64 | lam_lo, lam_hi, ok, pad]
+constexpr int kMeta = 196;
+
+__global__ void k_gram_meta(const float* __restrict__ Vs, int64_t ld, int R, int nb, float* __restrict__ meta,
+                            int* __restrict__ fail_count) {
+  const int blk = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (blk >= nb) return;
+  float g[64];
+  for (int i = 0; i < 8; ++i)
+    for (int j = i; j < 8; ++j) {
+      const float* a = Vs + (int64_t)(blk * 8 + i) * ld;
+      const float* b = Vs + (int64_t)(blk * 8 + j) * ld;
+      float acc = 0.f;
+      for (int r = lane; r < R; r += 32) acc += a[r] * b[r];
+      acc = warp_sum(acc);
+      g[i * 8 + j] = acc;
+      g[j * 8 + i] = acc;
+    }
+  if (lane != 0) return;
+  float* m = meta + (int64_t)blk * kMeta;
+  for (int i = 0; i < 64; ++i) m[i] = g[i];
+  // stabilize_cholesky: add 2^k * floor * I cumulatively until the factorization succeeds
+  float dmax = 0.f;
+  for (int i = 0; i < 8; ++i) dmax = fmaxf(dmax, fabsf(g[i * 9]));
+  const float floor_ = dmax * 1e-6f + 1e-6f;
+  float A[64], L[64];
+  for (int i = 0; i < 64; ++i) A[i] = g[i];
+  bool ok = false;
+  for (int k = 0; k < 7 && !ok; ++k) {
+    ok = chol8(A, L);
+    if (!ok && k < 6)
+      for (int i = 0; i < 8; ++i) A[i * 9] += (float)(1 << k) * floor_;
+  }
+  if (!ok) {
+    atomicAdd(fail_count, 1);
+    for (int i = 0; i < 64; ++i) L[i] = (i % 9 == 0) ? 1.f : 0.f;
+  }
+  for (int i = 0; i < 64; ++i) m[64 + i] = L[i];
+  // (L L^T)^-1 = Linv^T Linv  in double
+  double Li[64];
+  for (int i = 0; i < 64; ++i) Li[i] = 0.0;
+  for (int j = 0; j < 8; ++j) {
+    Li[j * 8 + j] = 1.0 / (double)L[j * 8 + j];
+    for (int i = j + 1; i < 8; ++i) {
+      double s = 0.0;
+      for (int k = j; k < i; ++k) s += (double)L[i * 8 + k] * Li[k * 8 + j];
+      Li[i * 8 + j] = -s / (double)L[i * 8 + i];
+    }
+  }
+  double S[64];
+  for (int i = 0; i < 8; ++i)
+    for (int j = 0; j < 8; ++j) {
+      double s = 0.0, q = 0.0;
+      for (int k = 0; k < 8; ++k) {
+        s += Li[k * 8 + i] * Li[k * 8 + j];
+        q += (double)L[i * 8 + k] * (double)L[j * 8 + k];
+      }
+      m[128 + i * 8 + j] = (float)s;
+      S[i * 8 + j] = q;
+    }
+  double lo, hi;
+  eig8_bounds(S, lo, hi);
+  m[192] = (float)fmax(lo * (1.0 - 1e-6), 0.0);
+  m[193] = (float)(hi * (1.0 + 1e-6));
+  m[194] = ok ? 1.f : 0.f;
+  m[195] = 0.f;
+}
+
+// gain[k] = mean_b sum_j rhs[b,8k+j] (rhs_bk Ginv_k)_j  (mpq/polish/block_cd.py:298-303); one CTA per block.
+__global__ void __launch_bounds__(256) k_gram_gain(const float* __restrict__ rhs, int64_t ld, int B,
+                                                   const float* __restrict__ meta, float* __restrict__ gain) {
+  __shared__ float red[32];
+  __shared__ float gi[64];
+  const int k = blockIdx.x;
+  for (int i = threadIdx.x; i < 64; i += blockDim.x) gi[i] = meta[(int64_t)k * kMeta + 128 + i];
+  __syncthreads();
+  float acc = 0.f;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    float r[8];
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = rhs[b * ld + k * 8 + j];
+    float s = 0.f;
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float d = 0.f;
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) d += r[i] * gi[i * 8 + j];
+      s += r[j] * d;
+    }
+    acc += s;
+  }
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) gain[k] = t / (float)(B > 0 ? B : 1);
+}
+
+// Chunk operands for the blocks order[c0 : c0 + Kb]:  VsJ (128 x R) = rows of Vs for the chunk's columns,
+// VsJT (R x 128) its transpose, Hsub (128 x 128) = Hf[cols, cols] with Hf = Vs Vs^T.
+__global__ void __launch_bounds__(256) k_gram_gather(const float* __restrict__ Vs, int64_t ldv, int R,
+                                                     const float* __restrict__ Hf, int64_t ldh,
+                                                     const int* __restrict__ order, int c0, int Kb,
+                                                     float* __restrict__ VsJ, float* __restrict__ VsJT,
+                                                     float* __restrict__ Hsub) {
+  __shared__ float tile[32][33];
+  const int r0 = blockIdx.x * 32, k0 = blockIdx.y * 32;  // k: chunk column 0..127
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int kk = ty; kk < 32; kk += 8) {
+    const int k = k0 + kk, r = r0 + tx;
+    float v = 0.f;
+    if (k < Kb * 8 && r < R) v = Vs[(int64_t)(order[c0 + k / 8] * 8 + (k & 7)) * ldv + r];
+    tile[kk][tx] = v;
+    if (r < R) VsJ[(int64_t)k * R + r] = v;
+  }
+  __syncthreads();
+  for (int rr = ty; rr < 32; rr += 8) {
+    const int r = r0 + rr, k = k0 + tx;
+    if (r < R) VsJT[(int64_t)r * kChunkCols + k] = tile[tx][rr];
+  }
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < 32 * kChunkCols; i += blockDim.x) {
+      const int k = k0 + i / kChunkCols, l = i % kChunkCols;
+      float v = 0.f;
+      if (k < Kb * 8 && l < Kb * 8)
+        v = Hf[(int64_t)(order[c0 + k / 8] * 8 + (k & 7)) * ldh + order[c0 + l / 8] * 8 + (l & 7)];
+      Hsub[k * kChunkCols + l] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// exact pruned gram search (warp-cooperative)
+// ---------------------------------------------------------------------------------------------
+
+struct E8Small {
+  const float* base_abs;   // 256 x 8 (shared memory)
+  const int* base_parity;  // 256 (shared memory)
+  const float* grid;       // 65536 x 8 (global)
+  const uint8_t* sign_id;  // 65536: sign bits of (grid[c] - offset(c)) (global)
+};
+
+// exact float32 score of codeword c:  (tn + |gL|^2) - 2 (tl . gL), index-ordered sums, no FMA
+__device__ __forceinline__ float exact_score(const float* __restrict__ grid, int c, const float* L, const float tl[8],
+                                             float tn) {
+  float gv[8];
+  const float4* gp = reinterpret_cast<const float4*>(grid + (int64_t)c * 8);
+  const float4 g0 = __ldg(gp), g1 = __ldg(gp + 1);
+  gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+  gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+  float gn = 0.f, cr = 0.f;
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float gl = 0.f;
+    #pragma unroll
+    for (int k = j; k < 8; ++k) gl = fadd(gl, fmul(gv[k], L[k * 8 + j]));  // L lower: k >= j
+    gn = fadd(gn, fmul(gl, gl));
+    cr = fadd(cr, fmul(tl[j], gl));
+  }
+  return fsub(fadd(tn, gn), fmul(2.f, cr));
+}
+
+__device__ __forceinline__ bool better(float s, int c, float bs, int bc) { return s < bs || (s == bs && c < bc); }
+
+__device__ __forceinline__ void warp_argmin(float& s, int& c) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float os = __shfl_xor_sync(0xffffffffu, s, o);
+    const int oc = __shfl_xor_sync(0xffffffffu, c, o);
+    if (better(os, oc, s, c)) { s = os; c = oc; }
+  }
+}
+
+// Returns the first-minimum codeword index (identical in every lane) and the number of exact evaluations.
+__device__ int gram_search_warp(const E8Small& e8, const float t[8], const float* L, float lam_lo, float lam_hi,
+                                int* n_exact) {
+  const int lane = threadIdx.x & 31;
+  float tl[8], tn = 0.f;
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float s = 0.f;
+    #pragma unroll
+    for (int k = j; k < 8; ++k) s = fadd(s, fmul(t[k], L[k * 8 + j]));
+    tl[j] = s;
+  }
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) tn = fadd(tn, fmul(tl[j], tl[j]));
+  // closed-form Euclidean data per component: base distance, per-coordinate flip weights, sign pattern
+  // lane owns abs = lane + 32*i, i = 0..7, for both branches
+  float dmin[16];
+  #pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int a = lane + 32 * i;
+    const float* ab = e8.base_abs + a * 8;
+    #pragma unroll
+    for (int br = 0; br < 2; ++br) {
+      const float off = br ? -0.25f : 0.25f;
+      float base = 0.f, mn = INFINITY;
+      int par = 0;
+      #pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float y = t[k] - off;
+        const float ay = fabsf(y);
+        const float d = ay - ab[k];
+        base += d * d;
+        const float w = ay * ab[k];
+        mn = fminf(mn, w);
+        par ^= (y < 0.f) ? 1 : 0;
+      }
+      dmin[i * 2 + br] = base + ((par != e8.base_parity[a]) ? 4.f * mn : 0.f);
+    }
+  }
+  // initial incumbent: the Euclidean-nearest codeword
+  float bd = INFINITY;
+  int bcomp = 0;
+  #pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const int comp = (lane + 32 * (q >> 1)) * 2 + (q & 1);
+    if (dmin[q] < bd || (dmin[q] == bd && comp < bcomp)) { bd = dmin[q]; bcomp = comp; }
+  }
+  {
+    float s = bd;
+    int c = bcomp;
+    warp_argmin(s, c);
+    bcomp = c;
+  }
+  int count = 0;
+  float best = INFINITY;
+  int best_c = 0x7fffffff;
+  // Safety margin on the bound: relative 1e-5 (float32 rounding of the distances) and an absolute term
+  // 1e-5 * (|tL|^2 + lam_hi * 16) well above the rounding of the float32 score.
+  const float marg = 1e-5f * (tn + lam_hi * 20.f) + 1e-30f;
+  const float lam = lam_lo * (1.f - 1e-5f);
+  auto eval_comp = [&](int comp) {
+    const int a = comp >> 1, br = comp & 1;
+    const float off = br ? -0.25f : 0.25f;
+    const float* ab = e8.base_abs + a * 8;
+    float w[8], base = 0.f;
+    int sgn = 0;
+    #pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float y = t[k] - off;
+      const float ay = fabsf(y);
+      const float d = ay - ab[k];
+      base += d * d;
+      w[k] = 4.f * ay * ab[k];
+      if (y < 0.f) sgn |= 1 << k;
+    }
+    // the 128 codewords (a<<8)|s with parity(s) = br; their sign pattern relative to the offset comes
+    // from the codebook's sign table, and the coordinates whose sign differs from y's cost 4|y_k||b_k|.
+    #pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      // enumerate the 128 raw sign bytes of this branch: s = 2*m + bit0, bit0 chosen to give parity br
+      const int m = lane * 4 + u;  // 0..127
+      const int hi7 = m << 1;
+      int par7 = 0;
+      #pragma unroll
+      for (int k = 1; k < 8; ++k) par7 ^= (hi7 >> k) & 1;
+      const int s = hi7 | (par7 ^ br);
+      const int real = __ldg(e8.sign_id + ((a << 8) | s));
+      const int diff = real ^ sgn;
+      float dE = base;
+      #pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (diff & (1 << k)) dE += w[k];
+      if (lam * dE > best + marg) continue;
+      const int c = (a << 8) | s;
+      const float sc = exact_score(e8.grid, c, L, tl, tn);
+      ++count;
+      if (better(sc, c, best, best_c)) { best = sc; best_c = c; }
+    }
+    warp_argmin(best, best_c);
+  };
+  eval_comp(bcomp);
+  #pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const int comp = (lane + 32 * (q >> 1)) * 2 + (q & 1);
+    unsigned mask = __ballot_sync(0xffffffffu, comp != bcomp && lam * dmin[q] <= best + marg);
+    while (mask) {
+      const int src = __ffs(mask) - 1;
+      mask &= mask - 1;
+      const int cc = (src + 32 * (q >> 1)) * 2 + (q & 1);
+      if (lam * __shfl_sync(0xffffffffu, dmin[q], src) <= best + marg) eval_comp(cc);
+    }
+  }
+  if (n_exact) *n_exact = count;
+  return best_c;
+}
+
+// ---------------------------------------------------------------------------------------------
+// chunk of greedy block decisions (one warp per row)
+// ---------------------------------------------------------------------------------------------
+
+struct GramChunkArgs {
+  float* x; int64_t ldx;           // B x n  (current decisions)
+  const float* rhs; int64_t ldr;   // B x 128: residual_u @ Vs_J^T at chunk start
+  const float* Hsub;               // 128 x 128 cross-block grams of the chunk
+  const float* meta;               // nb x kMeta
+  const int* order; int c0; int Kb;
+  const float* base_abs; const int* base_parity; const float* grid; const uint8_t* sign_id;
+  float* res;                      // B residual norms
+  int* idx; int64_t ldi;           // B x nb codeword indices
+  float* delta;                    // B x 128 accepted steps
+  int* accepted;                   // accepted-update counter
+  long long* evals;                // exact score evaluations (diagnostic)
+  int B; float accept_tol;
+};
+
+__global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
+  extern __shared__ float sm[];
+  float* Hs = sm;                                    // 128 x 128
+  float* s_abs = Hs + kChunkCols * kChunkCols;       // 256 x 8
+  int* s_par = reinterpret_cast<int*>(s_abs + 2048); // 256
+  float* s_meta = reinterpret_cast<float*>(s_par + 256);  // 16 x kMeta
+  float* s_rhs = s_meta + kChunkBlocks * kMeta;      // 8 warps x 128
+  for (int i = threadIdx.x; i < kChunkCols * kChunkCols; i += blockDim.x) Hs[i] = a.Hsub[i];
+  for (int i = threadIdx.x; i < 2048; i += blockDim.x) s_abs[i] = a.base_abs[i];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) s_par[i] = a.base_parity[i];
+  for (int i = threadIdx.x; i < a.Kb * kMeta; i += blockDim.x)
+    s_meta[i] = a.meta[(int64_t)a.order[a.c0 + i / kMeta] * kMeta + i % kMeta];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * 8 + warp;
+  if (b >= a.B) return;
+  float* rh = s_rhs + warp * kChunkCols;
+  for (int i = lane; i < kChunkCols; i += 32) rh[i] = i < a.Kb * 8 ? a.rhs[b * a.ldr + i] : 0.f;
+  __syncwarp();
+  E8Small e8{s_abs, s_par, a.grid, a.sign_id};
+  float res = a.res[b];
+  int acc_n = 0;
+  long long evals = 0;
+  for (int p = 0; p < a.Kb; ++p) {
+    const int blk = a.order[a.c0 + p];
+    const float* m = s_meta + p * kMeta;
+    const float* G = m;
+    const float* L = m + 64;
+    const float* Gi = m + 128;
+    float xb[8], r[8], t[8];
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      xb[j] = a.x[b * a.ldx + blk * 8 + j];
+      r[j] = rh[p * 8 + j];
+    }
+    // target = x_blk + rhs @ ginv
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float s = 0.f;
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) s = fadd(s, fmul(r[i], Gi[i * 8 + j]));
+      t[j] = fadd(xb[j], s);
+    }
+    int ne = 0;
+    const int c = gram_search_warp(e8, t, L, m[192], m[193], &ne);
+    evals += ne;
+    float d[8], cross = 0.f, dn = 0.f;
+    const float* gv = a.grid + (int64_t)c * 8;
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      d[j] = fsub(__ldg(gv + j), xb[j]);
+      cross = fadd(cross, fmul(r[j], d[j]));
+    }
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float s = 0.f;
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) s = fadd(s, fmul(d[i], G[i * 8 + j]));
+      dn = fadd(dn, fmul(s, d[j]));
+    }
+    dn = fmaxf(dn, 0.f);
+    const float cand = fmaxf(fsub(fadd(res, dn), fmul(2.f, cross)), 0.f);
+    const bool acc = fadd(cand, 1e-12f) < fmul(res, 1.f + a.accept_tol);
+    if (acc) {
+      res = cand;
+      ++acc_n;
+      if (lane < 8) a.x[b * a.ldx + blk * 8 + lane] = __ldg(gv + lane);
+      if (lane == 0) a.idx[b * a.ldi + blk] = c;
+      // later blocks of the chunk see this step: rhs_q -= d @ Hsub[p-block, q-block]
+      for (int col = lane; col < a.Kb * 8; col += 32) {
+        if (col >= (p + 1) * 8) {
+          float s = 0.f;
+          #pragma unroll
+          for (int i = 0; i < 8; ++i) s = fadd(s, fmul(d[i], Hs[(p * 8 + i) * kChunkCols + col]));
+          rh[col] = fsub(rh[col], s);
+        }
+      }
+    }
+    if (lane < 8) a.delta[(int64_t)b * kChunkCols + p * 8 + lane] = acc ? d[lane] : 0.f;
+    __syncwarp();
+  }
+  for (int i = a.Kb * 8 + lane; i < kChunkCols; i += 32) a.delta[(int64_t)b * kChunkCols + i] = 0.f;
+  if (lane == 0) {
+    a.res[b] = res;
+    if (acc_n) atomicAdd(a.accepted, acc_n);
+    if (a.evals) atomicAdd((unsigned long long*)a.evals, (unsigned long long)evals);
+  }
+}
+
+// Standalone search for a batch of targets that share one block factor (the provider entry point).
+__global__ void k_gram_search(const float* __restrict__ targets, int N, const float* __restrict__ L,
+                              float lam_lo, float lam_hi, const float* __restrict__ base_abs,
+                              const int* __restrict__ base_parity, const float* __restrict__ grid,
+                              const uint8_t* __restrict__ sign_id, int* __restrict__ out_idx) {
+  __shared__ float s_abs[2048];
+  __shared__ int s_par[256];
+  __shared__ float s_L[64];
+  for (int i = threadIdx.x; i < 2048; i += blockDim.x) s_abs[i] = base_abs[i];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) s_par[i] = base_parity[i];
+  for (int i = threadIdx.x; i < 64; i += blockDim.x) s_L[i] = L[i];
+  __syncthreads();
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (w >= N) return;
+  float t[8];
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) t[j] = targets[(int64_t)w * 8 + j];
+  E8Small e8{s_abs, s_par, grid, sign_id};
+  const int c = gram_search_warp(e8, t, s_L, lam_lo, lam_hi, nullptr);
+  if ((threadIdx.x & 31) == 0) out_idx[w] = c;
+}
+
+}  // namespace mpq
+
+using namespace mpq;
+
+MPQ_API int mpq_gram_meta(const float* Vs, int64_t ld, int R, int nb, float* meta, int* fail_count, void* stream) {
+  MPQ_CHECK_ARG(Vs && meta && fail_count, "mpq_gram_meta: null pointer");
+  if (nb == 0) return MPQ_OK;
+  k_gram_meta<<<(nb * 32 + 127) / 128, 128, 0, (cudaStream_t)stream>>>(Vs, ld, R, nb, meta, fail_count);
+  return launch_status("mpq_gram_meta");
+}
+
+MPQ_API int mpq_gram_gain(const float* rhs, int64_t ld, int B, int nb, const float* meta, float* gain, void* stream) {
+  MPQ_CHECK_ARG(rhs && meta && gain, "mpq_gram_gain: null pointer");
+  if (nb == 0) return MPQ_OK;
+  k_gram_gain<<<nb, 256, 0, (cudaStream_t)stream>>>(rhs, ld, B, meta, gain);
+  return launch_status("mpq_gram_gain");
+}
+
+MPQ_API int mpq_gram_gather(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order,
+                            int c0, int Kb, float* VsJ, float* VsJT, float* Hsub, void* stream) {
+  MPQ_CHECK_ARG(Vs && Hf && order && VsJ && VsJT && Hsub, "mpq_gram_gather: null pointer");
+  MPQ_CHECK_ARG(Kb >= 1 && Kb <= kChunkBlocks, "mpq_gram_gather: Kb must be in [1, %d]", kChunkBlocks);
+  dim3 grid((R + 31) / 32, kChunkCols / 32);
+  k_gram_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, VsJ, VsJT, Hsub);
+  return launch_status("mpq_gram_gather");
+}
+
+MPQ_API int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* Hsub, const float* meta,
+                           const int* order, int c0, int Kb, const float* base_abs, const int* base_parity,
+                           const float* grid, const uint8_t* sign_id, float* res, int* idx, int64_t ldi, float* delta,
+                           int* accepted, long long* evals, int B, float accept_tol, void* stream) {
+  MPQ_CHECK_ARG(x && rhs && Hsub && meta && order && base_abs && base_parity && grid && sign_id && res && idx && delta &&
+                    accepted,
+                "mpq_gram_chunk: null pointer");
+  MPQ_CHECK_ARG(Kb >= 1 && Kb <= kChunkBlocks, "mpq_gram_chunk: Kb must be in [1, %d]", kChunkBlocks);
+  MPQ_CHECK_ARG(((uintptr_t)grid & 15) == 0, "mpq_gram_chunk: grid must be 16-byte aligned");
+  if (B == 0) return MPQ_OK;
+  GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, base_abs, base_parity, grid, sign_id, res, idx, ldi,
+                  delta, accepted, evals, B, accept_tol};
+  const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
+  cudaFuncSetAttribute(k_gram_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_gram_chunk<<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
+  return launch_status("mpq_gram_chunk");
+}
+
+MPQ_API int mpq_gram_search(const float* targets, int N, const float* L, float lam_lo, float lam_hi,
+                            const float* base_abs, const int* base_parity, const float* grid, const uint8_t* sign_id,
+                            int* out_idx, void* stream) {
+  MPQ_CHECK_ARG(targets && L && base_abs && base_parity && grid && sign_id && out_idx, "mpq_gram_search: null pointer");
+  MPQ_CHECK_ARG(((uintptr_t)grid & 15) == 0, "mpq_gram_search: grid must be 16-byte aligned");
+  if (N == 0) return MPQ_OK;
+  k_gram_search<<<(N * 32 + 255) / 256, 256, 0, (cudaStream_t)stream>>>(targets, N, L, lam_lo, lam_hi, base_abs,
+                                                                        base_parity, grid, sign_id, out_idx);
+  return launch_status("mpq_gram_search");
+}

@@ -44,14 +44,14 @@ struct RowState {
 // Stage A+B of one VAMP iteration (mpq/solver.py:559-631 up to the linear module, plus the
 // gamma-only parts of linear_mmse_exact and the EM trace term).  One warp per row; the
 // rank-space sums over S run in a fixed lane-strided order.
-__global__ void k_vamp_rows(RowState st, const float* __restrict__ S, int B, int n, int R, float obs, float damping,
-                            int final_retry) {
+__global__ void k_vamp_rows(RowState st, const float* __restrict__ S, int B, int n, int n_var, int R, float obs,
+                            float damping, int final_retry) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= B) return;
   const int b = warp;
   const float g1w = st.gamma1_work[b];
-  const float a1_raw = fmul(g1w, fdiv(st.var_rowsum[b], (float)n));  // gamma1 * var.mean(dim=1)
+  const float a1_raw = fmul(g1w, fdiv(st.var_rowsum[b], (float)n_var));  // gamma1 * var.mean(dim=1)
   float a1 = a1_raw;
   if (!alpha_valid(a1_raw)) {
     if (lane == 0) {
@@ -253,7 +253,7 @@ using namespace mpq;
 MPQ_API int mpq_vamp_rows(const float* var_rowsum, float* gamma1, float* gamma1_work, float* alpha1, float* eta1,
                           float* gamma2_new, float* gamma2, const float* gamma2_prev, float* alpha2, float* eta2,
                           float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int B,
-                          int n, int R, float obs, float damping, int final_retry, void* stream) {
+                          int n, int n_var, int R, float obs, float damping, int final_retry, void* stream) {
   MPQ_CHECK_ARG(var_rowsum && gamma1 && gamma1_work && alpha1 && eta1 && gamma2_new && gamma2 && alpha2 && eta2 &&
                     gamma1_new && gamma1_next && trace && flags && S,
                 "mpq_vamp_rows: null pointer");
@@ -262,7 +262,8 @@ MPQ_API int mpq_vamp_rows(const float* var_rowsum, float* gamma1, float* gamma1_
               alpha2, eta2, gamma1_new, gamma1_next, trace, flags};
   const int threads = 256;
   const int blocks = (B * 32 + threads - 1) / threads;
-  k_vamp_rows<<<blocks, threads, 0, (cudaStream_t)stream>>>(st, S, B, n, R, obs, damping, final_retry);
+  MPQ_CHECK_ARG(n_var >= 1, "mpq_vamp_rows: n_var must be >= 1");
+  k_vamp_rows<<<blocks, threads, 0, (cudaStream_t)stream>>>(st, S, B, n, n_var, R, obs, damping, final_retry);
   return launch_status("mpq_vamp_rows");
 }
 

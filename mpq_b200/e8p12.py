@@ -1,0 +1,202 @@
+"""E8P12 prior (factorized posterior / MAP / nearest codeword) and the gram-metric block CD engine.
+
+Reference: mpq/priors/e8p12.py (prior_scale_from_center :47-63, vamp_vector_map_e8p12 :541-631,
+vamp_vector_discrete_mmse_e8p12 :815-968) and mpq/polish/block_cd.py (block_coordinate_descent_rankspace
+:332-625 with the E8P12 gram provider).  All numerical work runs in libmpq_b200.so.
+"""
+from __future__ import annotations
+
+from typing import Any, Dict, Optional, Tuple
+
+import torch
+
+from . import ops
+from ._lib import call, ptr
+from .codebook import factor_tables
+
+
+def prior_scale_from_center(prior_center_blocks: Optional[torch.Tensor], mode: str) -> Optional[torch.Tensor]:
+    """mpq/priors/e8p12.py:47-63 (per-block prior scale; plumbing on B x nb values)."""
+    if prior_center_blocks is None:
+        return None
+    mode = str(mode or "absmax").strip().lower()
+    c = prior_center_blocks.to(torch.float32)
+    if mode in ("none", "unit", "legacy"):
+        return torch.ones(c.shape[:-1] + (1,), dtype=torch.float32, device=c.device)
+    if mode in ("absmax", "exact_full", "exact_full_absmax"):
+        s = c.abs().amax(dim=-1, keepdim=True)
+    elif mode in ("rms", "std"):
+        s = c.square().mean(dim=-1, keepdim=True).sqrt()
+    elif mode in ("mean_abs", "l1"):
+        s = c.abs().mean(dim=-1, keepdim=True)
+    else:
+        raise ValueError(f"unsupported prior_tau_scale_mode={mode!r}; supported: none|absmax|rms|mean_abs")
+    return s.clamp_min_(1e-12)
+
+
+def _tab_ptrs(t):
+    return (ptr(t["base_abs"]), ptr(t["base_sqnorm"]), ptr(t["base_parity"]), ptr(t["idx_lut"]), ptr(t["grid"]))
+
+
+def e8p12_map_rows(r1: torch.Tensor, cb, *, gamma: Optional[torch.Tensor] = None, fixed_gamma: float = 0.0,
+                   center: Optional[torch.Tensor] = None, pscale: Optional[torch.Tensor] = None,
+                   prior_tau: float = 0.0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """MAP codewords of a (B, n) message (n = 8 nb): returns (values (B, n), indices (B, nb) int32)."""
+    if not r1.is_cuda:
+        raise ValueError("E8P12 kernels require CUDA tensors (there is no CPU path)")
+    B, n = r1.shape
+    nb = n // 8
+    t = factor_tables(cb, r1.device)
+    idx = torch.empty(B, nb, device=r1.device, dtype=torch.int32)
+    vals = torch.empty(B, n, device=r1.device, dtype=torch.float32)
+    call("mpq_e8p12_map", ptr(r1), r1.stride(0), ptr(center), center.stride(0) if center is not None else 0,
+         ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(gamma), float(fixed_gamma), float(prior_tau),
+         B, nb, *_tab_ptrs(t), ptr(idx), idx.stride(0), ptr(vals), vals.stride(0))
+    return vals, idx
+
+
+def e8p12_nearest(X: torch.Tensor, cb) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Nearest codeword of each 8-vector (N, 8): the MAP at unit precision without prior."""
+    X = X.to(torch.float32).reshape(-1, 8)
+    N = X.shape[0]
+    per = 64
+    rows = (N + per - 1) // per
+    pad = rows * per - N
+    Xp = torch.cat([X, X.new_zeros(pad, 8)]) if pad else X.contiguous()
+    vals, idx = e8p12_map_rows(Xp.reshape(rows, per * 8), cb, fixed_gamma=1.0)
+    return vals.reshape(-1, 8)[:N], idx.reshape(-1)[:N].to(torch.int64)
+
+
+def _fold_args(r1_blocks, prior_center_blocks, prior_scale_blocks, prior_tau, prior_tau_scale_mode):
+    B, nb, _ = r1_blocks.shape
+    r1 = r1_blocks.reshape(B, nb * 8).to(torch.float32).contiguous()
+    center = pscale = None
+    tau = float(prior_tau)
+    if tau > 0.0 and prior_center_blocks is not None:
+        center = prior_center_blocks.reshape(B, nb * 8).to(torch.float32).contiguous()
+        if prior_scale_blocks is None:
+            prior_scale_blocks = prior_scale_from_center(prior_center_blocks, prior_tau_scale_mode)
+        pscale = prior_scale_blocks.reshape(B, nb).to(torch.float32).contiguous()
+    else:
+        tau = 0.0
+    return r1, center, pscale, tau
+
+
+@torch.inference_mode()
+def vamp_vector_map_e8p12(*, r1_blocks, gamma1, cb, blocks_per_chunk: int = 64, need_stats: bool = False,
+                          prior_center_blocks=None, prior_scale_blocks=None, prior_tau: float = 0.0,
+                          prior_tau_scale_mode: str = "absmax") -> Dict[str, Any]:
+    """mpq/priors/e8p12.py:541-631."""
+    B, nb, _ = r1_blocks.shape
+    r1, center, pscale, tau = _fold_args(r1_blocks, prior_center_blocks, prior_scale_blocks, prior_tau,
+                                         prior_tau_scale_mode)
+    g = gamma1.reshape(B).to(device=r1.device, dtype=torch.float32).contiguous()
+    vals, idx = e8p12_map_rows(r1, cb, gamma=g, center=center, pscale=pscale, prior_tau=tau)
+    out: Dict[str, Any] = {"map_idxs": idx.to(torch.int64), "map_vals": vals.reshape(B, nb, 8)}
+    if need_stats:
+        out["margin"] = 0.0
+    return out
+
+
+@torch.inference_mode()
+def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, blocks_per_chunk: int = 64, need_stats: bool = False,
+                                    prior_center_blocks=None, prior_scale_blocks=None, prior_tau: float = 0.0,
+                                    prior_tau_scale_mode: str = "absmax", compile_prior: bool = True,
+                                    return_logZ_blocks: bool = False, return_margin_blocks: bool = False,
+                                    return_entropy_blocks: bool = False) -> Dict[str, Any]:
+    """mpq/priors/e8p12.py:815-968 (need_stats=False; the diagnostics entropy/margin are not computed)."""
+    if need_stats or return_logZ_blocks or return_margin_blocks or return_entropy_blocks:
+        raise NotImplementedError("E8P12 posterior diagnostics (entropy/margin/logZ) are not built")
+    B, nb, _ = r1_blocks.shape
+    r1, center, pscale, tau = _fold_args(r1_blocks, prior_center_blocks, prior_scale_blocks, prior_tau,
+                                         prior_tau_scale_mode)
+    dev = r1.device
+    t = factor_tables(cb, dev)
+    g = gamma1.reshape(B).to(device=dev, dtype=torch.float32).contiguous()
+    x1 = torch.empty(B, nb * 8, device=dev, dtype=torch.float32)
+    var1 = torch.empty(B, nb, device=dev, dtype=torch.float32)
+    idx = torch.empty(B, nb, device=dev, dtype=torch.int32)
+    mvals = torch.empty(B, nb * 8, device=dev, dtype=torch.float32)
+    vsum = torch.empty(B, device=dev, dtype=torch.float32)
+    call("mpq_e8p12_mmse", ptr(r1), r1.stride(0), ptr(center), center.stride(0) if center is not None else 0,
+         ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(g), float(tau), B, nb, *_tab_ptrs(t),
+         ptr(x1), x1.stride(0), ptr(var1), var1.stride(0), ptr(idx), idx.stride(0), ptr(mvals), mvals.stride(0),
+         ptr(vsum))
+    alpha1 = gamma1.to(device=dev, dtype=torch.float32).reshape(B, 1) * (vsum / float(nb)).reshape(B, 1)
+    return {"x1_blocks": x1.reshape(B, nb, 8), "var1": var1, "map_idxs": idx.to(torch.int64),
+            "map_vals": mvals.reshape(B, nb, 8), "alpha1": alpha1, "entropy": 0.0, "margin": 0.0}
+
+
+@torch.inference_mode()
+def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, sweeps: int,
+                  idxs_init: torch.Tensor, accept_tol: float = 0.0, opVs: Optional[ops.Operand] = None,
+                  opVsT: Optional[ops.Operand] = None) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
+    """Gram-metric greedy block CD over E8P12 8-blocks (mpq/polish/block_cd.py:332-625, E8P12Provider, metric
+    'gram').  Returns (x, idxs int64 (B, nb), stats)."""
+    dev = x.device
+    B, n = x.shape
+    nb = n // 8
+    R = int(Vs.shape[1])
+    t = factor_tables(cb, dev)
+    Vs = Vs.to(torch.float32).contiguous()
+    opVs = opVs or ops.Operand(Vs)
+    opVsT = opVsT or ops.Operand(Vs.t().contiguous())
+    x_work = x.to(torch.float32).clone()
+    idx = idxs_init.to(device=dev, dtype=torch.int32).contiguous().clone()
+    res_u = ops.mm_nt(x_work, opVsT)
+    res_norm = torch.empty(B, device=dev, dtype=torch.float32)
+    call("mpq_residual", ptr(Y_u), ptr(res_u), B, R, res_u.stride(0), ptr(res_norm))
+    meta = torch.empty(nb, 196, device=dev, dtype=torch.float32)
+    fails = torch.zeros(1, device=dev, dtype=torch.int32)
+    call("mpq_gram_meta", ptr(Vs), Vs.stride(0), R, nb, ptr(meta), ptr(fails))
+    Hf = ops.mm_nt(Vs, opVs)  # Vs Vs^T: cross-block grams
+    gain = torch.empty(nb, device=dev, dtype=torch.float32)
+    order = torch.empty(nb, device=dev, dtype=torch.int32)
+    VsJ = torch.empty(128, R, device=dev, dtype=torch.float32)
+    VsJT = torch.empty(R, 128, device=dev, dtype=torch.float32)
+    Hsub = torch.empty(128, 128, device=dev, dtype=torch.float32)
+    rhsJ = torch.empty(B, 128, device=dev, dtype=torch.float32)
+    delta = torch.empty(B, 128, device=dev, dtype=torch.float32)
+    accepted = torch.zeros(1, device=dev, dtype=torch.int32)
+    evals = torch.zeros(1, device=dev, dtype=torch.int64)
+    trace = [float(res_norm.double().mean().item())]
+    for _ in range(max(int(sweeps), 0)):
+        rhs_all = ops.mm_nt(res_u, opVs)
+        call("mpq_gram_gain", ptr(rhs_all), rhs_all.stride(0), B, nb, ptr(meta), ptr(gain))
+        del rhs_all
+        call("mpq_argsort_desc", ptr(gain), nb, ptr(order))
+        for c0 in range(0, nb, 16):
+            Kb = min(16, nb - c0)
+            kc = 8 * Kb
+            call("mpq_gram_gather", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb, ptr(VsJ),
+                 ptr(VsJT), ptr(Hsub))
+            ops.mm_nt(res_u, VsJ[:kc], out=rhsJ[:, :kc])
+            call("mpq_gram_chunk", ptr(x_work), x_work.stride(0), ptr(rhsJ), rhsJ.stride(0), ptr(Hsub), ptr(meta),
+                 ptr(order), c0, Kb, ptr(t["base_abs"]), ptr(t["base_parity"]), ptr(t["grid"]), ptr(t["sign_id"]),
+                 ptr(res_norm), ptr(idx), idx.stride(0), ptr(delta), ptr(accepted), ptr(evals), B, float(accept_tol))
+            ops.mm_nt(delta[:, :kc], VsJT[:, :kc], out=res_u, alpha=-1.0, beta=1.0)
+        trace.append(float(res_norm.double().mean().item()))
+    if int(fails.item()):
+        raise RuntimeError("stabilize_cholesky failed for an E8P12 block gram")
+    nonincreasing = all(b <= a + max(1e-8, abs(a) * 1e-7) for a, b in zip(trace, trace[1:]))
+    return x_work, idx.to(torch.int64), {"accepted_updates": float(accepted.item()), "exact_score_evals":
+                                         int(evals.item()), "stabilized_objective_trace": trace,
+                                         "stabilized_objective_nonincreasing": bool(nonincreasing)}
+
+
+@torch.inference_mode()
+def gram_search(targets: torch.Tensor, chol: torch.Tensor, cb, lam_bounds: Optional[Tuple[float, float]] = None
+                ) -> torch.Tensor:
+    """Exact first-minimum gram-metric search of N targets (N, 8) under one lower Cholesky factor (8, 8)."""
+    dev = targets.device
+    t = factor_tables(cb, dev)
+    L = chol.to(device=dev, dtype=torch.float32).contiguous()
+    if lam_bounds is None:
+        S = (L.double() @ L.double().T)
+        ev = torch.linalg.eigvalsh(S.cpu())
+        lam_bounds = (max(float(ev.min()) * (1 - 1e-6), 0.0), float(ev.max()) * (1 + 1e-6))
+    tg = targets.to(torch.float32).contiguous()
+    out = torch.empty(tg.shape[0], device=dev, dtype=torch.int32)
+    call("mpq_gram_search", ptr(tg), tg.shape[0], ptr(L), float(lam_bounds[0]), float(lam_bounds[1]),
+         ptr(t["base_abs"]), ptr(t["base_parity"]), ptr(t["grid"]), ptr(t["sign_id"]), ptr(out))
+    return out.to(torch.int64)

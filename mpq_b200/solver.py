@@ -122,7 +122,9 @@ class _UniformCtx:
         self.opVh = ops.Operand(Vh)      # r2 @ V                ==  r2 @ Vh^T
         self.opVsT = ops.Operand(self.VsT)  # x @ Vs
         self.opVs = ops.Operand(Vs)      # residual_u @ Vs^T
-        self.Y_u = ops.mm_nt(W, self.opVsT)
+        # Y_u anchors every residual of the solve; it is computed once with FP32 FMA chains (the tensor
+        # core's FP32 accumulation is ~10x coarser and the greedy CD order is sensitive to it)
+        self.Y_u = ops.mm_nt(W, self.opVsT, precision="fp32")
 
     def err(self, x, out=None, tmp=None):
         C = ops.mm_nt(x, self.opVsT, tmp)
@@ -355,7 +357,7 @@ def solve_uniform_rankspace_vamp(
             call("mpq_vamp_rows", ptr(rows["var"]), ptr(gamma1), ptr(rows["g1w"]), ptr(rows["a1"]), ptr(rows["eta1"]),
                  ptr(rows["g2n"]), ptr(rows["g2"]), ptr(rows["g2p"]) if (have_prev and damping < 1.0) else None,
                  ptr(rows["a2"]), ptr(rows["eta2"]), ptr(rows["g1n"]), ptr(rows["g1next"]), ptr(rows["trace"]),
-                 ptr(flags), ptr(S), B, n, R, obs, damping, int(final))
+                 ptr(flags), ptr(S), B, n, n, R, obs, damping, int(final))
             fl = flags.tolist()
             if fl[0] == 0:
                 break
@@ -478,3 +480,291 @@ def solve_uniform_rankspace_vamp(
         "rtn_rankspace_error_mean": float(ops.mean_rows(rtn_err).item()),
     }
     return q_final.to(torch.int32), x_final, err_final, rtn_err, stats
+
+
+# ------------------------------------------------------------------------------------------------
+# E8P12 (QUIP# 2-bit lattice codebook)
+# ------------------------------------------------------------------------------------------------
+
+def _resolve_e8p12_polish_metric(metric: str) -> str:
+    """mpq/solver.py:178-185."""
+    m = str(metric or "gram").strip().lower()
+    if m in ("isotropic", "diag"):
+        return "diag"
+    if m == "gram":
+        return "gram"
+    raise ValueError(f"unsupported polish_metric={metric!r}; expected 'gram'|'diag'.")
+
+
+@torch.inference_mode()
+def polish_e8p12_rankspace(
+    *,
+    x_init: torch.Tensor,
+    idxs_init: torch.Tensor,
+    Y_u: torch.Tensor,
+    Vs: torch.Tensor,
+    cb: object,
+    sweeps: int,
+    polish_mode: str,
+    polish_metric: str,
+    metric_rows_per_chunk: int = 0,
+    polish_max_blocks: int = 0,
+    topk_idxs: Optional[torch.Tensor] = None,
+    order_mode: str = "greedy_gain",
+    snapshot_budgets=None,
+    snapshots_out=None,
+    _ops: Optional[Tuple[Any, Any]] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Dict[str, Any]]:
+    """mpq/solver.py:369-423: gram-metric greedy block CD over the full E8P12 grid."""
+    from .e8p12 import gram_block_cd
+    mode = _resolve_polish_mode(sweeps=int(sweeps), mode=str(polish_mode))
+    metric = _resolve_e8p12_polish_metric(polish_metric)
+    dev = x_init.device
+    x_work = _f32c(x_init, dev)
+    Vs = _f32c(Vs, dev)
+    Y_u = _f32c(Y_u, dev)
+    opVs, opVsT = _ops if _ops is not None else (ops.Operand(Vs), ops.Operand(Vs.t().contiguous()))
+
+    def err_of(x):
+        C = ops.mm_nt(x, opVsT)
+        e = torch.empty(x.shape[0], device=dev, dtype=torch.float32)
+        call("mpq_row_sqerr", ptr(Y_u), ptr(C), x.shape[0], C.shape[1], Y_u.stride(0), C.stride(0), ptr(e))
+        return e
+
+    if mode == "none" or Vs.numel() == 0:
+        return x_work, idxs_init, err_of(x_work), {"accepted_updates": 0.0}
+    if mode != "block_cd" or metric != "gram":
+        raise NotImplementedError("only the gram-metric full-grid block CD (the default recipe) is built")
+    if str(order_mode or "greedy_gain").lower() != "greedy_gain" or int(polish_max_blocks) > 0:
+        raise NotImplementedError("only the greedy_gain order over all blocks is built")
+    x_out, idx_out, st = gram_block_cd(x=x_work, Y_u=Y_u, Vs=Vs, cb=cb, sweeps=int(sweeps), idxs_init=idxs_init,
+                                       opVs=opVs, opVsT=opVsT)
+    return x_out, idx_out, err_of(x_out), st
+
+
+@torch.inference_mode()
+def solve_e8p12_rankspace_vamp(
+    *,
+    Wr: torch.Tensor,
+    hatWr_init: torch.Tensor,
+    cb: object,
+    V: torch.Tensor,
+    Vh: torch.Tensor,
+    S: torch.Tensor,
+    Vs: torch.Tensor,
+    cfg: E8P12VampConfig,
+    module_name: str = "",
+    obs_precision_init: Optional[float] = None,
+    log_stats: bool = True,
+    debug_out: Optional[Dict[str, Any]] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Dict[str, Any]]:
+    """Scalar-precision VAMP for QUIP E8P12 in rank space with the gram-metric polish (mpq/solver.py:853-1276).
+
+    Returns (hatWr (B, n), Qidxs int64 (B, n/8), final_err (B,), stats)."""
+    from .e8p12 import prior_scale_from_center, e8p12_map_rows
+    from .codebook import factor_tables
+    if not Wr.is_cuda:
+        raise ValueError("solve_e8p12_rankspace_vamp requires CUDA tensors (there is no CPU path)")
+    dev = Wr.device
+    Wr = _f32c(Wr, dev)
+    hat0 = _f32c(hatWr_init, dev)
+    B, n = Wr.shape
+    codesz = int(getattr(cb, "codesz", 8))
+    if codesz != 8 or n % 8 != 0:
+        raise ValueError(f"E8P12 solver expects n divisible by 8; got n={n}, codesz={codesz}.")
+    nb = n // 8
+    V, Vh, S, Vs = (_f32c(t, dev) for t in (V, Vh, S, Vs))
+    R = int(S.numel())
+    if R == 0:
+        raise ValueError("rank-0 spectra are not supported by the CUDA solver")
+    iters = max(int(cfg.iters), 0)
+    reported_iters = iters
+    damping = float(cfg.damping)
+    tau = float(cfg.prior_tau)
+    mode_scale = str(cfg.prior_tau_scale_mode or "absmax").strip().lower()
+    tab = factor_tables(cb, dev)
+    f32 = dict(device=dev, dtype=torch.float32)
+    W_blocks = Wr.reshape(B, nb, 8)
+    pscale = prior_scale_from_center(W_blocks, mode_scale).reshape(B, nb).contiguous() if tau > 0.0 else None
+    center = Wr if tau > 0.0 else None
+    opV, opVh = ops.Operand(V), ops.Operand(Vh)
+    VsT = Vs.t().contiguous()
+    opVs, opVsT = ops.Operand(Vs), ops.Operand(VsT)
+    Y_u = ops.mm_nt(Wr, opVsT, precision="fp32")  # computed once with FP32 FMA chains (see _UniformCtx)
+    tmpBR = torch.empty(B, R, **f32)
+
+    def err_of(x, out=None):
+        C = ops.mm_nt(x, opVsT, tmpBR)
+        out = torch.empty(B, **f32) if out is None else out
+        call("mpq_row_sqerr", ptr(Y_u), ptr(C), B, R, Y_u.stride(0), C.stride(0), ptr(out))
+        return out
+
+    if float(cfg.obs_precision) > 0.0:
+        obs_start = float(cfg.obs_precision)
+    elif obs_precision_init is not None and float(obs_precision_init) > 0.0:
+        obs_start = float(obs_precision_init)
+    else:
+        obs_start = 1.0 / max(float(ops.mean_rows(err_of(hat0)).item()) / R, 1e-12)
+    obs = float(obs_start)
+    em_active = bool(cfg.em_obs_precision) and float(cfg.obs_precision) <= 0.0
+    r1 = hat0.clone()
+    gamma1 = torch.empty(B, **f32)
+    call("mpq_gamma_init", ptr(Wr), ptr(hat0), B, n, Wr.stride(0), float(cfg.gamma_start), ptr(gamma1))
+
+    def mmse(r, g, x_out, vsum):
+        call("mpq_e8p12_mmse", ptr(r), r.stride(0), ptr(center), center.stride(0) if center is not None else 0,
+             ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(g), tau, B, nb, ptr(tab["base_abs"]),
+             ptr(tab["base_sqnorm"]), ptr(tab["base_parity"]), ptr(tab["idx_lut"]), ptr(tab["grid"]), ptr(x_out),
+             x_out.stride(0), None, 0, None, 0, None, 0, ptr(vsum))
+
+    def map_state(r, g):
+        return e8p12_map_rows(r, cb, gamma=g, center=center, pscale=pscale, prior_tau=tau)
+
+    best_iterate = bool(getattr(cfg, "best_iterate", False))
+    best_err_mean = float("inf")
+    best_iter_idx = -1
+    stop_iter_idx = -1
+    best_r1 = best_g1 = None
+    best_obs = obs
+    if best_iterate:
+        hx, _ = map_state(r1, gamma1)
+        best_err_mean = float(ops.mean_rows(err_of(hx)).item())
+        best_r1, best_g1 = r1.clone(), gamma1.clone()
+
+    x1 = torch.empty(B, n, **f32)
+    r2 = torch.empty(B, n, **f32)
+    r2_prev = torch.empty(B, n, **f32)
+    have_prev = False
+    u = torch.empty(B, R, **f32)
+    rows = {k: torch.empty(B, **f32) for k in ("var", "g1w", "a1", "eta1", "g2n", "g2", "g2p", "a2", "eta2", "g1n",
+                                               "g1next", "trace", "resid")}
+    flags = torch.zeros(8, device=dev, dtype=torch.int32)
+    em_mean_t = torch.zeros(1, **f32)
+    factor = max(float(cfg.gamma_retry_factor), 1.000001)
+    retry_steps = max(int(cfg.gamma_retry_steps), 0)
+    alpha1_retry_count = alpha2_clip_count = gamma2_invalid_count = 0
+    obs_values = []
+    for it in range(iters):
+        rows["g1w"].copy_(gamma1)
+        for retry_idx in range(retry_steps + 1):
+            final = retry_idx >= retry_steps
+            mmse(r1, rows["g1w"], x1, rows["var"])
+            flags.zero_()
+            call("mpq_vamp_rows", ptr(rows["var"]), ptr(gamma1), ptr(rows["g1w"]), ptr(rows["a1"]), ptr(rows["eta1"]),
+                 ptr(rows["g2n"]), ptr(rows["g2"]), ptr(rows["g2p"]) if (have_prev and damping < 1.0) else None,
+                 ptr(rows["a2"]), ptr(rows["eta2"]), ptr(rows["g1n"]), ptr(rows["g1next"]), ptr(rows["trace"]),
+                 ptr(flags), ptr(S), B, n, nb, R, obs, damping, int(final))
+            fl = flags.tolist()
+            if fl[0] == 0:
+                break
+            if final:
+                if fl[1] > 0:
+                    raise RuntimeError(f"alpha1 invalid: expected all in ({ALPHA_EPS}, 1-{ALPHA_EPS}).")
+                break
+            alpha1_retry_count += int(fl[0])
+            call("mpq_gamma_retry", ptr(rows["g1w"]), ptr(rows["var"]), B, nb, factor)
+        if fl[2] > 0 or fl[3] > 0:
+            gamma2_invalid_count += 1
+            continue
+        alpha2_clip_count += int(fl[4])
+        call("mpq_vamp_r2", ptr(x1), ptr(r1), ptr(r2_prev) if (have_prev and damping < 1.0) else None, ptr(r2),
+             ptr(rows["eta1"]), ptr(rows["g1w"]), ptr(rows["g2n"]), B, n, r2.stride(0), damping)
+        P = ops.mm_nt(r2, opVh, tmpBR)
+        call("mpq_linear_epilogue", ptr(P), ptr(Y_u), ptr(S), ptr(rows["g2"]), obs, B, R, P.stride(0), ptr(u),
+             ptr(rows["resid"]))
+        D = ops.mm_nt(u, opV, x1)
+        call("mpq_vamp_r1", ptr(D), ptr(r2), ptr(r1), ptr(rows["eta2"]), ptr(rows["g2"]), ptr(rows["g1n"]), B, n,
+             r1.stride(0), damping)
+        gamma1.copy_(rows["g1next"])
+        r2, r2_prev = r2_prev, r2
+        rows["g2p"].copy_(rows["g2"])
+        have_prev = True
+        if em_active:
+            ops.mean_rows(rows["resid"], rows["trace"], out=em_mean_t)
+            em_mean = float(em_mean_t.item())
+            beta_new = float(R / max(em_mean, 1e-12))
+            beta = _log_damp_scalar(max(obs, 1e-12), beta_new, float(cfg.em_obs_precision_damping))
+            obs = float(min(max(beta, float(cfg.em_obs_precision_min)), float(cfg.em_obs_precision_max)))
+        obs_values.append(obs)
+        if best_iterate:
+            hx, _ = map_state(r1, gamma1)
+            cur = float(ops.mean_rows(err_of(hx)).item())
+            if cur + max(1e-10, abs(best_err_mean) * 1e-8) < best_err_mean:
+                best_err_mean = cur
+                best_r1.copy_(r1)
+                best_g1.copy_(gamma1)
+                best_obs = obs
+                best_iter_idx = it
+            else:
+                r1.copy_(best_r1)
+                gamma1.copy_(best_g1)
+                obs = float(best_obs)
+                stop_iter_idx = it
+                reported_iters = it + 1
+                break
+
+    final_hat, final_idx32 = map_state(r1, gamma1)
+    final_idx = final_idx32.to(torch.int64)
+    idxs_stage1 = final_idx
+    final_err = err_of(final_hat)
+    polish_sweeps = max(int(cfg.polish_sweeps), 0)
+    polish_mode = _resolve_polish_mode(sweeps=polish_sweeps, mode=str(getattr(cfg, "polish_mode", "block_cd")))
+    polish_metric = _resolve_e8p12_polish_metric(str(cfg.polish_metric or "gram"))
+    polish_stats: Dict[str, Any] = {}
+    polish_gain = polish_updates = 0.0
+    if polish_mode != "none":
+        err_before = final_err
+        final_hat, final_idx, err_after, polish_stats = polish_e8p12_rankspace(
+            x_init=final_hat, idxs_init=final_idx, Y_u=Y_u, Vs=Vs, cb=cb, sweeps=polish_sweeps,
+            polish_mode=polish_mode, polish_metric=polish_metric,
+            metric_rows_per_chunk=int(cfg.polish_metric_rows_per_chunk),
+            polish_max_blocks=int(getattr(cfg, "polish_max_blocks", 0) or 0), _ops=(opVs, opVsT))
+        polish_gain = float((err_before.double() - err_after.double()).mean().item())
+        polish_updates = float(polish_stats.get("accepted_updates", 0.0))
+        final_err = err_after
+    ops.check_status(dev)
+    if debug_out is not None:
+        g64 = gamma1.double()
+        debug_out["solver"] = "e8p12_exact_vamp"
+        debug_out["gamma1_sum"] = float(g64.sum())
+        debug_out["gamma1_count"] = int(g64.numel())
+        debug_out["gamma1_min"] = float(g64.min()) if B else 0.0
+        debug_out["gamma1_max"] = float(g64.max()) if B else 0.0
+        if bool(debug_out.get("summary_only", False)):
+            debug_out["changed_count"] = int((idxs_stage1 != final_idx).sum().item())
+            debug_out["changed_total"] = int(final_idx.numel())
+        if bool(debug_out.get("capture_r1", False)):
+            debug_out["r1"] = r1.detach().cpu()
+        if not bool(debug_out.get("summary_only", False)):
+            debug_out["gamma1"] = gamma1.detach().cpu()
+    stats: Dict[str, Any] = {
+        "solver": "e8p12_exact_vamp",
+        "module": str(module_name),
+        "iters": int(reported_iters),
+        "rank": R,
+        "nblocks": nb,
+        "damping": damping,
+        "prior_tau": tau,
+        "prior_tau_scale_mode": mode_scale,
+        "gamma_start": float(cfg.gamma_start),
+        "gamma_retry_factor": float(factor),
+        "gamma_retry_steps": int(retry_steps),
+        "obs_precision_initial": float(obs_start),
+        "obs_precision_final": float(obs),
+        "obs_precision_mean": float(sum(obs_values) / len(obs_values)) if obs_values else float(obs),
+        "alpha1_retry_count": int(alpha1_retry_count),
+        "alpha2_clip_count": int(alpha2_clip_count),
+        "gamma2_invalid_count": int(gamma2_invalid_count),
+        "polish_sweeps": polish_sweeps,
+        "polish_mode": polish_mode,
+        "polish_metric": polish_metric,
+        "polish_gain": polish_gain,
+        "polish_updates": polish_updates,
+        "polish_trace": polish_stats,
+        "best_iterate_enabled": best_iterate,
+        "best_iter": int(best_iter_idx),
+        "stop_iter": int(stop_iter_idx),
+        "best_rankspace_error_mean": float(best_err_mean) if best_iterate else 0.0,
+        "rankspace_error_mean": float(ops.mean_rows(final_err).item()),
+    }
+    return final_hat, final_idx, final_err, stats

@@ -24,6 +24,15 @@ f32 = np.float32
 LOG2 = math.log(2.0)
 
 
+def _cr(fn, x):
+    """float32 result of a transcendental, correctly rounded (float64 evaluation, one rounding).
+
+    torch's CPU float32 tanh/exp/log (what the reference runs) return correctly rounded values; numpy's
+    float32 SIMD versions differ from them in the last bit for 30-50% of inputs, which the reference's
+    clamped-tanh algebra amplifies.  Evaluating in float64 and rounding once reproduces torch."""
+    return fn(np.asarray(x, dtype=np.float64)).astype(np.float32)
+
+
 def _abs_patterns() -> np.ndarray:
     """256 x 8 abs patterns: the sorted abs patterns of half-integer E8 points with norm^2 <= 10 (227;
     every half-integer abs pattern has a signed version with even coordinate sum) followed by the first
@@ -193,7 +202,7 @@ def vamp_vector_map_e8p12(*, r1_blocks, gamma1, cb, prior_center_blocks=None, pr
 
 
 def _log1mexp(x):
-    return np.where(x < f32(-LOG2), np.log1p(-np.exp(x)), np.log(-np.expm1(x))).astype(np.float32)
+    return np.where(x < f32(-LOG2), _cr(np.log1p, -_cr(np.exp, x)), _cr(np.log, -_cr(np.expm1, x))).astype(np.float32)
 
 
 def _branch_stats(y, gamma, offset, branch, cache):
@@ -203,15 +212,16 @@ def _branch_stats(y, gamma, offset, branch, cache):
     a = (gamma[:, :, None] * y[:, None, :]) * base_abs[None, :, :]
     y_norm = (y * y).sum(axis=1, keepdims=True, dtype=np.float32)
     const = f32(-0.5) * gamma * (y_norm + cache["base_sqnorm"][None, :])
-    logC = np.logaddexp(a, -a).sum(axis=-1, dtype=np.float32)
-    t = np.tanh(a)
+    aa = np.abs(a)
+    logC = (aa + _cr(np.log1p, _cr(np.exp, f32(-2.0) * aa))).sum(axis=-1, dtype=np.float32)  # logaddexp(a, -a)
+    t = _cr(np.tanh, a)
     eps = f32(1e-7)
-    t = np.clip(t, f32(-1.0) + eps, f32(1.0) - eps)
-    lpt = np.log(np.maximum(np.abs(t), eps)).sum(axis=-1, dtype=np.float32)
+    t = np.clip(t, f32(-0.99999988079071044921875), f32(0.99999988079071044921875))
+    lpt = _cr(np.log, np.maximum(np.abs(t), eps)).sum(axis=-1, dtype=np.float32)
     neg = ((t < 0).sum(axis=-1) & 1).astype(bool)
-    pabs = np.exp(lpt)
+    pabs = _cr(np.exp, lpt)
     prod = np.where(neg, -pabs, pabs).astype(np.float32)
-    lae = np.logaddexp(np.zeros_like(lpt), lpt)
+    lae = _cr(np.log1p, _cr(np.exp, lpt))  # logaddexp(0, lpt), lpt <= 0
     l1me = _log1mexp(lpt)
     lop = np.where(neg, l1me, lae)
     lom = np.where(neg, lae, l1me)
@@ -261,8 +271,8 @@ def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, prior_center_block
         outs = [_branch_stats((y - f32(o)).astype(np.float32), g, o, b, cache) for b, o in enumerate((0.25, -0.25))]
         lc = np.concatenate([o["log_component"] for o in outs], axis=1)  # (n, 512)
         m = lc.max(axis=1, keepdims=True)
-        lz = m + np.log(np.exp(lc - m).sum(axis=1, keepdims=True))
-        w = np.exp(lc - lz)
+        lz = m + _cr(np.log, _cr(np.exp, lc - m).sum(axis=1, keepdims=True, dtype=np.float32))
+        w = _cr(np.exp, lc - lz)
         mu = np.zeros((y.shape[0], 8), np.float32)
         sec = np.zeros(y.shape[0], np.float32)
         for b in range(2):

@@ -32,7 +32,9 @@ def log_damp_positive(prev: np.ndarray, new: np.ndarray, damping: float) -> np.n
         return prev
     prev = np.maximum(prev, f32(1e-12))
     new = np.maximum(new, f32(1e-12))
-    return np.exp(f32(1.0 - damping) * np.log(prev) + f32(damping) * np.log(new)).astype(f32)
+    lp = np.log(prev.astype(np.float64)).astype(f32)  # correctly rounded float32 log/exp, as torch's CPU kernels
+    ln = np.log(new.astype(np.float64)).astype(f32)
+    return np.exp((f32(1.0 - damping) * lp + f32(damping) * ln).astype(np.float64)).astype(f32)
 
 
 def log_damp_positive_scalar(prev: float, new: float, damping: float) -> float:
@@ -91,8 +93,9 @@ def discrete_uniform_mmse(*, r1, gamma1, scale_full, zero_full, maxq, prior_cent
     gamma1 = gamma1.astype(f32)
     scores = uniform_scores(r1, gamma1, scale_full, prior_center, prior_tau, atoms)
     m = scores.max(axis=-1, keepdims=True)
-    lse = m + np.log(np.exp(scores - m).sum(axis=-1, keepdims=True))
-    probs = np.exp(scores - lse)
+    # float64 evaluation rounded once: the correctly rounded float32 exp/log of torch's CPU kernels
+    lse = m + np.log(np.exp((scores - m).astype(np.float64)).sum(axis=-1, keepdims=True).astype(f32).astype(np.float64)).astype(f32)
+    probs = np.exp((scores - lse).astype(np.float64)).astype(f32)
     mean = (probs * atoms).sum(axis=-1)
     second = (probs * (atoms * atoms)).sum(axis=-1)
     var = np.maximum(second - mean * mean, f32(0.0))

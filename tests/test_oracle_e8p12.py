@@ -57,12 +57,11 @@ def test_factorized_posterior_matches_reference(golden_dir, cb, case):
     close = np.isclose(x1, rx1, rtol=1e-4, atol=2e-5)
     assert close.mean() >= 0.99, close.mean()
     assert np.abs(x1 - rx1).max() <= 2e-2
-    # Where all |tanh(a_k)| saturate at the 1 - 1e-7 clamp, log(1 - prod) depends on 1-ulp tanh rounding
-    # (torch vs numpy vs CUDA), which moves that component's weight by a few percent: variances (and their
-    # row means, alpha1) agree tightly except on such items.
+    # With correctly rounded float32 transcendentals (as torch's) the remaining differences are float32
+    # summation order inside the ill-conditioned components.
     v, rv = post["var1"], z[f"{case}/var1"]
-    assert np.isclose(v, rv, rtol=2e-3, atol=2e-6).mean() >= 0.97
-    np.testing.assert_allclose(post["alpha1"], z[f"{case}/alpha1"], rtol=2e-2)
+    assert np.isclose(v, rv, rtol=2e-3, atol=2e-6).mean() >= 0.99
+    np.testing.assert_allclose(post["alpha1"], z[f"{case}/alpha1"], rtol=1e-4)
 
 
 def test_gram_cd_step_matches_reference(golden_dir, cb):
