@@ -1,17 +1,21 @@
 #!/usr/bin/env python
-"""Benchmark: seconds per 4096x4096 per-layer quantization solve on B200.
+"""Benchmark: seconds per 4096x4096 per-layer quantization solve (VAMP + 3 CD sweeps) on B200.
 
-Workload (the grouped-scalar case): W 4096x4096 ~ N(0, 0.02^2) (seed 0),
-calibration X 16384x4096 with log-normal channel scales, H = X^T X / 16384 + 0.01 mean(diag H) I,
-internal block-Hadamard rotation, 4-bit asymmetric g128 grid, RTN init, VAMP (20 iterations,
-tau 0.2, damping 0.5), 3 greedy CD sweeps.  One step = one full layer solve (eigh, rotation,
-group grid, warm start, VAMP, CD, audit) from device-resident (W, H).
+Workloads (seeded synthetic data with their shapes and distributions):
+  e8p12  (configs[1], default)  W 4096x4096 ~ N(0, 0.02^2) (seed 0); X 16384x4096 with log-normal channel
+         scales, H = X^T X / 16384 + 0.01 mean(diag H) I; randomized Hadamard on both dims (seeded +-1
+         sign vectors), one global RMS scale; 2-bit E8P12 (2^16 codewords); RTN init; fp64 eigh of H;
+         VAMP 16 iterations (tau 0.25) + 3 gram-metric block-CD sweeps.
+  scalar  same W, H; internal block-Hadamard; 4-bit asym g128; RTN; fp32 eigh; VAMP 20
+         iterations (tau 0.2) + 3 greedy scalar CD sweeps.
+One step = one full layer solve from device-resident (W, H): rotation, eigendecomposition, RTN / grid,
+warm start, VAMP, CD, audits.  `block_rows` = 4096 (the whole layer in one VAMP block).
 
-`--impl reference` times the CPU oracle port of the reference algorithm on the host cores on a
+`--impl reference` times the CPU oracle (the reference algorithm restated in numpy) on the host cores on a
 bounded row sample of the same layer and extrapolates to the per-layer metric.
 
-Multi-GPU (torchrun): the layer's rows are sharded across ranks; rank 0 builds H and broadcasts
-it over NCCL; time = max over ranks.
+Multi-GPU (torchrun): the layer's rows are sharded across ranks (each shard's VAMP starts from the
+global warm start); rank 0 builds H and broadcasts it and W over NCCL; time = max over ranks.
 """
 from __future__ import annotations
 
@@ -21,6 +25,7 @@ import os
 import subprocess
 import sys
 import time
+import types
 from pathlib import Path
 
 import numpy as np
@@ -31,9 +36,11 @@ sys.path.insert(0, str(ROOT))
 M_ROWS = 4096
 N_COLS = 4096
 T_CALIB = 16384
-BITS = 4
-GROUP = 128
-ITERS = 20
+METRIC = "s per 4096^2 layer solve (VAMP+3 CD)"
+WORKLOAD_DESC = {
+    "e8p12": "config1: 4096x4096 layer, 2-bit E8P12, two-sided RHT, RTN init, fp64 eigh, VAMP 16 it + 3 gram-CD sweeps",
+    "scalar": "config0: 4096x4096 layer, 4-bit asym g128, internal Hadamard, RTN init, VAMP 20 it + 3 CD sweeps",
+}
 
 
 def parse():
@@ -42,8 +49,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mpq", choices=["mpq", "reference"])
+    ap.add_argument("--workload", default="e8p12", choices=sorted(WORKLOAD_DESC))
     ap.add_argument("--block-rows", type=int, default=4096)
-    ap.add_argument("--cpu-sample-rows", type=int, default=64)
+    ap.add_argument("--cpu-sample-rows", type=int, default=0, help="0: workload default")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--profile", action="store_true",
@@ -51,28 +59,32 @@ def parse():
     a = ap.parse_args()
     if a.profile:
         a.steps, a.warmup, a.no_cpu_baseline, a.no_clocks = 1, 1, True, True
+    if a.cpu_sample_rows <= 0:
+        a.cpu_sample_rows = 16 if a.workload == "e8p12" else 64
     return a
 
 
 # ----------------------------------------------------------------------------------------------
-# synthetic inputs
+# synthetic inputs (same generator for the GPU arm and the CPU oracle)
 # ----------------------------------------------------------------------------------------------
 
-def synth_inputs_torch(device):
+def synth_cpu():
     import torch
     g = torch.Generator(device="cpu").manual_seed(0)
-    W = (torch.randn(M_ROWS, N_COLS, generator=g) * 0.02)
+    W = torch.randn(M_ROWS, N_COLS, generator=g) * 0.02
     s = torch.exp(torch.randn(N_COLS, generator=g))
     X = torch.randn(T_CALIB, N_COLS, generator=g) * s.sqrt()
-    return W.to(device), X.to(device)
+    SU = (torch.randint(0, 2, (M_ROWS,), generator=g).float() * 2 - 1)
+    SV = (torch.randint(0, 2, (N_COLS,), generator=g).float() * 2 - 1)
+    return W, X, SU, SV
 
 
 def hessian_device(X):
-    """H = X^T X / T + 0.01 mean(diag) I on the GPU (our GEMM)."""
+    """H = X^T X / T + 0.01 mean(diag) I on the GPU (tensor-core product)."""
     import torch
     from mpq_b200 import ops
     XT = X.t().contiguous()
-    H = ops.gemm_nt(XT, XT)
+    H = ops.mm_nt(XT, ops.Operand(XT))
     H.div_(float(X.shape[0]))
     H.add_(torch.eye(H.shape[0], device=H.device) * (0.01 * float(H.diagonal().mean())))
     return H
@@ -89,7 +101,6 @@ class ClockSampler:
 
     def __init__(self, index: int, enabled: bool = True):
         self.proc = None
-        self.index = index
         self.path = ROOT / "gpurun_out" / f"clocks_rank{index}.csv"
         if not enabled:
             return
@@ -112,6 +123,7 @@ class ClockSampler:
             self.proc.kill()
         self.fh.close()
         sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.path.read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
@@ -121,7 +133,6 @@ class ClockSampler:
                 mx = max(mx, float(parts[2]))
             except ValueError:
                 continue
-            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
@@ -131,29 +142,59 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------------------
-# the measured step
+# the measured steps
 # ----------------------------------------------------------------------------------------------
 
-def layer_config(block_rows):
-    import types
-    from mpq_b200.adapters.gptqmodel import GPTQAdapterConfig
-    from mpq_b200.solver import UniformVampConfig
-    qcfg = types.SimpleNamespace(bits=BITS, group_size=GROUP, desc_act=False,
-                                 mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
-    vcfg = UniformVampConfig(iters=ITERS, prior_tau=0.2, damping=0.5, polish_sweeps=3)
-    acfg = GPTQAdapterConfig(block_rows=block_rows, grow_block_rows=False)
-    return qcfg, vcfg, acfg
+class ScalarWorkload:
+    dominant = "gemm"
+
+    def __init__(self, dev, block_rows):
+        self.dev, self.block_rows = dev, block_rows
+
+    def step(self, W, H):
+        from mpq_b200.adapters.gptqmodel import GPTQAdapterConfig, run_mpq_quantization
+        from mpq_b200.solver import UniformVampConfig
+        qcfg = types.SimpleNamespace(bits=4, group_size=128, desc_act=False,
+                                     mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
+        out = run_mpq_quantization(W=W, H=2.0 * H, quantizer=None, qcfg=qcfg, module_name="bench.layer",
+                                   vamp_cfg=UniformVampConfig(iters=20, prior_tau=0.2, damping=0.5, polish_sweeps=3),
+                                   adapter_cfg=GPTQAdapterConfig(block_rows=self.block_rows, grow_block_rows=False))
+        Q, q_int, scale, zero, g_idx, _, st = out
+        return [q_int, scale, zero], {"raw_objective_mean": st["raw_objective_mean_final"],
+                                      "obs_final": st["obs_precision_final"],
+                                      "best_iters": [b["best_iter"] for b in st["block_stats"]]}
 
 
-def solve_step(W, H2, block_rows):
-    from mpq_b200.adapters.gptqmodel import run_mpq_quantization
-    qcfg, vcfg, acfg = layer_config(block_rows)
-    return run_mpq_quantization(W=W, H=H2, quantizer=None, qcfg=qcfg, module_name="bench.layer", vamp_cfg=vcfg,
-                                adapter_cfg=acfg)
+class E8Workload:
+    dominant = "gemm"
 
+    def __init__(self, dev, block_rows, SU, SV):
+        from mpq_b200.codebook import E8P12_codebook
+        self.dev, self.block_rows = dev, block_rows
+        self.cb = E8P12_codebook()
+        self.SU, self.SV = SU.to(dev), SV.to(dev)
 
-def flush_l2(buf):
-    buf.add_(1.0)
+    def step(self, W, H):
+        import torch
+        from mpq_b200 import ops
+        from mpq_b200._lib import call, ptr
+        from mpq_b200.adapters.quip_sharp import mpq_refine_codebook
+        from mpq_b200.rotation import rht_hessian, rht_weight
+        m, n = W.shape
+        Wr = rht_weight(W, self.SU, self.SV, m & -m, n & -n)
+        Hr = rht_hessian(H, self.SV, n & -n)
+        sq = torch.empty(m, device=W.device)
+        call("mpq_row_dot", ptr(Wr), Wr.stride(0), ptr(Wr), Wr.stride(0), m, n, ptr(sq))
+        wscale = float(ops.mean_rows(sq).item() / n) ** 0.5
+        Wn = Wr / wscale
+        args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=16, mpq_prior_tau=0.25, mpq_polish_sweeps=3,
+                                     mpq_block_rows=self.block_rows, quant_solver="vamp",
+                                     quant_polish_mode="block_cd", mpq_polish_metric="gram")
+        hat, idx, st = mpq_refine_codebook(Wn, Hr, Wn, torch.zeros(m, n // 8, dtype=torch.int64, device=W.device),
+                                           self.cb, args, module_name="bench.layer")
+        return [idx], {"surrogate_before": st["exact_surrogate_before_mean"],
+                       "surrogate_after": st["exact_surrogate_after_mean"], "obs_final": st["obs_precision_final"],
+                       "wscale": wscale, "changed_fraction": st["mechanism"]["cleanup_changed_fraction"]}
 
 
 def run_mpq(args):
@@ -170,32 +211,34 @@ def run_mpq(args):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    W, X = synth_inputs_torch(dev) if rank == 0 or world == 1 else (None, None)
-    if world > 1:
-        if W is None:
-            W = torch.empty(M_ROWS, N_COLS, device=dev)
+    Wc, Xc, SU, SV = synth_cpu()
+    W = Wc.to(dev) if rank == 0 else torch.empty(M_ROWS, N_COLS, device=dev)
+    H = hessian_device(Xc.to(dev)) if rank == 0 else torch.empty(N_COLS, N_COLS, device=dev)
+    del Xc
+    if world > 1:  # W and H over NVLink
         dist.broadcast(W, 0)
-    H = hessian_device(X) if X is not None else torch.empty(N_COLS, N_COLS, device=dev)
-    if world > 1:
-        dist.broadcast(H, 0)  # H over NVLink
-    del X
-    H2 = (2.0 * H).contiguous()  # GPTQModel convention (2/m X^T X); the adapter applies 0.5
+        dist.broadcast(H, 0)
     rows_per = M_ROWS // world
     Wr = W[rank * rows_per:(rank + 1) * rows_per].contiguous()
     block_rows = min(args.block_rows, rows_per)
+    if args.workload == "e8p12":
+        wl = E8Workload(dev, block_rows, SU[rank * rows_per:(rank + 1) * rows_per], SV)
+    else:
+        wl = ScalarWorkload(dev, block_rows)
     flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > 126 MB L2
 
     for _ in range(max(args.warmup, 0)):
-        solve_step(Wr, H2, block_rows)
+        wl.step(Wr, H)
     torch.cuda.synchronize()
 
     # ---- device-resident timed region ----
     clocks = ClockSampler(local, enabled=not args.no_clocks)
     launches0 = trace.launches()
     step_ms = []
-    with trace.timing(["gemm"]):
+    stats = {}
+    with trace.timing([wl.dominant]):
         for _ in range(args.steps):
-            flush_l2(flush)
+            flush.add_(1.0)
             if world > 1:
                 dist.barrier()
             torch.cuda.synchronize()
@@ -203,42 +246,41 @@ def run_mpq(args):
             e = torch.cuda.Event(enable_timing=True)
             s.record()
             torch.cuda.nvtx.range_push("timed_step")
-            out = solve_step(Wr, H2, block_rows)
+            outs, stats = wl.step(Wr, H)
             torch.cuda.nvtx.range_pop()
             e.record()
             torch.cuda.synchronize()
             step_ms.append(s.elapsed_time(e))
-        gemm = trace.summary("gemm")
+        dom = trace.summary(wl.dominant)
     launches = (trace.launches() - launches0) / max(args.steps, 1)
     clk = clocks.stop()
-    ms = float(np.sum(step_ms)) / args.steps
+    ms = float(np.sum(step_ms)) / max(args.steps, 1)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-
     if args.profile:
         if world > 1:
             dist.destroy_process_group()
-        return {"profile": True, "ms_per_step": ms, "gpu_launches": launches}
+        return {"profile": True, "ms_per_step": ms, "gpu_launches": launches} if rank == 0 else None
 
     # ---- e2e through the public API with host buffers ----
     W_host = Wr.cpu().pin_memory()
-    H_host = H2.cpu().pin_memory()
+    H_host = H.cpu().pin_memory()
     e2e_ms = []
     h2d = W_host.numel() * 4 + H_host.numel() * 4
     d2h = 0
     for _ in range(max(1, min(args.steps, 2))):
-        flush_l2(flush)
+        flush.add_(1.0)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         Wd = W_host.to(dev, non_blocking=True)
         Hd = H_host.to(dev, non_blocking=True)
-        Q, q_int, scale, zero, g_idx, _, st = solve_step(Wd, Hd, block_rows)
-        outs = [Q.cpu(), q_int.cpu(), scale.cpu(), zero.cpu(), g_idx.cpu()]
+        outs, _ = wl.step(Wd, Hd)
+        host = [o.cpu() for o in outs]
         torch.cuda.synchronize()
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
-        d2h = sum(o.numel() * o.element_size() for o in outs)
+        d2h = sum(o.numel() * o.element_size() for o in host)
     e2e = float(np.mean(e2e_ms))
     if world > 1:
         t = torch.tensor([e2e], device=dev)
@@ -247,49 +289,33 @@ def run_mpq(args):
 
     result = None
     if rank == 0:
-        peaks = {}
         pk = ROOT / "MEASURED_PEAKS.json"
-        if pk.exists():
-            peaks = json.loads(pk.read_text())
+        peaks = json.loads(pk.read_text()) if pk.exists() else {}
         peak_tf = float(peaks.get("bf16_tflops_sustained", 1394.3))
-        achieved = gemm["work_avg"] / (gemm["ms_avg"] * 1e-3) / 1e12 if gemm["ms_avg"] > 0 else 0.0
-        traffic = None
+        achieved = dom["work_avg"] / (dom["ms_avg"] * 1e-3) / 1e12 if dom["ms_avg"] > 0 else 0.0
         tf = ROOT / "profiles" / "gemm_traffic.json"
-        if tf.exists():
-            traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+        traffic = json.loads(tf.read_text()).get("bytes_per_launch") if tf.exists() else None
         result = {
-            "metric": "s per 4096^2 layer solve (VAMP+3 CD)",
-            "value": ms / 1e3,
-            "unit": "s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": ms,
-            "higher_is_better": False,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "f32",
+            "metric": METRIC, "value": ms / 1e3, "unit": "s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded W ~ N(0,0.02^2), X with log-normal channel scales)",
-            "config": {"workload": "config0: 4096x4096 layer, 4-bit asym g128, internal Hadamard, RTN init, "
-                                   "VAMP 20 it + 3 CD sweeps",
-                       "block_rows": block_rows, "rows_per_gpu": rows_per, "parallelism": f"rows{world}",
-                       "l2": "256 MB buffer written between timed steps"},
+            "config": {"workload": WORKLOAD_DESC[args.workload], "block_rows": block_rows, "rows_per_gpu": rows_per,
+                       "parallelism": f"rows{world}", "l2": "256 MB buffer written between timed steps"},
             "e2e": {"value": e2e / 1e3, "unit": "s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": int(round(launches)),
-            "roofline": {"bound": "tensor", "kernel": "mpq_gemm_f32 (rank-space GEMMs)",
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 3xTF32 rank-space products)",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf if peak_tf else None, "traffic": traffic,
                          "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (measured)",
-                         "gemm_launches_per_step": gemm["launches"] / max(args.steps, 1),
-                         "gemm_ms_per_step": gemm["ms_total"] / max(args.steps, 1),
-                         "gemm_flops_per_launch": gemm["work_avg"]},
+                         "achieved_counts": "algorithmic 2MNK per product (3xTF32 issues 3 TF32 MMAs per FLOP)",
+                         "launches_per_step": dom["launches"] / max(args.steps, 1),
+                         "ms_per_step": dom["ms_total"] / max(args.steps, 1)},
             "clocks": clk,
-            "stats": {"obs_final": out[6]["obs_precision_final"],
-                      "raw_objective_mean": out[6]["raw_objective_mean_final"],
-                      "best_iters": [b["best_iter"] for b in out[6]["block_stats"]]},
+            "stats": stats,
         }
         if not args.no_cpu_baseline and world == 1:
-            result["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows)
+            result["cpu_baseline"] = cpu_sample(args.workload, args.cpu_sample_rows)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -300,53 +326,74 @@ def run_mpq(args):
 # CPU oracle (the reference algorithm restated in numpy) on a bounded sample
 # ----------------------------------------------------------------------------------------------
 
-def cpu_sample(rows: int):
-    """Time the oracle's per-layer pipeline on `rows` rows of the same layer; extrapolate to s/layer."""
+def cpu_sample(workload: str, rows: int):
+    """Time the oracle's per-layer pipeline on `rows` rows of the same layer and extrapolate to s/layer:
+    per-layer setup (rotations, eigendecomposition) once + the row solve scaled by 4096 / rows."""
     import torch
     from oracle import layer as OL
-    from oracle import uniform_vamp as OU
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    g = torch.Generator(device="cpu").manual_seed(0)
-    W = (torch.randn(M_ROWS, N_COLS, generator=g) * 0.02).numpy()
-    s = torch.exp(torch.randn(N_COLS, generator=g))
-    X = (torch.randn(T_CALIB, N_COLS, generator=g) * s.sqrt()).numpy()
+    Wc, Xc, SU, SV = synth_cpu()
+    W, X = Wc.numpy(), Xc.numpy()
+    SU, SV = SU.numpy(), SV.numpy()
     t0 = time.perf_counter()
     H = OL.hessian_from_calibration(X)
     t_h = time.perf_counter() - t0
-    cfg = OU.UniformVampConfig(iters=ITERS, prior_tau=0.2, damping=0.5, polish_sweeps=3)
-    t0 = time.perf_counter()
-    Hw = (np.float32(0.5) * (2.0 * H)).astype(np.float32)
-    lam, V, _ = OL.vamp_hessian_eigen(Hw)
-    signs = OL.rademacher_signs_torch(N_COLS, "bench.layer:full", 0)
-    Wr = OL.right_block_hadamard(W[:rows], signs, N_COLS)
-    Hm = OL.right_block_hadamard(np.ascontiguousarray(Hw.T), signs, N_COLS).T.copy()
-    Hm = OL.right_block_hadamard(Hm, signs, N_COLS)
-    V = OL.right_block_hadamard(np.ascontiguousarray(V.T), signs, N_COLS).T.copy()
-    S = np.sqrt(lam).astype(np.float32)
-    Vs = (V * S[None, :]).astype(np.float32)
-    t_setup = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    sg = np.empty((rows, N_COLS // GROUP), np.float32)
-    zg = np.empty_like(sg)
-    for gi in range(N_COLS // GROUP):
-        a, b = OL.find_params_minmax(Wr[:, gi * GROUP:(gi + 1) * GROUP], 2**BITS - 1)
-        sg[:, gi], zg[:, gi] = a[:, 0], b[:, 0]
-    sf, zf = np.repeat(sg, GROUP, 1), np.repeat(zg, GROUP, 1)
-    q = np.clip(np.round(Wr / sf) + zf, 0, 2**BITS - 1).astype(np.float32)
-    xr = (sf * (q - zf)).astype(np.float32)
-    OU.solve_uniform_rankspace_vamp(W=Wr, x_rtn=xr, scale_full=sf, zero_full=zf, maxq=2**BITS - 1, V=V,
-                                    Vh=np.ascontiguousarray(V.T), S=S, Vs=Vs, cfg=cfg, gram_full=Hm)
-    t_rows = time.perf_counter() - t0
+    if workload == "e8p12":
+        from oracle import e8p12 as OE
+        cb = OE.E8P12_codebook()
+        t0 = time.perf_counter()
+        Hr = OL.right_block_hadamard(np.ascontiguousarray(H.T), SV, N_COLS).T.copy()
+        Hr = OL.right_block_hadamard(Hr, SV, N_COLS)
+        lam, V, _ = OL.vamp_hessian_eigen(Hr, fp64=True)
+        S = np.sqrt(lam).astype(np.float32)
+        Vs = (V * S[None, :]).astype(np.float32)
+        Wr = OL.right_block_hadamard(W, SV, N_COLS)
+        Wr = OL.right_block_hadamard(np.ascontiguousarray(Wr.T), SU, M_ROWS).T.copy()
+        Wn = (Wr / np.sqrt((Wr.astype(np.float64) ** 2).mean())).astype(np.float32)
+        mcache = OE.block_metric_cache(Vs, cb)
+        t_setup = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        hat0, _ = OE.rtn_init(Wn[:rows], cb)
+        OE.solve_e8p12_rankspace_vamp(Wr=Wn[:rows], hatWr_init=hat0, cb=cb, V=V, Vh=np.ascontiguousarray(V.T), S=S,
+                                      Vs=Vs, cfg=OE.E8P12VampConfig(iters=16, prior_tau=0.25, polish_sweeps=3),
+                                      metric_cache=mcache)
+        t_rows = time.perf_counter() - t0
+        what = "VAMP 16 it + 3 gram-CD sweeps"
+    else:
+        from oracle import uniform_vamp as OU
+        t0 = time.perf_counter()
+        Hw = (np.float32(0.5) * (2.0 * H)).astype(np.float32)
+        lam, V, _ = OL.vamp_hessian_eigen(Hw)
+        signs = OL.rademacher_signs_torch(N_COLS, "bench.layer:full", 0)
+        Wr = OL.right_block_hadamard(W[:rows], signs, N_COLS)
+        Hm = OL.right_block_hadamard(np.ascontiguousarray(Hw.T), signs, N_COLS).T.copy()
+        Hm = OL.right_block_hadamard(Hm, signs, N_COLS)
+        V = OL.right_block_hadamard(np.ascontiguousarray(V.T), signs, N_COLS).T.copy()
+        S = np.sqrt(lam).astype(np.float32)
+        Vs = (V * S[None, :]).astype(np.float32)
+        t_setup = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        G = 128
+        sg = np.empty((rows, N_COLS // G), np.float32)
+        zg = np.empty_like(sg)
+        for gi in range(N_COLS // G):
+            a, b = OL.find_params_minmax(Wr[:, gi * G:(gi + 1) * G], 15)
+            sg[:, gi], zg[:, gi] = a[:, 0], b[:, 0]
+        sf, zf = np.repeat(sg, G, 1), np.repeat(zg, G, 1)
+        q = np.clip(np.round(Wr / sf) + zf, 0, 15).astype(np.float32)
+        xr = (sf * (q - zf)).astype(np.float32)
+        OU.solve_uniform_rankspace_vamp(W=Wr, x_rtn=xr, scale_full=sf, zero_full=zf, maxq=15, V=V,
+                                        Vh=np.ascontiguousarray(V.T), S=S, Vs=Vs,
+                                        cfg=OU.UniformVampConfig(iters=20, prior_tau=0.2, damping=0.5,
+                                                                 polish_sweeps=3), gram_full=Hm)
+        t_rows = time.perf_counter() - t0
+        what = "VAMP 20 it + 3 CD sweeps"
     per_layer = t_setup + t_rows * (M_ROWS / rows)
     return {"value": per_layer, "unit": "s", "cores": cores, "kind": "port",
-            "sample": f"{rows} of {M_ROWS} rows solved (VAMP {ITERS} it + 3 CD); eigh + rotation once; "
-                      f"extrapolated x{M_ROWS // rows}; H accumulation ({t_h:.1f} s) not included",
+            "sample": f"{rows} of {M_ROWS} rows solved ({what}) in {t_rows:.1f} s, extrapolated x{M_ROWS // rows}; "
+                      f"rotation + eigendecomposition once ({t_setup:.1f} s); H accumulation ({t_h:.1f} s) excluded",
             "sample_seconds": t_setup + t_rows}
-
-
-def cpu_baseline(rows):
-    return cpu_sample(rows)
 
 
 def run_reference(args):
@@ -354,28 +401,22 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    vals = []
-    info = None
+    vals, info = [], None
     for _ in range(max(args.steps, 1)):
-        info = cpu_sample(args.cpu_sample_rows)
+        info = cpu_sample(args.workload, args.cpu_sample_rows)
         vals.append(info["value"])
     v = float(np.mean(vals))
-    return {"impl": "reference", "metric": "s per 4096^2 layer solve (VAMP+3 CD)", "value": v, "unit": "s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": v * 1e3,
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded)",
-            "config": {"workload": "config0: 4096x4096 layer, 4-bit asym g128, internal Hadamard, RTN init, "
-                                   "VAMP 20 it + 3 CD sweeps", "parallelism": "cpu"},
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "s", "n_gpus": world, "steps": args.steps,
+            "warmup": 0, "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": {"workload": WORKLOAD_DESC[args.workload], "parallelism": "cpu"},
             "cpu_baseline": {k: info[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": v, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
     args = parse()
-    if args.impl == "reference":
-        res = run_reference(args)
-    else:
-        res = run_mpq(args)
+    res = run_reference(args) if args.impl == "reference" else run_mpq(args)
     if res is not None:
         print(json.dumps(res))
 

@@ -77,3 +77,25 @@ def apply_right_block_hadamard(matrix: torch.Tensor, *, signs: torch.Tensor, had
 def apply_right_block_hadamard_inverse(matrix: torch.Tensor, *, signs: torch.Tensor, had_dim: int) -> torch.Tensor:
     """block Hadamard then * signs (mpq/rotation.py:437-439)."""
     return _apply(matrix, signs, had_dim, 1)
+
+
+@torch.inference_mode()
+def rht_weight(W: torch.Tensor, SU: torch.Tensor, SV: torch.Tensor, had_out: int, had_in: int) -> torch.Tensor:
+    """Two-sided randomized Hadamard of a weight (QUIP# incoherence processing, restated):
+    Wr = Had_out diag(SU) W diag(SV) Had_in  (normalized block Hadamard on each side)."""
+    t = apply_right_block_hadamard(W, signs=SV, had_dim=had_in)
+    t = apply_right_block_hadamard(t.T.contiguous(), signs=SU, had_dim=had_out)
+    return t.T.contiguous()
+
+
+@torch.inference_mode()
+def rht_weight_inverse(Wr: torch.Tensor, SU: torch.Tensor, SV: torch.Tensor, had_out: int, had_in: int) -> torch.Tensor:
+    t = apply_right_block_hadamard_inverse(Wr.T.contiguous(), signs=SU, had_dim=had_out)
+    return apply_right_block_hadamard_inverse(t.T.contiguous(), signs=SV, had_dim=had_in)
+
+
+@torch.inference_mode()
+def rht_hessian(H: torch.Tensor, SV: torch.Tensor, had_in: int) -> torch.Tensor:
+    """Hr = Had_in diag(SV) H diag(SV) Had_in (the input-side rotation of the Hessian)."""
+    t = apply_right_block_hadamard(H.T.contiguous(), signs=SV, had_dim=had_in)
+    return apply_right_block_hadamard(t.T.contiguous(), signs=SV, had_dim=had_in)

@@ -27,10 +27,26 @@ LOG2 = math.log(2.0)
 def _cr(fn, x):
     """float32 result of a transcendental, correctly rounded (float64 evaluation, one rounding).
 
-    torch's CPU float32 tanh/exp/log (what the reference runs) return correctly rounded values; numpy's
-    float32 SIMD versions differ from them in the last bit for 30-50% of inputs, which the reference's
-    clamped-tanh algebra amplifies.  Evaluating in float64 and rounding once reproduces torch."""
-    return fn(np.asarray(x, dtype=np.float64)).astype(np.float32)
+    torch's CPU float32 tanh/exp/log (what the reference runs) are correctly rounded for all but ~0.1-2% of
+    inputs; numpy's float32 SIMD versions differ from correct rounding for 30-50%, which the reference's
+    clamped-tanh algebra amplifies.  The float64 evaluation runs on torch's multi-threaded CPU kernels."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float64))
+    return _TORCH_FN[fn](t).to(torch.float32).numpy()
+
+
+def _torch_fns():
+    import torch
+    return {np.tanh: torch.tanh, np.exp: torch.exp, np.log: torch.log, np.log1p: torch.log1p, np.expm1: torch.expm1}
+
+
+class _LazyFns(dict):
+    def __missing__(self, key):
+        self.update(_torch_fns())
+        return dict.__getitem__(self, key)
+
+
+_TORCH_FN = _LazyFns()
 
 
 def _abs_patterns() -> np.ndarray:
@@ -124,29 +140,33 @@ def _branch_map(y, gamma, cache, branch):
 
     Float32 operation order: a = (gamma*y)*|b|; y_norm = sum_k y_k^2 (sequential k = 0..7);
     const = (-0.5*gamma) * (y_norm + |b|^2); linear = sum_k |a_k| (sequential) - 2*mismatch*min|a|.
+    (torch CPU tensors with separate float32 multiplies and adds: the same roundings as numpy.)
     """
-    base_abs = cache["base_abs"]  # (256, 8)
-    gy = (gamma * y)  # (N, 8)
+    import torch
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    base_abs = T(cache["base_abs"])  # (256, 8)
+    yt, gt = T(y), T(gamma)
+    gy = gt * yt  # (N, 8)
     a = gy[:, None, :] * base_abs[None, :, :]  # (N, 256, 8)
-    y_norm = np.zeros(y.shape[0], np.float32)
+    y_norm = torch.zeros(yt.shape[0], dtype=torch.float32)
     for k in range(8):
-        y_norm = y_norm + y[:, k] * y[:, k]
-    const = (f32(-0.5) * gamma[:, 0])[:, None] * (y_norm[:, None] + cache["base_sqnorm"][None, :])
-    abs_a = np.abs(a)
-    sum_abs = np.zeros(abs_a.shape[:2], np.float32)
+        y_norm = y_norm + yt[:, k] * yt[:, k]
+    const = (np.float32(-0.5) * gt[:, 0])[:, None] * (y_norm[:, None] + T(cache["base_sqnorm"])[None, :])
+    abs_a = a.abs()
+    sum_abs = torch.zeros(abs_a.shape[:2], dtype=torch.float32)
     for k in range(8):
         sum_abs = sum_abs + abs_a[:, :, k]
     neg = (a < 0)
-    best_parity = neg.sum(axis=2) & 1
-    min_pos = abs_a.argmin(axis=2)
-    min_abs = np.take_along_axis(abs_a, min_pos[..., None], axis=2)[..., 0]
-    mismatch = best_parity != cache["base_parity"][None, :]
-    sid = (neg.astype(np.int64) << np.arange(8)[None, None, :]).sum(axis=2)
-    sid = np.where(mismatch, sid ^ (1 << min_pos), sid)
-    best_linear = sum_abs - f32(2.0) * mismatch.astype(np.float32) * min_abs
+    best_parity = neg.sum(dim=2) & 1
+    min_abs, min_pos = abs_a.min(dim=2)  # first minimum
+    mismatch = best_parity != T(cache["base_parity"])[None, :]
+    bits = (1 << torch.arange(8, dtype=torch.int64))
+    sid = (neg.to(torch.int64) * bits).sum(dim=2)
+    sid = torch.where(mismatch, sid ^ bits[min_pos], sid)
+    best_linear = sum_abs - np.float32(2.0) * mismatch.to(torch.float32) * min_abs
     best_logscore = const + best_linear
-    idx = cache["idx_lut"][branch][np.arange(256)[None, :], sid]
-    return best_logscore.astype(np.float32), idx
+    idx = T(cache["idx_lut"][branch])[torch.arange(256)[None, :], sid]
+    return best_logscore.numpy(), idx.numpy()
 
 
 def _fold_prior(r1_blocks, gamma1, prior_center_blocks, prior_scale_blocks, prior_tau):
@@ -206,56 +226,59 @@ def _log1mexp(x):
 
 
 def _branch_stats(y, gamma, offset, branch, cache):
-    """mpq/priors/e8p12.py:169-308 (need_stats=False)."""
-    base_abs = cache["base_abs"]
-    parity_even = (cache["base_parity"] == 0)[None, :]
-    a = (gamma[:, :, None] * y[:, None, :]) * base_abs[None, :, :]
-    y_norm = (y * y).sum(axis=1, keepdims=True, dtype=np.float32)
-    const = f32(-0.5) * gamma * (y_norm + cache["base_sqnorm"][None, :])
-    aa = np.abs(a)
-    logC = (aa + _cr(np.log1p, _cr(np.exp, f32(-2.0) * aa))).sum(axis=-1, dtype=np.float32)  # logaddexp(a, -a)
-    t = _cr(np.tanh, a)
-    eps = f32(1e-7)
-    t = np.clip(t, f32(-0.99999988079071044921875), f32(0.99999988079071044921875))
-    lpt = _cr(np.log, np.maximum(np.abs(t), eps)).sum(axis=-1, dtype=np.float32)
-    neg = ((t < 0).sum(axis=-1) & 1).astype(bool)
-    pabs = _cr(np.exp, lpt)
-    prod = np.where(neg, -pabs, pabs).astype(np.float32)
-    lae = _cr(np.log1p, _cr(np.exp, lpt))  # logaddexp(0, lpt), lpt <= 0
-    l1me = _log1mexp(lpt)
-    lop = np.where(neg, l1me, lae)
-    lom = np.where(neg, lae, l1me)
-    logZ_even = logC + lop - f32(LOG2)
-    logZ_odd = logC + lom - f32(LOG2)
-    logZ = np.where(parity_even, logZ_even, logZ_odd)
-    prefix = np.ones_like(t)
-    acc = np.ones(t.shape[:2], np.float32)
+    """mpq/priors/e8p12.py:169-308 (need_stats=False).
+
+    Array work runs on torch CPU tensors (multi-threaded) in float32 with torch's own float32 CPU
+    transcendentals, i.e. the reference's arithmetic when it runs on the CPU."""
+    import torch
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    cr = lambda fn, x: fn(x)
+    base_abs = T(cache["base_abs"])
+    parity_even = T(cache["base_parity"] == 0)[None, :]
+    yt, gt = T(y), T(gamma)
+    a = (gt[:, :, None] * yt[:, None, :]) * base_abs[None, :, :]
+    y_norm = (yt * yt).sum(dim=1, keepdim=True)
+    const = np.float32(-0.5) * gt * (y_norm + T(cache["base_sqnorm"])[None, :])
+    aa = a.abs()
+    logC = (aa + cr(torch.log1p, cr(torch.exp, -2.0 * aa))).sum(dim=-1)  # logaddexp(a, -a)
+    t = cr(torch.tanh, a).clamp(-0.99999988079071044921875, 0.99999988079071044921875)
+    lpt = cr(torch.log, t.abs().clamp_min(1e-7)).sum(dim=-1)
+    neg = ((t < 0).sum(dim=-1) & 1).bool()
+    pabs = cr(torch.exp, lpt)
+    prod = torch.where(neg, -pabs, pabs)
+    lae = cr(torch.log1p, cr(torch.exp, lpt))  # logaddexp(0, lpt), lpt <= 0
+    l1me = torch.where(lpt < -LOG2, cr(torch.log1p, -cr(torch.exp, lpt)), cr(torch.log, -cr(torch.expm1, lpt)))
+    lop = torch.where(neg, l1me, lae)
+    lom = torch.where(neg, lae, l1me)
+    logZ = torch.where(parity_even, logC + lop - np.float32(LOG2), logC + lom - np.float32(LOG2))
+    prefix = torch.ones_like(t)
+    acc = torch.ones(t.shape[:2], dtype=torch.float32)
     for k in range(8):
         prefix[:, :, k] = acc
         acc = acc * t[:, :, k]
-    de = f32(1.0) + prod
-    do = f32(1.0) - prod
-    de = np.where(np.abs(de) > 1e-12, de, f32(1.0))
-    do = np.where(np.abs(do) > 1e-12, do, f32(1.0))
-    sm = np.empty_like(t)
-    suffix = np.ones(t.shape[:2], np.float32)
+    de = 1.0 + prod
+    do = 1.0 - prod
+    de = torch.where(de.abs() > 1e-12, de, torch.ones_like(de))
+    do = torch.where(do.abs() > 1e-12, do, torch.ones_like(do))
+    sm = torch.empty_like(t)
+    suffix = torch.ones(t.shape[:2], dtype=torch.float32)
     for k in reversed(range(8)):
         tk = t[:, :, k]
         ex = prefix[:, :, k] * suffix
-        sm[:, :, k] = np.where(parity_even, (tk + ex) / de, (tk - ex) / do)
+        sm[:, :, k] = torch.where(parity_even, (tk + ex) / de, (tk - ex) / do)
         suffix = suffix * tk
-    sm = np.nan_to_num(sm, nan=0.0, posinf=0.0, neginf=0.0)
-    off = f32(offset)
+    sm = torch.nan_to_num(sm, nan=0.0, posinf=0.0, neginf=0.0)
+    off = np.float32(offset)
     mu_core = sm * base_abs[None, :, :]
     mu = mu_core + off
-    second = cache["base_sqnorm"][None, :] + f32(8 * offset * offset) + f32(2.0) * off * mu_core.sum(axis=-1)
-    return {"log_component": (const + logZ).astype(np.float32), "mu_component": mu.astype(np.float32),
-            "second_component": second.astype(np.float32)}
+    second = T(cache["base_sqnorm"])[None, :] + np.float32(8 * offset * offset) + np.float32(2.0) * off * mu_core.sum(dim=-1)
+    return {"log_component": (const + logZ).numpy(), "mu_component": mu.numpy(), "second_component": second.numpy()}
 
 
 def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, prior_center_blocks=None, prior_scale_blocks=None,
                                     prior_tau=0.0, chunk_items=4096):
     """mpq/priors/e8p12.py:815-968 (need_stats=False): posterior mean, per-block variance, MAP."""
+    import torch
     B, nb, _ = r1_blocks.shape
     rw, gw = _fold_prior(r1_blocks, gamma1, prior_center_blocks, prior_scale_blocks, prior_tau)
     cache = factor_cache(cb)
@@ -269,17 +292,18 @@ def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, prior_center_block
         y = Y[s0:s0 + chunk_items]
         g = G[s0:s0 + chunk_items]
         outs = [_branch_stats((y - f32(o)).astype(np.float32), g, o, b, cache) for b, o in enumerate((0.25, -0.25))]
-        lc = np.concatenate([o["log_component"] for o in outs], axis=1)  # (n, 512)
-        m = lc.max(axis=1, keepdims=True)
-        lz = m + _cr(np.log, _cr(np.exp, lc - m).sum(axis=1, keepdims=True, dtype=np.float32))
-        w = _cr(np.exp, lc - lz)
-        mu = np.zeros((y.shape[0], 8), np.float32)
-        sec = np.zeros(y.shape[0], np.float32)
+        lc = torch.from_numpy(np.concatenate([o["log_component"] for o in outs], axis=1))  # (n, 512)
+        m = lc.max(dim=1, keepdim=True).values
+        lz = m + torch.log(torch.exp(lc - m).sum(dim=1, keepdim=True))
+        w = torch.exp(lc - lz)
+        mu = torch.zeros((y.shape[0], 8), dtype=torch.float32)
+        sec = torch.zeros(y.shape[0], dtype=torch.float32)
         for b in range(2):
             wb = w[:, b * 256:(b + 1) * 256]
-            mu += (wb[:, :, None] * outs[b]["mu_component"]).sum(axis=1)
-            sec += (wb * outs[b]["second_component"]).sum(axis=1)
-        var = np.maximum((sec - (mu * mu).sum(axis=1)) / f32(8.0), f32(0.0))
+            mu += (wb[:, :, None] * torch.from_numpy(outs[b]["mu_component"])).sum(dim=1)
+            sec += (wb * torch.from_numpy(outs[b]["second_component"])).sum(dim=1)
+        var = torch.clamp((sec - (mu * mu).sum(dim=1)) / np.float32(8.0), min=0.0).numpy()
+        mu = mu.numpy()
         idx, _ = map_search(y, g, cache)
         hi = g[:, 0] >= f32(1e3)
         mu[hi] = cb.grid[idx[hi]]
@@ -309,35 +333,75 @@ def stabilize_cholesky(gram, jitter=1e-6, max_tries=6):
     return np.linalg.cholesky(out).astype(np.float32)
 
 
-def gram_search(target, chol, grid):
+def metric_grid(chol, grid):
+    """gl = grid L (products and sums in index order k = 0..7, float32) and gn = |gl|^2 (order j = 0..7)."""
+    gT = np.ascontiguousarray(grid.T, dtype=np.float32)
+    cols = []
+    for j in range(8):
+        acc = np.zeros(grid.shape[0], np.float32)
+        for k in range(8):
+            if chol[k, j] != 0:  # exact zeros leave the float32 sum unchanged
+                acc += gT[k] * chol[k, j]
+        cols.append(acc)
+    gn = np.zeros(grid.shape[0], np.float32)
+    for j in range(8):
+        gn += cols[j] * cols[j]
+    return np.stack(cols, axis=1), gn
+
+
+def gram_search(target, chol, grid, metric=None):
     """argmin_c of  |t L|^2 + |g L|^2 - 2 (t L).(g L)  over the full grid (first minimum).
 
     Float32 with the products and sums in index order k = 0..7 (the fixed order of the CUDA kernel):
-    tl_j = sum_k t_k L[k, j]; gl_j likewise; score = (tn + gn) - 2 * sum_j tl_j gl_j."""
+    tl_j = sum_k t_k L[k, j]; gl_j likewise; score = (tn + gn) - 2 * sum_j tl_j gl_j.  `metric` is an
+    optional precomputed metric_grid(chol, grid)."""
     tl = np.zeros((target.shape[0], 8), np.float32)
-    gl = np.zeros((grid.shape[0], 8), np.float32)
     for j in range(8):
         for k in range(8):
             tl[:, j] = tl[:, j] + target[:, k] * chol[k, j]
-            gl[:, j] = gl[:, j] + grid[:, k] * chol[k, j]
+    gl, gn = metric if metric is not None else metric_grid(chol, grid)
     tn = np.zeros(target.shape[0], np.float32)
-    gn = np.zeros(grid.shape[0], np.float32)
     for j in range(8):
         tn = tn + tl[:, j] * tl[:, j]
-        gn = gn + gl[:, j] * gl[:, j]
-    best = np.empty(target.shape[0], np.int64)
-    for r0 in range(0, target.shape[0], 256):
-        t = tl[r0:r0 + 256]
-        cross = np.zeros((t.shape[0], grid.shape[0]), np.float32)
-        for j in range(8):
-            cross = cross + t[:, j:j + 1] * gl[None, :, j]
-        scores = (tn[r0:r0 + 256, None] + gn[None, :]) - f32(2.0) * cross
-        best[r0:r0 + 256] = scores.argmin(axis=1)
-    return best
+    glT = np.ascontiguousarray(gl.T)
+    R, G, CH = target.shape[0], grid.shape[0], 4096
+    best_s = np.full(R, np.inf, np.float32)
+    best_i = np.zeros(R, np.int64)
+    cross = np.empty((R, CH), np.float32)
+    tmp = np.empty((R, CH), np.float32)
+    rows = np.arange(R)
+    for c0 in range(0, G, CH):  # grid tiles that stay in cache; strict < keeps the first minimum
+        c1 = min(G, c0 + CH)
+        cr, tp = cross[:, :c1 - c0], tmp[:, :c1 - c0]
+        np.multiply(tl[:, 0:1], glT[0, None, c0:c1], out=cr)
+        for j in range(1, 8):
+            np.multiply(tl[:, j:j + 1], glT[j, None, c0:c1], out=tp)
+            np.add(cr, tp, out=cr)
+        np.add(tn[:, None], gn[None, c0:c1], out=tp)
+        np.multiply(cr, np.float32(2.0), out=cr)
+        np.subtract(tp, cr, out=tp)
+        i = tp.argmin(axis=1)
+        v = tp[rows, i]
+        upd = v < best_s
+        best_s = np.where(upd, v, best_s)
+        best_i = np.where(upd, i + c0, best_i)
+    return best_i
 
 
-def block_cd_gram(*, x, Y_u, Vs, cb, sweeps, idxs_init, accept_tol=0.0):
-    """Gram-metric greedy block CD over 8-blocks (mpq/polish/block_cd.py:332-625, compiled-step path)."""
+def block_metric_cache(Vs, cb):
+    """Every 8-block's metric grid (the per-layer part of block_cd_gram), keyed like its metric_cache."""
+    Vs = Vs.astype(np.float32)
+    grid = np.asarray(cb.grid, np.float32)
+    out = {}
+    for bi in range(Vs.shape[0] // 8):
+        vb = Vs[bi * 8:(bi + 1) * 8]
+        out[bi] = metric_grid(stabilize_cholesky((vb @ vb.T).astype(np.float32)), grid)
+    return out
+
+
+def block_cd_gram(*, x, Y_u, Vs, cb, sweeps, idxs_init, accept_tol=0.0, metric_cache=None):
+    """Gram-metric greedy block CD over 8-blocks (mpq/polish/block_cd.py:332-625, compiled-step path).
+    `metric_cache` (dict, optional) keeps each block's metric grid across sweeps and calls."""
     B, n = x.shape
     x_work = x.astype(np.float32).copy()
     Vs = Vs.astype(np.float32)
@@ -366,7 +430,12 @@ def block_cd_gram(*, x, Y_u, Vs, cb, sweeps, idxs_init, accept_tol=0.0):
             xb = x_work[:, bi * 8:(bi + 1) * 8]
             rhs = residual_u @ vb.T
             target = xb + rhs @ ginv
-            best = gram_search(target.astype(np.float32), L, grid)
+            mg = None
+            if metric_cache is not None:
+                mg = metric_cache.get(int(bi))
+                if mg is None:
+                    mg = metric_cache[int(bi)] = metric_grid(L, grid)
+            best = gram_search(target.astype(np.float32), L, grid, metric=mg)
             out = grid[best]
             delta = out - xb
             cross_r = (rhs * delta).sum(axis=1)
@@ -408,7 +477,7 @@ class E8P12VampConfig:
     best_iterate: bool = False
 
 
-def solve_e8p12_rankspace_vamp(*, Wr, hatWr_init, cb, V, Vh, S, Vs, cfg, obs_precision_init=None):
+def solve_e8p12_rankspace_vamp(*, Wr, hatWr_init, cb, V, Vh, S, Vs, cfg, obs_precision_init=None, metric_cache=None):
     """mpq/solver.py:853-1276 (block_cd polish with the gram metric)."""
     Wr = Wr.astype(f32)
     hat0 = hatWr_init.astype(f32)
@@ -524,7 +593,8 @@ def solve_e8p12_rankspace_vamp(*, Wr, hatWr_init, cb, V, Vh, S, Vs, cfg, obs_pre
     idx_stage1 = idx.copy()
     updates = 0.0
     if int(cfg.polish_sweeps) > 0:
-        hat, idx, st = block_cd_gram(x=hat, Y_u=Y_u, Vs=Vs, cb=cb, sweeps=int(cfg.polish_sweeps), idxs_init=idx)
+        hat, idx, st = block_cd_gram(x=hat, Y_u=Y_u, Vs=Vs, cb=cb, sweeps=int(cfg.polish_sweeps), idxs_init=idx,
+                                     metric_cache=metric_cache)
         updates = st["accepted_updates"]
     err = U.vamp_rankspace_error(Y_u=Y_u, x=hat, Vs=Vs)
     stats = {"obs_precision_initial": obs0, "obs_precision_final": obs, "alpha1_retry_count": retries,
@@ -560,10 +630,11 @@ def refine_codebook(*, Wr, Hr, cb, cfg: E8P12VampConfig, block_rows=128, jitter_
     hat = hat0.copy()
     idx = idx0.copy()
     blocks = []
+    mcache = {}
     for r0 in range(0, m, block_rows):
         rb = slice(r0, min(r0 + block_rows, m))
         h, i, e, st = solve_e8p12_rankspace_vamp(Wr=Wr[rb], hatWr_init=hat0[rb], cb=cb, V=V, Vh=Vh, S=S, Vs=Vs,
-                                                 cfg=cfg, obs_precision_init=obs)
+                                                 cfg=cfg, obs_precision_init=obs, metric_cache=mcache)
         hat[rb] = h
         idx[rb] = i
         if cfg.em_obs_precision and float(cfg.obs_precision) <= 0.0:
