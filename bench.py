@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--cpu-sample-rows", type=int, default=0, help="0: workload default")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="> 0: solve only this many rows per GPU (a small case for ncu; not a bench line)")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up + one timed step, no e2e / CPU legs (for an ncu launch list)")
     a = ap.parse_args()
@@ -219,6 +221,8 @@ def run_mpq(args):
         dist.broadcast(W, 0)
         dist.broadcast(H, 0)
     rows_per = M_ROWS // world
+    if args.rows > 0:
+        rows_per = min(rows_per, args.rows)
     Wr = W[rank * rows_per:(rank + 1) * rows_per].contiguous()
     block_rows = min(args.block_rows, rows_per)
     if args.workload == "e8p12":

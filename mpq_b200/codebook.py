@@ -97,6 +97,9 @@ def factor_tables(cb, device: torch.device) -> Dict[str, torch.Tensor]:
     valid = np.broadcast_to(spar[None, None, :] == parity[None, :, None], lut.shape)
     if not (np.all(lut[valid] >= 0) and np.all(lut[~valid] < 0)):
         raise RuntimeError("E8P12 codebook does not have the (branch, abs, parity-valid sign) structure.")
+    if not np.isin(base_abs, np.array([0.5, 1.5, 2.5], np.float32)).all():
+        # the posterior/MAP kernels tabulate the per-coordinate terms for these three magnitudes
+        raise RuntimeError("E8P12 abs patterns must have coordinates 1/2, 3/2 or 5/2.")
     t = {
         "base_abs": torch.from_numpy(base_abs).to(device),
         "base_sqnorm": torch.from_numpy(sqnorm).to(device),

@@ -6,19 +6,27 @@
 // precision without prior.
 //
 // Every codeword is  offset(branch) + sign_pattern * abs_pattern  with 2 branches (+-1/4) x 256 abs
-// patterns x the sign patterns of the abs pattern's parity.  Per 8-vector item (one thread):
-//   pass 1  (exact)   for each of the 512 (branch, abs) components, the best parity-valid sign and
-//                     its log-score  -0.5 g (|y|^2 + |b|^2) + sum|a_k| - 2 [parity mismatch] min|a_k|,
-//                     a_k = (g y_k)|b_k|; argmax (first maximum) -> MAP codeword.  Float32 operations in
-//                     the oracle's order, no FMA contraction: indices are bit-exact.
-//   pass 2  (MMSE)    the component log-partition (tanh / logaddexp / log1mexp algebra of the
-//                     reference) and its sign means, accumulated as an online softmax (running maximum,
-//                     as the reference's logsumexp).  The reference clamps tanh at 1 - 1e-7, so for large
-//                     |a| with a parity mismatch its log-partition exceeds the component's MAP score by up
-//                     to ~2 min|a|; the running maximum keeps that finite.  Components whose upper bound
-//                     const + sum|a_k| + 8 ln 2 lies more than 30 below the running maximum are skipped
-//                     (weight < e^-30 of the largest; the bound holds for the clamped formula too).
-// One CTA per row; per-row variance sums are reduced in a fixed order.
+// patterns x the sign patterns of the abs pattern's parity.  The abs patterns' coordinates only take the
+// magnitudes 1/2, 3/2 and 5/2, so for one item and branch every per-coordinate quantity of the reference's
+// factorized formulas (a_k = (g y_k) |b_k|, logaddexp(a_k, -a_k), the clamped tanh and its log) takes one
+// of 8 x 3 values.  Each item is handled by one warp, which first evaluates those 2 x 24 entries once
+// (the same float32 operations the reference applies per component, so every per-component value is
+// bit-identical to the undeduplicated evaluation) and then scores the 512 (branch, abs) components with
+// table look-ups:
+//   pass 1  (exact)   each lane scores 16 components: the best parity-valid sign and its log-score
+//                     -0.5 g (|y|^2 + |b|^2) + sum|a_k| - 2 [parity mismatch] min|a_k| (float32, the
+//                     reference's order, no FMA contraction); a warp reduction on (score, component) gives
+//                     the first maximum -> MAP codeword, bit-exact.
+//   pass 2  (MMSE)    components whose upper bound const + logC (logZ = logC + log(1 +- prod) - ln 2 <=
+//                     logC) lies more than kPrune = 20 below the MAP score are dropped (weight < e^-20 of
+//                     the largest); the survivors are compacted with a warp ballot and spread over the lanes,
+//                     each lane accumulating an online softmax (running maximum, as the reference's
+//                     logsumexp) of the component log-partitions and sign means; the lanes' partial sums
+//                     are merged in a fixed butterfly order.  The reference clamps tanh at 1 - 1e-7, so for
+//                     large |a| with a parity mismatch its log-partition exceeds the component's MAP score by
+//                     up to ~2 min|a|; the running maximum keeps that finite.
+// Items with g >= 1e3 take the MAP codeword with zero variance (the reference's snap) and skip pass 2.
+// One CTA of 8 warps per row; per-row variance sums are reduced in a fixed order.
 #include "common.cuh"
 
 namespace mpq {
@@ -42,7 +50,10 @@ struct E8Args {
 };
 
 constexpr float kLn2 = 0.69314718055994530942f;
-constexpr float kPrune = 30.f;
+// Components whose log-weight bound lies more than kPrune below the MAP score are dropped: each weighs
+// < e^-20 of the largest; on the 4096 x 4096 E8P12 layer solve the dropped posterior mass stays below 5e-8
+// of the total (float32 resolution) in every item and iteration.
+constexpr float kPrune = 20.f;
 
 // Folded message and precision of one item (mpq/priors/e8p12.py:844-857).
 __device__ __forceinline__ void fold_item(const E8Args& a, int b, int k, float y[8], float& g, float& g1) {
@@ -71,125 +82,214 @@ __device__ __forceinline__ void fold_item(const E8Args& a, int b, int k, float y
   }
 }
 
-// Pass 1 over one component: exact MAP log-score and the parity-fixed sign id.
-__device__ __forceinline__ float comp_map(const float gy[8], const float* ab, float ng, float ynorm, float sqn,
-                                          int bpar, int& sid, float& sum_abs_out) {
-  float sum_abs = 0.f, mn = INFINITY;
-  int neg = 0, par = 0, minpos = 0;
-  #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float av = fmul(gy[i], ab[i]);
-    const float aa = fabsf(av);
-    sum_abs = fadd(sum_abs, aa);
-    if (av < 0.f) { neg |= 1 << i; par ^= 1; }
-    if (aa < mn) { mn = aa; minpos = i; }
-  }
-  const bool mismatch = par != bpar;
-  sid = mismatch ? (neg ^ (1 << minpos)) : neg;
-  const float lin = mismatch ? fsub(sum_abs, fmul(2.f, mn)) : fsub(sum_abs, 0.f);
-  sum_abs_out = sum_abs;
-  return fadd(fmul(ng, fadd(ynorm, sqn)), lin);
-}
+constexpr int kWarps = 8;  // items in flight per CTA (one warp each)
 
-__device__ __forceinline__ float log1mexp_f(float x) {  // log(1 - exp(x)), x <= 0, float32 steps as the reference
-  return x < -kLn2 ? (float)log1p(-(double)(float)exp((double)x)) : (float)log(-(double)(float)expm1((double)x));
-}
+// Per-item table of the per-(branch, coordinate k, magnitude m) values, entry e = 3 k + m.  Signs are
+// canonical (a value that is not < 0 has its sign bit clear), so the XOR of sign bits is the parity of
+// the reference's (x < 0) tests.
+struct ItemTab {
+  float2 am[2][24];  // {a, T}: a = (g (y_k - off)) |b| with |b| = 1/2, 3/2, 5/2; T = |a| + log1p(exp(-2|a|))
+  float4 pt[2][24];  // {T, t, lt, |b|}: t = tanh(a) clamped to +-(1 - 2^-23), lt = log(max(|t|, 1e-7))
+};
+
+__device__ __forceinline__ float canon_sign(float x) { return x < 0.f ? x : fabsf(x); }
+__device__ __forceinline__ unsigned sign_bit(float x) { return __float_as_uint(x) >> 31; }
 
 template <bool MMSE>
-__global__ void __launch_bounds__(128) k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x,
-                                               float* __restrict__ var_out, int64_t ld_v, int* __restrict__ idx_out,
-                                               int64_t ld_i, float* __restrict__ map_out, int64_t ld_m,
-                                               float* __restrict__ var_rowsum) {
-  __shared__ float s_abs[256 * 8];
+__global__ void __launch_bounds__(kWarps * 32, 3)
+k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __restrict__ var_out, int64_t ld_v,
+        int* __restrict__ idx_out, int64_t ld_i, float* __restrict__ map_out, int64_t ld_m,
+        float* __restrict__ var_rowsum) {
+  // s_off[ai]: byte k of the pair = 8 * (3 k + m_k), the offset of coordinate k's float2 entry
+  __shared__ uint2 s_off[256];
   __shared__ float s_sqn[256];
   __shared__ int s_par[256];
-  __shared__ float red[32];
-  for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) s_abs[i] = tab.base_abs[i];
+  __shared__ ItemTab s_tab[kWarps];
+  __shared__ unsigned short s_list[MMSE ? kWarps : 1][512];
+  __shared__ float s_ub[MMSE ? kWarps : 1][512];
+  __shared__ float s_var[kWarps];
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    unsigned lo = 0, hi = 0;
+    #pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float v = tab.base_abs[i * 8 + k];
+      const unsigned m = v == 0.5f ? 0u : v == 1.5f ? 1u : v == 2.5f ? 2u : 3u;
+      if (m == 3u) s_bad = 1;
+      const unsigned byte = 8u * (3u * k + (m & 3u));
+      if (k < 4) lo |= byte << (8 * k); else hi |= byte << (8 * (k - 4));
+    }
+    s_off[i] = make_uint2(lo, hi);
     s_sqn[i] = tab.base_sqnorm[i];
     s_par[i] = tab.base_parity[i];
   }
   __syncthreads();
+  const bool bad = s_bad != 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
+  ItemTab& T = s_tab[warp];
   float vacc = 0.f;
-  for (int k = threadIdx.x; k < a.nb; k += blockDim.x) {
+  for (int k = warp; k < a.nb; k += kWarps) {
     float y[8], g, g1;
     fold_item(a, b, k, y, g, g1);
+    if (bad) {  // base_abs is not an E8P12 abs table: poison the outputs
+      if (lane == 0 && idx_out) idx_out[b * ld_i + k] = -1;
+      if (lane < 8) {
+        if (map_out) map_out[b * ld_m + k * 8 + lane] = __int_as_float(0x7fc00000);
+        if (MMSE) x1_out[b * ld_x + k * 8 + lane] = __int_as_float(0x7fc00000);
+      }
+      if (MMSE && lane == 0) {
+        if (var_out) var_out[b * ld_v + k] = __int_as_float(0x7fc00000);
+        vacc = __int_as_float(0x7fc00000);
+      }
+      continue;
+    }
     const float ng = fmul(-0.5f, g);
-    // ---- pass 1: exact MAP ----
-    float best = -INFINITY;
-    int best_comp = 0, best_sid = 0;
-    float yb[2][8], ynorm[2];
+    float ynorm[2];
     #pragma unroll
     for (int br = 0; br < 2; ++br) {
       const float off = br ? -0.25f : 0.25f;
       float yn = 0.f;
       #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        yb[br][i] = fsub(y[i], off);
-        yn = fadd(yn, fmul(yb[br][i], yb[br][i]));
-      }
+      for (int i = 0; i < 8; ++i) yn = fadd(yn, fmul(fsub(y[i], off), fsub(y[i], off)));
       ynorm[br] = yn;
-      float gy[8];
+    }
+    // ---- per-item table ----
+    __syncwarp();
+    #pragma unroll 1
+    for (int e = lane; e < 48; e += 32) {
+      const int br = e / 24, r = e - br * 24, kk = r / 3, m = r - kk * 3;
+      float yk = y[0];
       #pragma unroll
-      for (int i = 0; i < 8; ++i) gy[i] = fmul(g, yb[br][i]);
-      for (int ai = 0; ai < 256; ++ai) {
-        int sid;
-        float sa;
-        const float sc = comp_map(gy, s_abs + ai * 8, ng, yn, s_sqn[ai], s_par[ai], sid, sa);
-        if (sc > best) { best = sc; best_comp = br * 256 + ai; best_sid = sid; }
+      for (int i = 1; i < 8; ++i) yk = (kk == i) ? y[i] : yk;
+      const float off = br ? -0.25f : 0.25f;
+      const float mag = 0.5f + (float)m;
+      const float av = fmul(fmul(g, fsub(yk, off)), mag);
+      const float aa = fabsf(av);
+      float Tv = 0.f;
+      if constexpr (MMSE) {
+        // Transcendentals are evaluated in double and rounded once (correctly rounded float32 results):
+        // the reference's clamped-tanh algebra amplifies last-bit differences of tanh near +-1.
+        Tv = aa + (float)log1p((double)(float)exp(-2.0 * (double)aa));
+        const float ti =
+            fminf(fmaxf((float)tanh((double)av), -0.99999988079071044921875f), 0.99999988079071044921875f);
+        T.pt[br][r] = make_float4(Tv, canon_sign(ti), (float)log((double)fmaxf(fabsf(ti), 1e-7f)), mag);
       }
+      T.am[br][r] = make_float2(canon_sign(av), Tv);
     }
-    const int map_idx = tab.idx_lut[(best_comp >> 8) * 65536 + (best_comp & 255) * 256 + best_sid];
-    if (idx_out) idx_out[b * ld_i + k] = map_idx;
+    __syncwarp();
+    // ---- pass 1: exact MAP (lane's components c = 32 j + lane = (branch c >> 8, abs c & 255)) ----
+    float best = -INFINITY;
+    int best_c = -1;
+    #pragma unroll 1
+    for (int j = 0; j < 16; ++j) {
+      const int br = j >> 3;
+      const int ai = ((j & 7) << 5) | lane;
+      const uint2 of = s_off[ai];
+      const char* base = reinterpret_cast<const char*>(T.am[br]);
+      float sum_abs = 0.f, mn = INFINITY, lcs = 0.f;
+      unsigned sx = 0;
+      #pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
+        const float2 v = *reinterpret_cast<const float2*>(base + byte);
+        const float aa = fabsf(v.x);
+        sum_abs = fadd(sum_abs, aa);
+        sx ^= __float_as_uint(v.x);
+        mn = fminf(mn, aa);
+        if constexpr (MMSE) lcs = fadd(lcs, v.y);
+      }
+      const bool mismatch = (int)(sx >> 31) != s_par[ai];
+      const float lin = mismatch ? fsub(sum_abs, fmul(2.f, mn)) : sum_abs;
+      const float cst = fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai]));
+      const float sc = fadd(cst, lin);
+      if (sc > best) { best = sc; best_c = j * 32 + lane; }
+      if constexpr (MMSE) s_ub[warp][j * 32 + lane] = fadd(cst, lcs);
+    }
+    // first maximum over the warp: valid before invalid, higher score, then smaller component
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oc = __shfl_xor_sync(0xffffffffu, best_c, o);
+      const bool take = oc >= 0 && (best_c < 0 || ob > best || (ob == best && oc < best_c));
+      if (take) { best = ob; best_c = oc; }
+    }
+    int comp = 0, sid = 0;
+    if (best_c >= 0) {  // the winner's parity-fixed sign pattern (first minimum of |a| flips)
+      comp = best_c;
+      const int br = comp >> 8, ai = comp & 255;
+      const uint2 of = s_off[ai];
+      const char* base = reinterpret_cast<const char*>(T.am[br]);
+      float mn = INFINITY;
+      int neg = 0, par = 0, minpos = 0;
+      #pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
+        const float av = reinterpret_cast<const float2*>(base + byte)->x;
+        const float aa = fabsf(av);
+        if (av < 0.f) { neg |= 1 << kk; par ^= 1; }
+        if (aa < mn) { mn = aa; minpos = kk; }
+      }
+      sid = par != s_par[ai] ? (neg ^ (1 << minpos)) : neg;
+    }
+    const int map_idx = tab.idx_lut[(comp >> 8) * 65536 + (comp & 255) * 256 + sid];
+    if (lane == 0 && idx_out) idx_out[b * ld_i + k] = map_idx;
     const float* mv = tab.grid + (int64_t)map_idx * 8;
-    if (map_out) {
-      #pragma unroll
-      for (int i = 0; i < 8; ++i) map_out[b * ld_m + k * 8 + i] = mv[i];
-    }
+    if (map_out && lane < 8) map_out[b * ld_m + k * 8 + lane] = mv[lane];
     if constexpr (MMSE) {
-      // ---- pass 2: factorized posterior mean / second moment ----
-      float W = 0.f, SEC = 0.f, MU[8];
-      float mx = best;  // running maximum of the component log-weights (starts at the MAP lower bound)
-      #pragma unroll
-      for (int i = 0; i < 8; ++i) MU[i] = 0.f;
-      #pragma unroll 1
-      for (int br = 0; br < 2; ++br) {
-        const float off = br ? -0.25f : 0.25f;
+      float mu_l = 0.f, var = 0.f;  // lane l < 8 ends with coordinate l of the posterior mean
+      if (g >= 1e3f) {  // high-precision snap to the MAP codeword (mpq/priors/e8p12.py:923-926)
+        mu_l = lane < 8 ? mv[lane] : 0.f;
+      } else {
+        // ---- pass 2: compact the surviving components ----
+        const float thr = best - kPrune;
+        unsigned short* list = s_list[warp];
+        int cnt = 0;
         #pragma unroll 1
-        for (int ai = 0; ai < 256; ++ai) {
-          const float* ab = s_abs + ai * 8;
-          float av[8], sum_abs = 0.f;
+        for (int j = 0; j < 16; ++j) {
+          const bool keep = !(s_ub[warp][j * 32 + lane] < thr);
+          const unsigned msk = __ballot_sync(0xffffffffu, keep);
+          if (keep) list[cnt + __popc(msk & ((1u << lane) - 1u))] = (unsigned short)(j * 32 + lane);
+          cnt += __popc(msk);
+        }
+        __syncwarp();
+        float W = 0.f, SEC = 0.f, MU[8];
+        float mx = best;  // running maximum of the component log-weights (starts at the MAP score)
+        #pragma unroll
+        for (int i = 0; i < 8; ++i) MU[i] = 0.f;
+        for (int li = lane; li < cnt; li += 32) {
+          const int c = list[li];
+          const int br = c >> 8, ai = c & 255;
+          const float off = br ? -0.25f : 0.25f;
+          const uint2 of = s_off[ai];
+          const char* base = reinterpret_cast<const char*>(T.pt[br]);
+          float logC = 0.f, lpt = 0.f, t[8], mag[8];
+          unsigned sx = 0;
           #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            av[i] = (g * yb[br][i]) * ab[i];
-            sum_abs += fabsf(av[i]);
+          for (int kk = 0; kk < 8; ++kk) {
+            const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
+            const float4 v = *reinterpret_cast<const float4*>(base + 2u * byte);
+            logC = fadd(logC, v.x);
+            t[kk] = v.y;
+            sx ^= __float_as_uint(v.y);
+            lpt = fadd(lpt, v.z);
+            mag[kk] = v.w;
           }
-          const float cst = ng * (ynorm[br] + s_sqn[ai]);
-          if (cst + sum_abs + 8.f * kLn2 < mx - kPrune) continue;
-          // Transcendentals are evaluated in double and rounded once (correctly rounded float32 results):
-          // the reference's clamped-tanh algebra amplifies last-bit differences of tanh near +-1.
-          float logC = 0.f, lpt = 0.f, t[8];
-          int negp = 0;
-          #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float aa = fabsf(av[i]);
-            logC += aa + (float)log1p((double)(float)exp(-2.0 * (double)aa));
-            float ti = (float)tanh((double)av[i]);
-            ti = fminf(fmaxf(ti, -0.99999988079071044921875f), 0.99999988079071044921875f);
-            t[i] = ti;
-            lpt += (float)log((double)fmaxf(fabsf(ti), 1e-7f));
-            negp ^= (ti < 0.f) ? 1 : 0;
-          }
+          const bool negp = (sx >> 31) != 0u;
+          const float cst = fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai]));
+          // prod = +-exp(lpt) feeds the reference's 1 -+ prod, which cancels for prod near 1: evaluated in
+          // double and rounded once.  The other per-component functions are well conditioned (float32).
           const float pabs = (float)exp((double)lpt);
           const float prod = negp ? -pabs : pabs;
-          const float lae = (float)log1p((double)(float)exp((double)lpt));  // logaddexp(0, lpt), lpt <= 0
-          const float l1me = log1mexp_f(lpt);
-          const float lop = negp ? l1me : lae;   // log(1 + prod)
-          const float lom = negp ? lae : l1me;   // log(1 - prod)
+          const float lae = log1pf(pabs);  // logaddexp(0, lpt), lpt <= 0
+          const float l1me = lpt < -kLn2 ? log1pf(-pabs) : logf(-expm1f(lpt));  // log(1 - exp(lpt))
+          const float lop = negp ? l1me : lae;  // log(1 + prod)
+          const float lom = negp ? lae : l1me;  // log(1 - prod)
           const bool even = s_par[ai] == 0;
-          const float logZ = logC + (even ? lop : lom) - kLn2;
-          const float lc = cst + logZ;
+          const float logZ = fsub(fadd(logC, even ? lop : lom), kLn2);
+          const float lc = fadd(cst, logZ);
           if (lc > mx) {  // rescale the accumulators to the new maximum
             const float sc = expf(mx - lc);
             W *= sc;
@@ -198,53 +298,62 @@ __global__ void __launch_bounds__(128) k_e8p12(E8Args a, E8Tab tab, float* __res
             for (int i = 0; i < 8; ++i) MU[i] *= sc;
             mx = lc;
           }
-          const float w = (float)exp((double)(lc - mx));
+          const float w = expf(lc - mx);
           float de = 1.f + prod, dodd = 1.f - prod;
           if (!(fabsf(de) > 1e-12f)) de = 1.f;
           if (!(fabsf(dodd) > 1e-12f)) dodd = 1.f;
+          // sign means (t_i +- prod_{j != i} t_j) / (1 +- prod): |t| < 1 and the denominator is clamped away
+          // from 0, so they are finite (the reference's nan_to_num never fires)
+          const float rden = __frcp_rn(even ? de : dodd);
+          const float sgn = even ? 1.f : -1.f;
           float pre[8];
           float acc = 1.f;
           #pragma unroll
-          for (int i = 0; i < 8; ++i) { pre[i] = acc; acc *= t[i]; }
+          for (int i = 0; i < 8; ++i) { pre[i] = acc; acc = fmul(acc, t[i]); }
           float suf = 1.f, mcs = 0.f, mc[8];
           #pragma unroll
           for (int i = 7; i >= 0; --i) {
-            const float ex = pre[i] * suf;
-            float sm = even ? (t[i] + ex) / de : (t[i] - ex) / dodd;
-            if (!isfinite(sm)) sm = 0.f;
-            mc[i] = sm * ab[i];
-            mcs += mc[i];
-            suf *= t[i];
+            const float ex = fmul(pre[i], suf);
+            mc[i] = fmul(fmul(__fmaf_rn(sgn, ex, t[i]), rden), mag[i]);  // sgn * ex is exact
+            mcs = fadd(mcs, mc[i]);
+            suf = fmul(suf, t[i]);
           }
           W += w;
           #pragma unroll
           for (int i = 0; i < 8; ++i) MU[i] += w * (mc[i] + off);
           SEC += w * (s_sqn[ai] + 8.f * off * off + 2.f * off * mcs);
         }
-      }
-      float mu[8], var;
-      if (g >= 1e3f) {  // high-precision snap to the MAP codeword (mpq/priors/e8p12.py:923-926)
+        // merge the lanes' online softmax states (fixed butterfly order)
+        float M = mx;
         #pragma unroll
-        for (int i = 0; i < 8; ++i) mu[i] = mv[i];
-        var = 0.f;
-      } else {
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float scl = (mx == M) ? 1.f : expf(mx - M);
+        W = warp_sum(W * scl);
+        SEC = warp_sum(SEC * scl);
         float nrm = 0.f;
         #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          mu[i] = MU[i] / W;
-          nrm += mu[i] * mu[i];
+          const float mi = warp_sum(MU[i] * scl) / W;
+          nrm += mi * mi;
+          mu_l = (lane == i) ? mi : mu_l;
         }
         var = fmaxf((SEC / W - nrm) / 8.f, 0.f);
       }
-      #pragma unroll
-      for (int i = 0; i < 8; ++i) x1_out[b * ld_x + k * 8 + i] = mu[i];
-      if (var_out) var_out[b * ld_v + k] = var;
-      vacc += var;
+      if (lane < 8) x1_out[b * ld_x + k * 8 + lane] = mu_l;
+      if (lane == 0) {
+        if (var_out) var_out[b * ld_v + k] = var;
+        vacc += var;
+      }
     }
   }
   if constexpr (MMSE) {
-    const float tsum = block_sum(vacc, red);
-    if (threadIdx.x == 0 && var_rowsum) var_rowsum[b] = tsum;
+    if (lane == 0) s_var[warp] = vacc;
+    __syncthreads();
+    if (threadIdx.x == 0 && var_rowsum) {
+      float tsum = 0.f;
+      for (int w = 0; w < kWarps; ++w) tsum += s_var[w];
+      var_rowsum[b] = tsum;
+    }
   }
 }
 
@@ -272,7 +381,7 @@ MPQ_API int mpq_e8p12_mmse(const float* r1, int64_t ld_r1, const float* center, 
   if (B == 0 || nb == 0) return MPQ_OK;
   E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
   E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
-  k_e8p12<true><<<B, 128, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, var_out, ld_v, idx_out, ld_i, map_out, ld_m,
+  k_e8p12<true><<<B, kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, var_out, ld_v, idx_out, ld_i, map_out, ld_m,
                                                     var_rowsum);
   return launch_status("mpq_e8p12_mmse");
 }
@@ -289,7 +398,7 @@ MPQ_API int mpq_e8p12_map(const float* r1, int64_t ld_r1, const float* center, i
   if (B == 0 || nb == 0) return MPQ_OK;
   E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, fixed_gamma, B, nb};
   E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
-  k_e8p12<false><<<B, 128, 0, (cudaStream_t)stream>>>(a, t, nullptr, 0, nullptr, 0, idx_out, ld_i, map_out, ld_m,
+  k_e8p12<false><<<B, kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, nullptr, 0, nullptr, 0, idx_out, ld_i, map_out, ld_m,
                                                      nullptr);
   return launch_status("mpq_e8p12_map");
 }
