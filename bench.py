@@ -148,7 +148,7 @@ class ClockSampler:
 # ----------------------------------------------------------------------------------------------
 
 class ScalarWorkload:
-    dominant = "gemm"
+    dominant = "gemm_tc"
 
     def __init__(self, dev, block_rows):
         self.dev, self.block_rows = dev, block_rows
@@ -168,7 +168,7 @@ class ScalarWorkload:
 
 
 class E8Workload:
-    dominant = "gemm"
+    dominant = "e8p12_mmse"
 
     def __init__(self, dev, block_rows, SU, SV):
         from mpq_b200.codebook import E8P12_codebook
@@ -295,10 +295,7 @@ def run_mpq(args):
     if rank == 0:
         pk = ROOT / "MEASURED_PEAKS.json"
         peaks = json.loads(pk.read_text()) if pk.exists() else {}
-        peak_tf = float(peaks.get("bf16_tflops_sustained", 1394.3))
-        achieved = dom["work_avg"] / (dom["ms_avg"] * 1e-3) / 1e12 if dom["ms_avg"] > 0 else 0.0
-        tf = ROOT / "profiles" / "gemm_traffic.json"
-        traffic = json.loads(tf.read_text()).get("bytes_per_launch") if tf.exists() else None
+        roofline = dominant_roofline(wl.dominant, dom, peaks, args.steps)
         result = {
             "metric": METRIC, "value": ms / 1e3, "unit": "s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
@@ -308,13 +305,7 @@ def run_mpq(args):
                        "parallelism": f"rows{world}", "l2": "256 MB buffer written between timed steps"},
             "e2e": {"value": e2e / 1e3, "unit": "s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": int(round(launches)),
-            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 3xTF32 rank-space products)",
-                         "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved / peak_tf if peak_tf else None, "traffic": traffic,
-                         "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (measured)",
-                         "achieved_counts": "algorithmic 2MNK per product (3xTF32 issues 3 TF32 MMAs per FLOP)",
-                         "launches_per_step": dom["launches"] / max(args.steps, 1),
-                         "ms_per_step": dom["ms_total"] / max(args.steps, 1)},
+            "roofline": roofline,
             "clocks": clk,
             "stats": stats,
         }
@@ -324,6 +315,37 @@ def run_mpq(args):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+# DRAM traffic per launch of the dominant kernels, from ncu captures (dram__bytes_read.sum +
+# dram__bytes_write.sum); the summaries with their commands are under profiles/.
+TRAFFIC = {
+    # k_gemm_tc, one 4096 x 4096 x 4096 3xTF32 product (profiles/k_gemm_tc_4096.md)
+    "gemm_tc": {"bytes": 1.012e9 + 0.062e9, "launch": "4096x4096x4096 3xTF32 product"},
+    # k_e8p12<1>, 4096 rows x 512 blocks (profiles/k_e8p12_posterior.md)
+    "e8p12_mmse": {"bytes": 1.440e8 + 0.426e8, "launch": "4096 rows x 512 blocks"},
+}
+
+
+def dominant_roofline(name, dom, peaks, steps):
+    """roofline object of the dominant kernel from its CUDA-event launch times and algorithmic work."""
+    secs = dom["ms_avg"] * 1e-3
+    common = {"launches_per_step": dom["launches"] / max(steps, 1), "ms_per_step": dom["ms_total"] / max(steps, 1),
+              "traffic": TRAFFIC[name]["bytes"], "traffic_launch": TRAFFIC[name]["launch"]}
+    if name == "gemm_tc":
+        peak = float(peaks.get("bf16_tflops_sustained", 1394.3))
+        achieved = dom["work_avg"] / secs / 1e12 if secs > 0 else 0.0
+        return {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 3xTF32 rank-space products)", "achieved": achieved,
+                "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (measured)" if peaks else "fallback",
+                "achieved_counts": "algorithmic 2MNK per product (3xTF32 issues 3 TF32 MMAs per FLOP)", **common}
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = dom["work_avg"] / secs / 1e9 if secs > 0 else 0.0
+    return {"bound": "hbm", "kernel": "k_e8p12<1> (E8P12 factorized posterior)", "achieved": achieved, "peak": peak,
+            "unit": "GB/s", "frac": achieved / peak,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback",
+            "achieved_counts": "algorithmic bytes: r1, prior centre and x1 (12 B per coordinate) + per-row scalars",
+            "note": "compute-bound (FP32/ALU issue), not HBM-bound: see profiles/k_e8p12_posterior.md", **common}
 
 
 # ----------------------------------------------------------------------------------------------
@@ -406,12 +428,14 @@ def run_reference(args):
     if rank != 0:
         return None
     vals, info = [], None
+    for _ in range(max(args.warmup, 0)):  # warm-up: thread pools, allocator, page cache (small sample)
+        cpu_sample(args.workload, 2)
     for _ in range(max(args.steps, 1)):
         info = cpu_sample(args.workload, args.cpu_sample_rows)
         vals.append(info["value"])
     v = float(np.mean(vals))
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": "s", "n_gpus": world, "steps": args.steps,
-            "warmup": 0, "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong",
+            "warmup": args.warmup, "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
             "config": {"workload": WORKLOAD_DESC[args.workload], "parallelism": "cpu"},
             "cpu_baseline": {k: info[k] for k in ("value", "unit", "cores", "kind", "sample")},

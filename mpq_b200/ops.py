@@ -40,10 +40,10 @@ def gemm_nt(A: torch.Tensor, Bt: torch.Tensor, out: Optional[torch.Tensor] = Non
         raise ValueError(f"gemm_nt shape mismatch {tuple(A.shape)} x {tuple(Bt.shape)}^T")
     if out is None:
         out = torch.empty(M, N, device=A.device, dtype=torch.float32)
-    tok = trace.begin_timing("gemm")
+    tok = trace.begin_timing("gemm_f32")
     call("mpq_gemm_f32", 0, M, N, K, float(alpha), ptr(A), A.stride(0), ptr(Bt), Bt.stride(0), float(beta),
          ptr(out), out.stride(0))
-    trace.end_timing("gemm", tok, 2.0 * M * N * K)
+    trace.end_timing("gemm_f32", tok, 2.0 * M * N * K)
     return out
 
 
@@ -57,10 +57,10 @@ def gemm_nn(A: torch.Tensor, Bm: torch.Tensor, out: Optional[torch.Tensor] = Non
         raise ValueError(f"gemm_nn shape mismatch {tuple(A.shape)} x {tuple(Bm.shape)}")
     if out is None:
         out = torch.empty(M, N, device=A.device, dtype=torch.float32)
-    tok = trace.begin_timing("gemm")
+    tok = trace.begin_timing("gemm_f32")
     call("mpq_gemm_f32", 1, M, N, K, float(alpha), ptr(A), A.stride(0), ptr(Bm), Bm.stride(0), float(beta),
          ptr(out), out.stride(0))
-    trace.end_timing("gemm", tok, 2.0 * M * N * K)
+    trace.end_timing("gemm_f32", tok, 2.0 * M * N * K)
     return out
 
 
@@ -190,8 +190,8 @@ def mm_nt(A: torch.Tensor, B, out: Optional[torch.Tensor] = None, *, alpha: floa
     arrA = (_ct.c_void_p * 3)(*[t.data_ptr() for t in As])
     arrB = (_ct.c_void_p * 3)(*[t.data_ptr() for t in Bs])
     st = status_word(A.device)
-    tok = trace.begin_timing("gemm")
+    tok = trace.begin_timing("gemm_tc")
     call("mpq_gemm_tc", len(As), M, N, K, float(alpha), arrA, lda, arrB, ldb, float(beta), ptr(out), out.stride(0),
          ptr(st))
-    trace.end_timing("gemm", tok, 2.0 * M * N * K)
+    trace.end_timing("gemm_tc", tok, 2.0 * M * N * K)
     return out

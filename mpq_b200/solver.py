@@ -17,7 +17,7 @@ from typing import Any, Dict, Optional, Tuple
 
 import torch
 
-from . import ops
+from . import ops, trace
 from ._lib import call, ptr
 
 ALPHA_EPS = 1e-7
@@ -611,11 +611,16 @@ def solve_e8p12_rankspace_vamp(
     gamma1 = torch.empty(B, **f32)
     call("mpq_gamma_init", ptr(Wr), ptr(hat0), B, n, Wr.stride(0), float(cfg.gamma_start), ptr(gamma1))
 
+    # algorithmic bytes of one posterior launch: r1 and x1 (and the prior centre), gamma and the row sums
+    mmse_bytes = 4.0 * B * n * (3 if center is not None else 2) + 8.0 * B + (4.0 * B * nb if pscale is not None else 0.0)
+
     def mmse(r, g, x_out, vsum):
+        tok = trace.begin_timing("e8p12_mmse")
         call("mpq_e8p12_mmse", ptr(r), r.stride(0), ptr(center), center.stride(0) if center is not None else 0,
              ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(g), tau, B, nb, ptr(tab["base_abs"]),
              ptr(tab["base_sqnorm"]), ptr(tab["base_parity"]), ptr(tab["idx_lut"]), ptr(tab["grid"]), ptr(x_out),
              x_out.stride(0), None, 0, None, 0, None, 0, ptr(vsum))
+        trace.end_timing("e8p12_mmse", tok, mmse_bytes)
 
     def map_state(r, g):
         return e8p12_map_rows(r, cb, gamma=g, center=center, pscale=pscale, prior_tau=tau)
