@@ -149,6 +149,15 @@ int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float* const* 
                 int64_t ldb, float beta, float* C, int64_t ldc, int* status, void* stream);
 /* hi = TF32 round-to-nearest of x, lo = x - hi (the operand split of the 3xTF32 product). */
 int mpq_split_tf32(const float* x, int64_t ldx, float* hi, float* lo, int64_t ldo, int rows, int cols, void* stream);
+/* Allocation-free 3xTF32 product C = alpha A B^T + beta C (A: M x K, B: N x K, row-major fp32).  No counterpart in
+ * the reference: it serves callers that cannot allocate device memory where they need the product (memory-capped
+ * pools, FFI hosts holding only the buffers handed to them, paths where a cudaMalloc would synchronise).  The
+ * TF32 operand split and the status word live in a 16 MiB file-scope device array held by every GPU that loads
+ * the library until exit; 2 (M + N) round_up(K, 4) <= 4,194,240 floats, larger products return MPQ_ERR_ARG.
+ * Calls share the array: executions that overlap on the GPU race.  The first call on a device looks up the
+ * array's address; make it before any stream capture.  status: optional caller-owned device int (NULL: unreported). */
+int mpq_gemm_tf32x3_noalloc(int M, int N, int K, float alpha, const float* A, int64_t lda, const float* B, int64_t ldb,
+                            float beta, float* C, int64_t ldc, int* status, void* stream);
 
 /* ---- E8P12 (K3, K4, K6): mpq/priors/e8p12.py ----
  * Tables (from the codebook grid, as mpq/priors/e8p12.py:83-151 derives them): base_abs 256x8, base_sqnorm 256,

@@ -51,6 +51,7 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_gemm_f32": (I, I, I, I, F, P, L, P, L, F, P, L, P),
     "mpq_gemm_tc": (I, I, I, I, F, P, L, P, L, F, P, L, P, P),
     "mpq_split_tf32": (P, L, P, P, L, I, I, P),
+    "mpq_gemm_tf32x3_noalloc": (I, I, I, F, P, L, P, L, F, P, L, P, P),
     "mpq_cd_diag": (P, I, I, L, P, P, P),
     "mpq_cd_gain": (P, I, I, L, P, P, P),
     "mpq_argsort_desc": (P, I, P, P),

@@ -363,3 +363,115 @@ MPQ_API int mpq_split_tf32(const float* x, int64_t ldx, float* hi, float* lo, in
   k_split_tf32<<<(int)g, 256, 0, (cudaStream_t)stream>>>(x, ldx, hi, lo, ldo, rows, cols);
   return launch_status("mpq_split_tf32");
 }
+
+// ---------------------------------------------------------------------------------------------------------
+// Allocation-free 3xTF32 product.
+//
+// Some callers cannot allocate device memory at the point where they need this product: code that runs
+// while a caching allocator is forbidden from growing (inside a memory-capped pool or an allocator hook),
+// host runtimes that bind only a fixed set of device buffers handed to them (an FFI caller that receives
+// raw pointers and no allocator), and latency-critical paths where a cudaMalloc would synchronise the
+// device.  mpq_gemm_tc needs the hi/lo TF32 halves of both operands in caller-provided buffers; this
+// variant keeps them, and its pipeline status word, in one file-scope device array instead.
+//
+// The array (kNoAllocBytes = 16 MiB) exists on every GPU that loads the library, from module load until
+// process exit.  Its first 256 bytes hold the status word, the rest the four split operands, each
+// row-major with a leading dimension of round_up(K, 4) floats: 2 * (M + N) * round_up(K, 4) floats must
+// fit in (kNoAllocBytes - 256) / 4 = 4,194,240; larger products are rejected with MPQ_ERR_ARG.
+// Every call on a device shares the array and it keeps the previous call's contents: the status word is
+// cleared at the start of each call and the split operands are rewritten before they are read.  Calls
+// whose executions overlap on the GPU (different streams, or different host threads without ordering)
+// race on the array.
+// ---------------------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace mpq {
+namespace noalloc {
+
+constexpr size_t kNoAllocBytes = 16u << 20;
+constexpr size_t kStatusBytes = 256;
+constexpr int64_t kMaxOperandFloats = (int64_t)((kNoAllocBytes - kStatusBytes) / 4);
+constexpr int kMaxDevices = 64;
+
+// Device-side scratch.  In host code this name is only a handle for cudaGetSymbolAddress, never an address.
+static __device__ __align__(256) unsigned char g_scratch[kNoAllocBytes];
+
+static std::mutex g_mu;
+static unsigned char* g_base[kMaxDevices] = {};  // device address of g_scratch per device
+
+// Set-up, once per device, with that device current: look up the array's device address.
+static int scratch_base(unsigned char** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_error("mpq_gemm_tf32x3_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_last_error("mpq_gemm_tf32x3_noalloc: device %d out of range", dev);
+    return MPQ_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_base[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_scratch);
+    if (e != cudaSuccess || !p) {
+      set_last_error("mpq_gemm_tf32x3_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return e != cudaSuccess ? (int)e : MPQ_ERR_UNSUPPORTED;
+    }
+    g_base[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_base[dev];
+  return MPQ_OK;
+}
+
+}  // namespace noalloc
+}  // namespace mpq
+
+// C = alpha * A B^T + beta * C in 3xTF32 (A: M x K, B: N x K, row-major fp32), with no device allocation.
+// `status` (optional, device int owned by the caller) is cleared and receives a non-zero code if a pipeline
+// wait timed out; when it is NULL the status word inside the array is used and the code is not reported.
+// The first call on each device performs the set-up above; make it before any stream capture.
+MPQ_API int mpq_gemm_tf32x3_noalloc(int M, int N, int K, float alpha, const float* A, int64_t lda, const float* B,
+                                    int64_t ldb, float beta, float* C, int64_t ldc, int* status, void* stream) {
+  MPQ_CHECK_ARG(A && B && C, "mpq_gemm_tf32x3_noalloc: null pointer");
+  MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 1, "mpq_gemm_tf32x3_noalloc: bad shape");
+  MPQ_CHECK_ARG(lda >= K && ldb >= K && ldc >= N, "mpq_gemm_tf32x3_noalloc: leading dimensions too small");
+  const int64_t kp = ((int64_t)K + 3) / 4 * 4;
+  const int64_t need = 2 * ((int64_t)M + N) * kp;
+  MPQ_CHECK_ARG(need <= noalloc::kMaxOperandFloats,
+                "mpq_gemm_tf32x3_noalloc: 2*(M+N)*round_up(K,4) = %lld floats exceeds the %lld-float scratch",
+                (long long)need, (long long)noalloc::kMaxOperandFloats);
+  if (M == 0 || N == 0) return MPQ_OK;
+  unsigned char* base = nullptr;
+  int st = noalloc::scratch_base(&base);
+  if (st) return st;
+  st = tc::get_encoder();
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (!status) status = reinterpret_cast<int*>(base);
+  float* a_hi = reinterpret_cast<float*>(base + noalloc::kStatusBytes);
+  float* a_lo = a_hi + (int64_t)M * kp;
+  float* b_hi = a_lo + (int64_t)M * kp;
+  float* b_lo = b_hi + (int64_t)N * kp;
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), s);
+  if (e != cudaSuccess) {
+    set_last_error("mpq_gemm_tf32x3_noalloc: clearing the status word: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  st = mpq_split_tf32(A, lda, a_hi, a_lo, kp, M, K, stream);
+  if (st) return st;
+  st = mpq_split_tf32(B, ldb, b_hi, b_lo, kp, N, K, stream);
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  const float* As[3] = {a_hi, a_hi, a_lo};
+  const float* Bs[3] = {b_hi, b_lo, b_hi};
+  for (int r = 0; r < 3; ++r) {
+    st = tc::make_map(&maps.a[r], As[r], M, K, kp, tc::BM);
+    if (st) return st;
+    st = tc::make_map(&maps.b[r], Bs[r], N, K, kp, 256);
+    if (st) return st;
+  }
+  return tc::launch<256, 4>(maps, 3, M, N, K, alpha, beta, C, ldc, status, s);
+}
