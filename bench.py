@@ -170,13 +170,14 @@ class ScalarWorkload:
 class E8Workload:
     dominant = "e8p12_mmse"
 
-    def __init__(self, dev, block_rows, SU, SV):
+    def __init__(self, dev, block_rows, SU, SV, rows):
         from mpq_b200.codebook import E8P12_codebook
-        self.dev, self.block_rows = dev, block_rows
+        self.dev, self.block_rows, self.rows = dev, block_rows, rows
         self.cb = E8P12_codebook()
         self.SU, self.SV = SU.to(dev), SV.to(dev)
 
     def step(self, W, H):
+        """W: the whole layer (the two-sided rotation and the RMS scale are layer-wide); solves self.rows."""
         import torch
         from mpq_b200 import ops
         from mpq_b200._lib import call, ptr
@@ -188,7 +189,9 @@ class E8Workload:
         sq = torch.empty(m, device=W.device)
         call("mpq_row_dot", ptr(Wr), Wr.stride(0), ptr(Wr), Wr.stride(0), m, n, ptr(sq))
         wscale = float(ops.mean_rows(sq).item() / n) ** 0.5
-        Wn = Wr / wscale
+        r0, r1 = self.rows
+        Wn = Wr[r0:r1] / wscale
+        m = r1 - r0
         args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=16, mpq_prior_tau=0.25, mpq_polish_sweeps=3,
                                      mpq_block_rows=self.block_rows, quant_solver="vamp",
                                      quant_polish_mode="block_cd", mpq_polish_metric="gram")
@@ -213,22 +216,23 @@ def run_mpq(args):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from mpq_b200.shard import broadcast_, row_shards
     Wc, Xc, SU, SV = synth_cpu()
     W = Wc.to(dev) if rank == 0 else torch.empty(M_ROWS, N_COLS, device=dev)
     H = hessian_device(Xc.to(dev)) if rank == 0 else torch.empty(N_COLS, N_COLS, device=dev)
     del Xc
-    if world > 1:  # W and H over NVLink
-        dist.broadcast(W, 0)
-        dist.broadcast(H, 0)
-    rows_per = M_ROWS // world
+    broadcast_([W, H], src=0)  # W and H over NVLink (NCCL) to every rank
+    r0, r1 = row_shards(M_ROWS, world, 128)[rank]
     if args.rows > 0:
-        rows_per = min(rows_per, args.rows)
-    Wr = W[rank * rows_per:(rank + 1) * rows_per].contiguous()
+        r1 = min(r1, r0 + args.rows)
+    rows_per = r1 - r0
     block_rows = min(args.block_rows, rows_per)
     if args.workload == "e8p12":
-        wl = E8Workload(dev, block_rows, SU[rank * rows_per:(rank + 1) * rows_per], SV)
+        wl = E8Workload(dev, block_rows, SU, SV, (r0, r1))
+        Wr = W  # the rotation and scale are layer-wide; the workload solves rows r0:r1
     else:
         wl = ScalarWorkload(dev, block_rows)
+        Wr = W[r0:r1].contiguous()
     flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > 126 MB L2
 
     for _ in range(max(args.warmup, 0)):
