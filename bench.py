@@ -82,14 +82,34 @@ def synth_cpu():
 
 
 def hessian_device(X):
-    """H = X^T X / T + 0.01 mean(diag) I on the GPU (tensor-core product)."""
+    """H = X^T X / T + 0.01 mean(diag) I on the GPU (tensor-core symmetric product, mpq_syrk_tc)."""
     import torch
-    from mpq_b200 import ops
-    XT = X.t().contiguous()
-    H = ops.mm_nt(XT, ops.Operand(XT))
-    H.div_(float(X.shape[0]))
-    H.add_(torch.eye(H.shape[0], device=H.device) * (0.01 * float(H.diagonal().mean())))
+    from mpq_b200.hessian import accumulate_xtx
+    n = X.shape[1]
+    H = torch.empty(n, n, device=X.device)
+    accumulate_xtx(H, X, alpha=1.0 / X.shape[0], beta=0.0)
+    H.add_(torch.eye(n, device=H.device) * (0.01 * float(H.diagonal().mean())))
     return H
+
+
+def time_hessian(X, reps=3):
+    """Device time of the X^T X accumulation (T x n fp32 calibration activations, 3xTF32 SYRK)."""
+    import torch
+    from mpq_b200.hessian import accumulate_xtx
+    T, n = X.shape
+    H = torch.zeros(n, n, device=X.device)
+    accumulate_xtx(H, X, alpha=1.0 / T, beta=0.0)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        accumulate_xtx(H, X, alpha=1.0 / T, beta=0.0)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / reps
+    flops = float(T) * n * (n + 1)  # algorithmic SYRK count
+    return {"tokens": T, "n": n, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+            "what": "H = X^T X / T (split + 3xTF32 lower-triangle tcgen05 product), not part of the step time"}
 
 
 # ----------------------------------------------------------------------------------------------
@@ -219,7 +239,14 @@ def run_mpq(args):
     from mpq_b200.shard import broadcast_, row_shards
     Wc, Xc, SU, SV = synth_cpu()
     W = Wc.to(dev) if rank == 0 else torch.empty(M_ROWS, N_COLS, device=dev)
-    H = hessian_device(Xc.to(dev)) if rank == 0 else torch.empty(N_COLS, N_COLS, device=dev)
+    hess = None
+    if rank == 0:
+        Xd = Xc.to(dev)
+        H = hessian_device(Xd)
+        hess = time_hessian(Xd)
+        del Xd
+    else:
+        H = torch.empty(N_COLS, N_COLS, device=dev)
     del Xc
     broadcast_([W, H], src=0)  # W and H over NVLink (NCCL) to every rank
     r0, r1 = row_shards(M_ROWS, world, 128)[rank]
@@ -311,6 +338,7 @@ def run_mpq(args):
             "gpu_launches": int(round(launches)),
             "roofline": roofline,
             "clocks": clk,
+            "hessian": hess,
             "stats": stats,
         }
         if not args.no_cpu_baseline and world == 1:

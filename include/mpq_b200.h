@@ -149,6 +149,22 @@ int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float* const* 
                 int64_t ldb, float beta, float* C, int64_t ldc, int* status, void* stream);
 /* hi = TF32 round-to-nearest of x, lo = x - hi (the operand split of the 3xTF32 product). */
 int mpq_split_tf32(const float* x, int64_t ldx, float* hi, float* lo, int64_t ldo, int rows, int cols, void* stream);
+/* ---- calibration Hessian (K11) ----
+ * Symmetric product C = alpha sum_{r < nreg} A[r] B[r]^T + beta C (n x n) where A[r], B[r] (n x K row-major, lda) are
+ * halves of one matrix (3xTF32: (hi,hi),(hi,lo),(lo,hi)); only tiles with entries col <= row are computed and each
+ * entry is also stored at its mirror, so C is exactly symmetric; beta reads the lower triangle.  With the
+ * operand X^T this is the H += X^T X accumulation of the Hessian hooks the MPQ drivers consume (GPTQModel
+ * GPTQ.add_batch and QUIP# utils.register_H_hook, un-vendored; finalised at mpq/quip_generic.py:906-918). */
+int mpq_syrk_tc(int nreg, int n, int K, float alpha, const float* const* A, const float* const* B, int64_t lda,
+                float beta, float* C, int64_t ldc, int* status, void* stream);
+/* Transposing split of token-major activations X (T x n; dtype 0 = f32, 1 = bf16): hi[j,t] = tf32(X[t,j]),
+ * lo[j,t] = X[t,j] - hi[j,t] (lo may be NULL: bf16 values are exact in TF32). */
+int mpq_split_tf32_t(const void* x, int dtype, int64_t ldx, int tokens, int n, float* hi, float* lo, int64_t ldo,
+                     void* stream);
+/* out[j] = beta out[j] + alpha sum_t X[t,j] (the QUIP# hook's running sum of inputs, mpq/quip_generic.py:906-918). */
+int mpq_col_sum(const void* x, int dtype, int64_t ldx, int tokens, int n, float alpha, float beta, float* out,
+                void* stream);
+
 /* Allocation-free 3xTF32 product C = alpha A B^T + beta C (A: M x K, B: N x K, row-major fp32).  No counterpart in
  * the reference: it serves callers that cannot allocate device memory where they need the product (memory-capped
  * pools, FFI hosts holding only the buffers handed to them, paths where a cudaMalloc would synchronise).  The

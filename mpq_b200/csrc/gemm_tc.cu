@@ -94,7 +94,7 @@ struct Maps {
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ Maps maps, int nreg, int M, int N, int K, float alpha, float beta,
-              float* __restrict__ C, int64_t ldc, int* __restrict__ status) {
+              float* __restrict__ C, int64_t ldc, int* __restrict__ status, int sym) {
   constexpr uint32_t kStageA = BM * BK * 4;
   constexpr uint32_t kStageB = BN * BK * 4;
   constexpr uint32_t kIdesc = idesc_tf32(BM, BN);
@@ -112,6 +112,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  // symmetric product (A_r and B_r are the same operand): only tiles holding entries col <= row run
+  if (sym && n0 > m0 + BM - 1) return;
   const int kb_per_reg = (K + BK - 1) / BK;
   const int total_kb = kb_per_reg * nreg;
 
@@ -218,7 +220,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (row < M) {
+        if (sym) {
+          // lower entries (col <= row) and their mirrors: the result is exactly symmetric; the mirror
+          // stores of a warp (32 consecutive rows, one column) are contiguous
+          if (row < M) {
+            #pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              const int col = n0 + c0 + t;
+              if (col < N && col <= row) {
+                float o = alpha * __uint_as_float(v[t]);
+                if (beta != 0.f) o += beta * C[(int64_t)row * ldc + col];
+                C[(int64_t)row * ldc + col] = o;
+                if (col != row) C[(int64_t)col * ldc + row] = o;
+              }
+            }
+          }
+        } else if (row < M) {
           float* crow = C + (int64_t)row * ldc + n0 + c0;
           const int ncol = min(32, N - (n0 + c0));
           if (ncol == 32 && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
@@ -292,7 +309,7 @@ static int make_map(CUtensorMap* m, const float* p, int rows, int K, int64_t ld,
 
 template <int BN, int STAGES>
 static int launch(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
-                  int* status, cudaStream_t stream) {
+                  int* status, cudaStream_t stream, int sym = 0) {
   const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * BK * 4 + 256;
   static bool attr = false;
   if (!attr) {
@@ -300,7 +317,7 @@ static int launch(const Maps& maps, int nreg, int M, int N, int K, float alpha, 
     attr = true;
   }
   dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  k_gemm_tc<BN, STAGES><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status);
+  k_gemm_tc<BN, STAGES><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status, sym);
   return launch_status("mpq_gemm_tc");
 }
 
@@ -334,6 +351,32 @@ MPQ_API int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float*
   }
   MPQ_CHECK_ARG(status, "mpq_gemm_tc: status word required");
   return tc::launch<256, 4>(maps, nreg, M, N, K, alpha, beta, C, ldc, status, (cudaStream_t)stream);
+}
+
+// Symmetric product C = alpha * sum_{r < nreg} A_r B_r^T + beta * C for B_r holding the same matrix as A_r
+// (B_r = A_r, or the other half of the same 3xTF32 split), n x n result: only the tiles holding entries
+// col <= row are computed and every computed entry is also stored at its mirror position, so C is exactly
+// symmetric.  beta reads only the lower triangle of C (C must be symmetric on entry when beta != 0).
+MPQ_API int mpq_syrk_tc(int nreg, int n, int K, float alpha, const float* const* A, const float* const* B, int64_t lda,
+                        float beta, float* C, int64_t ldc, int* status, void* stream) {
+  MPQ_CHECK_ARG(nreg >= 1 && nreg <= 3, "mpq_syrk_tc: nreg must be 1..3");
+  MPQ_CHECK_ARG(A && B && C && status, "mpq_syrk_tc: null pointer");
+  MPQ_CHECK_ARG(n >= 0 && K >= 1, "mpq_syrk_tc: bad shape");
+  MPQ_CHECK_ARG(lda % 4 == 0 && lda >= K && ldc >= n, "mpq_syrk_tc: lda must be a multiple of 4 and >= K, ldc >= n");
+  if (n == 0) return MPQ_OK;
+  int st = tc::get_encoder();
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  for (int r = 0; r < nreg; ++r) {
+    MPQ_CHECK_ARG(A[r] && B[r], "mpq_syrk_tc: null operand %d", r);
+    MPQ_CHECK_ARG(((uintptr_t)A[r] & 15) == 0 && ((uintptr_t)B[r] & 15) == 0, "mpq_syrk_tc: operands must be 16-byte aligned");
+    st = tc::make_map(&maps.a[r], A[r], n, K, lda, tc::BM);
+    if (st) return st;
+    st = tc::make_map(&maps.b[r], B[r], n, K, lda, 256);
+    if (st) return st;
+  }
+  return tc::launch<256, 4>(maps, nreg, n, n, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 1);
 }
 
 // hi = tf32 round-to-nearest of x (low 13 mantissa bits cleared), lo = x - hi (exact in fp32).
