@@ -179,7 +179,7 @@ class ScalarWorkload:
         qcfg = types.SimpleNamespace(bits=4, group_size=128, desc_act=False,
                                      mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
         out = run_mpq_quantization(W=W, H=2.0 * H, quantizer=None, qcfg=qcfg, module_name="bench.layer",
-                                   vamp_cfg=UniformVampConfig(iters=20, prior_tau=0.2, damping=0.5, polish_sweeps=3),
+                                   vamp_cfg=UniformVampConfig(iters=20, prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto"),
                                    adapter_cfg=GPTQAdapterConfig(block_rows=self.block_rows, grow_block_rows=False))
         Q, q_int, scale, zero, g_idx, _, st = out
         return [q_int, scale, zero], {"raw_objective_mean": st["raw_objective_mean_final"],

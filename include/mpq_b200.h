@@ -217,6 +217,16 @@ int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const f
 int mpq_gram_search(const float* targets, int N, const float* L, float lam_lo, float lam_hi, const float* base_abs,
                     const int* base_parity, const float* grid, const uint8_t* sign_id, int* out_idx, void* stream);
 
+/* ---- generic rank-space block CD steps (any candidate provider): mpq/polish/block_cd.py:520-547 ----
+ * target = x_blk + rhs Ginv (bs x bs) or x_blk + rhs * diag_inv (bs <= 8).  Replaces :521-526. */
+int mpq_cd_target(const float* x, int64_t ldx, const float* rhs, int64_t ldr, int B, int bs, const float* ginv,
+                  const float* diag_inv, float* target, int64_t ldt, void* stream);
+/* Accept test of a proposal per row, x / residual norm / index updates, masked delta for the residual update and
+ * the accepted count.  Replaces _cd_accept_step_impl (mpq/polish/block_cd.py:28-48) and :538-547. */
+int mpq_cd_accept(float* x, int64_t ldx, const float* cand, int64_t ldc, const float* rhs, int64_t ldr,
+                  const float* gram, float* res_norm, int B, int bs, float accept_tol, float* delta, int64_t ldd,
+                  const int* cand_idx, int* idx, int64_t ldi, int* accepted, void* stream);
+
 /* ---- rotation ----
  * Block Walsh-Hadamard of the last dim, blocks of `had` (power of two <= 16384), normalized by sqrt(had);
  * mode 0: y = H(x * signs) (right rotation), mode 1: y = H(x) * signs (inverse).  signs may be NULL.

@@ -55,6 +55,8 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_syrk_tc": (I, I, I, F, P, P, L, F, P, L, P, P),
     "mpq_split_tf32_t": (P, I, L, I, I, P, P, L, P),
     "mpq_col_sum": (P, I, L, I, I, F, F, P, P),
+    "mpq_cd_target": (P, L, P, L, I, I, P, P, P, L, P),
+    "mpq_cd_accept": (P, L, P, L, P, L, P, P, I, I, F, P, L, P, P, L, P, P),
     "mpq_cd_diag": (P, I, I, L, P, P, P),
     "mpq_cd_gain": (P, I, I, L, P, P, P),
     "mpq_argsort_desc": (P, I, P, P),

@@ -95,6 +95,43 @@ struct ItemTab {
 __device__ __forceinline__ float canon_sign(float x) { return x < 0.f ? x : fabsf(x); }
 __device__ __forceinline__ unsigned sign_bit(float x) { return __float_as_uint(x) >> 31; }
 
+// One component's log-weight from the item table: lc = const + logC + log(1 +- prod) - ln 2 (the reference's
+// clamped-tanh formula), with the per-coordinate t and |b| and the products the sign means need.
+struct CompTerms {
+  float lc, prod, t[8], mag[8];
+  bool even;
+};
+
+__device__ __forceinline__ void comp_terms(const ItemTab& T, int br, int ai, uint2 of, float ng, float ynorm_br,
+                                           float sqn, int parity, CompTerms& o) {
+  const char* base = reinterpret_cast<const char*>(T.pt[br]);
+  float logC = 0.f, lpt = 0.f;
+  unsigned sx = 0;
+  #pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
+    const float4 v = *reinterpret_cast<const float4*>(base + 2u * byte);
+    logC = fadd(logC, v.x);
+    o.t[kk] = v.y;
+    sx ^= __float_as_uint(v.y);
+    lpt = fadd(lpt, v.z);
+    o.mag[kk] = v.w;
+  }
+  const bool negp = (sx >> 31) != 0u;
+  const float cst = fmul(ng, fadd(ynorm_br, sqn));
+  // float32 library functions: the only ill-conditioned term, 1 - |prod| for |prod| near 1, belongs to
+  // parity-mismatched components whose log-partition lies ~14 nats below their bound (the reference's tanh
+  // clamp), so its rounding moves the posterior by ~1e-7 relative.
+  const float pabs = expf(lpt);
+  o.prod = negp ? -pabs : pabs;
+  const float lae = log1pf(pabs);  // logaddexp(0, lpt), lpt <= 0
+  const float l1me = lpt < -kLn2 ? log1pf(-pabs) : logf(-expm1f(lpt));  // log(1 - exp(lpt))
+  const float lop = negp ? l1me : lae;  // log(1 + prod)
+  const float lom = negp ? lae : l1me;  // log(1 - prod)
+  o.even = parity == 0;
+  o.lc = fadd(cst, fsub(fadd(logC, o.even ? lop : lom), kLn2));
+}
+
 template <bool MMSE>
 __global__ void __launch_bounds__(kWarps * 32, 3)
 k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __restrict__ var_out, int64_t ld_v,
@@ -170,9 +207,10 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
       const float aa = fabsf(av);
       float Tv = 0.f;
       if constexpr (MMSE) {
-        // Transcendentals are evaluated in double and rounded once (correctly rounded float32 results):
-        // the reference's clamped-tanh algebra amplifies last-bit differences of tanh near +-1.
-        Tv = aa + (float)log1p((double)(float)exp(-2.0 * (double)aa));
+        // tanh and its log are evaluated in double and rounded once (correctly rounded float32 results): the
+        // reference's clamped-tanh algebra amplifies last-bit differences of tanh near +-1.  The logaddexp
+        // term is well conditioned.
+        Tv = aa + log1pf(expf(-2.f * aa));
         const float ti =
             fminf(fmaxf((float)tanh((double)av), -0.99999988079071044921875f), 0.99999988079071044921875f);
         T.pt[br][r] = make_float4(Tv, canon_sign(ti), (float)log((double)fmaxf(fabsf(ti), 1e-7f)), mag);
@@ -180,70 +218,109 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
       T.am[br][r] = make_float2(canon_sign(av), Tv);
     }
     __syncwarp();
-    // ---- pass 1: exact MAP (lane's components c = 32 j + lane = (branch c >> 8, abs c & 255)) ----
-    float best = -INFINITY;
-    int best_c = -1;
-    #pragma unroll 1
-    for (int j = 0; j < 16; ++j) {
-      const int br = j >> 3;
-      const int ai = ((j & 7) << 5) | lane;
-      const uint2 of = s_off[ai];
-      const char* base = reinterpret_cast<const char*>(T.am[br]);
-      float sum_abs = 0.f, mn = INFINITY, lcs = 0.f;
-      unsigned sx = 0;
-      #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
-        const float2 v = *reinterpret_cast<const float2*>(base + byte);
-        const float aa = fabsf(v.x);
-        sum_abs = fadd(sum_abs, aa);
-        sx ^= __float_as_uint(v.x);
-        mn = fminf(mn, aa);
-        if constexpr (MMSE) lcs = fadd(lcs, v.y);
+    // Lane's components c = 32 j + lane = (branch c >> 8, abs c & 255), the reference's component order.
+    // The exact MAP scan runs when MAP outputs are requested, for MAP-only calls and for items that snap to
+    // the MAP codeword (g >= 1e3); otherwise only the bounds const + logC are needed, and the pruning
+    // reference is the largest exact log-weight among the lanes' best-bound components.
+    const bool need_map = !MMSE || idx_out != nullptr || map_out != nullptr || g >= 1e3f;
+    float best = -INFINITY;  // lower bound on the largest component log-weight
+    const float* mv = nullptr;
+    if (need_map) {
+      // ---- pass 1: exact MAP ----
+      int best_c = -1;
+      #pragma unroll 1
+      for (int j = 0; j < 16; ++j) {
+        const int br = j >> 3;
+        const int ai = ((j & 7) << 5) | lane;
+        const uint2 of = s_off[ai];
+        const char* base = reinterpret_cast<const char*>(T.am[br]);
+        float sum_abs = 0.f, mn = INFINITY, lcs = 0.f;
+        unsigned sx = 0;
+        #pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
+          const float2 v = *reinterpret_cast<const float2*>(base + byte);
+          const float aa = fabsf(v.x);
+          sum_abs = fadd(sum_abs, aa);
+          sx ^= __float_as_uint(v.x);
+          mn = fminf(mn, aa);
+          if constexpr (MMSE) lcs = fadd(lcs, v.y);
+        }
+        const bool mismatch = (int)(sx >> 31) != s_par[ai];
+        const float lin = mismatch ? fsub(sum_abs, fmul(2.f, mn)) : sum_abs;
+        const float cst = fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai]));
+        const float sc = fadd(cst, lin);
+        if (sc > best) { best = sc; best_c = j * 32 + lane; }
+        if constexpr (MMSE) s_ub[warp][j * 32 + lane] = fadd(cst, lcs);
       }
-      const bool mismatch = (int)(sx >> 31) != s_par[ai];
-      const float lin = mismatch ? fsub(sum_abs, fmul(2.f, mn)) : sum_abs;
-      const float cst = fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai]));
-      const float sc = fadd(cst, lin);
-      if (sc > best) { best = sc; best_c = j * 32 + lane; }
-      if constexpr (MMSE) s_ub[warp][j * 32 + lane] = fadd(cst, lcs);
-    }
-    // first maximum over the warp: valid before invalid, higher score, then smaller component
-    #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oc = __shfl_xor_sync(0xffffffffu, best_c, o);
-      const bool take = oc >= 0 && (best_c < 0 || ob > best || (ob == best && oc < best_c));
-      if (take) { best = ob; best_c = oc; }
-    }
-    int comp = 0, sid = 0;
-    if (best_c >= 0) {  // the winner's parity-fixed sign pattern (first minimum of |a| flips)
-      comp = best_c;
-      const int br = comp >> 8, ai = comp & 255;
-      const uint2 of = s_off[ai];
-      const char* base = reinterpret_cast<const char*>(T.am[br]);
-      float mn = INFINITY;
-      int neg = 0, par = 0, minpos = 0;
+      // first maximum over the warp: valid before invalid, higher score, then smaller component
       #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
-        const float av = reinterpret_cast<const float2*>(base + byte)->x;
-        const float aa = fabsf(av);
-        if (av < 0.f) { neg |= 1 << kk; par ^= 1; }
-        if (aa < mn) { mn = aa; minpos = kk; }
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oc = __shfl_xor_sync(0xffffffffu, best_c, o);
+        const bool take = oc >= 0 && (best_c < 0 || ob > best || (ob == best && oc < best_c));
+        if (take) { best = ob; best_c = oc; }
       }
-      sid = par != s_par[ai] ? (neg ^ (1 << minpos)) : neg;
+      int comp = 0, sid = 0;
+      if (best_c >= 0) {  // the winner's parity-fixed sign pattern (first minimum of |a| flips)
+        comp = best_c;
+        const int br = comp >> 8, ai = comp & 255;
+        const uint2 of = s_off[ai];
+        const char* base = reinterpret_cast<const char*>(T.am[br]);
+        float mn = INFINITY;
+        int neg = 0, par = 0, minpos = 0;
+        #pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
+          const float av = reinterpret_cast<const float2*>(base + byte)->x;
+          const float aa = fabsf(av);
+          if (av < 0.f) { neg |= 1 << kk; par ^= 1; }
+          if (aa < mn) { mn = aa; minpos = kk; }
+        }
+        sid = par != s_par[ai] ? (neg ^ (1 << minpos)) : neg;
+      }
+      const int map_idx = tab.idx_lut[(comp >> 8) * 65536 + (comp & 255) * 256 + sid];
+      if (lane == 0 && idx_out) idx_out[b * ld_i + k] = map_idx;
+      mv = tab.grid + (int64_t)map_idx * 8;
+      if (map_out && lane < 8) map_out[b * ld_m + k * 8 + lane] = mv[lane];
+    } else if constexpr (MMSE) {
+      // ---- pass 1: bounds only ----
+      float bub = -INFINITY;
+      int bc = -1;
+      #pragma unroll 1
+      for (int j = 0; j < 16; ++j) {
+        const int br = j >> 3;
+        const int ai = ((j & 7) << 5) | lane;
+        const uint2 of = s_off[ai];
+        const char* base = reinterpret_cast<const char*>(T.am[br]);
+        float lcs = 0.f;
+        #pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
+          lcs = fadd(lcs, reinterpret_cast<const float2*>(base + byte)->y);
+        }
+        const float ub = fadd(fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai])), lcs);
+        s_ub[warp][j * 32 + lane] = ub;
+        if (ub > bub) { bub = ub; bc = j * 32 + lane; }
+      }
+      // exact log-weight of each lane's best-bound component; the warp maximum is the pruning reference
+      float lcb = -INFINITY;
+      if (bc >= 0) {
+        CompTerms ct;
+        const int br = bc >> 8, ai = bc & 255;
+        comp_terms(T, br, ai, s_off[ai], ng, br ? ynorm[1] : ynorm[0], s_sqn[ai], s_par[ai], ct);
+        if (ct.lc == ct.lc) lcb = ct.lc;
+      }
+      #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lcb = fmaxf(lcb, __shfl_xor_sync(0xffffffffu, lcb, o));
+      best = lcb;
     }
-    const int map_idx = tab.idx_lut[(comp >> 8) * 65536 + (comp & 255) * 256 + sid];
-    if (lane == 0 && idx_out) idx_out[b * ld_i + k] = map_idx;
-    const float* mv = tab.grid + (int64_t)map_idx * 8;
-    if (map_out && lane < 8) map_out[b * ld_m + k * 8 + lane] = mv[lane];
     if constexpr (MMSE) {
       float mu_l = 0.f, var = 0.f;  // lane l < 8 ends with coordinate l of the posterior mean
       if (g >= 1e3f) {  // high-precision snap to the MAP codeword (mpq/priors/e8p12.py:923-926)
         mu_l = lane < 8 ? mv[lane] : 0.f;
       } else {
-        // ---- pass 2: compact the surviving components ----
+        // ---- pass 2: compact the surviving components (bound within kPrune of the reference) ----
         const float thr = best - kPrune;
         unsigned short* list = s_list[warp];
         int cnt = 0;
@@ -255,44 +332,24 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
           cnt += __popc(msk);
         }
         __syncwarp();
-        float W = 0.f, SEC = 0.f, MU[8];
-        float mx = best;  // running maximum of the component log-weights (starts at the MAP score)
+        float W = 0.f, WOFF = 0.f, SEC = 0.f, MU[8];
+        float mx = best;  // running maximum of the component log-weights (starts at the pruning reference)
         #pragma unroll
         for (int i = 0; i < 8; ++i) MU[i] = 0.f;
         for (int li = lane; li < cnt; li += 32) {
           const int c = list[li];
           const int br = c >> 8, ai = c & 255;
           const float off = br ? -0.25f : 0.25f;
-          const uint2 of = s_off[ai];
-          const char* base = reinterpret_cast<const char*>(T.pt[br]);
-          float logC = 0.f, lpt = 0.f, t[8], mag[8];
-          unsigned sx = 0;
-          #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
-            const float4 v = *reinterpret_cast<const float4*>(base + 2u * byte);
-            logC = fadd(logC, v.x);
-            t[kk] = v.y;
-            sx ^= __float_as_uint(v.y);
-            lpt = fadd(lpt, v.z);
-            mag[kk] = v.w;
-          }
-          const bool negp = (sx >> 31) != 0u;
-          const float cst = fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai]));
-          // prod = +-exp(lpt) feeds the reference's 1 -+ prod, which cancels for prod near 1: evaluated in
-          // double and rounded once.  The other per-component functions are well conditioned (float32).
-          const float pabs = (float)exp((double)lpt);
-          const float prod = negp ? -pabs : pabs;
-          const float lae = log1pf(pabs);  // logaddexp(0, lpt), lpt <= 0
-          const float l1me = lpt < -kLn2 ? log1pf(-pabs) : logf(-expm1f(lpt));  // log(1 - exp(lpt))
-          const float lop = negp ? l1me : lae;  // log(1 + prod)
-          const float lom = negp ? lae : l1me;  // log(1 - prod)
-          const bool even = s_par[ai] == 0;
-          const float logZ = fsub(fadd(logC, even ? lop : lom), kLn2);
-          const float lc = fadd(cst, logZ);
+          CompTerms ct;
+          comp_terms(T, br, ai, s_off[ai], ng, br ? ynorm[1] : ynorm[0], s_sqn[ai], s_par[ai], ct);
+          const float lc = ct.lc, prod = ct.prod;
+          const bool even = ct.even;
+          const float* t = ct.t;
+          const float* mag = ct.mag;
           if (lc > mx) {  // rescale the accumulators to the new maximum
             const float sc = expf(mx - lc);
             W *= sc;
+            WOFF *= sc;
             SEC *= sc;
             #pragma unroll
             for (int i = 0; i < 8; ++i) MU[i] *= sc;
@@ -319,8 +376,9 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
             suf = fmul(suf, t[i]);
           }
           W += w;
+          WOFF += w * off;  // the branch offset's share of every coordinate's mean
           #pragma unroll
-          for (int i = 0; i < 8; ++i) MU[i] += w * (mc[i] + off);
+          for (int i = 0; i < 8; ++i) MU[i] += w * mc[i];
           SEC += w * (s_sqn[ai] + 8.f * off * off + 2.f * off * mcs);
         }
         // merge the lanes' online softmax states (fixed butterfly order)
@@ -329,11 +387,12 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
         for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         const float scl = (mx == M) ? 1.f : expf(mx - M);
         W = warp_sum(W * scl);
+        WOFF = warp_sum(WOFF * scl);
         SEC = warp_sum(SEC * scl);
         float nrm = 0.f;
         #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float mi = warp_sum(MU[i] * scl) / W;
+          const float mi = (warp_sum(MU[i] * scl) + WOFF) / W;
           nrm += mi * mi;
           mu_l = (lane == i) ? mi : mu_l;
         }

@@ -130,9 +130,10 @@ def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, blocks_per_chunk: 
 @torch.inference_mode()
 def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, sweeps: int,
                   idxs_init: torch.Tensor, accept_tol: float = 0.0, opVs: Optional[ops.Operand] = None,
-                  opVsT: Optional[ops.Operand] = None) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
+                  opVsT: Optional[ops.Operand] = None, on_sweep=None) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
     """Gram-metric greedy block CD over E8P12 8-blocks (mpq/polish/block_cd.py:332-625, E8P12Provider, metric
-    'gram').  Returns (x, idxs int64 (B, nb), stats)."""
+    'gram').  Returns (x, idxs int64 (B, nb), stats).  on_sweep(sweep, x, idx, res_norm, accepted_total) is
+    called before the first sweep (sweep 0) and after each sweep."""
     dev = x.device
     B, n = x.shape
     nb = n // 8
@@ -160,7 +161,9 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
     accepted = torch.zeros(1, device=dev, dtype=torch.int32)
     evals = torch.zeros(1, device=dev, dtype=torch.int64)
     trace = [float(res_norm.double().mean().item())]
-    for _ in range(max(int(sweeps), 0)):
+    if on_sweep is not None:
+        on_sweep(0, x_work, idx, res_norm, 0)
+    for sweep in range(1, max(int(sweeps), 0) + 1):
         rhs_all = ops.mm_nt(res_u, opVs)
         call("mpq_gram_gain", ptr(rhs_all), rhs_all.stride(0), B, nb, ptr(meta), ptr(gain))
         del rhs_all
@@ -176,6 +179,8 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
                  ptr(res_norm), ptr(idx), idx.stride(0), ptr(delta), ptr(accepted), ptr(evals), B, float(accept_tol))
             ops.mm_nt(delta[:, :kc], VsJT[:, :kc], out=res_u, alpha=-1.0, beta=1.0)
         trace.append(float(res_norm.double().mean().item()))
+        if on_sweep is not None:
+            on_sweep(sweep, x_work, idx, res_norm, int(accepted.item()))
     if int(fails.item()):
         raise RuntimeError("stabilize_cholesky failed for an E8P12 block gram")
     nonincreasing = all(b <= a + max(1e-8, abs(a) * 1e-7) for a, b in zip(trace, trace[1:]))

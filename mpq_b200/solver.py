@@ -87,6 +87,40 @@ def _resolve_polish_mode(*, sweeps: int, mode: str) -> str:
     raise ValueError(f"unsupported polish_mode={mode!r}; expected none|block_cd|topk_block_cd.")
 
 
+def _resolve_block_cd_backend(*, block_cd_backend: Optional[str], compile_block_cd: bool) -> str:
+    """mpq/solver.py:189-197: "triton"/"auto" select the raw-Hessian greedy scalar CD (here a CUDA kernel),
+    "eager"/"compile" the generic rank-space block CD engine with the scalar provider."""
+    backend = str(block_cd_backend or "").strip().lower()
+    if not backend:
+        return "compile" if bool(compile_block_cd) else "eager"
+    if backend not in {"eager", "compile", "triton", "auto"}:
+        raise ValueError(f"unsupported block_cd_backend={block_cd_backend!r}; expected eager|compile|triton|auto.")
+    return backend
+
+
+def _expand_groups(p: torch.Tensor, n: int) -> torch.Tensor:
+    """(B, n/group) -> (B, n) group-expanded; (B, n) unchanged."""
+    if p.shape[1] == n:
+        return p.contiguous()
+    return p.repeat_interleave(n // p.shape[1], dim=1).contiguous()
+
+
+def _generic_uniform_polish(*, x_init, Y_u, Vs, scale, zero, maxq, sweeps, order_mode, backend, raw_target, raw_gram,
+                            q_init):
+    """The generic engine with the scalar provider (mpq/solver.py:337-366)."""
+    from .block_cd import BlockCDConfig, UniformScalarProvider, block_coordinate_descent_rankspace
+    n = x_init.shape[1]
+    sf, zf = _expand_groups(scale, n), _expand_groups(zero, n)
+    x_pol, q_cd, st = block_coordinate_descent_rankspace(
+        x=x_init, Y_u=Y_u, Vs=Vs, block_size=1, provider=UniformScalarProvider(scale=sf, zero=zf, maxq=int(maxq)),
+        cfg=BlockCDConfig(sweeps=int(sweeps), metric="diag", accept_tol=0.0, order_mode=str(order_mode or "greedy_gain"),
+                          compile_steps=backend in {"compile", "auto"}),
+        idxs_init=q_init, raw_target=raw_target, raw_gram=raw_gram)
+    st = dict(st)
+    st["block_cd_backend"] = "cuda_generic"
+    return x_pol, q_cd, st
+
+
 def _log_damp_scalar(prev: float, new: float, damping: float) -> float:
     """mpq/utils.py:36-45."""
     if damping >= 1.0:
@@ -201,7 +235,8 @@ def polish_uniform_rankspace(
     raw_target: Optional[torch.Tensor] = None,
     raw_gram: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Dict[str, Any]]:
-    """mpq/solver.py:260-366 on CUDA: the raw-Hessian greedy scalar CD, then re-rounding."""
+    """mpq/solver.py:260-366 on CUDA: backends "triton"/"auto" (greedy order, raw Hessian given) run the raw-Hessian
+    greedy scalar CD kernel; the others run the generic block CD engine with the scalar provider."""
     mode = _resolve_polish_mode(sweeps=int(sweeps), mode=str(polish_mode))
     dev = x_init.device
     x_work = _f32c(x_init, dev)
@@ -228,8 +263,19 @@ def polish_uniform_rankspace(
         return finish(x_work, {"accepted_updates": 0.0})
     if mode == "topk_block_cd":
         raise NotImplementedError("topk_block_cd uniform polish is not built yet")
-    if gram_full is None:
-        raise NotImplementedError("the uniform polish needs gram_full (the raw Hessian)")
+    backend = _resolve_block_cd_backend(block_cd_backend=block_cd_backend, compile_block_cd=bool(compile_block_cd))
+    use_raw = (str(order_mode or "greedy_gain").strip().lower() == "greedy_gain" and backend in {"triton", "auto"}
+               and gram_full is not None)
+    if not use_raw:
+        q0 = torch.empty(B, n, device=dev, dtype=torch.uint8)
+        x0 = torch.empty(B, n, device=dev, dtype=torch.float32)
+        call("mpq_uniform_nearest", ptr(x_work), x_work.stride(0), ptr(scale_full), ptr(zero_full), ld_p, gshift, B, n,
+             int(maxq), ptr(q0), ptr(x0), x0.stride(0))
+        x_pol, _, st = _generic_uniform_polish(
+            x_init=x_work, Y_u=Y_u, Vs=Vs, scale=scale_full, zero=zero_full, maxq=maxq, sweeps=int(sweeps),
+            order_mode=order_mode, backend=backend, raw_target=raw_target,
+            raw_gram=_f32c(raw_gram, dev) if raw_gram is not None else None, q_init=q0.to(torch.int32))
+        return finish(x_pol, st)
     ctx = _UniformCtx.__new__(_UniformCtx)
     ctx.dev, ctx.B, ctx.n, ctx.R = dev, B, n, R
     ctx.scale, ctx.zero, ctx.ld_p, ctx.gshift, ctx.maxq = scale_full, zero_full, ld_p, gshift, int(maxq)
@@ -419,12 +465,23 @@ def solve_uniform_rankspace_vamp(
     if polish_mode != "none":
         if polish_mode != "block_cd":
             raise NotImplementedError("topk_block_cd uniform polish is not built yet")
-        if gram_full is None:
-            raise NotImplementedError("the uniform polish needs gram_full (the raw Hessian)")
-        x_pol, polish_stats = scalar_greedy_cd(ctx, x_final, _f32c(gram_full, dev), sweeps=polish_sweeps)
+        backend = _resolve_block_cd_backend(block_cd_backend=str(getattr(cfg, "block_cd_backend", "") or ""),
+                                            compile_block_cd=bool(getattr(cfg, "compile_block_cd", True)))
         q_pol = torch.empty_like(q_final)
         x_out = torch.empty_like(x_final)
-        ctx.nearest(x_pol, q_pol, x_out)
+        if backend in {"triton", "auto"} and gram_full is not None:
+            x_pol, polish_stats = scalar_greedy_cd(ctx, x_final, _f32c(gram_full, dev), sweeps=polish_sweeps)
+            polish_stats = dict(polish_stats, block_cd_backend="cuda")
+            ctx.nearest(x_pol, q_pol, x_out)
+        else:
+            x_pol, q_cd, polish_stats = _generic_uniform_polish(
+                x_init=x_final, Y_u=ctx.Y_u, Vs=ctx.Vs, scale=ctx.scale, zero=ctx.zero, maxq=ctx.maxq,
+                sweeps=polish_sweeps, order_mode="greedy_gain", backend=backend,
+                raw_target=W if gram_full is not None else None,
+                raw_gram=_f32c(gram_full, dev) if gram_full is not None else None, q_init=q_final.to(torch.int32))
+            q_pol.copy_(q_cd.to(torch.uint8))
+            call("mpq_uniform_nearest", ptr(x_pol), x_pol.stride(0), ptr(ctx.scale), ptr(ctx.zero), ctx.ld_p,
+                 ctx.gshift, B, n, ctx.maxq, ptr(q_pol), ptr(x_out), x_out.stride(0))
         err_after = ctx.err(x_out, tmp=tmpBR)
         err_before = err_final.clone()
         improved = torch.zeros(1, device=dev, dtype=torch.int32)
@@ -432,7 +489,6 @@ def solve_uniform_rankspace_vamp(
              ptr(q_pol), ptr(q_final), B, n, x_final.stride(0), ptr(improved))
         polish_updates = float(polish_stats.get("accepted_updates", 0.0))
         polish_stats = dict(polish_stats)
-        polish_stats["block_cd_backend"] = "cuda"
         polish_stats["rows_improved"] = int(improved.item())
 
     rtn_err = ctx.err(x_rtn, tmp=tmpBR)
@@ -533,12 +589,18 @@ def polish_e8p12_rankspace(
 
     if mode == "none" or Vs.numel() == 0:
         return x_work, idxs_init, err_of(x_work), {"accepted_updates": 0.0}
-    if mode != "block_cd" or metric != "gram":
-        raise NotImplementedError("only the gram-metric full-grid block CD (the default recipe) is built")
-    if str(order_mode or "greedy_gain").lower() != "greedy_gain" or int(polish_max_blocks) > 0:
-        raise NotImplementedError("only the greedy_gain order over all blocks is built")
-    x_out, idx_out, st = gram_block_cd(x=x_work, Y_u=Y_u, Vs=Vs, cb=cb, sweeps=int(sweeps), idxs_init=idxs_init,
-                                       opVs=opVs, opVsT=opVsT)
+    if mode != "block_cd":
+        raise NotImplementedError("topk_block_cd E8P12 polish is not built yet")
+    from .block_cd import BlockCDConfig, E8P12Provider, block_coordinate_descent_rankspace
+    x_out, idx_out, st = block_coordinate_descent_rankspace(
+        x=x_work, Y_u=Y_u, Vs=Vs, block_size=int(getattr(cb, "codesz", 8)),
+        provider=E8P12Provider(cb=cb, metric_rows_per_chunk=int(metric_rows_per_chunk)),
+        cfg=BlockCDConfig(sweeps=int(sweeps), metric="gram" if metric == "gram" else "diag", accept_tol=0.0,
+                          metric_rows_per_chunk=int(metric_rows_per_chunk), max_blocks_per_sweep=int(polish_max_blocks),
+                          order_mode=str(order_mode or "greedy_gain")),
+        idxs_init=idxs_init, snapshot_budgets=snapshot_budgets, snapshots_out=snapshots_out)
+    if idx_out is None:
+        raise RuntimeError("E8P12 polish must return block indices.")
     return x_out, idx_out, err_of(x_out), st
 
 

@@ -280,9 +280,63 @@ def gen_e8p12_layer(out):
     np.savez_compressed(out / "e8p12_layer.npz", **cases)
 
 
+def _block_cd_problem(B, n, R, seed, scale_rows=0.02):
+    """A rank-space least-squares problem Y_u = W Vs with Vs from a random Hessian's eigenbasis."""
+    g = torch.Generator().manual_seed(seed)
+    W = torch.randn(B, n, generator=g) * scale_rows
+    s = torch.exp(torch.randn(n, generator=g))
+    X = torch.randn(4 * n, n, generator=g) * s.sqrt()
+    H = X.T @ X / X.shape[0] + 0.01 * torch.eye(n)
+    lam, V = torch.linalg.eigh(H.double())
+    lam, V = lam.flip(0)[:R].clamp_min(1e-6), V.flip(1)[:, :R]
+    Vs = (V * lam.sqrt()).float().contiguous()
+    return W, H, Vs
+
+
+def gen_block_cd(out):
+    """The reference's generic rank-space block CD (plugin engine) with its own providers, eager steps."""
+    from mpq.polish.block_cd import BlockCDConfig, E8P12Provider, UniformScalarProvider, block_coordinate_descent_rankspace
+    cases = {}
+    # scalar provider, block_size 1, diag metric, three orders
+    for name, order in {"s_greedy": "greedy_gain", "s_static": "static", "s_cyclic": "cyclic"}.items():
+        B, n, maxq = 12, 64, 15
+        W, H, Vs = _block_cd_problem(B, n, n, 41)
+        q = MinMaxQuantizer(4)
+        q.find_params(W)
+        scale = q.scale.expand(B, n).contiguous()
+        zero = q.zero.expand(B, n).contiguous()
+        x0 = scale * (torch.clamp(torch.round(W / scale) + zero, 0, maxq) - zero)
+        Y_u = W @ Vs
+        cfg = BlockCDConfig(sweeps=2, metric="diag", order_mode=order, compile_steps=False)
+        prov = UniformScalarProvider(scale=scale, zero=zero, maxq=maxq)
+        q0 = torch.clamp(torch.round(x0 / scale + zero), 0, maxq).to(torch.int32)  # as polish_uniform_rankspace
+        xo, qo, st = block_coordinate_descent_rankspace(x=x0, Y_u=Y_u, Vs=Vs, block_size=1, provider=prov, cfg=cfg,
+                                                        idxs_init=q0, raw_target=W, raw_gram=H)
+        for k, v in dict(W=W, H=H, Vs=Vs, scale=scale, zero=zero, x0=x0, q0=q0, Y_u=Y_u, x=xo, q=qo).items():
+            cases[f"{name}/{k}"] = _np(v)
+        cases[f"{name}/meta"] = np.array(json.dumps({"order": order, "sweeps": 2, "maxq": maxq, "stats": st}))
+    # E8P12 provider, block_size 8: gram metric (eager generic path) and isotropic metric, capped blocks
+    cb = _reference_codebook()
+    for name, (metric, max_blocks) in {"e_gram": ("gram", 0), "e_iso": ("diag", 0), "e_gram_cap": ("gram", 5)}.items():
+        B, n = 10, 64
+        W, H, Vs = _block_cd_problem(B, n, n, 53, scale_rows=1.0)
+        x0, i0 = cb.quantize(W.reshape(-1, 8))
+        x0, i0 = x0.reshape(B, n), i0.reshape(B, n // 8)
+        Y_u = W @ Vs
+        cfg = BlockCDConfig(sweeps=2, metric=metric, order_mode="greedy_gain", max_blocks_per_sweep=max_blocks,
+                            compile_steps=False)
+        xo, io, st = block_coordinate_descent_rankspace(x=x0, Y_u=Y_u, Vs=Vs, block_size=8, provider=E8P12Provider(cb=cb),
+                                                        cfg=cfg, idxs_init=i0)
+        for k, v in dict(W=W, Vs=Vs, x0=x0, i0=i0, Y_u=Y_u, x=xo, idx=io).items():
+            cases[f"{name}/{k}"] = _np(v)
+        cases[f"{name}/meta"] = np.array(json.dumps({"metric": metric, "max_blocks": max_blocks, "sweeps": 2,
+                                                     "stats": st}))
+    np.savez_compressed(out / "block_cd.npz", **cases)
+
+
 GENERATORS = {"uniform_denoise": gen_uniform_denoise, "linear": gen_linear, "scalar_cd": gen_scalar_cd,
               "scalar_layer": gen_scalar_layer, "rotation": gen_rotation, "e8p12": gen_e8p12,
-              "e8p12_layer": gen_e8p12_layer}
+              "e8p12_layer": gen_e8p12_layer, "block_cd": gen_block_cd}
 
 
 def main():

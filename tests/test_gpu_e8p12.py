@@ -71,6 +71,42 @@ def test_e8p12_map_and_mmse_match_oracle(cuda_dev, ocb, pcb, gscale, tau):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("gscale", [3.0, 40.0])
+def test_e8p12_mmse_without_map_outputs(cuda_dev, ocb, pcb, gscale):
+    """The VAMP loop calls the posterior without MAP outputs (bound-only first pass, pruning reference = the
+    exact log-weight of the best-bound component); it must agree with the MAP-referenced call and the oracle."""
+    from mpq_b200 import e8p12 as PE
+    from mpq_b200._lib import call, ptr
+    from mpq_b200.codebook import factor_tables
+    B, nb, tau = 12, 64, 0.25
+    W, r1, gam = _case(int(gscale) + 21, B, nb, gscale)
+    ps = OE.prior_scale_from_center(W)
+    d = lambda a: _t(a, cuda_dev)
+    r1d, cen, psd = d(r1.reshape(B, nb * 8)), d(W.reshape(B, nb * 8)), d(ps.reshape(B, nb))
+    g = d(gam.reshape(B))
+    t = factor_tables(pcb, cuda_dev)
+    outs = []
+    for with_map in (True, False):
+        x1 = torch.empty(B, nb * 8, device=cuda_dev)
+        vsum = torch.empty(B, device=cuda_dev)
+        idx = torch.empty(B, nb, device=cuda_dev, dtype=torch.int32) if with_map else None
+        mv = torch.empty(B, nb * 8, device=cuda_dev) if with_map else None
+        call("mpq_e8p12_mmse", ptr(r1d), r1d.stride(0), ptr(cen), cen.stride(0), ptr(psd), psd.stride(0), ptr(g), tau,
+             B, nb, *PE._tab_ptrs(t), ptr(x1), x1.stride(0), None, 0, ptr(idx), nb if with_map else 0, ptr(mv),
+             nb * 8 if with_map else 0, ptr(vsum))
+        outs.append((x1.cpu().numpy(), vsum.cpu().numpy()))
+    torch.cuda.synchronize()
+    (xa, va), (xb, vb) = outs
+    np.testing.assert_allclose(xb, xa, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(vb, va, rtol=1e-5, atol=1e-7)
+    rpost = OE.vamp_vector_discrete_mmse_e8p12(r1_blocks=r1, gamma1=gam, cb=ocb, prior_center_blocks=W,
+                                               prior_scale_blocks=ps, prior_tau=tau)
+    rx1 = rpost["x1_blocks"].reshape(B, nb * 8)
+    assert np.isclose(xb, rx1, rtol=1e-4, atol=2e-5).mean() >= 0.99
+    assert np.abs(xb - rx1).max() <= 2e-2
+
+
+@pytest.mark.gpu
 def test_e8p12_mmse_golden_reference(cuda_dev, golden_dir, pcb):
     from mpq_b200 import e8p12 as PE
     z = np.load(golden_dir / "e8p12_prior.npz")

@@ -229,7 +229,7 @@ def test_solve_uniform_vamp_matches_oracle(cuda_dev, m, n, iters, maxq, group):
                                                               maxq=maxq, V=V, Vh=V.T.copy(), S=Sv, Vs=Vs, cfg=ocfg,
                                                               gram_full=H)
     d = lambda a: _t(a, cuda_dev)
-    cfg = S.UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=3)
+    cfg = S.UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto")
     q, x, err, rtn_err, st = S.solve_uniform_rankspace_vamp(W=d(W), x_rtn=d(x_rtn), scale_full=d(sg), zero_full=d(zg),
                                                             maxq=maxq, V=d(V), Vh=d(V.T.copy()), S=d(Sv), Vs=d(Vs),
                                                             cfg=cfg, gram_full=d(H))
@@ -253,7 +253,7 @@ def test_run_mpq_quantization_matches_reference_golden(cuda_dev, golden_dir, cas
     meta = json.loads(str(g("meta")))
     qcfg = types.SimpleNamespace(bits=meta["bits"], group_size=meta["group_size"], desc_act=False,
                                  mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
-    cfg = UniformVampConfig(iters=meta["iters"], prior_tau=0.2, damping=0.5, polish_sweeps=3)
+    cfg = UniformVampConfig(iters=meta["iters"], prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto")
     acfg = GPTQAdapterConfig(block_rows=meta["block_rows"], grow_block_rows=False)
     Q, q_int, scale, zero, g_idx, _, st = run_mpq_quantization(
         W=_t(g("W"), cuda_dev), H=_t(2.0 * g("H"), cuda_dev), quantizer=None, qcfg=qcfg, module_name=f"golden.{case}",
