@@ -38,6 +38,8 @@ N_COLS = 4096
 T_CALIB = 16384
 METRIC = "s per 4096^2 layer solve (VAMP+3 CD)"
 WORKLOAD_DESC = {
+    "model": "config 4: Llama-3-8B-shaped decoder, random init, 128 x 2048 uniform-random calibration tokens, 3-bit g128, "
+             "internal Hadamard, VAMP 20 it + 3 CD sweeps, GPTQ sequential layer walk; rows of every linear sharded over GPUs",
     "e8p12": "config1: 4096x4096 layer, 2-bit E8P12, two-sided RHT, RTN init, fp64 eigh, VAMP 16 it + 3 gram-CD sweeps",
     "scalar": "config0: 4096x4096 layer, 4-bit asym g128, internal Hadamard, RTN init, VAMP 20 it + 3 CD sweeps",
 }
@@ -58,6 +60,11 @@ def parse():
                     help="> 0: solve only this many rows per GPU (a small case for ncu; not a bench line)")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up + one timed step, no e2e / CPU legs (for an ncu launch list)")
+    ap.add_argument("--model", default="llama3_8b", help="model workload: registered decoder shape")
+    ap.add_argument("--model-layers", type=int, default=0, help="model workload: first N layers (0 = all)")
+    ap.add_argument("--calib-seqs", type=int, default=128)
+    ap.add_argument("--seq-len", type=int, default=2048)
+    ap.add_argument("--bits", type=int, default=3)
     a = ap.parse_args()
     if a.profile:
         a.steps, a.warmup, a.no_cpu_baseline, a.no_clocks = 1, 1, True, True
@@ -459,6 +466,9 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
+    if args.workload == "model":
+        return {"impl": "reference", "unavailable": "the whole-model CPU run (about 46 h for the 8B shape) is not "
+                "timed; the per-layer CPU baseline is the --workload e8p12 / scalar reference arm"}
     vals, info = [], None
     for _ in range(max(args.warmup, 0)):  # warm-up: thread pools, allocator, page cache (small sample)
         cpu_sample(args.workload, 2)
@@ -474,9 +484,70 @@ def run_reference(args):
             "e2e": {"value": v, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_model(args):
+    """Whole-model quantization time (one timed run; a full 8B-shape run takes minutes, so no warm-up steps)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from mpq_b200 import trace
+    from mpq_b200._lib import load
+    from mpq_b200.model import ModelQuantConfig, build_synthetic_decoder, calibration_ids, quantize_model
+    load()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=dev)
+    layers = args.model_layers if args.model_layers > 0 else None
+    model = build_synthetic_decoder(args.model, device=dev, seed=0, num_layers=layers)
+    ids = calibration_ids(args.calib_seqs, args.seq_len, model.config.vocab_size, seed=0)
+    cfg = ModelQuantConfig(bits=args.bits, group_size=128, iters=20, prior_tau=0.2, damping=0.5, polish_sweeps=3)
+    clocks = ClockSampler(local, enabled=not args.no_clocks)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = trace.launches()
+    t0 = time.perf_counter()
+    out = quantize_model(model, ids, cfg)
+    torch.cuda.synchronize()
+    secs = time.perf_counter() - t0
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([secs], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    res = None
+    if rank == 0:
+        mods = out["modules"]
+        res = {"metric": f"s per {args.model}-shape full-model quantization", "value": secs, "unit": "s",
+               "n_gpus": world, "steps": 1, "warmup": 0, "ms_per_step": secs * 1e3, "higher_is_better": False,
+               "scaling": "strong", "vs_baseline": None, "dtype": "f32 solve / bf16 model", "data": "synthetic",
+               "config": {"workload": WORKLOAD_DESC["model"], "model": args.model, "layers": model.config.num_hidden_layers,
+                          "calibration": [args.calib_seqs, args.seq_len], "bits": args.bits, "group_size": 128,
+                          "parallelism": f"rows{world}+calib{world}"},
+               "timings_rank0_s": out["timings"], "gpu_launches": trace.launches() - launches0, "clocks": clk,
+               "linears": len(mods),
+               "solve_s_by_projection_rank0": {k: round(sum(m["solve_s"] for n, m in mods.items() if n.endswith(k)), 3)
+                                               for k in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj",
+                                                         "down_proj")},
+               "rankspace_error_over_rtn": float(np.mean([m["rankspace_error_mean"] / max(m["rtn_rankspace_error_mean"], 1e-30)
+                                                          for m in mods.values() if m.get("rankspace_error_mean")]))}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
 def main():
     args = parse()
-    res = run_reference(args) if args.impl == "reference" else run_mpq(args)
+    if args.impl == "reference":
+        res = run_reference(args)
+    elif args.workload == "model":
+        res = run_model(args)
+    else:
+        res = run_mpq(args)
     if res is not None:
         print(json.dumps(res))
 

@@ -9,7 +9,7 @@ ojbkq) and ``desc_act`` column permutation raise ``ValueError``.
 from __future__ import annotations
 
 import time
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional, Tuple
 
 import torch
@@ -31,6 +31,9 @@ class GPTQAdapterConfig:
     # True: grow block_rows to the memory budget as the reference does on CUDA
     # (mpq/adapters/gptqmodel.py:313-327).  False: use block_rows as given (parity pinning).
     grow_block_rows: bool = True
+    # Optional dict shared by the linears of one layer: modules fed by the same input (q/k/v, gate/up) get the
+    # same Hessian tensor, and its floored eigendecomposition (taken before the per-module rotation) is reused.
+    eigen_cache: Optional[dict] = field(default=None, compare=False, hash=False)
 
 
 @torch.inference_mode()
@@ -133,8 +136,16 @@ def run_mpq_quantization(
                          f"got rotation={rotation!r}.")
 
     H_work = float(adapter_cfg.hessian_scale) * H
-    lam, V, eigen_floor = vamp_hessian_eigen(H_work, jitter_base=adapter_cfg.jitter_base,
-                                             floor_scale=adapter_cfg.eigen_floor_scale)
+    cache = adapter_cfg.eigen_cache
+    key = (H.data_ptr(), tuple(H.shape), float(adapter_cfg.hessian_scale), float(adapter_cfg.jitter_base),
+           float(adapter_cfg.eigen_floor_scale))
+    if cache is not None and key in cache:
+        lam, V, eigen_floor = cache[key]
+    else:
+        lam, V, eigen_floor = vamp_hessian_eigen(H_work, jitter_base=adapter_cfg.jitter_base,
+                                                 floor_scale=adapter_cfg.eigen_floor_scale)
+        if cache is not None:
+            cache[key] = (lam, V, eigen_floor)
     signs = None
     had_dim = 1
     effective = rotation

@@ -1,0 +1,238 @@
+"""Whole-model quantization driver for decoder LMs (GPTQModel-style sequential layer walk).
+
+The reference reaches a whole model through GPTQModel's processor loop, which collects each linear's
+Hessian with forward hooks (GPTQ.add_batch) and calls MPQ's ``run_mpq_quantization`` per linear
+(patches/gptqmodel.patch:672-756, mpq/adapters/gptqmodel.py:650-1163), and through the QUIP# driver for
+E8P12 (mpq/quip_generic.py).  This module restates that walk on the B200 kernels:
+
+* layers are processed in order; inside a layer the linears are quantized in GPTQ's sequential subsets
+  ([q, k, v], [o], [gate, up], [down]) and each subset's Hessian is collected with the already-quantized
+  subsets in place (``true_sequential``), then the layer's outputs with quantized weights feed the next layer;
+* Hessian hooks feed bfloat16 activations straight into the tensor-core X^T X (exact TF32 operands); linears
+  fed by the same input share one Hessian and one eigendecomposition;
+* with N ranks (one process per GPU) the calibration sequences are split across ranks, the partial sums
+  X^T X and sample counts are all-reduced (NCCL over NVLink), every linear's output rows are solved as row
+  shards, and the dequantized rows are all-gathered so every rank holds the quantized layer.
+
+The model shapes of the synthetic benchmark configs are in ``CONFIGS`` (random init, std 0.02).
+"""
+from __future__ import annotations
+
+import time
+import types
+from dataclasses import dataclass
+from typing import Any, Dict, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .hessian import accumulate_xtx
+from .shard import gather_rows, row_shards
+
+CONFIGS: Dict[str, Dict[str, Any]] = {
+    # Qwen3-0.6B shape
+    "qwen3_0p6b": dict(family="qwen3", hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                       num_attention_heads=16, num_key_value_heads=8, head_dim=128, vocab_size=151936),
+    # Llama-3.2-1B shape
+    "llama32_1b": dict(family="llama", hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=64, vocab_size=128256),
+    # Llama-3-8B shape
+    "llama3_8b": dict(family="llama", hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, vocab_size=128256),
+    # small shape for tests
+    "tiny_llama": dict(family="llama", hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                       num_attention_heads=4, num_key_value_heads=2, head_dim=64, vocab_size=1000),
+}
+
+SUBSETS = (("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"), ("self_attn.o_proj",),
+           ("mlp.gate_proj", "mlp.up_proj"), ("mlp.down_proj",))
+
+
+def build_synthetic_decoder(name: str, *, device, seed: int = 0, num_layers: Optional[int] = None,
+                            dtype=torch.bfloat16):
+    """Random-init (std 0.02) decoder LM of a registered shape, built directly on `device`."""
+    from transformers import AutoModelForCausalLM, LlamaConfig, Qwen3Config
+    spec = dict(CONFIGS[name])
+    fam = spec.pop("family")
+    if num_layers is not None:
+        spec["num_hidden_layers"] = int(num_layers)
+    cls = Qwen3Config if fam == "qwen3" else LlamaConfig
+    cfg = cls(initializer_range=0.02, attn_implementation="sdpa", max_position_embeddings=4096, **spec)
+    torch.manual_seed(int(seed))
+    with torch.device(device):
+        model = AutoModelForCausalLM.from_config(cfg, dtype=dtype)
+    return model.eval()
+
+
+def calibration_ids(n_seq: int, seq_len: int, vocab: int, seed: int = 0) -> torch.Tensor:
+    """Uniform-random token ids (n_seq x seq_len), the synthetic calibration set."""
+    g = torch.Generator(device="cpu").manual_seed(int(seed))
+    return torch.randint(0, int(vocab), (int(n_seq), int(seq_len)), generator=g)
+
+
+@dataclass
+class ModelQuantConfig:
+    bits: int = 4
+    group_size: int = 128
+    rotation_mode: str = "internal_hadamard"
+    iters: int = 20
+    prior_tau: float = 0.2
+    damping: float = 0.5
+    polish_sweeps: int = 3
+    block_cd_backend: str = "auto"
+    true_sequential: bool = True
+    batch_size: int = 8          # calibration sequences per forward
+    keep_codes: bool = False     # gather q_int / scale / zero of every linear to the host
+
+
+def _world(group=None) -> Tuple[int, int]:
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return 0, 1
+
+
+class _Timer:
+    def __init__(self, dev):
+        self.dev, self.acc = dev, {}
+
+    def __call__(self, name):
+        timer = self
+
+        class _Ctx:
+            def __enter__(self):
+                torch.cuda.synchronize(timer.dev)
+                self.t = time.perf_counter()
+
+            def __exit__(self, *a):
+                torch.cuda.synchronize(timer.dev)
+                timer.acc[name] = timer.acc.get(name, 0.0) + time.perf_counter() - self.t
+        return _Ctx()
+
+
+def _forward_layer(layer, hidden, out, bs, mask, pos_emb, pos_ids):
+    for b0 in range(0, hidden.shape[0], bs):
+        o = layer(hidden[b0:b0 + bs], attention_mask=mask, position_embeddings=pos_emb, position_ids=pos_ids)
+        if out is not None:
+            out[b0:b0 + bs].copy_(o)
+
+
+@torch.inference_mode()
+def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, group=None,
+                   layers: Optional[Sequence[int]] = None) -> Dict[str, Any]:
+    """Quantize every linear of every decoder layer in place (weights replaced by their dequantized values).
+
+    Returns {"modules": {name: stats (+ codes when keep_codes)}, "timings": {...}, "seconds": wall}."""
+    from .adapters.gptqmodel import GPTQAdapterConfig, run_mpq_quantization
+    from .solver import UniformVampConfig
+    rank, world = _world(group)
+    dev = next(model.parameters()).device
+    timer = _Timer(dev)
+    t_start = time.perf_counter()
+    inner = model.model
+    n_seq, seq_len = calib_ids.shape
+    s0, s1 = row_shards(n_seq, world, 1)[rank]
+    ids = calib_ids[s0:s1].to(dev)
+    qcfg = types.SimpleNamespace(bits=int(cfg.bits), group_size=int(cfg.group_size), desc_act=False,
+                                 mpq=types.SimpleNamespace(rotation_mode=cfg.rotation_mode, solver="vamp"))
+    vcfg = UniformVampConfig(iters=int(cfg.iters), prior_tau=float(cfg.prior_tau), damping=float(cfg.damping),
+                             polish_sweeps=int(cfg.polish_sweeps), block_cd_backend=cfg.block_cd_backend)
+    with timer("embed"):
+        hidden = inner.embed_tokens(ids)
+        nxt = torch.empty_like(hidden)
+    pos_ids = torch.arange(seq_len, device=dev)[None]
+    pos_emb = inner.rotary_emb(hidden[:1], position_ids=pos_ids)
+    mask = None  # sdpa causal attention without padding
+    results: Dict[str, Any] = {}
+    layer_ids = list(range(len(inner.layers))) if layers is None else list(layers)
+    for li in layer_ids:
+        layer = inner.layers[li]
+        subsets = SUBSETS if cfg.true_sequential else (sum(SUBSETS, ()),)
+        for subset in subsets:
+            # keyed by the Hessian's address: valid only while this subset's Hessians are alive
+            eigen_cache: dict = {}
+            mods = {name: layer.get_submodule(name) for name in subset}
+            # the linears of a subset read the same input (q/k/v: the attention norm's output, gate/up: the MLP
+            # norm's output): one Hessian per distinct input, collected on its first reader
+            readers: Dict[int, str] = {}
+            for name, m in mods.items():
+                readers.setdefault(id(_input_owner(layer, name)), name)
+            sums: Dict[str, torch.Tensor] = {}
+            counts: Dict[str, int] = {}
+
+            def make_hook(name):
+                def hook(mod, args):
+                    x = args[0]
+                    S = sums.get(name)
+                    if S is None:
+                        S = sums[name] = torch.zeros(x.shape[-1], x.shape[-1], device=dev, dtype=torch.float32)
+                        counts[name] = 0
+                    accumulate_xtx(S, x, alpha=1.0, beta=1.0)
+                    counts[name] += int(x.shape[0]) if x.dim() == 3 else 1  # GPTQ counts leading-dim samples
+                return hook
+
+            handles = [mods[name].register_forward_pre_hook(make_hook(name)) for name in readers.values()]
+            with timer("forward_hessian"):
+                _forward_layer(layer, hidden, None, int(cfg.batch_size), mask, pos_emb, pos_ids)
+            for h in handles:
+                h.remove()
+            Hs: Dict[str, torch.Tensor] = {}
+            with timer("hessian_reduce"):
+                for name, S in sums.items():  # GPTQ convention H = 2 / nsamples * sum x x^T, over all ranks
+                    cnt = torch.tensor([float(counts[name])], device=dev, dtype=torch.float64)
+                    if world > 1:
+                        dist.all_reduce(S, group=group)
+                        dist.all_reduce(cnt, group=group)
+                    S.mul_(2.0 / float(cnt.item()))
+                for name in mods:
+                    Hs[name] = sums[readers[id(_input_owner(layer, name))]]
+            for name, m in mods.items():
+                full = f"model.layers.{li}.{name}"
+                W = m.weight
+                rows = W.shape[0]
+                r0, r1 = row_shards(rows, world, 128)[rank]
+                with timer("solve"):
+                    if r1 > r0:
+                        Wl = W[r0:r1].to(torch.float32)
+                        acfg = GPTQAdapterConfig(block_rows=r1 - r0, grow_block_rows=False, eigen_cache=eigen_cache)
+                        Q, q_int, scale, zero, g_idx, secs, st = run_mpq_quantization(
+                            W=Wl, H=Hs[name], quantizer=None, qcfg=qcfg, module_name=full, vamp_cfg=vcfg,
+                            adapter_cfg=acfg)
+                    else:  # more ranks than row tiles: nothing to solve here
+                        ng = (W.shape[1] + int(cfg.group_size) - 1) // int(cfg.group_size)
+                        Q = torch.empty(0, W.shape[1], device=dev)
+                        q_int = torch.empty(0, W.shape[1], device=dev, dtype=torch.uint8)
+                        scale = zero = torch.empty(0, ng, device=dev)
+                        g_idx = torch.arange(W.shape[1], device=dev, dtype=torch.int32) // int(cfg.group_size)
+                        secs, st = 0.0, {}
+                with timer("gather"):
+                    Qa = gather_rows(Q.to(W.dtype).contiguous(), row_shards(rows, world, 128), group=group)
+                    W.copy_(Qa)
+                    lr = max(r1 - r0, 1)
+                    entry = {"rows": rows, "cols": W.shape[1], "rows_local": (r0, r1), "solve_s": secs,
+                             "rankspace_error_mean": st.get("stabilized_objective_mean_final"),
+                             "rtn_rankspace_error_mean": st.get("rtn_error_sum", 0.0) / lr,
+                             "raw_objective_mean": st.get("raw_objective_mean_final")}
+                    if cfg.keep_codes:
+                        sh = row_shards(rows, world, 128)
+                        entry.update(q_int=gather_rows(q_int, sh, group=group).cpu(),
+                                     scale=gather_rows(scale.contiguous(), sh, group=group).cpu(),
+                                     zero=gather_rows(zero.contiguous(), sh, group=group).cpu(), g_idx=g_idx.cpu())
+                    results[full] = entry
+            del sums, Hs
+        with timer("forward_out"):
+            _forward_layer(layer, hidden, nxt, int(cfg.batch_size), mask, pos_emb, pos_ids)
+        hidden, nxt = nxt, hidden
+    ops.check_status(dev)
+    torch.cuda.synchronize(dev)
+    return {"modules": results, "timings": dict(timer.acc), "seconds": time.perf_counter() - t_start}
+
+
+def _input_owner(layer, name: str):
+    """The module whose output is `name`'s input: the attention or MLP pre-norm for the projections that read
+    it, otherwise the module itself."""
+    if name in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"):
+        return layer.input_layernorm
+    if name in ("mlp.gate_proj", "mlp.up_proj"):
+        return layer.post_attention_layernorm
+    return layer.get_submodule(name)
