@@ -227,6 +227,14 @@ int mpq_cd_accept(float* x, int64_t ldx, const float* cand, int64_t ldc, const f
                   const float* gram, float* res_norm, int B, int bs, float accept_tol, float* delta, int64_t ldd,
                   const int* cand_idx, int* idx, int64_t ldi, int* accepted, void* stream);
 
+/* ---- export (GPTQ format) ----
+ * Little-endian bit-stream packing of b-bit codes (b in 2, 3, 4, 8) along one axis into int32 words: code (p, o) at
+ * src[p sp + o so], output word (w, o) holds stream bits [32 w, 32 w + 32) of line o; (code - offset) is masked to
+ * b bits (offset 1 gives the v1 qzeros).  The qweight/qzeros of GPTQModel's packer, applied to the codes of
+ * mpq/adapters/gptqmodel.py:650-1163 (patches/gptqmodel.patch:370-395; the packer itself is not vendored). */
+int mpq_pack_bits(const uint8_t* src, int64_t sp, int64_t so, int n_pack, int n_other, int bits, int offset,
+                  int32_t* out, int64_t ld_out, void* stream);
+
 /* ---- rotation ----
  * Block Walsh-Hadamard of the last dim, blocks of `had` (power of two <= 16384), normalized by sqrt(had);
  * mode 0: y = H(x * signs) (right rotation), mode 1: y = H(x) * signs (inverse).  signs may be NULL.

@@ -56,6 +56,7 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_split_tf32_t": (P, I, L, I, I, P, P, L, P),
     "mpq_col_sum": (P, I, L, I, I, F, F, P, P),
     "mpq_cd_target": (P, L, P, L, I, I, P, P, P, L, P),
+    "mpq_pack_bits": (P, L, L, I, I, I, I, P, L, P),
     "mpq_cd_accept": (P, L, P, L, P, L, P, P, I, I, F, P, L, P, P, L, P, P),
     "mpq_cd_diag": (P, I, I, L, P, P, P),
     "mpq_cd_gain": (P, I, I, L, P, P, P),

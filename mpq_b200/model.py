@@ -84,6 +84,7 @@ class ModelQuantConfig:
     true_sequential: bool = True
     batch_size: int = 8          # calibration sequences per forward
     keep_codes: bool = False     # gather q_int / scale / zero of every linear to the host
+    export_gptq: bool = False    # also pack them into GPTQ v1 tensors (qweight / qzeros / scales / g_idx)
 
 
 def _world(group=None) -> Tuple[int, int]:
@@ -213,11 +214,16 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
                              "rankspace_error_mean": st.get("stabilized_objective_mean_final"),
                              "rtn_rankspace_error_mean": st.get("rtn_error_sum", 0.0) / lr,
                              "raw_objective_mean": st.get("raw_objective_mean_final")}
-                    if cfg.keep_codes:
+                    if cfg.keep_codes or cfg.export_gptq:
                         sh = row_shards(rows, world, 128)
-                        entry.update(q_int=gather_rows(q_int, sh, group=group).cpu(),
-                                     scale=gather_rows(scale.contiguous(), sh, group=group).cpu(),
-                                     zero=gather_rows(zero.contiguous(), sh, group=group).cpu(), g_idx=g_idx.cpu())
+                        qa = gather_rows(q_int, sh, group=group)
+                        sa = gather_rows(scale.contiguous(), sh, group=group)
+                        za = gather_rows(zero.contiguous(), sh, group=group)
+                        if cfg.keep_codes:
+                            entry.update(q_int=qa.cpu(), scale=sa.cpu(), zero=za.cpu(), g_idx=g_idx.cpu())
+                        if cfg.export_gptq:
+                            from .export import pack_gptq
+                            entry["gptq"] = {k: v.cpu() for k, v in pack_gptq(qa, sa, za, g_idx, int(cfg.bits)).items()}
                     results[full] = entry
             del sums, Hs
         with timer("forward_out"):
