@@ -38,6 +38,7 @@ N_COLS = 4096
 T_CALIB = 16384
 METRIC = "s per 4096^2 layer solve (VAMP+3 CD)"
 WORKLOAD_DESC = {
+    "hessian": "calibration Hessian H = X^T X / T on the tensor cores (token-major activations X, T x n)",
     "model": "config 4: Llama-3-8B-shaped decoder, random init, 128 x 2048 uniform-random calibration tokens, 3-bit g128, "
              "internal Hadamard, VAMP 20 it + 3 CD sweeps, GPTQ sequential layer walk; rows of every linear sharded over GPUs",
     "e8p12": "config1: 4096x4096 layer, 2-bit E8P12, two-sided RHT, RTN init, fp64 eigh, VAMP 16 it + 3 gram-CD sweeps",
@@ -65,6 +66,11 @@ def parse():
     ap.add_argument("--calib-seqs", type=int, default=128)
     ap.add_argument("--seq-len", type=int, default=2048)
     ap.add_argument("--bits", type=int, default=3)
+    ap.add_argument("--gemm-precision", default="", help="tf32x3 | f16x3 (FP32-faithful split products); default: "
+                    "the library default")
+    ap.add_argument("--hess-n", type=int, default=14336, help="hessian workload: features n")
+    ap.add_argument("--hess-tokens", type=int, default=16384, help="hessian workload: tokens T per batch")
+    ap.add_argument("--hess-dtype", default="bf16", choices=["bf16", "f32"])
     a = ap.parse_args()
     if a.profile:
         a.steps, a.warmup, a.no_cpu_baseline, a.no_clocks = 1, 1, True, True
@@ -232,9 +238,11 @@ class E8Workload:
 def run_mpq(args):
     import torch
     import torch.distributed as dist
-    from mpq_b200 import trace
+    from mpq_b200 import ops, trace
     from mpq_b200._lib import load
     load()
+    if args.gemm_precision:
+        ops.set_gemm_precision(args.gemm_precision)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -337,7 +345,7 @@ def run_mpq(args):
         result = {
             "metric": METRIC, "value": ms / 1e3, "unit": "s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32",
+            "vs_baseline": None, "dtype": "f32", "gemm_precision": ops.gemm_precision(),
             "data": "synthetic (seeded W ~ N(0,0.02^2), X with log-normal channel scales)",
             "config": {"workload": WORKLOAD_DESC[args.workload], "block_rows": block_rows, "rows_per_gpu": rows_per,
                        "parallelism": f"rows{world}", "l2": "256 MB buffer written between timed steps"},
@@ -478,7 +486,7 @@ def run_reference(args):
     v = float(np.mean(vals))
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": "s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "vs_baseline": None, "dtype": "f32", "gemm_precision": ops.gemm_precision(), "data": "synthetic (seeded)",
             "config": {"workload": WORKLOAD_DESC[args.workload], "parallelism": "cpu"},
             "cpu_baseline": {k: info[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": v, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -540,12 +548,48 @@ def run_model(args):
     return res
 
 
+def run_hessian(args):
+    """Device time of one X^T X accumulation (the Hessian hooks' work per calibration batch)."""
+    import torch
+    from mpq_b200._lib import load
+    from mpq_b200.hessian import accumulate_xtx
+    load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, T = args.hess_n, args.hess_tokens
+    g = torch.Generator(device=dev).manual_seed(0)
+    X = torch.randn(T, n, device=dev, generator=g).to(torch.bfloat16 if args.hess_dtype == "bf16" else torch.float32)
+    H = torch.zeros(n, n, device=dev)
+    for _ in range(max(args.warmup, 1)):
+        accumulate_xtx(H, X, alpha=1.0 / T, beta=0.0)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        accumulate_xtx(H, X, alpha=1.0 / T, beta=1.0)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / max(args.steps, 1)
+    tf = float(T) * n * (n + 1) / (ms * 1e-3) / 1e12
+    pk = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(pk.read_text()) if pk.exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    return {"metric": "ms per X^T X accumulation", "value": ms, "unit": "ms", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False, "dtype": args.hess_dtype, "data": "synthetic",
+            "config": {"workload": WORKLOAD_DESC["hessian"], "n": n, "tokens": T},
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                         "achieved_counts": "algorithmic T n (n + 1) (symmetric product)",
+                         "peak_source": "MEASURED_PEAKS.json bf16_tflops (measured)" if peaks else "fallback"}}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         res = run_reference(args)
     elif args.workload == "model":
         res = run_model(args)
+    elif args.workload == "hessian":
+        res = run_hessian(args)
     else:
         res = run_mpq(args)
     if res is not None:

@@ -147,6 +147,15 @@ int mpq_cd_block(float* x, int64_t ldx, const float* rhs, int64_t ldr, const flo
  * mpq/polish/triton_scalar_cd.py:195-196,286-288. */
 int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float* const* A, int64_t lda, const float* const* B,
                 int64_t ldb, float beta, float* C, int64_t ldc, int* status, void* stream);
+/* FP32-faithful product on the fp16 tensor cores (kind::f16, twice the TF32 rate): C = alpha (sum over (hi,hi), (hi,lo),
+ * (lo,hi) of diag(sa) A B^T diag(sb)) + beta C from the row-scaled fp16 splits of mpq_split_f16 (16-bit row-major,
+ * lda/ldb multiples of 8, 16-byte aligned).  Same products as mpq_gemm_tc (mpq/linear.py:48,51,94, mpq/solver.py:485). */
+int mpq_gemm_f16x3(int M, int N, int K, float alpha, const void* a_hi, const void* a_lo, int64_t lda, const float* sa,
+                   const void* b_hi, const void* b_lo, int64_t ldb, const float* sb, float beta, float* C, int64_t ldc,
+                   int* status, void* stream);
+/* Row-scaled fp16 split: s = 2^(15 - E) with max|x_row| < 2^E, hi = fp16(x s), lo = fp16(x s - hi), inv_scale = 1 / s. */
+int mpq_split_f16(const float* x, int64_t ldx, int rows, int cols, void* hi, void* lo, int64_t ldo, float* inv_scale,
+                  void* stream);
 /* hi = TF32 round-to-nearest of x, lo = x - hi (the operand split of the 3xTF32 product). */
 int mpq_split_tf32(const float* x, int64_t ldx, float* hi, float* lo, int64_t ldo, int rows, int cols, void* stream);
 /* ---- calibration Hessian (K11) ----
@@ -161,6 +170,14 @@ int mpq_syrk_tc(int nreg, int n, int K, float alpha, const float* const* A, cons
  * lo[j,t] = X[t,j] - hi[j,t] (lo may be NULL: bf16 values are exact in TF32). */
 int mpq_split_tf32_t(const void* x, int dtype, int64_t ldx, int tokens, int n, float* hi, float* lo, int64_t ldo,
                      void* stream);
+/* Symmetric product of a bf16 operand C = alpha A A^T + beta C (A: n x K row-major bf16, lda a multiple of 8) with
+ * kind::f16 tensor-core MMAs (exact bf16 products, FP32 accumulation); mirror = 0 updates the lower triangle only
+ * (intermediate accumulation steps), 1 also stores every entry at its mirror.  The Hessian hooks' X^T X for bf16
+ * activations (see mpq_syrk_tc). */
+int mpq_syrk_bf16(int n, int K, float alpha, const void* A, int64_t lda, float beta, float* C, int64_t ldc, int mirror,
+                  int* status, void* stream);
+/* out[j,t] = X[t,j] for bf16 activations X (T x n): the K-major operand of mpq_syrk_bf16. */
+int mpq_transpose_bf16(const void* x, int64_t ldx, int tokens, int n, void* out, int64_t ldo, void* stream);
 /* out[j] = beta out[j] + alpha sum_t X[t,j] (the QUIP# hook's running sum of inputs, mpq/quip_generic.py:906-918). */
 int mpq_col_sum(const void* x, int dtype, int64_t ldx, int tokens, int n, float alpha, float beta, float* out,
                 void* stream);

@@ -51,10 +51,14 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_gemm_f32": (I, I, I, I, F, P, L, P, L, F, P, L, P),
     "mpq_gemm_tc": (I, I, I, I, F, P, L, P, L, F, P, L, P, P),
     "mpq_split_tf32": (P, L, P, P, L, I, I, P),
+    "mpq_gemm_f16x3": (I, I, I, F, P, P, L, P, P, P, L, P, F, P, L, P, P),
+    "mpq_split_f16": (P, L, I, I, P, P, L, P, P),
     "mpq_gemm_tf32x3_noalloc": (I, I, I, F, P, L, P, L, F, P, L, P, P),
     "mpq_syrk_tc": (I, I, I, F, P, P, L, F, P, L, P, P),
     "mpq_split_tf32_t": (P, I, L, I, I, P, P, L, P),
     "mpq_col_sum": (P, I, L, I, I, F, F, P, P),
+    "mpq_syrk_bf16": (I, I, F, P, L, F, P, L, I, P, P),
+    "mpq_transpose_bf16": (P, L, I, I, P, L, P),
     "mpq_cd_target": (P, L, P, L, I, I, P, P, P, L, P),
     "mpq_pack_bits": (P, L, L, I, I, I, I, P, L, P),
     "mpq_cd_accept": (P, L, P, L, P, L, P, P, I, I, F, P, L, P, P, L, P, P),

@@ -17,13 +17,14 @@
 // `status`, drains its own in-flight copies / MMAs (bounded), frees TMEM and exits.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 #include "common.cuh"
 
 namespace mpq {
 namespace tc {
 
 constexpr int BM = 128;
-constexpr int BK = 32;  // fp32 elements per k-block = 128 bytes = one 128B swizzle row
+constexpr int BK = 32;  // fp32 elements per k-block = 128 bytes = one 128B swizzle row (64 for bf16)
 constexpr int kThreads = 192;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
 
@@ -86,18 +87,37 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// Instruction descriptor: kind::f16 with BF16 A and B (both the same type), D = F32, both K-major, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// Instruction descriptor: kind::f16 with F16 A and B, D = F32, both K-major, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
 struct Maps {
   CUtensorMap a[3];
   CUtensorMap b[3];
 };
 
-template <int BN, int STAGES>
+// 32-bit operands: kind::tf32 (K = 8 per MMA); 16-bit operands: kind::f16 (K = 16 per MMA).  Either way a k-block is
+// one 128-byte swizzle row per operand row (32 fp32 or 64 16-bit elements) and 4 MMAs of 32 bytes.
+// sym: 0 general product; 1 symmetric (tiles with col <= row, entries stored with their mirrors); 2 symmetric,
+// lower triangle only (intermediate accumulation steps).
+// KIND 0: fp32 operands, kind::tf32; 1: bf16, kind::f16; 2: fp16, kind::f16.  sa / sb (optional, with KIND 2): per-row
+// scales of A's rows and of B's rows applied to the accumulator (the row-scaled fp16 split).
+template <int BN, int STAGES, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ Maps maps, int nreg, int M, int N, int K, float alpha, float beta,
-              float* __restrict__ C, int64_t ldc, int* __restrict__ status, int sym) {
-  constexpr uint32_t kStageA = BM * BK * 4;
-  constexpr uint32_t kStageB = BN * BK * 4;
-  constexpr uint32_t kIdesc = idesc_tf32(BM, BN);
+              float* __restrict__ C, int64_t ldc, int* __restrict__ status, int sym, const float* __restrict__ sa,
+              const float* __restrict__ sb) {
+  constexpr bool BF16 = KIND != 0;  // 16-bit operands
+  constexpr uint32_t kStageA = BM * 128;
+  constexpr uint32_t kStageB = BN * 128;
+  constexpr int kBKE = BF16 ? 64 : 32;  // elements per k-block
+  constexpr uint32_t kIdesc = KIND == 2 ? idesc_f16(BM, BN) : (KIND == 1 ? idesc_bf16(BM, BN) : idesc_tf32(BM, BN));
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte aligned ring (swizzle atoms need 1024 B alignment)
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -114,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   // symmetric product (A_r and B_r are the same operand): only tiles holding entries col <= row run
   if (sym && n0 > m0 + BM - 1) return;
-  const int kb_per_reg = (K + BK - 1) / BK;
+  const int kb_per_reg = (K + kBKE - 1) / kBKE;
   const int total_kb = kb_per_reg * nreg;
 
   if (threadIdx.x == 0) {
@@ -148,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int r = kb / kb_per_reg;
-        const int k0 = (kb % kb_per_reg) * BK;
+        const int k0 = (kb % kb_per_reg) * kBKE;
         mbar_expect_tx(&full[s], kStageA + kStageB);
         tma_load_2d(sA + s * kStageA, &maps.a[r], &full[s], k0, m0);
         tma_load_2d(sB + s * kStageB, &maps.b[r], &full[s], k0, n0);
@@ -176,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_addr = smem_u32(sA + s * kStageA);
         const uint32_t b_addr = smem_u32(sB + s * kStageB);
         #pragma unroll
-        for (int j = 0; j < BK / 8; ++j) {
+        for (int j = 0; j < 4; ++j) {  // 4 MMAs of 32 bytes per 128-byte k-block row (K = 8 tf32 / 16 bf16)
           const uint64_t da = smem_desc_k_sw128(a_addr + j * 32);
           const uint64_t db = smem_desc_k_sw128(b_addr + j * 32);
           const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
@@ -220,18 +240,50 @@ __global__ void __launch_bounds__(kThreads, 1)
               "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (sa) {  // power-of-two row scales of the fp16 split: exact unless the result over/underflows
+          const float ra = sa[row < M ? row : 0];
+          #pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            const int col = n0 + c0 + t;
+            v[t] = __float_as_uint(__uint_as_float(v[t]) * (ra * (col < N ? sb[col] : 0.f)));
+          }
+        }
         if (sym) {
-          // lower entries (col <= row) and their mirrors: the result is exactly symmetric; the mirror
-          // stores of a warp (32 consecutive rows, one column) are contiguous
-          if (row < M) {
+          // lower entries (col <= row) and their mirrors: the result is exactly symmetric.  Chunks entirely below
+          // the diagonal use 16-byte row stores per thread; the mirror stores of a warp (32 consecutive rows, one
+          // column) are contiguous.
+          const int cb = n0 + c0;
+          float* crow = C + (int64_t)row * ldc + cb;
+          if (row < M && cb + 31 < row && cb + 32 <= N && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
+            #pragma unroll
+            for (int t = 0; t < 32; t += 4) {
+              float4 o;
+              o.x = alpha * __uint_as_float(v[t]);
+              o.y = alpha * __uint_as_float(v[t + 1]);
+              o.z = alpha * __uint_as_float(v[t + 2]);
+              o.w = alpha * __uint_as_float(v[t + 3]);
+              float4* dst = reinterpret_cast<float4*>(crow + t);
+              if (beta != 0.f) {
+                const float4 c = *dst;
+                o.x += beta * c.x; o.y += beta * c.y; o.z += beta * c.z; o.w += beta * c.w;
+              }
+              *dst = o;
+              if (sym == 1) {
+                C[(int64_t)(cb + t) * ldc + row] = o.x;
+                C[(int64_t)(cb + t + 1) * ldc + row] = o.y;
+                C[(int64_t)(cb + t + 2) * ldc + row] = o.z;
+                C[(int64_t)(cb + t + 3) * ldc + row] = o.w;
+              }
+            }
+          } else if (row < M) {
             #pragma unroll
             for (int t = 0; t < 32; ++t) {
-              const int col = n0 + c0 + t;
+              const int col = cb + t;
               if (col < N && col <= row) {
                 float o = alpha * __uint_as_float(v[t]);
                 if (beta != 0.f) o += beta * C[(int64_t)row * ldc + col];
                 C[(int64_t)row * ldc + col] = o;
-                if (col != row) C[(int64_t)col * ldc + row] = o;
+                if (col != row && sym == 1) C[(int64_t)col * ldc + row] = o;
               }
             }
           }
@@ -292,12 +344,16 @@ static int get_encoder() {
 }
 
 // rows x K row-major fp32 (leading dimension ld), box = box_rows x 32, 128B swizzle
-static int make_map(CUtensorMap* m, const float* p, int rows, int K, int64_t ld, int box_rows) {
+// kind: 0 fp32, 1 bf16, 2 fp16
+static int make_map(CUtensorMap* m, const void* p, int rows, int K, int64_t ld, int box_rows, int kind = 0) {
+  const int esz = kind ? 2 : 4;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * esz};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esz), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, estr,
+  CUresult r = g_encode(m, kind == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                     : (kind == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32), 2,
+                        const_cast<void*>(p), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -307,17 +363,18 @@ static int make_map(CUtensorMap* m, const float* p, int rows, int K, int64_t ld,
   return MPQ_OK;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KIND = 0>
 static int launch(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
-                  int* status, cudaStream_t stream, int sym = 0) {
-  const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * BK * 4 + 256;
+                  int* status, cudaStream_t stream, int sym = 0, const float* sa = nullptr, const float* sb = nullptr) {
+  const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * 128 + 256;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_gemm_tc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(k_gemm_tc<BN, STAGES, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr = true;
   }
   dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  k_gemm_tc<BN, STAGES><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status, sym);
+  k_gemm_tc<BN, STAGES, KIND><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status, sym,
+                                                                 sa, sb);
   return launch_status("mpq_gemm_tc");
 }
 
@@ -377,6 +434,92 @@ MPQ_API int mpq_syrk_tc(int nreg, int n, int K, float alpha, const float* const*
     if (st) return st;
   }
   return tc::launch<256, 4>(maps, nreg, n, n, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 1);
+}
+
+// Symmetric product of a bf16 operand, C = alpha A A^T + beta C (A: n x K row-major bf16, lda a multiple of 8):
+// kind::f16 MMAs (bf16 x bf16 products are exact in FP32).  mirror != 0 stores every entry at its mirror too;
+// mirror == 0 updates the lower triangle only (intermediate steps of an accumulation).
+MPQ_API int mpq_syrk_bf16(int n, int K, float alpha, const void* A, int64_t lda, float beta, float* C, int64_t ldc,
+                          int mirror, int* status, void* stream) {
+  MPQ_CHECK_ARG(A && C && status, "mpq_syrk_bf16: null pointer");
+  MPQ_CHECK_ARG(n >= 0 && K >= 1, "mpq_syrk_bf16: bad shape");
+  MPQ_CHECK_ARG(lda % 8 == 0 && lda >= K && ldc >= n, "mpq_syrk_bf16: lda must be a multiple of 8 and >= K, ldc >= n");
+  MPQ_CHECK_ARG(((uintptr_t)A & 15) == 0, "mpq_syrk_bf16: A must be 16-byte aligned");
+  if (n == 0) return MPQ_OK;
+  int st = tc::get_encoder();
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  st = tc::make_map(&maps.a[0], A, n, K, lda, tc::BM, 1);
+  if (st) return st;
+  st = tc::make_map(&maps.b[0], A, n, K, lda, 256, 1);
+  if (st) return st;
+  return tc::launch<256, 4, 1>(maps, 1, n, n, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, mirror ? 1 : 2);
+}
+
+// FP32-faithful product on the fp16 tensor cores: C = alpha sum_{(a,b) in (hi,hi),(hi,lo),(lo,hi)} diag(sa) A_a B_b^T diag(sb)
+// + beta C, from the row-scaled fp16 split of mpq_split_f16 (A: M x K, B: N x K, 16-bit row-major, lda/ldb multiples
+// of 8; sa / sb the splits' per-row scales).  fp16 MMAs run at twice the TF32 rate; the split keeps 22 significant
+// bits per element as the 3xTF32 split does.
+MPQ_API int mpq_gemm_f16x3(int M, int N, int K, float alpha, const void* a_hi, const void* a_lo, int64_t lda,
+                           const float* sa, const void* b_hi, const void* b_lo, int64_t ldb, const float* sb, float beta,
+                           float* C, int64_t ldc, int* status, void* stream) {
+  MPQ_CHECK_ARG(a_hi && a_lo && b_hi && b_lo && sa && sb && C && status, "mpq_gemm_f16x3: null pointer");
+  MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 1, "mpq_gemm_f16x3: bad shape");
+  MPQ_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0 && lda >= K && ldb >= K, "mpq_gemm_f16x3: lda/ldb must be multiples of 8 and >= K");
+  const void* ptrs[4] = {a_hi, a_lo, b_hi, b_lo};
+  for (int i = 0; i < 4; ++i)
+    MPQ_CHECK_ARG(((uintptr_t)ptrs[i] & 15) == 0, "mpq_gemm_f16x3: operands must be 16-byte aligned");
+  if (M == 0 || N == 0) return MPQ_OK;
+  int st = tc::get_encoder();
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  const void* As[3] = {a_hi, a_hi, a_lo};
+  const void* Bs[3] = {b_hi, b_lo, b_hi};
+  for (int r = 0; r < 3; ++r) {
+    st = tc::make_map(&maps.a[r], As[r], M, K, lda, tc::BM, 2);
+    if (st) return st;
+    st = tc::make_map(&maps.b[r], Bs[r], N, K, ldb, 256, 2);
+    if (st) return st;
+  }
+  return tc::launch<256, 4, 2>(maps, 3, M, N, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 0, sa, sb);
+}
+
+namespace mpq {
+// Row-scaled fp16 split, one warp per row: s = 2^(15 - E) with max|x_row| < 2^E, y = x s (exact),
+// hi = fp16_rn(y), lo = fp16_rn(y - hi) (y - hi exact in fp32); inv_scale[row] = 1 / s.
+__global__ void k_split_f16(const float* __restrict__ x, int64_t ldx, int rows, int cols, __half* __restrict__ hi,
+                            __half* __restrict__ lo, int64_t ldo, float* __restrict__ inv_scale) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* xr = x + (int64_t)warp * ldx;
+  float mx = 0.f;
+  for (int c = lane; c < cols; c += 32) mx = fmaxf(mx, fabsf(xr[c]));
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  int e = 0;
+  if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx < 2^e
+  const float s = ldexpf(1.f, 15 - e), inv = ldexpf(1.f, e - 15);
+  for (int c = lane; c < cols; c += 32) {
+    const float y = xr[c] * s;
+    const __half h = __float2half_rn(y);
+    hi[(int64_t)warp * ldo + c] = h;
+    lo[(int64_t)warp * ldo + c] = __float2half_rn(y - __half2float(h));
+  }
+  if (lane == 0) inv_scale[warp] = inv;
+}
+}  // namespace mpq
+
+MPQ_API int mpq_split_f16(const float* x, int64_t ldx, int rows, int cols, void* hi, void* lo, int64_t ldo,
+                          float* inv_scale, void* stream) {
+  MPQ_CHECK_ARG(x && hi && lo && inv_scale, "mpq_split_f16: null pointer");
+  MPQ_CHECK_ARG(rows >= 0 && cols >= 0 && ldo >= cols && ldx >= cols, "mpq_split_f16: bad shape");
+  if (rows == 0 || cols == 0) return MPQ_OK;
+  const int warps_per_block = 8;
+  k_split_f16<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, (cudaStream_t)stream>>>(
+      x, ldx, rows, cols, (__half*)hi, (__half*)lo, ldo, inv_scale);
+  return launch_status("mpq_split_f16");
 }
 
 // hi = tf32 round-to-nearest of x (low 13 mantissa bits cleared), lo = x - hi (exact in fp32).

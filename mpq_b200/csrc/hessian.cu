@@ -44,6 +44,25 @@ __global__ void __launch_bounds__(256) k_split_tf32_t(const T* __restrict__ x, i
   }
 }
 
+// out[j, t] = X[t, j] for bf16 activations (the K-major operand of the bf16 symmetric product), 32 x 32 tiles.
+__global__ void __launch_bounds__(256) k_transpose_bf16(const __nv_bfloat16* __restrict__ x, int64_t ldx, int tokens,
+                                                        int n, __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  __shared__ __nv_bfloat16 tile[32][34];
+  const int t0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  #pragma unroll
+  for (int r = ty; r < 32; r += 8) {
+    const int t = t0 + r, j = j0 + tx;
+    tile[r][tx] = (t < tokens && j < n) ? x[(int64_t)t * ldx + j] : __float2bfloat16(0.f);
+  }
+  __syncthreads();
+  #pragma unroll
+  for (int r = ty; r < 32; r += 8) {
+    const int j = j0 + r, t = t0 + tx;
+    if (j < n && t < tokens) out[(int64_t)j * ldo + t] = tile[tx][r];
+  }
+}
+
 // out[j] = beta * out[j] + alpha * sum_t X[t, j]: each CTA owns 32 columns; 8 row-partial sums per column
 // combined in a fixed order.
 template <typename T>
@@ -82,6 +101,16 @@ MPQ_API int mpq_split_tf32_t(const void* x, int dtype, int64_t ldx, int tokens, 
     k_split_tf32_t<__nv_bfloat16><<<grid, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)x, ldx, tokens, n,
                                                                           hi, lo, ldo);
   return launch_status("mpq_split_tf32_t");
+}
+
+MPQ_API int mpq_transpose_bf16(const void* x, int64_t ldx, int tokens, int n, void* out, int64_t ldo, void* stream) {
+  MPQ_CHECK_ARG(x && out, "mpq_transpose_bf16: null pointer");
+  MPQ_CHECK_ARG(tokens >= 0 && n >= 0 && ldx >= n && ldo >= tokens, "mpq_transpose_bf16: bad shape");
+  if (tokens == 0 || n == 0) return MPQ_OK;
+  dim3 grid((tokens + 31) / 32, (n + 31) / 32);
+  k_transpose_bf16<<<grid, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)x, ldx, tokens, n,
+                                                          (__nv_bfloat16*)out, ldo);
+  return launch_status("mpq_transpose_bf16");
 }
 
 MPQ_API int mpq_col_sum(const void* x, int dtype, int64_t ldx, int tokens, int n, float alpha, float beta, float* out,

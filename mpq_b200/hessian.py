@@ -10,8 +10,8 @@ The MPQ drivers consume Hessians collected by third-party forward hooks (not par
   mpq/adapters/gptqmodel.py:650-679).
 
 Both are restated here from their published sources; their parity is unpinned (the code is absent from
-the reference tree).  Activations may be float32 (3xTF32: FP32-faithful) or bfloat16 (exact in TF32, so
-one TF32 product is exact up to the FP32 accumulation).
+the reference tree).  Activations may be float32 (3xTF32: FP32-faithful) or bfloat16 (bf16 tensor-core products,
+exact up to the FP32 accumulation).
 """
 from __future__ import annotations
 
@@ -48,6 +48,7 @@ class _Split:
 
 
 _split_cache: dict = {}
+_bf16_cache: dict = {}
 
 # The tensor core's FP32 accumulator does not round to nearest (its error grows with the K extent of one
 # product: 1.7e-5 relative low after 4100 tokens).  Each symmetric product covers at most CHUNK_TOKENS
@@ -71,10 +72,23 @@ def accumulate_xtx(H: torch.Tensor, x: torch.Tensor, *, alpha: float = 1.0, beta
             H.mul_(beta)
         return H
     key = (H.device.type, H.device.index)
+    st = ptr(ops.status_word(H.device))
+    if dtype == 1:  # bf16 activations: exact bf16 operands on the kind::f16 tensor-core path
+        ld = (T + 7) // 8 * 8
+        XT = _bf16_cache.get(key)
+        if XT is None or XT.shape[0] != n or XT.shape[1] < ld:
+            XT = _bf16_cache[key] = torch.empty(n, ld, device=H.device, dtype=torch.bfloat16)
+        ld = XT.stride(0)
+        call("mpq_transpose_bf16", ptr(X), X.stride(0), T, n, ptr(XT), ld)
+        for t0 in range(0, T, CHUNK_TOKENS):
+            kc = min(CHUNK_TOKENS, T - t0)
+            last = t0 + CHUNK_TOKENS >= T
+            call("mpq_syrk_bf16", n, kc, float(alpha), ptr(XT[:, t0:]), ld, float(beta) if t0 == 0 else 1.0, ptr(H),
+                 H.stride(0), 1 if last else 0, st)
+        return H
     sp = _split_cache.setdefault(key, _Split())
     hi, lo, ld = sp.get(n, T, H.device, need_lo=(dtype == 0))
     call("mpq_split_tf32_t", ptr(X), dtype, X.stride(0), T, n, ptr(hi), ptr(lo), ld)
-    st = ptr(ops.status_word(H.device))
     for t0 in range(0, T, CHUNK_TOKENS):  # hi/lo columns t0.. are the chunk's tokens (16-byte aligned)
         kc = min(CHUNK_TOKENS, T - t0)
         h = hi[:, t0:]

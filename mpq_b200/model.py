@@ -111,6 +111,10 @@ class _Timer:
         return _Ctx()
 
 
+class _StopForward(Exception):
+    """Raised by the last Hessian hook of a subset: the rest of the layer's forward is not needed."""
+
+
 def _forward_layer(layer, hidden, out, bs, mask, pos_emb, pos_ids):
     for b0 in range(0, hidden.shape[0], bs):
         o = layer(hidden[b0:b0 + bs], attention_mask=mask, position_embeddings=pos_emb, position_ids=pos_ids)
@@ -161,6 +165,8 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
             sums: Dict[str, torch.Tensor] = {}
             counts: Dict[str, int] = {}
 
+            last_reader = list(readers.values())[-1]
+
             def make_hook(name):
                 def hook(mod, args):
                     x = args[0]
@@ -170,11 +176,18 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
                         counts[name] = 0
                     accumulate_xtx(S, x, alpha=1.0, beta=1.0)
                     counts[name] += int(x.shape[0]) if x.dim() == 3 else 1  # GPTQ counts leading-dim samples
+                    if name == last_reader:
+                        raise _StopForward()
                 return hook
 
             handles = [mods[name].register_forward_pre_hook(make_hook(name)) for name in readers.values()]
             with timer("forward_hessian"):
-                _forward_layer(layer, hidden, None, int(cfg.batch_size), mask, pos_emb, pos_ids)
+                for b0 in range(0, hidden.shape[0], int(cfg.batch_size)):
+                    try:
+                        layer(hidden[b0:b0 + int(cfg.batch_size)], attention_mask=mask, position_embeddings=pos_emb,
+                              position_ids=pos_ids)
+                    except _StopForward:
+                        pass
             for h in handles:
                 h.remove()
             Hs: Dict[str, torch.Tensor] = {}

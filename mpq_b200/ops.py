@@ -88,16 +88,16 @@ def mean_rows(a: torch.Tensor, c: Optional[torch.Tensor] = None, out: Optional[t
 
 import ctypes as _ct
 
-_PRECISION = "tf32x3"
+_PRECISION = "f16x3"
 _scratch = {}
 _status = {}
 
 
 def set_gemm_precision(mode: str) -> None:
-    """'tf32x3' (FP32-faithful split products, default), 'tf32' (single TF32 product) or 'fp32'
-    (CUDA-core FP32 kernel)."""
+    """'tf32x3' (FP32-faithful 3xTF32 split products), 'f16x3' (FP32-faithful row-scaled 3xFP16 split products on the
+    fp16 tensor cores, twice the TF32 rate), 'tf32' (single TF32 product) or 'fp32' (CUDA-core FP32 kernel)."""
     global _PRECISION
-    if mode not in ("tf32x3", "tf32", "fp32"):
+    if mode not in ("tf32x3", "f16x3", "tf32", "fp32"):
         raise ValueError(f"unknown GEMM precision {mode!r}")
     _PRECISION = mode
 
@@ -139,15 +139,31 @@ def split_tf32(x: torch.Tensor, hi: Optional[torch.Tensor] = None, lo: Optional[
     return hi, lo
 
 
+def split_f16(x: torch.Tensor, bufs=None):
+    """Row-scaled fp16 split: hi = fp16(x s), lo = fp16(x s - hi) with s = 2^(15 - E), max|x_row| < 2^E;
+    returns (hi, lo, 1 / s) with hi / lo row-major, leading dimension a multiple of 8."""
+    rows, cols = x.shape
+    if bufs is None:
+        ld = (cols + 7) // 8 * 8
+        hi = torch.empty(rows, ld, device=x.device, dtype=torch.float16)
+        bufs = (hi, torch.empty_like(hi), torch.empty(rows, device=x.device, dtype=torch.float32))
+    hi, lo, inv = bufs
+    call("mpq_split_f16", ptr(x), x.stride(0), rows, cols, ptr(hi), ptr(lo), hi.stride(0), ptr(inv))
+    return hi, lo, inv
+
+
 class Operand:
-    """A row-major K-major matrix used as the B side of repeated products, with its TF32 split."""
+    """A row-major K-major matrix used as the B side of repeated products, with its split for the precision."""
 
     def __init__(self, t: torch.Tensor, precision: Optional[str] = None):
         self.full = t
         self.precision = precision or _PRECISION
         self.hi = self.lo = None
+        self.f16 = None
         if self.precision == "tf32x3" and _tma_ok(t):
             self.hi, self.lo = split_tf32(t)
+        elif self.precision == "f16x3" and t.dim() == 2 and t.dtype == torch.float32:
+            self.f16 = split_f16(t)
 
     @property
     def shape(self):
@@ -164,6 +180,17 @@ def _scratch_split(A: torch.Tensor):
     return split_tf32(A, buf[0], buf[1])
 
 
+def _scratch_split16(A: torch.Tensor):
+    key = ("f16", A.device.index, tuple(A.shape))
+    buf = _scratch.get(key)
+    if buf is None:
+        ld = (A.shape[1] + 7) // 8 * 8
+        hi = torch.empty(A.shape[0], ld, device=A.device, dtype=torch.float16)
+        buf = (hi, torch.empty_like(hi), torch.empty(A.shape[0], device=A.device, dtype=torch.float32))
+        _scratch[key] = buf
+    return split_f16(A, buf)
+
+
 def mm_nt(A: torch.Tensor, B, out: Optional[torch.Tensor] = None, *, alpha: float = 1.0, beta: float = 0.0,
           precision: Optional[str] = None) -> torch.Tensor:
     """C = alpha * A @ B^T + beta * C on the tensor cores.  B: Operand or (N x K) tensor."""
@@ -176,6 +203,17 @@ def mm_nt(A: torch.Tensor, B, out: Optional[torch.Tensor] = None, *, alpha: floa
         raise ValueError(f"mm_nt shape mismatch {tuple(A.shape)} x {tuple(B.full.shape)}^T")
     if out is None:
         out = torch.empty(M, N, device=A.device, dtype=torch.float32)
+    if prec == "f16x3" and B.f16 is None:
+        B = Operand(B.full, "f16x3")
+    if prec == "f16x3" and A.dtype == torch.float32 and A.stride(-1) == 1:
+        Ah, Al, Ai = _scratch_split16(A)
+        Bh, Bl, Bi = B.f16
+        st = status_word(A.device)
+        tok = trace.begin_timing("gemm_tc")
+        call("mpq_gemm_f16x3", M, N, K, float(alpha), ptr(Ah), ptr(Al), Ah.stride(0), ptr(Ai), ptr(Bh), ptr(Bl),
+             Bh.stride(0), ptr(Bi), float(beta), ptr(out), out.stride(0), ptr(st))
+        trace.end_timing("gemm_tc", tok, 2.0 * M * N * K)
+        return out
     if prec == "fp32" or not (_tma_ok(A) and _tma_ok(B.full) and (prec != "tf32x3" or B.hi is not None)):
         return gemm_nt(A, B.full, out, alpha=alpha, beta=beta)
     if prec == "tf32x3":
