@@ -367,8 +367,8 @@ def run_mpq(args):
 # DRAM traffic per launch of the dominant kernels, from ncu captures (dram__bytes_read.sum +
 # dram__bytes_write.sum); the summaries with their commands are under profiles/.
 TRAFFIC = {
-    # k_gemm_tc, one 4096 x 4096 x 4096 3xTF32 product (profiles/k_gemm_tc_4096.md)
-    "gemm_tc": {"bytes": 1.012e9 + 0.062e9, "launch": "4096x4096x4096 3xTF32 product"},
+    # k_gemm_tc, one 4096 x 4096 x 4096 3xFP16 product (profiles/k_gemm_tc_4096.md)
+    "gemm_tc": {"bytes": 3.545e8 + 0.564e8, "launch": "4096x4096x4096 f16x3 product"},
     # k_e8p12<1>, 4096 rows x 512 blocks (profiles/k_e8p12_posterior.md)
     "e8p12_mmse": {"bytes": 1.440e8 + 0.426e8, "launch": "4096 rows x 512 blocks"},
 }
@@ -382,10 +382,11 @@ def dominant_roofline(name, dom, peaks, steps):
     if name == "gemm_tc":
         peak = float(peaks.get("bf16_tflops_sustained", 1394.3))
         achieved = dom["work_avg"] / secs / 1e12 if secs > 0 else 0.0
-        return {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 3xTF32 rank-space products)", "achieved": achieved,
-                "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+        return {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 FP32-faithful split rank-space products)",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (measured)" if peaks else "fallback",
-                "achieved_counts": "algorithmic 2MNK per product (3xTF32 issues 3 TF32 MMAs per FLOP)", **common}
+                "achieved_counts": "algorithmic 2MNK per product (the f16x3 split issues 3 fp16 MMAs per FLOP, so "
+                                   "its ceiling is 1/3 of the dense fp16/bf16 peak)", **common}
     peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = dom["work_avg"] / secs / 1e9 if secs > 0 else 0.0
     return {"bound": "hbm", "kernel": "k_e8p12<1> (E8P12 factorized posterior)", "achieved": achieved, "peak": peak,
