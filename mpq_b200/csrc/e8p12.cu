@@ -119,13 +119,14 @@ __device__ __forceinline__ void comp_terms(const ItemTab& T, int br, int ai, uin
   }
   const bool negp = (sx >> 31) != 0u;
   const float cst = fmul(ng, fadd(ynorm_br, sqn));
-  // float32 library functions: the only ill-conditioned term, 1 - |prod| for |prod| near 1, belongs to
-  // parity-mismatched components whose log-partition lies ~14 nats below their bound (the reference's tanh
-  // clamp), so its rounding moves the posterior by ~1e-7 relative.
-  const float pabs = expf(lpt);
+  // Hardware exp2/log2 approximations (relative error ~2^-21): a component's log-weight lc is O(10^2-10^3) in
+  // magnitude, so its own float32 rounding (~1e-5) exceeds their error.  The only ill-conditioned term,
+  // 1 - |prod| for |prod| near 1, is evaluated through expm1f and belongs to parity-mismatched components whose
+  // log-partition lies ~14 nats below their bound (the reference's tanh clamp).
+  const float pabs = __expf(lpt);
   o.prod = negp ? -pabs : pabs;
-  const float lae = log1pf(pabs);  // logaddexp(0, lpt), lpt <= 0
-  const float l1me = lpt < -kLn2 ? log1pf(-pabs) : logf(-expm1f(lpt));  // log(1 - exp(lpt))
+  const float lae = __logf(1.f + pabs);  // logaddexp(0, lpt), lpt <= 0: 1 + pabs in (1, 2]
+  const float l1me = lpt < -kLn2 ? __logf(1.f - pabs) : __logf(-expm1f(lpt));  // log(1 - exp(lpt))
   const float lop = negp ? l1me : lae;  // log(1 + prod)
   const float lom = negp ? lae : l1me;  // log(1 - prod)
   o.even = parity == 0;
@@ -355,7 +356,7 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
             for (int i = 0; i < 8; ++i) MU[i] *= sc;
             mx = lc;
           }
-          const float w = expf(lc - mx);
+          const float w = __expf(lc - mx);  // lc - mx in [-kPrune - margin, 0]
           float de = 1.f + prod, dodd = 1.f - prod;
           if (!(fabsf(de) > 1e-12f)) de = 1.f;
           if (!(fabsf(dodd) > 1e-12f)) dodd = 1.f;
