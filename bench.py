@@ -38,6 +38,9 @@ N_COLS = 4096
 T_CALIB = 16384
 METRIC = "s per 4096^2 layer solve (VAMP+3 CD)"
 WORKLOAD_DESC = {
+    "model_e8": "config 3: Llama-3.2-1B-shaped decoder, random init, 128 x 2048 uniform-random calibration tokens, 2-bit "
+                "E8P12 with randomized Hadamard on both sides, VAMP 16 it + 3 gram-CD sweeps, QUIP#-style float-model "
+                "Hessians; layers solved round-robin over GPUs",
     "hessian": "calibration Hessian H = X^T X / T on the tensor cores (token-major activations X, T x n)",
     "model": "config 4: Llama-3-8B-shaped decoder, random init, 128 x 2048 uniform-random calibration tokens, 3-bit g128, "
              "internal Hadamard, VAMP 20 it + 3 CD sweeps, GPTQ sequential layer walk; rows of every linear sharded over GPUs",
@@ -475,7 +478,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    if args.workload == "model":
+    if args.workload in ("model", "model_e8"):
         return {"impl": "reference", "unavailable": "the whole-model CPU run (about 46 h for the 8B shape) is not "
                 "timed; the per-layer CPU baseline is the --workload e8p12 / scalar reference arm"}
     vals, info = [], None
@@ -510,7 +513,9 @@ def run_model(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=dev)
     layers = args.model_layers if args.model_layers > 0 else None
-    model = build_synthetic_decoder(args.model, device=dev, seed=0, num_layers=layers)
+    e8 = args.workload == "model_e8"
+    name = ("llama32_1b" if args.model == "llama3_8b" else args.model) if e8 else args.model
+    model = build_synthetic_decoder(name, device=dev, seed=0, num_layers=layers)
     ids = calibration_ids(args.calib_seqs, args.seq_len, model.config.vocab_size, seed=0)
     cfg = ModelQuantConfig(bits=args.bits, group_size=128, iters=20, prior_tau=0.2, damping=0.5, polish_sweeps=3)
     clocks = ClockSampler(local, enabled=not args.no_clocks)
@@ -519,7 +524,12 @@ def run_model(args):
     torch.cuda.synchronize()
     launches0 = trace.launches()
     t0 = time.perf_counter()
-    out = quantize_model(model, ids, cfg)
+    if e8:
+        from mpq_b200.model import QuipModelConfig, quantize_model_quip
+        out = quantize_model_quip(model, ids, QuipModelConfig(iters=16, prior_tau=0.25, polish_sweeps=3,
+                                                               keep_attrs=False))
+    else:
+        out = quantize_model(model, ids, cfg)
     torch.cuda.synchronize()
     secs = time.perf_counter() - t0
     clk = clocks.stop()
@@ -528,7 +538,18 @@ def run_model(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         secs = float(t.item())
     res = None
-    if rank == 0:
+    if rank == 0 and e8:
+        groups = out["groups"]
+        res = {"metric": f"s per {name}-shape full-model quantization", "value": secs, "unit": "s", "n_gpus": world,
+               "steps": 1, "warmup": 0, "ms_per_step": secs * 1e3, "higher_is_better": False, "scaling": "strong",
+               "vs_baseline": None, "dtype": "f32 solve / bf16 model", "data": "synthetic",
+               "config": {"workload": WORKLOAD_DESC["model_e8"], "model": name,
+                          "layers": model.config.num_hidden_layers, "calibration": [args.calib_seqs, args.seq_len],
+                          "parallelism": f"layers{world}+calib{world}"},
+               "timings_rank0_s": out["timings"], "gpu_launches": trace.launches() - launches0, "clocks": clk,
+               "groups": len(groups),
+               "proxy_error_mean": float(np.mean([g["proxy_error"] for g in groups.values()]))}
+    elif rank == 0:
         mods = out["modules"]
         res = {"metric": f"s per {args.model}-shape full-model quantization", "value": secs, "unit": "s",
                "n_gpus": world, "steps": 1, "warmup": 0, "ms_per_step": secs * 1e3, "higher_is_better": False,
@@ -587,7 +608,7 @@ def main():
     args = parse()
     if args.impl == "reference":
         res = run_reference(args)
-    elif args.workload == "model":
+    elif args.workload in ("model", "model_e8"):
         res = run_model(args)
     elif args.workload == "hessian":
         res = run_hessian(args)

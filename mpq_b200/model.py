@@ -255,3 +255,134 @@ def _input_owner(layer, name: str):
     if name in ("mlp.gate_proj", "mlp.up_proj"):
         return layer.post_attention_layernorm
     return layer.get_submodule(name)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# QUIP#-style E8P12 walk (mpq/quip_generic.py): Hessians from the float model, fused projection groups,
+# randomized Hadamard incoherence on both sides, mpq_refine_codebook per group, checkpoint attribute dicts.
+# ------------------------------------------------------------------------------------------------------------------
+
+QUIP_GROUPS = (("qkv", ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj")), ("o", ("self_attn.o_proj",)),
+               ("up", ("mlp.up_proj", "mlp.gate_proj")), ("down", ("mlp.down_proj",)))
+
+
+@dataclass
+class QuipModelConfig:
+    iters: int = 16
+    prior_tau: float = 0.25
+    polish_sweeps: int = 3
+    sigma_reg: float = 1e-2
+    seed: int = 0
+    batch_size: int = 8
+    write_back: bool = True      # replace the float weights by the dequantized E8P12 weights
+    keep_attrs: bool = True      # keep the per-group checkpoint attributes (on the host)
+
+
+@torch.inference_mode()
+def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *, group=None) -> Dict[str, Any]:
+    """E8P12 quantization of every decoder layer (2 bits per weight), QUIP#-style.
+
+    Hessians: one float forward per layer with QUIP# hooks (sum x^T x, sum x, token count) on the inputs of
+    q (the fused qkv), o, up (the fused up+gate) and down, finalised as H / ct - mu mu^T and re-centred to the
+    second moment H / ct (mpq/quip_generic.py:906-918, 373-375), then regularize_H (sigma_reg, :378).  Each group
+    W = vstack(w_i / rms(w_i)) gets random sign vectors SU, SV (seeded by the group's name), a two-sided block
+    Hadamard, unit RMS scaling and mpq_refine_codebook (RTN init, VAMP, gram-metric CD).  With N ranks the
+    calibration sequences are split across ranks (partial sums all-reduced) and layer l's groups are solved on
+    rank l mod N; the attributes are gathered on rank 0.  The packed Qidxs layout of QUIP#'s decode kernels is
+    QUIP#'s own (not part of the reference tree): Qidxs are kept unpacked (int16, rows x cols / 8)."""
+    from .adapters.quip_sharp import mpq_refine_codebook
+    from .codebook import E8P12_codebook
+    from .hessian import HessianAccumulator, regularize_H
+    from .rotation import rht_hessian, rht_weight, rht_weight_inverse, sample_rademacher_signs
+    rank, world = _world(group)
+    dev = next(model.parameters()).device
+    timer = _Timer(dev)
+    t_start = time.perf_counter()
+    cb = E8P12_codebook()
+    inner = model.model
+    n_seq, seq_len = calib_ids.shape
+    s0, s1 = row_shards(n_seq, world, 1)[rank]
+    with timer("embed"):
+        hidden = inner.embed_tokens(calib_ids[s0:s1].to(dev))
+        nxt = torch.empty_like(hidden)
+    pos_ids = torch.arange(seq_len, device=dev)[None]
+    pos_emb = inner.rotary_emb(hidden[:1], position_ids=pos_ids)
+    args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=int(cfg.iters), mpq_prior_tau=float(cfg.prior_tau),
+                                 mpq_polish_sweeps=int(cfg.polish_sweeps), mpq_block_rows=1 << 30,
+                                 quant_solver="vamp", quant_polish_mode="block_cd", mpq_polish_metric="gram",
+                                 seed=int(cfg.seed))
+    attrs: Dict[str, Any] = {}
+    for li in range(len(inner.layers)):
+        layer = inner.layers[li]
+        accs = {name: HessianAccumulator(layer.get_submodule(mods[0]).in_features, device=dev, mode="quip")
+                for name, mods in QUIP_GROUPS}
+        handles = [layer.get_submodule(mods[0]).register_forward_pre_hook(
+            (lambda acc: (lambda mod, a: acc.add_batch(a[0])))(accs[name])) for name, mods in QUIP_GROUPS]
+        with timer("forward_hessian"):  # float activations feed both the Hessians and the next layer
+            _forward_layer(layer, hidden, nxt, int(cfg.batch_size), None, pos_emb, pos_ids)
+        for h in handles:
+            h.remove()
+        with timer("hessian_reduce"):
+            Hs = {}
+            for name, acc in accs.items():
+                S, mu = acc.H, acc.mu
+                ct = torch.tensor([float(acc.ct)], device=dev, dtype=torch.float64)
+                if world > 1:
+                    dist.all_reduce(S, group=group)
+                    dist.all_reduce(mu, group=group)
+                    dist.all_reduce(ct, group=group)
+                H = S / float(ct.item())  # = (H / ct - mu mu^T) + mu mu^T with mu = sum x / ct
+                Hs[name] = regularize_H(H, H.shape[0], float(cfg.sigma_reg))
+            del accs
+        owner = li % world
+        for name, mods in QUIP_GROUPS:
+            key = f"{li}_{name}"
+            if rank != owner:
+                continue
+            with timer("solve"):
+                ws = [layer.get_submodule(m).weight.to(torch.float32) for m in mods]
+                scales = [float(w.square().mean().sqrt().item()) for w in ws]
+                W = torch.cat([w / s for w, s in zip(ws, scales)], dim=0).contiguous()
+                m, n = W.shape
+                SU = sample_rademacher_signs(width=m, key=f"{key}:SU", seed=int(cfg.seed), device=dev)
+                SV = sample_rademacher_signs(width=n, key=f"{key}:SV", seed=int(cfg.seed), device=dev)
+                Wr = rht_weight(W, SU, SV, m & -m, n & -n)
+                Hr = rht_hessian(Hs[name], SV, n & -n)
+                wscale = float(Wr.square().mean().sqrt().item())
+                Wn = (Wr / wscale).contiguous()
+                hat, idx, st = mpq_refine_codebook(Wn, Hr, Wn, torch.zeros(m, n // 8, dtype=torch.int64, device=dev),
+                                                   cb, args, module_name=key)
+                hatW = rht_weight_inverse(hat * wscale, SU, SV, m & -m, n & -n)
+                if cfg.write_back:
+                    r0 = 0
+                    for mod_name, w, sc in zip(mods, ws, scales):
+                        rows = w.shape[0]
+                        layer.get_submodule(mod_name).weight.copy_((hatW[r0:r0 + rows] * sc).to(w.dtype))
+                        r0 += rows
+                diff = hatW - W
+                err_proxy = float(((diff @ Hs[name]) * diff).sum().item() / max(((W @ Hs[name]) * W).sum().abs().item(),
+                                                                                   1e-12))
+                entry = {"fused": len(mods) > 1, "shapes": [tuple(w.shape) for w in ws], "scales": scales,
+                         "proxy_error": err_proxy, "surrogate_before": st["exact_surrogate_before_mean"],
+                         "surrogate_after": st["exact_surrogate_after_mean"]}
+                if cfg.keep_attrs:
+                    entry.update(Qidxs=idx.to(torch.int16).cpu(), SU=SU.to(torch.float16).cpu(),
+                                 SV=(SV * wscale).to(torch.float16).cpu())
+                attrs[key] = entry
+        if world > 1 and cfg.write_back:
+            with timer("gather"):  # every rank holds the quantized layer (the owner's weights)
+                for _, mods in QUIP_GROUPS:
+                    for mod_name in mods:
+                        dist.broadcast(layer.get_submodule(mod_name).weight, owner, group=group)
+        hidden, nxt = nxt, hidden
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, {k: {kk: vv for kk, vv in v.items() if not torch.is_tensor(vv)}
+                                          for k, v in attrs.items()}, group=group)
+        if rank == 0:
+            for part in gathered:
+                for k, v in part.items():
+                    attrs.setdefault(k, v)
+    ops.check_status(dev)
+    torch.cuda.synchronize(dev)
+    return {"groups": attrs, "timings": dict(timer.acc), "seconds": time.perf_counter() - t_start}

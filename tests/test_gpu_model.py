@@ -37,3 +37,25 @@ def test_quantize_tiny_llama(cuda_dev):
     rel = (logits - ref_logits).norm() / ref_logits.norm()
     assert rel < 0.5, rel
     assert set(out["timings"]) >= {"forward_hessian", "solve", "forward_out"}
+
+
+@pytest.mark.gpu
+def test_quantize_tiny_llama_e8p12(cuda_dev):
+    from mpq_b200.model import QuipModelConfig, build_synthetic_decoder, calibration_ids, quantize_model_quip
+    model = build_synthetic_decoder("tiny_llama", device=cuda_dev, seed=0)
+    ids = calibration_ids(8, 64, model.config.vocab_size, seed=2)
+    cfg = QuipModelConfig(iters=6, polish_sweeps=1, batch_size=4)
+    out = quantize_model_quip(model, ids, cfg)
+    groups = out["groups"]
+    assert sorted(groups) == sorted(f"{l}_{g}" for l in range(2) for g in ("qkv", "o", "up", "down"))
+    for key, g in groups.items():
+        rows = sum(s[0] for s in g["shapes"])
+        cols = g["shapes"][0][1]
+        assert g["Qidxs"].shape == (rows, cols // 8) and g["Qidxs"].dtype == torch.int16
+        assert g["SU"].shape == (rows,) and g["SV"].shape == (cols,)
+        assert g["surrogate_after"] <= g["surrogate_before"] * (1 + 1e-6), key
+        assert g["proxy_error"] < 0.5, key
+        assert g["fused"] == (len(g["shapes"]) > 1)
+    with torch.inference_mode():
+        logits = model(ids[:2].to(cuda_dev)).logits.float()
+    assert torch.isfinite(logits).all()
