@@ -106,6 +106,88 @@ struct Maps {
 // one 128-byte swizzle row per operand row (32 fp32 or 64 16-bit elements) and 4 MMAs of 32 bytes.
 // sym: 0 general product; 1 symmetric (tiles with col <= row, entries stored with their mirrors); 2 symmetric,
 // lower triangle only (intermediate accumulation steps).
+// One 32-column chunk of a thread's accumulator row -> C (alpha, beta, split row scales, symmetric modes).
+__device__ __forceinline__ void store_chunk(uint32_t (&v)[32], int row, int n0, int c0, int M, int N, float alpha,
+                                            float beta, float* __restrict__ C, int64_t ldc, int sym,
+                                            const float* __restrict__ sa, const float* __restrict__ sb) {
+  if (sa) {  // power-of-two row scales of the fp16 split: exact unless the result over/underflows
+    const float ra = sa[row < M ? row : 0];
+    #pragma unroll
+    for (int t = 0; t < 32; ++t) {
+      const int col = n0 + c0 + t;
+      v[t] = __float_as_uint(__uint_as_float(v[t]) * (ra * (col < N ? sb[col] : 0.f)));
+    }
+  }
+  if (sym) {
+    // lower entries (col <= row) and their mirrors: the result is exactly symmetric.  Chunks entirely below
+    // the diagonal use 16-byte row stores per thread; the mirror stores of a warp (32 consecutive rows, one
+    // column) are contiguous.
+    const int cb = n0 + c0;
+    float* crow = C + (int64_t)row * ldc + cb;
+    if (row < M && cb + 31 < row && cb + 32 <= N && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
+      #pragma unroll
+      for (int t = 0; t < 32; t += 4) {
+        float4 o;
+        o.x = alpha * __uint_as_float(v[t]);
+        o.y = alpha * __uint_as_float(v[t + 1]);
+        o.z = alpha * __uint_as_float(v[t + 2]);
+        o.w = alpha * __uint_as_float(v[t + 3]);
+        float4* dst = reinterpret_cast<float4*>(crow + t);
+        if (beta != 0.f) {
+          const float4 c = *dst;
+          o.x += beta * c.x; o.y += beta * c.y; o.z += beta * c.z; o.w += beta * c.w;
+        }
+        *dst = o;
+        if (sym == 1) {
+          C[(int64_t)(cb + t) * ldc + row] = o.x;
+          C[(int64_t)(cb + t + 1) * ldc + row] = o.y;
+          C[(int64_t)(cb + t + 2) * ldc + row] = o.z;
+          C[(int64_t)(cb + t + 3) * ldc + row] = o.w;
+        }
+      }
+    } else if (row < M) {
+      #pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        const int col = cb + t;
+        if (col < N && col <= row) {
+          float o = alpha * __uint_as_float(v[t]);
+          if (beta != 0.f) o += beta * C[(int64_t)row * ldc + col];
+          C[(int64_t)row * ldc + col] = o;
+          if (col != row && sym == 1) C[(int64_t)col * ldc + row] = o;
+        }
+      }
+    }
+  } else if (row < M) {
+    float* crow = C + (int64_t)row * ldc + n0 + c0;
+    const int ncol = min(32, N - (n0 + c0));
+    if (ncol == 32 && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
+      #pragma unroll
+      for (int t = 0; t < 32; t += 4) {
+        float4 o;
+        o.x = alpha * __uint_as_float(v[t]);
+        o.y = alpha * __uint_as_float(v[t + 1]);
+        o.z = alpha * __uint_as_float(v[t + 2]);
+        o.w = alpha * __uint_as_float(v[t + 3]);
+        float4* dst = reinterpret_cast<float4*>(crow + t);
+        if (beta != 0.f) {
+          const float4 c = *dst;
+          o.x += beta * c.x; o.y += beta * c.y; o.z += beta * c.z; o.w += beta * c.w;
+        }
+        *dst = o;
+      }
+    } else {
+      #pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        if (t < ncol) {
+          float o = alpha * __uint_as_float(v[t]);
+          if (beta != 0.f) o += beta * crow[t];
+          crow[t] = o;
+        }
+      }
+    }
+  }
+}
+
 // KIND 0: fp32 operands, kind::tf32; 1: bf16, kind::f16; 2: fp16, kind::f16.  sa / sb (optional, with KIND 2): per-row
 // scales of A's rows and of B's rows applied to the accumulator (the row-scaled fp16 split).
 template <int BN, int STAGES, int KIND>
@@ -200,12 +282,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t da = smem_desc_k_sw128(a_addr + j * 32);
           const uint64_t db = smem_desc_k_sw128(b_addr + j * 32);
           const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-          asm volatile(
-              "{\n\t.reg .pred p;\n\t"
-              "setp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-              "l"(da), "l"(db), "r"(kIdesc), "r"(acc)
-              : "memory");
+          if constexpr (BF16) {  // 16-bit operands (bf16 or fp16, as the instruction descriptor says)
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+                "l"(da), "l"(db), "r"(kIdesc), "r"(acc)
+                : "memory");
+          } else {
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+                "l"(da), "l"(db), "r"(kIdesc), "r"(acc)
+                : "memory");
+          }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                          smem_u32(&empty[s]))
@@ -240,82 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (sa) {  // power-of-two row scales of the fp16 split: exact unless the result over/underflows
-          const float ra = sa[row < M ? row : 0];
-          #pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const int col = n0 + c0 + t;
-            v[t] = __float_as_uint(__uint_as_float(v[t]) * (ra * (col < N ? sb[col] : 0.f)));
-          }
-        }
-        if (sym) {
-          // lower entries (col <= row) and their mirrors: the result is exactly symmetric.  Chunks entirely below
-          // the diagonal use 16-byte row stores per thread; the mirror stores of a warp (32 consecutive rows, one
-          // column) are contiguous.
-          const int cb = n0 + c0;
-          float* crow = C + (int64_t)row * ldc + cb;
-          if (row < M && cb + 31 < row && cb + 32 <= N && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
-            #pragma unroll
-            for (int t = 0; t < 32; t += 4) {
-              float4 o;
-              o.x = alpha * __uint_as_float(v[t]);
-              o.y = alpha * __uint_as_float(v[t + 1]);
-              o.z = alpha * __uint_as_float(v[t + 2]);
-              o.w = alpha * __uint_as_float(v[t + 3]);
-              float4* dst = reinterpret_cast<float4*>(crow + t);
-              if (beta != 0.f) {
-                const float4 c = *dst;
-                o.x += beta * c.x; o.y += beta * c.y; o.z += beta * c.z; o.w += beta * c.w;
-              }
-              *dst = o;
-              if (sym == 1) {
-                C[(int64_t)(cb + t) * ldc + row] = o.x;
-                C[(int64_t)(cb + t + 1) * ldc + row] = o.y;
-                C[(int64_t)(cb + t + 2) * ldc + row] = o.z;
-                C[(int64_t)(cb + t + 3) * ldc + row] = o.w;
-              }
-            }
-          } else if (row < M) {
-            #pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              const int col = cb + t;
-              if (col < N && col <= row) {
-                float o = alpha * __uint_as_float(v[t]);
-                if (beta != 0.f) o += beta * C[(int64_t)row * ldc + col];
-                C[(int64_t)row * ldc + col] = o;
-                if (col != row && sym == 1) C[(int64_t)col * ldc + row] = o;
-              }
-            }
-          }
-        } else if (row < M) {
-          float* crow = C + (int64_t)row * ldc + n0 + c0;
-          const int ncol = min(32, N - (n0 + c0));
-          if (ncol == 32 && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
-            #pragma unroll
-            for (int t = 0; t < 32; t += 4) {
-              float4 o;
-              o.x = alpha * __uint_as_float(v[t]);
-              o.y = alpha * __uint_as_float(v[t + 1]);
-              o.z = alpha * __uint_as_float(v[t + 2]);
-              o.w = alpha * __uint_as_float(v[t + 3]);
-              float4* dst = reinterpret_cast<float4*>(crow + t);
-              if (beta != 0.f) {
-                const float4 c = *dst;
-                o.x += beta * c.x; o.y += beta * c.y; o.z += beta * c.z; o.w += beta * c.w;
-              }
-              *dst = o;
-            }
-          } else {
-            #pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              if (t < ncol) {
-                float o = alpha * __uint_as_float(v[t]);
-                if (beta != 0.f) o += beta * crow[t];
-                crow[t] = o;
-              }
-            }
-          }
-        }
+        store_chunk(v, row, n0, c0, M, N, alpha, beta, C, ldc, sym, sa, sb);
       }
     }
   }
@@ -324,6 +340,220 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN) : "memory");
+  }
+}
+
+// ---- persistent form: one CTA per SM walks a tile list; two TMEM accumulators (2 x BN = 512 columns) let the
+// epilogue of one tile overlap the MMAs of the next.  Roles as above; acc_full[b] is committed by the MMA thread when
+// buffer b holds a finished tile, acc_empty[b] collects one arrival per epilogue warp when it has been drained.
+// Symmetric products enumerate only the tiles holding entries col <= row.
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Tile t -> (m-block, n-block): row-major over the n-blocks of each m-block; with sym only n-blocks whose first
+// column is <= the m-block's last row.
+template <int BN>
+__device__ __forceinline__ void tile_coords(int t, int mt, int nt, int sym, int& mb, int& nb) {
+  if (!sym) {
+    mb = t / nt;
+    nb = t - mb * nt;
+    return;
+  }
+  mb = 0;
+  for (;; ++mb) {
+    const int cnt = min((mb * BM + BM - 1) / BN + 1, nt);
+    if (t < cnt || mb == mt - 1) break;
+    t -= cnt;
+  }
+  nb = t;
+}
+
+template <int BN, int STAGES, int KIND>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc_pt(const __grid_constant__ Maps maps, int nreg, int M, int N, int K, float alpha, float beta,
+                 float* __restrict__ C, int64_t ldc, int* __restrict__ status, int sym, const float* __restrict__ sa,
+                 const float* __restrict__ sb, int mt, int nt, int ntiles) {
+  constexpr bool B16 = KIND != 0;
+  constexpr uint32_t kStageA = BM * 128;
+  constexpr uint32_t kStageB = BN * 128;
+  constexpr int kBKE = B16 ? 64 : 32;
+  constexpr uint32_t kIdesc = KIND == 2 ? idesc_f16(BM, BN) : (KIND == 1 ? idesc_bf16(BM, BN) : idesc_tf32(BM, BN));
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = base;
+  unsigned char* sB = base + STAGES * kStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kStageB);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb_per_reg = (K + kBKE - 1) / kBKE;
+  const int total_kb = kb_per_reg * nreg;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)(2 * BN))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords<BN>(t, mt, nt, sym, mb, nb);
+        for (int kb = 0; kb < total_kb; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
+          if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          const int r = kb / kb_per_reg;
+          const int k0 = (kb % kb_per_reg) * kBKE;
+          mbar_expect_tx(&full[s], kStageA + kStageB);
+          tma_load_2d(sA + s * kStageA, &maps.a[r], &full[s], k0, mb * BM);
+          tma_load_2d(sB + s * kStageB, &maps.b[r], &full[s], k0, nb * BN);
+        }
+      }
+      if (!ok) {
+        // drain: wait (bounded) for the copies this thread issued into the ring
+        for (int q = g - STAGES < 0 ? 0 : g - STAGES; q < g; ++q) mbar_wait(&full[q % STAGES], (uint32_t)(q / STAGES) & 1u);
+        atomicCAS(status, 0, 2);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int g = 0, i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
+        const int b = i & 1;
+        const uint32_t use = (uint32_t)(i >> 1);
+        if (*abort_flag || !mbar_wait(&acc_empty[b], (use & 1u) ^ 1u)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t dacc = tmem + (uint32_t)(b * BN);
+        for (int kb = 0; kb < total_kb; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
+          if (*abort_flag || !mbar_wait(&full[s], ph)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(sA + s * kStageA);
+          const uint32_t b_addr = smem_u32(sB + s * kStageB);
+          #pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t da = smem_desc_k_sw128(a_addr + j * 32);
+            const uint64_t db = smem_desc_k_sw128(b_addr + j * 32);
+            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+            if constexpr (B16) {
+              asm volatile(
+                  "{\n\t.reg .pred p;\n\t"
+                  "setp.ne.b32 p, %4, 0;\n\t"
+                  "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dacc),
+                  "l"(da), "l"(db), "r"(kIdesc), "r"(acc)
+                  : "memory");
+            } else {
+              asm volatile(
+                  "{\n\t.reg .pred p;\n\t"
+                  "setp.ne.b32 p, %4, 0;\n\t"
+                  "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(dacc),
+                  "l"(da), "l"(db), "r"(kIdesc), "r"(acc)
+                  : "memory");
+            }
+          }
+          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                           smem_u32(&empty[s]))
+                       : "memory");
+        }
+        if (!ok) break;
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&acc_full[b]))
+                     : "memory");
+      }
+      // every MMA this thread issued has retired before teardown (bounded)
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(drain_bar))
+                   : "memory");
+      mbar_wait(drain_bar, 0);
+      if (!ok) atomicCAS(status, 0, 3);
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+    const int quad = warp & 3;
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      const uint32_t use = (uint32_t)(i >> 1);
+      if (*abort_flag) break;
+      if (!mbar_wait(&acc_full[b], use & 1u)) {
+        *abort_flag = 1;
+        atomicCAS(status, 0, 4);
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      int mb, nb;
+      tile_coords<BN>(t, mt, nt, sym, mb, nb);
+      const int row = mb * BM + quad * 32 + lane;
+      #pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN + c0), v);
+        store_chunk(v, row, nb * BN, c0, M, N, alpha, beta, C, ldc, sym, sa, sb);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN)) : "memory");
   }
 }
 
