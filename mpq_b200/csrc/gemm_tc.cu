@@ -17,6 +17,7 @@
 // `status`, drains its own in-flight copies / MMAs (bounded), frees TMEM and exits.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <cuda_fp16.h>
 #include "common.cuh"
 
@@ -24,7 +25,7 @@ namespace mpq {
 namespace tc {
 
 constexpr int BM = 128;
-constexpr int BK = 32;  // fp32 elements per k-block = 128 bytes = one 128B swizzle row (64 for bf16)
+// A k-block is one 128-byte swizzle row per operand row: 32 fp32 or 64 16-bit elements.
 constexpr int kThreads = 192;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
 
@@ -608,6 +609,42 @@ static int launch(const Maps& maps, int nreg, int M, int N, int K, float alpha, 
   return launch_status("mpq_gemm_tc");
 }
 
+static int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// Persistent launch: one CTA per SM (the ring and two TMEM accumulators need the whole SM) over the tile list.
+template <int BN, int STAGES, int KIND>
+static int launch_pt(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
+                     int* status, cudaStream_t stream, int sym = 0, const float* sa = nullptr, const float* sb = nullptr) {
+  const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * 128 + 256;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm_tc_pt<BN, STAGES, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+  int64_t ntiles = 0;
+  if (sym) {
+    for (int mb = 0; mb < mt; ++mb) ntiles += std::min((mb * BM + BM - 1) / BN + 1, nt);
+  } else {
+    ntiles = (int64_t)mt * nt;
+  }
+  if (ntiles == 0) return MPQ_OK;
+  const int grid = (int)std::min<int64_t>(ntiles, num_sms());
+  k_gemm_tc_pt<BN, STAGES, KIND><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status,
+                                                                    sym, sa, sb, mt, nt, (int)ntiles);
+  return launch_status("mpq_gemm_tc (persistent)");
+}
+
 }  // namespace tc
 }  // namespace mpq
 
@@ -684,7 +721,7 @@ MPQ_API int mpq_syrk_bf16(int n, int K, float alpha, const void* A, int64_t lda,
   if (st) return st;
   st = tc::make_map(&maps.b[0], A, n, K, lda, 256, 1);
   if (st) return st;
-  return tc::launch<256, 4, 1>(maps, 1, n, n, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, mirror ? 1 : 2);
+  return tc::launch_pt<256, 4, 1>(maps, 1, n, n, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, mirror ? 1 : 2);
 }
 
 // FP32-faithful product on the fp16 tensor cores: C = alpha sum_{(a,b) in (hi,hi),(hi,lo),(lo,hi)} diag(sa) A_a B_b^T diag(sb)
@@ -713,7 +750,7 @@ MPQ_API int mpq_gemm_f16x3(int M, int N, int K, float alpha, const void* a_hi, c
     st = tc::make_map(&maps.b[r], Bs[r], N, K, ldb, 256, 2);
     if (st) return st;
   }
-  return tc::launch<256, 4, 2>(maps, 3, M, N, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 0, sa, sb);
+  return tc::launch_pt<256, 4, 2>(maps, 3, M, N, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 0, sa, sb);
 }
 
 namespace mpq {
