@@ -287,8 +287,9 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
     second moment H / ct (mpq/quip_generic.py:906-918, 373-375), then regularize_H (sigma_reg, :378).  Each group
     W = vstack(w_i / rms(w_i)) gets random sign vectors SU, SV (seeded by the group's name), a two-sided block
     Hadamard, unit RMS scaling and mpq_refine_codebook (RTN init, VAMP, gram-metric CD).  With N ranks the
-    calibration sequences are split across ranks (partial sums all-reduced) and layer l's groups are solved on
-    rank l mod N; the attributes are gathered on rank 0.  The packed Qidxs layout of QUIP#'s decode kernels is
+    calibration sequences are split across ranks (partial sums all-reduced); all layers' Hessians are collected
+    first, then layer l's groups are solved on rank l mod N concurrently, the owners broadcast the quantized weights
+    and the attributes are gathered on rank 0.  The packed Qidxs layout of QUIP#'s decode kernels is
     QUIP#'s own (not part of the reference tree): Qidxs are kept unpacked (int16, rows x cols / 8)."""
     from .adapters.quip_sharp import mpq_refine_codebook
     from .codebook import E8P12_codebook
@@ -312,18 +313,20 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                                  quant_solver="vamp", quant_polish_mode="block_cd", mpq_polish_metric="gram",
                                  seed=int(cfg.seed))
     attrs: Dict[str, Any] = {}
-    for li in range(len(inner.layers)):
+    nl = len(inner.layers)
+    # phase 1: every layer's Hessians from the float model (float activations feed the next layer)
+    Hs_all: Dict[Tuple[int, str], torch.Tensor] = {}
+    for li in range(nl):
         layer = inner.layers[li]
         accs = {name: HessianAccumulator(layer.get_submodule(mods[0]).in_features, device=dev, mode="quip")
                 for name, mods in QUIP_GROUPS}
         handles = [layer.get_submodule(mods[0]).register_forward_pre_hook(
             (lambda acc: (lambda mod, a: acc.add_batch(a[0])))(accs[name])) for name, mods in QUIP_GROUPS]
-        with timer("forward_hessian"):  # float activations feed both the Hessians and the next layer
+        with timer("forward_hessian"):
             _forward_layer(layer, hidden, nxt, int(cfg.batch_size), None, pos_emb, pos_ids)
         for h in handles:
             h.remove()
         with timer("hessian_reduce"):
-            Hs = {}
             for name, acc in accs.items():
                 S, mu = acc.H, acc.mu
                 ct = torch.tensor([float(acc.ct)], device=dev, dtype=torch.float64)
@@ -332,14 +335,19 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                     dist.all_reduce(mu, group=group)
                     dist.all_reduce(ct, group=group)
                 H = S / float(ct.item())  # = (H / ct - mu mu^T) + mu mu^T with mu = sum x / ct
-                Hs[name] = regularize_H(H, H.shape[0], float(cfg.sigma_reg))
+                Hs_all[(li, name)] = regularize_H(H, H.shape[0], float(cfg.sigma_reg))
             del accs
-        owner = li % world
+        hidden, nxt = nxt, hidden
+    del hidden, nxt
+    # phase 2: layer l is solved on rank l mod N (the layers are independent given the float Hessians)
+    for li in range(nl):
+        if li % world != rank:
+            continue
+        layer = inner.layers[li]
         for name, mods in QUIP_GROUPS:
             key = f"{li}_{name}"
-            if rank != owner:
-                continue
             with timer("solve"):
+                H = Hs_all[(li, name)]
                 ws = [layer.get_submodule(m).weight.to(torch.float32) for m in mods]
                 scales = [float(w.square().mean().sqrt().item()) for w in ws]
                 W = torch.cat([w / s for w, s in zip(ws, scales)], dim=0).contiguous()
@@ -347,7 +355,7 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                 SU = sample_rademacher_signs(width=m, key=f"{key}:SU", seed=int(cfg.seed), device=dev)
                 SV = sample_rademacher_signs(width=n, key=f"{key}:SV", seed=int(cfg.seed), device=dev)
                 Wr = rht_weight(W, SU, SV, m & -m, n & -n)
-                Hr = rht_hessian(Hs[name], SV, n & -n)
+                Hr = rht_hessian(H, SV, n & -n)
                 wscale = float(Wr.square().mean().sqrt().item())
                 Wn = (Wr / wscale).contiguous()
                 hat, idx, st = mpq_refine_codebook(Wn, Hr, Wn, torch.zeros(m, n // 8, dtype=torch.int64, device=dev),
@@ -360,8 +368,7 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                         layer.get_submodule(mod_name).weight.copy_((hatW[r0:r0 + rows] * sc).to(w.dtype))
                         r0 += rows
                 diff = hatW - W
-                err_proxy = float(((diff @ Hs[name]) * diff).sum().item() / max(((W @ Hs[name]) * W).sum().abs().item(),
-                                                                                   1e-12))
+                err_proxy = float(((diff @ H) * diff).sum().item() / max(((W @ H) * W).sum().abs().item(), 1e-12))
                 entry = {"fused": len(mods) > 1, "shapes": [tuple(w.shape) for w in ws], "scales": scales,
                          "proxy_error": err_proxy, "surrogate_before": st["exact_surrogate_before_mean"],
                          "surrogate_after": st["exact_surrogate_after_mean"]}
@@ -369,12 +376,15 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                     entry.update(Qidxs=idx.to(torch.int16).cpu(), SU=SU.to(torch.float16).cpu(),
                                  SV=(SV * wscale).to(torch.float16).cpu())
                 attrs[key] = entry
-        if world > 1 and cfg.write_back:
-            with timer("gather"):  # every rank holds the quantized layer (the owner's weights)
+    del Hs_all
+    # phase 3: every rank holds the quantized model (the owners' weights)
+    if world > 1 and cfg.write_back:
+        with timer("gather"):
+            for li in range(nl):
+                layer = inner.layers[li]
                 for _, mods in QUIP_GROUPS:
                     for mod_name in mods:
-                        dist.broadcast(layer.get_submodule(mod_name).weight, owner, group=group)
-        hidden, nxt = nxt, hidden
+                        dist.broadcast(layer.get_submodule(mod_name).weight, li % world, group=group)
     if world > 1:
         gathered = [None] * world
         dist.all_gather_object(gathered, {k: {kk: vv for kk, vv in v.items() if not torch.is_tensor(vv)}
