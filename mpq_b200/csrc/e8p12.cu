@@ -227,32 +227,42 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
     float best = -INFINITY;  // lower bound on the largest component log-weight
     const float* mv = nullptr;
     if (need_map) {
-      // ---- pass 1: exact MAP ----
+      // ---- pass 1: exact MAP (both branches of an abs pattern share its coordinate offsets; ties keep the
+      // smaller component, so the lane's candidate is its first maximum in component order) ----
       int best_c = -1;
       #pragma unroll 1
-      for (int j = 0; j < 16; ++j) {
-        const int br = j >> 3;
-        const int ai = ((j & 7) << 5) | lane;
+      for (int j = 0; j < 8; ++j) {
+        const int ai = (j << 5) | lane;
         const uint2 of = s_off[ai];
-        const char* base = reinterpret_cast<const char*>(T.am[br]);
-        float sum_abs = 0.f, mn = INFINITY, lcs = 0.f;
-        unsigned sx = 0;
+        const char* base = reinterpret_cast<const char*>(T.am[0]);
+        float sum_abs[2] = {0.f, 0.f}, mn[2] = {INFINITY, INFINITY}, lcs[2] = {0.f, 0.f};
+        unsigned sx[2] = {0u, 0u};
         #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
-          const float2 v = *reinterpret_cast<const float2*>(base + byte);
-          const float aa = fabsf(v.x);
-          sum_abs = fadd(sum_abs, aa);
-          sx ^= __float_as_uint(v.x);
-          mn = fminf(mn, aa);
-          if constexpr (MMSE) lcs = fadd(lcs, v.y);
+          const float2* e = reinterpret_cast<const float2*>(base + byte);
+          #pragma unroll
+          for (int br = 0; br < 2; ++br) {
+            const float2 v = e[24 * br];  // the same coordinate and magnitude in branch br
+            const float aa = fabsf(v.x);
+            sum_abs[br] = fadd(sum_abs[br], aa);
+            sx[br] ^= __float_as_uint(v.x);
+            mn[br] = fminf(mn[br], aa);
+            if constexpr (MMSE) lcs[br] = fadd(lcs[br], v.y);
+          }
         }
-        const bool mismatch = (int)(sx >> 31) != s_par[ai];
-        const float lin = mismatch ? fsub(sum_abs, fmul(2.f, mn)) : sum_abs;
-        const float cst = fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai]));
-        const float sc = fadd(cst, lin);
-        if (sc > best) { best = sc; best_c = j * 32 + lane; }
-        if constexpr (MMSE) s_ub[warp][j * 32 + lane] = fadd(cst, lcs);
+        const float sq = s_sqn[ai];
+        const int par = s_par[ai];
+        #pragma unroll
+        for (int br = 0; br < 2; ++br) {
+          const bool mismatch = (int)(sx[br] >> 31) != par;
+          const float lin = mismatch ? fsub(sum_abs[br], fmul(2.f, mn[br])) : sum_abs[br];
+          const float cst = fmul(ng, fadd(ynorm[br], sq));
+          const float sc = fadd(cst, lin);
+          const int c = (j + 8 * br) * 32 + lane;
+          if (sc > best || (sc == best && best_c >= 0 && c < best_c)) { best = sc; best_c = c; }
+          if constexpr (MMSE) s_ub[warp][c] = fadd(cst, lcs[br]);
+        }
       }
       // first maximum over the warp: valid before invalid, higher score, then smaller component
       #pragma unroll
@@ -285,24 +295,29 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
       mv = tab.grid + (int64_t)map_idx * 8;
       if (map_out && lane < 8) map_out[b * ld_m + k * 8 + lane] = mv[lane];
     } else if constexpr (MMSE) {
-      // ---- pass 1: bounds only ----
+      // ---- pass 1: bounds only (both branches of an abs pattern share its coordinate offsets) ----
       float bub = -INFINITY;
       int bc = -1;
       #pragma unroll 1
-      for (int j = 0; j < 16; ++j) {
-        const int br = j >> 3;
-        const int ai = ((j & 7) << 5) | lane;
+      for (int j = 0; j < 8; ++j) {
+        const int ai = (j << 5) | lane;
         const uint2 of = s_off[ai];
-        const char* base = reinterpret_cast<const char*>(T.am[br]);
-        float lcs = 0.f;
+        const char* base = reinterpret_cast<const char*>(T.am[0]);
+        float l0 = 0.f, l1 = 0.f;
         #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
-          lcs = fadd(lcs, reinterpret_cast<const float2*>(base + byte)->y);
+          const float2* e = reinterpret_cast<const float2*>(base + byte);
+          l0 = fadd(l0, e->y);
+          l1 = fadd(l1, (e + 24)->y);  // the same coordinate and magnitude in branch 1
         }
-        const float ub = fadd(fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai])), lcs);
-        s_ub[warp][j * 32 + lane] = ub;
-        if (ub > bub) { bub = ub; bc = j * 32 + lane; }
+        const float sq = s_sqn[ai];
+        const float ub0 = fadd(fmul(ng, fadd(ynorm[0], sq)), l0);
+        const float ub1 = fadd(fmul(ng, fadd(ynorm[1], sq)), l1);
+        s_ub[warp][j * 32 + lane] = ub0;
+        s_ub[warp][(j + 8) * 32 + lane] = ub1;
+        if (ub0 > bub) { bub = ub0; bc = j * 32 + lane; }
+        if (ub1 > bub) { bub = ub1; bc = (j + 8) * 32 + lane; }
       }
       // exact log-weight of each lane's best-bound component; the warp maximum is the pruning reference
       float lcb = -INFINITY;
