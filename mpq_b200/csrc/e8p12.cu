@@ -438,8 +438,9 @@ using namespace mpq;
 
 static int e8_check(const float* r1, int B, int nb, const float* base_abs, const float* base_sqnorm,
                     const int* base_parity, const int* idx_lut, const float* grid) {
+  MPQ_CHECK_ARG(B >= 0 && nb >= 0, "e8p12: bad shape");
+  if (B == 0 || nb == 0) return MPQ_OK;  // empty tensors may carry null pointers
   MPQ_CHECK_ARG(r1 && base_abs && base_sqnorm && base_parity && idx_lut && grid, "e8p12: null pointer");
-  MPQ_CHECK_ARG(B >= 0 && nb >= 0 && B <= 2147483647, "e8p12: bad shape");
   return MPQ_OK;
 }
 
@@ -452,8 +453,8 @@ MPQ_API int mpq_e8p12_mmse(const float* r1, int64_t ld_r1, const float* center, 
                            float* map_out, int64_t ld_m, float* var_rowsum, void* stream) {
   int st = e8_check(r1, B, nb, base_abs, base_sqnorm, base_parity, idx_lut, grid);
   if (st) return st;
-  MPQ_CHECK_ARG(gamma && x1_out && var_rowsum, "mpq_e8p12_mmse: gamma, x1_out and var_rowsum are required");
   if (B == 0 || nb == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(gamma && x1_out && var_rowsum, "mpq_e8p12_mmse: gamma, x1_out and var_rowsum are required");
   E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
   E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
   k_e8p12<true><<<B, kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, var_out, ld_v, idx_out, ld_i, map_out, ld_m,
@@ -469,8 +470,8 @@ MPQ_API int mpq_e8p12_map(const float* r1, int64_t ld_r1, const float* center, i
                           const float* grid, int* idx_out, int64_t ld_i, float* map_out, int64_t ld_m, void* stream) {
   int st = e8_check(r1, B, nb, base_abs, base_sqnorm, base_parity, idx_lut, grid);
   if (st) return st;
-  MPQ_CHECK_ARG(gamma || fixed_gamma > 0.f, "mpq_e8p12_map: gamma or fixed_gamma required");
   if (B == 0 || nb == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(gamma || fixed_gamma > 0.f, "mpq_e8p12_map: gamma or fixed_gamma required");
   E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, fixed_gamma, B, nb};
   E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
   k_e8p12<false><<<B, kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, nullptr, 0, nullptr, 0, idx_out, ld_i, map_out, ld_m,

@@ -96,10 +96,10 @@ using namespace mpq;
 // layout: 0 = "NT" (B is N x K row-major), 1 = "NN" (B is K x N row-major)
 MPQ_API int mpq_gemm_f32(int layout, int M, int N, int K, float alpha, const float* A, int64_t lda, const float* B,
                          int64_t ldb, float beta, float* C, int64_t ldc, void* stream) {
-  MPQ_CHECK_ARG(A && B && C, "mpq_gemm_f32: null pointer");
   MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "mpq_gemm_f32: negative shape");
   MPQ_CHECK_ARG(layout == 0 || layout == 1, "mpq_gemm_f32: layout must be 0 (NT) or 1 (NN)");
-  if (M == 0 || N == 0) return MPQ_OK;
+  if (M == 0 || N == 0) return MPQ_OK;  // empty tensors may carry null pointers
+  MPQ_CHECK_ARG(A && B && C, "mpq_gemm_f32: null pointer");
   dim3 grid((N + 127) / 128, (M + 127) / 128);
   MPQ_CHECK_ARG(grid.y <= 65535, "mpq_gemm_f32: M too large");
   if (layout == 0)

@@ -657,8 +657,9 @@ MPQ_API int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float*
                         const float* const* B, int64_t ldb, float beta, float* C, int64_t ldc, int* status,
                         void* stream) {
   MPQ_CHECK_ARG(nreg >= 1 && nreg <= 3, "mpq_gemm_tc: nreg must be 1..3");
-  MPQ_CHECK_ARG(A && B && C, "mpq_gemm_tc: null pointer");
   MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 1, "mpq_gemm_tc: bad shape");
+  if (M == 0 || N == 0) return MPQ_OK;  // empty tensors may carry null pointers
+  MPQ_CHECK_ARG(A && B && C, "mpq_gemm_tc: null pointer");
   MPQ_CHECK_ARG(lda % 4 == 0 && ldb % 4 == 0 && lda >= K && ldb >= K, "mpq_gemm_tc: lda/ldb must be multiples of 4 and >= K");
   if (M == 0 || N == 0) return MPQ_OK;
   int st = tc::get_encoder();
@@ -731,8 +732,9 @@ MPQ_API int mpq_syrk_bf16(int n, int K, float alpha, const void* A, int64_t lda,
 MPQ_API int mpq_gemm_f16x3(int M, int N, int K, float alpha, const void* a_hi, const void* a_lo, int64_t lda,
                            const float* sa, const void* b_hi, const void* b_lo, int64_t ldb, const float* sb, float beta,
                            float* C, int64_t ldc, int* status, void* stream) {
-  MPQ_CHECK_ARG(a_hi && a_lo && b_hi && b_lo && sa && sb && C && status, "mpq_gemm_f16x3: null pointer");
   MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 1, "mpq_gemm_f16x3: bad shape");
+  if (M == 0 || N == 0) return MPQ_OK;  // empty tensors may carry null pointers
+  MPQ_CHECK_ARG(a_hi && a_lo && b_hi && b_lo && sa && sb && C && status, "mpq_gemm_f16x3: null pointer");
   MPQ_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0 && lda >= K && ldb >= K, "mpq_gemm_f16x3: lda/ldb must be multiples of 8 and >= K");
   const void* ptrs[4] = {a_hi, a_lo, b_hi, b_lo};
   for (int i = 0; i < 4; ++i)
@@ -780,9 +782,9 @@ __global__ void k_split_f16(const float* __restrict__ x, int64_t ldx, int rows, 
 
 MPQ_API int mpq_split_f16(const float* x, int64_t ldx, int rows, int cols, void* hi, void* lo, int64_t ldo,
                           float* inv_scale, void* stream) {
-  MPQ_CHECK_ARG(x && hi && lo && inv_scale, "mpq_split_f16: null pointer");
   MPQ_CHECK_ARG(rows >= 0 && cols >= 0 && ldo >= cols && ldx >= cols, "mpq_split_f16: bad shape");
   if (rows == 0 || cols == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(x && hi && lo && inv_scale, "mpq_split_f16: null pointer");
   const int warps_per_block = 8;
   k_split_f16<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, (cudaStream_t)stream>>>(
       x, ldx, rows, cols, (__half*)hi, (__half*)lo, ldo, inv_scale);
@@ -808,9 +810,9 @@ __global__ void k_split_tf32(const float* __restrict__ x, int64_t ldx, float* __
 
 MPQ_API int mpq_split_tf32(const float* x, int64_t ldx, float* hi, float* lo, int64_t ldo, int rows, int cols,
                            void* stream) {
-  MPQ_CHECK_ARG(x && hi && lo, "mpq_split_tf32: null pointer");
   const int64_t total = (int64_t)rows * cols;
-  if (total == 0) return MPQ_OK;
+  if (total <= 0) return MPQ_OK;  // empty tensors may carry null pointers
+  MPQ_CHECK_ARG(x && hi && lo, "mpq_split_tf32: null pointer");
   int64_t g = (total + 255) / 256;
   if (g > 148 * 16) g = 148 * 16;
   k_split_tf32<<<(int)g, 256, 0, (cudaStream_t)stream>>>(x, ldx, hi, lo, ldo, rows, cols);

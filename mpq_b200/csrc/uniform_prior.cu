@@ -149,8 +149,9 @@ __global__ void k_nearest_dequant(const float* __restrict__ x, int64_t ld_x, con
 }
 
 static int uniform_check(const UniformArgs& a, int B) {
-  MPQ_CHECK_ARG(a.r1 && a.center && a.scale && a.zero && a.gamma, "uniform prior: null input pointer");
   MPQ_CHECK_ARG(B >= 0 && a.n >= 0, "uniform prior: negative shape");
+  if (B == 0 || a.n == 0) return MPQ_OK;  // empty tensors may carry null pointers
+  MPQ_CHECK_ARG(a.r1 && a.center && a.scale && a.zero && a.gamma, "uniform prior: null input pointer");
   MPQ_CHECK_ARG(a.maxq >= 1 && a.maxq <= 255, "uniform prior: maxq must be in [1, 255], got %d", a.maxq);
   MPQ_CHECK_ARG(a.gshift >= 0 && a.gshift < 31, "uniform prior: bad gshift %d", a.gshift);
   return MPQ_OK;
@@ -167,8 +168,8 @@ MPQ_API int mpq_uniform_mmse(const float* r1, int64_t ld_r1, const float* center
   UniformArgs a{r1, ld_r1, center, ld_c, scale, zero, ld_p, gshift, gamma, n, maxq, prior_tau, prior_tau > 0.f};
   int st = uniform_check(a, B);
   if (st) return st;
+  if (B == 0 || n == 0) return MPQ_OK;
   MPQ_CHECK_ARG(mean_out && var_rowsum, "mpq_uniform_mmse: mean_out and var_rowsum are required");
-  if (B == 0) return MPQ_OK;
   cudaStream_t s = (cudaStream_t)stream;
   switch (maxq) {
     case 1: k_uniform_mmse<1><<<B, 256, 0, s>>>(a, mean_out, ld_out, var_out, map_value_out, map_idx_out, var_rowsum); break;
@@ -187,7 +188,7 @@ MPQ_API int mpq_uniform_map_decision(const float* r1, int64_t ld_r1, const float
   UniformArgs a{r1, ld_r1, center, ld_c, scale, zero, ld_p, gshift, gamma, n, maxq, prior_tau, prior_tau > 0.f};
   int st = uniform_check(a, B);
   if (st) return st;
-  if (B == 0) return MPQ_OK;
+  if (B == 0 || n == 0) return MPQ_OK;
   cudaStream_t s = (cudaStream_t)stream;
   if (maxq == 15) k_uniform_map_decision<15><<<B, 256, 0, s>>>(a, q_out, x_out, ld_out);
   else k_uniform_map_decision<0><<<B, 256, 0, s>>>(a, q_out, x_out, ld_out);

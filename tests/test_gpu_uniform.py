@@ -218,7 +218,8 @@ def test_scalar_cd_matches_oracle(cuda_dev):
     assert abs(st["accepted_updates"] - ref_st["accepted_updates"]) <= 0.01 * ref_st["accepted_updates"] + 2
 
 
-@pytest.mark.parametrize("m,n,iters,maxq,group", [(64, 256, 20, 15, 64), (40, 192, 16, 7, 64), (1, 128, 10, 15, 128)])
+@pytest.mark.parametrize("m,n,iters,maxq,group", [(64, 256, 20, 15, 64), (40, 192, 16, 7, 64), (1, 128, 10, 15, 128),
+                                                   (48, 256, 16, 3, 128)])
 def test_solve_uniform_vamp_matches_oracle(cuda_dev, m, n, iters, maxq, group):
     from mpq_b200 import solver as S
     W, H = _layer_fixture(m, n, 3 + m)
