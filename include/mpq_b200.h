@@ -212,6 +212,33 @@ int mpq_e8p12_map(const float* r1, int64_t ld_r1, const float* center, int64_t l
                   const float* base_abs, const float* base_sqnorm, const int* base_parity, const int* idx_lut,
                   const float* grid, int* idx_out, int64_t ld_i, float* map_out, int64_t ld_m, void* stream);
 
+/* ---- top-k polish candidates ----
+ * Per block, the k (1..1024) highest-scoring of 1024 candidates: for each (branch, abs pattern) the best and the
+ * second-best parity-valid sign pattern under the folded message (mpq/priors/e8p12.py:367-449 need_stats and
+ * :453-538 vamp_vector_map_topk_e8p12); scores descending, ties by the reference's flat candidate order.
+ * idx_out B x nb x k; score_out and val_out (B x nb x k x 8 codewords) may be NULL.
+ * Replaces mpq/solver.py:227-260 (build_e8p12_vamp_topk_candidates). */
+int mpq_e8p12_topk(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                   int64_t ld_s, const float* gamma, float prior_tau, int B, int nb, const float* base_abs,
+                   const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid, int k,
+                   int32_t* idx_out, float* score_out, float* val_out, void* stream);
+
+/* k (1..min(64, maxq+1)) best grid atoms per coordinate by the score -g/2 (atom - r1)^2 [- (atom - W)^2 / (2 tau^2
+ * max(s, 1e-12)^2)], descending, ties to the lower level: out_q / out_v / out_s (out_s may be NULL) are B x n x k.
+ * Replaces mpq/priors/uniform.py:253-284 (uniform_map_topk) behind mpq/solver.py:201-224. */
+int mpq_uniform_topk(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* scale,
+                     const float* zero, int64_t ld_p, int gshift, const float* gamma, int B, int n, int maxq,
+                     float prior_tau, int k, int32_t* out_q, float* out_v, float* out_s, void* stream);
+
+/* Per row, the candidate (k candidates of bs <= 8 values, row stride ld_cand) nearest to the row's target: with
+ * chol (bs x bs) the metric distance max(|t L|^2 + |c L|^2 - 2 (t L).(c L), 0), else the squared distance; first
+ * minimum wins.  Writes the values (out_v) and, with cand_idx, the chosen index (out_idx).
+ * Replaces the selection of mpq/polish/block_cd.py:657-685 (UniformTopKProvider) and :93-101, :768-860
+ * (E8P12TopKProvider, _topk_metric_select_impl). */
+int mpq_topk_pick(const float* target, int64_t ld_t, const float* cand, int64_t ld_cand, const int32_t* cand_idx,
+                  int64_t ld_ci, int B, int k, int bs, const float* chol, float* out_v, int64_t ld_o,
+                  int32_t* out_idx, void* stream);
+
 /* ---- gram-metric block CD (K5, K10): mpq/polish/block_cd.py:332-625 ----
  * meta per block (196 floats): gram Vs_blk Vs_blk^T | L = stabilize_cholesky(gram) | (L L^T)^-1 | eigenvalue
  * bounds of L L^T.  Replaces mpq/polish/block_cd.py:383-404 and mpq/linear.py:121-141. */

@@ -31,6 +31,9 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_block_hadamard": (P, L, P, L, I, I, I, P, I, P),
     "mpq_e8p12_mmse": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, L, P, L, P, L, P, P),
     "mpq_e8p12_map": (P, L, P, L, P, L, P, F, F, I, I, P, P, P, P, P, P, L, P, L, P),
+    "mpq_e8p12_topk": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, I, P, P, P, P),
+    "mpq_uniform_topk": (P, L, P, L, P, P, L, I, P, I, I, I, F, I, P, P, P, P),
+    "mpq_topk_pick": (P, L, P, L, P, L, I, I, I, P, P, L, P, P),
     "mpq_gram_meta": (P, L, I, I, P, P, P),
     "mpq_gram_gain": (P, L, I, I, P, P, P),
     "mpq_gram_gather": (P, L, I, P, L, P, I, I, P, P, P, P),

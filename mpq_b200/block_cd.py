@@ -1,7 +1,8 @@
 """Generic rank-space block coordinate descent with pluggable candidate providers.
 
 Reference: mpq/polish/block_cd.py — CandidateProvider :12-25, BlockCDConfig :309-317,
-block_coordinate_descent_rankspace :332-625, UniformScalarProvider :629-654, E8P12Provider :688-764.
+block_coordinate_descent_rankspace :332-625, UniformScalarProvider :629-654, UniformTopKProvider :657-685,
+E8P12Provider :688-764, E8P12TopKProvider :768-860.
 
 Objective: minimise ||Y_u - x Vs||^2 over discrete block assignments proposed by a provider.  Two engines sit
 behind one entry point:
@@ -84,6 +85,74 @@ class E8P12Provider:
             return grid.index_select(0, idx.to(torch.int64)), idx.to(torch.int64)
         vals, idx = e8p12_nearest(target.contiguous(), self.cb)
         return vals, idx.to(torch.int64)
+
+
+@dataclass
+class UniformTopKProvider:
+    """Nearest of the coordinate's precomputed top-k atoms (block_size 1, squared distance, first minimum)."""
+    topk_values: torch.Tensor  # (B, n, k)
+    topk_q: Optional[torch.Tensor] = None  # (B, n, k)
+    _vals: Optional[torch.Tensor] = field(default=None, init=False, repr=False)
+    _q: Optional[torch.Tensor] = field(default=None, init=False, repr=False)
+
+    @torch.inference_mode()
+    def propose(self, *, block_idx, start, end, x_block, target, metric, gram_chol):
+        if end != start + 1:
+            raise ValueError("UniformTopKProvider expects block_size=1.")
+        dev = target.device
+        if self._vals is None or self._vals.device != dev:
+            self._vals = self.topk_values.to(device=dev, dtype=torch.float32).contiguous()
+            self._q = None if self.topk_q is None else self.topk_q.to(device=dev, dtype=torch.int32).contiguous()
+        B, n, k = self._vals.shape
+        tg = target.to(torch.float32).contiguous()
+        out_v = torch.empty(B, 1, device=dev, dtype=torch.float32)
+        out_q = None if self._q is None else torch.empty(B, device=dev, dtype=torch.int32)
+        call("mpq_topk_pick", ptr(tg), tg.stride(0), ptr(self._vals[:, start]), n * k,
+             ptr(None if self._q is None else self._q[:, start]), n * k, B, k, 1, None, ptr(out_v), 1, ptr(out_q))
+        return out_v, out_q
+
+
+@dataclass
+class E8P12TopKProvider:
+    """Best of the block's precomputed top-k E8P12 codewords: metric "gram" measures |(t - c) L|^2 through the
+    block's Cholesky factor (|tL|^2 + |cL|^2 - 2 (tL).(cL), clamped at 0), otherwise |t - c|^2; first minimum."""
+    cb: object
+    topk_idxs: torch.Tensor  # (rows, nblocks, k)
+    topk_vals: Optional[torch.Tensor] = None  # (rows, nblocks, k, 8); gathered from the grid when absent
+    _idx: Optional[torch.Tensor] = field(default=None, init=False, repr=False)
+    _vals: Optional[torch.Tensor] = field(default=None, init=False, repr=False)
+
+    def _on(self, dev):
+        if self._idx is None or self._idx.device != dev:
+            self._idx = self.topk_idxs.to(device=dev, dtype=torch.int32).contiguous()
+            if self.topk_vals is not None:
+                self._vals = self.topk_vals.to(device=dev, dtype=torch.float32).contiguous()
+            else:
+                from .codebook import factor_tables
+                grid = factor_tables(self.cb, dev)["grid"]
+                self._vals = grid.index_select(0, self._idx.reshape(-1).to(torch.int64)).view(*self._idx.shape, 8)
+        return self._idx, self._vals
+
+    @torch.inference_mode()
+    def propose(self, *, block_idx, start, end, x_block, target, metric, gram_chol):
+        codesz = int(getattr(self.cb, "codesz", 8))
+        if (end - start) != codesz:
+            raise ValueError(f"E8P12TopKProvider expects block_size={codesz}, got {end - start}.")
+        dev = target.device
+        idx, vals = self._on(dev)
+        B, nb, k = idx.shape
+        chol = None
+        if metric == "gram":
+            if gram_chol is None:
+                raise ValueError("metric='gram' requires gram_chol.")
+            chol = gram_chol.to(device=dev, dtype=torch.float32).contiguous()
+        tg = target.to(torch.float32).contiguous()
+        out_v = torch.empty(B, 8, device=dev, dtype=torch.float32)
+        out_i = torch.empty(B, device=dev, dtype=torch.int32)
+        bi = int(block_idx)
+        call("mpq_topk_pick", ptr(tg), tg.stride(0), ptr(vals[:, bi]), nb * k * 8, ptr(idx[:, bi]), nb * k, B, k, 8,
+             ptr(chol), ptr(out_v), 8, ptr(out_i))
+        return out_v, out_i.to(torch.int64)
 
 
 def _resolve_blocks(n: int, block_size: int):

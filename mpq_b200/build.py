@@ -12,7 +12,7 @@ CSRC = HERE / "csrc"
 OUT = HERE / "libmpq_b200.so"
 
 SOURCES = ["capi.cu", "uniform_prior.cu", "vamp_uniform.cu", "gemm_simt.cu", "scalar_cd.cu", "hadamard.cu", "gemm_tc.cu", "e8p12.cu",
-           "gram_cd.cu", "hessian.cu", "block_cd.cu", "pack.cu"]
+           "gram_cd.cu", "hessian.cu", "block_cd.cu", "pack.cu", "topk.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -27,6 +27,8 @@
 //                     up to ~2 min|a|; the running maximum keeps that finite.
 // Items with g >= 1e3 take the MAP codeword with zero variance (the reference's snap) and skip pass 2.
 // One CTA of 8 warps per row; per-row variance sums are reduced in a fixed order.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace mpq {
@@ -133,6 +135,31 @@ __device__ __forceinline__ void comp_terms(const ItemTab& T, int br, int ai, uin
   o.lc = fadd(cst, fsub(fadd(logC, o.even ? lop : lom), kLn2));
 }
 
+// Stages the 256 abs patterns in shared memory: s_off[ai] packs byte k = 8 (3 k + m_k), the offset of coordinate
+// k's 8-byte table entry (magnitude index m_k of 1/2, 3/2, 5/2).  Returns true (for every thread) when base_abs
+// holds any other magnitude, i.e. is not an E8P12 abs table.
+__device__ __forceinline__ bool stage_abs_patterns(const E8Tab& tab, uint2* s_off, float* s_sqn, int* s_par,
+                                                   int* s_bad) {
+  if (threadIdx.x == 0) *s_bad = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    unsigned lo = 0, hi = 0;
+    #pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float v = tab.base_abs[i * 8 + k];
+      const unsigned m = v == 0.5f ? 0u : v == 1.5f ? 1u : v == 2.5f ? 2u : 3u;
+      if (m == 3u) *s_bad = 1;
+      const unsigned byte = 8u * (3u * k + (m & 3u));
+      if (k < 4) lo |= byte << (8 * k); else hi |= byte << (8 * (k - 4));
+    }
+    s_off[i] = make_uint2(lo, hi);
+    s_sqn[i] = tab.base_sqnorm[i];
+    s_par[i] = tab.base_parity[i];
+  }
+  __syncthreads();
+  return *s_bad != 0;
+}
+
 template <bool MMSE>
 __global__ void __launch_bounds__(kWarps * 32, 3)
 k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __restrict__ var_out, int64_t ld_v,
@@ -147,24 +174,7 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
   __shared__ float s_ub[MMSE ? kWarps : 1][512];
   __shared__ float s_var[kWarps];
   __shared__ int s_bad;
-  if (threadIdx.x == 0) s_bad = 0;
-  __syncthreads();
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    unsigned lo = 0, hi = 0;
-    #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float v = tab.base_abs[i * 8 + k];
-      const unsigned m = v == 0.5f ? 0u : v == 1.5f ? 1u : v == 2.5f ? 2u : 3u;
-      if (m == 3u) s_bad = 1;
-      const unsigned byte = 8u * (3u * k + (m & 3u));
-      if (k < 4) lo |= byte << (8 * k); else hi |= byte << (8 * (k - 4));
-    }
-    s_off[i] = make_uint2(lo, hi);
-    s_sqn[i] = tab.base_sqnorm[i];
-    s_par[i] = tab.base_parity[i];
-  }
-  __syncthreads();
-  const bool bad = s_bad != 0;
+  const bool bad = stage_abs_patterns(tab, s_off, s_sqn, s_par, &s_bad);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
   ItemTab& T = s_tab[warp];
@@ -432,6 +442,152 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
   }
 }
 
+
+// ---- top-k candidates (mpq/priors/e8p12.py:367-449 with need_stats, :453-538) ----
+// Per item and (branch, abs pattern): the best parity-valid sign pattern (flip the first minimum of |a| on a parity
+// mismatch) and the second best (mismatch: flip the second minimum instead; match: flip both minima), scored
+// const + linear as the MAP pass.  The 1024 candidates sit in the reference's flat order f = 2 (256 br + ai) + s;
+// the k largest scores are selected by k rounds of a warp argmax (ties: smaller f first).
+constexpr int kTopkWarps = 8;
+
+__global__ void __launch_bounds__(kTopkWarps * 32)
+k_e8p12_topk(E8Args a, E8Tab tab, int k, int* __restrict__ idx_out, float* __restrict__ score_out,
+             float* __restrict__ val_out) {
+  __shared__ uint2 s_off[256];
+  __shared__ float s_sqn[256];
+  __shared__ int s_par[256];
+  __shared__ float s_a[kTopkWarps][48];              // a = (g (y_k - off)) |b| per (branch, 3 k + m)
+  __shared__ float s_sc[kTopkWarps][1024];           // entry e of lane l at [e * 32 + l], e = (8 br + j) * 2 + s
+  __shared__ unsigned char s_sid[kTopkWarps][1024];  // its sign pattern (bit k: coordinate k negative)
+  __shared__ int s_bad;
+  const bool bad = stage_abs_patterns(tab, s_off, s_sqn, s_par, &s_bad);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sa = s_a[warp];
+  float* ssc = s_sc[warp];
+  unsigned char* ssid = s_sid[warp];
+  const int64_t items = (int64_t)a.B * a.nb;
+  for (int64_t it = (int64_t)blockIdx.x * kTopkWarps + warp; it < items; it += (int64_t)gridDim.x * kTopkWarps) {
+    const int b = (int)(it / a.nb), kb = (int)(it - (int64_t)b * a.nb);
+    int* io = idx_out + it * k;
+    float* so = score_out ? score_out + it * k : nullptr;
+    float* vo = val_out ? val_out + it * k * 8 : nullptr;
+    if (bad) {
+      for (int t = lane; t < k; t += 32) {
+        io[t] = -1;
+        if (so) so[t] = __int_as_float(0x7fc00000);
+      }
+      if (vo)
+        for (int t = lane; t < 8 * k; t += 32) vo[t] = __int_as_float(0x7fc00000);
+      continue;
+    }
+    float y[8], g, g1;
+    fold_item(a, b, kb, y, g, g1);
+    const float ng = fmul(-0.5f, g);
+    float ynorm[2];
+    #pragma unroll
+    for (int br = 0; br < 2; ++br) {
+      const float off = br ? -0.25f : 0.25f;
+      float yn = 0.f;
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) yn = fadd(yn, fmul(fsub(y[i], off), fsub(y[i], off)));
+      ynorm[br] = yn;
+    }
+    __syncwarp();
+    for (int e = lane; e < 48; e += 32) {
+      const int br = e / 24, r = e - br * 24, kk = r / 3, m = r - kk * 3;
+      float yk = y[0];
+      #pragma unroll
+      for (int i = 1; i < 8; ++i) yk = (kk == i) ? y[i] : yk;
+      const float off = br ? -0.25f : 0.25f;
+      sa[e] = canon_sign(fmul(fmul(g, fsub(yk, off)), 0.5f + (float)m));
+    }
+    __syncwarp();
+    #pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+      const int ai = (j << 5) | lane;
+      const uint2 of = s_off[ai];
+      float sum_abs[2] = {0.f, 0.f}, mn[2] = {INFINITY, INFINITY}, mn2[2] = {INFINITY, INFINITY};
+      int p1[2] = {0, 0}, p2[2] = {0, 0};
+      unsigned neg[2] = {0u, 0u};
+      #pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const unsigned ent = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3)) >> 3;
+        #pragma unroll
+        for (int br = 0; br < 2; ++br) {
+          const float av = sa[24 * br + ent];
+          const float aa = fabsf(av);
+          sum_abs[br] = fadd(sum_abs[br], aa);
+          neg[br] |= sign_bit(av) << kk;
+          if (aa < mn[br]) {  // first minimum, then the first minimum of the others
+            mn2[br] = mn[br]; p2[br] = p1[br];
+            mn[br] = aa; p1[br] = kk;
+          } else if (aa < mn2[br]) {
+            mn2[br] = aa; p2[br] = kk;
+          }
+        }
+      }
+      const float sq = s_sqn[ai];
+      const int par = s_par[ai];
+      #pragma unroll
+      for (int br = 0; br < 2; ++br) {
+        const bool mismatch = (int)(__popc(neg[br]) & 1) != par;
+        const float cst = fmul(ng, fadd(ynorm[br], sq));
+        const float lin1 = mismatch ? fsub(sum_abs[br], fmul(2.f, mn[br])) : sum_abs[br];
+        const float lin2 = mismatch ? fsub(sum_abs[br], fmul(2.f, mn2[br]))
+                                    : fsub(sum_abs[br], fmul(2.f, fadd(mn[br], mn2[br])));
+        const unsigned b1 = 1u << p1[br], b2 = 1u << p2[br];
+        const int e0 = (8 * br + j) * 2;
+        ssc[e0 * 32 + lane] = fadd(cst, lin1);
+        ssid[e0 * 32 + lane] = (unsigned char)(mismatch ? neg[br] ^ b1 : neg[br]);
+        ssc[(e0 + 1) * 32 + lane] = fadd(cst, lin2);
+        ssid[(e0 + 1) * 32 + lane] = (unsigned char)(mismatch ? neg[br] ^ b2 : neg[br] ^ b1 ^ b2);
+      }
+    }
+    // k rounds of a warp argmax; each lane keeps the best of its own 32 entries (ascending e = ascending f)
+    unsigned taken = 0u;
+    float lbest = -INFINITY;
+    int le = -1;
+    #pragma unroll 1
+    for (int e = 0; e < 32; ++e) {
+      const float v = ssc[e * 32 + lane];
+      if (le < 0 || v > lbest) { lbest = v; le = e; }
+    }
+    #pragma unroll 1
+    for (int t = 0; t < k; ++t) {
+      float wb = lbest;
+      int wf = le < 0 ? -1 : 512 * (le >> 4) + 64 * ((le >> 1) & 7) + 2 * lane + (le & 1);
+      #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, wb, o);
+        const int of2 = __shfl_xor_sync(0xffffffffu, wf, o);
+        if (of2 >= 0 && (wf < 0 || ob > wb || (ob == wb && of2 < wf))) { wb = ob; wf = of2; }
+      }
+      if (wf < 0) break;  // unreachable for k <= 1024
+      const int wbr = wf >> 9, wai = (wf >> 1) & 255, ws = wf & 1;
+      const int wl = wai & 31, we = (8 * wbr + (wai >> 5)) * 2 + ws;
+      const int sid = ssid[we * 32 + wl];
+      const int cidx = tab.idx_lut[wbr * 65536 + wai * 256 + sid];
+      if (lane == 0) {
+        io[t] = cidx;
+        if (so) so[t] = wb;
+      }
+      if (vo && lane < 8) vo[t * 8 + lane] = cidx >= 0 ? tab.grid[(int64_t)cidx * 8 + lane] : __int_as_float(0x7fc00000);
+      if (lane == wl) {
+        taken |= 1u << we;
+        lbest = -INFINITY;
+        le = -1;
+        #pragma unroll 1
+        for (int e = 0; e < 32; ++e) {
+          if ((taken >> e) & 1u) continue;
+          const float v = ssc[e * 32 + lane];
+          if (le < 0 || v > lbest) { lbest = v; le = e; }
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
 }  // namespace mpq
 
 using namespace mpq;
@@ -477,4 +633,23 @@ MPQ_API int mpq_e8p12_map(const float* r1, int64_t ld_r1, const float* center, i
   k_e8p12<false><<<B, kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, nullptr, 0, nullptr, 0, idx_out, ld_i, map_out, ld_m,
                                                      nullptr);
   return launch_status("mpq_e8p12_map");
+}
+
+// Top-k candidates per block (1 <= k <= 1024): idx_out (B x nb x k codebook indices, -1 where the index table has
+// no entry), optional score_out (B x nb x k log-scores, descending) and val_out (B x nb x k x 8 codewords).
+MPQ_API int mpq_e8p12_topk(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                           int64_t ld_s, const float* gamma, float prior_tau, int B, int nb, const float* base_abs,
+                           const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,
+                           int k, int* idx_out, float* score_out, float* val_out, void* stream) {
+  MPQ_CHECK_ARG(k >= 1 && k <= 1024, "mpq_e8p12_topk: k must be in [1, 1024]");
+  int st = e8_check(r1, B, nb, base_abs, base_sqnorm, base_parity, idx_lut, grid);
+  if (st) return st;
+  if (B == 0 || nb == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(gamma && idx_out, "mpq_e8p12_topk: gamma and idx_out are required");
+  E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
+  E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
+  const int64_t items = (int64_t)B * nb;
+  const int64_t blocks = std::min<int64_t>((items + kTopkWarps - 1) / kTopkWarps, 148 * 32);
+  k_e8p12_topk<<<(unsigned)blocks, kTopkWarps * 32, 0, (cudaStream_t)stream>>>(a, t, k, idx_out, score_out, val_out);
+  return launch_status("mpq_e8p12_topk");
 }

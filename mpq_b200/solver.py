@@ -121,6 +121,57 @@ def _generic_uniform_polish(*, x_init, Y_u, Vs, scale, zero, maxq, sweeps, order
     return x_pol, q_cd, st
 
 
+def _uniform_topk_polish(*, x_init, Y_u, Vs, topk_values, topk_q, sweeps, order_mode, backend, raw_target, raw_gram,
+                         q_init):
+    """The generic engine with the top-k provider (mpq/solver.py:292-295, 341-366)."""
+    from .block_cd import BlockCDConfig, UniformTopKProvider, block_coordinate_descent_rankspace
+    x_pol, q_cd, st = block_coordinate_descent_rankspace(
+        x=x_init, Y_u=Y_u, Vs=Vs, block_size=1, provider=UniformTopKProvider(topk_values=topk_values, topk_q=topk_q),
+        cfg=BlockCDConfig(sweeps=int(sweeps), metric="diag", accept_tol=0.0, order_mode=str(order_mode or "greedy_gain"),
+                          compile_steps=backend in {"compile", "auto"}),
+        idxs_init=q_init, raw_target=raw_target, raw_gram=raw_gram)
+    st = dict(st)
+    st["block_cd_backend"] = "cuda_generic"
+    return x_pol, q_cd, st
+
+
+def _dequant(q: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor) -> torch.Tensor:
+    """s (q - z) in float32 with group-compressed or expanded scale / zero."""
+    n = q.shape[1]
+    return _expand_groups(scale, n) * (q.to(torch.float32) - _expand_groups(zero, n))
+
+
+@torch.inference_mode()
+def build_uniform_vamp_topk_candidates(*, r1: torch.Tensor, gamma1: torch.Tensor, W: torch.Tensor,
+                                       scale_full: torch.Tensor, zero_full: torch.Tensor, maxq: int, prior_tau: float,
+                                       k: int, atoms: Optional[torch.Tensor] = None) -> Dict[str, torch.Tensor]:
+    """mpq/solver.py:201-224: the k best grid levels per coordinate under the final VAMP message."""
+    from .topk import uniform_map_topk
+    return uniform_map_topk(r1=r1, gamma1=gamma1, scale_full=scale_full, zero_full=zero_full, maxq=maxq,
+                            prior_center=W, prior_tau=float(prior_tau), k=max(int(k), 1), atoms=atoms)
+
+
+@torch.inference_mode()
+def build_e8p12_vamp_topk_candidates(*, r1: torch.Tensor, gamma1: torch.Tensor, Wr: torch.Tensor, cb: object,
+                                     blocks_per_chunk: int, prior_tau: float, prior_tau_scale_mode: str,
+                                     k: int) -> Dict[str, torch.Tensor]:
+    """mpq/solver.py:227-260: the k best of the 1024 {best, second-best} sign-pattern candidates per block."""
+    from .e8p12 import prior_scale_from_center
+    from .topk import vamp_vector_map_topk_e8p12
+    B, n = Wr.shape
+    codesz = int(getattr(cb, "codesz", 8))
+    if codesz != 8 or (n % codesz) != 0:
+        raise ValueError(f"E8P12 top-k expects n divisible by 8; got n={n}, codesz={codesz}.")
+    nb = n // codesz
+    W_blocks = Wr.reshape(B, nb, codesz)
+    prior_scale_blocks = prior_scale_from_center(W_blocks, prior_tau_scale_mode) if float(prior_tau) > 0.0 else None
+    return vamp_vector_map_topk_e8p12(
+        r1_blocks=r1.reshape(B, nb, codesz), gamma1=gamma1, cb=cb, k=max(int(k), 1),
+        blocks_per_chunk=max(int(blocks_per_chunk), 1),
+        prior_center_blocks=W_blocks if float(prior_tau) > 0.0 else None, prior_scale_blocks=prior_scale_blocks,
+        prior_tau=float(prior_tau), prior_tau_scale_mode=str(prior_tau_scale_mode))
+
+
 def _log_damp_scalar(prev: float, new: float, damping: float) -> float:
     """mpq/utils.py:36-45."""
     if damping >= 1.0:
@@ -261,9 +312,26 @@ def polish_uniform_rankspace(
 
     if mode == "none" or Vs.numel() == 0:
         return finish(x_work, {"accepted_updates": 0.0})
-    if mode == "topk_block_cd":
-        raise NotImplementedError("topk_block_cd uniform polish is not built yet")
     backend = _resolve_block_cd_backend(block_cd_backend=block_cd_backend, compile_block_cd=bool(compile_block_cd))
+    if mode == "topk_block_cd":
+        if topk_values is None:
+            raise ValueError("topk_block_cd requires topk_values for uniform polish.")
+        q0 = torch.empty(B, n, device=dev, dtype=torch.uint8)
+        x0 = torch.empty(B, n, device=dev, dtype=torch.float32)
+        call("mpq_uniform_nearest", ptr(x_work), x_work.stride(0), ptr(scale_full), ptr(zero_full), ld_p, gshift, B, n,
+             int(maxq), ptr(q0), ptr(x0), x0.stride(0))
+        x_pol, q_cd, st = _uniform_topk_polish(
+            x_init=x_work, Y_u=Y_u, Vs=Vs, topk_values=topk_values, topk_q=topk_q, sweeps=int(sweeps),
+            order_mode=order_mode, backend=backend, raw_target=raw_target,
+            raw_gram=_f32c(raw_gram, dev) if raw_gram is not None else None, q_init=q0.to(torch.int32))
+        if q_cd is None:
+            return finish(x_pol, st)
+        q_pol = q_cd.to(torch.int32)
+        x_q = _dequant(q_pol, scale_full, zero_full).contiguous()
+        C = ops.mm_nt(x_q, ops.Operand(VsT))
+        err = torch.empty(B, device=dev, dtype=torch.float32)
+        call("mpq_row_sqerr", ptr(Y_u), ptr(C), B, C.shape[1], Y_u.stride(0), C.stride(0), ptr(err))
+        return q_pol, x_q, err, st
     use_raw = (str(order_mode or "greedy_gain").strip().lower() == "greedy_gain" and backend in {"triton", "auto"}
                and gram_full is not None)
     if not use_raw:
@@ -463,13 +531,23 @@ def solve_uniform_rankspace_vamp(
     polish_updates = 0.0
     polish_gain = 0.0
     if polish_mode != "none":
-        if polish_mode != "block_cd":
-            raise NotImplementedError("topk_block_cd uniform polish is not built yet")
         backend = _resolve_block_cd_backend(block_cd_backend=str(getattr(cfg, "block_cd_backend", "") or ""),
                                             compile_block_cd=bool(getattr(cfg, "compile_block_cd", True)))
         q_pol = torch.empty_like(q_final)
         x_out = torch.empty_like(x_final)
-        if backend in {"triton", "auto"} and gram_full is not None:
+        if polish_mode == "topk_block_cd":
+            topk = build_uniform_vamp_topk_candidates(
+                r1=r1, gamma1=gamma1, W=W, scale_full=ctx.scale, zero_full=ctx.zero, maxq=ctx.maxq,
+                prior_tau=prior_tau, k=max(int(getattr(cfg, "topk_k", 16) or 16), 1))
+            x_pol, q_cd, polish_stats = _uniform_topk_polish(
+                x_init=x_final, Y_u=ctx.Y_u, Vs=ctx.Vs, topk_values=topk["topk_values"], topk_q=topk["topk_q"],
+                sweeps=polish_sweeps, order_mode="greedy_gain", backend=backend,
+                raw_target=W if gram_full is not None else None,
+                raw_gram=_f32c(gram_full, dev) if gram_full is not None else None, q_init=q_final.to(torch.int32))
+            q_pol.copy_(q_cd.to(torch.uint8))
+            x_out.copy_(_dequant(q_pol, ctx.scale, ctx.zero))
+            del topk
+        elif backend in {"triton", "auto"} and gram_full is not None:
             x_pol, polish_stats = scalar_greedy_cd(ctx, x_final, _f32c(gram_full, dev), sweeps=polish_sweeps)
             polish_stats = dict(polish_stats, block_cd_backend="cuda")
             ctx.nearest(x_pol, q_pol, x_out)
@@ -570,8 +648,10 @@ def polish_e8p12_rankspace(
     snapshot_budgets=None,
     snapshots_out=None,
     _ops: Optional[Tuple[Any, Any]] = None,
+    topk_vals: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Dict[str, Any]]:
-    """mpq/solver.py:369-423: gram-metric greedy block CD over the full E8P12 grid."""
+    """mpq/solver.py:369-423: gram-metric greedy block CD over the full E8P12 grid ("block_cd") or over each block's
+    precomputed top-k codewords ("topk_block_cd"; ``topk_vals`` optionally carries their values)."""
     from .e8p12 import gram_block_cd
     mode = _resolve_polish_mode(sweeps=int(sweeps), mode=str(polish_mode))
     metric = _resolve_e8p12_polish_metric(polish_metric)
@@ -589,12 +669,15 @@ def polish_e8p12_rankspace(
 
     if mode == "none" or Vs.numel() == 0:
         return x_work, idxs_init, err_of(x_work), {"accepted_updates": 0.0}
-    if mode != "block_cd":
-        raise NotImplementedError("topk_block_cd E8P12 polish is not built yet")
-    from .block_cd import BlockCDConfig, E8P12Provider, block_coordinate_descent_rankspace
+    from .block_cd import BlockCDConfig, E8P12Provider, E8P12TopKProvider, block_coordinate_descent_rankspace
+    if mode == "topk_block_cd":
+        if topk_idxs is None:
+            raise ValueError("topk_block_cd requires topk_idxs for E8P12 polish.")
+        provider = E8P12TopKProvider(cb=cb, topk_idxs=topk_idxs, topk_vals=topk_vals)
+    else:
+        provider = E8P12Provider(cb=cb, metric_rows_per_chunk=int(metric_rows_per_chunk))
     x_out, idx_out, st = block_coordinate_descent_rankspace(
-        x=x_work, Y_u=Y_u, Vs=Vs, block_size=int(getattr(cb, "codesz", 8)),
-        provider=E8P12Provider(cb=cb, metric_rows_per_chunk=int(metric_rows_per_chunk)),
+        x=x_work, Y_u=Y_u, Vs=Vs, block_size=int(getattr(cb, "codesz", 8)), provider=provider,
         cfg=BlockCDConfig(sweeps=int(sweeps), metric="gram" if metric == "gram" else "diag", accept_tol=0.0,
                           metric_rows_per_chunk=int(metric_rows_per_chunk), max_blocks_per_sweep=int(polish_max_blocks),
                           order_mode=str(order_mode or "greedy_gain")),
@@ -781,11 +864,20 @@ def solve_e8p12_rankspace_vamp(
     polish_gain = polish_updates = 0.0
     if polish_mode != "none":
         err_before = final_err
+        topk = None
+        if polish_mode == "topk_block_cd":
+            topk = build_e8p12_vamp_topk_candidates(
+                r1=r1, gamma1=gamma1, Wr=Wr, cb=cb, blocks_per_chunk=int(getattr(cfg, "blocks_per_chunk", 64) or 64),
+                prior_tau=tau, prior_tau_scale_mode=mode_scale, k=max(int(getattr(cfg, "topk_k", 16) or 16), 1))
         final_hat, final_idx, err_after, polish_stats = polish_e8p12_rankspace(
             x_init=final_hat, idxs_init=final_idx, Y_u=Y_u, Vs=Vs, cb=cb, sweeps=polish_sweeps,
             polish_mode=polish_mode, polish_metric=polish_metric,
             metric_rows_per_chunk=int(cfg.polish_metric_rows_per_chunk),
-            polish_max_blocks=int(getattr(cfg, "polish_max_blocks", 0) or 0), _ops=(opVs, opVsT))
+            polish_max_blocks=int(getattr(cfg, "polish_max_blocks", 0) or 0), _ops=(opVs, opVsT),
+            topk_idxs=None if topk is None else topk["topk_idxs"], topk_vals=None if topk is None else topk["topk_vals"])
+        if debug_out is not None and topk is not None:
+            debug_out["topk_idxs"] = topk["topk_idxs"].detach().to(device="cpu")
+        del topk
         polish_gain = float((err_before.double() - err_after.double()).mean().item())
         polish_updates = float(polish_stats.get("accepted_updates", 0.0))
         final_err = err_after

@@ -475,6 +475,8 @@ class E8P12VampConfig:
     em_obs_precision_max: float = 1e8
     polish_sweeps: int = 3
     best_iterate: bool = False
+    polish_mode: str = "block_cd"  # "block_cd" | "topk_block_cd"
+    topk_k: int = 16
 
 
 def solve_e8p12_rankspace_vamp(*, Wr, hatWr_init, cb, V, Vh, S, Vs, cfg, obs_precision_init=None, metric_cache=None):
@@ -592,7 +594,18 @@ def solve_e8p12_rankspace_vamp(*, Wr, hatWr_init, cb, V, Vh, S, Vs, cfg, obs_pre
     idx = fin["map_idxs"]
     idx_stage1 = idx.copy()
     updates = 0.0
-    if int(cfg.polish_sweeps) > 0:
+    if int(cfg.polish_sweeps) > 0 and str(getattr(cfg, "polish_mode", "block_cd")) == "topk_block_cd":
+        # mpq/solver.py:1177-1215: top-k candidates from the final message, generic engine with the top-k provider
+        from . import block_cd as OB
+        from . import topk as OT
+        tk = OT.vamp_vector_map_topk_e8p12(r1_blocks=r1.reshape(B, nb, 8), gamma1=gamma1, cb=cb,
+                                           k=max(int(cfg.topk_k), 1), prior_center_blocks=pc,
+                                           prior_scale_blocks=pscale, prior_tau=tau)
+        hat, idx, st = OB.block_coordinate_descent_rankspace(
+            x=hat, Y_u=Y_u, Vs=Vs, block_size=8, propose=OT.e8p12_topk_provider(tk["topk_idxs"], cb.grid),
+            sweeps=int(cfg.polish_sweeps), metric="gram", order_mode="greedy_gain", idxs_init=idx)
+        updates = st["accepted_updates"]
+    elif int(cfg.polish_sweeps) > 0:
         hat, idx, st = block_cd_gram(x=hat, Y_u=Y_u, Vs=Vs, cb=cb, sweeps=int(cfg.polish_sweeps), idxs_init=idx,
                                      metric_cache=metric_cache)
         updates = st["accepted_updates"]

@@ -252,6 +252,8 @@ class UniformVampConfig:
     em_obs_precision_min: float = 1e-4
     em_obs_precision_max: float = 1e8
     polish_sweeps: int = 3
+    polish_mode: str = "block_cd"  # "block_cd" | "topk_block_cd"
+    topk_k: int = 16
 
 
 def solve_uniform_rankspace_vamp(*, W, x_rtn, scale_full, zero_full, maxq, V, Vh, S, Vs, cfg,
@@ -374,11 +376,25 @@ def solve_uniform_rankspace_vamp(*, W, x_rtn, scale_full, zero_full, maxq, V, Vh
 
     q_final, x_final, err_final = best_q, best_x, best_err
     polish_updates = 0.0
-    if int(cfg.polish_sweeps) > 0 and Vs.size and gram_full is not None:
+    topk = str(getattr(cfg, "polish_mode", "block_cd")) == "topk_block_cd"
+    if int(cfg.polish_sweeps) > 0 and Vs.size and (gram_full is not None or topk):
         err_before = vamp_rankspace_error(Y_u=Y_u, x=x_final, Vs=Vs)
-        q_p, x_p, err_after, pst = polish_uniform_gpu_semantics(
-            x_init=x_final, Y_u=Y_u, Vs=Vs, scale_full=scale_full, zero_full=zero_full, maxq=maxq,
-            sweeps=int(cfg.polish_sweeps), gram_full=gram_full)
+        if topk:  # mpq/solver.py:704-745 with polish_uniform_rankspace :292-366 (generic engine, top-k provider)
+            from . import block_cd as OB
+            from . import topk as OT
+            tk = OT.uniform_map_topk(r1=r1, gamma1=gamma1, scale_full=scale_full, zero_full=zero_full, maxq=maxq,
+                                     prior_center=W, prior_tau=float(cfg.prior_tau), k=max(int(cfg.topk_k), 1))
+            q0 = nearest_atom_idx(x=x_final, scale_full=scale_full, zero_full=zero_full, maxq=maxq)
+            _, q_p, pst = OB.block_coordinate_descent_rankspace(
+                x=x_final, Y_u=Y_u, Vs=Vs, block_size=1, propose=OT.uniform_topk_provider(tk["topk_values"], tk["topk_q"]),
+                sweeps=int(cfg.polish_sweeps), metric="diag", order_mode="greedy_gain", idxs_init=q0)
+            q_p = q_p.astype(np.int32)
+            x_p = dequant_from_q(q_int=q_p, scale_full=scale_full, zero_full=zero_full)
+            err_after = vamp_rankspace_error(Y_u=Y_u, x=x_p, Vs=Vs)
+        else:
+            q_p, x_p, err_after, pst = polish_uniform_gpu_semantics(
+                x_init=x_final, Y_u=Y_u, Vs=Vs, scale_full=scale_full, zero_full=zero_full, maxq=maxq,
+                sweeps=int(cfg.polish_sweeps), gram_full=gram_full)
         improve = (err_after + f32(1e-12)) < err_before
         if improve.any():
             q_final = np.where(improve[:, None], q_p, q_final)

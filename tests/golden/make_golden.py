@@ -334,9 +334,89 @@ def gen_block_cd(out):
     np.savez_compressed(out / "block_cd.npz", **cases)
 
 
+def gen_topk(out):
+    """Top-k candidate sets (uniform and E8P12) and the generic block CD with the top-k providers."""
+    from mpq.priors.uniform import uniform_map_topk
+    from mpq.priors.e8p12 import vamp_vector_map_topk_e8p12, prior_scale_from_center
+    from mpq.polish.block_cd import BlockCDConfig, E8P12TopKProvider, UniformTopKProvider, block_coordinate_descent_rankspace
+    cases = {}
+    g = torch.Generator().manual_seed(71)
+    for name, (bits, tau, k) in {"u4p": (4, 0.25, 5), "u4": (4, 0.0, 16), "u2p": (2, 0.5, 16)}.items():
+        B, n, maxq = 6, 48, 2 ** bits - 1
+        W = torch.randn(B, n, generator=g) * 0.05
+        q = MinMaxQuantizer(bits)
+        q.find_params(W)
+        scale = q.scale.expand(B, n).contiguous()
+        zero = q.zero.expand(B, n).contiguous()
+        r1 = W + torch.randn(B, n, generator=g) * 0.01
+        gam = torch.rand(B, 1, generator=g) * 2e4 + 1e3
+        o = uniform_map_topk(r1=r1, gamma1=gam, scale_full=scale, zero_full=zero, maxq=maxq, prior_center=W,
+                             prior_tau=tau, k=k)
+        for kk, v in dict(W=W, scale=scale, zero=zero, r1=r1, gamma=gam, q=o["topk_q"], values=o["topk_values"],
+                          scores=o["topk_scores"]).items():
+            cases[f"{name}/{kk}"] = _np(v)
+        cases[f"{name}/meta"] = np.array(json.dumps({"maxq": maxq, "tau": tau, "k": k}))
+    cb = _reference_codebook()
+    B, nb = 8, 24
+    W = torch.randn(B, nb, 8, generator=g) * 0.8
+    r1 = W + torch.randn(B, nb, 8, generator=g) * 0.3
+    ps = prior_scale_from_center(W, "absmax")
+    for name, (lo, hi, tau, k) in {"e_lo_p": (1.0, 5.0, 0.25, 16), "e_hi": (10.0, 50.0, 0.0, 40),
+                                   "e_lo": (0.5, 2.0, 0.0, 7)}.items():
+        gam = torch.rand(B, 1, generator=g) * (hi - lo) + lo
+        o = vamp_vector_map_topk_e8p12(r1_blocks=r1, gamma1=gam, cb=cb, k=k, blocks_per_chunk=nb,
+                                       prior_center_blocks=W if tau > 0 else None,
+                                       prior_scale_blocks=ps if tau > 0 else None, prior_tau=tau)
+        cases[f"{name}/gamma"] = _np(gam)
+        cases[f"{name}/idxs"] = _np(o["topk_idxs"])
+        cases[f"{name}/scores"] = _np(o["topk_scores"])
+        cases[f"{name}/meta"] = np.array(json.dumps({"tau": tau, "k": k}))
+    cases["e/r1"] = _np(r1)
+    cases["e/W"] = _np(W)
+    # generic block CD with the top-k providers (eager steps)
+    B, n, maxq = 12, 64, 15
+    W, H, Vs = _block_cd_problem(B, n, n, 83)
+    q = MinMaxQuantizer(4)
+    q.find_params(W)
+    scale = q.scale.expand(B, n).contiguous()
+    zero = q.zero.expand(B, n).contiguous()
+    r1 = W + torch.randn(B, n, generator=g) * 0.004
+    gam = torch.full((B, 1), 3e4)
+    tk = uniform_map_topk(r1=r1, gamma1=gam, scale_full=scale, zero_full=zero, maxq=maxq, prior_center=W,
+                          prior_tau=0.0, k=4)
+    x0 = tk["topk_values"][:, :, 0].contiguous()
+    q0 = tk["topk_q"][:, :, 0].to(torch.int32)
+    Y_u = W @ Vs
+    cfg = BlockCDConfig(sweeps=2, metric="diag", order_mode="greedy_gain", compile_steps=False)
+    xo, qo, st = block_coordinate_descent_rankspace(
+        x=x0, Y_u=Y_u, Vs=Vs, block_size=1, provider=UniformTopKProvider(topk_values=tk["topk_values"], topk_q=tk["topk_q"]),
+        cfg=cfg, idxs_init=q0, raw_target=W, raw_gram=H)
+    for kk, v in dict(W=W, H=H, Vs=Vs, Y_u=Y_u, x0=x0, q0=q0, tq=tk["topk_q"], tv=tk["topk_values"], x=xo, q=qo).items():
+        cases[f"cd_u/{kk}"] = _np(v)
+    cases["cd_u/meta"] = np.array(json.dumps({"stats": st}))
+    for name, metric in {"cd_eg": "gram", "cd_ed": "diag"}.items():
+        B, n = 10, 64
+        W, H, Vs = _block_cd_problem(B, n, n, 97, scale_rows=1.0)
+        r1 = (W + torch.randn(B, n, generator=g) * 0.2).view(B, n // 8, 8)
+        gam = torch.rand(B, 1, generator=g) * 4 + 2
+        tk = vamp_vector_map_topk_e8p12(r1_blocks=r1, gamma1=gam, cb=cb, k=12, blocks_per_chunk=1 << 20)
+        i0 = tk["topk_idxs"][:, :, 0].contiguous()
+        x0 = cb.grid[i0].reshape(B, n)
+        Y_u = W @ Vs
+        cfg = BlockCDConfig(sweeps=2, metric=metric, order_mode="greedy_gain", compile_steps=False)
+        xo, io, st = block_coordinate_descent_rankspace(
+            x=x0, Y_u=Y_u, Vs=Vs, block_size=8, provider=E8P12TopKProvider(cb=cb, topk_idxs=tk["topk_idxs"]), cfg=cfg,
+            idxs_init=i0)
+        for kk, v in dict(W=W, Vs=Vs, Y_u=Y_u, r1=r1, gamma=gam, ti=tk["topk_idxs"], x0=x0, i0=i0, x=xo,
+                          idx=io).items():
+            cases[f"{name}/{kk}"] = _np(v)
+        cases[f"{name}/meta"] = np.array(json.dumps({"metric": metric, "stats": st}))
+    np.savez_compressed(out / "topk.npz", **cases)
+
+
 GENERATORS = {"uniform_denoise": gen_uniform_denoise, "linear": gen_linear, "scalar_cd": gen_scalar_cd,
               "scalar_layer": gen_scalar_layer, "rotation": gen_rotation, "e8p12": gen_e8p12,
-              "e8p12_layer": gen_e8p12_layer, "block_cd": gen_block_cd}
+              "e8p12_layer": gen_e8p12_layer, "block_cd": gen_block_cd, "topk": gen_topk}
 
 
 def main():

@@ -201,6 +201,36 @@ def test_solve_e8p12_matches_oracle(cuda_dev, ocb, pcb, m, n, iters):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("m,n,iters,k,tau", [(32, 256, 12, 16, 0.25), (16, 128, 8, 6, 0.0)])
+def test_solve_e8p12_topk_matches_oracle(cuda_dev, ocb, pcb, m, n, iters, k, tau):
+    """polish_mode "topk_block_cd": per-block top-k codewords from the final message, gram-metric provider."""
+    from mpq_b200 import solver as PS
+    W, H, V, S, Vs = _layer(m, n, 31 + m)
+    x0, _ = OE.rtn_init(W, ocb)
+    cfg = OE.E8P12VampConfig(iters=iters, polish_sweeps=2, prior_tau=tau, polish_mode="topk_block_cd", topk_k=k)
+    rhat, ridx, rerr, rst = OE.solve_e8p12_rankspace_vamp(Wr=W, hatWr_init=x0, cb=ocb, V=V, Vh=V.T.copy(), S=S,
+                                                          Vs=Vs, cfg=cfg)
+    d = lambda a: _t(a, cuda_dev)
+    dbg = {}
+    hat, idx, err, st = PS.solve_e8p12_rankspace_vamp(
+        Wr=d(W), hatWr_init=d(x0), cb=pcb, V=d(V), Vh=d(V.T.copy()), S=d(S), Vs=d(Vs),
+        cfg=PS.E8P12VampConfig(iters=iters, polish_sweeps=2, prior_tau=tau, polish_mode="topk_block_cd", topk_k=k),
+        debug_out=dbg)
+    agree = (idx.cpu().numpy() == ridx).mean()
+    l, rl = OL.proxy_loss(W, hat.cpu().numpy(), H), OL.proxy_loss(W, rhat, H)
+    diag = dict(agree=agree, loss=l, ref_loss=rl, upd=st["polish_updates"], ref_upd=rst["polish_updates"])
+    assert agree >= 0.995, diag
+    assert abs(l - rl) <= 0.005 * rl, diag
+    assert st["polish_updates"] > 0, diag
+    ti = dbg["topk_idxs"].numpy()
+    assert ti.shape == (m, n // 8, k)
+    # every polished block is one of its top-k candidates or its pre-polish MAP codeword
+    moved = idx.cpu().numpy()[:, :, None] == ti
+    assert moved.any(axis=2).mean() >= 0.5
+    np.testing.assert_array_equal(hat.cpu().numpy().reshape(m, -1, 8), ocb.grid[idx.cpu().numpy()])
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("case", ["a", "b"])
 def test_mpq_refine_codebook_matches_reference_golden(cuda_dev, golden_dir, pcb, case):
     import types

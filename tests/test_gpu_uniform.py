@@ -242,6 +242,62 @@ def test_solve_uniform_vamp_matches_oracle(cuda_dev, m, n, iters, maxq, group):
     np.testing.assert_allclose(rtn_err.cpu().numpy(), rrtn, rtol=1e-3)
 
 
+@pytest.mark.parametrize("m,n,iters,maxq,group,k", [(48, 256, 12, 15, 64, 4), (32, 192, 10, 3, 64, 16)])
+def test_solve_uniform_vamp_topk_matches_oracle(cuda_dev, m, n, iters, maxq, group, k):
+    """polish_mode "topk_block_cd": top-k atoms from the final message, generic engine with the top-k provider."""
+    from mpq_b200 import solver as S
+    W, H = _layer_fixture(m, n, 70 + m)
+    V, Sv, Vs = _eig(H)
+    sg, zg, sf, zf, x_rtn = _rtn(W, maxq, group)
+    ocfg = OU.UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=2, polish_mode="topk_block_cd",
+                                topk_k=k)
+    rq, rx, rerr, _, rst = OU.solve_uniform_rankspace_vamp(W=W, x_rtn=x_rtn, scale_full=sf, zero_full=zf, maxq=maxq,
+                                                           V=V, Vh=V.T.copy(), S=Sv, Vs=Vs, cfg=ocfg, gram_full=H)
+    d = lambda a: _t(a, cuda_dev)
+    cfg = S.UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=2, polish_mode="topk_block_cd",
+                              topk_k=k)
+    q, x, err, _, st = S.solve_uniform_rankspace_vamp(W=d(W), x_rtn=d(x_rtn), scale_full=d(sg), zero_full=d(zg),
+                                                      maxq=maxq, V=d(V), Vh=d(V.T.copy()), S=d(Sv), Vs=d(Vs), cfg=cfg,
+                                                      gram_full=d(H))
+    agree = (q.cpu().numpy() == rq).mean()
+    assert agree >= 0.995, (agree, st["polish_updates"], rst["polish_updates"])
+    loss, rloss = OL.proxy_loss(W, x.cpu().numpy(), H), OL.proxy_loss(W, rx, H)
+    assert abs(loss - rloss) <= 0.005 * rloss
+    assert st["polish_updates"] > 0
+    # every final level is one of the coordinate's top-k candidates or the pre-polish MAP level
+    np.testing.assert_array_equal(x.cpu().numpy(), (sf * (q.cpu().numpy().astype(np.float32) - zf)))
+
+
+def test_polish_uniform_topk_entry(cuda_dev):
+    """polish_uniform_rankspace(polish_mode="topk_block_cd") against the oracle engine with the top-k provider."""
+    from mpq_b200 import solver as S
+    from oracle import block_cd as OB
+    from oracle import topk as OT
+    W, H = _layer_fixture(40, 256, 91)
+    V, Sv, Vs = _eig(H)
+    maxq, group = 7, 64
+    sg, zg, sf, zf, x0 = _rtn(W, maxq, group)
+    Y_u = (W @ Vs).astype(np.float32)
+    r1 = (W + _rng(4).standard_normal(W.shape).astype(np.float32) * 0.003).astype(np.float32)
+    gam = np.full((W.shape[0], 1), 2e4, np.float32)
+    tk = OT.uniform_map_topk(r1=r1, gamma1=gam, scale_full=sf, zero_full=zf, maxq=maxq, prior_center=W,
+                             prior_tau=0.2, k=3)
+    q0 = OU.nearest_atom_idx(x=x0, scale_full=sf, zero_full=zf, maxq=maxq)
+    _, rq, rst = OB.block_coordinate_descent_rankspace(
+        x=x0, Y_u=Y_u, Vs=Vs, block_size=1, propose=OT.uniform_topk_provider(tk["topk_values"], tk["topk_q"]),
+        sweeps=2, metric="diag", order_mode="greedy_gain", idxs_init=q0)
+    d = lambda a: _t(a, cuda_dev)
+    q, x, err, st = S.polish_uniform_rankspace(x_init=d(x0), Y_u=d(Y_u), Vs=d(Vs), scale_full=d(sg), zero_full=d(zg),
+                                               maxq=maxq, sweeps=2, polish_mode="topk_block_cd",
+                                               topk_values=d(tk["topk_values"]), topk_q=d(tk["topk_q"]))
+    assert q.dtype == torch.int32
+    assert (q.cpu().numpy() == rq).mean() >= 0.995
+    assert abs(st["accepted_updates"] - rst["accepted_updates"]) <= 0.01 * rst["accepted_updates"] + 2
+    with pytest.raises(ValueError, match="topk_values"):
+        S.polish_uniform_rankspace(x_init=d(x0), Y_u=d(Y_u), Vs=d(Vs), scale_full=d(sg), zero_full=d(zg), maxq=maxq,
+                                   sweeps=2, polish_mode="topk_block_cd")
+
+
 @pytest.mark.parametrize("case", ["a", "b"])
 def test_run_mpq_quantization_matches_reference_golden(cuda_dev, golden_dir, case):
     """The full per-linear driver against the reference's own output (tests/golden/scalar_layer.npz)."""
