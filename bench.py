@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--hess-n", type=int, default=14336, help="hessian workload: features n")
     ap.add_argument("--hess-tokens", type=int, default=16384, help="hessian workload: tokens T per batch")
     ap.add_argument("--hess-dtype", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--polish-mode", default="block_cd", choices=["block_cd", "topk_block_cd"],
+                    help="layer workloads: the polish recipe (block_cd is the reference's default)")
     a = ap.parse_args()
     if a.profile:
         a.steps, a.warmup, a.no_cpu_baseline, a.no_clocks = 1, 1, True, True
@@ -186,8 +188,8 @@ class ClockSampler:
 class ScalarWorkload:
     dominant = "gemm_tc"
 
-    def __init__(self, dev, block_rows):
-        self.dev, self.block_rows = dev, block_rows
+    def __init__(self, dev, block_rows, polish_mode="block_cd"):
+        self.dev, self.block_rows, self.polish_mode = dev, block_rows, polish_mode
 
     def step(self, W, H):
         from mpq_b200.adapters.gptqmodel import GPTQAdapterConfig, run_mpq_quantization
@@ -195,7 +197,8 @@ class ScalarWorkload:
         qcfg = types.SimpleNamespace(bits=4, group_size=128, desc_act=False,
                                      mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
         out = run_mpq_quantization(W=W, H=2.0 * H, quantizer=None, qcfg=qcfg, module_name="bench.layer",
-                                   vamp_cfg=UniformVampConfig(iters=20, prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto"),
+                                   vamp_cfg=UniformVampConfig(iters=20, prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto",
+                                                              polish_mode=self.polish_mode),
                                    adapter_cfg=GPTQAdapterConfig(block_rows=self.block_rows, grow_block_rows=False))
         Q, q_int, scale, zero, g_idx, _, st = out
         return [q_int, scale, zero], {"raw_objective_mean": st["raw_objective_mean_final"],
@@ -206,9 +209,9 @@ class ScalarWorkload:
 class E8Workload:
     dominant = "e8p12_mmse"
 
-    def __init__(self, dev, block_rows, SU, SV, rows):
+    def __init__(self, dev, block_rows, SU, SV, rows, polish_mode="block_cd"):
         from mpq_b200.codebook import E8P12_codebook
-        self.dev, self.block_rows, self.rows = dev, block_rows, rows
+        self.dev, self.block_rows, self.rows, self.polish_mode = dev, block_rows, rows, polish_mode
         self.cb = E8P12_codebook()
         self.SU, self.SV = SU.to(dev), SV.to(dev)
 
@@ -230,7 +233,7 @@ class E8Workload:
         m = r1 - r0
         args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=16, mpq_prior_tau=0.25, mpq_polish_sweeps=3,
                                      mpq_block_rows=self.block_rows, quant_solver="vamp",
-                                     quant_polish_mode="block_cd", mpq_polish_metric="gram")
+                                     quant_polish_mode=self.polish_mode, mpq_polish_metric="gram")
         hat, idx, st = mpq_refine_codebook(Wn, Hr, Wn, torch.zeros(m, n // 8, dtype=torch.int64, device=W.device),
                                            self.cb, args, module_name="bench.layer")
         return [idx], {"surrogate_before": st["exact_surrogate_before_mean"],
@@ -273,10 +276,10 @@ def run_mpq(args):
     rows_per = r1 - r0
     block_rows = min(args.block_rows, rows_per)
     if args.workload == "e8p12":
-        wl = E8Workload(dev, block_rows, SU, SV, (r0, r1))
+        wl = E8Workload(dev, block_rows, SU, SV, (r0, r1), polish_mode=args.polish_mode)
         Wr = W  # the rotation and scale are layer-wide; the workload solves rows r0:r1
     else:
-        wl = ScalarWorkload(dev, block_rows)
+        wl = ScalarWorkload(dev, block_rows, polish_mode=args.polish_mode)
         Wr = W[r0:r1].contiguous()
     flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > 126 MB L2
 
@@ -351,7 +354,8 @@ def run_mpq(args):
             "vs_baseline": None, "dtype": "f32", "gemm_precision": ops.gemm_precision(),
             "data": "synthetic (seeded W ~ N(0,0.02^2), X with log-normal channel scales)",
             "config": {"workload": WORKLOAD_DESC[args.workload], "block_rows": block_rows, "rows_per_gpu": rows_per,
-                       "parallelism": f"rows{world}", "l2": "256 MB buffer written between timed steps"},
+                       "parallelism": f"rows{world}", "l2": "256 MB buffer written between timed steps",
+                       "polish_mode": args.polish_mode},
             "e2e": {"value": e2e / 1e3, "unit": "s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": int(round(launches)),
             "roofline": roofline,

@@ -138,6 +138,14 @@ int mpq_cd_block(float* x, int64_t ldx, const float* rhs, int64_t ldr, const flo
                  int64_t ld_p, int gshift, const float* diag, const float* diag_inv, const int* order, int c0, int K,
                  const float* Hsub, float* res, float* delta, int* accepted, int B, int maxq, float accept_tol,
                  void* stream);
+/* mpq_cd_block with the top-k provider's candidates: each column's step goes to the nearest (first minimum of
+ * the squared distance to the target) of its kc <= 32 candidate values cand[b, col, :] (row stride ld_cand);
+ * an accepted step writes the candidate's grid level cand_q[b, col, c] to qout.  With H = Vs Vs^T this is the
+ * generic block CD of mpq/polish/block_cd.py:548-580 with UniformTopKProvider :657-685, block size 1. */
+int mpq_cd_block_topk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* cand, const int32_t* cand_q,
+                      int64_t ld_cand, int kc, int32_t* qout, int64_t ldq, const float* diag, const float* diag_inv,
+                      const int* order, int c0, int K, const float* Hsub, float* res, float* delta, int* accepted,
+                      int B, float accept_tol, void* stream);
 
 /* ---- tensor-core products (tcgen05 + TMEM + TMA, sm_100a) ----
  * C = alpha * sum_{r < nreg} A[r] B[r]^T + beta C, TF32 operands with FP32 accumulation; A[r]: M x K row-major,
@@ -255,6 +263,13 @@ int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const f
                    const int* order, int c0, int Kb, const float* base_abs, const int* base_parity, const float* grid,
                    const uint8_t* sign_id, float* res, int* idx, int64_t ldi, float* delta, int* accepted,
                    long long* evals, int B, float accept_tol, void* stream);
+/* mpq_gram_chunk over each block's kc precomputed candidates (cand B x nb x kc x 8, 16-byte aligned; cand_idx
+ * B x nb x kc codebook indices): first minimum of the metric distance.  Replaces the top-k block step
+ * mpq/polish/block_cd.py:137-172 (_topk_gram_step_impl) with E8P12TopKProvider :768-860. */
+int mpq_gram_chunk_topk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* Hsub, const float* meta,
+                        const int* order, int c0, int Kb, const float* cand, const int32_t* cand_idx, int kc, int nb,
+                        float* res, int* idx, int64_t ldi, float* delta, int* accepted, long long* evals, int B,
+                        float accept_tol, void* stream);
 /* Standalone exact gram-metric search for N targets sharing one factor L (first minimum of
  * |tL|^2 + |cL|^2 - 2 (tL).(cL) over the grid).  Replaces E8P12Provider._metric_map_assign
  * (mpq/polish/block_cd.py:702-739) and the Triton search mpq/polish/triton_e8p12_cd.py:83-180. */

@@ -70,6 +70,8 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_argsort_desc": (P, I, P, P),
     "mpq_cd_gather": (P, L, I, P, I, I, P, P, P),
     "mpq_cd_block": (P, L, P, L, P, P, L, I, P, P, P, I, I, P, P, P, P, I, I, F, P),
+    "mpq_cd_block_topk": (P, L, P, L, P, P, L, I, P, L, P, P, P, I, I, P, P, P, P, I, F, P),
+    "mpq_gram_chunk_topk": (P, L, P, L, P, P, P, I, I, P, P, I, I, P, P, L, P, P, P, I, F, P),
 }
 
 _lib = None

@@ -1,7 +1,8 @@
 """Per-linear grouped-scalar driver (the GPTQModel hook point).
 
 Reference: mpq/adapters/gptqmodel.py:650-1163 (run_mpq_quantization), :276-310
-(_vamp_hessian_eigen), :313-327 (_resolve_block_rows), :46-118 (_resolve_internal_rotation).
+(_vamp_hessian_eigen), :313-327 (_resolve_block_rows), :46-118 (_resolve_internal_rotation), :330-358
+(_uniform_vamp_cfg_from_qcfg), :1250-1470 (postprocess_gptq_quantization: the MPQ polish of a GPTQ solution).
 
 Only the default ``vamp`` solver is on this path; the research baselines (cdquant, quantease,
 ojbkq) and ``desc_act`` column permutation raise ``ValueError``.
@@ -280,3 +281,187 @@ def run_mpq_quantization(
         "stage1_gamma1_mean": float(gamma_sum / max(gamma_count, 1)),
     }
     return Q, q_int_work, scale_groups, zero_groups, g_idx, float(time.time() - start), stats
+
+
+def uniform_vamp_cfg_from_qcfg(qcfg: Any) -> UniformVampConfig:
+    """mpq/adapters/gptqmodel.py:330-358: the scalar VAMP knobs from GPTQModel's ``qcfg.mpq``."""
+    mpq_cfg = getattr(qcfg, "mpq", None)
+    g = lambda k, d: getattr(mpq_cfg, k, d)
+    backend = str(g("block_cd_backend", "") or "").strip().lower()
+    if not backend:
+        backend = "compile" if bool(g("compile_block_cd", False)) else "eager"
+    return UniformVampConfig(
+        iters=int(g("iters", 10)), damping=float(g("damping", 0.5)), final_decision=str(g("final_decision", "map") or "map"),
+        init_from="rtn", gamma_start=float(g("gamma_start", 1.0)), gamma_retry_factor=float(g("gamma_retry_factor", 4.0)),
+        gamma_retry_steps=int(g("gamma_retry_steps", 3)), prior_tau=float(g("prior_tau", 0.2)),
+        obs_precision=float(g("obs_precision", 0.0)), em_obs_precision=bool(g("em_obs_precision", True)),
+        em_obs_precision_damping=float(g("em_obs_precision_damping", 0.3)),
+        em_obs_precision_min=float(g("em_obs_precision_min", 1e-4)),
+        em_obs_precision_max=float(g("em_obs_precision_max", 1e8)), polish_sweeps=int(g("polish_sweeps", 3)),
+        polish_mode=str(g("polish_mode", "block_cd") or "block_cd"), topk_k=int(g("topk_k", 16) or 16),
+        vamp_backend=str(g("vamp_backend", "auto") or "auto"), compile_block_cd=bool(g("compile_block_cd", False)),
+        block_cd_backend=backend)
+
+
+def _tensor_sha256(t: torch.Tensor) -> str:
+    """mpq/data.py:14-20: sha256 over dtype, shape and the C-order bytes."""
+    import hashlib
+    import json
+    v = t.detach().to("cpu").contiguous()
+    h = hashlib.sha256()
+    h.update(str(v.dtype).encode("ascii"))
+    h.update(json.dumps(list(v.shape), separators=(",", ":")).encode("ascii"))
+    h.update(v.numpy().tobytes(order="C"))
+    return h.hexdigest()
+
+
+def _input_fingerprint(W: torch.Tensor, H: torch.Tensor, basis: str) -> Dict[str, Any]:
+    """The paired (W, H) record of mpq/adapters/gptqmodel.py:121-144 with the on-disk cache disabled."""
+    return {"protocol": "paired_w_h_sha256_v1", "w_sha256": _tensor_sha256(W), "h_sha256": _tensor_sha256(H),
+            "w_shape": [int(d) for d in W.shape], "h_shape": [int(d) for d in H.shape], "basis": str(basis),
+            "cache": "disabled"}
+
+
+def _raw_objective(W: torch.Tensor, Q: torch.Tensor, opHT) -> torch.Tensor:
+    """(W - Q) H (W - Q)^T per row."""
+    d = torch.empty_like(W)
+    call("mpq_sub", ptr(W), ptr(Q), ptr(d), d.shape[0], d.shape[1], d.stride(0))
+    dH = ops.mm_nt(d, opHT)
+    out = torch.empty(d.shape[0], device=W.device, dtype=torch.float32)
+    call("mpq_row_dot", ptr(dH), dH.stride(0), ptr(d), d.stride(0), d.shape[0], d.shape[1], ptr(out))
+    return out
+
+
+@torch.inference_mode()
+def postprocess_gptq_quantization(
+    *,
+    W: torch.Tensor,
+    H: torch.Tensor,
+    Q_init: torch.Tensor,
+    scale_groups: torch.Tensor,
+    zero_groups: torch.Tensor,
+    g_idx: torch.Tensor,
+    qcfg: Any,
+    module_name: str,
+    adapter_cfg: GPTQAdapterConfig = GPTQAdapterConfig(),
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, float, Dict[str, Any]]:
+    """Polish a finished GPTQ solution in the rank space of H (mpq/adapters/gptqmodel.py:1250-1470).
+
+    GPTQModel's own solve produced ``Q_init`` on the grid ``scale_groups``/``zero_groups`` (columns mapped to
+    groups by ``g_idx``).  Its codes are the starting point of the rank-space block CD (``qcfg.mpq.polish_mode``
+    "block_cd", or "topk_block_cd" with candidates from an auxiliary VAMP solve of the whole module); rows whose
+    rank-space error does not drop keep the GPTQ codes, and the module keeps the GPTQ solution outright when the
+    result is not finite or its mean error rose (fail closed).
+
+    Returns (Q dense float32, q_int int32, scale_groups, zero_groups, g_idx int32, seconds, stats).
+    """
+    start = time.time()
+    if not W.is_cuda:
+        raise ValueError("postprocess_gptq_quantization requires CUDA tensors (there is no CPU path)")
+    dev = W.device
+    W = W.to(torch.float32).contiguous()
+    H = H.to(device=dev, dtype=torch.float32).contiguous()
+    Q_init = Q_init.to(device=dev, dtype=torch.float32).contiguous()
+    scale_groups = scale_groups.to(device=dev, dtype=torch.float32)
+    zero_groups = zero_groups.to(device=dev, dtype=torch.float32)
+    g_idx = g_idx.to(device=dev, dtype=torch.int32)
+    bits = int(getattr(qcfg, "bits"))
+    maxq = int(2**bits - 1)
+    rows, cols = W.shape
+    block_rows = resolve_block_rows(rows, cols, maxq, int(adapter_cfg.block_rows), dev,
+                                    grow=bool(adapter_cfg.grow_block_rows))
+    gl = g_idx.to(torch.long)
+    scale_full = scale_groups.index_select(1, gl).contiguous()
+    zero_full = zero_groups.index_select(1, gl).contiguous()
+    q_init8 = torch.empty(rows, cols, device=dev, dtype=torch.uint8)
+    x_snap = torch.empty_like(Q_init)
+    call("mpq_uniform_nearest", ptr(Q_init), Q_init.stride(0), ptr(scale_full), ptr(zero_full), scale_full.stride(0), 0,
+         rows, cols, maxq, ptr(q_init8), ptr(x_snap), x_snap.stride(0))
+    q_init = q_init8.to(torch.int32)
+
+    mpq_cfg = getattr(qcfg, "mpq", None)
+    H_work = float(adapter_cfg.hessian_scale) * H
+    fingerprint = _input_fingerprint(W, H_work, str(getattr(mpq_cfg, "rotation_effective", "internal_block_hadamard")))
+    lam, V, eigen_floor = vamp_hessian_eigen(H_work, jitter_base=adapter_cfg.jitter_base,
+                                             floor_scale=adapter_cfg.eigen_floor_scale)
+    V = V.contiguous()
+    Vh = V.T.contiguous()
+    S = torch.sqrt(lam).contiguous()
+    Vs = (V * S.unsqueeze(0)).contiguous()
+    VsT = Vs.T.contiguous()
+    Y_u = ops.gemm_nt(W, VsT)  # W Vs in FP32
+    opHT = ops.Operand(H_work.T.contiguous())
+
+    polish_mode = str(getattr(mpq_cfg, "polish_mode", "none") or "none").strip().lower()
+    polish_sweeps = int(getattr(mpq_cfg, "polish_sweeps", 0))
+    vamp_cfg = uniform_vamp_cfg_from_qcfg(qcfg)
+    err_before = ops.rankspace_error(Y_u, Q_init, VsT)
+    raw_before = _raw_objective(W, Q_init, opHT)
+
+    topk = None
+    aux_stats: Dict[str, Any] = {}
+    if polish_mode in {"topk_block_cd", "topk_cd", "topk", "vamp_topk"}:
+        from dataclasses import replace
+        aux_debug: Dict[str, Any] = {"capture_r1": True}
+        aux_cfg = replace(vamp_cfg, init_from="rtn", polish_sweeps=0, polish_mode="none")
+        _, _, _, _, aux_stats = solve_uniform_rankspace_vamp(
+            W=W, x_rtn=Q_init, scale_full=scale_full, zero_full=zero_full, maxq=maxq, V=V, Vh=Vh, S=S, Vs=Vs,
+            cfg=aux_cfg, gram_full=H_work, log_stats=False, debug_out=aux_debug)
+        from ..solver import build_uniform_vamp_topk_candidates
+        topk = build_uniform_vamp_topk_candidates(
+            r1=aux_debug["r1"].to(dev), gamma1=aux_debug["gamma1"].to(dev), W=W, scale_full=scale_full,
+            zero_full=zero_full, maxq=maxq, prior_tau=float(vamp_cfg.prior_tau), k=int(vamp_cfg.topk_k))
+
+    from ..solver import polish_uniform_rankspace
+    q_pol, x_pol, err_after, polish_stats = polish_uniform_rankspace(
+        x_init=Q_init, Y_u=Y_u, Vs=Vs, scale_full=scale_full, zero_full=zero_full, maxq=maxq, sweeps=polish_sweeps,
+        polish_mode=polish_mode, topk_values=None if topk is None else topk["topk_values"],
+        topk_q=None if topk is None else topk["topk_q"], compile_block_cd=bool(vamp_cfg.compile_block_cd),
+        block_cd_backend=str(vamp_cfg.block_cd_backend or ""), gram_full=H_work, raw_target=W, raw_gram=H_work)
+    improve = (err_after + 1e-12 < err_before).unsqueeze(-1)
+    Q_final = torch.where(improve, x_pol, Q_init)
+    q_final = torch.where(improve, q_pol.to(torch.int32), q_init)
+    err_final = ops.rankspace_error(Y_u, Q_final, VsT)
+    before_mean = float(err_before.double().mean().item()) if err_before.numel() else 0.0
+    final_mean = float(err_final.double().mean().item()) if err_final.numel() else 0.0
+    fail_closed = (not bool(torch.isfinite(err_final).all().item())) or (final_mean > before_mean + 1e-9)
+    if fail_closed:
+        Q_final, q_final, err_final, final_mean = Q_init, q_init, err_before, before_mean
+    raw_final = _raw_objective(W, Q_final, opHT)
+    stats: Dict[str, Any] = {
+        "method": "mpq",
+        "solver": "gptq",
+        "polish_mode": polish_mode,
+        "module": str(module_name),
+        "bits": bits,
+        "group_size": int(getattr(qcfg, "group_size", cols)),
+        "rows": int(rows),
+        "cols": int(cols),
+        "rank": int(S.numel()),
+        "eigen_floor": float(eigen_floor),
+        "block_rows": int(block_rows),
+        "polish_sweeps": polish_sweeps,
+        "topk_k": int(getattr(mpq_cfg, "topk_k", 16) or 16),
+        "rankspace_error_mean_before": before_mean,
+        "rankspace_error_mean_after": float(err_after.double().mean().item()) if err_after.numel() else 0.0,
+        "rankspace_error_mean_final": final_mean,
+        "raw_objective_mean_before": float(raw_before.double().mean().item()) if raw_before.numel() else 0.0,
+        "raw_objective_mean_final": float(raw_final.double().mean().item()) if raw_final.numel() else 0.0,
+        "polish_gain": float((err_before.double() - err_after.double()).mean().item()) if err_after.numel() else 0.0,
+        "polish_updates": float(polish_stats.get("accepted_updates", 0.0)),
+        "cd_trace": list(polish_stats.get("cd_trace") or polish_stats.get("sweep_trace") or []),
+        "polish_assignment_changes": int((q_final != q_init).sum().item()),
+        "polish_assignments_total": int(q_init.numel()),
+        "block_cd_backend": str(polish_stats.get("block_cd_backend", vamp_cfg.block_cd_backend)),
+        "module_fail_closed": bool(fail_closed),
+        "aux_vamp": aux_stats if topk is not None else {},
+        "quant_time_s": float(time.time() - start),
+        "input_fingerprint": fingerprint,
+    }
+    bucket = getattr(mpq_cfg, "_layer_stats", None)
+    if mpq_cfg is not None:
+        if not isinstance(bucket, list):
+            bucket = []
+            setattr(mpq_cfg, "_layer_stats", bucket)
+        bucket.append(stats)
+    return Q_final, q_final, scale_groups, zero_groups, g_idx, float(time.time() - start), stats

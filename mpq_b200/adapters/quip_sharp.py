@@ -115,7 +115,9 @@ def mpq_refine_codebook(
     solver, polish_mode = _resolve_solver(args)
     if solver != "vamp":
         raise ValueError(f"QUIP adapter solver {solver!r} is not on the CUDA path (only 'vamp').")
-    if polish_mode not in ("block_cd", "none"):
+    if polish_mode in ("topk_cd", "topk", "vamp_topk"):
+        polish_mode = "topk_block_cd"
+    if polish_mode not in ("block_cd", "topk_block_cd", "none"):
         raise ValueError(f"QUIP adapter polish {polish_mode!r} is not on the CUDA path.")
     init_mode = str(getattr(args, "mpq_init", "rtn") or "rtn").strip().lower()
     seed = int(getattr(args, "seed", getattr(args, "mpq_seed", 0)) or 0)

@@ -95,14 +95,18 @@ class UniformTopKProvider:
     _vals: Optional[torch.Tensor] = field(default=None, init=False, repr=False)
     _q: Optional[torch.Tensor] = field(default=None, init=False, repr=False)
 
+    def _on_q(self, dev):
+        if self._vals is None or self._vals.device != dev:
+            self._vals = self.topk_values.to(device=dev, dtype=torch.float32).contiguous()
+            self._q = None if self.topk_q is None else self.topk_q.to(device=dev, dtype=torch.int32).contiguous()
+        return self._vals, self._q
+
     @torch.inference_mode()
     def propose(self, *, block_idx, start, end, x_block, target, metric, gram_chol):
         if end != start + 1:
             raise ValueError("UniformTopKProvider expects block_size=1.")
         dev = target.device
-        if self._vals is None or self._vals.device != dev:
-            self._vals = self.topk_values.to(device=dev, dtype=torch.float32).contiguous()
-            self._q = None if self.topk_q is None else self.topk_q.to(device=dev, dtype=torch.int32).contiguous()
+        self._on_q(dev)
         B, n, k = self._vals.shape
         tg = target.to(torch.float32).contiguous()
         out_v = torch.empty(B, 1, device=dev, dtype=torch.float32)
@@ -214,11 +218,19 @@ def block_coordinate_descent_rankspace(*, x: torch.Tensor, Y_u: torch.Tensor, Vs
     max_blocks = int(getattr(cfg, "max_blocks_per_sweep", 0) or 0)
     requested = {int(b) for b in (snapshot_budgets or set()) if 0 <= int(b) <= sweeps}
 
-    if (isinstance(provider, E8P12Provider) and metric == "gram" and order_mode == "greedy_gain" and max_blocks == 0
+    fused_order = order_mode == "greedy_gain" and max_blocks == 0
+    if (isinstance(provider, (E8P12Provider, E8P12TopKProvider)) and metric == "gram" and fused_order
             and idxs_init is not None):
         return _e8p12_gram_engine(x=x, Y_u=Y_u, Vs=Vs, cb=provider.cb, sweeps=sweeps, accept_tol=float(cfg.accept_tol),
                                   idxs_init=idxs_init, requested=requested, snapshots_out=snapshots_out,
-                                  raw_target=raw_target, raw_gram=raw_gram)
+                                  raw_target=raw_target, raw_gram=raw_gram,
+                                  topk=provider if isinstance(provider, E8P12TopKProvider) else None)
+    if (isinstance(provider, UniformTopKProvider) and provider.topk_q is not None and metric == "diag" and fused_order
+            and idxs_init is not None and int(provider.topk_values.shape[-1]) <= 32):
+        return _uniform_topk_engine(x=x, Y_u=Y_u, Vs=Vs, provider=provider, sweeps=sweeps,
+                                    accept_tol=max(float(cfg.accept_tol), 0.0), idxs_init=idxs_init,
+                                    requested=requested, snapshots_out=snapshots_out, raw_target=raw_target,
+                                    raw_gram=raw_gram)
     return _generic_engine(x=x, Y_u=Y_u, Vs=Vs, bs=bs, blocks=blocks, provider=provider, metric=metric,
                            order_mode=order_mode, max_blocks=max_blocks, sweeps=sweeps,
                            accept_tol=max(float(cfg.accept_tol), 0.0), idxs_init=idxs_init, requested=requested,
@@ -249,7 +261,7 @@ class _Trace:
 
 
 def _e8p12_gram_engine(*, x, Y_u, Vs, cb, sweeps, accept_tol, idxs_init, requested, snapshots_out, raw_target,
-                       raw_gram):
+                       raw_gram, topk=None):
     from .e8p12 import gram_block_cd
     dev = x.device
     idx0 = idxs_init.to(device=dev, dtype=torch.int64)
@@ -265,10 +277,69 @@ def _e8p12_gram_engine(*, x, Y_u, Vs, cb, sweeps, accept_tol, idxs_init, request
         if snapshots_out is not None and sweep in requested and sweep > 0:
             snapshots_out[sweep] = idx64.detach().cpu().clone()
 
+    tv = ti = None
+    if topk is not None:
+        ti, tv = topk._on(dev)
     x_out, idx_out, st = gram_block_cd(x=x, Y_u=Y_u.to(torch.float32).contiguous(), Vs=Vs, cb=cb, sweeps=sweeps,
-                                       idxs_init=idx0, accept_tol=accept_tol, on_sweep=on_sweep)
+                                       idxs_init=idx0, accept_tol=accept_tol, on_sweep=on_sweep, topk_vals=tv,
+                                       topk_idx=ti)
     return x_out.to(dtype=x.dtype), idx_out.to(getattr(cb, "idx_dtype", torch.int64)), tr.stats(
         st["accepted_updates"], {"exact_score_evals": st.get("exact_score_evals", 0)})
+
+
+def _uniform_topk_engine(*, x, Y_u, Vs, provider, sweeps, accept_tol, idxs_init, requested, snapshots_out, raw_target,
+                         raw_gram):
+    """Scalar blocks, diag metric, greedy order with the top-k provider, in 128-column lazy blocks: per row one warp
+    runs a block's sequential decisions against the block's rank-space grams G[J, J] (G = Vs Vs^T) in shared
+    memory, and one GEMM applies the accepted steps to the right-hand side of every column."""
+    dev = x.device
+    B, n = x.shape
+    R = int(Vs.shape[1])
+    vals, qc = provider._on_q(dev)
+    kc = int(vals.shape[2])
+    if tuple(vals.shape) != (B, n, kc):
+        raise ValueError(f"topk_values must be (B, n, k) = ({B}, {n}, k); got {tuple(vals.shape)}")
+    x_work = x.to(torch.float32).contiguous().clone()
+    Vs = Vs.to(device=dev, dtype=torch.float32).contiguous()
+    opVs, opVsT = ops.Operand(Vs), ops.Operand(Vs.t().contiguous())
+    res_u = ops.mm_nt(x_work, opVsT)
+    res_norm = torch.empty(B, device=dev, dtype=torch.float32)
+    Yc = Y_u.to(torch.float32).contiguous()
+    call("mpq_residual", ptr(Yc), ptr(res_u), B, R, res_u.stride(0), ptr(res_norm))
+    rhs = ops.mm_nt(res_u, opVs)  # residual_u Vs^T (B, n)
+    del res_u
+    G = ops.mm_nt(Vs, opVs)  # Vs Vs^T: the rank-space grams of every column pair
+    diag = torch.empty(n, device=dev, dtype=torch.float32)
+    diag_inv = torch.empty(n, device=dev, dtype=torch.float32)
+    call("mpq_cd_diag", ptr(Vs), n, R, Vs.stride(0), ptr(diag), ptr(diag_inv))
+    q = idxs_init.to(device=dev, dtype=torch.int32).reshape(B, n).contiguous().clone()
+    tr = _Trace(raw_target, raw_gram, q.clone())
+    if snapshots_out is not None and 0 in requested:
+        snapshots_out[0] = q.detach().cpu().to(idxs_init.dtype).clone()
+    tr.add(0, res_norm, x_work, q, 0, 0)
+    gain = torch.empty(n, device=dev, dtype=torch.float32)
+    order = torch.empty(n, device=dev, dtype=torch.int32)
+    HJT = torch.empty(n, 128, device=dev, dtype=torch.float32)
+    Hsub = torch.empty(128, 128, device=dev, dtype=torch.float32)
+    delta = torch.empty(B, 128, device=dev, dtype=torch.float32)
+    accepted = torch.zeros(1, device=dev, dtype=torch.int32)
+    acc_prev = 0
+    for sweep in range(1, sweeps + 1):
+        call("mpq_cd_gain", ptr(rhs), B, n, rhs.stride(0), ptr(diag_inv), ptr(gain))
+        call("mpq_argsort_desc", ptr(gain), n, ptr(order))
+        for c0 in range(0, n, 128):
+            K = min(128, n - c0)
+            call("mpq_cd_gather", ptr(G), G.stride(0), n, ptr(order), c0, K, ptr(HJT), ptr(Hsub))
+            call("mpq_cd_block_topk", ptr(x_work), x_work.stride(0), ptr(rhs), rhs.stride(0), ptr(vals), ptr(qc),
+                 n * kc, kc, ptr(q), q.stride(0), ptr(diag), ptr(diag_inv), ptr(order), c0, K, ptr(Hsub),
+                 ptr(res_norm), ptr(delta), ptr(accepted), B, float(accept_tol))
+            ops.mm_nt(delta[:, :K], HJT[:, :K], out=rhs, alpha=-1.0, beta=1.0)
+        acc_now = int(accepted.item())
+        tr.add(sweep, res_norm, x_work, q, acc_now - acc_prev, acc_now)
+        acc_prev = acc_now
+        if snapshots_out is not None and sweep in requested:
+            snapshots_out[sweep] = q.detach().cpu().clone()
+    return x_work.to(dtype=x.dtype), q, tr.stats(acc_prev)
 
 
 def _generic_engine(*, x, Y_u, Vs, bs, blocks, provider, metric, order_mode, max_blocks, sweeps, accept_tol, idxs_init,

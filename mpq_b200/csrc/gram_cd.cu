@@ -393,8 +393,53 @@ struct GramChunkArgs {
   int* accepted;                   // accepted-update counter
   long long* evals;                // exact score evaluations (diagnostic)
   int B; float accept_tol;
+  // top-k candidate mode: per (row, block) kc codewords (values B x nb x kc x 8, indices B x nb x kc)
+  const float* cand; const int* cand_idx; int kc; int nb;
 };
 
+// Top-k candidate choice of one block (mpq/polish/block_cd.py:137-172 _topk_gram_step_impl): metric distance
+// |tL|^2 + |cL|^2 - 2 (tL).(cL) clamped at 0 (index-ordered sums), first minimum over the candidates.
+__device__ __forceinline__ int topk_pick_warp(const float t[8], const float* L, const float* cv, int kc) {
+  const int lane = threadIdx.x & 31;
+  float tm[8], tn = 0.f;
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float acc = 0.f;
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) acc = fadd(acc, fmul(t[i], L[i * 8 + j]));
+    tm[j] = acc;
+  }
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) tn = fadd(tn, fmul(tm[j], tm[j]));
+  float key = INFINITY;
+  int ci = 0x7fffffff;
+  for (int c = lane; c < kc; c += 32) {
+    const float4 v0 = __ldg(reinterpret_cast<const float4*>(cv + c * 8));
+    const float4 v1 = __ldg(reinterpret_cast<const float4*>(cv + c * 8 + 4));
+    const float cvv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float cn = 0.f, cross = 0.f;
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float cm = 0.f;
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) cm = fadd(cm, fmul(cvv[i], L[i * 8 + j]));
+      cn = fadd(cn, fmul(cm, cm));
+      cross = fadd(cross, fmul(cm, tm[j]));
+    }
+    float dist = fmaxf(fsub(fadd(tn, cn), fmul(2.f, cross)), 0.f);
+    if (dist != dist) dist = INFINITY;
+    if (ci == 0x7fffffff || dist < key) { key = dist; ci = c; }
+  }
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ok = __shfl_xor_sync(0xffffffffu, key, o);
+    const int oc = __shfl_xor_sync(0xffffffffu, ci, o);
+    if (oc != 0x7fffffff && (ci == 0x7fffffff || ok < key || (ok == key && oc < ci))) { key = ok; ci = oc; }
+  }
+  return ci;
+}
+
+template <bool TOPK>
 __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
   extern __shared__ float sm[];
   float* Hs = sm;                                    // 128 x 128
@@ -403,8 +448,10 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
   float* s_meta = reinterpret_cast<float*>(s_par + 256);  // 16 x kMeta
   float* s_rhs = s_meta + kChunkBlocks * kMeta;      // 8 warps x 128
   for (int i = threadIdx.x; i < kChunkCols * kChunkCols; i += blockDim.x) Hs[i] = a.Hsub[i];
-  for (int i = threadIdx.x; i < 2048; i += blockDim.x) s_abs[i] = a.base_abs[i];
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) s_par[i] = a.base_parity[i];
+  if constexpr (!TOPK) {
+    for (int i = threadIdx.x; i < 2048; i += blockDim.x) s_abs[i] = a.base_abs[i];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_par[i] = a.base_parity[i];
+  }
   for (int i = threadIdx.x; i < a.Kb * kMeta; i += blockDim.x)
     s_meta[i] = a.meta[(int64_t)a.order[a.c0 + i / kMeta] * kMeta + i % kMeta];
   __syncthreads();
@@ -438,11 +485,22 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
       for (int i = 0; i < 8; ++i) s = fadd(s, fmul(r[i], Gi[i * 8 + j]));
       t[j] = fadd(xb[j], s);
     }
-    int ne = 0;
-    const int c = gram_search_warp(e8, t, L, m[192], m[193], &ne);
-    evals += ne;
+    int c;
+    const float* gv;
+    if constexpr (TOPK) {
+      const int64_t item = (int64_t)b * a.nb + blk;
+      const float* cv = a.cand + item * a.kc * 8;
+      const int pick = topk_pick_warp(t, L, cv, a.kc);
+      gv = cv + pick * 8;
+      c = a.cand_idx ? a.cand_idx[item * a.kc + pick] : pick;
+      evals += a.kc;
+    } else {
+      int ne = 0;
+      c = gram_search_warp(e8, t, L, m[192], m[193], &ne);
+      evals += ne;
+      gv = a.grid + (int64_t)c * 8;
+    }
     float d[8], cross = 0.f, dn = 0.f;
-    const float* gv = a.grid + (int64_t)c * 8;
     #pragma unroll
     for (int j = 0; j < 8; ++j) {
       d[j] = fsub(__ldg(gv + j), xb[j]);
@@ -544,11 +602,29 @@ MPQ_API int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr,
   MPQ_CHECK_ARG(((uintptr_t)grid & 15) == 0, "mpq_gram_chunk: grid must be 16-byte aligned");
   if (B == 0) return MPQ_OK;
   GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, base_abs, base_parity, grid, sign_id, res, idx, ldi,
-                  delta, accepted, evals, B, accept_tol};
+                  delta, accepted, evals, B, accept_tol, nullptr, nullptr, 0, 0};
   const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
-  cudaFuncSetAttribute(k_gram_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_gram_chunk<<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
+  cudaFuncSetAttribute(k_gram_chunk<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_gram_chunk<false><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
   return launch_status("mpq_gram_chunk");
+}
+
+MPQ_API int mpq_gram_chunk_topk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* Hsub,
+                                const float* meta, const int* order, int c0, int Kb, const float* cand,
+                                const int* cand_idx, int kc, int nb, float* res, int* idx, int64_t ldi, float* delta,
+                                int* accepted, long long* evals, int B, float accept_tol, void* stream) {
+  MPQ_CHECK_ARG(Kb >= 1 && Kb <= kChunkBlocks, "mpq_gram_chunk_topk: Kb must be in [1, %d]", kChunkBlocks);
+  MPQ_CHECK_ARG(kc >= 1 && nb >= 1, "mpq_gram_chunk_topk: bad candidate shape");
+  if (B == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(x && rhs && Hsub && meta && order && cand && res && idx && delta && accepted,
+                "mpq_gram_chunk_topk: null pointer");
+  MPQ_CHECK_ARG(((uintptr_t)cand & 15) == 0, "mpq_gram_chunk_topk: candidates must be 16-byte aligned");
+  GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, nullptr, nullptr, nullptr, nullptr, res, idx, ldi,
+                  delta, accepted, evals, B, accept_tol, cand, cand_idx, kc, nb};
+  const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
+  cudaFuncSetAttribute(k_gram_chunk<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_gram_chunk<true><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
+  return launch_status("mpq_gram_chunk_topk");
 }
 
 MPQ_API int mpq_gram_search(const float* targets, int N, const float* L, float lam_lo, float lam_hi,

@@ -113,6 +113,10 @@ struct CdArgs {
   float* x; int64_t ldx;
   const float* rhs; int64_t ldr;
   const float* scale; const float* zero; int64_t ld_p; int gshift;
+  // top-k candidate mode: per (row, column) kc <= 32 candidate values (and their grid levels), row stride ld_cand;
+  // the chosen level of an accepted step is written to qout
+  const float* cand; const int* cand_q; int64_t ld_cand; int kc;
+  int* qout; int64_t ldq;
   const float* diag; const float* diag_inv;
   const int* order; int c0; int K;
   const float* Hsub;
@@ -122,7 +126,10 @@ struct CdArgs {
   int B; int maxq; float accept_tol;
 };
 
-// One warp per row: the sequential decisions of one column block (triton_scalar_cd.py:59-107).
+// One warp per row: the sequential decisions of one column block (triton_scalar_cd.py:59-107).  TOPK: the
+// candidate of a column is the nearest of its precomputed top-k values to the target (first minimum of the
+// squared distance, mpq/polish/block_cd.py:657-685) instead of the rounded grid level.
+template <bool TOPK>
 __global__ void __launch_bounds__(256) k_cd_block(CdArgs a) {
   extern __shared__ float Hs[];  // kCdBlock x kCdBlock
   __shared__ float s_diag[kCdBlock], s_dinv[kCdBlock];
@@ -147,8 +154,12 @@ __global__ void __launch_bounds__(256) k_cd_block(CdArgs a) {
       const int col = s_col[l];
       rhs[t] = a.rhs[b * a.ldr + col];
       xv[t] = a.x[b * a.ldx + col];
-      sv[t] = a.scale[b * a.ld_p + (col >> a.gshift)];
-      zv[t] = a.zero[b * a.ld_p + (col >> a.gshift)];
+      if constexpr (TOPK) {
+        sv[t] = 1.f; zv[t] = 0.f;
+      } else {
+        sv[t] = a.scale[b * a.ld_p + (col >> a.gshift)];
+        zv[t] = a.zero[b * a.ld_p + (col >> a.gshift)];
+      }
     } else {
       rhs[t] = 0.f; xv[t] = 0.f; sv[t] = 1.f; zv[t] = 0.f;
     }
@@ -156,6 +167,9 @@ __global__ void __launch_bounds__(256) k_cd_block(CdArgs a) {
   float res = a.res[b];
   const float tol1 = 1.f + a.accept_tol;
   int acc_count = 0;
+  const float* crow = TOPK ? a.cand + (int64_t)b * a.ld_cand : nullptr;
+  float cnext = 0.f;  // this lane's candidate of the next column (loaded one decision ahead)
+  if constexpr (TOPK) cnext = lane < a.kc ? crow[(int64_t)s_col[0] * a.kc + lane] : 0.f;
   #pragma unroll
   for (int t = 0; t < 4; ++t) {
     for (int lk = 0; lk < 32; ++lk) {
@@ -163,18 +177,45 @@ __global__ void __launch_bounds__(256) k_cd_block(CdArgs a) {
       if (k >= a.K) break;
       const float rk = __shfl_sync(0xffffffffu, rhs[t], lk);
       const float xk = __shfl_sync(0xffffffffu, xv[t], lk);
-      const float sk = fmaxf(__shfl_sync(0xffffffffu, sv[t], lk), 1e-12f);
-      const float zk = __shfl_sync(0xffffffffu, zv[t], lk);
       const float target = fadd(xk, fmul(rk, s_dinv[k]));
-      float qf = rintf(fadd(fdiv(target, sk), zk));
-      qf = fminf(fmaxf(qf, 0.f), (float)a.maxq);
-      const float xq = fmul(sk, fsub(qf, zk));
+      float xq;
+      int pick = 0;
+      if constexpr (TOPK) {
+        const float cv = cnext;
+        if (k + 1 < a.K && lane < a.kc) cnext = crow[(int64_t)s_col[k + 1] * a.kc + lane];
+        float key = INFINITY;
+        int ci = 0x7fffffff;
+        if (lane < a.kc) {
+          const float dd = fsub(cv, target);
+          key = fmul(dd, dd);
+          if (key != key) key = INFINITY;
+          ci = lane;
+        }
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {  // first minimum: smaller distance, then smaller candidate index
+          const float ok = __shfl_xor_sync(0xffffffffu, key, o);
+          const int oc = __shfl_xor_sync(0xffffffffu, ci, o);
+          if (oc != 0x7fffffff && (ci == 0x7fffffff || ok < key || (ok == key && oc < ci))) { key = ok; ci = oc; }
+        }
+        pick = ci;
+        xq = __shfl_sync(0xffffffffu, cv, pick);
+      } else {
+        const float sk = fmaxf(__shfl_sync(0xffffffffu, sv[t], lk), 1e-12f);
+        const float zk = __shfl_sync(0xffffffffu, zv[t], lk);
+        float qf = rintf(fadd(fdiv(target, sk), zk));
+        qf = fminf(fmaxf(qf, 0.f), (float)a.maxq);
+        xq = fmul(sk, fsub(qf, zk));
+      }
       const float d = fsub(xq, xk);
       const float cand = fmaxf(fsub(fadd(res, fmul(fmul(d, d), s_diag[k])), fmul(fmul(2.f, rk), d)), 0.f);
       if (fadd(cand, 1e-12f) < fmul(res, tol1)) {
         res = cand;
         ++acc_count;
         if (lane == lk) { xv[t] = xq; dl[t] = d; }
+        if constexpr (TOPK) {
+          if (lane == 0 && a.qout && a.cand_q)
+            a.qout[b * a.ldq + s_col[k]] = a.cand_q[(int64_t)b * a.ld_cand + (int64_t)s_col[k] * a.kc + pick];
+        }
         const float* hrow = Hs + k * kCdBlock;
         #pragma unroll
         for (int u = 0; u < 4; ++u) rhs[u] = fsub(rhs[u], fmul(d, hrow[u * 32 + lane]));
@@ -242,10 +283,27 @@ MPQ_API int mpq_cd_block(float* x, int64_t ldx, const float* rhs, int64_t ldr, c
   MPQ_CHECK_ARG(K >= 1 && K <= kCdBlock, "mpq_cd_block: K must be in [1, %d]", kCdBlock);
   MPQ_CHECK_ARG(maxq >= 1 && maxq <= 255, "mpq_cd_block: bad maxq");
   if (B == 0) return MPQ_OK;
-  CdArgs a{x, ldx, rhs, ldr, scale, zero, ld_p, gshift, diag, diag_inv, order, c0, K, Hsub, res, delta, accepted,
-           B, maxq, accept_tol};
+  CdArgs a{x, ldx, rhs, ldr, scale, zero, ld_p, gshift, nullptr, nullptr, 0, 0, nullptr, 0, diag, diag_inv, order, c0,
+           K, Hsub, res, delta, accepted, B, maxq, accept_tol};
   const size_t smem = (size_t)kCdBlock * kCdBlock * sizeof(float);
-  cudaFuncSetAttribute(k_cd_block, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_cd_block<<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
+  cudaFuncSetAttribute(k_cd_block<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_cd_block<false><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
   return launch_status("mpq_cd_block");
+}
+
+MPQ_API int mpq_cd_block_topk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* cand,
+                              const int* cand_q, int64_t ld_cand, int kc, int* qout, int64_t ldq, const float* diag,
+                              const float* diag_inv, const int* order, int c0, int K, const float* Hsub, float* res,
+                              float* delta, int* accepted, int B, float accept_tol, void* stream) {
+  MPQ_CHECK_ARG(K >= 1 && K <= kCdBlock, "mpq_cd_block_topk: K must be in [1, %d]", kCdBlock);
+  MPQ_CHECK_ARG(kc >= 1 && kc <= 32, "mpq_cd_block_topk: kc must be in [1, 32]");
+  if (B == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(x && rhs && cand && diag && diag_inv && order && Hsub && res && delta && accepted,
+                "mpq_cd_block_topk: null pointer");
+  CdArgs a{x, ldx, rhs, ldr, nullptr, nullptr, 0, 0, cand, cand_q, ld_cand, kc, qout, ldq, diag, diag_inv, order, c0,
+           K, Hsub, res, delta, accepted, B, 1, accept_tol};
+  const size_t smem = (size_t)kCdBlock * kCdBlock * sizeof(float);
+  cudaFuncSetAttribute(k_cd_block<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_cd_block<true><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
+  return launch_status("mpq_cd_block_topk");
 }

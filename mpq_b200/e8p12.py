@@ -130,10 +130,13 @@ def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, blocks_per_chunk: 
 @torch.inference_mode()
 def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, sweeps: int,
                   idxs_init: torch.Tensor, accept_tol: float = 0.0, opVs: Optional[ops.Operand] = None,
-                  opVsT: Optional[ops.Operand] = None, on_sweep=None) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
+                  opVsT: Optional[ops.Operand] = None, on_sweep=None, topk_vals: Optional[torch.Tensor] = None,
+                  topk_idx: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
     """Gram-metric greedy block CD over E8P12 8-blocks (mpq/polish/block_cd.py:332-625, E8P12Provider, metric
     'gram').  Returns (x, idxs int64 (B, nb), stats).  on_sweep(sweep, x, idx, res_norm, accepted_total) is
-    called before the first sweep (sweep 0) and after each sweep."""
+    called before the first sweep (sweep 0) and after each sweep.  With ``topk_vals`` (B, nb, k, 8) and
+    ``topk_idx`` (B, nb, k) every block decision picks among the block's k candidates (E8P12TopKProvider,
+    _topk_gram_step_impl :137-172) instead of searching the full grid."""
     dev = x.device
     B, n = x.shape
     nb = n // 8
@@ -160,6 +163,14 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
     delta = torch.empty(B, 128, device=dev, dtype=torch.float32)
     accepted = torch.zeros(1, device=dev, dtype=torch.int32)
     evals = torch.zeros(1, device=dev, dtype=torch.int64)
+    n_cand = 0
+    if topk_vals is not None:
+        topk_vals = topk_vals.to(device=dev, dtype=torch.float32).contiguous()
+        topk_idx = topk_idx.to(device=dev, dtype=torch.int32).contiguous()
+        n_cand = int(topk_idx.shape[2])
+        if tuple(topk_vals.shape) != (B, nb, n_cand, 8) or tuple(topk_idx.shape) != (B, nb, n_cand):
+            raise ValueError(f"top-k candidates must be (B, nb, k, 8) / (B, nb, k); got {tuple(topk_vals.shape)}, "
+                             f"{tuple(topk_idx.shape)}")
     trace = [float(res_norm.double().mean().item())]
     if on_sweep is not None:
         on_sweep(0, x_work, idx, res_norm, 0)
@@ -174,9 +185,15 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
             call("mpq_gram_gather", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb, ptr(VsJ),
                  ptr(VsJT), ptr(Hsub))
             ops.mm_nt(res_u, VsJ[:kc], out=rhsJ[:, :kc])
-            call("mpq_gram_chunk", ptr(x_work), x_work.stride(0), ptr(rhsJ), rhsJ.stride(0), ptr(Hsub), ptr(meta),
-                 ptr(order), c0, Kb, ptr(t["base_abs"]), ptr(t["base_parity"]), ptr(t["grid"]), ptr(t["sign_id"]),
-                 ptr(res_norm), ptr(idx), idx.stride(0), ptr(delta), ptr(accepted), ptr(evals), B, float(accept_tol))
+            if n_cand:
+                call("mpq_gram_chunk_topk", ptr(x_work), x_work.stride(0), ptr(rhsJ), rhsJ.stride(0), ptr(Hsub),
+                     ptr(meta), ptr(order), c0, Kb, ptr(topk_vals), ptr(topk_idx), n_cand, nb, ptr(res_norm), ptr(idx),
+                     idx.stride(0), ptr(delta), ptr(accepted), ptr(evals), B, float(accept_tol))
+            else:
+                call("mpq_gram_chunk", ptr(x_work), x_work.stride(0), ptr(rhsJ), rhsJ.stride(0), ptr(Hsub), ptr(meta),
+                     ptr(order), c0, Kb, ptr(t["base_abs"]), ptr(t["base_parity"]), ptr(t["grid"]), ptr(t["sign_id"]),
+                     ptr(res_norm), ptr(idx), idx.stride(0), ptr(delta), ptr(accepted), ptr(evals), B,
+                     float(accept_tol))
             ops.mm_nt(delta[:, :kc], VsJT[:, :kc], out=res_u, alpha=-1.0, beta=1.0)
         trace.append(float(res_norm.double().mean().item()))
         if on_sweep is not None:

@@ -80,6 +80,8 @@ class ModelQuantConfig:
     prior_tau: float = 0.2
     damping: float = 0.5
     polish_sweeps: int = 3
+    polish_mode: str = "block_cd"  # "block_cd" | "topk_block_cd" | "none"
+    topk_k: int = 16
     block_cd_backend: str = "auto"
     true_sequential: bool = True
     batch_size: int = 8          # calibration sequences per forward
@@ -141,7 +143,8 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
     qcfg = types.SimpleNamespace(bits=int(cfg.bits), group_size=int(cfg.group_size), desc_act=False,
                                  mpq=types.SimpleNamespace(rotation_mode=cfg.rotation_mode, solver="vamp"))
     vcfg = UniformVampConfig(iters=int(cfg.iters), prior_tau=float(cfg.prior_tau), damping=float(cfg.damping),
-                             polish_sweeps=int(cfg.polish_sweeps), block_cd_backend=cfg.block_cd_backend)
+                             polish_sweeps=int(cfg.polish_sweeps), polish_mode=str(cfg.polish_mode),
+                             topk_k=int(cfg.topk_k), block_cd_backend=cfg.block_cd_backend)
     with timer("embed"):
         hidden = inner.embed_tokens(ids)
         nxt = torch.empty_like(hidden)
@@ -271,6 +274,8 @@ class QuipModelConfig:
     iters: int = 16
     prior_tau: float = 0.25
     polish_sweeps: int = 3
+    polish_mode: str = "block_cd"  # "block_cd" | "topk_block_cd" | "none"
+    topk_k: int = 16
     sigma_reg: float = 1e-2
     seed: int = 0
     batch_size: int = 8
@@ -310,8 +315,8 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
     pos_emb = inner.rotary_emb(hidden[:1], position_ids=pos_ids)
     args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=int(cfg.iters), mpq_prior_tau=float(cfg.prior_tau),
                                  mpq_polish_sweeps=int(cfg.polish_sweeps), mpq_block_rows=1 << 30,
-                                 quant_solver="vamp", quant_polish_mode="block_cd", mpq_polish_metric="gram",
-                                 seed=int(cfg.seed))
+                                 quant_solver="vamp", quant_polish_mode=str(cfg.polish_mode), mpq_polish_metric="gram",
+                                 mpq_topk_k=int(cfg.topk_k), seed=int(cfg.seed))
     attrs: Dict[str, Any] = {}
     nl = len(inner.layers)
     # phase 1: every layer's Hessians from the float model (float activations feed the next layer)

@@ -8,6 +8,7 @@ TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).
   un-vendored; restated from the published GPTQ quantizer, parity vs GPTQModel unpinned)
 - serial row-block chain          (mpq/adapters/gptqmodel.py:911-1088)
 - calibration Hessian             (H = X^T X / T, then + 0.01 * mean(diag) * I)
+- GPTQ postprocess polish         (mpq/adapters/gptqmodel.py:1250-1470)
 """
 from __future__ import annotations
 
@@ -192,3 +193,53 @@ def proxy_loss(W_work: np.ndarray, Q_work: np.ndarray, H: np.ndarray) -> float:
     """tr((W - Q) H (W - Q)^T) — the proxy loss of the acceptance bar."""
     d = (W_work - Q_work).astype(np.float64)
     return float(((d @ H.astype(np.float64)) * d).sum())
+
+
+def postprocess_gptq(*, W, H, Q_init, scale_groups, zero_groups, g_idx, bits, polish_mode, polish_sweeps, topk_k=16,
+                     vamp_cfg: Optional[UniformVampConfig] = None, hessian_scale=0.5, jitter_base=1e-6,
+                     eigen_floor_scale=1e-6) -> Dict[str, Any]:
+    """mpq/adapters/gptqmodel.py:1250-1470 with the generic block CD (the eager/compile backends): the GPTQ codes
+    start a rank-space block CD (scalar provider, or the top-k provider with candidates from an auxiliary VAMP
+    solve); per-row improve merge; fail closed on a non-finite or worse module mean."""
+    from . import block_cd as OB
+    from . import topk as OT
+    from .uniform_vamp import dequant_from_q, nearest_atom_idx
+    W = W.astype(f32)
+    Q_init = Q_init.astype(f32)
+    maxq = 2 ** int(bits) - 1
+    H_work = (f32(hessian_scale) * H.astype(f32)).astype(f32)
+    lam, V, _ = vamp_hessian_eigen(H_work, jitter_base=jitter_base, floor_scale=eigen_floor_scale)
+    S = np.sqrt(lam).astype(f32)
+    Vs = (V * S[None, :]).astype(f32)
+    sf = scale_groups.astype(f32)[:, g_idx]
+    zf = zero_groups.astype(f32)[:, g_idx]
+    q_init = nearest_atom_idx(x=Q_init, scale_full=sf, zero_full=zf, maxq=maxq).astype(np.int32)
+    Y_u = (W @ Vs).astype(f32)
+    err_before = vamp_rankspace_error(Y_u=Y_u, x=Q_init, Vs=Vs)
+    if polish_mode == "topk_block_cd":
+        cfg = vamp_cfg or UniformVampConfig()
+        from dataclasses import replace
+        dbg: Dict[str, Any] = {}
+        solve_uniform_rankspace_vamp(W=W, x_rtn=Q_init, scale_full=sf, zero_full=zf, maxq=maxq, V=V,
+                                     Vh=np.ascontiguousarray(V.T), S=S, Vs=Vs, cfg=replace(cfg, polish_sweeps=0),
+                                     gram_full=None, debug=dbg)
+        tk = OT.uniform_map_topk(r1=dbg["r1"], gamma1=dbg["gamma1"], scale_full=sf, zero_full=zf, maxq=maxq,
+                                 prior_center=W, prior_tau=float(cfg.prior_tau), k=int(topk_k))
+        propose = OT.uniform_topk_provider(tk["topk_values"], tk["topk_q"])
+    else:
+        propose = OB.scalar_provider(sf, zf, maxq)
+    _, q_p, st = OB.block_coordinate_descent_rankspace(x=Q_init, Y_u=Y_u, Vs=Vs, block_size=1, propose=propose,
+                                                       sweeps=int(polish_sweeps), metric="diag",
+                                                       order_mode="greedy_gain", idxs_init=q_init)
+    q_p = q_p.astype(np.int32)
+    x_p = dequant_from_q(q_int=q_p, scale_full=sf, zero_full=zf)
+    err_after = vamp_rankspace_error(Y_u=Y_u, x=x_p, Vs=Vs)
+    improve = (err_after + f32(1e-12)) < err_before
+    Q_final = np.where(improve[:, None], x_p, Q_init).astype(f32)
+    q_final = np.where(improve[:, None], q_p, q_init).astype(np.int32)
+    err_final = vamp_rankspace_error(Y_u=Y_u, x=Q_final, Vs=Vs)
+    fail = (not np.isfinite(err_final).all()) or float(err_final.mean()) > float(err_before.mean()) + 1e-9
+    if fail:
+        Q_final, q_final, err_final = Q_init, q_init, err_before
+    return {"Q": Q_final, "q": q_final, "err_before": err_before, "err_final": err_final, "fail_closed": bool(fail),
+            "accepted_updates": st["accepted_updates"]}

@@ -257,7 +257,7 @@ class UniformVampConfig:
 
 
 def solve_uniform_rankspace_vamp(*, W, x_rtn, scale_full, zero_full, maxq, V, Vh, S, Vs, cfg,
-                                 gram_full=None, obs_precision_init=None):
+                                 gram_full=None, obs_precision_init=None, debug=None):
     """mpq/solver.py:426-830 with the CUDA polish dispatch (:299-333) when gram_full is given."""
     W = W.astype(f32)
     x_rtn = x_rtn.astype(f32)
@@ -402,6 +402,9 @@ def solve_uniform_rankspace_vamp(*, W, x_rtn, scale_full, zero_full, maxq, V, Vh
             err_final = np.where(improve, err_after, err_final)
         polish_updates = pst["accepted_updates"]
     rtn_err = vamp_rankspace_error(Y_u=Y_u, x=x_rtn, Vs=Vs)
+    if debug is not None:  # mpq/solver.py:757-777 (capture_r1)
+        debug["r1"] = r1.copy()
+        debug["gamma1"] = gamma1.copy()
     stats = {"obs_precision_initial": obs0, "obs_precision_final": obs, "best_iter": best_iter,
              "stop_iter": stop_iter, "alpha1_retry_count": retries, "gamma2_invalid_count": g2_invalid,
              "best_rankspace_error_mean": best_err_mean, "polish_updates": polish_updates,

@@ -280,6 +280,28 @@ def gen_e8p12_layer(out):
     np.savez_compressed(out / "e8p12_layer.npz", **cases)
 
 
+def gen_e8p12_topk_layer(out):
+    """mpq_refine_codebook with the top-k polish recipe (quant_polish_mode "topk_block_cd")."""
+    from mpq.adapters.quip_sharp import mpq_refine_codebook
+    cb = _reference_codebook()
+    cases = {}
+    m, n, block_rows, iters, k = 24, 128, 24, 8, 12
+    W, H = synth_layer(m, n, 777)
+    Wr = W / W.square().mean().sqrt() * 0.9
+    args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=iters, mpq_prior_tau=0.25, mpq_polish_sweeps=3,
+                                 mpq_block_rows=block_rows, mpq_blocks_per_chunk=1 << 20, mpq_compile_prior=False,
+                                 quant_solver="vamp", quant_polish_mode="topk_block_cd", mpq_polish_metric="gram",
+                                 mpq_topk_k=k)
+    hat0, q0 = cb.quantize(Wr.reshape(-1, 8))
+    hatWr, Qidxs, st = mpq_refine_codebook(Wr, H, hat0.view(m, n), q0.view(m, n // 8), cb, args,
+                                           module_name="golden.e8.topk")
+    for kk, v in dict(Wr=Wr, H=H, hatWr=hatWr, Qidxs=Qidxs).items():
+        cases[f"t/{kk}"] = _np(v)
+    cases["t/meta"] = np.array(json.dumps(dict(block_rows=block_rows, iters=iters, k=k,
+                                                surrogate_after=st["exact_surrogate_after_mean"])))
+    np.savez_compressed(out / "e8p12_topk_layer.npz", **cases)
+
+
 def _block_cd_problem(B, n, R, seed, scale_rows=0.02):
     """A rank-space least-squares problem Y_u = W Vs with Vs from a random Hessian's eigenbasis."""
     g = torch.Generator().manual_seed(seed)
@@ -414,9 +436,41 @@ def gen_topk(out):
     np.savez_compressed(out / "topk.npz", **cases)
 
 
+def gen_postprocess(out):
+    """postprocess_gptq_quantization (the MPQ polish of a GPTQ solution), block_cd and topk_block_cd."""
+    from mpq.adapters.gptqmodel import postprocess_gptq_quantization, GPTQAdapterConfig
+    cases = {}
+    for name, (m, n, bits, gs, mode, k) in {"pp_cd": (24, 128, 4, 32, "block_cd", 16),
+                                            "pp_topk": (20, 128, 3, 64, "topk_block_cd", 3)}.items():
+        W, H = synth_layer(m, n, 500 + m)
+        maxq = 2 ** bits - 1
+        sg = torch.empty(m, n // gs)
+        zg = torch.empty(m, n // gs)
+        for gi in range(n // gs):
+            q = MinMaxQuantizer(bits)
+            q.find_params(W[:, gi * gs:(gi + 1) * gs])
+            sg[:, gi], zg[:, gi] = q.scale[:, 0], q.zero[:, 0]
+        g_idx = torch.arange(n, dtype=torch.int32) // gs
+        sf, zf = sg[:, g_idx.long()], zg[:, g_idx.long()]
+        Q0 = sf * (torch.clamp(torch.round(W / sf) + zf, 0, maxq) - zf)
+        qcfg = types.SimpleNamespace(bits=bits, group_size=gs, mpq=types.SimpleNamespace(
+            polish_mode=mode, polish_sweeps=3, topk_k=k, iters=10, prior_tau=0.2, block_cd_backend=""))
+        Q, qf, _, _, _, _, st = postprocess_gptq_quantization(W=W, H=H, Q_init=Q0, scale_groups=sg, zero_groups=zg,
+                                                               g_idx=g_idx, qcfg=qcfg, module_name=f"golden.pp.{name}",
+                                                               adapter_cfg=GPTQAdapterConfig(block_rows=m))
+        for kk, v in dict(W=W, H=H, Q0=Q0, sg=sg, zg=zg, g_idx=g_idx, Q=Q, q=qf).items():
+            cases[f"{name}/{kk}"] = _np(v)
+        keep = {k2: st[k2] for k2 in ("rankspace_error_mean_before", "rankspace_error_mean_final", "polish_updates",
+                                       "module_fail_closed", "polish_assignment_changes", "raw_objective_mean_final")}
+        keep["fp"] = st["input_fingerprint"]
+        cases[f"{name}/meta"] = np.array(json.dumps(dict(bits=bits, gs=gs, mode=mode, k=k, stats=keep)))
+    np.savez_compressed(out / "postprocess.npz", **cases)
+
+
 GENERATORS = {"uniform_denoise": gen_uniform_denoise, "linear": gen_linear, "scalar_cd": gen_scalar_cd,
               "scalar_layer": gen_scalar_layer, "rotation": gen_rotation, "e8p12": gen_e8p12,
-              "e8p12_layer": gen_e8p12_layer, "block_cd": gen_block_cd, "topk": gen_topk}
+              "e8p12_layer": gen_e8p12_layer, "block_cd": gen_block_cd, "topk": gen_topk,
+              "postprocess": gen_postprocess, "e8p12_topk_layer": gen_e8p12_topk_layer}
 
 
 def main():

@@ -258,3 +258,42 @@ def test_mpq_refine_codebook_matches_reference_golden(cuda_dev, golden_dir, pcb,
     else:
         assert same.mean() >= 0.999, same.mean()
         assert abs(l - rl) <= 0.005 * rl, (l, rl)
+
+
+@pytest.mark.gpu
+def test_mpq_refine_codebook_topk_matches_reference_golden(cuda_dev, golden_dir, pcb):
+    """quant_polish_mode "topk_block_cd" through the QUIP# adapter, and the mpq/solvers wrapper."""
+    import types
+    from mpq_b200.adapters.quip_sharp import mpq_refine_codebook
+    z = np.load(golden_dir / "e8p12_topk_layer.npz")
+    g = lambda k: z[f"t/{k}"]
+    meta = json.loads(str(g("meta")))
+    args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=meta["iters"], mpq_prior_tau=0.25, mpq_polish_sweeps=3,
+                                 mpq_block_rows=meta["block_rows"], quant_solver="vamp",
+                                 quant_polish_mode="topk_block_cd", mpq_polish_metric="gram", mpq_topk_k=meta["k"])
+    Wr, H = _t(g("Wr"), cuda_dev), _t(g("H"), cuda_dev)
+    hat, idx, st = mpq_refine_codebook(Wr, H, Wr.clone(), torch.zeros(Wr.shape[0], Wr.shape[1] // 8,
+                                                                     dtype=torch.int64, device=cuda_dev), pcb, args,
+                                       module_name="golden.e8.topk")
+    assert st["polish_mode"] == "topk_block_cd"
+    same = (idx.cpu().numpy() == g("Qidxs")).mean()
+    assert same >= 0.995, same
+    l = OL.proxy_loss(g("Wr"), hat.cpu().numpy(), g("H"))
+    rl = OL.proxy_loss(g("Wr"), g("hatWr"), g("H"))
+    assert abs(l - rl) <= 0.005 * rl, (l, rl)
+
+
+@pytest.mark.gpu
+def test_solvers_topk_polish_wrapper(cuda_dev, ocb, pcb):
+    from mpq_b200 import solver as PS
+    from mpq_b200.solvers import solve_e8p12_rankspace_vamp_topk_polish
+    W, H, V, S, Vs = _layer(16, 128, 5)
+    x0, _ = OE.rtn_init(W, ocb)
+    d = lambda a: _t(a, cuda_dev)
+    kw = dict(Wr=d(W), hatWr_init=d(x0), cb=pcb, V=d(V), Vh=d(V.T.copy()), S=d(S), Vs=d(Vs))
+    hat_a, idx_a, err_a, _ = solve_e8p12_rankspace_vamp_topk_polish(cfg=PS.E8P12VampConfig(iters=6), candidate_k=5,
+                                                                   **kw)
+    hat_b, idx_b, err_b, st = PS.solve_e8p12_rankspace_vamp(
+        cfg=PS.E8P12VampConfig(iters=6, polish_mode="topk_block_cd", topk_k=5), **kw)
+    assert torch.equal(idx_a, idx_b) and torch.equal(err_a, err_b)
+    assert st["polish_mode"] == "topk_block_cd"

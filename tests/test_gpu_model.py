@@ -59,3 +59,26 @@ def test_quantize_tiny_llama_e8p12(cuda_dev):
     with torch.inference_mode():
         logits = model(ids[:2].to(cuda_dev)).logits.float()
     assert torch.isfinite(logits).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("walk", ["gptq", "quip"])
+def test_quantize_tiny_llama_topk_polish(cuda_dev, walk):
+    """Both whole-model walks with the top-k polish recipe."""
+    from mpq_b200.model import (ModelQuantConfig, QuipModelConfig, build_synthetic_decoder, calibration_ids,
+                                quantize_model, quantize_model_quip)
+    model = build_synthetic_decoder("tiny_llama", device=cuda_dev, seed=0)
+    ids = calibration_ids(8, 64, model.config.vocab_size, seed=3)
+    if walk == "gptq":
+        out = quantize_model(model, ids, ModelQuantConfig(bits=3, group_size=64, iters=6, polish_sweeps=1, batch_size=4,
+                                                          polish_mode="topk_block_cd", topk_k=4))
+        for name, st in out["modules"].items():
+            assert st["rankspace_error_mean"] <= st["rtn_rankspace_error_mean"] * (1 + 1e-6), name
+    else:
+        out = quantize_model_quip(model, ids, QuipModelConfig(iters=6, polish_sweeps=1, batch_size=4,
+                                                              polish_mode="topk_block_cd", topk_k=8))
+        for key, g in out["groups"].items():
+            assert g["surrogate_after"] <= g["surrogate_before"] * (1 + 1e-6), key
+    with torch.inference_mode():
+        logits = model(ids[:2].to(cuda_dev)).logits.float()
+    assert torch.isfinite(logits).all()

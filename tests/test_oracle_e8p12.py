@@ -92,3 +92,19 @@ def test_e8p12_layer_matches_reference(golden_dir, cb, case):
     ref_loss = OL.proxy_loss(g("Wr"), g("hatWr"), H)
     my_loss = OL.proxy_loss(g("Wr"), out["hatWr"], H)
     assert abs(my_loss - ref_loss) <= 0.005 * ref_loss
+
+
+def test_e8p12_topk_layer_matches_reference(golden_dir, cb):
+    """The QUIP# adapter with the top-k polish recipe (candidates from the final VAMP message)."""
+    z = np.load(golden_dir / "e8p12_topk_layer.npz")
+    g = lambda k: z[f"t/{k}"]
+    meta = json.loads(str(g("meta")))
+    cfg = E.E8P12VampConfig(iters=meta["iters"], prior_tau=0.25, polish_sweeps=3, polish_mode="topk_block_cd",
+                            topk_k=meta["k"])
+    out = E.refine_codebook(Wr=g("Wr"), Hr=g("H"), cb=cb, cfg=cfg, block_rows=meta["block_rows"])
+    agree = (out["Qidxs"] == g("Qidxs")).mean()
+    assert agree >= 0.999, agree
+    H = g("H")
+    ref_loss = OL.proxy_loss(g("Wr"), g("hatWr"), H)
+    my_loss = OL.proxy_loss(g("Wr"), out["hatWr"], H)
+    assert abs(my_loss - ref_loss) <= 0.005 * ref_loss

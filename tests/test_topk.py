@@ -232,3 +232,76 @@ def test_gpu_topk_pick_matches_oracle(cuda_dev):
              ptr(out_v), 8, ptr(out_i))
         np.testing.assert_array_equal(out_i.cpu().numpy(), ref_i)
         np.testing.assert_array_equal(out_v.cpu().numpy(), ref_v)
+
+
+class _Wrapped:
+    """A provider that is not one of the built-in classes: the engine takes its generic per-block loop."""
+
+    def __init__(self, inner):
+        self.inner = inner
+
+    def propose(self, **kw):
+        return self.inner.propose(**kw)
+
+
+@pytest.mark.gpu
+def test_gpu_fused_uniform_topk_engine_matches_generic(cuda_dev, gz):
+    from mpq_b200.block_cd import BlockCDConfig, UniformTopKProvider, block_coordinate_descent_rankspace
+    c = "cd_u"
+    args = dict(x=_d(gz[f"{c}/x0"], cuda_dev), Y_u=_d(gz[f"{c}/Y_u"], cuda_dev), Vs=_d(gz[f"{c}/Vs"], cuda_dev),
+                block_size=1, cfg=BlockCDConfig(sweeps=3, metric="diag"), idxs_init=_d(gz[f"{c}/q0"], cuda_dev))
+    mk = lambda: UniformTopKProvider(topk_values=_d(gz[f"{c}/tv"], cuda_dev), topk_q=_d(gz[f"{c}/tq"], cuda_dev))
+    x_f, q_f, s_f = block_coordinate_descent_rankspace(provider=mk(), **args)
+    x_g, q_g, s_g = block_coordinate_descent_rankspace(provider=_Wrapped(mk()), **args)
+    assert (q_f.cpu() == q_g.cpu()).float().mean() >= 0.99
+    assert abs(s_f["accepted_updates"] - s_g["accepted_updates"]) <= 0.01 * s_g["accepted_updates"] + 2
+    np.testing.assert_allclose([t["stabilized_objective_mean"] for t in s_f["sweep_trace"]],
+                               [t["stabilized_objective_mean"] for t in s_g["sweep_trace"]], rtol=2e-3)
+    assert s_f["stabilized_objective_nonincreasing"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ["cd_eg"])
+def test_gpu_fused_e8p12_topk_engine_matches_generic(cuda_dev, gz, case):
+    from mpq_b200.block_cd import BlockCDConfig, E8P12TopKProvider, block_coordinate_descent_rankspace
+    from mpq_b200.codebook import E8P12_codebook
+    cb = E8P12_codebook()
+    args = dict(x=_d(gz[f"{case}/x0"], cuda_dev), Y_u=_d(gz[f"{case}/Y_u"], cuda_dev),
+                Vs=_d(gz[f"{case}/Vs"], cuda_dev), block_size=8, cfg=BlockCDConfig(sweeps=3, metric="gram"),
+                idxs_init=_d(gz[f"{case}/i0"], cuda_dev))
+    mk = lambda: E8P12TopKProvider(cb=cb, topk_idxs=_d(gz[f"{case}/ti"], cuda_dev))
+    _, i_f, s_f = block_coordinate_descent_rankspace(provider=mk(), **args)
+    _, i_g, s_g = block_coordinate_descent_rankspace(provider=_Wrapped(mk()), **args)
+    assert i_f.dtype == torch.int64
+    assert (i_f.cpu() == i_g.cpu()).float().mean() >= 0.99
+    assert abs(s_f["accepted_updates"] - s_g["accepted_updates"]) <= 0.02 * s_g["accepted_updates"] + 2
+
+
+@pytest.mark.gpu
+def test_gpu_fused_topk_engines_large(cuda_dev):
+    """A 512 x 1024 problem through the fused top-k engines against the oracle engine."""
+    from mpq_b200.block_cd import BlockCDConfig, UniformTopKProvider, block_coordinate_descent_rankspace
+    rng = np.random.default_rng(17)
+    B, n, maxq, k = 96, 512, 15, 6
+    A = rng.standard_normal((2 * n, n)).astype(np.float32) * np.exp(rng.standard_normal(n)).astype(np.float32) ** 0.5
+    H = (A.T @ A / (2 * n)).astype(np.float32) + 0.01 * np.eye(n, dtype=np.float32)
+    lam, V = np.linalg.eigh(H.astype(np.float64))
+    Vs = (V[:, ::-1] * np.sqrt(lam[::-1])).astype(np.float32)
+    W = (rng.standard_normal((B, n)) * 0.02).astype(np.float32)
+    s = np.full((B, n), 0.006, np.float32)
+    z = np.full((B, n), 8.0, np.float32)
+    r1 = (W + rng.standard_normal((B, n)).astype(np.float32) * 0.002).astype(np.float32)
+    tk = OT.uniform_map_topk(r1=r1, gamma1=np.full((B, 1), 5e4, np.float32), scale_full=s, zero_full=z, maxq=maxq,
+                             prior_center=W, prior_tau=0.2, k=k)
+    q0 = tk["topk_q"][:, :, 0].astype(np.int32)
+    x0 = tk["topk_values"][:, :, 0].copy()
+    Y_u = (W @ Vs).astype(np.float32)
+    _, rq, rst = OB.block_coordinate_descent_rankspace(
+        x=x0, Y_u=Y_u, Vs=Vs, block_size=1, propose=OT.uniform_topk_provider(tk["topk_values"], tk["topk_q"]),
+        sweeps=2, metric="diag", order_mode="greedy_gain", idxs_init=q0)
+    x, q, st = block_coordinate_descent_rankspace(
+        x=_d(x0, cuda_dev), Y_u=_d(Y_u, cuda_dev), Vs=_d(Vs, cuda_dev), block_size=1,
+        provider=UniformTopKProvider(topk_values=_d(tk["topk_values"], cuda_dev), topk_q=_d(tk["topk_q"], cuda_dev)),
+        cfg=BlockCDConfig(sweeps=2, metric="diag"), idxs_init=_d(q0, cuda_dev))
+    assert (q.cpu().numpy() == rq).mean() >= 0.99
+    assert abs(st["accepted_updates"] - rst["accepted_updates"]) <= 0.01 * rst["accepted_updates"] + 2
