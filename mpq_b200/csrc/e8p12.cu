@@ -543,44 +543,74 @@ k_e8p12_topk(E8Args a, E8Tab tab, int k, int* __restrict__ idx_out, float* __res
         ssid[(e0 + 1) * 32 + lane] = (unsigned char)(mismatch ? neg[br] ^ b2 : neg[br] ^ b1 ^ b2);
       }
     }
-    // k rounds of a warp argmax; each lane keeps the best of its own 32 entries (ascending e = ascending f)
+    // k rounds of a warp argmax.  Each lane keeps the two best of its own 32 entries (ascending e = ascending f,
+    // so a strict comparison keeps the first of equal scores); a lane rescans its entries only when it wins a
+    // round with no valid second entry.  Round t's winner is parked in lane t % 32 and written out every 32
+    // rounds (the index-table and codeword loads of 32 winners run in parallel).
+    auto top2 = [&](unsigned taken_mask, float& b1, int& e1, float& b2, int& e2) {
+      b1 = -INFINITY; e1 = -1; b2 = -INFINITY; e2 = -1;
+      #pragma unroll 4
+      for (int e = 0; e < 32; ++e) {
+        if ((taken_mask >> e) & 1u) continue;
+        const float v = ssc[e * 32 + lane];
+        if (e1 < 0 || v > b1) {
+          b2 = b1; e2 = e1; b1 = v; e1 = e;
+        } else if (e2 < 0 || v > b2) {
+          b2 = v; e2 = e;
+        }
+      }
+    };
     unsigned taken = 0u;
-    float lbest = -INFINITY;
-    int le = -1;
-    #pragma unroll 1
-    for (int e = 0; e < 32; ++e) {
-      const float v = ssc[e * 32 + lane];
-      if (le < 0 || v > lbest) { lbest = v; le = e; }
-    }
+    float b1, b2;
+    int e1, e2;
+    top2(0u, b1, e1, b2, e2);
+    bool second_valid = true;
+    int park_f = -1;
+    float park_sc = 0.f;
     #pragma unroll 1
     for (int t = 0; t < k; ++t) {
-      float wb = lbest;
-      int wf = le < 0 ? -1 : 512 * (le >> 4) + 64 * ((le >> 1) & 7) + 2 * lane + (le & 1);
+      float wb = b1;
+      int wf = e1 < 0 ? -1 : 512 * (e1 >> 4) + 64 * ((e1 >> 1) & 7) + 2 * lane + (e1 & 1);
       #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, wb, o);
         const int of2 = __shfl_xor_sync(0xffffffffu, wf, o);
         if (of2 >= 0 && (wf < 0 || ob > wb || (ob == wb && of2 < wf))) { wb = ob; wf = of2; }
       }
-      if (wf < 0) break;  // unreachable for k <= 1024
-      const int wbr = wf >> 9, wai = (wf >> 1) & 255, ws = wf & 1;
-      const int wl = wai & 31, we = (8 * wbr + (wai >> 5)) * 2 + ws;
-      const int sid = ssid[we * 32 + wl];
-      const int cidx = tab.idx_lut[wbr * 65536 + wai * 256 + sid];
-      if (lane == 0) {
-        io[t] = cidx;
-        if (so) so[t] = wb;
+      if (lane == (t & 31)) { park_f = wf; park_sc = wb; }
+      const int wai = (wf >> 1) & 255;
+      if (wf >= 0 && lane == (wai & 31)) {  // the winner's lane drops the entry
+        taken |= 1u << e1;
+        if (second_valid && e2 >= 0) {
+          b1 = b2; e1 = e2; b2 = -INFINITY; e2 = -1;
+          second_valid = false;
+        } else {
+          top2(taken, b1, e1, b2, e2);
+          second_valid = true;
+        }
       }
-      if (vo && lane < 8) vo[t * 8 + lane] = cidx >= 0 ? tab.grid[(int64_t)cidx * 8 + lane] : __int_as_float(0x7fc00000);
-      if (lane == wl) {
-        taken |= 1u << we;
-        lbest = -INFINITY;
-        le = -1;
-        #pragma unroll 1
-        for (int e = 0; e < 32; ++e) {
-          if ((taken >> e) & 1u) continue;
-          const float v = ssc[e * 32 + lane];
-          if (le < 0 || v > lbest) { lbest = v; le = e; }
+      if ((t & 31) == 31 || t == k - 1) {  // write the parked winners of rounds (t & ~31) .. t
+        const int tt = (t & ~31) + lane;
+        if (tt <= t) {
+          int cidx = -1;
+          if (park_f >= 0) {
+            const int pbr = park_f >> 9, pai = (park_f >> 1) & 255, ps = park_f & 1;
+            const int pe = (8 * pbr + (pai >> 5)) * 2 + ps;
+            cidx = tab.idx_lut[pbr * 65536 + pai * 256 + ssid[pe * 32 + (pai & 31)]];
+          }
+          io[tt] = cidx;
+          if (so) so[tt] = park_sc;
+          if (vo) {
+            float4 v0 = make_float4(__int_as_float(0x7fc00000), __int_as_float(0x7fc00000),
+                                    __int_as_float(0x7fc00000), __int_as_float(0x7fc00000));
+            float4 v1 = v0;
+            if (cidx >= 0) {
+              v0 = __ldg(reinterpret_cast<const float4*>(tab.grid + (int64_t)cidx * 8));
+              v1 = __ldg(reinterpret_cast<const float4*>(tab.grid + (int64_t)cidx * 8 + 4));
+            }
+            reinterpret_cast<float4*>(vo + (int64_t)tt * 8)[0] = v0;
+            reinterpret_cast<float4*>(vo + (int64_t)tt * 8)[1] = v1;
+          }
         }
       }
     }
@@ -646,6 +676,8 @@ MPQ_API int mpq_e8p12_topk(const float* r1, int64_t ld_r1, const float* center, 
   if (st) return st;
   if (B == 0 || nb == 0) return MPQ_OK;
   MPQ_CHECK_ARG(gamma && idx_out, "mpq_e8p12_topk: gamma and idx_out are required");
+  MPQ_CHECK_ARG(((uintptr_t)grid & 15) == 0 && ((uintptr_t)val_out & 15) == 0,
+                "mpq_e8p12_topk: grid and val_out must be 16-byte aligned");
   E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
   E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
   const int64_t items = (int64_t)B * nb;

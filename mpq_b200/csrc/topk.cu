@@ -62,6 +62,56 @@ __global__ void k_uniform_topk(const float* __restrict__ r1, int64_t ld_r1, cons
   }
 }
 
+// The same selection for grids of L <= 16 levels without a sorted list: all L scores stay in registers and the
+// output position of level q is its rank  #{q' : s[q'] > s[q] or (s[q'] == s[q] and q' < q)}.
+template <int L>
+__global__ void k_uniform_topk_small(const float* __restrict__ r1, int64_t ld_r1, const float* __restrict__ center,
+                                     int64_t ld_c, const float* __restrict__ scale, const float* __restrict__ zero,
+                                     int64_t ld_p, int gshift, const float* __restrict__ gamma, int B, int n,
+                                     float prior_tau, int k, int* __restrict__ out_q, float* __restrict__ out_v,
+                                     float* __restrict__ out_s) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= (int64_t)B * n) return;
+  const int b = (int)(i / n), j = (int)(i % n);
+  const float r = r1[b * ld_r1 + j];
+  const float s = scale[b * ld_p + (j >> gshift)];
+  const float z = zero[b * ld_p + (j >> gshift)];
+  const float ng = fmul(-0.5f, gamma[b]);
+  const bool prior = prior_tau > 0.f && center;
+  const float c = prior ? center[b * ld_c + j] : 0.f;
+  float tau2 = 1.f;
+  if (prior) {
+    const float st = fmul(prior_tau, fmaxf(s, 1e-12f));
+    tau2 = fmul(st, st);
+  }
+  float sc[L], at[L];
+  #pragma unroll
+  for (int q = 0; q < L; ++q) {
+    at[q] = fmul(s, fsub((float)q, z));
+    const float d = fsub(at[q], r);
+    float v = fmul(ng, fmul(d, d));
+    if (prior) {
+      const float dc = fsub(at[q], c);
+      v = fsub(v, fdiv(fmul(0.5f, fmul(dc, dc)), tau2));
+    }
+    sc[q] = v;
+  }
+  float key[L];  // NaN scores rank last, so the ranks are a permutation and every output slot is written
+  #pragma unroll
+  for (int q = 0; q < L; ++q) key[q] = sc[q] != sc[q] ? -INFINITY : sc[q];
+  #pragma unroll
+  for (int q = 0; q < L; ++q) {
+    int rank = 0;
+    #pragma unroll
+    for (int p = 0; p < L; ++p) rank += (key[p] > key[q] || (key[p] == key[q] && p < q)) ? 1 : 0;
+    if (rank < k) {
+      out_q[i * k + rank] = q;
+      out_v[i * k + rank] = at[q];
+      if (out_s) out_s[i * k + rank] = sc[q];
+    }
+  }
+}
+
 // Per row: the candidate (of k, each bs floats) nearest to the row's target.  chol != null: metric distance
 // |tL|^2 + |cL|^2 - 2 (tL).(cL) clamped at 0 (products and sums in index order); otherwise sum_j (c_j - t_j)^2.
 // First minimum wins.  Writes the chosen values and, when cand_idx is given, its index.
@@ -127,8 +177,21 @@ MPQ_API int mpq_uniform_topk(const float* r1, int64_t ld_r1, const float* center
   if (B == 0 || n == 0) return MPQ_OK;
   MPQ_CHECK_ARG(r1 && scale && zero && gamma && out_q && out_v, "mpq_uniform_topk: null pointer");
   const int64_t total = (int64_t)B * n;
-  k_uniform_topk<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      r1, ld_r1, center, ld_c, scale, zero, ld_p, gshift, gamma, B, n, maxq, prior_tau, k, out_q, out_v, out_s);
+  const unsigned grid = (unsigned)((total + 255) / 256);
+  cudaStream_t st = (cudaStream_t)stream;
+#define MPQ_TOPK_SMALL(L_)                                                                                            \
+  k_uniform_topk_small<L_><<<grid, 256, 0, st>>>(r1, ld_r1, center, ld_c, scale, zero, ld_p, gshift, gamma, B, n, \
+                                                 prior_tau, k, out_q, out_v, out_s)
+  switch (maxq) {
+    case 1: MPQ_TOPK_SMALL(2); break;
+    case 3: MPQ_TOPK_SMALL(4); break;
+    case 7: MPQ_TOPK_SMALL(8); break;
+    case 15: MPQ_TOPK_SMALL(16); break;
+    default:
+      k_uniform_topk<<<grid, 256, 0, st>>>(r1, ld_r1, center, ld_c, scale, zero, ld_p, gshift, gamma, B, n, maxq,
+                                           prior_tau, k, out_q, out_v, out_s);
+  }
+#undef MPQ_TOPK_SMALL
   return launch_status("mpq_uniform_topk");
 }
 

@@ -875,7 +875,7 @@ def solve_e8p12_rankspace_vamp(
             metric_rows_per_chunk=int(cfg.polish_metric_rows_per_chunk),
             polish_max_blocks=int(getattr(cfg, "polish_max_blocks", 0) or 0), _ops=(opVs, opVsT),
             topk_idxs=None if topk is None else topk["topk_idxs"], topk_vals=None if topk is None else topk["topk_vals"])
-        if debug_out is not None and topk is not None:
+        if debug_out is not None and topk is not None and not bool(debug_out.get("summary_only", False)):
             debug_out["topk_idxs"] = topk["topk_idxs"].detach().to(device="cpu")
         del topk
         polish_gain = float((err_before.double() - err_after.double()).mean().item())

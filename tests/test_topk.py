@@ -116,7 +116,7 @@ def test_gpu_uniform_topk_matches_reference(cuda_dev, gz, case):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("bits,k,group", [(4, 16, 0), (3, 5, 64), (2, 7, 32)])
+@pytest.mark.parametrize("bits,k,group", [(4, 16, 0), (3, 5, 64), (2, 7, 32), (5, 9, 32), (8, 40, 64)])
 def test_gpu_uniform_topk_matches_oracle(cuda_dev, bits, k, group):
     from mpq_b200.topk import uniform_map_topk
     rng = np.random.default_rng(bits * 31 + k)
