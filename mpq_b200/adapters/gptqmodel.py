@@ -465,3 +465,105 @@ def postprocess_gptq_quantization(
             setattr(mpq_cfg, "_layer_stats", bucket)
         bucket.append(stats)
     return Q_final, q_final, scale_groups, zero_groups, g_idx, float(time.time() - start), stats
+
+
+@torch.inference_mode()
+def resolve_internal_rotation(*, requested: str, cols: int, module_name: str, seed: int,
+                              device: torch.device) -> Dict[str, Any]:
+    """The rotation plan of one linear (mpq/adapters/gptqmodel.py:46-118): requested / effective basis, block
+    Hadamard width and the module's Rademacher signs (None unless the internal block Hadamard applies)."""
+    req = str(requested or "none").strip().lower()
+    plan = {"requested": req or "none", "effective": req or "none", "mode": "none", "signs": None, "block_dim": 1,
+            "fallback_reason": "", "internal": False}
+    if req in {"", "none", "model_random", "model_hadamard"}:
+        plan["requested"] = plan["effective"] = req or "none"
+        return plan
+    if req != "internal_hadamard":
+        raise ValueError("mpq only supports rotation in {none, model_hadamard, model_random, internal_hadamard}; "
+                         f"got rotation={requested!r}.")
+    mode, block_dim = resolve_block_hadamard_plan(int(cols))
+    if mode == "none":
+        plan.update(effective="none", fallback_reason=f"unsupported_block_hadamard_width:{int(cols)}")
+        return plan
+    plan.update(effective="internal_block_hadamard", mode="block", block_dim=int(block_dim), internal=True,
+                signs=sample_rademacher_signs(width=int(cols), key=f"{module_name}:full", seed=int(seed),
+                                              device=device))
+    return plan
+
+
+@torch.inference_mode()
+def prepare_gptq_internal_hadamard(*, W: torch.Tensor, H: torch.Tensor, qcfg: Any, module_name: str,
+                                   adapter_cfg: GPTQAdapterConfig = GPTQAdapterConfig(),
+                                   ) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
+    """W and H in the solver basis for GPTQModel's own solve (mpq/adapters/gptqmodel.py:593-633):
+    W diag(s) Had and Had^T diag(s) H diag(s) Had, with the plan that undoes it."""
+    mpq_cfg = getattr(qcfg, "mpq", None)
+    plan = resolve_internal_rotation(
+        requested=str(getattr(mpq_cfg, "rotation_mode", getattr(qcfg, "rotation", None) or "none")),
+        cols=int(W.shape[1]), module_name=str(module_name), seed=int(adapter_cfg.rotation_seed), device=W.device)
+    if float(adapter_cfg.hessian_scale) <= 0.0:
+        raise ValueError(f"hessian_scale must be positive, got {float(adapter_cfg.hessian_scale)}")
+    W32 = W.to(torch.float32).contiguous()
+    H32 = H.to(device=W.device, dtype=torch.float32).contiguous()
+    if not plan["internal"]:
+        return W32, H32, plan
+    s, had = plan["signs"], int(plan["block_dim"])
+    W_work = apply_right_block_hadamard(W32, signs=s, had_dim=had)
+    H_work = apply_right_block_hadamard(H32.T.contiguous(), signs=s, had_dim=had).T.contiguous()
+    H_work = apply_right_block_hadamard(H_work, signs=s, had_dim=had).contiguous()
+    return W_work, H_work, plan
+
+
+@torch.inference_mode()
+def finalize_gptq_internal_hadamard(*, Q_work: torch.Tensor, rotation_plan: Dict[str, Any]) -> torch.Tensor:
+    """Back to the original basis (mpq/adapters/gptqmodel.py:636-648)."""
+    if not bool(rotation_plan.get("internal", False)):
+        return Q_work.to(torch.float32).contiguous()
+    return apply_right_block_hadamard_inverse(Q_work.to(torch.float32), signs=rotation_plan["signs"],
+                                              had_dim=int(rotation_plan["block_dim"])).contiguous()
+
+
+@torch.inference_mode()
+def install_internal_hadamard_input_hooks(model: torch.nn.Module, *, rotation_seed: int = 0) -> int:
+    """Rotate the inputs of packed internal-Hadamard linears at load time (mpq/adapters/gptqmodel.py:1166-1247).
+
+    The packed qweight/qzeros/scales of such a module hold the codes in the solver basis; the pre-hook applies
+    the module's signed block Hadamard (same key "<module>:full" and seed as the solve) to its input, so the
+    packed weights reproduce the dense inverse-rotated weights.  Returns the number of hooks installed."""
+    installed = 0
+    for name, module in model.named_modules():
+        if not name or getattr(module, "_mpq_internal_hadamard_hook", None) is not None:
+            continue
+        if not all(hasattr(module, a) for a in ("qweight", "qzeros", "scales")):
+            continue
+        width = int(getattr(module, "in_features", 0) or getattr(module, "infeatures", 0) or 0)
+        if width <= 0:
+            qweight = getattr(module, "qweight", None)
+            bits = int(getattr(module, "bits", 0) or 0)
+            pdt = getattr(qweight, "dtype", torch.int32)
+            pack_bits = torch.iinfo(pdt).bits if isinstance(pdt, torch.dtype) and not pdt.is_floating_point else 32
+            if isinstance(qweight, torch.Tensor) and bits > 0:
+                width = int(qweight.shape[0]) * int(pack_bits // bits)
+        if width <= 0:
+            raise RuntimeError(f"Cannot determine MPQ input width for quantized module {name!r}")
+        mode, block_dim = resolve_block_hadamard_plan(width)
+        if mode == "none":
+            continue
+        cache: Dict[torch.device, torch.Tensor] = {}
+
+        def _rotate(_module, args, *, _name=name, _width=width, _block=block_dim, _cache=cache):
+            if not args or not isinstance(args[0], torch.Tensor):
+                return args
+            v = args[0]
+            if int(v.shape[-1]) != int(_width):
+                raise RuntimeError(f"MPQ input width mismatch for {_name!r}: expected {_width}, got {int(v.shape[-1])}")
+            s = _cache.get(v.device)
+            if s is None:
+                s = sample_rademacher_signs(width=int(_width), key=f"{_name}:full", seed=int(rotation_seed),
+                                            device=v.device)
+                _cache[v.device] = s
+            return (apply_right_block_hadamard(v, signs=s, had_dim=int(_block)).to(v.dtype), *args[1:])
+
+        module._mpq_internal_hadamard_hook = module.register_forward_pre_hook(_rotate)
+        installed += 1
+    return installed

@@ -43,3 +43,92 @@ def pack_gptq(q_int: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor, g_id
     qzeros = _pack(z8, z8.stride(0), 1, out_f, groups, bits, 1).t().contiguous()
     return {"qweight": qweight, "qzeros": qzeros, "scales": scale.to(torch.float16).t().contiguous(),
             "g_idx": g_idx.to(torch.int32).contiguous()}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# checkpoint directories
+# ---------------------------------------------------------------------------------------------------------------
+
+def save_gptq_checkpoint(model, modules: Dict[str, Dict], out_dir, *, bits: int, group_size: int,
+                         rotation: str = "internal_hadamard", rotation_seed: int = 0, extra: Dict = None) -> str:
+    """A GPTQ-format model directory: ``model.safetensors`` with every packed linear's ``<name>.qweight``,
+    ``.qzeros``, ``.scales``, ``.g_idx`` (+ ``.bias``) and all other parameters as they are, ``config.json`` and
+    ``quantize_config.json`` (GPTQ v1, asymmetric, no act-order).  With the internal Hadamard rotation the codes
+    are in the solver basis: a loader installs the input hooks
+    (``mpq_b200.adapters.gptqmodel.install_internal_hadamard_input_hooks``), as the reference's load path does.
+    ``modules`` is ``quantize_model(...)["modules"]`` run with ``export_gptq=True``.  Returns the directory."""
+    import json
+    import os
+
+    from safetensors.torch import save_file
+    os.makedirs(out_dir, exist_ok=True)
+    tensors: Dict[str, torch.Tensor] = {}
+    packed = set()
+    for name, entry in modules.items():
+        g = entry.get("gptq")
+        if g is None:
+            raise ValueError(f"module {name!r} has no packed tensors (run quantize_model with export_gptq=True)")
+        for k in ("qweight", "qzeros", "scales", "g_idx"):
+            tensors[f"{name}.{k}"] = g[k].detach().cpu().contiguous()
+        packed.add(name)
+    for pname, p in model.state_dict().items():
+        mod = pname.rsplit(".", 1)[0]
+        if mod in packed:
+            if pname.endswith(".bias"):
+                tensors[pname] = p.detach().cpu().contiguous()
+            continue
+        tensors[pname] = p.detach().cpu().contiguous()
+    # tied embeddings share storage: safetensors stores each tensor once
+    seen: Dict[int, str] = {}
+    for k in list(tensors):
+        ptr_ = tensors[k].data_ptr()
+        if ptr_ in seen and tensors[k].numel() and tensors[seen[ptr_]].shape == tensors[k].shape:
+            tensors[k] = tensors[k].clone()
+        seen[ptr_] = k
+    save_file(tensors, os.path.join(out_dir, "model.safetensors"), metadata={"format": "pt"})
+    model.config.to_json_file(os.path.join(out_dir, "config.json"))
+    qc = {"bits": int(bits), "group_size": int(group_size), "desc_act": False, "sym": False, "true_sequential": True,
+          "quant_method": "gptq", "checkpoint_format": "gptq",
+          "mpq": {"rotation_mode": str(rotation), "rotation_seed": int(rotation_seed),
+                  "rotation_effective": "internal_block_hadamard" if rotation == "internal_hadamard" else rotation}}
+    if extra:
+        qc["mpq"].update(extra)
+    with open(os.path.join(out_dir, "quantize_config.json"), "w") as f:
+        json.dump(qc, f, indent=2, sort_keys=True)
+    return str(out_dir)
+
+
+def quip_group_attrs(entry: Dict) -> Dict:
+    """The saved attribute dict of one QUIP# group (mpq/quip_generic.py:398-426): Qidxs, SU, SV (fp16, the RMS scale
+    folded into SV), fused, shapes, scales.  Qidxs are stored unpacked (int16, rows x cols / 8): the packed layout
+    of QUIP#'s decode kernels belongs to QUIP#'s codebook class, which is not part of the reference tree."""
+    keep = ("Qidxs", "SU", "SV", "fused", "shapes", "scales", "proxy_error", "surrogate_before", "surrogate_after")
+    out = {k: entry[k] for k in keep if k in entry}
+    out.update(packed=False, codebook="E8P12", codesz=8, scaleWH=None)
+    return out
+
+
+def save_quip_layer(out_dir, li: int, layer, groups: Dict[str, Dict]) -> None:
+    """``{li}_{group}.pt`` for each quantized group of layer li and ``{li}_layernorm.pt`` (mpq/quip_generic.py:
+    650-734)."""
+    import os
+    os.makedirs(out_dir, exist_ok=True)
+    for name, entry in groups.items():
+        torch.save(quip_group_attrs(entry), os.path.join(out_dir, f"{li}_{name}.pt"))
+    payload = {"input_layernorm": layer.input_layernorm.weight.detach().cpu(),
+               "post_attention_layernorm": layer.post_attention_layernorm.weight.detach().cpu()}
+    torch.save(payload, os.path.join(out_dir, f"{li}_layernorm.pt"))
+
+
+def save_quip_config(out_dir, model, quant_args: Dict) -> None:
+    """``config.pt``: the quantization arguments and the model config with its ``quip_params``
+    (mpq/quip_generic.py:936-953)."""
+    import copy
+    import os
+    os.makedirs(out_dir, exist_ok=True)
+    cfg = copy.deepcopy(model.config)
+    cfg.update({"quip_params": {"lora_rank": 0, "rescale_WH": False, "codebook": "E8P12", "codebook_version": 1,
+                                "codesz": 8, "idx_dtype": "torch.int16", "packsz": 1, "resid_scale_override": -1,
+                                "adapter_name": "llama_like_dense_decoder"}})
+    torch.save({"quant_args": dict(quant_args), "model_config": cfg, "adapter_name": "llama_like_dense_decoder"},
+               os.path.join(out_dir, "config.pt"))

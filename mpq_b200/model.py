@@ -82,11 +82,13 @@ class ModelQuantConfig:
     polish_sweeps: int = 3
     polish_mode: str = "block_cd"  # "block_cd" | "topk_block_cd" | "none"
     topk_k: int = 16
+    init: str = "rtn"  # "rtn" | "float" (VAMP's starting message)
     block_cd_backend: str = "auto"
     true_sequential: bool = True
     batch_size: int = 8          # calibration sequences per forward
     keep_codes: bool = False     # gather q_int / scale / zero of every linear to the host
     export_gptq: bool = False    # also pack them into GPTQ v1 tensors (qweight / qzeros / scales / g_idx)
+    checkpoint_dir: Optional[str] = None  # per-layer resume state: layer_<i>.pt after each layer; done layers load
 
 
 def _world(group=None) -> Tuple[int, int]:
@@ -144,7 +146,7 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
                                  mpq=types.SimpleNamespace(rotation_mode=cfg.rotation_mode, solver="vamp"))
     vcfg = UniformVampConfig(iters=int(cfg.iters), prior_tau=float(cfg.prior_tau), damping=float(cfg.damping),
                              polish_sweeps=int(cfg.polish_sweeps), polish_mode=str(cfg.polish_mode),
-                             topk_k=int(cfg.topk_k), block_cd_backend=cfg.block_cd_backend)
+                             topk_k=int(cfg.topk_k), init_from=str(cfg.init), block_cd_backend=cfg.block_cd_backend)
     with timer("embed"):
         hidden = inner.embed_tokens(ids)
         nxt = torch.empty_like(hidden)
@@ -155,6 +157,11 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
     layer_ids = list(range(len(inner.layers))) if layers is None else list(layers)
     for li in layer_ids:
         layer = inner.layers[li]
+        if _resume_layer(cfg.checkpoint_dir, li, layer, results, rank, world, group):
+            with timer("forward_out"):
+                _forward_layer(layer, hidden, nxt, int(cfg.batch_size), mask, pos_emb, pos_ids)
+            hidden, nxt = nxt, hidden
+            continue
         subsets = SUBSETS if cfg.true_sequential else (sum(SUBSETS, ()),)
         for subset in subsets:
             # keyed by the Hessian's address: valid only while this subset's Hessians are alive
@@ -242,12 +249,49 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
                             entry["gptq"] = {k: v.cpu() for k, v in pack_gptq(qa, sa, za, g_idx, int(cfg.bits)).items()}
                     results[full] = entry
             del sums, Hs
+        if cfg.checkpoint_dir and rank == 0:
+            _save_layer(cfg.checkpoint_dir, li, layer, {k: v for k, v in results.items()
+                                                        if k.startswith(f"model.layers.{li}.")})
         with timer("forward_out"):
             _forward_layer(layer, hidden, nxt, int(cfg.batch_size), mask, pos_emb, pos_ids)
         hidden, nxt = nxt, hidden
     ops.check_status(dev)
     torch.cuda.synchronize(dev)
     return {"modules": results, "timings": dict(timer.acc), "seconds": time.perf_counter() - t_start}
+
+
+def _layer_path(ckpt_dir: str, li: int) -> str:
+    import os
+    return os.path.join(ckpt_dir, f"layer_{li}.pt")
+
+
+def _save_layer(ckpt_dir: str, li: int, layer, entries: Dict[str, Any]) -> None:
+    """The resume state of one finished layer: its quantized (dequantized) linear weights and module entries,
+    written to a temporary name and renamed so that a partial file is never taken for a finished layer."""
+    import os
+    os.makedirs(ckpt_dir, exist_ok=True)
+    weights = {name: layer.get_submodule(name).weight.detach().cpu() for name in sum(SUBSETS, ())}
+    path = _layer_path(ckpt_dir, li)
+    torch.save({"weights": weights, "modules": entries}, path + ".tmp")
+    os.replace(path + ".tmp", path)
+
+
+def _resume_layer(ckpt_dir: Optional[str], li: int, layer, results: Dict[str, Any], rank: int, world: int,
+                  group) -> bool:
+    """Load layer li's saved state when it exists (the decision is rank 0's, shared with every rank)."""
+    import os
+    if not ckpt_dir:
+        return False
+    flag = [os.path.isfile(_layer_path(ckpt_dir, li)) if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(flag, src=0, group=group)
+    if not flag[0]:
+        return False
+    state = torch.load(_layer_path(ckpt_dir, li), map_location="cpu", weights_only=False)
+    for name, w in state["weights"].items():
+        layer.get_submodule(name).weight.copy_(w)
+    results.update(state["modules"])
+    return True
 
 
 def _input_owner(layer, name: str):
@@ -273,6 +317,8 @@ QUIP_GROUPS = (("qkv", ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_pro
 class QuipModelConfig:
     iters: int = 16
     prior_tau: float = 0.25
+    damping: float = 0.5
+    init: str = "rtn"  # "rtn" | "float"
     polish_sweeps: int = 3
     polish_mode: str = "block_cd"  # "block_cd" | "topk_block_cd" | "none"
     topk_k: int = 16
@@ -281,6 +327,8 @@ class QuipModelConfig:
     batch_size: int = 8
     write_back: bool = True      # replace the float weights by the dequantized E8P12 weights
     keep_attrs: bool = True      # keep the per-group checkpoint attributes (on the host)
+    checkpoint_dir: Optional[str] = None  # QUIP#-layout ckpt: {layer}_{group}.pt / {layer}_layernorm.pt written as
+    #                                       layers finish; groups whose file exists are loaded instead of solved
 
 
 @torch.inference_mode()
@@ -313,20 +361,23 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
         nxt = torch.empty_like(hidden)
     pos_ids = torch.arange(seq_len, device=dev)[None]
     pos_emb = inner.rotary_emb(hidden[:1], position_ids=pos_ids)
-    args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=int(cfg.iters), mpq_prior_tau=float(cfg.prior_tau),
+    args = types.SimpleNamespace(mpq_init=str(cfg.init), mpq_iters=int(cfg.iters), mpq_prior_tau=float(cfg.prior_tau),
+                                 mpq_damping=float(cfg.damping),
                                  mpq_polish_sweeps=int(cfg.polish_sweeps), mpq_block_rows=1 << 30,
                                  quant_solver="vamp", quant_polish_mode=str(cfg.polish_mode), mpq_polish_metric="gram",
                                  mpq_topk_k=int(cfg.topk_k), seed=int(cfg.seed))
     attrs: Dict[str, Any] = {}
     nl = len(inner.layers)
+    done = _quip_done_groups(cfg.checkpoint_dir, nl, rank, world, group)
     # phase 1: every layer's Hessians from the float model (float activations feed the next layer)
     Hs_all: Dict[Tuple[int, str], torch.Tensor] = {}
     for li in range(nl):
         layer = inner.layers[li]
         accs = {name: HessianAccumulator(layer.get_submodule(mods[0]).in_features, device=dev, mode="quip")
-                for name, mods in QUIP_GROUPS}
+                for name, mods in QUIP_GROUPS if f"{li}_{name}" not in done}
         handles = [layer.get_submodule(mods[0]).register_forward_pre_hook(
-            (lambda acc: (lambda mod, a: acc.add_batch(a[0])))(accs[name])) for name, mods in QUIP_GROUPS]
+            (lambda acc: (lambda mod, a: acc.add_batch(a[0])))(accs[name])) for name, mods in QUIP_GROUPS
+            if name in accs]
         with timer("forward_hessian"):
             _forward_layer(layer, hidden, nxt, int(cfg.batch_size), None, pos_emb, pos_ids)
         for h in handles:
@@ -351,6 +402,10 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
         layer = inner.layers[li]
         for name, mods in QUIP_GROUPS:
             key = f"{li}_{name}"
+            if key in done:
+                with timer("resume"):
+                    attrs[key] = _quip_load_group(cfg.checkpoint_dir, key, layer, mods, cb, bool(cfg.write_back))
+                continue
             with timer("solve"):
                 H = Hs_all[(li, name)]
                 ws = [layer.get_submodule(m).weight.to(torch.float32) for m in mods]
@@ -377,9 +432,15 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                 entry = {"fused": len(mods) > 1, "shapes": [tuple(w.shape) for w in ws], "scales": scales,
                          "proxy_error": err_proxy, "surrogate_before": st["exact_surrogate_before_mean"],
                          "surrogate_after": st["exact_surrogate_after_mean"]}
-                if cfg.keep_attrs:
+                if cfg.keep_attrs or cfg.checkpoint_dir:
                     entry.update(Qidxs=idx.to(torch.int16).cpu(), SU=SU.to(torch.float16).cpu(),
                                  SV=(SV * wscale).to(torch.float16).cpu())
+                if cfg.checkpoint_dir:
+                    from .export import save_quip_layer
+                    save_quip_layer(cfg.checkpoint_dir, li, layer, {name: entry})
+                if not cfg.keep_attrs:
+                    for k in ("Qidxs", "SU", "SV"):
+                        entry.pop(k, None)
                 attrs[key] = entry
     del Hs_all
     # phase 3: every rank holds the quantized model (the owners' weights)
@@ -401,3 +462,42 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
     ops.check_status(dev)
     torch.cuda.synchronize(dev)
     return {"groups": attrs, "timings": dict(timer.acc), "seconds": time.perf_counter() - t_start}
+
+
+def _quip_done_groups(ckpt_dir: Optional[str], nl: int, rank: int, world: int, group) -> set:
+    """Groups whose checkpoint file exists (rank 0's view, shared with every rank)."""
+    import os
+    done = [None]
+    if rank == 0:
+        done[0] = {f"{li}_{name}" for li in range(nl) for name, _ in QUIP_GROUPS
+                   if ckpt_dir and os.path.isfile(os.path.join(ckpt_dir, f"{li}_{name}.pt"))}
+    if world > 1:
+        dist.broadcast_object_list(done, src=0, group=group)
+    return done[0]
+
+
+def _quip_load_group(ckpt_dir: str, key: str, layer, mods, cb, write_back: bool) -> Dict[str, Any]:
+    """Load a finished group and (optionally) write its decoded weights back: W_i = scale_i * rows_i of
+    diag(SU) Had^T grid[Qidxs] Had^T diag(SV) (SV carries the RMS scale), the inverse of the incoherence
+    processing applied before the solve."""
+    import os
+    from .codebook import factor_tables
+    from .rotation import rht_weight_inverse
+    attr = torch.load(os.path.join(ckpt_dir, f"{key}.pt"), map_location="cpu", weights_only=False)
+    if write_back:
+        dev = layer.get_submodule(mods[0]).weight.device
+        # Qidxs are stored as int16 (QUIP#'s dtype): codes >= 2^15 read back negative, so take the low 16 bits
+        idx = attr["Qidxs"].to(device=dev, dtype=torch.int64) & 0xFFFF
+        m, nb = idx.shape
+        n = nb * 8
+        grid = factor_tables(cb, dev)["grid"]
+        hat = grid.index_select(0, idx.reshape(-1)).reshape(m, n)
+        hatW = rht_weight_inverse(hat, attr["SU"].to(dev).float(), attr["SV"].to(dev).float(), m & -m, n & -n)
+        r0 = 0
+        for mod_name, sc in zip(mods, attr["scales"]):
+            w = layer.get_submodule(mod_name).weight
+            rows = w.shape[0]
+            w.copy_((hatW[r0:r0 + rows] * float(sc)).to(w.dtype))
+            r0 += rows
+    attr["resumed"] = True
+    return attr

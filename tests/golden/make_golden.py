@@ -302,6 +302,42 @@ def gen_e8p12_topk_layer(out):
     np.savez_compressed(out / "e8p12_topk_layer.npz", **cases)
 
 
+def _tiny_llama(seed, dtype=torch.float64):
+    from transformers import AutoModelForCausalLM, LlamaConfig
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=2,
+                      num_key_value_heads=2, head_dim=32, vocab_size=128, initializer_range=0.02,
+                      attn_implementation="sdpa", max_position_embeddings=256)
+    torch.manual_seed(seed)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=dtype).eval()
+    with torch.no_grad():  # log-normal channel gains: activation outliers for the scale search to find
+        for layer in model.model.layers:
+            layer.input_layernorm.weight.copy_(torch.exp(1.5 * torch.randn(cfg.hidden_size)))
+            layer.post_attention_layernorm.weight.copy_(torch.exp(1.5 * torch.randn(cfg.hidden_size)))
+    return model
+
+
+def gen_awq(out):
+    """mpq/awq_scale.py apply_awq_scaling on a tiny Llama (4-bit g32, asymmetric), in float64: with float32 weights
+    on the CPU the reference's saved copies (`.to(float32).cpu().contiguous()`) alias the live weights, so its
+    per-ratio restore is a no-op; in float64 (as in bf16 on the GPU) the copy is real."""
+    from mpq.awq_scale import apply_awq_scaling
+    from mpq.dense_decoder_adapter import resolve_dense_decoder_adapter_for_model
+    model = _tiny_llama(5)
+    before = {k: v.clone() for k, v in model.state_dict().items()}
+    g = torch.Generator().manual_seed(9)
+    ids = torch.randint(0, 128, (4, 32), generator=g)
+    blocks = [{"input_ids": ids[i:i + 1]} for i in range(ids.shape[0])]
+    adapter = resolve_dense_decoder_adapter_for_model(model)
+    dbg = apply_awq_scaling(model, adapter, blocks, bits=4, group_size=32, sym=False, batch_size=2, device="cpu")
+    cases = {"ids": _np(ids)}
+    for k, v in before.items():
+        cases[f"before/{k}"] = _np(v)
+    for k, v in model.state_dict().items():
+        cases[f"after/{k}"] = _np(v)
+    cases["meta"] = np.array(json.dumps(dbg))
+    np.savez_compressed(out / "awq.npz", **cases)
+
+
 def _block_cd_problem(B, n, R, seed, scale_rows=0.02):
     """A rank-space least-squares problem Y_u = W Vs with Vs from a random Hessian's eigenbasis."""
     g = torch.Generator().manual_seed(seed)
@@ -470,7 +506,7 @@ def gen_postprocess(out):
 GENERATORS = {"uniform_denoise": gen_uniform_denoise, "linear": gen_linear, "scalar_cd": gen_scalar_cd,
               "scalar_layer": gen_scalar_layer, "rotation": gen_rotation, "e8p12": gen_e8p12,
               "e8p12_layer": gen_e8p12_layer, "block_cd": gen_block_cd, "topk": gen_topk,
-              "postprocess": gen_postprocess, "e8p12_topk_layer": gen_e8p12_topk_layer}
+              "postprocess": gen_postprocess, "e8p12_topk_layer": gen_e8p12_topk_layer, "awq": gen_awq}
 
 
 def main():

@@ -1,0 +1,50 @@
+"""AWQ scaling (the 3/4-bit preprocess) against the reference's apply_awq_scaling run on the same tiny model
+(float64, so that both searches see the same losses to far below the gaps between ratios)."""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+
+def _tiny_llama(dev, dtype=torch.float64):
+    from transformers import AutoModelForCausalLM, LlamaConfig
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=2,
+                      num_key_value_heads=2, head_dim=32, vocab_size=128, initializer_range=0.02,
+                      attn_implementation="sdpa", max_position_embeddings=256)
+    with torch.device(dev):
+        return AutoModelForCausalLM.from_config(cfg, dtype=dtype).eval()
+
+
+@pytest.mark.gpu
+def test_awq_matches_reference(cuda_dev, golden_dir):
+    from mpq_b200.awq import apply_awq_scaling
+    z = np.load(golden_dir / "awq.npz")
+    ref = json.loads(str(z["meta"]))
+    model = _tiny_llama(cuda_dev)
+    sd = {k[len("before/"):]: torch.from_numpy(z[k]) for k in z.files if k.startswith("before/")}
+    model.load_state_dict(sd)
+    with torch.no_grad():
+        ref_logits = model(torch.from_numpy(z["ids"]).to(cuda_dev)).logits
+    dbg = apply_awq_scaling(model, torch.from_numpy(z["ids"]), bits=4, group_size=32, sym=False, batch_size=2)
+    mine = [(g["name"], g["best_ratio"]) for l in dbg["layers"] for g in l["groups"]]
+    theirs = [(g["name"], g["best_ratio"]) for l in ref["layers"] for g in l["groups"]]
+    assert [n for n, _ in mine] == [n for n, _ in theirs]
+    assert mine == theirs
+    errs = [g["best_error"] for l in dbg["layers"] for g in l["groups"]]
+    ref_errs = [g["best_error"] for l in ref["layers"] for g in l["groups"]]
+    np.testing.assert_allclose(errs, ref_errs, rtol=1e-5)
+    after = model.state_dict()
+    for k in z.files:
+        if k.startswith("after/"):
+            np.testing.assert_allclose(after[k[len("after/"):]].cpu().numpy(), z[k], rtol=1e-5, atol=1e-6, err_msg=k)
+    # the folded scales leave the float model's function unchanged
+    with torch.no_grad():
+        logits = model(torch.from_numpy(z["ids"]).to(cuda_dev)).logits
+    torch.testing.assert_close(logits, ref_logits, rtol=1e-6, atol=1e-8)
+
+
+def test_awq_requires_gpu():
+    from mpq_b200.awq import apply_awq_scaling
+    with pytest.raises(ValueError, match="GPU"):
+        apply_awq_scaling(_tiny_llama("cpu"), torch.zeros(1, 4, dtype=torch.long), bits=4, group_size=32)
