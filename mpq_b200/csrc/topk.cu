@@ -62,53 +62,45 @@ __global__ void k_uniform_topk(const float* __restrict__ r1, int64_t ld_r1, cons
   }
 }
 
-// The same selection for grids of L <= 16 levels without a sorted list: all L scores stay in registers and the
-// output position of level q is its rank  #{q' : s[q'] > s[q] or (s[q'] == s[q] and q' < q)}.
+// The same selection for grids of L <= 32 levels, L lanes per coordinate: lane q scores level q, its output
+// position is its rank  #{q' : s[q'] > s[q] or (s[q'] == s[q] and q' < q)}  (NaN scores rank last, so the ranks
+// are a permutation), and the L lanes of a coordinate write its k outputs as one contiguous segment.
 template <int L>
-__global__ void k_uniform_topk_small(const float* __restrict__ r1, int64_t ld_r1, const float* __restrict__ center,
+__global__ void k_uniform_topk_lanes(const float* __restrict__ r1, int64_t ld_r1, const float* __restrict__ center,
                                      int64_t ld_c, const float* __restrict__ scale, const float* __restrict__ zero,
                                      int64_t ld_p, int gshift, const float* __restrict__ gamma, int B, int n,
                                      float prior_tau, int k, int* __restrict__ out_q, float* __restrict__ out_v,
                                      float* __restrict__ out_s) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= (int64_t)B * n) return;
-  const int b = (int)(i / n), j = (int)(i % n);
+  const int64_t gt = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t i = gt / L;
+  const int q = (int)(gt % L);
+  const bool valid = i < (int64_t)B * n;  // every lane takes part in the shuffles
+  const int64_t ii = valid ? i : 0;
+  const int b = (int)(ii / n), j = (int)(ii % n);
   const float r = r1[b * ld_r1 + j];
   const float s = scale[b * ld_p + (j >> gshift)];
   const float z = zero[b * ld_p + (j >> gshift)];
   const float ng = fmul(-0.5f, gamma[b]);
   const bool prior = prior_tau > 0.f && center;
-  const float c = prior ? center[b * ld_c + j] : 0.f;
-  float tau2 = 1.f;
+  const float atom = fmul(s, fsub((float)q, z));
+  const float d = fsub(atom, r);
+  float sc = fmul(ng, fmul(d, d));
   if (prior) {
     const float st = fmul(prior_tau, fmaxf(s, 1e-12f));
-    tau2 = fmul(st, st);
+    const float dc = fsub(atom, center[b * ld_c + j]);
+    sc = fsub(sc, fdiv(fmul(0.5f, fmul(dc, dc)), fmul(st, st)));
   }
-  float sc[L], at[L];
+  const float key = sc != sc ? -INFINITY : sc;
+  int rank = 0;
   #pragma unroll
-  for (int q = 0; q < L; ++q) {
-    at[q] = fmul(s, fsub((float)q, z));
-    const float d = fsub(at[q], r);
-    float v = fmul(ng, fmul(d, d));
-    if (prior) {
-      const float dc = fsub(at[q], c);
-      v = fsub(v, fdiv(fmul(0.5f, fmul(dc, dc)), tau2));
-    }
-    sc[q] = v;
+  for (int p = 0; p < L; ++p) {
+    const float kp = __shfl_sync(0xffffffffu, key, p, L);
+    rank += (kp > key || (kp == key && p < q)) ? 1 : 0;
   }
-  float key[L];  // NaN scores rank last, so the ranks are a permutation and every output slot is written
-  #pragma unroll
-  for (int q = 0; q < L; ++q) key[q] = sc[q] != sc[q] ? -INFINITY : sc[q];
-  #pragma unroll
-  for (int q = 0; q < L; ++q) {
-    int rank = 0;
-    #pragma unroll
-    for (int p = 0; p < L; ++p) rank += (key[p] > key[q] || (key[p] == key[q] && p < q)) ? 1 : 0;
-    if (rank < k) {
-      out_q[i * k + rank] = q;
-      out_v[i * k + rank] = at[q];
-      if (out_s) out_s[i * k + rank] = sc[q];
-    }
+  if (valid && rank < k) {
+    out_q[i * k + rank] = q;
+    out_v[i * k + rank] = atom;
+    if (out_s) out_s[i * k + rank] = sc;
   }
 }
 
@@ -179,19 +171,20 @@ MPQ_API int mpq_uniform_topk(const float* r1, int64_t ld_r1, const float* center
   const int64_t total = (int64_t)B * n;
   const unsigned grid = (unsigned)((total + 255) / 256);
   cudaStream_t st = (cudaStream_t)stream;
-#define MPQ_TOPK_SMALL(L_)                                                                                            \
-  k_uniform_topk_small<L_><<<grid, 256, 0, st>>>(r1, ld_r1, center, ld_c, scale, zero, ld_p, gshift, gamma, B, n, \
-                                                 prior_tau, k, out_q, out_v, out_s)
+#define MPQ_TOPK_LANES(L_)                                                                                    \
+  k_uniform_topk_lanes<L_><<<(unsigned)((total * L_ + 255) / 256), 256, 0, st>>>(                             \
+      r1, ld_r1, center, ld_c, scale, zero, ld_p, gshift, gamma, B, n, prior_tau, k, out_q, out_v, out_s)
   switch (maxq) {
-    case 1: MPQ_TOPK_SMALL(2); break;
-    case 3: MPQ_TOPK_SMALL(4); break;
-    case 7: MPQ_TOPK_SMALL(8); break;
-    case 15: MPQ_TOPK_SMALL(16); break;
+    case 1: MPQ_TOPK_LANES(2); break;
+    case 3: MPQ_TOPK_LANES(4); break;
+    case 7: MPQ_TOPK_LANES(8); break;
+    case 15: MPQ_TOPK_LANES(16); break;
+    case 31: MPQ_TOPK_LANES(32); break;
     default:
       k_uniform_topk<<<grid, 256, 0, st>>>(r1, ld_r1, center, ld_c, scale, zero, ld_p, gshift, gamma, B, n, maxq,
                                            prior_tau, k, out_q, out_v, out_s);
   }
-#undef MPQ_TOPK_SMALL
+#undef MPQ_TOPK_LANES
   return launch_status("mpq_uniform_topk");
 }
 
