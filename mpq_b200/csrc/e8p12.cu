@@ -457,7 +457,11 @@ k_e8p12_topk(E8Args a, E8Tab tab, int k, int* __restrict__ idx_out, float* __res
   __shared__ float s_sqn[256];
   __shared__ int s_par[256];
   __shared__ float s_a[kTopkWarps][48];              // a = (g (y_k - off)) |b| per (branch, 3 k + m)
-  __shared__ float s_sc[kTopkWarps][1024];           // entry e of lane l at [e * 32 + l], e = (8 br + j) * 2 + s
+  // candidate f = 2 (256 br + ai) + s lives in slot e = f >> 5 of lane (f + e) & 31, at [e * 32 + lane]: the
+  // best / second-best of an abs pattern and its two branches sit in different lanes (so the top candidates,
+  // which cluster by abs pattern, are spread over lanes), a lane's slots run in ascending f, and the 32 lanes of
+  // one scoring store hit 32 different banks
+  __shared__ float s_sc[kTopkWarps][1024];
   __shared__ unsigned char s_sid[kTopkWarps][1024];  // its sign pattern (bit k: coordinate k negative)
   __shared__ int s_bad;
   const bool bad = stage_abs_patterns(tab, s_off, s_sqn, s_par, &s_bad);
@@ -536,11 +540,12 @@ k_e8p12_topk(E8Args a, E8Tab tab, int k, int* __restrict__ idx_out, float* __res
         const float lin2 = mismatch ? fsub(sum_abs[br], fmul(2.f, mn2[br]))
                                     : fsub(sum_abs[br], fmul(2.f, fadd(mn[br], mn2[br])));
         const unsigned b1 = 1u << p1[br], b2 = 1u << p2[br];
-        const int e0 = (8 * br + j) * 2;
-        ssc[e0 * 32 + lane] = fadd(cst, lin1);
-        ssid[e0 * 32 + lane] = (unsigned char)(mismatch ? neg[br] ^ b1 : neg[br]);
-        ssc[(e0 + 1) * 32 + lane] = fadd(cst, lin2);
-        ssid[(e0 + 1) * 32 + lane] = (unsigned char)(mismatch ? neg[br] ^ b2 : neg[br] ^ b1 ^ b2);
+        const int f0 = 2 * (256 * br + ai);  // s = 0; s = 1 is f0 + 1, in the same slot and the next lane
+        const int slot = (f0 >> 5) * 32, own = (f0 + (f0 >> 5)) & 31;
+        ssc[slot + own] = fadd(cst, lin1);
+        ssid[slot + own] = (unsigned char)(mismatch ? neg[br] ^ b1 : neg[br]);
+        ssc[slot + ((own + 1) & 31)] = fadd(cst, lin2);
+        ssid[slot + ((own + 1) & 31)] = (unsigned char)(mismatch ? neg[br] ^ b2 : neg[br] ^ b1 ^ b2);
       }
     }
     // k rounds of a warp argmax.  Each lane keeps the two best of its own 32 entries (ascending e = ascending f,
@@ -570,7 +575,7 @@ k_e8p12_topk(E8Args a, E8Tab tab, int k, int* __restrict__ idx_out, float* __res
     #pragma unroll 1
     for (int t = 0; t < k; ++t) {
       float wb = b1;
-      int wf = e1 < 0 ? -1 : 512 * (e1 >> 4) + 64 * ((e1 >> 1) & 7) + 2 * lane + (e1 & 1);
+      int wf = e1 < 0 ? -1 : e1 * 32 + ((lane - e1) & 31);
       #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, wb, o);
@@ -578,8 +583,7 @@ k_e8p12_topk(E8Args a, E8Tab tab, int k, int* __restrict__ idx_out, float* __res
         if (of2 >= 0 && (wf < 0 || ob > wb || (ob == wb && of2 < wf))) { wb = ob; wf = of2; }
       }
       if (lane == (t & 31)) { park_f = wf; park_sc = wb; }
-      const int wai = (wf >> 1) & 255;
-      if (wf >= 0 && lane == (wai & 31)) {  // the winner's lane drops the entry
+      if (wf >= 0 && lane == ((wf + (wf >> 5)) & 31)) {  // the winner's lane drops the entry
         taken |= 1u << e1;
         if (second_valid && e2 >= 0) {
           b1 = b2; e1 = e2; b2 = -INFINITY; e2 = -1;
@@ -594,9 +598,8 @@ k_e8p12_topk(E8Args a, E8Tab tab, int k, int* __restrict__ idx_out, float* __res
         if (tt <= t) {
           int cidx = -1;
           if (park_f >= 0) {
-            const int pbr = park_f >> 9, pai = (park_f >> 1) & 255, ps = park_f & 1;
-            const int pe = (8 * pbr + (pai >> 5)) * 2 + ps;
-            cidx = tab.idx_lut[pbr * 65536 + pai * 256 + ssid[pe * 32 + (pai & 31)]];
+            const int pbr = park_f >> 9, pai = (park_f >> 1) & 255;
+            cidx = tab.idx_lut[pbr * 65536 + pai * 256 + ssid[(park_f >> 5) * 32 + ((park_f + (park_f >> 5)) & 31)]];
           }
           io[tt] = cidx;
           if (so) so[tt] = park_sc;

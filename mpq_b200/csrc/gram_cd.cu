@@ -439,6 +439,41 @@ __device__ __forceinline__ int topk_pick_warp(const float t[8], const float* L, 
   return ci;
 }
 
+// topk_pick_warp for kc <= 32 with each lane's candidate already in registers (v0, v1; valid = lane < kc).
+__device__ __forceinline__ int topk_pick_reg(const float t[8], const float* L, float4 v0, float4 v1, bool valid) {
+  float tm[8], tn = 0.f;
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float acc = 0.f;
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) acc = fadd(acc, fmul(t[i], L[i * 8 + j]));
+    tm[j] = acc;
+  }
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) tn = fadd(tn, fmul(tm[j], tm[j]));
+  const float cvv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  float cn = 0.f, cross = 0.f;
+  #pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float cm = 0.f;
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) cm = fadd(cm, fmul(cvv[i], L[i * 8 + j]));
+    cn = fadd(cn, fmul(cm, cm));
+    cross = fadd(cross, fmul(cm, tm[j]));
+  }
+  float key = fmaxf(fsub(fadd(tn, cn), fmul(2.f, cross)), 0.f);
+  if (key != key) key = INFINITY;
+  int ci = valid ? (int)(threadIdx.x & 31) : 0x7fffffff;
+  if (!valid) key = INFINITY;
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ok = __shfl_xor_sync(0xffffffffu, key, o);
+    const int oc = __shfl_xor_sync(0xffffffffu, ci, o);
+    if (oc != 0x7fffffff && (ci == 0x7fffffff || ok < key || (ok == key && oc < ci))) { key = ok; ci = oc; }
+  }
+  return ci;
+}
+
 template <bool TOPK>
 __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
   extern __shared__ float sm[];
@@ -465,6 +500,15 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
   float res = a.res[b];
   int acc_n = 0;
   long long evals = 0;
+  // top-k with kc <= 32: each lane holds its candidate of the current block and loads the next block's ahead
+  const bool reg_cand = TOPK && a.kc <= 32;
+  float4 cv0 = make_float4(0.f, 0.f, 0.f, 0.f), cv1 = cv0;
+  auto load_cand = [&](int p, float4& v0, float4& v1) {
+    const float* cp = a.cand + (((int64_t)b * a.nb + a.order[a.c0 + p]) * a.kc + lane) * 8;
+    v0 = __ldg(reinterpret_cast<const float4*>(cp));
+    v1 = __ldg(reinterpret_cast<const float4*>(cp + 4));
+  };
+  if (reg_cand && lane < a.kc) load_cand(0, cv0, cv1);
   for (int p = 0; p < a.Kb; ++p) {
     const int blk = a.order[a.c0 + p];
     const float* m = s_meta + p * kMeta;
@@ -490,7 +534,16 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
     if constexpr (TOPK) {
       const int64_t item = (int64_t)b * a.nb + blk;
       const float* cv = a.cand + item * a.kc * 8;
-      const int pick = topk_pick_warp(t, L, cv, a.kc);
+      int pick;
+      if (reg_cand) {
+        float4 nv0 = make_float4(0.f, 0.f, 0.f, 0.f), nv1 = nv0;
+        if (p + 1 < a.Kb && lane < a.kc) load_cand(p + 1, nv0, nv1);
+        pick = topk_pick_reg(t, L, cv0, cv1, lane < a.kc);
+        cv0 = nv0;
+        cv1 = nv1;
+      } else {
+        pick = topk_pick_warp(t, L, cv, a.kc);
+      }
       gv = cv + pick * 8;
       c = a.cand_idx ? a.cand_idx[item * a.kc + pick] : pick;
       evals += a.kc;

@@ -168,8 +168,16 @@ __global__ void __launch_bounds__(256) k_cd_block(CdArgs a) {
   const float tol1 = 1.f + a.accept_tol;
   int acc_count = 0;
   const float* crow = TOPK ? a.cand + (int64_t)b * a.ld_cand : nullptr;
-  float cnext = 0.f;  // this lane's candidate of the next column (loaded one decision ahead)
-  if constexpr (TOPK) cnext = lane < a.kc ? crow[(int64_t)s_col[0] * a.kc + lane] : 0.f;
+  // this lane's candidate of the next four columns (loads issued four decisions ahead)
+  float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+  if constexpr (TOPK) {
+    if (lane < a.kc) {
+      c0 = crow[(int64_t)s_col[0] * a.kc + lane];
+      if (a.K > 1) c1 = crow[(int64_t)s_col[1] * a.kc + lane];
+      if (a.K > 2) c2 = crow[(int64_t)s_col[2] * a.kc + lane];
+      if (a.K > 3) c3 = crow[(int64_t)s_col[3] * a.kc + lane];
+    }
+  }
   #pragma unroll
   for (int t = 0; t < 4; ++t) {
     for (int lk = 0; lk < 32; ++lk) {
@@ -181,8 +189,11 @@ __global__ void __launch_bounds__(256) k_cd_block(CdArgs a) {
       float xq;
       int pick = 0;
       if constexpr (TOPK) {
-        const float cv = cnext;
-        if (k + 1 < a.K && lane < a.kc) cnext = crow[(int64_t)s_col[k + 1] * a.kc + lane];
+        const float cv = c0;
+        c0 = c1;
+        c1 = c2;
+        c2 = c3;
+        if (k + 4 < a.K && lane < a.kc) c3 = crow[(int64_t)s_col[k + 4] * a.kc + lane];
         float key = INFINITY;
         int ci = 0x7fffffff;
         if (lane < a.kc) {
