@@ -494,7 +494,7 @@ def run_reference(args):
     v = float(np.mean(vals))
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": "s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "gemm_precision": ops.gemm_precision(), "data": "synthetic (seeded)",
+            "vs_baseline": None, "dtype": "f32", "gemm_precision": "fp32 (CPU)", "data": "synthetic (seeded)",
             "config": {"workload": WORKLOAD_DESC[args.workload], "parallelism": "cpu"},
             "cpu_baseline": {k: info[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": v, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
