@@ -141,7 +141,9 @@ class ClockSampler:
 
     def __init__(self, index: int, enabled: bool = True):
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_rank{index}.csv"
+        # the raw samples go to MPQ_CLOCKS_DIR (default: the system temp directory); the JSON line carries the summary
+        import tempfile
+        self.path = Path(os.environ.get("MPQ_CLOCKS_DIR", tempfile.gettempdir())) / f"clocks_rank{index}.csv"
         if not enabled:
             return
         try:
