@@ -69,6 +69,9 @@ def parse():
     ap.add_argument("--calib-seqs", type=int, default=128)
     ap.add_argument("--seq-len", type=int, default=2048)
     ap.add_argument("--bits", type=int, default=3)
+    ap.add_argument("--preprocess", default="none", choices=["none", "awq"],
+                    help="model workload: AWQ scaling before the walk (BASELINE config 2: --model qwen3_0p6b "
+                         "--bits 4 --preprocess awq); timed with the walk and reported separately")
     ap.add_argument("--gemm-precision", default="", help="tf32x3 | f16x3 (FP32-faithful split products); default: "
                     "the library default")
     ap.add_argument("--hess-n", type=int, default=14336, help="hessian workload: features n")
@@ -530,6 +533,12 @@ def run_model(args):
     torch.cuda.synchronize()
     launches0 = trace.launches()
     t0 = time.perf_counter()
+    awq_s = None
+    if args.preprocess == "awq" and not e8:
+        from mpq_b200.awq import apply_awq_scaling
+        apply_awq_scaling(model, ids, bits=args.bits, group_size=128, sym=False, batch_size=32)
+        torch.cuda.synchronize()
+        awq_s = time.perf_counter() - t0
     if e8:
         from mpq_b200.model import QuipModelConfig, quantize_model_quip
         out = quantize_model_quip(model, ids, QuipModelConfig(iters=16, prior_tau=0.25, polish_sweeps=3,
@@ -562,7 +571,8 @@ def run_model(args):
                "scaling": "strong", "vs_baseline": None, "dtype": "f32 solve / bf16 model", "data": "synthetic",
                "config": {"workload": WORKLOAD_DESC["model"], "model": args.model, "layers": model.config.num_hidden_layers,
                           "calibration": [args.calib_seqs, args.seq_len], "bits": args.bits, "group_size": 128,
-                          "parallelism": f"rows{world}+calib{world}"},
+                          "preprocess": args.preprocess, "parallelism": f"rows{world}+calib{world}"},
+               "awq_s_rank0": awq_s,
                "timings_rank0_s": out["timings"], "gpu_launches": trace.launches() - launches0, "clocks": clk,
                "linears": len(mods),
                "solve_s_by_projection_rank0": {k: round(sum(m["solve_s"] for n, m in mods.items() if n.endswith(k)), 3)

@@ -143,12 +143,13 @@ def _calibration(resolved: ResolvedQuantizationConfig, vocab: int, calibration_i
 
 
 def quantize(model, output_dir, config: Optional[QuantizationConfig] = None, *, calibration_ids=None,
-             device=None, resume: bool = True, group=None) -> Dict[str, Any]:
+             device=None, resume: bool = True, group=None, awq_batch_size: int = 16) -> Dict[str, Any]:
     """Quantize a decoder LM and return the result payload (also written to ``output_dir/backend_results.json``).
 
     ``model``: a loaded ``*ForCausalLM`` (quantized in place), a local checkpoint directory, or a registered
     synthetic shape name.  With ``resume`` the per-layer state under ``output_dir`` lets an interrupted run skip the
-    layers it finished.  Under ``torchrun`` pass the process group in ``group``; rank 0 writes the files."""
+    layers it finished.  Under ``torchrun`` pass the process group in ``group``; rank 0 writes the files.
+    ``awq_batch_size`` sequences go through each module forward of the AWQ search (a throughput knob)."""
     import torch.distributed as dist
 
     from .model import ModelQuantConfig, QuipModelConfig, quantize_model, quantize_model_quip
@@ -174,7 +175,7 @@ def quantize(model, output_dir, config: Optional[QuantizationConfig] = None, *, 
         t = time.time()
         payload["awq"] = apply_awq_scaling(m, ids, bits=resolved.bits,
                                            group_size=resolved.group_size if resolved.group_size > 0 else -1,
-                                           sym=bool(resolved.symmetric))
+                                           sym=bool(resolved.symmetric), batch_size=awq_batch_size)
         timings["awq_preprocess"] = time.time() - t
     paths: Dict[str, str] = {}
     if resolved.backend == "quip":
