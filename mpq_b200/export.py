@@ -98,13 +98,32 @@ def save_gptq_checkpoint(model, modules: Dict[str, Dict], out_dir, *, bits: int,
     return str(out_dir)
 
 
+def _rotation_state_keys(prefix: str, width: int) -> Dict:
+    """The serialized rotation state of the randomized Hadamard ("had") rotation, whose structured-state fields
+    are all zero (patches/quip_sharp.patch:153-165, 453-462)."""
+    return {f"{prefix}rotation_code": torch.tensor(0), f"{prefix}block_size": torch.tensor(0),
+            f"{prefix}depth": torch.tensor(0), f"{prefix}householder_count": torch.tensor(0),
+            f"{prefix}stage_signs": torch.zeros(4, width), f"{prefix}stage_perms": torch.zeros(3, width, dtype=torch.int64),
+            f"{prefix}stage_inv_perms": torch.zeros(3, width, dtype=torch.int64),
+            f"{prefix}householder": torch.zeros(1, width)}
+
+
 def quip_group_attrs(entry: Dict) -> Dict:
-    """The saved attribute dict of one QUIP# group (mpq/quip_generic.py:398-426): Qidxs, SU, SV (fp16, the RMS scale
-    folded into SV), fused, shapes, scales.  Qidxs are stored unpacked (int16, rows x cols / 8): the packed layout
-    of QUIP#'s decode kernels belongs to QUIP#'s codebook class, which is not part of the reference tree."""
-    keep = ("Qidxs", "SU", "SV", "fused", "shapes", "scales", "proxy_error", "surrogate_before", "surrogate_after")
+    """The saved attribute dict of one QUIP# group (mpq/quip_generic.py:398-426, patches/quip_sharp.patch:440-475):
+    Qidxs, SU, SV (fp16, the RMS scale folded into SV), scaleWH, the rotation state of both sides ("had"), fused,
+    shapes, scales, mpq_stats and, when computed, input_fingerprint.  Qidxs are stored unpacked (int16,
+    rows x cols / 8): the packed layout of QUIP#'s decode kernels belongs to QUIP#'s codebook class, which is not part
+    of the reference tree."""
+    keep = ("Qidxs", "SU", "SV", "fused", "shapes", "scales", "proxy_error", "surrogate_before", "surrogate_after",
+            "mpq_stats", "input_fingerprint")
     out = {k: entry[k] for k in keep if k in entry}
-    out.update(packed=False, codebook="E8P12", codesz=8, scaleWH=None)
+    out.update(packed=False, codebook="E8P12", codesz=8, scaleWH=None, rotation_family="had",
+               left_rotation_family="had", right_rotation_family="had", left_rotation_fallback_reason="",
+               right_rotation_fallback_reason="")
+    if "Qidxs" in entry:
+        m, nb = entry["Qidxs"].shape
+        out.update(_rotation_state_keys("left_", nb * 8))
+        out.update(_rotation_state_keys("right_", m))
     return out
 
 

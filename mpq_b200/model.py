@@ -329,6 +329,7 @@ class QuipModelConfig:
     keep_attrs: bool = True      # keep the per-group checkpoint attributes (on the host)
     checkpoint_dir: Optional[str] = None  # QUIP#-layout ckpt: {layer}_{group}.pt / {layer}_layernorm.pt written as
     #                                       layers finish; groups whose file exists are loaded instead of solved
+    fingerprint: bool = False    # sha256 of each group's W and H in the ckpt (host hashing: seconds per layer)
 
 
 @torch.inference_mode()
@@ -434,7 +435,13 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                          "surrogate_after": st["exact_surrogate_after_mean"]}
                 if cfg.keep_attrs or cfg.checkpoint_dir:
                     entry.update(Qidxs=idx.to(torch.int16).cpu(), SU=SU.to(torch.float16).cpu(),
-                                 SV=(SV * wscale).to(torch.float16).cpu())
+                                 SV=(SV * wscale).to(torch.float16).cpu(),
+                                 mpq_stats={k: v for k, v in st.items() if isinstance(v, (int, float, str, bool))})
+                if cfg.fingerprint:
+                    from .adapters.gptqmodel import _tensor_sha256
+                    entry["input_fingerprint"] = {"protocol": "paired_w_h_sha256_v1", "w_sha256": _tensor_sha256(W),
+                                                  "h_sha256": _tensor_sha256(H), "w_shape": [int(d) for d in W.shape],
+                                                  "h_shape": [int(d) for d in H.shape], "basis": "pre_incoherence"}
                 if cfg.checkpoint_dir:
                     from .export import save_quip_layer
                     save_quip_layer(cfg.checkpoint_dir, li, layer, {name: entry})

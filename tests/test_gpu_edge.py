@@ -22,6 +22,24 @@ def test_empty_inputs_are_no_ops(cuda_dev):
     call("mpq_uniform_mmse", ptr(dummy), 8, ptr(dummy), 8, ptr(dummy), ptr(dummy), 1, 0, ptr(dummy), 0, 8, 15, 0.0,
          ptr(dummy), 8, None, None, None, ptr(dummy))
     call("mpq_uniform_mmse", None, 8, None, 8, None, None, 1, 0, None, 0, 8, 15, 0.0, None, 8, None, None, None, None)
+    # top-k entries: empty shapes succeed, bad k is rejected with a message
+    call("mpq_e8p12_topk", None, 8, None, 0, None, 0, None, 0.0, 0, 4, *_tab_ptrs(t), 16, None, None, None)
+    call("mpq_uniform_topk", None, 8, None, 0, None, None, 1, 0, None, 0, 8, 15, 0.0, 4, None, None, None)
+    call("mpq_topk_pick", None, 8, None, 8, None, 8, 0, 4, 8, None, None, 8, None)
+    with pytest.raises(RuntimeError, match="k must be in"):
+        call("mpq_e8p12_topk", ptr(dummy), 8, None, 0, None, 0, ptr(dummy), 0.0, 1, 1, *_tab_ptrs(t), 2000,
+             ptr(dummy), None, None)
+    with pytest.raises(RuntimeError, match="k must be in"):
+        call("mpq_uniform_topk", ptr(dummy), 8, None, 0, ptr(dummy), ptr(dummy), 1, 0, ptr(dummy), 1, 8, 3, 0.0, 5,
+             ptr(dummy), ptr(dummy), None)
+    from mpq_b200.topk import uniform_map_topk, vamp_vector_map_topk_e8p12
+    e = torch.zeros(0, 16, device=cuda_dev)
+    o = uniform_map_topk(r1=e, gamma1=torch.zeros(0, 1, device=cuda_dev), scale_full=e, zero_full=e, maxq=15,
+                         prior_center=e, prior_tau=0.2, k=4)
+    assert o["topk_q"].shape == (0, 16, 4)
+    o = vamp_vector_map_topk_e8p12(r1_blocks=torch.zeros(0, 2, 8, device=cuda_dev),
+                                   gamma1=torch.zeros(0, 1, device=cuda_dev), cb=E8P12_codebook(), k=8)
+    assert o["topk_idxs"].shape == (0, 2, 8)
     A = torch.zeros(0, 64, device=cuda_dev)
     B = torch.randn(32, 64, device=cuda_dev)
     for prec in ("f16x3", "tf32x3", "fp32"):

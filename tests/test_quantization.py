@@ -94,6 +94,7 @@ def test_quantize_quip_backend_end_to_end(cuda_dev, tmp_path):
     assert "config.pt" in names and "0_qkv.pt" in names and "1_down.pt" in names and "1_layernorm.pt" in names
     a = torch.load(ck / "0_qkv.pt", weights_only=False)
     assert a["Qidxs"].dtype == torch.int16 and a["fused"] and len(a["shapes"]) == 3 and a["packed"] is False
+    assert a["rotation_family"] == "had" and a["left_stage_signs"].shape == (4, 256) and "mpq_stats" in a
     conf = torch.load(ck / "config.pt", weights_only=False)
     assert conf["model_config"].quip_params["codebook"] == "E8P12"
     assert (tmp_path / "hf" / "config.json").is_file()
