@@ -159,6 +159,9 @@ def quantize(model, output_dir, config: Optional[QuantizationConfig] = None, *, 
         raise ValueError(f"init={resolved.init!r} is not on the CUDA path (use 'rtn' or 'float')")
     if resolved.symmetric:
         raise ValueError("symmetric grids are not on the CUDA path (the solve uses the asymmetric GPTQ grid)")
+    if resolved.evaluate:
+        raise ValueError("evaluate=True runs the reference's text-dataset evaluation scripts, which are not part of "
+                         "this package; quantize with evaluate=False and evaluate the saved model separately")
     rank = dist.get_rank(group) if dist.is_available() and dist.is_initialized() else 0
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     out = Path(output_dir).expanduser()

@@ -43,6 +43,15 @@ def test_polish_sweeps_zero_disables_polish_and_overrides():
     assert (r.polish_mode, r.preprocess, r.prior_tau, r.symmetric) == ("none", "none", 0.3, True)
 
 
+def test_unbuilt_options_fail_loudly(tmp_path):
+    from mpq_b200 import quantize
+    for cfg, msg in ((QuantizationConfig(bits=4, evaluate=True), "evaluate"),
+                     (QuantizationConfig(bits=4, init="ldlq"), "init"),
+                     (QuantizationConfig(bits=4, symmetric=True), "symmetric")):
+        with pytest.raises(ValueError, match=msg):
+            quantize("tiny_llama", tmp_path, cfg)
+
+
 def test_text_calibration_needs_ids():
     from mpq_b200.quantization import _calibration
     r = QuantizationConfig(bits=4).resolve()
