@@ -329,11 +329,12 @@ def gen_awq(out):
     blocks = [{"input_ids": ids[i:i + 1]} for i in range(ids.shape[0])]
     adapter = resolve_dense_decoder_adapter_for_model(model)
     dbg = apply_awq_scaling(model, adapter, blocks, bits=4, group_size=32, sym=False, batch_size=2, device="cpu")
-    cases = {"ids": _np(ids)}
-    for k, v in before.items():
-        cases[f"before/{k}"] = _np(v)
+    # the starting weights are rebuilt by the test from the same seeded CPU initialisation (a checksum pins them);
+    # the scaled weights are stored in float32 (the test's tolerance is 1e-5)
+    cases = {"ids": _np(ids), "before_checksum": np.array([float(v.double().abs().sum()) for v in before.values()])}
     for k, v in model.state_dict().items():
-        cases[f"after/{k}"] = _np(v)
+        if not torch.equal(v, before[k]):
+            cases[f"after/{k}"] = _np(v.float())
     cases["meta"] = np.array(json.dumps(dbg))
     np.savez_compressed(out / "awq.npz", **cases)
 

@@ -7,13 +7,21 @@ import pytest
 import torch
 
 
-def _tiny_llama(dev, dtype=torch.float64):
+def _tiny_llama(dev, dtype=torch.float64, seed=None):
+    """The golden run's model: seeded CPU initialisation (as tests/golden/make_golden.py builds it), then moved."""
     from transformers import AutoModelForCausalLM, LlamaConfig
     cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=2,
                       num_key_value_heads=2, head_dim=32, vocab_size=128, initializer_range=0.02,
                       attn_implementation="sdpa", max_position_embeddings=256)
-    with torch.device(dev):
-        return AutoModelForCausalLM.from_config(cfg, dtype=dtype).eval()
+    if seed is not None:
+        torch.manual_seed(seed)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=dtype).eval()
+    if seed is not None:
+        with torch.no_grad():
+            for layer in model.model.layers:
+                layer.input_layernorm.weight.copy_(torch.exp(1.5 * torch.randn(cfg.hidden_size)))
+                layer.post_attention_layernorm.weight.copy_(torch.exp(1.5 * torch.randn(cfg.hidden_size)))
+    return model.to(dev)
 
 
 @pytest.mark.gpu
@@ -21,9 +29,9 @@ def test_awq_matches_reference(cuda_dev, golden_dir):
     from mpq_b200.awq import apply_awq_scaling
     z = np.load(golden_dir / "awq.npz")
     ref = json.loads(str(z["meta"]))
-    model = _tiny_llama(cuda_dev)
-    sd = {k[len("before/"):]: torch.from_numpy(z[k]) for k in z.files if k.startswith("before/")}
-    model.load_state_dict(sd)
+    model = _tiny_llama(cuda_dev, seed=5)
+    sums = np.array([float(v.double().abs().sum()) for v in model.state_dict().values()])
+    np.testing.assert_allclose(sums, z["before_checksum"], rtol=1e-12, err_msg="seeded initialisation drifted")
     with torch.no_grad():
         ref_logits = model(torch.from_numpy(z["ids"]).to(cuda_dev)).logits
     dbg = apply_awq_scaling(model, torch.from_numpy(z["ids"]), bits=4, group_size=32, sym=False, batch_size=2)
@@ -37,7 +45,8 @@ def test_awq_matches_reference(cuda_dev, golden_dir):
     after = model.state_dict()
     for k in z.files:
         if k.startswith("after/"):
-            np.testing.assert_allclose(after[k[len("after/"):]].cpu().numpy(), z[k], rtol=1e-5, atol=1e-6, err_msg=k)
+            np.testing.assert_allclose(after[k[len("after/"):]].float().cpu().numpy(), z[k], rtol=1e-5, atol=1e-6,
+                                       err_msg=k)
     # the folded scales leave the float model's function unchanged
     with torch.no_grad():
         logits = model(torch.from_numpy(z["ids"]).to(cuda_dev)).logits
