@@ -5,7 +5,8 @@ Reference: mpq/adapters/gptqmodel.py:650-1163 (run_mpq_quantization), :276-310
 (_uniform_vamp_cfg_from_qcfg), :1250-1470 (postprocess_gptq_quantization: the MPQ polish of a GPTQ solution).
 
 Only the default ``vamp`` solver is on this path; the research baselines (cdquant, quantease,
-ojbkq) and ``desc_act`` column permutation raise ``ValueError``.
+ojbkq) raise ``ValueError``.  ``desc_act`` (activation order) permutes the solver-basis columns by
+descending Hessian diagonal as the reference does (:700-738) and un-permutes the outputs (:819-822).
 """
 from __future__ import annotations
 
@@ -129,8 +130,7 @@ def run_mpq_quantization(
     solver_name = str(getattr(mpq_cfg, "dispatch_solver", getattr(mpq_cfg, "solver", "vamp")) or "vamp").lower()
     if solver_name != "vamp":
         raise ValueError(f"unsupported GPTQModel MPQ solver={solver_name!r} (only 'vamp' is on the CUDA path).")
-    if bool(getattr(qcfg, "desc_act", False)):
-        raise ValueError("desc_act column ordering is not supported by the CUDA path.")
+    use_activation_order = bool(getattr(qcfg, "desc_act", False))
     rotation = str(getattr(mpq_cfg, "rotation_mode", getattr(qcfg, "rotation", None) or "none") or "none").lower()
     if rotation not in {"none", "internal_hadamard", "model_hadamard", "model_random"}:
         raise ValueError("mpq only supports rotation in {none, model_hadamard, model_random, internal_hadamard}; "
@@ -140,7 +140,11 @@ def run_mpq_quantization(
     cache = adapter_cfg.eigen_cache
     key = (H.data_ptr(), tuple(H.shape), float(adapter_cfg.hessian_scale), float(adapter_cfg.jitter_base),
            float(adapter_cfg.eigen_floor_scale))
-    if cache is not None and key in cache:
+    lam = V = None
+    eigen_floor = 0.0
+    if use_activation_order:
+        pass  # (:716-721, :885-892) decomposed below in the permuted solver basis
+    elif cache is not None and key in cache:
         lam, V, eigen_floor = cache[key]
     else:
         lam, V, eigen_floor = vamp_hessian_eigen(H_work, jitter_base=adapter_cfg.jitter_base,
@@ -162,16 +166,28 @@ def run_mpq_quantization(
         W_work = apply_right_block_hadamard(W, signs=signs, had_dim=had_dim)
         H_metric = apply_right_block_hadamard(H_work.T.contiguous(), signs=signs, had_dim=had_dim).T.contiguous()
         H_metric = apply_right_block_hadamard(H_metric, signs=signs, had_dim=had_dim)
-        V = apply_right_block_hadamard(V.T.contiguous(), signs=signs, had_dim=had_dim).T.contiguous()
+        if V is not None:
+            V = apply_right_block_hadamard(V.T.contiguous(), signs=signs, had_dim=had_dim).T.contiguous()
     else:
         W_work, H_metric = W, H_work.contiguous()
+    activation_invperm = None
+    if use_activation_order:
+        # (:731-736) columns by descending Hessian diagonal in the solver basis; a stable sort keeps equal
+        # diagonals in column order
+        activation_perm = torch.argsort(torch.diagonal(H_metric), descending=True, stable=True)
+        activation_invperm = torch.argsort(activation_perm)
+        W_work = W_work.index_select(1, activation_perm).contiguous()
+        H_metric = H_metric.index_select(0, activation_perm).index_select(1, activation_perm).contiguous()
     dead = torch.diagonal(H_metric) == 0
-    if bool(dead.any().item()):
-        # mpq/adapters/gptqmodel.py:743-749 then a re-decomposition in the solver basis (:885-892)
+    has_dead = bool(dead.any().item())
+    if has_dead:
+        # mpq/adapters/gptqmodel.py:743-749
         H_metric = H_metric.clone()
         W_work = W_work.clone()
         H_metric[dead, dead] = 1
         W_work[:, dead] = 0
+    if has_dead or V is None:
+        # re-decomposition of the exact solver-basis Hessian (:885-892)
         lam, V, eigen_floor = vamp_hessian_eigen(H_metric, jitter_base=adapter_cfg.jitter_base,
                                                  floor_scale=adapter_cfg.eigen_floor_scale)
     V = V.contiguous()
@@ -253,6 +269,10 @@ def run_mpq_quantization(
         block_stats.append(st)
 
     g_idx = torch.arange(cols, device=device, dtype=torch.int32) // int(group_size)
+    if activation_invperm is not None:  # (:819-822)
+        Q_work = Q_work.index_select(1, activation_invperm).contiguous()
+        q_int_work = q_int_work.index_select(1, activation_invperm).contiguous()
+        g_idx = g_idx.index_select(0, activation_invperm).contiguous()
     Q = apply_right_block_hadamard_inverse(Q_work, signs=signs, had_dim=had_dim) if signs is not None else Q_work
     stats: Dict[str, Any] = {
         "method": "mpq",
@@ -264,6 +284,7 @@ def run_mpq_quantization(
         "rotation_effective": effective,
         "rotation_internal": signs is not None,
         "rotation_block_dim": int(had_dim),
+        "desc_act": bool(use_activation_order),
         "rows": int(rows),
         "cols": int(cols),
         "rank": R,

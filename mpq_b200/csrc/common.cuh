@@ -17,6 +17,10 @@ namespace mpq {
 
 void set_last_error(const char* fmt, ...);
 
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device (once per device and kernel;
+// thread-safe).  Returns MPQ_OK or the cudaError_t of the failing call, with the message in mpq_last_error().
+int smem_opt_in(const void* kernel, size_t bytes, const char* what);
+
 inline int launch_status(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -598,11 +598,8 @@ template <int BN, int STAGES, int KIND = 0>
 static int launch(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
                   int* status, cudaStream_t stream, int sym = 0, const float* sa = nullptr, const float* sb = nullptr) {
   const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * 128 + 256;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_gemm_tc<BN, STAGES, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  const int ast = smem_opt_in((const void*)k_gemm_tc<BN, STAGES, KIND>, smem, "mpq_gemm_tc");
+  if (ast) return ast;
   dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
   k_gemm_tc<BN, STAGES, KIND><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status, sym,
                                                                  sa, sb);
@@ -626,11 +623,8 @@ template <int BN, int STAGES, int KIND>
 static int launch_pt(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
                      int* status, cudaStream_t stream, int sym = 0, const float* sa = nullptr, const float* sb = nullptr) {
   const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * 128 + 256;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_gemm_tc_pt<BN, STAGES, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  const int ast = smem_opt_in((const void*)k_gemm_tc_pt<BN, STAGES, KIND>, smem, "mpq_gemm_tc (persistent)");
+  if (ast) return ast;
   const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
   int64_t ntiles = 0;
   if (sym) {
@@ -661,7 +655,6 @@ MPQ_API int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float*
   if (M == 0 || N == 0) return MPQ_OK;  // empty tensors may carry null pointers
   MPQ_CHECK_ARG(A && B && C, "mpq_gemm_tc: null pointer");
   MPQ_CHECK_ARG(lda % 4 == 0 && ldb % 4 == 0 && lda >= K && ldb >= K, "mpq_gemm_tc: lda/ldb must be multiples of 4 and >= K");
-  if (M == 0 || N == 0) return MPQ_OK;
   int st = tc::get_encoder();
   if (st) return st;
   tc::Maps maps;
@@ -739,7 +732,6 @@ MPQ_API int mpq_gemm_f16x3(int M, int N, int K, float alpha, const void* a_hi, c
   const void* ptrs[4] = {a_hi, a_lo, b_hi, b_lo};
   for (int i = 0; i < 4; ++i)
     MPQ_CHECK_ARG(((uintptr_t)ptrs[i] & 15) == 0, "mpq_gemm_f16x3: operands must be 16-byte aligned");
-  if (M == 0 || N == 0) return MPQ_OK;
   int st = tc::get_encoder();
   if (st) return st;
   tc::Maps maps;
@@ -889,7 +881,6 @@ static int scratch_base(unsigned char** out) {
 // The first call on each device performs the set-up above; make it before any stream capture.
 MPQ_API int mpq_gemm_tf32x3_noalloc(int M, int N, int K, float alpha, const float* A, int64_t lda, const float* B,
                                     int64_t ldb, float beta, float* C, int64_t ldc, int* status, void* stream) {
-  MPQ_CHECK_ARG(A && B && C, "mpq_gemm_tf32x3_noalloc: null pointer");
   MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 1, "mpq_gemm_tf32x3_noalloc: bad shape");
   MPQ_CHECK_ARG(lda >= K && ldb >= K && ldc >= N, "mpq_gemm_tf32x3_noalloc: leading dimensions too small");
   const int64_t kp = ((int64_t)K + 3) / 4 * 4;
@@ -897,7 +888,8 @@ MPQ_API int mpq_gemm_tf32x3_noalloc(int M, int N, int K, float alpha, const floa
   MPQ_CHECK_ARG(need <= noalloc::kMaxOperandFloats,
                 "mpq_gemm_tf32x3_noalloc: 2*(M+N)*round_up(K,4) = %lld floats exceeds the %lld-float scratch",
                 (long long)need, (long long)noalloc::kMaxOperandFloats);
-  if (M == 0 || N == 0) return MPQ_OK;
+  if (M == 0 || N == 0) return MPQ_OK;  // empty tensors may carry null pointers
+  MPQ_CHECK_ARG(A && B && C, "mpq_gemm_tf32x3_noalloc: null pointer");
   unsigned char* base = nullptr;
   int st = noalloc::scratch_base(&base);
   if (st) return st;

@@ -657,7 +657,10 @@ MPQ_API int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr,
   GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, base_abs, base_parity, grid, sign_id, res, idx, ldi,
                   delta, accepted, evals, B, accept_tol, nullptr, nullptr, 0, 0};
   const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
-  cudaFuncSetAttribute(k_gram_chunk<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const int ast = smem_opt_in((const void*)k_gram_chunk<false>, smem, "mpq_gram_chunk");
+    if (ast) return ast;
+  }
   k_gram_chunk<false><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
   return launch_status("mpq_gram_chunk");
 }
@@ -675,7 +678,10 @@ MPQ_API int mpq_gram_chunk_topk(float* x, int64_t ldx, const float* rhs, int64_t
   GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, nullptr, nullptr, nullptr, nullptr, res, idx, ldi,
                   delta, accepted, evals, B, accept_tol, cand, cand_idx, kc, nb};
   const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
-  cudaFuncSetAttribute(k_gram_chunk<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const int ast = smem_opt_in((const void*)k_gram_chunk<true>, smem, "mpq_gram_chunk_topk");
+    if (ast) return ast;
+  }
   k_gram_chunk<true><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
   return launch_status("mpq_gram_chunk_topk");
 }

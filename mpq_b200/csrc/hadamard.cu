@@ -56,7 +56,10 @@ MPQ_API int mpq_block_hadamard(const float* x, int64_t ldx, float* y, int64_t ld
   MPQ_CHECK_ARG(rows <= 65535, "mpq_block_hadamard: at most 65535 rows per call");
   if (rows == 0 || n == 0) return MPQ_OK;
   const size_t smem = (size_t)had * sizeof(float);
-  cudaFuncSetAttribute(k_block_hadamard, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const int ast = smem_opt_in((const void*)k_block_hadamard, smem, "mpq_block_hadamard");
+    if (ast) return ast;
+  }
   dim3 grid(n / had, rows);
   int threads = had / 2 < 1024 ? (had / 2 > 32 ? had / 2 : 32) : 1024;
   k_block_hadamard<<<grid, threads, smem, (cudaStream_t)stream>>>(x, ldx, y, ldy, n, had, signs, mode);

@@ -271,7 +271,10 @@ MPQ_API int mpq_argsort_desc(const float* key, int n, int* order, void* stream) 
   while (np2 < n) np2 <<= 1;
   if (np2 < 2) np2 = 2;
   const size_t smem = (size_t)np2 * 8;
-  cudaFuncSetAttribute(k_argsort_desc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const int ast = smem_opt_in((const void*)k_argsort_desc, smem, "mpq_argsort_desc");
+    if (ast) return ast;
+  }
   k_argsort_desc<<<1, 1024, smem, (cudaStream_t)stream>>>(key, n, np2, order);
   return launch_status("mpq_argsort_desc");
 }
@@ -297,7 +300,10 @@ MPQ_API int mpq_cd_block(float* x, int64_t ldx, const float* rhs, int64_t ldr, c
   CdArgs a{x, ldx, rhs, ldr, scale, zero, ld_p, gshift, nullptr, nullptr, 0, 0, nullptr, 0, diag, diag_inv, order, c0,
            K, Hsub, res, delta, accepted, B, maxq, accept_tol};
   const size_t smem = (size_t)kCdBlock * kCdBlock * sizeof(float);
-  cudaFuncSetAttribute(k_cd_block<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const int ast = smem_opt_in((const void*)k_cd_block<false>, smem, "mpq_cd_block");
+    if (ast) return ast;
+  }
   k_cd_block<false><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
   return launch_status("mpq_cd_block");
 }
@@ -314,7 +320,10 @@ MPQ_API int mpq_cd_block_topk(float* x, int64_t ldx, const float* rhs, int64_t l
   CdArgs a{x, ldx, rhs, ldr, nullptr, nullptr, 0, 0, cand, cand_q, ld_cand, kc, qout, ldq, diag, diag_inv, order, c0,
            K, Hsub, res, delta, accepted, B, 1, accept_tol};
   const size_t smem = (size_t)kCdBlock * kCdBlock * sizeof(float);
-  cudaFuncSetAttribute(k_cd_block<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const int ast = smem_opt_in((const void*)k_cd_block<true>, smem, "mpq_cd_block_topk");
+    if (ast) return ast;
+  }
   k_cd_block<true><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
   return launch_status("mpq_cd_block_topk");
 }

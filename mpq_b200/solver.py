@@ -392,8 +392,8 @@ def solve_uniform_rankspace_vamp(
     prior_tau = float(cfg.prior_tau)
     final_decision = str(cfg.final_decision or "map").strip().lower()
     init_from = str(cfg.init_from or "rtn").strip().lower()
-    if final_decision != "map":
-        raise ValueError(f"unsupported final_decision={cfg.final_decision!r} (the CUDA path implements 'map')")
+    if final_decision not in {"map", "round_mean"}:
+        raise ValueError(f"unsupported final_decision={cfg.final_decision!r}")
     B, n = W.shape
     R = int(S.numel())
     if R == 0:
@@ -427,8 +427,18 @@ def solve_uniform_rankspace_vamp(
         return (ptr(r), r.stride(0), ptr(W), W.stride(0), ptr(scale_full), ptr(zero_full), ctx.ld_p, ctx.gshift,
                 ptr(g), B, n, maxq, prior_tau)
 
+    mean_tmp = torch.empty(B, n, **f32) if final_decision == "round_mean" else None
+    vsum_tmp = torch.empty(B, **f32) if final_decision == "round_mean" else None
+
     def hard_state(r, g, q_out, x_out, err_out):
-        call("mpq_uniform_map_decision", *args_uniform(r, g), ptr(q_out), ptr(x_out), x_out.stride(0))
+        """mpq/solver.py:513-541 + _uniform_hard_decision :833-850: 'map' rounds the posterior's MAP atom,
+        'round_mean' rounds the posterior mean to the nearest grid level."""
+        if final_decision == "map":
+            call("mpq_uniform_map_decision", *args_uniform(r, g), ptr(q_out), ptr(x_out), x_out.stride(0))
+        else:
+            call("mpq_uniform_mmse", *args_uniform(r, g), ptr(mean_tmp), mean_tmp.stride(0), None, None, None,
+                 ptr(vsum_tmp))
+            ctx.nearest(mean_tmp, q_out, x_out)
         ctx.err(x_out, out=err_out, tmp=tmpBR)
 
     best_q = torch.empty(B, n, device=dev, dtype=torch.uint8)

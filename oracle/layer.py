@@ -118,24 +118,36 @@ def rademacher_signs_torch(width: int, key: str, seed: int = 0) -> np.ndarray:
 def run_scalar_layer(*, W, H, bits, group_size, vamp_cfg: UniformVampConfig, block_rows: int,
                      module_name: str = "layer", rotation: str = "internal_hadamard",
                      hessian_scale: float = 0.5, rotation_seed: int = 0,
-                     jitter_base=1e-6, eigen_floor_scale=1e-6) -> Dict[str, Any]:
-    """mpq/adapters/gptqmodel.py:650-1163 (vamp solver, no desc_act, no dead columns,
-    no paired-matrix cache), with the CUDA polish semantics of mpq/solver.py:299-333."""
+                     jitter_base=1e-6, eigen_floor_scale=1e-6, desc_act: bool = False) -> Dict[str, Any]:
+    """mpq/adapters/gptqmodel.py:650-1163 (vamp solver, no dead columns, no paired-matrix cache), with the CUDA
+    polish semantics of mpq/solver.py:299-333.  desc_act (:700-738, :819-822): the solver-basis columns are
+    ordered by descending Hessian diagonal, the Hessian is decomposed in that basis, and the outputs (Q, q_int,
+    g_idx) are put back in column order."""
     W = W.astype(f32)
     rows, cols = W.shape
     maxq = 2 ** int(bits) - 1
     H_work = (f32(hessian_scale) * H.astype(f32)).astype(f32)
-    lam, V, floor = vamp_hessian_eigen(H_work, jitter_base=jitter_base, floor_scale=eigen_floor_scale)
+    lam = V = None
+    if not desc_act:
+        lam, V, floor = vamp_hessian_eigen(H_work, jitter_base=jitter_base, floor_scale=eigen_floor_scale)
     if rotation == "internal_hadamard":
         had = largest_pow2_factor(cols)
         signs = rademacher_signs_torch(cols, f"{module_name}:full", rotation_seed)
         W_work = right_block_hadamard(W, signs, had)
         Hm = right_block_hadamard(np.ascontiguousarray(H_work.T), signs, had).T.copy()
         Hm = right_block_hadamard(Hm, signs, had)
-        V = right_block_hadamard(np.ascontiguousarray(V.T), signs, had).T.copy()
+        if V is not None:
+            V = right_block_hadamard(np.ascontiguousarray(V.T), signs, had).T.copy()
     else:
         had, signs = 1, None
         W_work, Hm = W, H_work
+    invperm = None
+    if desc_act:
+        perm = np.argsort(-np.diagonal(Hm), kind="stable")
+        invperm = np.argsort(perm, kind="stable")
+        W_work = np.ascontiguousarray(W_work[:, perm])
+        Hm = np.ascontiguousarray(Hm[perm][:, perm])
+        lam, V, floor = vamp_hessian_eigen(Hm, jitter_base=jitter_base, floor_scale=eigen_floor_scale)
     Vh = np.ascontiguousarray(V.T)
     S = np.sqrt(lam).astype(f32)
     Vs = (V * S[None, :]).astype(f32)
@@ -183,10 +195,16 @@ def run_scalar_layer(*, W, H, bits, group_size, vamp_cfg: UniformVampConfig, blo
         if vamp_cfg.em_obs_precision:
             obs = float(st["obs_precision_final"])
         blocks.append(st)
+    g_idx = (np.arange(cols) // int(group_size)).astype(np.int32)
+    Q_solver, q_solver = Q, q_int
+    if invperm is not None:
+        Q = np.ascontiguousarray(Q[:, invperm])
+        q_int = np.ascontiguousarray(q_int[:, invperm])
+        g_idx = np.ascontiguousarray(g_idx[invperm])
     Q_out = right_block_hadamard_inverse(Q, signs, had) if signs is not None else Q
-    return {"Q": Q_out, "Q_work": Q, "q_int": q_int, "scale": scale_g, "zero": zero_g,
-            "W_work": W_work, "H_metric": Hm, "V": V, "S": S, "Vs": Vs, "signs": signs, "had_dim": had,
-            "obs_precision_initial": obs_init, "obs_precision_final": obs, "block_stats": blocks}
+    return {"Q": Q_out, "Q_work": Q_solver, "q_int": q_int, "q_solver": q_solver, "scale": scale_g, "zero": zero_g,
+            "g_idx": g_idx, "W_work": W_work, "H_metric": Hm, "V": V, "S": S, "Vs": Vs, "signs": signs, "had_dim": had,
+            "invperm": invperm, "obs_precision_initial": obs_init, "obs_precision_final": obs, "block_stats": blocks}
 
 
 def proxy_loss(W_work: np.ndarray, Q_work: np.ndarray, H: np.ndarray) -> float:

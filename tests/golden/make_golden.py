@@ -151,18 +151,23 @@ def gen_scalar_layer(out):
     from mpq.adapters.gptqmodel import run_mpq_quantization, GPTQAdapterConfig
     from mpq.solver import UniformVampConfig
     cases = {}
-    for name, (m, n, bits, block_rows, iters) in {"a": (48, 256, 4, 16, 20), "b": (32, 128, 3, 32, 16)}.items():
+    # (m, n, bits, block_rows, iters, desc_act, final_decision); "c" activation order, "d" round-mean decision
+    layers = {"a": (48, 256, 4, 16, 20, False, "map"), "b": (32, 128, 3, 32, 16, False, "map"),
+              "c": (40, 256, 4, 16, 16, True, "map"), "d": (32, 256, 3, 16, 12, False, "round_mean")}
+    for name, (m, n, bits, block_rows, iters, desc_act, decision) in layers.items():
         W, H = synth_layer(m, n, 100 + m)
-        qcfg = types.SimpleNamespace(bits=bits, group_size=64, desc_act=False,
+        qcfg = types.SimpleNamespace(bits=bits, group_size=64, desc_act=desc_act,
                                      mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
-        cfg = UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto")
+        cfg = UniformVampConfig(iters=iters, prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto",
+                                final_decision=decision)
         acfg = GPTQAdapterConfig(block_rows=block_rows)
         Q, q_int, scale, zero, g_idx, _, st = run_mpq_quantization(
             W=W, H=2.0 * H, quantizer=MinMaxQuantizer(bits), qcfg=qcfg, module_name=f"golden.{name}",
             vamp_cfg=cfg, adapter_cfg=acfg)
-        for k, v in dict(W=W, H=H, Q=Q, q_int=q_int, scale=scale, zero=zero).items():
+        for k, v in dict(W=W, H=H, Q=Q, q_int=q_int, scale=scale, zero=zero, g_idx=g_idx).items():
             cases[f"{name}/{k}"] = _np(v)
         cases[f"{name}/meta"] = np.array(json.dumps(dict(bits=bits, group_size=64, block_rows=block_rows, iters=iters,
+                                                          desc_act=desc_act, final_decision=decision,
                                                           obs_init=st["obs_precision_initial"],
                                                           obs_final=st["obs_precision_final"],
                                                           raw_objective=st["raw_objective_mean_final"],

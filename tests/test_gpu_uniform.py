@@ -298,9 +298,10 @@ def test_polish_uniform_topk_entry(cuda_dev):
                                    sweeps=2, polish_mode="topk_block_cd")
 
 
-@pytest.mark.parametrize("case", ["a", "b"])
+@pytest.mark.parametrize("case", ["a", "b", "c", "d"])
 def test_run_mpq_quantization_matches_reference_golden(cuda_dev, golden_dir, case):
-    """The full per-linear driver against the reference's own output (tests/golden/scalar_layer.npz)."""
+    """The full per-linear driver against the reference's own output (tests/golden/scalar_layer.npz): a/b the default
+    recipe, c activation order (desc_act), d the round-mean final decision."""
     import json
     import types
     from mpq_b200.adapters.gptqmodel import GPTQAdapterConfig, run_mpq_quantization
@@ -308,15 +309,19 @@ def test_run_mpq_quantization_matches_reference_golden(cuda_dev, golden_dir, cas
     z = np.load(golden_dir / "scalar_layer.npz")
     g = lambda k: z[f"{case}/{k}"]
     meta = json.loads(str(g("meta")))
-    qcfg = types.SimpleNamespace(bits=meta["bits"], group_size=meta["group_size"], desc_act=False,
+    qcfg = types.SimpleNamespace(bits=meta["bits"], group_size=meta["group_size"],
+                                 desc_act=bool(meta.get("desc_act", False)),
                                  mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
-    cfg = UniformVampConfig(iters=meta["iters"], prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto")
+    cfg = UniformVampConfig(iters=meta["iters"], prior_tau=0.2, damping=0.5, polish_sweeps=3, block_cd_backend="auto",
+                            final_decision=meta.get("final_decision", "map"))
     acfg = GPTQAdapterConfig(block_rows=meta["block_rows"], grow_block_rows=False)
     Q, q_int, scale, zero, g_idx, _, st = run_mpq_quantization(
         W=_t(g("W"), cuda_dev), H=_t(2.0 * g("H"), cuda_dev), quantizer=None, qcfg=qcfg, module_name=f"golden.{case}",
         vamp_cfg=cfg, adapter_cfg=acfg)
     np.testing.assert_allclose(scale.cpu().numpy(), g("scale"), rtol=1e-6)
     np.testing.assert_array_equal(zero.cpu().numpy(), g("zero"))
+    np.testing.assert_array_equal(g_idx.cpu().numpy(), g("g_idx"))
+    assert st["desc_act"] == bool(meta.get("desc_act", False))
     agree = (q_int.cpu().numpy() == g("q_int")).mean()
     assert agree >= 0.999, agree
     rel = abs(st["raw_objective_mean_final"] - meta["raw_objective"]) / meta["raw_objective"]

@@ -70,18 +70,25 @@ def test_rotation_and_seeds(golden_dir):
     np.testing.assert_allclose(L.right_block_hadamard_inverse(R, signs, 64), z["Ri"], rtol=0, atol=1e-6)
 
 
-@pytest.mark.parametrize("case", ["a", "b"])
+@pytest.mark.parametrize("case", ["a", "b", "c", "d"])
 def test_scalar_layer_matches_reference(golden_dir, case):
+    """Cases: a/b default recipe, c activation order (desc_act), d round-mean final decision."""
     z = _load(golden_dir, "scalar_layer")
     g = lambda k: z[f"{case}/{k}"]
     meta = json.loads(str(g("meta")))
-    cfg = U.UniformVampConfig(iters=meta["iters"], prior_tau=0.2, damping=0.5, polish_sweeps=3)
+    cfg = U.UniformVampConfig(iters=meta["iters"], prior_tau=0.2, damping=0.5, polish_sweeps=3,
+                              final_decision=meta.get("final_decision", "map"))
     out = L.run_scalar_layer(W=g("W"), H=2.0 * g("H"), bits=meta["bits"], group_size=meta["group_size"],
-                             vamp_cfg=cfg, block_rows=meta["block_rows"], module_name=f"golden.{case}")
+                             vamp_cfg=cfg, block_rows=meta["block_rows"], module_name=f"golden.{case}",
+                             desc_act=bool(meta.get("desc_act", False)))
     np.testing.assert_allclose(out["scale"], g("scale"), rtol=1e-6)
     np.testing.assert_array_equal(out["zero"], g("zero"))
+    np.testing.assert_array_equal(out["g_idx"], g("g_idx"))
     agree = (out["q_int"] == g("q_int")).mean()
     assert agree >= 0.999, agree
-    ref_loss = L.proxy_loss(out["W_work"], L.right_block_hadamard(g("Q"), out["signs"], out["had_dim"]), out["H_metric"])
+    ref_q = L.right_block_hadamard(g("Q"), out["signs"], out["had_dim"])
+    if out["invperm"] is not None:
+        ref_q = ref_q[:, np.argsort(out["invperm"])]
+    ref_loss = L.proxy_loss(out["W_work"], ref_q, out["H_metric"])
     my_loss = L.proxy_loss(out["W_work"], out["Q_work"], out["H_metric"])
     assert abs(my_loss - ref_loss) <= 0.005 * ref_loss
