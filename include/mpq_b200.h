@@ -113,6 +113,46 @@ int mpq_row_dot(const float* A, int64_t lda, const float* C, int64_t ldc, int B,
 /* D = A - C (same leading dimension).  mpq/adapters/gptqmodel.py:932, :1049. */
 int mpq_sub(const float* A, const float* C, float* D, int B, int n, int64_t ld, void* stream);
 
+/* ---- device-resident VAMP control (mpq/solver.py:553-699 and :961-1122 without host round trips) ----
+ * The host decisions of the reference's loop -- gamma retries (:553-596), skipped iterations on invalid gamma2
+ * (:598-616), the EM update of the observation precision (mpq/linear.py:59-82, log-damped as
+ * mpq/utils.py:36-45) and the scalar best-iterate test (:668-699) -- are taken by small kernels reading and writing
+ * a 64-byte control block in device memory (mpq_vamp_ctl_size() bytes, zeroed, then obs (float64 at offset 0) set
+ * to the starting precision).  Layout: double obs; int active, skip, have_prev, stopped, fail, alpha1_retry_count,
+ * alpha2_clip_count, gamma2_invalid_count, committed, best_iter, stop_iter; 3 ints padding.  The *_ctl variants of
+ * the iteration kernels do nothing on a skipped iteration and read obs from the block. */
+int mpq_vamp_ctl_size(void);
+/* Opens an iteration: gamma1_work = gamma1, flags[0..7] = 0, active = !stopped, skip = stopped. */
+int mpq_vamp_ctl_begin(void* ctl, const float* gamma1, float* gamma1_work, int B, int* flags, void* stream);
+/* Closes retry round `final_round` (0 or 1 for the last): counts retries and rescales gamma1_work of invalid rows, or
+ * closes the round and applies the invalid-gamma2 skip / alpha2 clip counts. */
+int mpq_vamp_ctl_round(void* ctl, int* flags, float* gamma1_work, const float* var_rowsum, int B, int n_var,
+                       float factor, int final_round, void* stream);
+/* Commits a live iteration: gamma1 <- gamma1_next, gamma2_prev <- gamma2, EM update of obs from
+ * mean(resid_rowsum + trace); obs_hist[it] (optional) records obs (NaN for a skipped iteration). */
+int mpq_vamp_ctl_commit(void* ctl, float* gamma1, const float* gamma1_next, float* gamma2_prev, const float* gamma2,
+                        const float* resid_rowsum, const float* trace, int B, int R, int em_active, double em_damping,
+                        double em_min, double em_max, double* obs_hist, int it, void* stream);
+/* Best-iterate test and state copies of the scalar loop (mpq/solver.py:668-699); decision[0] = 1 improved, 0 stopped
+ * (r1, gamma1, obs restored), -1 skipped. */
+int mpq_vamp_ctl_best(void* ctl, const float* err_cur, int B, int n, double* best_mean, double* best_obs,
+                      uint8_t* best_q, const uint8_t* cur_q, float* best_x, const float* cur_x, float* best_err,
+                      float* best_r1, float* r1, float* best_g1, float* gamma1, int64_t ld, int it, int* decision,
+                      void* stream);
+int mpq_vamp_rows_ctl(const float* var_rowsum, float* gamma1, float* gamma1_work, float* alpha1, float* eta1,
+                      float* gamma2_new, float* gamma2, const float* gamma2_prev, float* alpha2, float* eta2,
+                      float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int B, int n,
+                      int n_var, int R, float damping, int final_retry, const void* ctl, void* stream);
+int mpq_vamp_r2_ctl(const float* x1, const float* r1, const float* r2_prev, float* r2, const float* eta1,
+                    const float* gamma1_work, const float* gamma2_new, int B, int n, int64_t ld, float damping,
+                    const void* ctl, void* stream);
+int mpq_linear_epilogue_ctl(const float* P, const float* Y_u, const float* S, const float* gamma2, int B, int R,
+                            int64_t ld, float* u, float* resid_rowsum, const void* ctl, void* stream);
+/* r2_keep (optional) receives r2 (the next iteration's r2_prev). */
+int mpq_vamp_r1_ctl(const float* D, const float* r2, float* r1, const float* eta2, const float* gamma2,
+                    const float* gamma1_new, int B, int n, int64_t ld, float damping, float* r2_keep, const void* ctl,
+                    void* stream);
+
 /* ---- dense products (K7/K8, scalar-CD block updates) ----
  * C = alpha A op(B) + beta C with A: M x K row-major; layout 0: B is N x K ("NT"), layout 1: B is K x N ("NN").
  * Replaces the torch matmuls of mpq/linear.py:48,51,94, mpq/solver.py:485 and
@@ -161,6 +201,13 @@ int mpq_gemm_tc(int nreg, int M, int N, int K, float alpha, const float* const* 
 int mpq_gemm_f16x3(int M, int N, int K, float alpha, const void* a_hi, const void* a_lo, int64_t lda, const float* sa,
                    const void* b_hi, const void* b_lo, int64_t ldb, const float* sb, float beta, float* C, int64_t ldc,
                    int* status, void* stream);
+/* mpq_gemm_f16x3 with split-K for small-M products (a 128-row VAMP block against the n x n basis, mpq/linear.py:48,51
+ * at the block sizes of mpq/adapters/quip_sharp.py:28): the k-blocks of each output tile are cut into `splits`
+ * ranges run by different CTAs; their partials go to ws (caller-owned, splits * M * N floats) and are summed in a
+ * fixed order (deterministic).  1 <= splits <= 3 * ceil(K / 64). */
+int mpq_gemm_f16x3_splitk(int M, int N, int K, float alpha, const void* a_hi, const void* a_lo, int64_t lda,
+                          const float* sa, const void* b_hi, const void* b_lo, int64_t ldb, const float* sb, float beta,
+                          float* C, int64_t ldc, int splits, float* ws, int64_t ws_floats, int* status, void* stream);
 /* Row-scaled fp16 split: s = 2^(15 - E) with max|x_row| < 2^E, hi = fp16(x s), lo = fp16(x s - hi), inv_scale = 1 / s. */
 int mpq_split_f16(const float* x, int64_t ldx, int rows, int cols, void* hi, void* lo, int64_t ldo, float* inv_scale,
                   void* stream);
@@ -212,6 +259,16 @@ int mpq_e8p12_mmse(const float* r1, int64_t ld_r1, const float* center, int64_t 
                    const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,
                    float* x1_out, int64_t ld_x, float* var_out, int64_t ld_v, int* idx_out, int64_t ld_i,
                    float* map_out, int64_t ld_m, float* var_rowsum, void* stream);
+/* The posterior mean and per-row variance sum of mpq_e8p12_mmse with each row cut into `chunks` item ranges (one CTA
+ * each), so a 128-row block (mpq/adapters/quip_sharp.py:28, 555-586) still fills the GPU.  work: caller-owned
+ * B (chunks + 1) 32-bit words, zeroed once before the first call (chunk partials + arrival counters, left at zero);
+ * partials are added in chunk order.  active: optional device int; while it is 0 the launch does nothing (the gamma
+ * retries of mpq/solver.py:553-596 decided on the device). */
+int mpq_e8p12_mmse_rows(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                        int64_t ld_s, const float* gamma, float prior_tau, int B, int nb, const float* base_abs,
+                        const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,
+                        float* x1_out, int64_t ld_x, float* var_rowsum, int chunks, void* work, const int* active,
+                        void* stream);
 /* MAP codeword (bit-exact first maximum); fixed_gamma > 0 with prior_tau <= 0 is the nearest codeword (RTN).
  * Replaces mpq/priors/e8p12.py:541-631 (vamp_vector_map_e8p12, _branch_factorized_map :367-449) and the
  * nearest-codeword cb.quantize of mpq/adapters/quip_sharp.py:212-241. */

@@ -20,6 +20,7 @@ P = ctypes.c_void_p
 I = ctypes.c_int
 L = ctypes.c_int64
 F = ctypes.c_float
+D = ctypes.c_double
 
 # name -> argtypes (every entry returns int status; `stream` is the trailing c_void_p)
 SIGNATURES: Dict[str, Tuple[Any, ...]] = {
@@ -30,6 +31,7 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_uniform_rtn": (P, L, P, P, L, I, I, I, I, P, P, L, P),
     "mpq_block_hadamard": (P, L, P, L, I, I, I, P, I, P),
     "mpq_e8p12_mmse": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, L, P, L, P, L, P, P),
+    "mpq_e8p12_mmse_rows": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, I, P, P, P),
     "mpq_e8p12_map": (P, L, P, L, P, L, P, F, F, I, I, P, P, P, P, P, P, L, P, L, P),
     "mpq_e8p12_topk": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, I, P, P, P, P),
     "mpq_uniform_topk": (P, L, P, L, P, P, L, I, P, I, I, I, F, I, P, P, P, P),
@@ -55,6 +57,7 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_gemm_tc": (I, I, I, I, F, P, L, P, L, F, P, L, P, P),
     "mpq_split_tf32": (P, L, P, P, L, I, I, P),
     "mpq_gemm_f16x3": (I, I, I, F, P, P, L, P, P, P, L, P, F, P, L, P, P),
+    "mpq_gemm_f16x3_splitk": (I, I, I, F, P, P, L, P, P, P, L, P, F, P, L, I, P, L, P, P),
     "mpq_split_f16": (P, L, I, I, P, P, L, P, P),
     "mpq_gemm_tf32x3_noalloc": (I, I, I, F, P, L, P, L, F, P, L, P, P),
     "mpq_syrk_tc": (I, I, I, F, P, P, L, F, P, L, P, P),
@@ -71,6 +74,15 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_cd_gather": (P, L, I, P, I, I, P, P, P),
     "mpq_cd_block": (P, L, P, L, P, P, L, I, P, P, P, I, I, P, P, P, P, I, I, F, P),
     "mpq_cd_block_topk": (P, L, P, L, P, P, L, I, P, L, P, P, P, I, I, P, P, P, P, I, F, P),
+    "mpq_vamp_ctl_size": (),
+    "mpq_vamp_ctl_begin": (P, P, P, I, P, P),
+    "mpq_vamp_ctl_round": (P, P, P, P, I, I, F, I, P),
+    "mpq_vamp_ctl_commit": (P, P, P, P, P, P, P, I, I, I, D, D, D, P, I, P),
+    "mpq_vamp_ctl_best": (P, P, I, I, P, P, P, P, P, P, P, P, P, P, P, L, I, P, P),
+    "mpq_vamp_rows_ctl": (P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, F, I, P, P),
+    "mpq_vamp_r2_ctl": (P, P, P, P, P, P, P, I, I, L, F, P, P),
+    "mpq_linear_epilogue_ctl": (P, P, P, P, I, I, L, P, P, P, P),
+    "mpq_vamp_r1_ctl": (P, P, P, P, P, P, I, I, L, F, P, P, P),
     "mpq_gram_chunk_topk": (P, L, P, L, P, P, P, I, I, P, P, I, I, P, P, L, P, P, P, I, F, P),
 }
 

@@ -18,6 +18,7 @@ from .. import ops
 from .._lib import call, ptr
 from ..e8p12 import e8p12_nearest
 from ..rotation import stable_seed
+from ..chain import chain_supported, e8p12_layer_chain
 from ..solver import E8P12VampConfig, solve_e8p12_rankspace_vamp
 from .gptqmodel import vamp_hessian_eigen
 
@@ -77,14 +78,18 @@ class _Surrogate:
         return out
 
     def chunk_means(self, W, hat, block_rows) -> Tuple[float, List[float]]:
+        """Per-row surrogates of all rows in one product (rows are independent), then the means of the block_rows
+        chunks and of all rows, read back together."""
         m = W.shape[0]
-        tot, cnt, means = 0.0, 0, []
-        for r0 in range(0, m, block_rows):
-            s = self.rows(W[r0:r0 + block_rows], hat[r0:r0 + block_rows]).double()
-            means.append(float(s.mean().item()) if s.numel() else 0.0)
-            tot += float(s.sum().item())
-            cnt += int(s.numel())
-        return tot / max(cnt, 1), means
+        if m == 0:
+            return 0.0, []
+        s = self.rows(W, hat).double()
+        nfull = m // block_rows
+        parts = [s[:nfull * block_rows].reshape(nfull, block_rows).mean(1)] if nfull else []
+        if m % block_rows:
+            parts.append(s[nfull * block_rows:].mean().reshape(1))
+        means = torch.cat(parts + [s.mean().reshape(1)]).cpu().tolist()
+        return float(means[-1]), [float(v) for v in means[:-1]]
 
 
 @torch.inference_mode()
@@ -154,18 +159,15 @@ def mpq_refine_codebook(
     if requested_obs > 0.0:
         obs_precision = requested_obs
     else:
-        sum_sq, count = 0.0, 0
-        for r0 in range(0, m, block_rows):
-            rb = slice(r0, min(r0 + block_rows, m))
-            d = torch.empty_like(Wr[rb])
-            call("mpq_sub", ptr(Wr[rb]), ptr(hat_init[rb]), ptr(d), d.shape[0], n, d.stride(0))
-            du = ops.mm_nt(d, opVsT)
-            zeros = torch.zeros_like(du)
-            e = torch.empty(du.shape[0], device=device, dtype=torch.float32)
-            call("mpq_row_sqerr", ptr(du), ptr(zeros), du.shape[0], R, du.stride(0), zeros.stride(0), ptr(e))
-            sum_sq += float(e.double().sum().item())
-            count += int(du.numel())
-        obs_precision = 1.0 / float(max(sum_sq / max(count, 1), 1e-12))
+        # (:520-535) the mean squared rank-space RTN error over all rows; rows are independent, so one product
+        d = torch.empty_like(Wr)
+        call("mpq_sub", ptr(Wr), ptr(hat_init), ptr(d), m, n, d.stride(0))
+        du = ops.mm_nt(d, opVsT)
+        zeros = torch.zeros_like(du)
+        e = torch.empty(m, device=device, dtype=torch.float32)
+        call("mpq_row_sqerr", ptr(du), ptr(zeros), m, R, du.stride(0), zeros.stride(0), ptr(e))
+        sum_sq = float(e.double().sum().item())
+        obs_precision = 1.0 / float(max(sum_sq / max(m * R, 1), 1e-12))
     vamp_cfg = _build_vamp_cfg(args, polish_mode=polish_mode)
     sur = _Surrogate(Hr)
     exact_ldlq, exact_ldlq_chunks = sur.chunk_means(Wr, hatWr0.to(device=device, dtype=torch.float32).contiguous(),
@@ -176,20 +178,37 @@ def mpq_refine_codebook(
     obs_block = float(obs_precision)
     gamma_sum, gamma_count, changed, changed_total = 0.0, 0, 0, 0
     stats_chunk: Dict[str, Any] = {}
-    for r0 in range(0, m, block_rows):
-        rb = slice(r0, min(r0 + block_rows, m))
-        dbg: Dict[str, Any] = {"summary_only": True}
-        hat_c, idx_c, _err, stats_chunk = solve_e8p12_rankspace_vamp(
-            Wr=Wr[rb], hatWr_init=final_hat[rb], cb=cb, V=V, Vh=Vh, S=S, Vs=Vs, cfg=vamp_cfg,
-            module_name=module_name, obs_precision_init=obs_block, log_stats=False, debug_out=dbg)
-        final_hat[rb] = hat_c
-        final_idx[rb] = idx_c
-        if bool(vamp_cfg.em_obs_precision) and float(vamp_cfg.obs_precision) <= 0.0:
-            obs_block = float(stats_chunk.get("obs_precision_final", obs_block))
-        gamma_sum += float(dbg.get("gamma1_sum", 0.0))
-        gamma_count += int(dbg.get("gamma1_count", 0))
-        changed += int(dbg.get("changed_count", 0))
-        changed_total += int(dbg.get("changed_total", 0))
+    if chain_supported(vamp_cfg):
+        # the serial chain of row blocks on the device (VAMP chain on one stream, polish overlapped on others)
+        final_hat, final_idx, per_block = e8p12_layer_chain(
+            Wr=Wr, hat_init=hat_init, cb=cb, V=V, Vh=Vh, S=S, Vs=Vs, cfg=vamp_cfg, block_rows=block_rows,
+            obs_init=obs_precision)
+        for bst in per_block:
+            gamma_sum += bst.pop("_gamma1_sum")
+            gamma_count += bst.pop("_gamma1_count")
+            bst.pop("_gamma1_min")
+            bst.pop("_gamma1_max")
+            changed += bst.pop("_changed_count")
+            changed_total += bst.pop("_changed_total")
+            bst["module"] = str(module_name)
+        stats_chunk = per_block[-1] if per_block else {}
+        if bool(vamp_cfg.em_obs_precision) and float(vamp_cfg.obs_precision) <= 0.0 and per_block:
+            obs_block = float(per_block[-1]["obs_precision_final"])
+    else:
+        for r0 in range(0, m, block_rows):
+            rb = slice(r0, min(r0 + block_rows, m))
+            dbg: Dict[str, Any] = {"summary_only": True}
+            hat_c, idx_c, _err, stats_chunk = solve_e8p12_rankspace_vamp(
+                Wr=Wr[rb], hatWr_init=final_hat[rb], cb=cb, V=V, Vh=Vh, S=S, Vs=Vs, cfg=vamp_cfg,
+                module_name=module_name, obs_precision_init=obs_block, log_stats=False, debug_out=dbg)
+            final_hat[rb] = hat_c
+            final_idx[rb] = idx_c
+            if bool(vamp_cfg.em_obs_precision) and float(vamp_cfg.obs_precision) <= 0.0:
+                obs_block = float(stats_chunk.get("obs_precision_final", obs_block))
+            gamma_sum += float(dbg.get("gamma1_sum", 0.0))
+            gamma_count += int(dbg.get("gamma1_count", 0))
+            changed += int(dbg.get("changed_count", 0))
+            changed_total += int(dbg.get("changed_total", 0))
     exact_after, exact_after_chunks = sur.chunk_means(Wr, final_hat, block_rows)
     violations, max_delta, max_ratio = 0, 0.0, 0.0
     for ld, mp in zip(exact_ldlq_chunks, exact_after_chunks):

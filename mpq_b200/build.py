@@ -12,13 +12,11 @@ CSRC = HERE / "csrc"
 OUT = HERE / "libmpq_b200.so"
 
 SOURCES = ["capi.cu", "uniform_prior.cu", "vamp_uniform.cu", "gemm_simt.cu", "scalar_cd.cu", "hadamard.cu", "gemm_tc.cu", "e8p12.cu",
-           "gram_cd.cu", "hessian.cu", "block_cd.cu", "pack.cu", "topk.cu"]
+           "gram_cd.cu", "hessian.cu", "block_cd.cu", "pack.cu", "topk.cu", "vamp_ctl.cu"]
 
-NVCC_FLAGS = [
-    "-gencode", "arch=compute_100a,code=sm_100a",
-    "-O3", "-lineinfo", "-std=c++17",
-    "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-]
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17"]
+COMPILE_FLAGS = ARCH_FLAGS + ["-Xcompiler", "-fPIC,-fvisibility=hidden"]
+LINK_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-shared"]
 
 
 def nvcc_path() -> str:
@@ -28,21 +26,38 @@ def nvcc_path() -> str:
     return cand
 
 
+def _compile(nvcc: str, src: Path, obj: Path, verbose: bool) -> str:
+    cmd = [nvcc, *COMPILE_FLAGS, *(["-Xptxas", "-v"] if verbose else []), "-c", "-o", str(obj), str(src)]
+    res = subprocess.run(cmd, cwd=str(CSRC), capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src.name} ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    return res.stdout + res.stderr
+
+
 def build(verbose: bool = False, force: bool = False) -> Path:
+    """Compile every source to an object (in parallel, sm_100a) and link libmpq_b200.so in place."""
+    from concurrent.futures import ThreadPoolExecutor
     srcs = [CSRC / s for s in SOURCES]
     deps = srcs + sorted(CSRC.glob("*.cuh"))
     if OUT.exists() and not force:
         newest = max(p.stat().st_mtime for p in deps)
         if OUT.stat().st_mtime >= newest:
             return OUT
+    nvcc = nvcc_path()
+    objdir = HERE / "_build" / f"obj{os.getpid()}"
+    objdir.mkdir(parents=True, exist_ok=True)
+    objs = [objdir / (s.stem + ".o") for s in srcs]
+    with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
+        logs = list(ex.map(lambda so: _compile(nvcc, so[0], so[1], verbose), zip(srcs, objs)))
     tmp = OUT.with_suffix(f".so.tmp{os.getpid()}")
-    cmd = [nvcc_path(), *NVCC_FLAGS, *(["-Xptxas", "-v"] if verbose else []), "-o", str(tmp), *map(str, srcs)]
-    res = subprocess.run(cmd, cwd=str(CSRC), capture_output=True, text=True)
+    res = subprocess.run([nvcc, *LINK_FLAGS, "-o", str(tmp), *map(str, objs)], cwd=str(CSRC), capture_output=True,
+                         text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+        raise RuntimeError(f"nvcc link failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose:
-        print(res.stdout, res.stderr, sep="\n")
+        print("\n".join(logs))
     tmp.replace(OUT)
+    shutil.rmtree(objdir, ignore_errors=True)
     return OUT
 
 

@@ -21,6 +21,24 @@ void set_last_error(const char* fmt, ...);
 // thread-safe).  Returns MPQ_OK or the cudaError_t of the failing call, with the message in mpq_last_error().
 int smem_opt_in(const void* kernel, size_t bytes, const char* what);
 
+// Device-resident control block of one VAMP iteration loop (see vamp_ctl.cu).
+struct VampCtl {
+  double obs;               //  0: observation precision (float64, as the reference's Python float)
+  int active;               //  8: a retry round is still open (denoiser / row stage run while 1)
+  int skip;                 // 12: the rest of this iteration is skipped (invalid gamma2) or the loop stopped
+  int have_prev;            // 16: r2_prev / gamma2_prev exist (damping of r2 and gamma2)
+  int stopped;              // 20: best-iterate stop (no further iteration runs)
+  int fail;                 // 24: alpha1 non-finite after the last retry (the reference raises)
+  int alpha1_retry_count;   // 28
+  int alpha2_clip_count;    // 32
+  int gamma2_invalid_count; // 36
+  int committed;            // 40: iterations committed
+  int best_iter;            // 44: best-iterate index (-1: the start state)
+  int stop_iter;            // 48
+  int pad[3];               // 52..63
+};
+static_assert(sizeof(VampCtl) == 64, "VampCtl layout");
+
 inline int launch_status(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

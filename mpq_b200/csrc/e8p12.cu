@@ -41,6 +41,13 @@ struct E8Tab {
   const float* grid;        // 65536 x 8
 };
 
+// Row split of the posterior launch (several CTAs per row when rows are few) and device-side launch control.
+struct RowSplit {
+  float* part;           // B x chunks per-chunk variance sums (chunks > 1)
+  unsigned* counters;    // B arrival counters, zero between launches (chunks > 1)
+  const int* active;     // optional: the launch does nothing while *active == 0
+};
+
 struct E8Args {
   const float* r1; int64_t ld_r1;       // B x n (n = 8 * nb)
   const float* center; int64_t ld_c;    // prior centre (W) or null
@@ -164,7 +171,7 @@ template <bool MMSE>
 __global__ void __launch_bounds__(kWarps * 32, 3)
 k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __restrict__ var_out, int64_t ld_v,
         int* __restrict__ idx_out, int64_t ld_i, float* __restrict__ map_out, int64_t ld_m,
-        float* __restrict__ var_rowsum) {
+        float* __restrict__ var_rowsum, RowSplit rs) {
   // s_off[ai]: byte k of the pair = 8 * (3 k + m_k), the offset of coordinate k's float2 entry
   __shared__ uint2 s_off[256];
   __shared__ float s_sqn[256];
@@ -174,12 +181,15 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
   __shared__ float s_ub[MMSE ? kWarps : 1][512];
   __shared__ float s_var[kWarps];
   __shared__ int s_bad;
+  if (rs.active && *rs.active == 0) return;  // device-side control: this launch is not needed
   const bool bad = stage_abs_patterns(tab, s_off, s_sqn, s_par, &s_bad);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
+  // items [k0, k1) of row b: the row is cut into gridDim.y contiguous chunks (one CTA each)
+  const int k0 = (int)((int64_t)a.nb * blockIdx.y / gridDim.y), k1 = (int)((int64_t)a.nb * (blockIdx.y + 1) / gridDim.y);
   ItemTab& T = s_tab[warp];
   float vacc = 0.f;
-  for (int k = warp; k < a.nb; k += kWarps) {
+  for (int k = k0 + warp; k < k1; k += kWarps) {
     float y[8], g, g1;
     fold_item(a, b, k, y, g, g1);
     if (bad) {  // base_abs is not an E8P12 abs table: poison the outputs
@@ -437,7 +447,21 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
     if (threadIdx.x == 0 && var_rowsum) {
       float tsum = 0.f;
       for (int w = 0; w < kWarps; ++w) tsum += s_var[w];
-      var_rowsum[b] = tsum;
+      if (gridDim.y == 1) {
+        var_rowsum[b] = tsum;
+      } else {
+        // chunk partials in a fixed order: the last chunk of the row to finish sums them (c = 0, 1, ...)
+        rs.part[(int64_t)b * gridDim.y + blockIdx.y] = tsum;
+        __threadfence();
+        const unsigned prev = atomicAdd(&rs.counters[b], 1u);
+        if (prev == gridDim.y - 1) {
+          __threadfence();
+          float t = 0.f;
+          for (unsigned c = 0; c < gridDim.y; ++c) t += __ldcg(&rs.part[(int64_t)b * gridDim.y + c]);
+          var_rowsum[b] = t;
+          rs.counters[b] = 0u;  // ready for the next launch
+        }
+      }
     }
   }
 }
@@ -646,9 +670,34 @@ MPQ_API int mpq_e8p12_mmse(const float* r1, int64_t ld_r1, const float* center, 
   MPQ_CHECK_ARG(gamma && x1_out && var_rowsum, "mpq_e8p12_mmse: gamma, x1_out and var_rowsum are required");
   E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
   E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
-  k_e8p12<true><<<B, kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, var_out, ld_v, idx_out, ld_i, map_out, ld_m,
-                                                    var_rowsum);
+  k_e8p12<true><<<dim3(B, 1), kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, var_out, ld_v, idx_out, ld_i,
+                                                                      map_out, ld_m, var_rowsum, RowSplit{});
   return launch_status("mpq_e8p12_mmse");
+}
+
+// mpq_e8p12_mmse with each row cut into `chunks` contiguous item ranges (one CTA each, so a few rows still fill the
+// GPU) and optional device-side launch control.  work: caller-owned B * (chunks + 1) 32-bit words, zeroed before the
+// first call (the chunk partials and the per-row arrival counters, which every launch leaves at zero); the row's
+// variance sum adds the chunk partials in chunk order (deterministic).  active: optional device int, the launch
+// does nothing while it is 0.
+MPQ_API int mpq_e8p12_mmse_rows(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                                int64_t ld_s, const float* gamma, float prior_tau, int B, int nb, const float* base_abs,
+                                const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,
+                                float* x1_out, int64_t ld_x, float* var_rowsum, int chunks, void* work,
+                                const int* active, void* stream) {
+  int st = e8_check(r1, B, nb, base_abs, base_sqnorm, base_parity, idx_lut, grid);
+  if (st) return st;
+  if (B == 0 || nb == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(gamma && x1_out && var_rowsum, "mpq_e8p12_mmse_rows: gamma, x1_out and var_rowsum are required");
+  MPQ_CHECK_ARG(chunks >= 1 && chunks <= nb && chunks <= 1024, "mpq_e8p12_mmse_rows: chunks must be in [1, min(nb, 1024)]");
+  MPQ_CHECK_ARG(chunks == 1 || work, "mpq_e8p12_mmse_rows: work buffer required for chunks > 1");
+  E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
+  E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
+  RowSplit rs{static_cast<float*>(work), work ? reinterpret_cast<unsigned*>(static_cast<float*>(work) + (int64_t)B * chunks)
+                                              : nullptr, active};
+  k_e8p12<true><<<dim3(B, chunks), kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, nullptr, 0, nullptr, 0,
+                                                                           nullptr, 0, var_rowsum, rs);
+  return launch_status("mpq_e8p12_mmse_rows");
 }
 
 // MAP codeword under the folded message (fixed_gamma > 0 replaces gamma for every row, e.g. 1 with no
@@ -663,8 +712,10 @@ MPQ_API int mpq_e8p12_map(const float* r1, int64_t ld_r1, const float* center, i
   MPQ_CHECK_ARG(gamma || fixed_gamma > 0.f, "mpq_e8p12_map: gamma or fixed_gamma required");
   E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, fixed_gamma, B, nb};
   E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
-  k_e8p12<false><<<B, kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, nullptr, 0, nullptr, 0, idx_out, ld_i, map_out, ld_m,
-                                                     nullptr);
+  // MAP only: no per-row reduction, so rows split freely into chunks of 64 items (enough CTAs for small row counts)
+  const int chunks = std::max(1, std::min(nb / 64, (1776 + B - 1) / B));
+  k_e8p12<false><<<dim3(B, chunks), kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, nullptr, 0, nullptr, 0, idx_out, ld_i,
+                                                                            map_out, ld_m, nullptr, RowSplit{});
   return launch_status("mpq_e8p12_map");
 }
 

@@ -383,11 +383,31 @@ __device__ __forceinline__ void tile_coords(int t, int mt, int nt, int sym, int&
   nb = t;
 }
 
+// k-block range [kb0, kb1) of split s of `splits` over total_kb k-blocks (near-equal contiguous pieces).
+__device__ __forceinline__ void split_range(int s, int splits, int total_kb, int& kb0, int& kb1) {
+  kb0 = (int)((int64_t)total_kb * s / splits);
+  kb1 = (int)((int64_t)total_kb * (s + 1) / splits);
+}
+
+// Split-K reduction in a fixed order: C = alpha * sum_{s < splits} ws[s] + beta * C  (ws: splits x M x N).
+__global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int M, int N, float alpha, float beta,
+                                float* __restrict__ C, int64_t ldc) {
+  const int64_t total = (int64_t)M * N;
+  const int64_t plane = total;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = ws[i];
+    for (int s = 1; s < splits; ++s) acc += ws[(int64_t)s * plane + i];
+    const int r = (int)(i / N), c = (int)(i % N);
+    float* cp = C + (int64_t)r * ldc + c;
+    *cp = beta != 0.f ? alpha * acc + beta * *cp : alpha * acc;
+  }
+}
+
 template <int BN, int STAGES, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc_pt(const __grid_constant__ Maps maps, int nreg, int M, int N, int K, float alpha, float beta,
                  float* __restrict__ C, int64_t ldc, int* __restrict__ status, int sym, const float* __restrict__ sa,
-                 const float* __restrict__ sb, int mt, int nt, int ntiles) {
+                 const float* __restrict__ sb, int mt, int nt, int ntiles, int splits, float* __restrict__ ws) {
   constexpr bool B16 = KIND != 0;
   constexpr uint32_t kStageA = BM * 128;
   constexpr uint32_t kStageB = BN * 128;
@@ -437,9 +457,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        int mb, nb;
-        tile_coords<BN>(t, mt, nt, sym, mb, nb);
-        for (int kb = 0; kb < total_kb; ++kb, ++g) {
+        int mb, nb, kb0, kb1;
+        tile_coords<BN>(t / splits, mt, nt, sym, mb, nb);
+        split_range(t % splits, splits, total_kb, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
           if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
@@ -474,7 +495,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t dacc = tmem + (uint32_t)(b * BN);
-        for (int kb = 0; kb < total_kb; ++kb, ++g) {
+        int kb0, kb1;
+        split_range(t % splits, splits, total_kb, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
           if (*abort_flag || !mbar_wait(&full[s], ph)) {
@@ -489,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 4; ++j) {
             const uint64_t da = smem_desc_k_sw128(a_addr + j * 32);
             const uint64_t db = smem_desc_k_sw128(b_addr + j * 32);
-            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > kb0 || j > 0) ? 1u : 0u;
             if constexpr (B16) {
               asm volatile(
                   "{\n\t.reg .pred p;\n\t"
@@ -537,13 +560,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       int mb, nb;
-      tile_coords<BN>(t, mt, nt, sym, mb, nb);
+      tile_coords<BN>(t / splits, mt, nt, sym, mb, nb);
       const int row = mb * BM + quad * 32 + lane;
+      // split-K: the unit's partial sum (row scales applied, no alpha / beta) goes to its own M x N slice of ws
+      float* dst = splits > 1 ? ws + (int64_t)(t % splits) * M * N : C;
+      const int64_t ldd = splits > 1 ? (int64_t)N : ldc;
+      const float al = splits > 1 ? 1.f : alpha, be = splits > 1 ? 0.f : beta;
       #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN + c0), v);
-        store_chunk(v, row, nb * BN, c0, M, N, alpha, beta, C, ldc, sym, sa, sb);
+        store_chunk(v, row, nb * BN, c0, M, N, al, be, dst, ldd, sym, sa, sb);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -621,7 +648,8 @@ static int num_sms() {
 // Persistent launch: one CTA per SM (the ring and two TMEM accumulators need the whole SM) over the tile list.
 template <int BN, int STAGES, int KIND>
 static int launch_pt(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
-                     int* status, cudaStream_t stream, int sym = 0, const float* sa = nullptr, const float* sb = nullptr) {
+                     int* status, cudaStream_t stream, int sym = 0, const float* sa = nullptr, const float* sb = nullptr,
+                     int splits = 1, float* ws = nullptr) {
   const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * 128 + 256;
   const int ast = smem_opt_in((const void*)k_gemm_tc_pt<BN, STAGES, KIND>, smem, "mpq_gemm_tc (persistent)");
   if (ast) return ast;
@@ -633,10 +661,17 @@ static int launch_pt(const Maps& maps, int nreg, int M, int N, int K, float alph
     ntiles = (int64_t)mt * nt;
   }
   if (ntiles == 0) return MPQ_OK;
-  const int grid = (int)std::min<int64_t>(ntiles, num_sms());
+  if (splits < 1 || !ws) splits = 1;
+  const int64_t units = ntiles * splits;
+  const int grid = (int)std::min<int64_t>(units, num_sms());
   k_gemm_tc_pt<BN, STAGES, KIND><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status,
-                                                                    sym, sa, sb, mt, nt, (int)ntiles);
-  return launch_status("mpq_gemm_tc (persistent)");
+                                                                    sym, sa, sb, mt, nt, (int)units, splits, ws);
+  int st = launch_status("mpq_gemm_tc (persistent)");
+  if (st || splits == 1) return st;
+  const int64_t total = (int64_t)M * N;
+  const int rgrid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
+  k_splitk_reduce<<<rgrid, 256, 0, stream>>>(ws, splits, M, N, alpha, beta, C, ldc);
+  return launch_status("mpq_gemm_tc (split-K reduction)");
 }
 
 }  // namespace tc
@@ -745,6 +780,44 @@ MPQ_API int mpq_gemm_f16x3(int M, int N, int K, float alpha, const void* a_hi, c
     if (st) return st;
   }
   return tc::launch_pt<256, 4, 2>(maps, 3, M, N, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 0, sa, sb);
+}
+
+// mpq_gemm_f16x3 with split-K: the 3 x round_up(K, 64) / 64 k-blocks of each 128 x 256 output tile are cut into
+// `splits` contiguous ranges processed by different CTAs, so small-M products (a 128-row VAMP block against a
+// 4096-wide basis: 16 tiles) still occupy every SM.  Each range's partial (row scales applied) is stored to its own
+// M x N slice of `ws` (caller-owned, splits * M * N floats), then C = alpha * sum_s ws[s] + beta * C is summed in a
+// fixed order (deterministic).  splits = 1 is mpq_gemm_f16x3.
+MPQ_API int mpq_gemm_f16x3_splitk(int M, int N, int K, float alpha, const void* a_hi, const void* a_lo, int64_t lda,
+                                  const float* sa, const void* b_hi, const void* b_lo, int64_t ldb, const float* sb,
+                                  float beta, float* C, int64_t ldc, int splits, float* ws, int64_t ws_floats,
+                                  int* status, void* stream) {
+  MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 1, "mpq_gemm_f16x3_splitk: bad shape");
+  MPQ_CHECK_ARG(splits >= 1 && splits <= 1024, "mpq_gemm_f16x3_splitk: splits must be in [1, 1024]");
+  if (M == 0 || N == 0) return MPQ_OK;
+  const int total_kb = 3 * ((K + 63) / 64);
+  MPQ_CHECK_ARG(splits <= total_kb, "mpq_gemm_f16x3_splitk: %d splits for %d k-blocks", splits, total_kb);
+  MPQ_CHECK_ARG(splits == 1 || (ws && ws_floats >= (int64_t)splits * M * N),
+                "mpq_gemm_f16x3_splitk: workspace of %lld floats < splits * M * N", (long long)ws_floats);
+  MPQ_CHECK_ARG(a_hi && a_lo && b_hi && b_lo && sa && sb && C && status, "mpq_gemm_f16x3_splitk: null pointer");
+  MPQ_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0 && lda >= K && ldb >= K,
+                "mpq_gemm_f16x3_splitk: lda/ldb must be multiples of 8 and >= K");
+  const void* ptrs[4] = {a_hi, a_lo, b_hi, b_lo};
+  for (int i = 0; i < 4; ++i)
+    MPQ_CHECK_ARG(((uintptr_t)ptrs[i] & 15) == 0, "mpq_gemm_f16x3_splitk: operands must be 16-byte aligned");
+  int st = tc::get_encoder();
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  const void* As[3] = {a_hi, a_hi, a_lo};
+  const void* Bs[3] = {b_hi, b_lo, b_hi};
+  for (int r = 0; r < 3; ++r) {
+    st = tc::make_map(&maps.a[r], As[r], M, K, lda, tc::BM, 2);
+    if (st) return st;
+    st = tc::make_map(&maps.b[r], Bs[r], N, K, ldb, 256, 2);
+    if (st) return st;
+  }
+  return tc::launch_pt<256, 4, 2>(maps, 3, M, N, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 0, sa, sb,
+                                  splits, splits > 1 ? ws : nullptr);
 }
 
 namespace mpq {

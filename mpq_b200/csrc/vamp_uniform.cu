@@ -42,24 +42,29 @@ struct RowState {
 };
 
 // Stage A+B of one VAMP iteration (mpq/solver.py:559-631 up to the linear module, plus the
-// gamma-only parts of linear_mmse_exact and the EM trace term).  One warp per row; the
-// rank-space sums over S run in a fixed lane-strided order.
-__global__ void k_vamp_rows(RowState st, const float* __restrict__ S, int B, int n, int n_var, int R, float obs,
-                            float damping, int final_retry) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= B) return;
-  const int b = warp;
+// gamma-only parts of linear_mmse_exact and the EM trace term).  One CTA of kRowThreads threads per row; the
+// rank-space sums over S are thread-strided and reduced in a fixed tree order.
+constexpr int kRowThreads = 128;
+
+// ctl (optional): device-side control -- the launch does nothing unless a retry round is open, obs is read from the
+// control block, and gamma2_prev is used only once an iteration has been committed.
+__global__ void __launch_bounds__(kRowThreads) k_vamp_rows(RowState st, const float* __restrict__ S, int B, int n,
+                                                          int n_var, int R, float obs, float damping, int final_retry,
+                                                          const VampCtl* __restrict__ ctl) {
+  __shared__ float red[2][kRowThreads / 32];
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (b >= B) return;
+  if (ctl) {
+    if (!ctl->active) return;
+    obs = (float)ctl->obs;
+    if (!ctl->have_prev) st.gamma2_prev = nullptr;
+  }
   const float g1w = st.gamma1_work[b];
   const float a1_raw = fmul(g1w, fdiv(st.var_rowsum[b], (float)n_var));  // gamma1 * var.mean(dim=1)
   float a1 = a1_raw;
-  if (!alpha_valid(a1_raw)) {
-    if (lane == 0) {
-      atomicAdd(&st.flags[0], 1);
-      if (!isfinite(a1_raw)) atomicAdd(&st.flags[1], 1);
-    }
-    if (final_retry) a1 = clip_alpha(a1_raw);
-  }
+  const bool a1_bad = !alpha_valid(a1_raw);
+  if (a1_bad && final_retry) a1 = clip_alpha(a1_raw);
   const float eta1 = fdiv(g1w, a1);
   const float g2n = fmaxf(nan_to_num(fsub(eta1, g1w), 1e-12f, 1e12f, 1e-12f), 1e-12f);
   float g2 = g2n;
@@ -67,7 +72,7 @@ __global__ void k_vamp_rows(RowState st, const float* __restrict__ S, int B, int
   if (damp) g2 = log_damp(st.gamma2_prev[b], g2n, (float)(1.0 - (double)damping), damping);
   // gamma-only parts of linear_mmse_exact: sum_r 1/denom and sum_r s^2/denom, denom = obs*s^2 + gamma2
   float inv_sum = 0.f, tr_sum = 0.f;
-  for (int r = lane; r < R; r += 32) {
+  for (int r = threadIdx.x; r < R; r += kRowThreads) {
     const float s = S[r];
     const float s2 = fmul(s, s);
     const float den = fadd(fmul(obs, s2), g2);
@@ -76,6 +81,18 @@ __global__ void k_vamp_rows(RowState st, const float* __restrict__ S, int B, int
   }
   inv_sum = warp_sum(inv_sum);
   tr_sum = warp_sum(tr_sum);
+  if (lane == 0) {
+    red[0][wid] = inv_sum;
+    red[1][wid] = tr_sum;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  inv_sum = 0.f;
+  tr_sum = 0.f;
+  for (int w = 0; w < kRowThreads / 32; ++w) {
+    inv_sum += red[0][w];
+    tr_sum += red[1][w];
+  }
   const float c0 = (float)(1.0 - (double)R / (double)n);
   const float a2_raw = fadd(c0, fmul(fdiv(g2, (float)n), inv_sum));
   const float a2 = clip_alpha(a2_raw);
@@ -83,20 +100,22 @@ __global__ void k_vamp_rows(RowState st, const float* __restrict__ S, int B, int
   const float g1n = fmaxf(nan_to_num(fsub(eta2, g2), 1e-12f, 1e12f, 1e-12f), 1e-12f);
   const float g1c = st.gamma1[b];
   const float g1next = damping >= 1.f ? g1n : log_damp(g1c, g1n, (float)(1.0 - (double)damping), damping);
-  if (lane == 0) {
-    st.alpha1[b] = a1;
-    st.eta1[b] = eta1;
-    st.gamma2_new[b] = g2n;
-    st.gamma2[b] = g2;
-    st.alpha2[b] = a2;
-    st.eta2[b] = eta2;
-    st.gamma1_new[b] = g1n;
-    st.gamma1_next[b] = g1next;
-    st.trace[b] = tr_sum;
-    if (!precision_valid(g2n)) atomicAdd(&st.flags[2], 1);
-    if (!precision_valid(g2)) atomicAdd(&st.flags[3], 1);
-    if (!alpha_valid(a2_raw)) atomicAdd(&st.flags[4], 1);
+  st.alpha1[b] = a1;
+  st.eta1[b] = eta1;
+  st.gamma2_new[b] = g2n;
+  st.gamma2[b] = g2;
+  st.alpha2[b] = a2;
+  st.eta2[b] = eta2;
+  st.gamma1_new[b] = g1n;
+  st.gamma1_next[b] = g1next;
+  st.trace[b] = tr_sum;
+  if (a1_bad) {
+    atomicAdd(&st.flags[0], 1);
+    if (!isfinite(a1_raw)) atomicAdd(&st.flags[1], 1);
   }
+  if (!precision_valid(g2n)) atomicAdd(&st.flags[2], 1);
+  if (!precision_valid(g2)) atomicAdd(&st.flags[3], 1);
+  if (!alpha_valid(a2_raw)) atomicAdd(&st.flags[4], 1);
 }
 
 // gamma retry (mpq/solver.py:593-596): divide/multiply the work precision of invalid rows.
@@ -114,7 +133,12 @@ __global__ void k_gamma_retry(float* gamma1_work, const float* alpha1_raw_src_va
 // r2 = damp(r2_prev, (eta1*x1 - gamma1w*r1)/gamma2_new)          (mpq/solver.py:605-612)
 __global__ void k_vamp_r2(const float* __restrict__ x1, const float* __restrict__ r1, const float* __restrict__ r2_prev,
                           float* __restrict__ r2, const float* __restrict__ eta1, const float* __restrict__ g1w,
-                          const float* __restrict__ g2n, int B, int n, int64_t ld, float damping) {
+                          const float* __restrict__ g2n, int B, int n, int64_t ld, float damping,
+                          const VampCtl* __restrict__ ctl) {
+  if (ctl) {
+    if (ctl->skip) return;
+    if (!ctl->have_prev) r2_prev = nullptr;
+  }
   const int64_t total = (int64_t)B * n;
   const float omd = (float)(1.0 - (double)damping);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -131,9 +155,14 @@ __global__ void k_vamp_r2(const float* __restrict__ x1, const float* __restrict_
 __global__ void __launch_bounds__(256) k_linear_epilogue(const float* __restrict__ P, const float* __restrict__ Y_u,
                                                          const float* __restrict__ S, const float* __restrict__ g2,
                                                          float obs, int R, int64_t ld, float* __restrict__ u,
-                                                         float* __restrict__ resid_rowsum) {
+                                                         float* __restrict__ resid_rowsum,
+                                                         const VampCtl* __restrict__ ctl) {
   __shared__ float red[32];
   const int b = blockIdx.x;
+  if (ctl) {
+    if (ctl->skip) return;
+    obs = (float)ctl->obs;
+  }
   const float gb = g2[b];
   float acc = 0.f;
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
@@ -151,14 +180,19 @@ __global__ void __launch_bounds__(256) k_linear_epilogue(const float* __restrict
 
 // r1 update from D = u @ V^T  (mpq/linear.py:51-52, mpq/solver.py:645-653):
 //   x2 = r2 + D;  r1_new = (eta2*x2 - gamma2*r2)/gamma1_new;  r1 = (1-d) r1 + d r1_new
+// ctl (optional): nothing happens on a skipped iteration; r2_keep (optional) receives a copy of r2 (the next
+// iteration's r2_prev).
 __global__ void k_vamp_r1(const float* __restrict__ D, const float* __restrict__ r2, float* __restrict__ r1,
                           const float* __restrict__ eta2, const float* __restrict__ g2, const float* __restrict__ g1n,
-                          int B, int n, int64_t ld, float damping) {
+                          int B, int n, int64_t ld, float damping, const VampCtl* __restrict__ ctl,
+                          float* __restrict__ r2_keep) {
+  if (ctl && ctl->skip) return;
   const int64_t total = (int64_t)B * n;
   const float omd = (float)(1.0 - (double)damping);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int b = (int)(i / n), j = (int)(i % n);
     const int64_t o = b * ld + j;
+    if (r2_keep) r2_keep[o] = r2[o];
     const float x2 = fadd(r2[o], D[o]);
     const float rn = fdiv(fsub(fmul(eta2[b], x2), fmul(g2[b], r2[o])), g1n[b]);
     r1[o] = damping >= 1.f ? rn : fadd(fmul(omd, r1[o]), fmul(damping, rn));
@@ -260,11 +294,27 @@ MPQ_API int mpq_vamp_rows(const float* var_rowsum, float* gamma1, float* gamma1_
   if (B == 0) return MPQ_OK;
   RowState st{var_rowsum, gamma1, gamma1_work, alpha1, eta1, gamma2_new, gamma2, gamma2_prev,
               alpha2, eta2, gamma1_new, gamma1_next, trace, flags};
-  const int threads = 256;
-  const int blocks = (B * 32 + threads - 1) / threads;
   MPQ_CHECK_ARG(n_var >= 1, "mpq_vamp_rows: n_var must be >= 1");
-  k_vamp_rows<<<blocks, threads, 0, (cudaStream_t)stream>>>(st, S, B, n, n_var, R, obs, damping, final_retry);
+  k_vamp_rows<<<B, kRowThreads, 0, (cudaStream_t)stream>>>(st, S, B, n, n_var, R, obs, damping, final_retry, nullptr);
   return launch_status("mpq_vamp_rows");
+}
+
+// mpq_vamp_rows under device-side control (ctl: VampCtl): runs only while ctl.active, obs from ctl, gamma2_prev
+// (always given) used once ctl.have_prev.
+MPQ_API int mpq_vamp_rows_ctl(const float* var_rowsum, float* gamma1, float* gamma1_work, float* alpha1, float* eta1,
+                              float* gamma2_new, float* gamma2, const float* gamma2_prev, float* alpha2, float* eta2,
+                              float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int B,
+                              int n, int n_var, int R, float damping, int final_retry, const void* ctl, void* stream) {
+  MPQ_CHECK_ARG(var_rowsum && gamma1 && gamma1_work && alpha1 && eta1 && gamma2_new && gamma2 && gamma2_prev &&
+                    alpha2 && eta2 && gamma1_new && gamma1_next && trace && flags && S && ctl,
+                "mpq_vamp_rows_ctl: null pointer");
+  MPQ_CHECK_ARG(n_var >= 1, "mpq_vamp_rows_ctl: n_var must be >= 1");
+  if (B == 0) return MPQ_OK;
+  RowState st{var_rowsum, gamma1, gamma1_work, alpha1, eta1, gamma2_new, gamma2, damping < 1.f ? gamma2_prev : nullptr,
+              alpha2, eta2, gamma1_new, gamma1_next, trace, flags};
+  k_vamp_rows<<<B, kRowThreads, 0, (cudaStream_t)stream>>>(st, S, B, n, n_var, R, 0.f, damping, final_retry,
+                                                            static_cast<const VampCtl*>(ctl));
+  return launch_status("mpq_vamp_rows_ctl");
 }
 
 MPQ_API int mpq_gamma_retry(float* gamma1_work, const float* var_rowsum, int B, int n, float factor, void* stream) {
@@ -280,16 +330,39 @@ MPQ_API int mpq_vamp_r2(const float* x1, const float* r1, const float* r2_prev, 
   MPQ_CHECK_ARG(x1 && r1 && r2 && eta1 && gamma1_work && gamma2_new, "mpq_vamp_r2: null pointer");
   if ((int64_t)B * n == 0) return MPQ_OK;
   k_vamp_r2<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(x1, r1, r2_prev, r2, eta1, gamma1_work,
-                                                                       gamma2_new, B, n, ld, damping);
+                                                                       gamma2_new, B, n, ld, damping, nullptr);
   return launch_status("mpq_vamp_r2");
+}
+
+// mpq_vamp_r2 under device-side control: nothing on a skipped iteration; r2_prev (always given) used once
+// ctl.have_prev.
+MPQ_API int mpq_vamp_r2_ctl(const float* x1, const float* r1, const float* r2_prev, float* r2, const float* eta1,
+                            const float* gamma1_work, const float* gamma2_new, int B, int n, int64_t ld, float damping,
+                            const void* ctl, void* stream) {
+  MPQ_CHECK_ARG(x1 && r1 && r2_prev && r2 && eta1 && gamma1_work && gamma2_new && ctl, "mpq_vamp_r2_ctl: null pointer");
+  if ((int64_t)B * n == 0) return MPQ_OK;
+  k_vamp_r2<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(
+      x1, r1, damping < 1.f ? r2_prev : nullptr, r2, eta1, gamma1_work, gamma2_new, B, n, ld, damping,
+      static_cast<const VampCtl*>(ctl));
+  return launch_status("mpq_vamp_r2_ctl");
 }
 
 MPQ_API int mpq_linear_epilogue(const float* P, const float* Y_u, const float* S, const float* gamma2, float obs,
                                 int B, int R, int64_t ld, float* u, float* resid_rowsum, void* stream) {
   MPQ_CHECK_ARG(P && Y_u && S && gamma2 && u && resid_rowsum, "mpq_linear_epilogue: null pointer");
   if (B == 0) return MPQ_OK;
-  k_linear_epilogue<<<B, 256, 0, (cudaStream_t)stream>>>(P, Y_u, S, gamma2, obs, R, ld, u, resid_rowsum);
+  k_linear_epilogue<<<B, 256, 0, (cudaStream_t)stream>>>(P, Y_u, S, gamma2, obs, R, ld, u, resid_rowsum, nullptr);
   return launch_status("mpq_linear_epilogue");
+}
+
+// mpq_linear_epilogue under device-side control: nothing on a skipped iteration, obs from ctl.
+MPQ_API int mpq_linear_epilogue_ctl(const float* P, const float* Y_u, const float* S, const float* gamma2, int B,
+                                    int R, int64_t ld, float* u, float* resid_rowsum, const void* ctl, void* stream) {
+  MPQ_CHECK_ARG(P && Y_u && S && gamma2 && u && resid_rowsum && ctl, "mpq_linear_epilogue_ctl: null pointer");
+  if (B == 0) return MPQ_OK;
+  k_linear_epilogue<<<B, 256, 0, (cudaStream_t)stream>>>(P, Y_u, S, gamma2, 0.f, R, ld, u, resid_rowsum,
+                                                         static_cast<const VampCtl*>(ctl));
+  return launch_status("mpq_linear_epilogue_ctl");
 }
 
 MPQ_API int mpq_vamp_r1(const float* D, const float* r2, float* r1, const float* eta2, const float* gamma2,
@@ -297,8 +370,20 @@ MPQ_API int mpq_vamp_r1(const float* D, const float* r2, float* r1, const float*
   MPQ_CHECK_ARG(D && r2 && r1 && eta2 && gamma2 && gamma1_new, "mpq_vamp_r1: null pointer");
   if ((int64_t)B * n == 0) return MPQ_OK;
   k_vamp_r1<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(D, r2, r1, eta2, gamma2, gamma1_new, B, n, ld,
-                                                                       damping);
+                                                                       damping, nullptr, nullptr);
   return launch_status("mpq_vamp_r1");
+}
+
+// mpq_vamp_r1 under device-side control: nothing on a skipped iteration; r2_keep (optional) receives r2.
+MPQ_API int mpq_vamp_r1_ctl(const float* D, const float* r2, float* r1, const float* eta2, const float* gamma2,
+                            const float* gamma1_new, int B, int n, int64_t ld, float damping, float* r2_keep,
+                            const void* ctl, void* stream) {
+  MPQ_CHECK_ARG(D && r2 && r1 && eta2 && gamma2 && gamma1_new && ctl, "mpq_vamp_r1_ctl: null pointer");
+  if ((int64_t)B * n == 0) return MPQ_OK;
+  k_vamp_r1<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(D, r2, r1, eta2, gamma2, gamma1_new, B, n, ld,
+                                                                       damping, static_cast<const VampCtl*>(ctl),
+                                                                       r2_keep);
+  return launch_status("mpq_vamp_r1_ctl");
 }
 
 MPQ_API int mpq_row_sqerr(const float* Y, const float* C, int B, int R, int64_t ldy, int64_t ldc, float* out,

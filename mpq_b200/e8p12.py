@@ -127,33 +127,49 @@ def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, blocks_per_chunk: 
             "map_vals": mvals.reshape(B, nb, 8), "alpha1": alpha1, "entropy": 0.0, "margin": 0.0}
 
 
+class GramLayer:
+    """Per-layer operands of the gram-metric CD, shared by every row block of a layer: the 8x8 block metadata
+    (grams, Cholesky factors, inverses; mpq_gram_meta) and the cross-block grams Vs Vs^T."""
+
+    def __init__(self, Vs: torch.Tensor, opVs: Optional[ops.Operand] = None, opVsT: Optional[ops.Operand] = None):
+        dev = Vs.device
+        self.Vs = Vs.to(torch.float32).contiguous()
+        n, R = self.Vs.shape
+        nb = n // 8
+        self.opVs = opVs or ops.Operand(self.Vs)
+        self.opVsT = opVsT or ops.Operand(self.Vs.t().contiguous())
+        self.meta = torch.empty(nb, 196, device=dev, dtype=torch.float32)
+        self.fails = torch.zeros(1, device=dev, dtype=torch.int32)
+        call("mpq_gram_meta", ptr(self.Vs), self.Vs.stride(0), R, nb, ptr(self.meta), ptr(self.fails))
+        self.Hf = ops.mm_nt(self.Vs, self.opVs)  # Vs Vs^T: cross-block grams
+
+
 @torch.inference_mode()
 def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, sweeps: int,
                   idxs_init: torch.Tensor, accept_tol: float = 0.0, opVs: Optional[ops.Operand] = None,
                   opVsT: Optional[ops.Operand] = None, on_sweep=None, topk_vals: Optional[torch.Tensor] = None,
-                  topk_idx: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
+                  topk_idx: Optional[torch.Tensor] = None, layer: Optional[GramLayer] = None,
+                  deferred: bool = False) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
     """Gram-metric greedy block CD over E8P12 8-blocks (mpq/polish/block_cd.py:332-625, E8P12Provider, metric
     'gram').  Returns (x, idxs int64 (B, nb), stats).  on_sweep(sweep, x, idx, res_norm, accepted_total) is
     called before the first sweep (sweep 0) and after each sweep.  With ``topk_vals`` (B, nb, k, 8) and
     ``topk_idx`` (B, nb, k) every block decision picks among the block's k candidates (E8P12TopKProvider,
-    _topk_gram_step_impl :137-172) instead of searching the full grid."""
+    _topk_gram_step_impl :137-172) instead of searching the full grid.  ``layer`` carries the per-layer
+    metadata when several row blocks of one layer are polished.  ``deferred``: no host synchronisation --
+    the stats hold device tensors (``finish_gram_stats`` converts them once the work has completed)."""
     dev = x.device
     B, n = x.shape
     nb = n // 8
     R = int(Vs.shape[1])
     t = factor_tables(cb, dev)
-    Vs = Vs.to(torch.float32).contiguous()
-    opVs = opVs or ops.Operand(Vs)
-    opVsT = opVsT or ops.Operand(Vs.t().contiguous())
+    if layer is None:
+        layer = GramLayer(Vs, opVs, opVsT)
+    Vs, opVs, opVsT, meta, fails, Hf = layer.Vs, layer.opVs, layer.opVsT, layer.meta, layer.fails, layer.Hf
     x_work = x.to(torch.float32).clone()
     idx = idxs_init.to(device=dev, dtype=torch.int32).contiguous().clone()
     res_u = ops.mm_nt(x_work, opVsT)
     res_norm = torch.empty(B, device=dev, dtype=torch.float32)
     call("mpq_residual", ptr(Y_u), ptr(res_u), B, R, res_u.stride(0), ptr(res_norm))
-    meta = torch.empty(nb, 196, device=dev, dtype=torch.float32)
-    fails = torch.zeros(1, device=dev, dtype=torch.int32)
-    call("mpq_gram_meta", ptr(Vs), Vs.stride(0), R, nb, ptr(meta), ptr(fails))
-    Hf = ops.mm_nt(Vs, opVs)  # Vs Vs^T: cross-block grams
     gain = torch.empty(nb, device=dev, dtype=torch.float32)
     order = torch.empty(nb, device=dev, dtype=torch.int32)
     VsJ = torch.empty(128, R, device=dev, dtype=torch.float32)
@@ -171,7 +187,8 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
         if tuple(topk_vals.shape) != (B, nb, n_cand, 8) or tuple(topk_idx.shape) != (B, nb, n_cand):
             raise ValueError(f"top-k candidates must be (B, nb, k, 8) / (B, nb, k); got {tuple(topk_vals.shape)}, "
                              f"{tuple(topk_idx.shape)}")
-    trace = [float(res_norm.double().mean().item())]
+    trace_dev = torch.empty(max(int(sweeps), 0) + 1, device=dev, dtype=torch.float64)
+    trace_dev[0:1].copy_(res_norm.double().mean().reshape(1))
     if on_sweep is not None:
         on_sweep(0, x_work, idx, res_norm, 0)
     for sweep in range(1, max(int(sweeps), 0) + 1):
@@ -195,15 +212,24 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
                      ptr(res_norm), ptr(idx), idx.stride(0), ptr(delta), ptr(accepted), ptr(evals), B,
                      float(accept_tol))
             ops.mm_nt(delta[:, :kc], VsJT[:, :kc], out=res_u, alpha=-1.0, beta=1.0)
-        trace.append(float(res_norm.double().mean().item()))
+        trace_dev[sweep:sweep + 1].copy_(res_norm.double().mean().reshape(1))
         if on_sweep is not None:
             on_sweep(sweep, x_work, idx, res_norm, int(accepted.item()))
-    if int(fails.item()):
+    st = {"accepted_updates": accepted, "exact_score_evals": evals, "stabilized_objective_trace": trace_dev,
+          "_fails": fails}
+    if deferred:
+        return x_work, idx.to(torch.int64), st
+    return x_work, idx.to(torch.int64), finish_gram_stats(st)
+
+
+def finish_gram_stats(st: Dict[str, Any]) -> Dict[str, Any]:
+    """Host values of a deferred gram_block_cd's stats (synchronises with the work that produced them)."""
+    if int(st["_fails"].item()):
         raise RuntimeError("stabilize_cholesky failed for an E8P12 block gram")
+    trace = [float(v) for v in st["stabilized_objective_trace"].cpu().tolist()]
     nonincreasing = all(b <= a + max(1e-8, abs(a) * 1e-7) for a, b in zip(trace, trace[1:]))
-    return x_work, idx.to(torch.int64), {"accepted_updates": float(accepted.item()), "exact_score_evals":
-                                         int(evals.item()), "stabilized_objective_trace": trace,
-                                         "stabilized_objective_nonincreasing": bool(nonincreasing)}
+    return {"accepted_updates": float(st["accepted_updates"].item()), "exact_score_evals": int(st["exact_score_evals"].item()),
+            "stabilized_objective_trace": trace, "stabilized_objective_nonincreasing": bool(nonincreasing)}
 
 
 @torch.inference_mode()

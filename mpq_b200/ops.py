@@ -170,25 +170,105 @@ class Operand:
         return self.full.shape
 
 
+def _stream_key(dev: torch.device):
+    """Scratch buffers are private to one (device, stream): work ordered on one stream never races on them, and work
+    on concurrent streams (the chained solve's polish streams) never shares them.  Inside a CUDA-graph capture the
+    scratch is private to the capture (graph-pool memory must not leak into eager calls)."""
+    s = torch.cuda.current_stream(dev)
+    if torch.cuda.is_current_stream_capturing():
+        return ("capture", id(_capture_scratch()))
+    return (dev.index, s.cuda_stream)
+
+
+_capture_local = {}
+
+
+def _capture_scratch():
+    import threading
+    d = _capture_local.get(threading.get_ident())
+    if d is None:
+        raise RuntimeError("tensor-core products inside a CUDA-graph capture need ops.graph_scratch()")
+    return d
+
+
+class graph_scratch:
+    """Context for a CUDA-graph capture: the products captured inside use scratch buffers private to this capture
+    (allocated from the graph's memory pool); keep the returned dict alive as long as the graph."""
+
+    def __enter__(self):
+        import threading
+        self.key = threading.get_ident()
+        self.prev = _capture_local.get(self.key)
+        self.d = {}
+        _capture_local[self.key] = self.d
+        return self.d
+
+    def __exit__(self, *exc):
+        if self.prev is None:
+            _capture_local.pop(self.key, None)
+        else:
+            _capture_local[self.key] = self.prev
+        return False
+
+
+def _scratch_dict(dev: torch.device):
+    if torch.cuda.is_current_stream_capturing():
+        return _capture_scratch()
+    return _scratch
+
+
 def _scratch_split(A: torch.Tensor):
-    key = (A.device.index, tuple(A.shape))
-    buf = _scratch.get(key)
+    key = ("tf32", _stream_key(A.device), tuple(A.shape))
+    sd = _scratch_dict(A.device)
+    buf = sd.get(key)
     if buf is None:
         buf = (torch.empty(A.shape, device=A.device, dtype=torch.float32),
                torch.empty(A.shape, device=A.device, dtype=torch.float32))
-        _scratch[key] = buf
+        sd[key] = buf
     return split_tf32(A, buf[0], buf[1])
 
 
 def _scratch_split16(A: torch.Tensor):
-    key = ("f16", A.device.index, tuple(A.shape))
-    buf = _scratch.get(key)
+    key = ("f16", _stream_key(A.device), tuple(A.shape))
+    sd = _scratch_dict(A.device)
+    buf = sd.get(key)
     if buf is None:
         ld = (A.shape[1] + 7) // 8 * 8
         hi = torch.empty(A.shape[0], ld, device=A.device, dtype=torch.float16)
         buf = (hi, torch.empty_like(hi), torch.empty(A.shape[0], device=A.device, dtype=torch.float32))
-        _scratch[key] = buf
+        sd[key] = buf
     return split_f16(A, buf)
+
+
+def _splitk_workspace(dev: torch.device, floats: int) -> torch.Tensor:
+    key = ("splitk", _stream_key(dev))
+    sd = _scratch_dict(dev)
+    ws = sd.get(key)
+    if ws is None or ws.numel() < floats:
+        ws = torch.empty(max(int(floats), 1), device=dev, dtype=torch.float32)
+        sd[key] = ws
+    return ws
+
+
+_NUM_SMS = {}
+
+
+def num_sms(dev: torch.device) -> int:
+    n = _NUM_SMS.get(dev.index)
+    if n is None:
+        n = torch.cuda.get_device_properties(dev).multi_processor_count
+        _NUM_SMS[dev.index] = n
+    return n
+
+
+def splitk_for(M: int, N: int, K: int, sms: int) -> int:
+    """K-splits for a 3-region fp16 product: 1 when the 128 x 256 tiles already fill half the SMs; otherwise enough
+    splits to reach about one unit per SM, with at least 8 of the 3 * ceil(K / 64) k-blocks per unit."""
+    tiles = ((M + 127) // 128) * ((N + 255) // 256)
+    total_kb = 3 * ((K + 63) // 64)
+    if tiles * 2 >= sms or total_kb < 16:
+        return 1
+    return max(1, min(sms // tiles, total_kb // 8))
 
 
 def mm_nt(A: torch.Tensor, B, out: Optional[torch.Tensor] = None, *, alpha: float = 1.0, beta: float = 0.0,
@@ -209,9 +289,16 @@ def mm_nt(A: torch.Tensor, B, out: Optional[torch.Tensor] = None, *, alpha: floa
         Ah, Al, Ai = _scratch_split16(A)
         Bh, Bl, Bi = B.f16
         st = status_word(A.device)
+        splits = splitk_for(M, N, K, num_sms(A.device)) if M and N else 1
         tok = trace.begin_timing("gemm_tc")
-        call("mpq_gemm_f16x3", M, N, K, float(alpha), ptr(Ah), ptr(Al), Ah.stride(0), ptr(Ai), ptr(Bh), ptr(Bl),
-             Bh.stride(0), ptr(Bi), float(beta), ptr(out), out.stride(0), ptr(st))
+        if splits > 1:
+            ws = _splitk_workspace(A.device, splits * M * N)
+            call("mpq_gemm_f16x3_splitk", M, N, K, float(alpha), ptr(Ah), ptr(Al), Ah.stride(0), ptr(Ai), ptr(Bh),
+                 ptr(Bl), Bh.stride(0), ptr(Bi), float(beta), ptr(out), out.stride(0), splits, ptr(ws), ws.numel(),
+                 ptr(st))
+        else:
+            call("mpq_gemm_f16x3", M, N, K, float(alpha), ptr(Ah), ptr(Al), Ah.stride(0), ptr(Ai), ptr(Bh), ptr(Bl),
+                 Bh.stride(0), ptr(Bi), float(beta), ptr(out), out.stride(0), ptr(st))
         trace.end_timing("gemm_tc", tok, 2.0 * M * N * K)
         return out
     if prec == "fp32" or not (_tma_ok(A) and _tma_ok(B.full) and (prec != "tf32x3" or B.hi is not None)):

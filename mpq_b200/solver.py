@@ -697,93 +697,162 @@ def polish_e8p12_rankspace(
     return x_out, idx_out, err_of(x_out), st
 
 
-@torch.inference_mode()
-def solve_e8p12_rankspace_vamp(
-    *,
-    Wr: torch.Tensor,
-    hatWr_init: torch.Tensor,
-    cb: object,
-    V: torch.Tensor,
-    Vh: torch.Tensor,
-    S: torch.Tensor,
-    Vs: torch.Tensor,
-    cfg: E8P12VampConfig,
-    module_name: str = "",
-    obs_precision_init: Optional[float] = None,
-    log_stats: bool = True,
-    debug_out: Optional[Dict[str, Any]] = None,
-) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Dict[str, Any]]:
-    """Scalar-precision VAMP for QUIP E8P12 in rank space with the gram-metric polish (mpq/solver.py:853-1276).
+# ------------------------------------------------------------------------------------------------
+# device-resident E8P12 VAMP loop (no host round trip inside a row block or between chained blocks)
+# ------------------------------------------------------------------------------------------------
 
-    Returns (hatWr (B, n), Qidxs int64 (B, n/8), final_err (B,), stats)."""
-    from .e8p12 import prior_scale_from_center, e8p12_map_rows
-    from .codebook import factor_tables
-    if not Wr.is_cuda:
-        raise ValueError("solve_e8p12_rankspace_vamp requires CUDA tensors (there is no CPU path)")
-    dev = Wr.device
-    Wr = _f32c(Wr, dev)
-    hat0 = _f32c(hatWr_init, dev)
-    B, n = Wr.shape
-    codesz = int(getattr(cb, "codesz", 8))
-    if codesz != 8 or n % 8 != 0:
-        raise ValueError(f"E8P12 solver expects n divisible by 8; got n={n}, codesz={codesz}.")
+# int32 view of the 64-byte control block (csrc/common.cuh VampCtl): obs is the float64 at ints 0-1
+_CTL_ACTIVE, _CTL_SKIP, _CTL_HAVE_PREV, _CTL_STOPPED, _CTL_FAIL = 2, 3, 4, 5, 6
+_CTL_RETRY, _CTL_CLIP, _CTL_INVALID, _CTL_COMMITTED, _CTL_BEST, _CTL_STOP = 7, 8, 9, 10, 11, 12
+
+
+def vamp_ctl_new(device, obs: Optional[float] = None) -> torch.Tensor:
+    """A zeroed control block (16 int32 = 64 bytes) with best/stop iteration -1 and, optionally, obs set."""
+    ctl = torch.zeros(16, device=device, dtype=torch.int32)
+    vamp_ctl_reset(ctl)
+    if obs is not None:
+        ctl.view(torch.float64)[0:1].fill_(float(obs))
+    return ctl
+
+
+def vamp_ctl_reset(ctl: torch.Tensor) -> None:
+    """Clear every field but obs (the chain's warm start for the next row block); asynchronous."""
+    ctl[2:].zero_()
+    ctl[_CTL_BEST:_CTL_STOP + 1].fill_(-1)
+
+
+def _posterior_chunks(B: int, nb: int, slots: int = 148 * 3) -> int:
+    """Item chunks per row of the posterior launch (CTA slots: 148 SMs x 3 resident CTAs).  Rows alone fill the GPU
+    from about two waves up; below that, the chunk count whose last wave is fullest (>= 32 items per chunk)."""
+    if B <= 0 or B >= 2 * slots:
+        return 1
+    best, best_eff = 1, 0.0
+    for c in range(1, max(1, nb // 32) + 1):
+        ctas = B * c
+        waves = -(-ctas // slots)
+        eff = ctas / (waves * slots) * min(1.0, ctas / (2.0 * slots))
+        if eff > best_eff + 1e-9:
+            best, best_eff = c, eff
+    return best
+
+
+class E8Layer:
+    """Operands of one E8P12 layer solve shared by all its row blocks: the factor tables, the rank-space basis with
+    its pre-split tensor-core operands, and (for the gram-metric polish) the per-layer block metadata."""
+
+    def __init__(self, *, V, Vh, S, Vs, cb, device):
+        from .codebook import factor_tables
+        self.dev = device
+        self.cb = cb
+        self.V, self.Vh, self.S, self.Vs = V, Vh, S, Vs
+        self.R = int(S.numel())
+        self.tab = factor_tables(cb, device)
+        self.opV, self.opVh = ops.Operand(V), ops.Operand(Vh)
+        self.VsT = Vs.t().contiguous()
+        self.opVs, self.opVsT = ops.Operand(Vs), ops.Operand(self.VsT)
+        self._gram = None
+
+    def gram(self):
+        from .e8p12 import GramLayer
+        if self._gram is None:
+            self._gram = GramLayer(self.Vs, self.opVs, self.opVsT)
+        return self._gram
+
+    def tab_ptrs(self):
+        t = self.tab
+        return ptr(t["base_abs"]), ptr(t["base_sqnorm"]), ptr(t["base_parity"]), ptr(t["idx_lut"]), ptr(t["grid"])
+
+
+class E8VampState:
+    """Device buffers of the VAMP loop for row blocks of B rows (reused from block to block)."""
+
+    def __init__(self, B: int, n: int, R: int, iters: int, device):
+        f32 = dict(device=device, dtype=torch.float32)
+        self.B, self.n, self.R = B, n, R
+        nb = n // 8
+        self.r1 = torch.empty(B, n, **f32)
+        self.x1 = torch.empty(B, n, **f32)
+        self.r2 = torch.empty(B, n, **f32)
+        self.r2_prev = torch.empty(B, n, **f32)
+        self.u = torch.empty(B, R, **f32)
+        self.P = torch.empty(B, R, **f32)
+        self.gamma1 = torch.empty(B, **f32)
+        self.rows = {k: torch.empty(B, **f32) for k in ("var", "g1w", "a1", "eta1", "g2n", "g2", "g2p", "a2", "eta2",
+                                                          "g1n", "g1next", "trace", "resid")}
+        self.flags = torch.zeros(8, device=device, dtype=torch.int32)
+        self.obs_hist = torch.empty(max(iters, 1), device=device, dtype=torch.float64)
+        self.chunks = _posterior_chunks(B, nb)
+        self.work = torch.zeros(B * (self.chunks + 1), device=device, dtype=torch.int32)
+
+
+def e8_vamp_device(st: E8VampState, ctl: torch.Tensor, L: E8Layer, *, Wr, hat0, center, pscale, tau: float, Y_u,
+                   cfg: "E8P12VampConfig", em_active: bool) -> None:
+    """Enqueue the VAMP iterations of one row block (mpq/solver.py:961-1122 with best_iterate off) on the current
+    stream.  ctl holds the starting observation precision and receives the final one; nothing is read back."""
+    B, n, R = st.B, st.n, st.R
     nb = n // 8
-    V, Vh, S, Vs = (_f32c(t, dev) for t in (V, Vh, S, Vs))
-    R = int(S.numel())
-    if R == 0:
-        raise ValueError("rank-0 spectra are not supported by the CUDA solver")
-    iters = max(int(cfg.iters), 0)
-    reported_iters = iters
+    rows, flags = st.rows, st.flags
     damping = float(cfg.damping)
-    tau = float(cfg.prior_tau)
-    mode_scale = str(cfg.prior_tau_scale_mode or "absmax").strip().lower()
-    tab = factor_tables(cb, dev)
+    factor = max(float(cfg.gamma_retry_factor), 1.000001)
+    retry_steps = max(int(cfg.gamma_retry_steps), 0)
+    c = ptr(ctl)
+    st.r1.copy_(hat0)
+    call("mpq_gamma_init", ptr(Wr), ptr(hat0), B, n, Wr.stride(0), float(cfg.gamma_start), ptr(st.gamma1))
+    tabs = L.tab_ptrs()
+    for it in range(max(int(cfg.iters), 0)):
+        call("mpq_vamp_ctl_begin", c, ptr(st.gamma1), ptr(rows["g1w"]), B, ptr(flags))
+        for rnd in range(retry_steps + 1):
+            final = int(rnd >= retry_steps)
+            tok = trace.begin_timing("e8p12_mmse")
+            call("mpq_e8p12_mmse_rows", ptr(st.r1), st.r1.stride(0), ptr(center), center.stride(0) if center is not None else 0,
+                 ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(rows["g1w"]), tau, B, nb, *tabs,
+                 ptr(st.x1), st.x1.stride(0), ptr(rows["var"]), st.chunks, ptr(st.work), c + 8)
+            trace.end_timing("e8p12_mmse", tok, 4.0 * B * n * (3 if center is not None else 2) + 8.0 * B
+                             + (4.0 * B * nb if pscale is not None else 0.0))
+            call("mpq_vamp_rows_ctl", ptr(rows["var"]), ptr(st.gamma1), ptr(rows["g1w"]), ptr(rows["a1"]),
+                 ptr(rows["eta1"]), ptr(rows["g2n"]), ptr(rows["g2"]), ptr(rows["g2p"]), ptr(rows["a2"]),
+                 ptr(rows["eta2"]), ptr(rows["g1n"]), ptr(rows["g1next"]), ptr(rows["trace"]), ptr(flags), ptr(L.S), B,
+                 n, nb, R, damping, final, c)
+            call("mpq_vamp_ctl_round", c, ptr(flags), ptr(rows["g1w"]), ptr(rows["var"]), B, nb, factor, final)
+        call("mpq_vamp_r2_ctl", ptr(st.x1), ptr(st.r1), ptr(st.r2_prev), ptr(st.r2), ptr(rows["eta1"]),
+             ptr(rows["g1w"]), ptr(rows["g2n"]), B, n, st.r2.stride(0), damping, c)
+        ops.mm_nt(st.r2, L.opVh, st.P)
+        call("mpq_linear_epilogue_ctl", ptr(st.P), ptr(Y_u), ptr(L.S), ptr(rows["g2"]), B, R, st.P.stride(0), ptr(st.u),
+             ptr(rows["resid"]), c)
+        ops.mm_nt(st.u, L.opV, st.x1)
+        call("mpq_vamp_r1_ctl", ptr(st.x1), ptr(st.r2), ptr(st.r1), ptr(rows["eta2"]), ptr(rows["g2"]),
+             ptr(rows["g1n"]), B, n, st.r1.stride(0), damping, ptr(st.r2_prev) if damping < 1.0 else None, c)
+        call("mpq_vamp_ctl_commit", c, ptr(st.gamma1), ptr(rows["g1next"]), ptr(rows["g2p"]), ptr(rows["g2"]),
+             ptr(rows["resid"]), ptr(rows["trace"]), B, R, int(em_active), float(cfg.em_obs_precision_damping),
+             float(cfg.em_obs_precision_min), float(cfg.em_obs_precision_max), ptr(st.obs_hist), it)
+
+
+def vamp_ctl_stats(ctl_host, obs_hist_host, iters: int) -> Dict[str, Any]:
+    """Host view of a finished loop's control block (int32 numpy array of 16) and obs history."""
+    import numpy as np
+    c = np.asarray(ctl_host, dtype=np.int32)
+    obs = float(c[:2].view(np.float64)[0])
+    hist = [float(v) for v in list(obs_hist_host)[:iters] if v == v]
+    return {"obs": obs, "obs_values": hist, "fail": int(c[_CTL_FAIL]), "alpha1_retry_count": int(c[_CTL_RETRY]),
+            "alpha2_clip_count": int(c[_CTL_CLIP]), "gamma2_invalid_count": int(c[_CTL_INVALID]),
+            "best_iter": int(c[_CTL_BEST]), "stop_iter": int(c[_CTL_STOP])}
+
+
+def _e8_host_loop(*, Wr, hat0, B, n, nb, R, iters, cfg, obs, em_active, mmse, map_state, err_of, opV, opVh, S, Y_u,
+                  tmpBR, dev):
+    """The E8P12 VAMP loop with the host deciding between launches (needed for the best-iterate test,
+    mpq/solver.py:1089-1122, which restores the best iterate and stops)."""
+    damping = float(cfg.damping)
     f32 = dict(device=dev, dtype=torch.float32)
-    W_blocks = Wr.reshape(B, nb, 8)
-    pscale = prior_scale_from_center(W_blocks, mode_scale).reshape(B, nb).contiguous() if tau > 0.0 else None
-    center = Wr if tau > 0.0 else None
-    opV, opVh = ops.Operand(V), ops.Operand(Vh)
-    VsT = Vs.t().contiguous()
-    opVs, opVsT = ops.Operand(Vs), ops.Operand(VsT)
-    Y_u = ops.mm_nt(Wr, opVsT, precision="fp32")  # computed once with FP32 FMA chains (see _UniformCtx)
-    tmpBR = torch.empty(B, R, **f32)
-
-    def err_of(x, out=None):
-        C = ops.mm_nt(x, opVsT, tmpBR)
-        out = torch.empty(B, **f32) if out is None else out
-        call("mpq_row_sqerr", ptr(Y_u), ptr(C), B, R, Y_u.stride(0), C.stride(0), ptr(out))
-        return out
-
-    if float(cfg.obs_precision) > 0.0:
-        obs_start = float(cfg.obs_precision)
-    elif obs_precision_init is not None and float(obs_precision_init) > 0.0:
-        obs_start = float(obs_precision_init)
-    else:
-        obs_start = 1.0 / max(float(ops.mean_rows(err_of(hat0)).item()) / R, 1e-12)
-    obs = float(obs_start)
-    em_active = bool(cfg.em_obs_precision) and float(cfg.obs_precision) <= 0.0
     r1 = hat0.clone()
     gamma1 = torch.empty(B, **f32)
     call("mpq_gamma_init", ptr(Wr), ptr(hat0), B, n, Wr.stride(0), float(cfg.gamma_start), ptr(gamma1))
 
-    # algorithmic bytes of one posterior launch: r1 and x1 (and the prior centre), gamma and the row sums
-    mmse_bytes = 4.0 * B * n * (3 if center is not None else 2) + 8.0 * B + (4.0 * B * nb if pscale is not None else 0.0)
-
-    def mmse(r, g, x_out, vsum):
-        tok = trace.begin_timing("e8p12_mmse")
-        call("mpq_e8p12_mmse", ptr(r), r.stride(0), ptr(center), center.stride(0) if center is not None else 0,
-             ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(g), tau, B, nb, ptr(tab["base_abs"]),
-             ptr(tab["base_sqnorm"]), ptr(tab["base_parity"]), ptr(tab["idx_lut"]), ptr(tab["grid"]), ptr(x_out),
-             x_out.stride(0), None, 0, None, 0, None, 0, ptr(vsum))
-        trace.end_timing("e8p12_mmse", tok, mmse_bytes)
-
-    def map_state(r, g):
-        return e8p12_map_rows(r, cb, gamma=g, center=center, pscale=pscale, prior_tau=tau)
-
-    best_iterate = bool(getattr(cfg, "best_iterate", False))
+    best_iterate = True
     best_err_mean = float("inf")
     best_iter_idx = -1
     stop_iter_idx = -1
+    reported_iters = iters
     best_r1 = best_g1 = None
     best_obs = obs
     if best_iterate:
@@ -862,6 +931,122 @@ def solve_e8p12_rankspace_vamp(
                 stop_iter_idx = it
                 reported_iters = it + 1
                 break
+
+    return (r1, gamma1, obs, obs_values, (alpha1_retry_count, alpha2_clip_count, gamma2_invalid_count), best_err_mean,
+            best_iter_idx, stop_iter_idx, reported_iters)
+
+
+@torch.inference_mode()
+def solve_e8p12_rankspace_vamp(
+    *,
+    Wr: torch.Tensor,
+    hatWr_init: torch.Tensor,
+    cb: object,
+    V: torch.Tensor,
+    Vh: torch.Tensor,
+    S: torch.Tensor,
+    Vs: torch.Tensor,
+    cfg: E8P12VampConfig,
+    module_name: str = "",
+    obs_precision_init: Optional[float] = None,
+    log_stats: bool = True,
+    debug_out: Optional[Dict[str, Any]] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Dict[str, Any]]:
+    """Scalar-precision VAMP for QUIP E8P12 in rank space with the gram-metric polish (mpq/solver.py:853-1276).
+
+    Returns (hatWr (B, n), Qidxs int64 (B, n/8), final_err (B,), stats)."""
+    from .e8p12 import prior_scale_from_center, e8p12_map_rows
+    from .codebook import factor_tables
+    if not Wr.is_cuda:
+        raise ValueError("solve_e8p12_rankspace_vamp requires CUDA tensors (there is no CPU path)")
+    dev = Wr.device
+    Wr = _f32c(Wr, dev)
+    hat0 = _f32c(hatWr_init, dev)
+    B, n = Wr.shape
+    codesz = int(getattr(cb, "codesz", 8))
+    if codesz != 8 or n % 8 != 0:
+        raise ValueError(f"E8P12 solver expects n divisible by 8; got n={n}, codesz={codesz}.")
+    nb = n // 8
+    V, Vh, S, Vs = (_f32c(t, dev) for t in (V, Vh, S, Vs))
+    R = int(S.numel())
+    if R == 0:
+        raise ValueError("rank-0 spectra are not supported by the CUDA solver")
+    iters = max(int(cfg.iters), 0)
+    reported_iters = iters
+    damping = float(cfg.damping)
+    tau = float(cfg.prior_tau)
+    mode_scale = str(cfg.prior_tau_scale_mode or "absmax").strip().lower()
+    tab = factor_tables(cb, dev)
+    f32 = dict(device=dev, dtype=torch.float32)
+    W_blocks = Wr.reshape(B, nb, 8)
+    pscale = prior_scale_from_center(W_blocks, mode_scale).reshape(B, nb).contiguous() if tau > 0.0 else None
+    center = Wr if tau > 0.0 else None
+    opV, opVh = ops.Operand(V), ops.Operand(Vh)
+    VsT = Vs.t().contiguous()
+    opVs, opVsT = ops.Operand(Vs), ops.Operand(VsT)
+    Y_u = ops.mm_nt(Wr, opVsT, precision="fp32")  # computed once with FP32 FMA chains (see _UniformCtx)
+    tmpBR = torch.empty(B, R, **f32)
+
+    def err_of(x, out=None):
+        C = ops.mm_nt(x, opVsT, tmpBR)
+        out = torch.empty(B, **f32) if out is None else out
+        call("mpq_row_sqerr", ptr(Y_u), ptr(C), B, R, Y_u.stride(0), C.stride(0), ptr(out))
+        return out
+
+    if float(cfg.obs_precision) > 0.0:
+        obs_start = float(cfg.obs_precision)
+    elif obs_precision_init is not None and float(obs_precision_init) > 0.0:
+        obs_start = float(obs_precision_init)
+    else:
+        obs_start = 1.0 / max(float(ops.mean_rows(err_of(hat0)).item()) / R, 1e-12)
+    # algorithmic bytes of one posterior launch: r1 and x1 (and the prior centre), gamma and the row sums
+    mmse_bytes = 4.0 * B * n * (3 if center is not None else 2) + 8.0 * B + (4.0 * B * nb if pscale is not None else 0.0)
+
+    def mmse(r, g, x_out, vsum):
+        tok = trace.begin_timing("e8p12_mmse")
+        call("mpq_e8p12_mmse", ptr(r), r.stride(0), ptr(center), center.stride(0) if center is not None else 0,
+             ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(g), tau, B, nb, ptr(tab["base_abs"]),
+             ptr(tab["base_sqnorm"]), ptr(tab["base_parity"]), ptr(tab["idx_lut"]), ptr(tab["grid"]), ptr(x_out),
+             x_out.stride(0), None, 0, None, 0, None, 0, ptr(vsum))
+        trace.end_timing("e8p12_mmse", tok, mmse_bytes)
+
+    def map_state(r, g):
+        return e8p12_map_rows(r, cb, gamma=g, center=center, pscale=pscale, prior_tau=tau)
+
+    obs = float(obs_start)
+    em_active = bool(cfg.em_obs_precision) and float(cfg.obs_precision) <= 0.0
+    best_iterate = bool(getattr(cfg, "best_iterate", False))
+    best_err_mean = float("inf")
+    best_iter_idx = -1
+    stop_iter_idx = -1
+
+    if not best_iterate:
+        # device-resident loop: one host synchronisation after the iterations instead of one per iteration
+        L = E8Layer(V=V, Vh=Vh, S=S, Vs=Vs, cb=cb, device=dev)
+        L.opVs, L.opVsT, L.VsT = opVs, opVsT, VsT
+        st_dev = E8VampState(B, n, R, iters, dev)
+        ctl = vamp_ctl_new(dev, obs)
+        e8_vamp_device(st_dev, ctl, L, Wr=Wr, hat0=hat0, center=center, pscale=pscale, tau=tau, Y_u=Y_u, cfg=cfg,
+                       em_active=em_active)
+        r1, gamma1 = st_dev.r1, st_dev.gamma1
+        cst = vamp_ctl_stats(ctl.cpu().numpy(), st_dev.obs_hist.cpu().tolist(), iters)
+        if cst["fail"]:
+            raise RuntimeError(f"alpha1 invalid: expected all in ({ALPHA_EPS}, 1-{ALPHA_EPS}).")
+        obs = cst["obs"]
+        obs_values = cst["obs_values"]
+        alpha1_retry_count = cst["alpha1_retry_count"]
+        alpha2_clip_count = cst["alpha2_clip_count"]
+        gamma2_invalid_count = cst["gamma2_invalid_count"]
+        factor = max(float(cfg.gamma_retry_factor), 1.000001)
+        retry_steps = max(int(cfg.gamma_retry_steps), 0)
+    else:
+        r1, gamma1, obs, obs_values, counts, best_err_mean, best_iter_idx, stop_iter_idx, reported_iters = \
+            _e8_host_loop(Wr=Wr, hat0=hat0, B=B, n=n, nb=nb, R=R, iters=iters, cfg=cfg, obs=obs, em_active=em_active,
+                          mmse=mmse, map_state=map_state, err_of=err_of, opV=opV, opVh=opVh, S=S, Y_u=Y_u, tmpBR=tmpBR,
+                          dev=dev)
+        alpha1_retry_count, alpha2_clip_count, gamma2_invalid_count = counts
+        factor = max(float(cfg.gamma_retry_factor), 1.000001)
+        retry_steps = max(int(cfg.gamma_retry_steps), 0)
 
     final_hat, final_idx32 = map_state(r1, gamma1)
     final_idx = final_idx32.to(torch.int64)

@@ -24,7 +24,7 @@ def launches() -> int:
 
 def begin_timing(name: str):
     """Return an event pair if `name` is being timed, else None."""
-    if _timed_names is None or name not in _timed_names:
+    if _timed_names is None or name not in _timed_names or torch.cuda.is_current_stream_capturing():
         return None
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)

@@ -149,7 +149,8 @@ def test_gemm_f32(cuda_dev, M, N, K):
     torch.testing.assert_close(C2, (C0.double() - A.double() @ Bn.double()).float(), rtol=1e-5, atol=1e-4)
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (300, 200, 196), (128, 256, 32), (1000, 4096, 4096)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (300, 200, 196), (128, 256, 32), (1000, 4096, 4096),
+                                   (128, 4096, 4096), (128, 128, 4096), (96, 200, 1000), (128, 4096, 128)])
 @pytest.mark.parametrize("prec", ["tf32x3", "f16x3", "tf32"])
 def test_gemm_tensor_core(cuda_dev, M, N, K, prec):
     """tcgen05 TF32 GEMM (3xTF32 split or single product) against an fp64 product."""
@@ -172,6 +173,58 @@ def test_gemm_tensor_core(cuda_dev, M, N, K, prec):
                      precision=prec)
     err2 = (out2.cpu().double() - (2.0 * C0.double() - 0.5 * ref)).abs().max().item()
     assert err2 <= tol * scale + 1e-5
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 4096, 4096), (512, 768, 1000)])
+def test_gemm_splitk_matches_single_pass(cuda_dev, M, N, K):
+    """The split-K form of the f16x3 product (chosen for small M) against the single-pass kernel and fp64: same
+    bound, deterministic across calls."""
+    from mpq_b200 import ops
+    from mpq_b200._lib import call, ptr
+    g = torch.Generator(device="cpu").manual_seed(M + 3 * K)
+    A = torch.randn(M, K, generator=g).to(cuda_dev)
+    Bt = torch.randn(N, K, generator=g).to(cuda_dev)
+    opB = ops.Operand(Bt, "f16x3")
+    Ah, Al, Ai = ops.split_f16(A)
+    Bh, Bl, Bi = opB.f16
+    st = ops.status_word(cuda_dev)
+    outs = []
+    for splits in (1, 5, 5, 24):
+        C = torch.full((M, N), 3.0, device=cuda_dev)
+        ws = torch.empty(splits * M * N, device=cuda_dev)
+        call("mpq_gemm_f16x3_splitk", M, N, K, -0.5, ptr(Ah), ptr(Al), Ah.stride(0), ptr(Ai), ptr(Bh), ptr(Bl),
+             Bh.stride(0), ptr(Bi), 2.0, ptr(C), C.stride(0), splits, ptr(ws), ws.numel(), ptr(st))
+        outs.append(C)
+    torch.cuda.synchronize()
+    ops.check_status(cuda_dev)
+    ref = 6.0 - 0.5 * (A.double() @ Bt.double().T)
+    scale = 0.5 * (A.double().abs() @ Bt.double().abs().T).max().item()
+    for C in outs:
+        assert (C.double() - ref).abs().max().item() <= 1e-5 * scale + 1e-5
+    assert torch.equal(outs[1], outs[2])  # fixed reduction order
+
+
+def test_gemm_f16x3_wide_dynamic_range(cuda_dev):
+    """f16x3 on rows whose entries span 2^20 (log-uniform magnitudes, as Vs rows under log-normal channel scales
+    and small eigenvalues): every entry within 1e-5 of its own |A||B|^T scale plus the split's absolute floor
+    (entries below 2^-18 of their row maximum keep an absolute error of at most 2^-38 of that maximum)."""
+    from mpq_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(5)
+    M, N, K = 256, 384, 2048
+    A = torch.randn(M, K, generator=g, dtype=torch.float64) * torch.exp2(-20.0 * torch.rand(M, K, generator=g,
+                                                                                              dtype=torch.float64))
+    Bt = torch.randn(N, K, generator=g, dtype=torch.float64) * torch.exp2(-20.0 * torch.rand(N, K, generator=g,
+                                                                                               dtype=torch.float64))
+    A32, B32 = A.float(), Bt.float()
+    out = ops.mm_nt(A32.to(cuda_dev), ops.Operand(B32.to(cuda_dev), "f16x3"), precision="f16x3").cpu().double()
+    ops.check_status(cuda_dev)
+    Ad, Bd = A32.double(), B32.double()
+    ref = Ad @ Bd.T
+    per_entry = Ad.abs() @ Bd.abs().T
+    floor = 2.0 ** -36 * (Ad.abs().amax(1, keepdim=True) * Bd.abs().sum(1)[None, :]
+                          + Ad.abs().sum(1, keepdim=True) * Bd.abs().amax(1)[None, :])
+    excess = ((out - ref).abs() - (1e-5 * per_entry + floor)).max().item()
+    assert excess <= 0.0, excess
 
 
 def _layer_fixture(m, n, seed):
