@@ -28,6 +28,8 @@ from .solver import (E8Layer, E8P12VampConfig, E8VampState, _resolve_e8p12_polis
 
 # host-side timing of the last chained solve: seconds to enqueue all blocks, and to the end of the device work
 last_timing: Dict[str, float] = {}
+# CUDA graphs for the per-block launch sequences (False: host launches, e.g. to time single kernels with events)
+use_graphs = True
 
 
 def chain_supported(cfg: E8P12VampConfig) -> bool:
@@ -62,17 +64,24 @@ class _Graphable:
         raise NotImplementedError
 
     def capture(self, stream: torch.cuda.Stream) -> None:
+        """Capture body() on `stream` (idle, dedicated) into a graph with its own memory pool; unlike
+        torch.cuda.graph this neither synchronises the device nor empties the allocator, so earlier work keeps
+        running while the host captures."""
         g = torch.cuda.CUDAGraph()
         n0 = trace.launches()
         with ops.graph_scratch() as d:
-            with torch.cuda.graph(g, stream=stream):
-                self.body()
+            with torch.cuda.stream(stream):
+                g.capture_begin()
+                try:
+                    self.body()
+                finally:
+                    g.capture_end()
         self.scratch = d
         self.nodes = trace.launches() - n0
         self.graph = g
 
-    def run(self) -> None:
-        if self.graph is None:
+    def run(self, use_graph: bool = True) -> None:
+        if self.graph is None or not use_graph:
             self.body()
         else:
             self.graph.replay()
@@ -153,16 +162,43 @@ class _PolishBlock(_Graphable):
         self.stats[2:3].copy_((self.idx != self.idx_out).sum().double().reshape(1))
 
 
+class _ChainState:
+    """Everything a chained solve of one shape keeps between calls: the static layer buffers, the control block, the
+    block's VAMP graph and the polish streams' graphs (captured once, replayed for every block of every layer)."""
+
+    def __init__(self, *, n, R, B, cb, cfg, tau, with_pscale, em_active, sweeps, polish_streams, dev):
+        self.cb = cb  # keeps the codebook (and so its factor tables' key) alive
+        self.L = E8Layer.static(n=n, R=R, cb=cb, device=dev)
+        self.gram = self.L.gram() if sweeps > 0 else None
+        self.ctl = vamp_ctl_new(dev)
+        self.vamp = _VampBlock(self.L, cb, cfg, self.ctl, B, n, tau, with_pscale, em_active)
+        self.polish = [_PolishBlock(self.L, self.gram, cb, B, n, sweeps) for _ in range(max(int(polish_streams), 1))]
+        self.cap_stream = torch.cuda.Stream(dev)
+
+    def capture(self):
+        self.vamp.capture(self.cap_stream)
+        for pb in self.polish:
+            pb.capture(pb.stream)
+
+
+_STATES: Dict[tuple, _ChainState] = {}
+_WARM: set = set()  # devices whose kernels have run once in this process (launch attributes, tables, scratch)
+
+
 @torch.inference_mode()
 def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.Tensor, Vh: torch.Tensor,
                       S: torch.Tensor, Vs: torch.Tensor, cfg: E8P12VampConfig, block_rows: int, obs_init: float,
-                      polish_streams: int = 3, graphs: bool = True
+                      polish_streams: int = 6, graphs: Optional[bool] = None
                       ) -> Tuple[torch.Tensor, torch.Tensor, List[Dict[str, Any]]]:
-    """Solve all rows of one E8P12 layer as the reference's serial chain of `block_rows`-row blocks.
+    """Solve all rows of one E8P12 layer as the reference's serial chain of `block_rows`-row blocks.  graphs=False
+    launches every kernel from the host (the same kernels and arguments as the graphs; per-launch timing works);
+    None means the module default (use_graphs).
 
     Returns (hatWr (m, n), Qidxs int64 (m, n/8), per-block stats in the keys of solve_e8p12_rankspace_vamp plus
     the adapter's mechanism sums)."""
-    from .e8p12 import finish_gram_stats, prior_scale_from_center
+    from .e8p12 import prior_scale_from_center
+    if graphs is None:
+        graphs = use_graphs
     dev = Wr.device
     m, n = Wr.shape
     nb = n // 8
@@ -175,16 +211,24 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     if polish_mode == "none":
         sweeps = 0
     em_active = bool(cfg.em_obs_precision) and float(cfg.obs_precision) <= 0.0
-    L = E8Layer(V=V, Vh=Vh, S=S, Vs=Vs, cb=cb, device=dev)
+    B = min(int(block_rows), m)
+    key = (dev.index, n, R, B, id(cb), cfg, tau > 0.0, em_active, sweeps, int(polish_streams))
+    cs = _STATES.get(key)
+    if cs is None:
+        cs = _ChainState(n=n, R=R, B=B, cb=cb, cfg=cfg, tau=tau, with_pscale=tau > 0.0, em_active=em_active,
+                         sweeps=sweeps, polish_streams=polish_streams, dev=dev)
+        _STATES[key] = cs
+    L, ctl = cs.L, cs.ctl
+    L.load(V=V, Vh=Vh, S=S, Vs=Vs)
     pscale_all = (prior_scale_from_center(Wr.reshape(m, nb, 8), mode_scale).reshape(m, nb).contiguous()
                   if tau > 0.0 else None)
     Y_u_all = ops.mm_nt(Wr, L.opVsT, precision="fp32")  # FP32 FMA chains, all rows at once (rows are independent)
-    gram = L.gram() if sweeps > 0 else None
     obs0 = float(cfg.obs_precision) if float(cfg.obs_precision) > 0.0 else float(obs_init)
-    ctl = vamp_ctl_new(dev, obs0)
+    vamp_ctl_reset(ctl)
+    ctl.view(torch.float64)[0:1].fill_(obs0)
     final_hat = torch.empty_like(Wr)
     final_idx = torch.empty(m, nb, device=dev, dtype=torch.int64)
-    starts = list(range(0, m, block_rows))
+    starts = list(range(0, m, B))
     nblk = len(starts)
     # per-block statistics, read back once at the end
     b_ctl = torch.zeros(nblk, 16, device=dev, dtype=torch.int32)
@@ -195,31 +239,24 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     b_trace = torch.zeros(nblk, sweeps + 1, device=dev, dtype=torch.float64)
     main = torch.cuda.current_stream(dev)
     t_start = time.perf_counter()
-    vamp: Dict[int, _VampBlock] = {}
-    polish: Dict[int, List[_PolishBlock]] = {}
-
-    def vamp_for(B):
-        if B not in vamp:
-            vamp[B] = _VampBlock(L, cb, cfg, ctl, B, n, tau, pscale_all is not None, em_active)
-        return vamp[B]
-
-    def polish_for(B, bi):
-        if B not in polish:
-            polish[B] = [_PolishBlock(L, gram, cb, B, n, sweeps) for _ in range(max(int(polish_streams), 1))]
-        return polish[B][bi % len(polish[B])]
-
+    if graphs and cs.vamp.graph is None and dev.index in _WARM:
+        cs.capture()
+    tail = None  # a last block with fewer rows runs eagerly with its own buffers
     for bi, r0 in enumerate(starts):
-        r1 = min(r0 + block_rows, m)
+        r1 = min(r0 + B, m)
         Bb = r1 - r0
         rb = slice(r0, r1)
-        vb = vamp_for(Bb)
-        pb = polish_for(Bb, bi)
-        if graphs and bi > 0 and Bb == block_rows and vb.graph is None:
-            # the first block ran eagerly (kernel attributes, tables, scratch set up); capture the block's VAMP graph
-            # and every polish stream's graph once (each capture begins with a device synchronisation)
-            vb.capture(torch.cuda.Stream(dev))
-            for q in polish[Bb]:
-                q.capture(q.stream)
+        if Bb == B:
+            vb, pb = cs.vamp, cs.polish[bi % len(cs.polish)]
+        else:
+            if tail is None:
+                tail = (_VampBlock(L, cb, cfg, ctl, Bb, n, tau, pscale_all is not None, em_active),
+                        _PolishBlock(L, cs.gram, cb, Bb, n, sweeps))
+            vb, pb = tail
+        if graphs and bi > 0 and Bb == B and cs.vamp.graph is None:
+            # first use in this process: block 0 ran eagerly (kernel attributes, tables, scratch set up)
+            _WARM.add(dev.index)
+            cs.capture()
         if bi > 0:
             vamp_ctl_reset(ctl)
             if float(cfg.obs_precision) > 0.0:
@@ -229,7 +266,7 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
         vb.Y.copy_(Y_u_all[rb])
         if vb.pscale is not None:
             vb.pscale.copy_(pscale_all[rb])
-        vb.run()
+        vb.run(graphs)
         final_hat[rb].copy_(vb.vals)
         final_idx[rb].copy_(vb.idx)
         b_ctl[bi].copy_(ctl)
@@ -243,14 +280,15 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
             pb.x.copy_(final_hat[rb])
             pb.idx.copy_(final_idx[rb])
             pb.Y.copy_(Y_u_all[rb])
-            pb.run()
+            pb.run(graphs)
             final_hat[rb].copy_(pb.x_out)
             final_idx[rb].copy_(pb.idx_out)
             b_pol[bi].copy_(pb.stats)
             b_trace[bi].copy_(pb.trace)
-    for plist in polish.values():
-        for pb in plist:
-            main.wait_stream(pb.stream)
+    for pb in cs.polish + ([tail[1]] if tail is not None else []):
+        main.wait_stream(pb.stream)
+    if not graphs or cs.vamp.graph is None:
+        _WARM.add(dev.index)
     t_enq = time.perf_counter()
     ops.check_status(dev)  # synchronises: every block has finished
     last_timing.update(enqueue_s=t_enq - t_start, total_s=time.perf_counter() - t_start, blocks=float(nblk))
@@ -258,7 +296,7 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     g_h, pol_h, trace_h = b_g.cpu().tolist(), b_pol.cpu().tolist(), b_trace.cpu().tolist()
     out: List[Dict[str, Any]] = []
     for bi, r0 in enumerate(starts):
-        rows = min(r0 + block_rows, m) - r0
+        rows = min(r0 + B, m) - r0
         cst = vamp_ctl_stats(ctl_h[bi], hist_h[bi], iters)
         if cst["fail"]:
             raise RuntimeError(f"alpha1 invalid: expected all in ({ALPHA_EPS}, 1-{ALPHA_EPS}).")

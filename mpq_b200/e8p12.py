@@ -140,8 +140,15 @@ class GramLayer:
         self.opVsT = opVsT or ops.Operand(self.Vs.t().contiguous())
         self.meta = torch.empty(nb, 196, device=dev, dtype=torch.float32)
         self.fails = torch.zeros(1, device=dev, dtype=torch.int32)
-        call("mpq_gram_meta", ptr(self.Vs), self.Vs.stride(0), R, nb, ptr(self.meta), ptr(self.fails))
-        self.Hf = ops.mm_nt(self.Vs, self.opVs)  # Vs Vs^T: cross-block grams
+        self.Hf = torch.empty(n, n, device=dev, dtype=torch.float32)
+        self.refresh()
+
+    def refresh(self) -> None:
+        """Recompute the metadata in place from self.Vs (after its values changed)."""
+        n, R = self.Vs.shape
+        self.fails.zero_()
+        call("mpq_gram_meta", ptr(self.Vs), self.Vs.stride(0), R, n // 8, ptr(self.meta), ptr(self.fails))
+        ops.mm_nt(self.Vs, self.opVs, self.Hf)  # Vs Vs^T: cross-block grams
 
 
 @torch.inference_mode()

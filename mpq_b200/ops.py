@@ -165,6 +165,15 @@ class Operand:
         elif self.precision == "f16x3" and t.dim() == 2 and t.dtype == torch.float32:
             self.f16 = split_f16(t)
 
+    def reload(self, t: torch.Tensor) -> None:
+        """Copy new values (same shape) into this operand's buffers and re-split them in place: products captured in a
+        CUDA graph against this operand see the new matrix."""
+        self.full.copy_(t)
+        if self.hi is not None:
+            split_tf32(self.full, self.hi, self.lo)
+        if self.f16 is not None:
+            split_f16(self.full, self.f16)
+
     @property
     def shape(self):
         return self.full.shape

@@ -92,3 +92,14 @@ def test_scalar_layer_matches_reference(golden_dir, case):
     ref_loss = L.proxy_loss(out["W_work"], ref_q, out["H_metric"])
     my_loss = L.proxy_loss(out["W_work"], out["Q_work"], out["H_metric"])
     assert abs(my_loss - ref_loss) <= 0.005 * ref_loss
+
+
+def test_layer4096_fixture_records_the_references_own_polish_sensitivity(golden_dir):
+    """The reference's gram-metric polish at 128-row blocks, started from its own VAMP-stage codes with two of the
+    block's 65,536 codes changed, disagrees with its unperturbed result on a large share of codes: the greedy block
+    order is shared by the block's rows, so one changed row reorders near-tied blocks for every row.  This is why
+    the full-solve codes are compared stage by stage (tests/test_gpu_layer4096.py)."""
+    z = np.load(golden_dir / "layer4096.npz")
+    sens = json.loads(str(z["e8/meta"]))["polish_sensitivity"]
+    assert sens["changed_inputs"] == 2 and sens["matches_chain"] == 1.0
+    assert sens["agreement"] < 0.95 and sens["rows_equal"] < 128
