@@ -153,6 +153,19 @@ int mpq_vamp_r1_ctl(const float* D, const float* r2, float* r1, const float* eta
                     const float* gamma1_new, int B, int n, int64_t ld, float damping, float* r2_keep, const void* ctl,
                     void* stream);
 
+/* Fused forms of the loop above (same arithmetic): the rank-space products come as split-K partial planes that the
+ * consumer adds in plane order (mpq_gemm_f16x3_parts), and the producers of a product's A operand write it in the
+ * row-scaled fp16 split of mpq_split_f16 (mpq/solver.py:605-653, mpq/linear.py:46-55). */
+int mpq_vamp_r2_split_ctl(const float* x1, const float* r1, const float* r2_prev, float* r2, const float* eta1,
+                          const float* gamma1_work, const float* gamma2_new, int B, int n, int64_t ld, float damping,
+                          void* hi, void* lo, int64_t ldo, float* inv_scale, const void* ctl, void* stream);
+int mpq_linear_epilogue_parts_ctl(const float* parts, int splits, const float* Y_u, int64_t ldy, const float* S,
+                                  const float* gamma2, int B, int R, float* u, void* hi, void* lo, int64_t ldo,
+                                  float* inv_scale, float* resid_rowsum, const void* ctl, void* stream);
+int mpq_vamp_r1_parts_ctl(const float* parts, int splits, const float* r2, float* r1, const float* eta2,
+                          const float* gamma2, const float* gamma1_new, int B, int n, int64_t ld, float damping,
+                          float* r2_keep, const void* ctl, void* stream);
+
 /* ---- dense products (K7/K8, scalar-CD block updates) ----
  * C = alpha A op(B) + beta C with A: M x K row-major; layout 0: B is N x K ("NT"), layout 1: B is K x N ("NN").
  * Replaces the torch matmuls of mpq/linear.py:48,51,94, mpq/solver.py:485 and
@@ -205,6 +218,11 @@ int mpq_gemm_f16x3(int M, int N, int K, float alpha, const void* a_hi, const voi
  * at the block sizes of mpq/adapters/quip_sharp.py:28): the k-blocks of each output tile are cut into `splits`
  * ranges run by different CTAs; their partials go to ws (caller-owned, splits * M * N floats) and are summed in a
  * fixed order (deterministic).  1 <= splits <= 3 * ceil(K / 64). */
+/* The partial products of mpq_gemm_f16x3_splitk without the reduction: plane s of ws (M x N, leading dimension N)
+ * holds the s-th k-range's sum (row scales applied); consumers add planes 0, 1, ... in order. */
+int mpq_gemm_f16x3_parts(int M, int N, int K, const void* a_hi, const void* a_lo, int64_t lda, const float* sa,
+                         const void* b_hi, const void* b_lo, int64_t ldb, const float* sb, int splits, float* ws,
+                         int64_t ws_floats, int* status, void* stream);
 int mpq_gemm_f16x3_splitk(int M, int N, int K, float alpha, const void* a_hi, const void* a_lo, int64_t lda,
                           const float* sa, const void* b_hi, const void* b_lo, int64_t ldb, const float* sb, float beta,
                           float* C, int64_t ldc, int splits, float* ws, int64_t ws_floats, int* status, void* stream);

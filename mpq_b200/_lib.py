@@ -83,6 +83,10 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_vamp_r2_ctl": (P, P, P, P, P, P, P, I, I, L, F, P, P),
     "mpq_linear_epilogue_ctl": (P, P, P, P, I, I, L, P, P, P, P),
     "mpq_vamp_r1_ctl": (P, P, P, P, P, P, I, I, L, F, P, P, P),
+    "mpq_vamp_r2_split_ctl": (P, P, P, P, P, P, P, I, I, L, F, P, P, L, P, P, P),
+    "mpq_linear_epilogue_parts_ctl": (P, I, P, L, P, P, I, I, P, P, P, L, P, P, P, P),
+    "mpq_vamp_r1_parts_ctl": (P, I, P, P, P, P, P, I, I, L, F, P, P, P),
+    "mpq_gemm_f16x3_parts": (I, I, I, P, P, L, P, P, P, L, P, I, P, L, P, P),
     "mpq_gram_chunk_topk": (P, L, P, L, P, P, P, I, I, P, P, I, I, P, P, L, P, P, P, I, F, P),
 }
 

@@ -1,5 +1,6 @@
 // Shared helpers for the MPQ B200 kernels (sm_100a).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <math.h>
@@ -94,6 +95,41 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
   }
   return t;  // valid in warp 0
+}
+
+// Row-scaled fp16 split (the FP32-faithful operand format of the fp16 tensor-core products): for a row whose largest
+// magnitude is mx (< 2^e), s = 2^(15 - e) and inv = 2^(e - 15); every element x of the row is stored as
+// hi = fp16_rn(x s), lo = fp16_rn(x s - hi)  (x s and x s - hi are exact in fp32).
+__device__ __forceinline__ void split_f16_scale(float mx, float& s, float& inv) {
+  int e = 0;
+  if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx < 2^e
+  s = ldexpf(1.f, 15 - e);
+  inv = ldexpf(1.f, e - 15);
+}
+
+__device__ __forceinline__ void split_f16_store(float x, float s, unsigned short* hi, unsigned short* lo) {
+  const float y = x * s;
+  const __half h = __float2half_rn(y);
+  *reinterpret_cast<__half*>(hi) = h;
+  *reinterpret_cast<__half*>(lo) = __float2half_rn(y - __half2float(h));
+}
+
+// Deterministic block-wide maximum (valid in warp 0); `red` must hold blockDim.x/32 floats.
+__device__ __forceinline__ float block_max(float v, float* red) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = 0.f;
+  if (wid == 0) {
+    t = lane < nw ? red[lane] : 0.f;
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+  }
+  return t;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

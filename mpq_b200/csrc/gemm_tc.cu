@@ -649,7 +649,7 @@ static int num_sms() {
 template <int BN, int STAGES, int KIND>
 static int launch_pt(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
                      int* status, cudaStream_t stream, int sym = 0, const float* sa = nullptr, const float* sb = nullptr,
-                     int splits = 1, float* ws = nullptr) {
+                     int splits = 1, float* ws = nullptr, bool reduce = true) {
   const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * 128 + 256;
   const int ast = smem_opt_in((const void*)k_gemm_tc_pt<BN, STAGES, KIND>, smem, "mpq_gemm_tc (persistent)");
   if (ast) return ast;
@@ -667,7 +667,7 @@ static int launch_pt(const Maps& maps, int nreg, int M, int N, int K, float alph
   k_gemm_tc_pt<BN, STAGES, KIND><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status,
                                                                     sym, sa, sb, mt, nt, (int)units, splits, ws);
   int st = launch_status("mpq_gemm_tc (persistent)");
-  if (st || splits == 1) return st;
+  if (st || splits == 1 || !reduce) return st;
   const int64_t total = (int64_t)M * N;
   const int rgrid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
   k_splitk_reduce<<<rgrid, 256, 0, stream>>>(ws, splits, M, N, alpha, beta, C, ldc);
@@ -820,6 +820,41 @@ MPQ_API int mpq_gemm_f16x3_splitk(int M, int N, int K, float alpha, const void* 
                                   splits, splits > 1 ? ws : nullptr);
 }
 
+// The split-K partial products of mpq_gemm_f16x3_splitk without the reduction: plane s (M x N, leading dimension N) of
+// ws holds the sum over the s-th k-range (row scales applied); a consumer adds the planes in order 0, 1, ...
+// (which reproduces the reduction's result bit for bit).  splits = 1 writes the whole product to plane 0.
+MPQ_API int mpq_gemm_f16x3_parts(int M, int N, int K, const void* a_hi, const void* a_lo, int64_t lda, const float* sa,
+                                 const void* b_hi, const void* b_lo, int64_t ldb, const float* sb, int splits,
+                                 float* ws, int64_t ws_floats, int* status, void* stream) {
+  MPQ_CHECK_ARG(M >= 0 && N >= 0 && K >= 1, "mpq_gemm_f16x3_parts: bad shape");
+  MPQ_CHECK_ARG(splits >= 1 && splits <= 1024, "mpq_gemm_f16x3_parts: splits must be in [1, 1024]");
+  if (M == 0 || N == 0) return MPQ_OK;
+  const int total_kb = 3 * ((K + 63) / 64);
+  MPQ_CHECK_ARG(splits <= total_kb, "mpq_gemm_f16x3_parts: %d splits for %d k-blocks", splits, total_kb);
+  MPQ_CHECK_ARG(ws && ws_floats >= (int64_t)splits * M * N, "mpq_gemm_f16x3_parts: workspace of %lld floats < splits * M * N",
+                (long long)ws_floats);
+  MPQ_CHECK_ARG(a_hi && a_lo && b_hi && b_lo && sa && sb && status, "mpq_gemm_f16x3_parts: null pointer");
+  MPQ_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0 && lda >= K && ldb >= K,
+                "mpq_gemm_f16x3_parts: lda/ldb must be multiples of 8 and >= K");
+  const void* ptrs[4] = {a_hi, a_lo, b_hi, b_lo};
+  for (int i = 0; i < 4; ++i)
+    MPQ_CHECK_ARG(((uintptr_t)ptrs[i] & 15) == 0, "mpq_gemm_f16x3_parts: operands must be 16-byte aligned");
+  int st = tc::get_encoder();
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  const void* As[3] = {a_hi, a_hi, a_lo};
+  const void* Bs[3] = {b_hi, b_lo, b_hi};
+  for (int r = 0; r < 3; ++r) {
+    st = tc::make_map(&maps.a[r], As[r], M, K, lda, tc::BM, 2);
+    if (st) return st;
+    st = tc::make_map(&maps.b[r], Bs[r], N, K, ldb, 256, 2);
+    if (st) return st;
+  }
+  return tc::launch_pt<256, 4, 2>(maps, 3, M, N, K, 1.f, 0.f, ws, N, status, (cudaStream_t)stream, 0, sa, sb, splits,
+                                  splits > 1 ? ws : nullptr, false);
+}
+
 namespace mpq {
 // Row-scaled fp16 split, one warp per row: s = 2^(15 - E) with max|x_row| < 2^E, y = x s (exact),
 // hi = fp16_rn(y), lo = fp16_rn(y - hi) (y - hi exact in fp32); inv_scale[row] = 1 / s.
@@ -832,15 +867,11 @@ __global__ void k_split_f16(const float* __restrict__ x, int64_t ldx, int rows, 
   for (int c = lane; c < cols; c += 32) mx = fmaxf(mx, fabsf(xr[c]));
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  int e = 0;
-  if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx < 2^e
-  const float s = ldexpf(1.f, 15 - e), inv = ldexpf(1.f, e - 15);
-  for (int c = lane; c < cols; c += 32) {
-    const float y = xr[c] * s;
-    const __half h = __float2half_rn(y);
-    hi[(int64_t)warp * ldo + c] = h;
-    lo[(int64_t)warp * ldo + c] = __float2half_rn(y - __half2float(h));
-  }
+  float s, inv;
+  split_f16_scale(mx, s, inv);
+  for (int c = lane; c < cols; c += 32)
+    split_f16_store(xr[c], s, reinterpret_cast<unsigned short*>(hi + (int64_t)warp * ldo + c),
+                    reinterpret_cast<unsigned short*>(lo + (int64_t)warp * ldo + c));
   if (lane == 0) inv_scale[warp] = inv;
 }
 }  // namespace mpq

@@ -199,6 +199,114 @@ __global__ void k_vamp_r1(const float* __restrict__ D, const float* __restrict__
   }
 }
 
+// ---- fused forms for the device-resident loop: the products' split-K partial planes are added by the consumer (in
+// plane order, as the split-K reduction does), and the producers of the next product's A operand write it already
+// split (row-scaled fp16 halves, as mpq_split_f16) ----
+
+__device__ __forceinline__ float sum_parts(const float* __restrict__ parts, int splits, int64_t plane, int64_t o) {
+  float acc = parts[o];
+  for (int s = 1; s < splits; ++s) acc += parts[(int64_t)s * plane + o];
+  return acc;
+}
+
+// r2 (as k_vamp_r2) plus its row-scaled fp16 split; one CTA per row: pass 1 writes r2 and finds the row maximum,
+// pass 2 re-reads the row (this thread's own writes) and stores the halves.
+__global__ void __launch_bounds__(256) k_vamp_r2_split(const float* __restrict__ x1, const float* __restrict__ r1,
+                                                       const float* __restrict__ r2_prev, float* __restrict__ r2,
+                                                       const float* __restrict__ eta1, const float* __restrict__ g1w,
+                                                       const float* __restrict__ g2n, int n, int64_t ld, float damping,
+                                                       unsigned short* __restrict__ hi, unsigned short* __restrict__ lo,
+                                                       int64_t ldo, float* __restrict__ inv_scale,
+                                                       const VampCtl* __restrict__ ctl) {
+  __shared__ float red[32];
+  if (ctl) {
+    if (ctl->skip) return;
+    if (!ctl->have_prev) r2_prev = nullptr;
+  }
+  const int b = blockIdx.x;
+  const float omd = (float)(1.0 - (double)damping);
+  const float e1 = eta1[b], gw = g1w[b], gn = g2n[b];
+  float mx = 0.f;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const int64_t o = b * ld + j;
+    const float rn = fdiv(fsub(fmul(e1, x1[o]), fmul(gw, r1[o])), gn);
+    const float v = r2_prev ? fadd(fmul(omd, r2_prev[o]), fmul(damping, rn)) : rn;
+    r2[o] = v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  __shared__ float s_scale[2];
+  const float m = block_max(mx, red);
+  if (threadIdx.x == 0) {
+    split_f16_scale(m, s_scale[0], s_scale[1]);
+    inv_scale[b] = s_scale[1];
+  }
+  __syncthreads();
+  const float sc = s_scale[0];
+  for (int j = threadIdx.x; j < n; j += blockDim.x)
+    split_f16_store(r2[b * ld + j], sc, hi + b * ldo + j, lo + b * ldo + j);
+}
+
+// Linear-module epilogue (as k_linear_epilogue) over P given as split-K partial planes, with u written as its
+// row-scaled fp16 split (u itself goes to `u` as scratch for the second pass).
+__global__ void __launch_bounds__(256) k_linear_epilogue_parts(const float* __restrict__ parts, int splits,
+                                                               int64_t plane, const float* __restrict__ Y_u,
+                                                               int64_t ldy, const float* __restrict__ S,
+                                                               const float* __restrict__ g2, int R,
+                                                               float* __restrict__ u, unsigned short* __restrict__ hi,
+                                                               unsigned short* __restrict__ lo, int64_t ldo,
+                                                               float* __restrict__ inv_scale,
+                                                               float* __restrict__ resid_rowsum,
+                                                               const VampCtl* __restrict__ ctl) {
+  __shared__ float red[32];
+  if (ctl && ctl->skip) return;
+  const float obs = (float)ctl->obs;
+  const int b = blockIdx.x;
+  const float gb = g2[b];
+  float acc = 0.f, mx = 0.f;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const float s = S[r];
+    const float den = fadd(fmul(obs, fmul(s, s)), gb);
+    const float P = sum_parts(parts, splits, plane, (int64_t)b * R + r);
+    const float rb = fsub(Y_u[b * ldy + r], fmul(P, s));
+    const float coeff = fdiv(fmul(obs, s), den);
+    const float uv = fmul(rb, coeff);
+    u[(int64_t)b * R + r] = uv;
+    mx = fmaxf(mx, fabsf(uv));
+    const float ra = fmul(rb, fdiv(gb, den));
+    acc += ra * ra;
+  }
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) resid_rowsum[b] = t;
+  __shared__ float s_scale[2];
+  const float m = block_max(mx, red);
+  if (threadIdx.x == 0) {
+    split_f16_scale(m, s_scale[0], s_scale[1]);
+    inv_scale[b] = s_scale[1];
+  }
+  __syncthreads();
+  const float sc = s_scale[0];
+  for (int r = threadIdx.x; r < R; r += blockDim.x)
+    split_f16_store(u[(int64_t)b * R + r], sc, hi + b * ldo + r, lo + b * ldo + r);
+}
+
+// r1 update (as k_vamp_r1) with D given as split-K partial planes (B x n each).
+__global__ void k_vamp_r1_parts(const float* __restrict__ parts, int splits, int64_t plane,
+                                const float* __restrict__ r2, float* __restrict__ r1, const float* __restrict__ eta2,
+                                const float* __restrict__ g2, const float* __restrict__ g1n, int B, int n, int64_t ld,
+                                float damping, const VampCtl* __restrict__ ctl, float* __restrict__ r2_keep) {
+  if (ctl && ctl->skip) return;
+  const int64_t total = (int64_t)B * n;
+  const float omd = (float)(1.0 - (double)damping);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i / n), j = (int)(i % n);
+    const int64_t o = b * ld + j;
+    if (r2_keep) r2_keep[o] = r2[o];
+    const float x2 = fadd(r2[o], sum_parts(parts, splits, plane, (int64_t)b * n + j));
+    const float rn = fdiv(fsub(fmul(eta2[b], x2), fmul(g2[b], r2[o])), g1n[b]);
+    r1[o] = damping >= 1.f ? rn : fadd(fmul(omd, r1[o]), fmul(damping, rn));
+  }
+}
+
 // rowsum((Y - C)^2) (vamp_rankspace_error), optionally rowsum((Y - C)^2) + add[b]; one CTA per row.
 __global__ void __launch_bounds__(256) k_row_sqerr(const float* __restrict__ Y, const float* __restrict__ C, int R,
                                                    int64_t ldy, int64_t ldc, float* __restrict__ out) {
@@ -462,4 +570,52 @@ MPQ_API int mpq_sub(const float* A, const float* C, float* D, int B, int n, int6
   if ((int64_t)B * n == 0) return MPQ_OK;
   k_sub<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(A, C, D, B, n, ld);
   return launch_status("mpq_sub");
+}
+
+// ---- entry points of the fused forms (device-resident loop) ----
+
+// r2 = damp(r2_prev, (eta1 x1 - gamma1w r1) / gamma2_new) and its row-scaled fp16 split (hi, lo: B x ldo halves,
+// inv_scale: B) under device control: nothing on a skipped iteration, r2_prev used once ctl.have_prev.
+MPQ_API int mpq_vamp_r2_split_ctl(const float* x1, const float* r1, const float* r2_prev, float* r2, const float* eta1,
+                                  const float* gamma1_work, const float* gamma2_new, int B, int n, int64_t ld,
+                                  float damping, void* hi, void* lo, int64_t ldo, float* inv_scale, const void* ctl,
+                                  void* stream) {
+  MPQ_CHECK_ARG(x1 && r1 && r2_prev && r2 && eta1 && gamma1_work && gamma2_new && hi && lo && inv_scale && ctl,
+                "mpq_vamp_r2_split_ctl: null pointer");
+  MPQ_CHECK_ARG(ldo >= n && ld >= n, "mpq_vamp_r2_split_ctl: bad leading dimension");
+  if ((int64_t)B * n == 0) return MPQ_OK;
+  k_vamp_r2_split<<<B, 256, 0, (cudaStream_t)stream>>>(x1, r1, damping < 1.f ? r2_prev : nullptr, r2, eta1,
+                                                       gamma1_work, gamma2_new, n, ld, damping,
+                                                       static_cast<unsigned short*>(hi), static_cast<unsigned short*>(lo),
+                                                       ldo, inv_scale, static_cast<const VampCtl*>(ctl));
+  return launch_status("mpq_vamp_r2_split_ctl");
+}
+
+// Linear-module epilogue over P = sum of `splits` partial planes (B x R each, plane stride B R) with u written split
+// (u: B x R fp32 scratch; hi, lo: B x ldo halves; inv_scale: B) and rowsum(residual_after^2), under device control.
+MPQ_API int mpq_linear_epilogue_parts_ctl(const float* parts, int splits, const float* Y_u, int64_t ldy, const float* S,
+                                          const float* gamma2, int B, int R, float* u, void* hi, void* lo, int64_t ldo,
+                                          float* inv_scale, float* resid_rowsum, const void* ctl, void* stream) {
+  MPQ_CHECK_ARG(parts && Y_u && S && gamma2 && u && hi && lo && inv_scale && resid_rowsum && ctl,
+                "mpq_linear_epilogue_parts_ctl: null pointer");
+  MPQ_CHECK_ARG(splits >= 1 && ldo >= R && ldy >= R, "mpq_linear_epilogue_parts_ctl: bad argument");
+  if (B == 0) return MPQ_OK;
+  k_linear_epilogue_parts<<<B, 256, 0, (cudaStream_t)stream>>>(parts, splits, (int64_t)B * R, Y_u, ldy, S, gamma2, R, u,
+                                                               static_cast<unsigned short*>(hi),
+                                                               static_cast<unsigned short*>(lo), ldo, inv_scale,
+                                                               resid_rowsum, static_cast<const VampCtl*>(ctl));
+  return launch_status("mpq_linear_epilogue_parts_ctl");
+}
+
+// r1 update with D = sum of `splits` partial planes (B x n each, plane stride B n), under device control.
+MPQ_API int mpq_vamp_r1_parts_ctl(const float* parts, int splits, const float* r2, float* r1, const float* eta2,
+                                  const float* gamma2, const float* gamma1_new, int B, int n, int64_t ld, float damping,
+                                  float* r2_keep, const void* ctl, void* stream) {
+  MPQ_CHECK_ARG(parts && r2 && r1 && eta2 && gamma2 && gamma1_new && ctl, "mpq_vamp_r1_parts_ctl: null pointer");
+  MPQ_CHECK_ARG(splits >= 1, "mpq_vamp_r1_parts_ctl: splits must be >= 1");
+  if ((int64_t)B * n == 0) return MPQ_OK;
+  k_vamp_r1_parts<<<ew_grid((int64_t)B * n), 256, 0, (cudaStream_t)stream>>>(
+      parts, splits, (int64_t)B * n, r2, r1, eta2, gamma2, gamma1_new, B, n, ld, damping,
+      static_cast<const VampCtl*>(ctl), r2_keep);
+  return launch_status("mpq_vamp_r1_parts_ctl");
 }

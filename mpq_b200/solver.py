@@ -747,7 +747,8 @@ class E8Layer:
         self.V, self.Vh, self.S, self.Vs = V, Vh, S, Vs
         self.R = int(S.numel())
         self.tab = factor_tables(cb, device)
-        self.opV, self.opVh = ops.Operand(V), ops.Operand(Vh)
+        # the device-resident loop's products take the row-scaled fp16 split of V and Vh
+        self.opV, self.opVh = ops.Operand(V, "f16x3"), ops.Operand(Vh, "f16x3")
         self.V, self.Vh = self.opV.full, self.opVh.full
         self.VsT = Vs.t().contiguous()
         self.opVs, self.opVsT = ops.Operand(Vs), ops.Operand(self.VsT)
@@ -802,6 +803,16 @@ class E8VampState:
         self.obs_hist = torch.empty(max(iters, 1), device=device, dtype=torch.float64)
         self.chunks = _posterior_chunks(B, nb)
         self.work = torch.zeros(B * (self.chunks + 1), device=device, dtype=torch.int32)
+        # row-scaled fp16 splits of the products' A operands (r2, u), written by their producers, and the split-K
+        # partial planes of the two products (added by their consumers)
+        h16 = dict(device=device, dtype=torch.float16)
+        ldn, ldr = (n + 7) // 8 * 8, (R + 7) // 8 * 8
+        self.r2_hi, self.r2_lo, self.r2_inv = torch.empty(B, ldn, **h16), torch.empty(B, ldn, **h16), torch.empty(B, **f32)
+        self.u_hi, self.u_lo, self.u_inv = torch.empty(B, ldr, **h16), torch.empty(B, ldr, **h16), torch.empty(B, **f32)
+        sms = ops.num_sms(torch.device(device))
+        self.splits_p = ops.splitk_for(B, R, n, sms)
+        self.splits_d = ops.splitk_for(B, n, R, sms)
+        self.ws = torch.empty(max(self.splits_p * B * R, self.splits_d * B * n, 1), **f32)
 
 
 def e8_vamp_device(st: E8VampState, ctl: torch.Tensor, L: E8Layer, *, Wr, hat0, center, pscale, tau: float, Y_u,
@@ -835,13 +846,25 @@ def e8_vamp_device(st: E8VampState, ctl: torch.Tensor, L: E8Layer, *, Wr, hat0, 
                  ptr(rows["eta2"]), ptr(rows["g1n"]), ptr(rows["g1next"]), ptr(rows["trace"]), ptr(flags), ptr(L.S), B,
                  n, nb, R, damping, final, c)
             call("mpq_vamp_ctl_round", c, ptr(flags), ptr(rows["g1w"]), ptr(rows["var"]), B, nb, factor, final)
-        call("mpq_vamp_r2_ctl", ptr(st.x1), ptr(st.r1), ptr(st.r2_prev), ptr(st.r2), ptr(rows["eta1"]),
-             ptr(rows["g1w"]), ptr(rows["g2n"]), B, n, st.r2.stride(0), damping, c)
-        ops.mm_nt(st.r2, L.opVh, st.P)
-        call("mpq_linear_epilogue_ctl", ptr(st.P), ptr(Y_u), ptr(L.S), ptr(rows["g2"]), B, R, st.P.stride(0), ptr(st.u),
-             ptr(rows["resid"]), c)
-        ops.mm_nt(st.u, L.opV, st.x1)
-        call("mpq_vamp_r1_ctl", ptr(st.x1), ptr(st.r2), ptr(st.r1), ptr(rows["eta2"]), ptr(rows["g2"]),
+        # r2 and its fp16 split -> P = r2 V (partial planes) -> linear epilogue (adds the planes, writes u split)
+        # -> D = u V^T (partial planes) -> r1 update (adds the planes)
+        call("mpq_vamp_r2_split_ctl", ptr(st.x1), ptr(st.r1), ptr(st.r2_prev), ptr(st.r2), ptr(rows["eta1"]),
+             ptr(rows["g1w"]), ptr(rows["g2n"]), B, n, st.r2.stride(0), damping, ptr(st.r2_hi), ptr(st.r2_lo),
+             st.r2_hi.stride(0), ptr(st.r2_inv), c)
+        Bh, Bl, Bi = L.opVh.f16
+        status = ops.status_word(L.dev)
+        tok = trace.begin_timing("gemm_tc")
+        call("mpq_gemm_f16x3_parts", B, R, n, ptr(st.r2_hi), ptr(st.r2_lo), st.r2_hi.stride(0), ptr(st.r2_inv), ptr(Bh),
+             ptr(Bl), Bh.stride(0), ptr(Bi), st.splits_p, ptr(st.ws), st.ws.numel(), ptr(status))
+        trace.end_timing("gemm_tc", tok, 2.0 * B * R * n)
+        call("mpq_linear_epilogue_parts_ctl", ptr(st.ws), st.splits_p, ptr(Y_u), Y_u.stride(0), ptr(L.S), ptr(rows["g2"]),
+             B, R, ptr(st.u), ptr(st.u_hi), ptr(st.u_lo), st.u_hi.stride(0), ptr(st.u_inv), ptr(rows["resid"]), c)
+        Bh, Bl, Bi = L.opV.f16
+        tok = trace.begin_timing("gemm_tc")
+        call("mpq_gemm_f16x3_parts", B, n, R, ptr(st.u_hi), ptr(st.u_lo), st.u_hi.stride(0), ptr(st.u_inv), ptr(Bh),
+             ptr(Bl), Bh.stride(0), ptr(Bi), st.splits_d, ptr(st.ws), st.ws.numel(), ptr(status))
+        trace.end_timing("gemm_tc", tok, 2.0 * B * R * n)
+        call("mpq_vamp_r1_parts_ctl", ptr(st.ws), st.splits_d, ptr(st.r2), ptr(st.r1), ptr(rows["eta2"]), ptr(rows["g2"]),
              ptr(rows["g1n"]), B, n, st.r1.stride(0), damping, ptr(st.r2_prev) if damping < 1.0 else None, c)
         call("mpq_vamp_ctl_commit", c, ptr(st.gamma1), ptr(rows["g1next"]), ptr(rows["g2p"]), ptr(rows["g2"]),
              ptr(rows["resid"]), ptr(rows["trace"]), B, R, int(em_active), float(cfg.em_obs_precision_damping),
@@ -1046,7 +1069,9 @@ def solve_e8p12_rankspace_vamp(
         L = E8Layer.__new__(E8Layer)
         L.dev, L.cb, L.R, L.tab, L._gram = dev, cb, R, tab, None
         L.V, L.Vh, L.S, L.Vs, L.VsT = V, Vh, S, Vs, VsT
-        L.opV, L.opVh, L.opVs, L.opVsT = opV, opVh, opVs, opVsT
+        L.opV = opV if opV.f16 is not None else ops.Operand(V, "f16x3")
+        L.opVh = opVh if opVh.f16 is not None else ops.Operand(Vh, "f16x3")
+        L.opVs, L.opVsT = opVs, opVsT
         st_dev = E8VampState(B, n, R, iters, dev)
         ctl = vamp_ctl_new(dev, obs)
         e8_vamp_device(st_dev, ctl, L, Wr=Wr, hat0=hat0, center=center, pscale=pscale, tau=tau, Y_u=Y_u, cfg=cfg,
