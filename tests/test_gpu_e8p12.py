@@ -249,15 +249,18 @@ def test_mpq_refine_codebook_matches_reference_golden(cuda_dev, golden_dir, pcb,
     l = OL.proxy_loss(g("Wr"), hat.cpu().numpy(), g("H"))
     rl = OL.proxy_loss(g("Wr"), g("hatWr"), g("H"))
     assert torch.isfinite(hat).all()
+    br = meta["block_rows"]
+    diag = dict(all=same.mean(), blocks=[same[r:r + br].mean() for r in range(0, same.shape[0], br)], loss=l,
+                ref_loss=rl)
+    assert abs(l - rl) <= 0.005 * rl, diag
     if case == "a":
-        # In the second row block of case a the reference's EM drives the observation precision from 15 to
-        # its 1e-4 floor; there gamma1_new ~ 1e-7 gamma2 and (gamma2 (x2 - r2)) / gamma1_new amplifies
-        # float32 rounding ~1e7-fold, so only the stable first block is held to parity.
-        assert same[:meta["block_rows"]].mean() >= 0.99, same[:meta["block_rows"]].mean()
-        assert abs(l - rl) <= 0.05 * rl, (l, rl)
+        # One row of case a's second block diverges inside the reference's own VAMP (message r1 above 1e9), and
+        # whether float32 overflow leaves its alpha1 inside (0, 1) decides that block's codes through the shared
+        # EM update (tests/test_oracle_e8p12.py::test_e8p12_layer_case_a_second_block_is_set_by_a_diverging_row):
+        # the first block is held to the codes, the whole layer to the proxy loss.
+        assert same[:br].mean() >= 0.999, diag
     else:
-        assert same.mean() >= 0.999, same.mean()
-        assert abs(l - rl) <= 0.005 * rl, (l, rl)
+        assert same.mean() >= 0.999, diag
 
 
 @pytest.mark.gpu
