@@ -84,6 +84,9 @@ def parse():
     ap.add_argument("--hess-n", type=int, default=14336, help="hessian workload: features n")
     ap.add_argument("--hess-tokens", type=int, default=16384, help="hessian workload: tokens T per batch")
     ap.add_argument("--hess-dtype", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--serial", action="store_true",
+                    help="e8p12: run each step's layer set-up (rotations, eigendecomposition) before its solve instead "
+                         "of on the set-up pipeline ahead of it")
     ap.add_argument("--polish-mode", default="block_cd", choices=["block_cd", "topk_block_cd"],
                     help="layer workloads: the polish recipe (block_cd is the reference's default)")
     a = ap.parse_args()
@@ -216,9 +219,12 @@ class ScalarWorkload:
     def __init__(self, dev, block_rows, polish_mode="block_cd"):
         self.dev, self.block_rows, self.polish_mode = dev, block_rows, polish_mode
 
-    def step(self, W, H):
+    def step(self, k, W, H, ahead=True):
         from mpq_b200.adapters.gptqmodel import GPTQAdapterConfig, run_mpq_quantization
         from mpq_b200.solver import UniformVampConfig
+        if not W.is_cuda:
+            W = W.to(self.dev, non_blocking=True)
+            H = H.to(self.dev, non_blocking=True)
         qcfg = types.SimpleNamespace(bits=4, group_size=128, desc_act=False,
                                      mpq=types.SimpleNamespace(rotation_mode="internal_hadamard", solver="vamp"))
         out = run_mpq_quantization(W=W, H=2.0 * H, quantizer=None, qcfg=qcfg, module_name="bench.layer",
@@ -231,40 +237,108 @@ class ScalarWorkload:
                                       "obs_final": st["obs_precision_final"], "block_rows": st["block_rows"],
                                       "best_iters": [b["best_iter"] for b in st["block_stats"]]}
 
+    def finish(self, k):
+        return k
+
+    def close(self):
+        pass
+
 
 class E8Workload:
+    """One step = one 4096 x 4096 layer: its layer-wide set-up (two-sided RHT of W and H, the RMS scale, the fp64
+    eigendecomposition of the rotated Hessian) and the chained solve of this rank's rows.
+
+    Pipelined (the default): the set-up of step k + N is queued on the set-up pipeline's worker (mpq_b200.pipeline)
+    once step k's blocks are enqueued.  With N ranks the eigendecomposition of step k is computed on rank k mod N
+    only and the other ranks copy it from that rank's memory (mpq_b200.exchange) -- every step still carries one
+    full set-up and one full solve of the layer across the job.  Serial: every rank sets up each step itself
+    before solving it."""
     dominant = "e8p12_mmse"
 
-    def __init__(self, dev, block_rows, SU, SV, rows, polish_mode="block_cd"):
+    def __init__(self, dev, block_rows, SU, SV, rows, polish_mode="block_cd", rank=0, world=1, pipelined=True,
+                 n=None):
         from mpq_b200.codebook import E8P12_codebook
+        from mpq_b200.pipeline import SetupPipeline
         self.dev, self.block_rows, self.rows, self.polish_mode = dev, block_rows, rows, polish_mode
+        self.rank, self.world = rank, world
         self.cb = E8P12_codebook()
         self.SU, self.SV = SU.to(dev), SV.to(dev)
+        self.pipe = SetupPipeline(dev) if pipelined else None
+        self.xchg = None
+        if pipelined and world > 1:
+            from mpq_b200.exchange import EigenExchange
+            self.xchg = EigenExchange(n or N_COLS, dev)
 
-    def step(self, W, H):
-        """W: the whole layer (the two-sided rotation and the RMS scale are layer-wide); solves self.rows."""
-        import torch
-        from mpq_b200 import ops
-        from mpq_b200._lib import call, ptr
-        from mpq_b200.adapters.quip_sharp import mpq_refine_codebook
+    def owner(self, k: int) -> int:
+        return k % self.world if self.pipe is not None else self.rank
+
+    def setup(self, k, W, H):
+        """Layer set-up of step k (W, H on the host are copied in first; the rotation and the scale are layer-wide,
+        so every rank rotates the whole W and keeps its rows)."""
+        from mpq_b200.adapters.gptqmodel import vamp_hessian_eigen
         from mpq_b200.rotation import rht_hessian, rht_weight
+        if not W.is_cuda:
+            W = W.to(self.dev, non_blocking=True)
+            H = H.to(self.dev, non_blocking=True)
         m, n = W.shape
         Wr = rht_weight(W, self.SU, self.SV, m & -m, n & -n)
         Hr = rht_hessian(H, self.SV, n & -n)
         wscale = float(Wr.double().square().mean().sqrt())  # QUIP#'s global RMS scale, in float64
         r0, r1 = self.rows
-        Wn = Wr[r0:r1] / wscale
-        m = r1 - r0
+        Wn = (Wr[r0:r1] / wscale).contiguous()
+        eig = None
+        if self.owner(k) == self.rank:
+            eig = vamp_hessian_eigen(Hr, fp64=True)
+            if self.xchg is not None:
+                self.xchg.publish(k, eig)
+        return {"Wn": Wn, "Hr": Hr, "wscale": wscale, "eig": eig}
+
+    def queue(self, k, W, H):
+        if self.pipe is not None and not self.pipe.pending(k):
+            self.pipe.submit(k, self.setup, k, W, H)
+
+    def step(self, k, W, H, ahead=True):
+        """Solve step k (its set-up queued earlier, or run now); queue the set-up of step k + N once step k's device
+        work is enqueued."""
+        import torch
+        from mpq_b200.adapters.quip_sharp import mpq_refine_codebook
+        if self.pipe is not None:
+            self.queue(k, W, H)
+            P = self.pipe.get(k)
+        else:
+            P = self.setup(k, W, H)
+        eig = P["eig"] if P["eig"] is not None else self.xchg.fetch(k)
+        Wn = P["Wn"]
+        m, n = Wn.shape
         args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=16, mpq_prior_tau=0.25, mpq_polish_sweeps=3,
                                      mpq_block_rows=self.block_rows, quant_solver="vamp",
                                      quant_polish_mode=self.polish_mode, mpq_polish_metric="gram")
-        hat, idx, st = mpq_refine_codebook(Wn, Hr, Wn, torch.zeros(m, n // 8, dtype=torch.int64, device=W.device),
-                                           self.cb, args, module_name="bench.layer")
+        nxt = (lambda: self.queue(k + self.world, W, H)) if (ahead and self.pipe is not None) else None
+        hat, idx, st = mpq_refine_codebook(Wn, P["Hr"], Wn, torch.zeros(m, n // 8, dtype=torch.int64, device=self.dev),
+                                           self.cb, args, module_name="bench.layer", eigen=eig, after_enqueue=nxt)
         from mpq_b200 import chain
         return [idx], {"surrogate_before": st["exact_surrogate_before_mean"],
                        "surrogate_after": st["exact_surrogate_after_mean"], "obs_final": st["obs_precision_final"],
-                       "wscale": wscale, "changed_fraction": st["mechanism"]["cleanup_changed_fraction"],
+                       "wscale": P["wscale"], "changed_fraction": st["mechanism"]["cleanup_changed_fraction"],
                        "block_rows": st["block_rows"], "chain_host_s": dict(chain.last_timing)}
+
+    def finish(self, k):
+        """Wait for the set-ups still queued (their work belongs to the steps that queued them) and drop them;
+        returns the next step index (dropped steps' indices are not reused)."""
+        if self.pipe is None:
+            return k
+        dropped = self.pipe.keys()
+        self.pipe.drain()
+        for j in dropped:
+            if self.xchg is not None:
+                self.xchg.skip(j)
+        return max([k] + [j + 1 for j in dropped])
+
+    def close(self):
+        if self.pipe is not None:
+            self.pipe.close()
+        if self.xchg is not None:
+            self.xchg.close()
 
 
 def run_mpq(args):
@@ -305,37 +379,43 @@ def run_mpq(args):
     else:
         block_rows = min(args.block_rows, rows_per) if args.block_rows > 0 else 0
     if args.workload == "e8p12":
-        wl = E8Workload(dev, block_rows, SU, SV, (r0, r1), polish_mode=args.polish_mode)
+        wl = E8Workload(dev, block_rows, SU, SV, (r0, r1), polish_mode=args.polish_mode, rank=rank, world=world,
+                        pipelined=not args.serial)
         Wr = W  # the rotation and scale are layer-wide; the workload solves rows r0:r1
     else:
         wl = ScalarWorkload(dev, block_rows, polish_mode=args.polish_mode)
         Wr = W[r0:r1].contiguous()
     flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > 126 MB L2
 
+    k = 0
     for _ in range(max(args.warmup, 0)):
-        wl.step(Wr, H)
+        wl.step(k, Wr, H)
+        k += 1
     torch.cuda.synchronize()
 
-    # ---- device-resident timed region ----
+    # ---- device-resident timed region: K steps from one start event to one end event; the set-ups the timed
+    # steps queued for later steps finish inside the region ----
     clocks = ClockSampler(local, enabled=not args.no_clocks)
     launches0 = trace.launches()
-    step_ms = []
     stats = {}
     with trace.timing([wl.dominant]):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t_s = torch.cuda.Event(enable_timing=True)
+        t_e = torch.cuda.Event(enable_timing=True)
+        t_s.record()
+        torch.cuda.nvtx.range_push("timed_steps")
         for _ in range(args.steps):
             flush.add_(1.0)
-            if world > 1:
-                dist.barrier()
-            torch.cuda.synchronize()
-            s = torch.cuda.Event(enable_timing=True)
-            e = torch.cuda.Event(enable_timing=True)
-            s.record()
-            torch.cuda.nvtx.range_push("timed_step")
-            outs, stats = wl.step(Wr, H)
-            torch.cuda.nvtx.range_pop()
-            e.record()
-            torch.cuda.synchronize()
-            step_ms.append(s.elapsed_time(e))
+            outs, stats = wl.step(k, Wr, H)
+            k += 1
+        k = wl.finish(k)
+        torch.cuda.nvtx.range_pop()
+        t_e.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         dom = trace.summary(wl.dominant)
     launches = (trace.launches() - launches0) / max(args.steps, 1)
     dom_note = "CUDA events around every launch in the timed steps"
@@ -345,19 +425,21 @@ def run_mpq(args):
         from mpq_b200 import chain
         chain.use_graphs = False
         with trace.timing([wl.dominant]):
-            wl.step(Wr, H)
+            wl.step(k, Wr, H, ahead=False)
+            k += 1
             torch.cuda.synchronize()
             dom = trace.summary(wl.dominant)
         chain.use_graphs = True
         dom_note = ("CUDA events around every launch of one extra step launched from the host (the timed steps replay "
                     "CUDA graphs of the same kernels with the same arguments)")
     clk = clocks.stop()
-    ms = float(np.sum(step_ms)) / max(args.steps, 1)
+    ms = t_s.elapsed_time(t_e) / max(args.steps, 1)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     if args.profile:
+        wl.close()
         if world > 1:
             dist.destroy_process_group()
         return {"profile": True, "ms_per_step": ms, "gpu_launches": launches} if rank == 0 else None
@@ -365,21 +447,24 @@ def run_mpq(args):
     # ---- e2e through the public API with host buffers ----
     W_host = Wr.cpu().pin_memory()
     H_host = H.cpu().pin_memory()
-    e2e_ms = []
     h2d = W_host.numel() * 4 + H_host.numel() * 4
     d2h = 0
-    for _ in range(max(1, min(args.steps, 2))):
+    n_e2e = max(1, min(args.steps, 3))
+    if hasattr(wl, "queue"):
+        wl.queue(k, W_host, H_host)  # as in the timed region: the first step's set-up was queued by the step before
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
         flush.add_(1.0)
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        Wd = W_host.to(dev, non_blocking=True)
-        Hd = H_host.to(dev, non_blocking=True)
-        outs, _ = wl.step(Wd, Hd)
+        outs, _ = wl.step(k, W_host, H_host)  # the set-up copies this step's W and H from pinned host memory
+        k += 1
         host = [o.cpu() for o in outs]
-        torch.cuda.synchronize()
-        e2e_ms.append((time.perf_counter() - t0) * 1e3)
         d2h = sum(o.numel() * o.element_size() for o in host)
-    e2e = float(np.mean(e2e_ms))
+    k = wl.finish(k)
+    torch.cuda.synchronize()
+    e2e = (time.perf_counter() - t0) * 1e3 / n_e2e
     if world > 1:
         t = torch.tensor([e2e], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -406,6 +491,13 @@ def run_mpq(args):
             "hessian": hess,
             "stats": stats,
         }
+        if args.workload == "e8p12":
+            result["schedule"] = ("serial: each step's layer set-up (rotations, fp64 eigendecomposition), then its solve"
+                                  if args.serial else
+                                  "pipelined: the layer set-up of step k+N (rotations, fp64 eigendecomposition) runs on "
+                                  "a low-priority worker stream while step k is solved; with N ranks the "
+                                  "eigendecomposition of step k runs on rank k mod N and the others copy it over NVLink; "
+                                  "the set-ups queued by the timed steps finish inside the timed region")
         if not args.no_cpu_baseline and world == 1:
             oracle = CpuOracle(args.workload, H=H.cpu())
             t_rows, ref_out = oracle.solve_rows(0, args.cpu_sample_rows)
@@ -415,6 +507,7 @@ def run_mpq(args):
                 "sample": f"{rows} of {M_ROWS} rows solved as one block ({oracle.what}) in {t_rows:.1f} s, "
                           f"extrapolated x{M_ROWS // rows}; rotation + eigendecomposition once ({oracle.t_setup:.1f} s)"}
             result["parity_sample"] = gpu_vs_oracle(args.workload, oracle, ref_out, Wr, H, rows, dev)
+    wl.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -17,6 +17,7 @@
 #ifndef MPQ_B200_H
 #define MPQ_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -375,6 +376,20 @@ int mpq_pack_bits(const uint8_t* src, int64_t sp, int64_t so, int n_pack, int n_
  * Replaces mpq/rotation.py:404-441 (apply_block_hadamard, apply_right_block_hadamard[_inverse]). */
 int mpq_block_hadamard(const float* x, int64_t ldx, float* y, int64_t ldy, int rows, int n, int had,
                        const float* signs, int mode, void* stream);
+
+/* ---- peer memory between the processes of one node ----
+ * Multi-GPU layer solves compute each layer's eigendecomposition (mpq/adapters/quip_sharp.py:33-67) on one rank;
+ * the ranks solving the layer's other row shards copy it from that rank's memory over NVLink instead of repeating
+ * it.  The reference has no multi-GPU path; these replace nothing in it.
+ * mpq_peer_alloc: cudaMalloc on the current device and export the CUDA IPC handle (64 bytes into out_handle).
+ * mpq_peer_open / mpq_peer_close: map / unmap another process's exported buffer in this device's context.
+ * mpq_peer_free: free an mpq_peer_alloc buffer after every peer closed it.
+ * mpq_copy_bytes: asynchronous copy on `stream`; either side may be a peer mapping. */
+int mpq_peer_alloc(size_t bytes, void** out_ptr, void* out_handle, void* stream);
+int mpq_peer_open(const void* handle, void** out_ptr, void* stream);
+int mpq_peer_close(void* ptr, void* stream);
+int mpq_peer_free(void* ptr, void* stream);
+int mpq_copy_bytes(void* dst, const void* src, size_t bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -53,6 +53,11 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_gamma_init": (P, P, I, I, L, F, P, P),
     "mpq_row_dot": (P, L, P, L, I, I, P, P),
     "mpq_sub": (P, P, P, I, I, L, P),
+    "mpq_peer_alloc": (ctypes.c_size_t, P, P, P),
+    "mpq_peer_open": (P, P, P),
+    "mpq_peer_close": (P, P),
+    "mpq_peer_free": (P, P),
+    "mpq_copy_bytes": (P, P, ctypes.c_size_t, P),
     "mpq_gemm_f32": (I, I, I, I, F, P, L, P, L, F, P, L, P),
     "mpq_gemm_tc": (I, I, I, I, F, P, L, P, L, F, P, L, P, P),
     "mpq_split_tf32": (P, L, P, P, L, I, I, P),

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass
-from typing import Any, Dict, List, Optional, Tuple
+from typing import Any, Callable, Dict, List, Optional, Tuple
 
 import torch
 
@@ -103,8 +103,15 @@ def mpq_refine_codebook(
     *,
     module_name: str = "",
     adapter_cfg: QuipAdapterConfig = QuipAdapterConfig(),
+    eigen: Optional[Tuple[torch.Tensor, torch.Tensor, float]] = None,
+    after_enqueue: Optional[Callable[[], None]] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, Any]]:
     """QUIP# adapter: refine codebook decisions with VAMP + greedy gram-metric polish.
+
+    eigen: (lam, V, floor) of vamp_hessian_eigen(Hr, fp64=True) with this adapter_cfg's jitter and floor, computed
+    ahead (by mpq_b200.pipeline while the previous layer was solved, or on another rank); None computes it here, as
+    the reference does.  after_enqueue: called once the solve's device work is enqueued (the chained path) or
+    before it starts (the block-by-block path).
 
     Returns (hatWr (m, n), Qidxs int64 (m, n/8), stats)."""
     start = time.time()
@@ -146,8 +153,13 @@ def mpq_refine_codebook(
     else:
         raise ValueError(f"unknown mpq_init={init_mode!r} (expected 'float', 'random', 'rtn', 'zero', or 'ldlq').")
 
-    lam, V, eigen_floor = vamp_hessian_eigen(Hr, jitter_base=adapter_cfg.jitter_base,
-                                             floor_scale=adapter_cfg.eigen_floor_scale, fp64=True)
+    if eigen is None:
+        eigen = vamp_hessian_eigen(Hr, jitter_base=adapter_cfg.jitter_base, floor_scale=adapter_cfg.eigen_floor_scale,
+                                   fp64=True)
+    lam, V, eigen_floor = eigen
+    if lam.shape != (n,) or V.shape != (n, n) or lam.device != device or V.device != device:
+        raise ValueError(f"eigen: expected lam ({n},) and V ({n}, {n}) on {device}; got {tuple(lam.shape)} and "
+                         f"{tuple(V.shape)}")
     V = V.contiguous()
     Vh = V.T.contiguous()
     S = torch.sqrt(lam).contiguous()
@@ -182,7 +194,7 @@ def mpq_refine_codebook(
         # the serial chain of row blocks on the device (VAMP chain on one stream, polish overlapped on others)
         final_hat, final_idx, per_block = e8p12_layer_chain(
             Wr=Wr, hat_init=hat_init, cb=cb, V=V, Vh=Vh, S=S, Vs=Vs, cfg=vamp_cfg, block_rows=block_rows,
-            obs_init=obs_precision)
+            obs_init=obs_precision, after_enqueue=after_enqueue)
         for bst in per_block:
             gamma_sum += bst.pop("_gamma1_sum")
             gamma_count += bst.pop("_gamma1_count")
@@ -195,6 +207,8 @@ def mpq_refine_codebook(
         if bool(vamp_cfg.em_obs_precision) and float(vamp_cfg.obs_precision) <= 0.0 and per_block:
             obs_block = float(per_block[-1]["obs_precision_final"])
     else:
+        if after_enqueue is not None:
+            after_enqueue()
         for r0 in range(0, m, block_rows):
             rb = slice(r0, min(r0 + block_rows, m))
             dbg: Dict[str, Any] = {"summary_only": True}

@@ -16,7 +16,7 @@ The first block runs without graphs (it initialises every kernel's launch state)
 from __future__ import annotations
 
 import time
-from typing import Any, Dict, List, Optional, Tuple
+from typing import Any, Callable, Dict, List, Optional, Tuple
 
 import torch
 
@@ -30,6 +30,14 @@ from .solver import (E8Layer, E8P12VampConfig, E8VampState, _resolve_e8p12_polis
 last_timing: Dict[str, float] = {}
 # CUDA graphs for the per-block launch sequences (False: host launches, e.g. to time single kernels with events)
 use_graphs = True
+
+
+def _priority(level: int) -> int:
+    """Stream priority `level` steps above the default (clamped to the device's range): the VAMP chain is the
+    critical path (2), the overlapped polish next (1); work on default-priority streams (such as the layer set-up
+    of mpq_b200.pipeline) takes the SMs they leave."""
+    lo, hi = torch.cuda.Stream.priority_range()
+    return max(hi, lo - int(level))
 
 
 def chain_supported(cfg: E8P12VampConfig) -> bool:
@@ -71,7 +79,8 @@ class _Graphable:
         n0 = trace.launches()
         with ops.graph_scratch() as d:
             with torch.cuda.stream(stream):
-                g.capture_begin()
+                # thread_local: a set-up worker thread (mpq_b200.pipeline) may allocate or synchronise meanwhile
+                g.capture_begin(capture_error_mode="thread_local")
                 try:
                     self.body()
                 finally:
@@ -131,7 +140,7 @@ class _PolishBlock(_Graphable):
         dev = L.dev
         nb = n // 8
         self.L, self.gram, self.cb, self.sweeps = L, gram, cb, sweeps
-        self.stream = torch.cuda.Stream(dev)
+        self.stream = torch.cuda.Stream(dev, priority=_priority(1))
         self.x = torch.empty(B, n, device=dev)
         self.idx = torch.empty(B, nb, device=dev, dtype=torch.int64)
         self.Y = torch.empty(B, L.R, device=dev)
@@ -174,6 +183,7 @@ class _ChainState:
         self.vamp = _VampBlock(self.L, cb, cfg, self.ctl, B, n, tau, with_pscale, em_active)
         self.polish = [_PolishBlock(self.L, self.gram, cb, B, n, sweeps) for _ in range(max(int(polish_streams), 1))]
         self.cap_stream = torch.cuda.Stream(dev)
+        self.vamp_stream = torch.cuda.Stream(dev, priority=_priority(2))
 
     def capture(self):
         self.vamp.capture(self.cap_stream)
@@ -188,11 +198,13 @@ _WARM: set = set()  # devices whose kernels have run once in this process (launc
 @torch.inference_mode()
 def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.Tensor, Vh: torch.Tensor,
                       S: torch.Tensor, Vs: torch.Tensor, cfg: E8P12VampConfig, block_rows: int, obs_init: float,
-                      polish_streams: int = 6, graphs: Optional[bool] = None
+                      polish_streams: int = 6, graphs: Optional[bool] = None,
+                      after_enqueue: Optional[Callable[[], None]] = None
                       ) -> Tuple[torch.Tensor, torch.Tensor, List[Dict[str, Any]]]:
     """Solve all rows of one E8P12 layer as the reference's serial chain of `block_rows`-row blocks.  graphs=False
     launches every kernel from the host (the same kernels and arguments as the graphs; per-launch timing works);
-    None means the module default (use_graphs).
+    None means the module default (use_graphs).  after_enqueue() runs once every block is enqueued, while the
+    device works through them (e.g. to start the next layer's set-up without competing for the host thread).
 
     Returns (hatWr (m, n), Qidxs int64 (m, n/8), per-block stats in the keys of solve_e8p12_rankspace_vamp plus
     the adapter's mechanism sums)."""
@@ -241,55 +253,63 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     t_start = time.perf_counter()
     if graphs and cs.vamp.graph is None and dev.index in _WARM:
         cs.capture()
+    # the VAMP chain runs on the state's high-priority stream, the polish on the polish streams; every tensor they
+    # share with the caller was allocated above on the caller's stream, which waits for both before returning
+    vs = cs.vamp_stream
+    vs.wait_stream(main)
     tail = None  # a last block with fewer rows runs eagerly with its own buffers
-    for bi, r0 in enumerate(starts):
-        r1 = min(r0 + B, m)
-        Bb = r1 - r0
-        rb = slice(r0, r1)
-        if Bb == B:
-            vb, pb = cs.vamp, cs.polish[bi % len(cs.polish)]
-        else:
-            if tail is None:
-                tail = (_VampBlock(L, cb, cfg, ctl, Bb, n, tau, pscale_all is not None, em_active),
-                        _PolishBlock(L, cs.gram, cb, Bb, n, sweeps))
-            vb, pb = tail
-        if graphs and bi > 0 and Bb == B and cs.vamp.graph is None:
-            # first use in this process: block 0 ran eagerly (kernel attributes, tables, scratch set up)
-            _WARM.add(dev.index)
-            cs.capture()
-        if bi > 0:
-            vamp_ctl_reset(ctl)
-            if float(cfg.obs_precision) > 0.0:
-                ctl.view(torch.float64)[0:1].fill_(obs0)
-        vb.W.copy_(Wr[rb])
-        vb.hat0.copy_(hat_init[rb])
-        vb.Y.copy_(Y_u_all[rb])
-        if vb.pscale is not None:
-            vb.pscale.copy_(pscale_all[rb])
-        vb.run(graphs)
-        final_hat[rb].copy_(vb.vals)
-        final_idx[rb].copy_(vb.idx)
-        b_ctl[bi].copy_(ctl)
-        b_hist[bi, :iters].copy_(vb.st.obs_hist[:iters])
-        b_obs_in[bi:bi + 1].copy_(vb.obs_in)
-        b_g[bi].copy_(vb.gstats)
-        ev = torch.cuda.Event()
-        ev.record(main)
-        pb.stream.wait_event(ev)
-        with torch.cuda.stream(pb.stream):
-            pb.x.copy_(final_hat[rb])
-            pb.idx.copy_(final_idx[rb])
-            pb.Y.copy_(Y_u_all[rb])
-            pb.run(graphs)
-            final_hat[rb].copy_(pb.x_out)
-            final_idx[rb].copy_(pb.idx_out)
-            b_pol[bi].copy_(pb.stats)
-            b_trace[bi].copy_(pb.trace)
+    with torch.cuda.stream(vs):
+        for bi, r0 in enumerate(starts):
+            r1 = min(r0 + B, m)
+            Bb = r1 - r0
+            rb = slice(r0, r1)
+            if Bb == B:
+                vb, pb = cs.vamp, cs.polish[bi % len(cs.polish)]
+            else:
+                if tail is None:
+                    tail = (_VampBlock(L, cb, cfg, ctl, Bb, n, tau, pscale_all is not None, em_active),
+                            _PolishBlock(L, cs.gram, cb, Bb, n, sweeps))
+                vb, pb = tail
+            if graphs and bi > 0 and Bb == B and cs.vamp.graph is None:
+                # first use in this process: block 0 ran eagerly (kernel attributes, tables, scratch set up)
+                _WARM.add(dev.index)
+                cs.capture()
+            if bi > 0:
+                vamp_ctl_reset(ctl)
+                if float(cfg.obs_precision) > 0.0:
+                    ctl.view(torch.float64)[0:1].fill_(obs0)
+            vb.W.copy_(Wr[rb])
+            vb.hat0.copy_(hat_init[rb])
+            vb.Y.copy_(Y_u_all[rb])
+            if vb.pscale is not None:
+                vb.pscale.copy_(pscale_all[rb])
+            vb.run(graphs)
+            final_hat[rb].copy_(vb.vals)
+            final_idx[rb].copy_(vb.idx)
+            b_ctl[bi].copy_(ctl)
+            b_hist[bi, :iters].copy_(vb.st.obs_hist[:iters])
+            b_obs_in[bi:bi + 1].copy_(vb.obs_in)
+            b_g[bi].copy_(vb.gstats)
+            ev = torch.cuda.Event()
+            ev.record(vs)
+            pb.stream.wait_event(ev)
+            with torch.cuda.stream(pb.stream):
+                pb.x.copy_(final_hat[rb])
+                pb.idx.copy_(final_idx[rb])
+                pb.Y.copy_(Y_u_all[rb])
+                pb.run(graphs)
+                final_hat[rb].copy_(pb.x_out)
+                final_idx[rb].copy_(pb.idx_out)
+                b_pol[bi].copy_(pb.stats)
+                b_trace[bi].copy_(pb.trace)
+    main.wait_stream(vs)
     for pb in cs.polish + ([tail[1]] if tail is not None else []):
         main.wait_stream(pb.stream)
     if not graphs or cs.vamp.graph is None:
         _WARM.add(dev.index)
     t_enq = time.perf_counter()
+    if after_enqueue is not None:
+        after_enqueue()
     ops.check_status(dev)  # synchronises: every block has finished
     last_timing.update(enqueue_s=t_enq - t_start, total_s=time.perf_counter() - t_start, blocks=float(nblk))
     ctl_h, hist_h, obs_in_h = b_ctl.cpu().numpy(), b_hist.cpu().tolist(), b_obs_in.cpu().tolist()

@@ -6,6 +6,7 @@
 #include <math.h>
 
 #define MPQ_API extern "C" __attribute__((visibility("default")))
+#define MPQ_IPC_HANDLE_BYTES 64
 
 // Status codes returned by every C-ABI entry point (0 = success; >0 = cudaError_t).
 enum MpqStatus {

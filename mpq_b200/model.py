@@ -28,6 +28,7 @@ import torch.distributed as dist
 
 from . import ops
 from .hessian import accumulate_xtx
+from .pipeline import SetupPipeline
 from .shard import gather_rows, row_shards
 
 CONFIGS: Dict[str, Dict[str, Any]] = {
@@ -330,6 +331,28 @@ class QuipModelConfig:
     checkpoint_dir: Optional[str] = None  # QUIP#-layout ckpt: {layer}_{group}.pt / {layer}_layernorm.pt written as
     #                                       layers finish; groups whose file exists are loaded instead of solved
     fingerprint: bool = False    # sha256 of each group's W and H in the ckpt (host hashing: seconds per layer)
+    block_rows: int = 128        # the adapter's chained row blocks (mpq/adapters/quip_sharp.py:28)
+    pipelined: bool = True       # set up the next group (rotations, eigendecomposition) while a group is solved
+
+
+def _quip_group_setup(layer, mods, H, key: str, seed: int, dev) -> Dict[str, Any]:
+    """Layer-wide set-up of one projection group: W = vstack(w_i / rms(w_i)), sign vectors seeded by the group's
+    name, the two-sided randomized Hadamard of W and H, the unit-RMS scale and the floored fp64 eigendecomposition
+    of the rotated Hessian (mpq/quip_generic.py:1012-1046, mpq/adapters/quip_sharp.py:33-67)."""
+    from .adapters.gptqmodel import vamp_hessian_eigen
+    from .rotation import rht_hessian, rht_weight, sample_rademacher_signs
+    ws = [layer.get_submodule(m).weight.to(torch.float32) for m in mods]
+    scales = [float(w.square().mean().sqrt().item()) for w in ws]
+    W = torch.cat([w / s for w, s in zip(ws, scales)], dim=0).contiguous()
+    m, n = W.shape
+    SU = sample_rademacher_signs(width=m, key=f"{key}:SU", seed=seed, device=dev)
+    SV = sample_rademacher_signs(width=n, key=f"{key}:SV", seed=seed, device=dev)
+    Wr = rht_weight(W, SU, SV, m & -m, n & -n)
+    Hr = rht_hessian(H, SV, n & -n)
+    wscale = float(Wr.square().mean().sqrt().item())
+    Wn = (Wr / wscale).contiguous()
+    return {"ws": ws, "scales": scales, "W": W, "SU": SU, "SV": SV, "Hr": Hr, "wscale": wscale, "Wn": Wn,
+            "eig": vamp_hessian_eigen(Hr, fp64=True)}
 
 
 @torch.inference_mode()
@@ -364,7 +387,7 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
     pos_emb = inner.rotary_emb(hidden[:1], position_ids=pos_ids)
     args = types.SimpleNamespace(mpq_init=str(cfg.init), mpq_iters=int(cfg.iters), mpq_prior_tau=float(cfg.prior_tau),
                                  mpq_damping=float(cfg.damping),
-                                 mpq_polish_sweeps=int(cfg.polish_sweeps), mpq_block_rows=1 << 30,
+                                 mpq_polish_sweeps=int(cfg.polish_sweeps), mpq_block_rows=int(cfg.block_rows),
                                  quant_solver="vamp", quant_polish_mode=str(cfg.polish_mode), mpq_polish_metric="gram",
                                  mpq_topk_k=int(cfg.topk_k), seed=int(cfg.seed))
     attrs: Dict[str, Any] = {}
@@ -396,31 +419,41 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
             del accs
         hidden, nxt = nxt, hidden
     del hidden, nxt
-    # phase 2: layer l is solved on rank l mod N (the layers are independent given the float Hessians)
-    for li in range(nl):
-        if li % world != rank:
-            continue
-        layer = inner.layers[li]
-        for name, mods in QUIP_GROUPS:
-            key = f"{li}_{name}"
+    # phase 2: layer l is solved on rank l mod N (the layers are independent given the float Hessians); the set-up of
+    # the next group runs on the set-up pipeline while a group is solved
+    jobs = [(li, name, mods, f"{li}_{name}") for li in range(nl) if li % world == rank for name, mods in QUIP_GROUPS]
+    todo = [j for j in jobs if j[3] not in done]
+    pipe = SetupPipeline(dev) if (cfg.pipelined and todo) else None
+
+    def queue(j):
+        li, name, mods, key = j
+        pipe.submit(key, _quip_group_setup, inner.layers[li], mods, Hs_all[(li, name)], key, int(cfg.seed), dev)
+
+    try:
+        if pipe is not None:
+            queue(todo[0])
+        ti = 0
+        for li, name, mods, key in jobs:
+            layer = inner.layers[li]
             if key in done:
                 with timer("resume"):
                     attrs[key] = _quip_load_group(cfg.checkpoint_dir, key, layer, mods, cb, bool(cfg.write_back))
                 continue
             with timer("solve"):
                 H = Hs_all[(li, name)]
-                ws = [layer.get_submodule(m).weight.to(torch.float32) for m in mods]
-                scales = [float(w.square().mean().sqrt().item()) for w in ws]
-                W = torch.cat([w / s for w, s in zip(ws, scales)], dim=0).contiguous()
+                if pipe is not None:
+                    P = pipe.get(key)
+                    nxt = todo[ti + 1] if ti + 1 < len(todo) else None
+                    after = (lambda j=nxt: queue(j)) if nxt is not None else None
+                else:
+                    P = _quip_group_setup(layer, mods, H, key, int(cfg.seed), dev)
+                    after = None
+                ti += 1
+                ws, scales, W, SU, SV = P["ws"], P["scales"], P["W"], P["SU"], P["SV"]
+                wscale, Wn = P["wscale"], P["Wn"]
                 m, n = W.shape
-                SU = sample_rademacher_signs(width=m, key=f"{key}:SU", seed=int(cfg.seed), device=dev)
-                SV = sample_rademacher_signs(width=n, key=f"{key}:SV", seed=int(cfg.seed), device=dev)
-                Wr = rht_weight(W, SU, SV, m & -m, n & -n)
-                Hr = rht_hessian(H, SV, n & -n)
-                wscale = float(Wr.square().mean().sqrt().item())
-                Wn = (Wr / wscale).contiguous()
-                hat, idx, st = mpq_refine_codebook(Wn, Hr, Wn, torch.zeros(m, n // 8, dtype=torch.int64, device=dev),
-                                                   cb, args, module_name=key)
+                hat, idx, st = mpq_refine_codebook(Wn, P["Hr"], Wn, torch.zeros(m, n // 8, dtype=torch.int64, device=dev),
+                                                   cb, args, module_name=key, eigen=P["eig"], after_enqueue=after)
                 hatW = rht_weight_inverse(hat * wscale, SU, SV, m & -m, n & -n)
                 if cfg.write_back:
                     r0 = 0
@@ -449,6 +482,10 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                     for k in ("Qidxs", "SU", "SV"):
                         entry.pop(k, None)
                 attrs[key] = entry
+                del P
+    finally:
+        if pipe is not None:
+            pipe.close()
     del Hs_all
     # phase 3: every rank holds the quantized model (the owners' weights)
     if world > 1 and cfg.write_back:
