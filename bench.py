@@ -84,9 +84,12 @@ def parse():
     ap.add_argument("--hess-n", type=int, default=14336, help="hessian workload: features n")
     ap.add_argument("--hess-tokens", type=int, default=16384, help="hessian workload: tokens T per batch")
     ap.add_argument("--hess-dtype", default="bf16", choices=["bf16", "f32"])
-    ap.add_argument("--serial", action="store_true",
-                    help="e8p12: run each step's layer set-up (rotations, eigendecomposition) before its solve instead "
-                         "of on the set-up pipeline ahead of it")
+    ap.add_argument("--schedule", default="auto", choices=["auto", "serial", "pipelined"],
+                    help="e8p12: 'serial' sets up each step (rotations, eigendecomposition) before solving it; "
+                         "'pipelined' sets up step k+N on a worker stream while step k is solved and, with N ranks, "
+                         "computes each step's eigendecomposition on one rank and copies it to the others; 'auto' is "
+                         "pipelined with more than one GPU, serial on one (one GPU is busy through the solve, so the "
+                         "overlap gains nothing there)")
     ap.add_argument("--polish-mode", default="block_cd", choices=["block_cd", "topk_block_cd"],
                     help="layer workloads: the polish recipe (block_cd is the reference's default)")
     a = ap.parse_args()
@@ -378,9 +381,10 @@ def run_mpq(args):
         block_rows = min(args.block_rows if args.block_rows > 0 else 128, rows_per)
     else:
         block_rows = min(args.block_rows, rows_per) if args.block_rows > 0 else 0
+    pipelined = args.schedule == "pipelined" or (args.schedule == "auto" and world > 1)
     if args.workload == "e8p12":
         wl = E8Workload(dev, block_rows, SU, SV, (r0, r1), polish_mode=args.polish_mode, rank=rank, world=world,
-                        pipelined=not args.serial)
+                        pipelined=pipelined)
         Wr = W  # the rotation and scale are layer-wide; the workload solves rows r0:r1
     else:
         wl = ScalarWorkload(dev, block_rows, polish_mode=args.polish_mode)
@@ -493,7 +497,7 @@ def run_mpq(args):
         }
         if args.workload == "e8p12":
             result["schedule"] = ("serial: each step's layer set-up (rotations, fp64 eigendecomposition), then its solve"
-                                  if args.serial else
+                                  if not pipelined else
                                   "pipelined: the layer set-up of step k+N (rotations, fp64 eigendecomposition) runs on "
                                   "a low-priority worker stream while step k is solved; with N ranks the "
                                   "eigendecomposition of step k runs on rank k mod N and the others copy it over NVLink; "

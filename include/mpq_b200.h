@@ -130,10 +130,13 @@ int mpq_vamp_ctl_begin(void* ctl, const float* gamma1, float* gamma1_work, int B
 int mpq_vamp_ctl_round(void* ctl, int* flags, float* gamma1_work, const float* var_rowsum, int B, int n_var,
                        float factor, int final_round, void* stream);
 /* Commits a live iteration: gamma1 <- gamma1_next, gamma2_prev <- gamma2, EM update of obs from
- * mean(resid_rowsum + trace); obs_hist[it] (optional) records obs (NaN for a skipped iteration). */
+ * mean(resid_rowsum + trace); obs_hist[it] (optional) records obs, alpha1_hist[it] / alpha2_hist[it] (optional,
+ * together) the row means of alpha1 and alpha2 (the reference's alpha1_mean / alpha2_mean terms,
+ * mpq/solver.py:1064-1065); NaN for a skipped iteration. */
 int mpq_vamp_ctl_commit(void* ctl, float* gamma1, const float* gamma1_next, float* gamma2_prev, const float* gamma2,
                         const float* resid_rowsum, const float* trace, int B, int R, int em_active, double em_damping,
-                        double em_min, double em_max, double* obs_hist, int it, void* stream);
+                        double em_min, double em_max, double* obs_hist, const float* alpha1, const float* alpha2,
+                        double* alpha1_hist, double* alpha2_hist, int it, void* stream);
 /* Best-iterate test and state copies of the scalar loop (mpq/solver.py:668-699); decision[0] = 1 improved, 0 stopped
  * (r1, gamma1, obs restored), -1 skipped. */
 int mpq_vamp_ctl_best(void* ctl, const float* err_cur, int B, int n, double* best_mean, double* best_obs,
@@ -273,6 +276,14 @@ int mpq_gemm_tf32x3_noalloc(int M, int N, int K, float alpha, const float* A, in
  * per block with scale = absmax of the centre block unless pscale (B x nb) is given. */
 /* Factorized posterior mean x1 (B x n), per-block variance, MAP index / values and the per-row variance sum.
  * Replaces mpq/priors/e8p12.py:815-968 (vamp_vector_discrete_mmse_e8p12, _branch_factorized_stats :169-308). */
+/* Posterior diagnostics per 8-block (need_stats / return_{logZ,margin,entropy}_blocks): log-partition over the
+ * 512 (branch, abs) components, entropy -sum w log w + sum w H_sign and the gap between the two largest
+ * best / second-best sign-pattern log-scores; outputs B x nb with leading dimension ld.  Replaces
+ * mpq/priors/e8p12.py:292-306 and :945-960 (all components evaluated, no pruning). */
+int mpq_e8p12_stats(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                    int64_t ld_s, const float* gamma, float prior_tau, int B, int nb, const float* base_abs,
+                    const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,
+                    float* logz_out, float* entropy_out, float* margin_out, int64_t ld, void* stream);
 int mpq_e8p12_mmse(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
                    int64_t ld_s, const float* gamma, float prior_tau, int B, int nb, const float* base_abs,
                    const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,

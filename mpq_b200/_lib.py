@@ -33,6 +33,7 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_e8p12_mmse": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, L, P, L, P, L, P, P),
     "mpq_e8p12_mmse_rows": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, I, P, P, P),
     "mpq_e8p12_map": (P, L, P, L, P, L, P, F, F, I, I, P, P, P, P, P, P, L, P, L, P),
+    "mpq_e8p12_stats": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, P, P, L, P),
     "mpq_e8p12_topk": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, I, P, P, P, P),
     "mpq_uniform_topk": (P, L, P, L, P, P, L, I, P, I, I, I, F, I, P, P, P, P),
     "mpq_topk_pick": (P, L, P, L, P, L, I, I, I, P, P, L, P, P),
@@ -82,7 +83,7 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_vamp_ctl_size": (),
     "mpq_vamp_ctl_begin": (P, P, P, I, P, P),
     "mpq_vamp_ctl_round": (P, P, P, P, I, I, F, I, P),
-    "mpq_vamp_ctl_commit": (P, P, P, P, P, P, P, I, I, I, D, D, D, P, I, P),
+    "mpq_vamp_ctl_commit": (P, P, P, P, P, P, P, I, I, I, D, D, D, P, P, P, P, P, I, P),
     "mpq_vamp_ctl_best": (P, P, I, I, P, P, P, P, P, P, P, P, P, P, P, L, I, P, P),
     "mpq_vamp_rows_ctl": (P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, F, I, P, P),
     "mpq_vamp_r2_ctl": (P, P, P, P, P, P, P, I, I, L, F, P, P),

@@ -244,7 +244,7 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     nblk = len(starts)
     # per-block statistics, read back once at the end
     b_ctl = torch.zeros(nblk, 16, device=dev, dtype=torch.int32)
-    b_hist = torch.zeros(nblk, max(iters, 1), device=dev, dtype=torch.float64)
+    b_hist = torch.zeros(nblk, 3, max(iters, 1), device=dev, dtype=torch.float64)
     b_obs_in = torch.zeros(nblk, device=dev, dtype=torch.float64)
     b_g = torch.zeros(nblk, 3, device=dev, dtype=torch.float64)
     b_pol = torch.zeros(nblk, 6, device=dev, dtype=torch.float64)
@@ -287,7 +287,7 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
             final_hat[rb].copy_(vb.vals)
             final_idx[rb].copy_(vb.idx)
             b_ctl[bi].copy_(ctl)
-            b_hist[bi, :iters].copy_(vb.st.obs_hist[:iters])
+            b_hist[bi, :, :iters].copy_(vb.st.hist[:, :iters])
             b_obs_in[bi:bi + 1].copy_(vb.obs_in)
             b_g[bi].copy_(vb.gstats)
             ev = torch.cuda.Event()
@@ -317,7 +317,7 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     out: List[Dict[str, Any]] = []
     for bi, r0 in enumerate(starts):
         rows = min(r0 + B, m) - r0
-        cst = vamp_ctl_stats(ctl_h[bi], hist_h[bi], iters)
+        cst = vamp_ctl_stats(ctl_h[bi], hist_h[bi][0], iters, hist_h[bi][1], hist_h[bi][2])
         if cst["fail"]:
             raise RuntimeError(f"alpha1 invalid: expected all in ({ALPHA_EPS}, 1-{ALPHA_EPS}).")
         gain, err_mean, changed, acc, evals, fails = pol_h[bi]
@@ -339,7 +339,11 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
             "obs_precision_initial": float(obs_in_h[bi]), "obs_precision_final": cst["obs"],
             "obs_precision_mean": float(sum(obs_vals) / len(obs_vals)) if obs_vals else cst["obs"],
             "alpha1_retry_count": cst["alpha1_retry_count"], "alpha2_clip_count": cst["alpha2_clip_count"],
-            "gamma2_invalid_count": cst["gamma2_invalid_count"], "polish_sweeps": sweeps, "polish_mode": polish_mode,
+            "gamma2_invalid_count": cst["gamma2_invalid_count"], "alpha1_mean": cst["alpha1_mean"],
+            "alpha2_mean": cst["alpha2_mean"], "mean_entropy": 0.0, "mean_margin": 0.0,
+            "compile_prior": bool(getattr(cfg, "compile_prior", True)),
+            "blocks_per_chunk": int(getattr(cfg, "blocks_per_chunk", 16)), "topk_k": int(getattr(cfg, "topk_k", 16)),
+            "polish_sweeps": sweeps, "polish_mode": polish_mode,
             "polish_metric": _resolve_e8p12_polish_metric(str(cfg.polish_metric or "gram")),
             "polish_gain": float(gain), "polish_updates": float(pol.get("accepted_updates", 0.0)),
             "polish_trace": pol, "best_iterate_enabled": False, "best_iter": -1, "stop_iter": -1,

@@ -467,6 +467,173 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
 }
 
 
+// ---- posterior diagnostics (mpq/priors/e8p12.py:292-306, :945-960; need_stats) ----
+// Per item: logZ = logsumexp of the 512 component log-weights; entropy = -sum w log w + sum w H_sign(component)
+// with H_sign = max(logZ_sign - sum_k a_k m_k, 0) (m_k the component's sign means); margin = the gap between the
+// two largest of the 1024 log-scores {best, second-best parity-valid sign pattern} of the components.  All 512
+// components are evaluated (no pruning): these are diagnostics, off the solve's path.  One warp per item; the
+// per-coordinate table is the posterior kernel's (correctly rounded tanh and its log).
+__global__ void __launch_bounds__(kWarps * 32) k_e8p12_stats(E8Args a, E8Tab tab, float* __restrict__ logz_out,
+                                                             float* __restrict__ ent_out, float* __restrict__ mar_out,
+                                                             int64_t ld) {
+  __shared__ uint2 s_off[256];
+  __shared__ float s_sqn[256];
+  __shared__ int s_par[256];
+  __shared__ ItemTab s_tab[kWarps];
+  __shared__ int s_bad;
+  const bool bad = stage_abs_patterns(tab, s_off, s_sqn, s_par, &s_bad);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t it = (int64_t)blockIdx.x * kWarps + warp;
+  if (it >= (int64_t)a.B * a.nb) return;
+  const int b = (int)(it / a.nb), k = (int)(it % a.nb);
+  if (bad) {
+    if (lane == 0) {
+      logz_out[b * ld + k] = __int_as_float(0x7fc00000);
+      ent_out[b * ld + k] = __int_as_float(0x7fc00000);
+      mar_out[b * ld + k] = __int_as_float(0x7fc00000);
+    }
+    return;
+  }
+  float y[8], g, g1;
+  fold_item(a, b, k, y, g, g1);
+  const float ng = fmul(-0.5f, g);
+  float ynorm[2];
+  #pragma unroll
+  for (int br = 0; br < 2; ++br) {
+    const float off = br ? -0.25f : 0.25f;
+    float yn = 0.f;
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) yn = fadd(yn, fmul(fsub(y[i], off), fsub(y[i], off)));
+    ynorm[br] = yn;
+  }
+  ItemTab& T = s_tab[warp];
+  for (int e = lane; e < 48; e += 32) {
+    const int br = e / 24, r = e - br * 24, kk = r / 3, m = r - kk * 3;
+    float yk = y[0];
+    #pragma unroll
+    for (int i = 1; i < 8; ++i) yk = (kk == i) ? y[i] : yk;
+    const float off = br ? -0.25f : 0.25f;
+    const float mag = 0.5f + (float)m;
+    const float av = fmul(fmul(g, fsub(yk, off)), mag);
+    const float aa = fabsf(av);
+    const float Tv = aa + log1pf(expf(-2.f * aa));
+    const float ti = fminf(fmaxf((float)tanh((double)av), -0.99999988079071044921875f), 0.99999988079071044921875f);
+    T.pt[br][r] = make_float4(Tv, canon_sign(ti), (float)log((double)fmaxf(fabsf(ti), 1e-7f)), mag);
+    T.am[br][r] = make_float2(canon_sign(av), Tv);
+  }
+  __syncwarp();
+  float mx = -INFINITY, S = 0.f, SL = 0.f, SE = 0.f;  // online softmax: sum w, sum w (lc - mx), sum w H_sign
+  float t1 = -INFINITY, t2 = -INFINITY;             // the lane's two largest log-scores
+  for (int j = 0; j < 16; ++j) {
+    const int c = j * 32 + lane, br = c >> 8, ai = c & 255;
+    const uint2 of = s_off[ai];
+    const char* bp = reinterpret_cast<const char*>(T.pt[br]);
+    const char* ba = reinterpret_cast<const char*>(T.am[br]);
+    float logC = 0.f, lpt = 0.f, t[8], av[8];
+    unsigned sx = 0;
+    int nneg = 0;
+    #pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
+      const float4 v = *reinterpret_cast<const float4*>(bp + 2u * byte);
+      logC = fadd(logC, v.x);
+      t[kk] = v.y;
+      sx ^= __float_as_uint(v.y);
+      lpt = fadd(lpt, v.z);
+      av[kk] = reinterpret_cast<const float2*>(ba + byte)->x;
+      nneg += av[kk] < 0.f ? 1 : 0;
+    }
+    const bool negp = (sx >> 31) != 0u, even = s_par[ai] == 0;
+    const float pabs = expf(lpt);
+    const float prod = negp ? -pabs : pabs;
+    const float lae = log1pf(pabs);
+    const float l1me = lpt < -kLn2 ? log1pf(-pabs) : logf(-expm1f(lpt));
+    const float lzs = fsub(fadd(logC, even ? (negp ? l1me : lae) : (negp ? lae : l1me)), kLn2);
+    const float cst = fmul(ng, fadd(br ? ynorm[1] : ynorm[0], s_sqn[ai]));
+    const float lc = fadd(cst, lzs);
+    // sign means and the component's sign entropy
+    float de = fadd(1.f, prod), dodd = fsub(1.f, prod);
+    if (!(fabsf(de) > 1e-12f)) de = 1.f;
+    if (!(fabsf(dodd) > 1e-12f)) dodd = 1.f;
+    float pre[8], acc = 1.f;
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) { pre[i] = acc; acc = fmul(acc, t[i]); }
+    float suf = 1.f, am[8];
+    #pragma unroll
+    for (int i = 7; i >= 0; --i) {
+      const float ex = fmul(pre[i], suf);
+      float smv = even ? fdiv(fadd(t[i], ex), de) : fdiv(fsub(t[i], ex), dodd);
+      if (!isfinite(smv)) smv = 0.f;
+      am[i] = fmul(av[i], smv);
+      suf = fmul(suf, t[i]);
+    }
+    float asum = 0.f;
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) asum = fadd(asum, am[i]);
+    const float hs = isfinite(lzs) ? fmaxf(fsub(lzs, asum), 0.f) : 0.f;
+    // best and second-best parity-valid sign patterns of the component
+    float sum_abs = 0.f, m1 = INFINITY, m2 = INFINITY;
+    int p1 = 0;
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = fabsf(av[i]);
+      sum_abs = fadd(sum_abs, x);
+      if (x < m1) { m1 = x; p1 = i; }
+    }
+    #pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i != p1) m2 = fminf(m2, fabsf(av[i]));
+    const bool mismatch = (nneg & 1) != s_par[ai];
+    const float bl = mismatch ? fsub(sum_abs, fmul(2.f, m1)) : sum_abs;
+    const float sl = mismatch ? fsub(sum_abs, fmul(2.f, m2)) : fsub(sum_abs, fmul(2.f, fadd(m1, m2)));
+    const float sc1 = fadd(cst, bl), sc2 = fadd(cst, sl);
+    if (sc1 > t1) { t2 = t1; t1 = sc1; } else if (sc1 > t2) { t2 = sc1; }
+    if (sc2 > t1) { t2 = t1; t1 = sc2; } else if (sc2 > t2) { t2 = sc2; }
+    if (lc == lc && lc > -INFINITY) {
+      if (lc > mx) {
+        const float sc = (mx == -INFINITY) ? 0.f : expf(mx - lc);
+        SL = sc * (SL + S * (mx == -INFINITY ? 0.f : (mx - lc)));
+        S *= sc;
+        SE *= sc;
+        mx = lc;
+      }
+      const float w = expf(lc - mx);
+      S += w;
+      SL += w * (lc - mx);
+      SE += w * hs;
+    }
+  }
+  // merge the lanes (fixed butterfly order)
+  float M = mx;
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (mx > -INFINITY) {
+    const float sc = expf(mx - M);
+    SL = sc * (SL + S * (mx - M));
+    S *= sc;
+    SE *= sc;
+  } else {
+    S = SL = SE = 0.f;
+  }
+  S = warp_sum(S);
+  SL = warp_sum(SL);
+  SE = warp_sum(SE);
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float o1 = __shfl_xor_sync(0xffffffffu, t1, o), o2 = __shfl_xor_sync(0xffffffffu, t2, o);
+    const float n1 = fmaxf(t1, o1);
+    const float n2 = fmaxf(fminf(t1, o1), fmaxf(t2, o2));
+    t1 = n1;
+    t2 = n2;
+  }
+  if (lane == 0) {
+    const float ls = logf(S);
+    logz_out[b * ld + k] = M + ls;
+    ent_out[b * ld + k] = ls - SL / S + SE / S;
+    mar_out[b * ld + k] = t1 - t2;
+  }
+}
+
 // ---- top-k candidates (mpq/priors/e8p12.py:367-449 with need_stats, :453-538) ----
 // Per item and (branch, abs pattern): the best parity-valid sign pattern (flip the first minimum of |a| on a parity
 // mismatch) and the second best (mismatch: flip the second minimum instead; match: flip both minima), scored
@@ -698,6 +865,24 @@ MPQ_API int mpq_e8p12_mmse_rows(const float* r1, int64_t ld_r1, const float* cen
   k_e8p12<true><<<dim3(B, chunks), kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, nullptr, 0, nullptr, 0,
                                                                            nullptr, 0, var_rowsum, rs);
   return launch_status("mpq_e8p12_mmse_rows");
+}
+
+// Posterior diagnostics per item (B x nb outputs with leading dimension ld): log-partition, entropy, margin.
+MPQ_API int mpq_e8p12_stats(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                            int64_t ld_s, const float* gamma, float prior_tau, int B, int nb, const float* base_abs,
+                            const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,
+                            float* logz_out, float* entropy_out, float* margin_out, int64_t ld, void* stream) {
+  int st = e8_check(r1, B, nb, base_abs, base_sqnorm, base_parity, idx_lut, grid);
+  if (st) return st;
+  if (B == 0 || nb == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(gamma && logz_out && entropy_out && margin_out, "mpq_e8p12_stats: gamma and the outputs are required");
+  MPQ_CHECK_ARG(ld >= nb, "mpq_e8p12_stats: ld < nb");
+  E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
+  E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
+  const int64_t items = (int64_t)B * nb;
+  k_e8p12_stats<<<(unsigned)((items + kWarps - 1) / kWarps), kWarps * 32, 0, (cudaStream_t)stream>>>(
+      a, t, logz_out, entropy_out, margin_out, ld);
+  return launch_status("mpq_e8p12_stats");
 }
 
 // MAP codeword under the folded message (fixed_gamma > 0 replaces gamma for every row, e.g. 1 with no

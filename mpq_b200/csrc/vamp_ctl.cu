@@ -79,15 +79,36 @@ __global__ void __launch_bounds__(1024) k_ctl_commit(VampCtl* ctl, float* __rest
                                                      const float* __restrict__ g2, const float* __restrict__ resid,
                                                      const float* __restrict__ trace, int B, int R, int em_active,
                                                      double em_damping, double em_min, double em_max,
-                                                     double* __restrict__ obs_hist, int it) {
+                                                     double* __restrict__ obs_hist, const float* __restrict__ a1,
+                                                     const float* __restrict__ a2, double* __restrict__ a1_hist,
+                                                     double* __restrict__ a2_hist, int it) {
   __shared__ float red[32];
   if (ctl->skip) {
-    if (threadIdx.x == 0 && obs_hist) obs_hist[it] = __longlong_as_double(0x7ff8000000000000ll);
+    if (threadIdx.x == 0) {
+      const double nan = __longlong_as_double(0x7ff8000000000000ll);
+      if (obs_hist) obs_hist[it] = nan;
+      if (a1_hist) a1_hist[it] = nan;
+      if (a2_hist) a2_hist[it] = nan;
+    }
     return;
   }
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     gamma1[b] = g1next[b];
     g2p[b] = g2[b];
+  }
+  // the iteration's mean alpha1 (accepted, clipped) and alpha2 (clipped), mpq/solver.py:1064-1065
+  if (a1_hist && a2_hist) {
+    float s1 = 0.f, s2 = 0.f;
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+      s1 += a1[b];
+      s2 += a2[b];
+    }
+    const float t1 = block_sum(s1, red);
+    const float t2 = block_sum(s2, red);
+    if (threadIdx.x == 0) {
+      a1_hist[it] = B > 0 ? (double)(t1 / (float)B) : 0.0;
+      a2_hist[it] = B > 0 ? (double)(t2 / (float)B) : 0.0;
+    }
   }
   float acc = 0.f;
   if (em_active)
@@ -208,13 +229,17 @@ MPQ_API int mpq_vamp_ctl_round(void* ctl, int* flags, float* gamma1_work, const 
 MPQ_API int mpq_vamp_ctl_commit(void* ctl, float* gamma1, const float* gamma1_next, float* gamma2_prev,
                                 const float* gamma2, const float* resid_rowsum, const float* trace, int B, int R,
                                 int em_active, double em_damping, double em_min, double em_max, double* obs_hist,
+                                const float* alpha1, const float* alpha2, double* alpha1_hist, double* alpha2_hist,
                                 int it, void* stream) {
   MPQ_CHECK_ARG(ctl, "mpq_vamp_ctl_commit: null pointer");
   MPQ_CHECK_ARG(B == 0 || (gamma1 && gamma1_next && gamma2_prev && gamma2 && resid_rowsum && trace),
                 "mpq_vamp_ctl_commit: null pointer");
+  MPQ_CHECK_ARG((alpha1_hist == nullptr) == (alpha2_hist == nullptr) &&
+                    (alpha1_hist == nullptr || B == 0 || (alpha1 && alpha2)),
+                "mpq_vamp_ctl_commit: alpha histories need both rows and both outputs");
   k_ctl_commit<<<1, 1024, 0, (cudaStream_t)stream>>>(static_cast<VampCtl*>(ctl), gamma1, gamma1_next, gamma2_prev,
                                                      gamma2, resid_rowsum, trace, B, R, em_active, em_damping, em_min,
-                                                     em_max, obs_hist, it);
+                                                     em_max, obs_hist, alpha1, alpha2, alpha1_hist, alpha2_hist, it);
   return launch_status("mpq_vamp_ctl_commit");
 }
 

@@ -104,9 +104,10 @@ def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, blocks_per_chunk: 
                                     prior_tau_scale_mode: str = "absmax", compile_prior: bool = True,
                                     return_logZ_blocks: bool = False, return_margin_blocks: bool = False,
                                     return_entropy_blocks: bool = False) -> Dict[str, Any]:
-    """mpq/priors/e8p12.py:815-968 (need_stats=False; the diagnostics entropy/margin are not computed)."""
-    if need_stats or return_logZ_blocks or return_margin_blocks or return_entropy_blocks:
-        raise NotImplementedError("E8P12 posterior diagnostics (entropy/margin/logZ) are not built")
+    """mpq/priors/e8p12.py:815-968.  need_stats / return_*_blocks add the diagnostics (per-block log-partition,
+    entropy and top-2 margin, and the means "entropy" / "margin" over the reference's item chunks) from the
+    unpruned diagnostics kernel."""
+    want_stats = bool(need_stats) or bool(return_margin_blocks) or bool(return_entropy_blocks)
     B, nb, _ = r1_blocks.shape
     r1, center, pscale, tau = _fold_args(r1_blocks, prior_center_blocks, prior_scale_blocks, prior_tau,
                                          prior_tau_scale_mode)
@@ -123,8 +124,61 @@ def vamp_vector_discrete_mmse_e8p12(*, r1_blocks, gamma1, cb, blocks_per_chunk: 
          ptr(x1), x1.stride(0), ptr(var1), var1.stride(0), ptr(idx), idx.stride(0), ptr(mvals), mvals.stride(0),
          ptr(vsum))
     alpha1 = gamma1.to(device=dev, dtype=torch.float32).reshape(B, 1) * (vsum / float(nb)).reshape(B, 1)
-    return {"x1_blocks": x1.reshape(B, nb, 8), "var1": var1, "map_idxs": idx.to(torch.int64),
-            "map_vals": mvals.reshape(B, nb, 8), "alpha1": alpha1, "entropy": 0.0, "margin": 0.0}
+    out = {"x1_blocks": x1.reshape(B, nb, 8), "var1": var1, "map_idxs": idx.to(torch.int64),
+           "map_vals": mvals.reshape(B, nb, 8), "alpha1": alpha1, "entropy": 0.0, "margin": 0.0}
+    if want_stats or return_logZ_blocks:
+        ps = posterior_stats(r1, g, cb, center=center, pscale=pscale, prior_tau=tau,
+                             blocks_per_chunk=int(blocks_per_chunk), means=want_stats)
+        if return_logZ_blocks:
+            out["logZ_blocks"] = ps["logZ_blocks"]
+        if return_margin_blocks:
+            out["margin_blocks"] = ps["margin_blocks"]
+        if return_entropy_blocks:
+            out["entropy_blocks"] = ps["entropy_blocks"]
+        if want_stats:
+            out["entropy"], out["margin"] = ps["entropy"], ps["margin"]
+    return out
+
+
+def posterior_stats(r1: torch.Tensor, gamma: torch.Tensor, cb, *, center=None, pscale=None, prior_tau: float = 0.0,
+                    blocks_per_chunk: int = 64, means: bool = True) -> Dict[str, Any]:
+    """Posterior diagnostics of a (B, n) message under the folded prior (mpq/priors/e8p12.py:292-306, :945-960):
+    logZ_blocks, entropy_blocks, margin_blocks (B x nb) and, with means, the means "entropy" / "margin" as the
+    reference forms them (per item chunk, then over the chunks)."""
+    B, n = r1.shape
+    nb = n // 8
+    dev = r1.device
+    t = factor_tables(cb, dev)
+    r1 = r1.to(torch.float32).contiguous()
+    g = gamma.reshape(B).to(device=dev, dtype=torch.float32).contiguous()
+    tau = float(prior_tau) if center is not None else 0.0
+    logz = torch.empty(B, nb, device=dev, dtype=torch.float32)
+    ent = torch.empty_like(logz)
+    mar = torch.empty_like(logz)
+    call("mpq_e8p12_stats", ptr(r1), r1.stride(0), ptr(center), center.stride(0) if center is not None else 0,
+         ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(g), tau, B, nb, *_tab_ptrs(t),
+         ptr(logz), ptr(ent), ptr(mar), nb)
+    out: Dict[str, Any] = {"logZ_blocks": logz, "entropy_blocks": ent, "margin_blocks": mar}
+    if means:
+        bpc = _stats_chunk_blocks(B, nb, int(blocks_per_chunk), dev)
+        ents = [ent[:, c:c + bpc].mean() for c in range(0, nb, bpc)]
+        mars = [mar[:, c:c + bpc].mean() for c in range(0, nb, bpc)]
+        vals = torch.stack(ents + mars).double().cpu().tolist()
+        k = len(ents)
+        out["entropy"] = float(sum(vals[:k]) / k)
+        out["margin"] = float(sum(vals[k:]) / k)
+    return out
+
+
+def _stats_chunk_blocks(B: int, nb: int, requested: int, dev: torch.device) -> int:
+    """Blocks per item chunk of the reference's posterior loop (mpq/priors/e8p12.py:67-80, CUDA branch)."""
+    requested = max(int(requested or 1), 1)
+    if nb <= requested:
+        return nb
+    total = int(torch.cuda.get_device_properties(dev).total_memory)
+    budget = min(max(total // 8, 256 * 1024 ** 2), 4 * 1024 ** 3)
+    auto = max(1, int(budget // max(B * 256 * 4 * 48, 1)))
+    return int(min(nb, max(requested, auto)))
 
 
 class GramLayer:

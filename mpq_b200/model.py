@@ -332,7 +332,8 @@ class QuipModelConfig:
     #                                       layers finish; groups whose file exists are loaded instead of solved
     fingerprint: bool = False    # sha256 of each group's W and H in the ckpt (host hashing: seconds per layer)
     block_rows: int = 128        # the adapter's chained row blocks (mpq/adapters/quip_sharp.py:28)
-    pipelined: bool = True       # set up the next group (rotations, eigendecomposition) while a group is solved
+    pipelined: bool = False      # set up the next group (rotations, eigendecomposition) while a group is solved
+    #                              (same results; on B200 the solve keeps the GPU busy, so this measured no faster)
 
 
 def _quip_group_setup(layer, mods, H, key: str, seed: int, dev) -> Dict[str, Any]:

@@ -800,7 +800,9 @@ class E8VampState:
         self.rows = {k: torch.empty(B, **f32) for k in ("var", "g1w", "a1", "eta1", "g2n", "g2", "g2p", "a2", "eta2",
                                                           "g1n", "g1next", "trace", "resid")}
         self.flags = torch.zeros(8, device=device, dtype=torch.int32)
-        self.obs_hist = torch.empty(max(iters, 1), device=device, dtype=torch.float64)
+        # per iteration: obs, mean alpha1, mean alpha2 (NaN for skipped iterations)
+        self.hist = torch.empty(3, max(iters, 1), device=device, dtype=torch.float64)
+        self.obs_hist, self.a1_hist, self.a2_hist = self.hist[0], self.hist[1], self.hist[2]
         self.chunks = _posterior_chunks(B, nb)
         self.work = torch.zeros(B * (self.chunks + 1), device=device, dtype=torch.int32)
         # row-scaled fp16 splits of the products' A operands (r2, u), written by their producers, and the split-K
@@ -868,31 +870,36 @@ def e8_vamp_device(st: E8VampState, ctl: torch.Tensor, L: E8Layer, *, Wr, hat0, 
              ptr(rows["g1n"]), B, n, st.r1.stride(0), damping, ptr(st.r2_prev) if damping < 1.0 else None, c)
         call("mpq_vamp_ctl_commit", c, ptr(st.gamma1), ptr(rows["g1next"]), ptr(rows["g2p"]), ptr(rows["g2"]),
              ptr(rows["resid"]), ptr(rows["trace"]), B, R, int(em_active), float(cfg.em_obs_precision_damping),
-             float(cfg.em_obs_precision_min), float(cfg.em_obs_precision_max), ptr(st.obs_hist), it)
+             float(cfg.em_obs_precision_min), float(cfg.em_obs_precision_max), ptr(st.obs_hist), ptr(rows["a1"]),
+             ptr(rows["a2"]), ptr(st.a1_hist), ptr(st.a2_hist), it)
 
 
-def vamp_ctl_stats(ctl_host, obs_hist_host, iters: int) -> Dict[str, Any]:
-    """Host view of a finished loop's control block (int32 numpy array of 16) and obs history."""
+def vamp_ctl_stats(ctl_host, obs_hist_host, iters: int, a1_hist_host=None, a2_hist_host=None) -> Dict[str, Any]:
+    """Host view of a finished loop's control block (int32 numpy array of 16) and per-iteration histories."""
     import numpy as np
     c = np.asarray(ctl_host, dtype=np.int32)
     obs = float(c[:2].view(np.float64)[0])
-    hist = [float(v) for v in list(obs_hist_host)[:iters] if v == v]
+    live = lambda h: [float(v) for v in list(h)[:iters] if v == v] if h is not None else []
+    hist = live(obs_hist_host)
+    a1, a2 = live(a1_hist_host), live(a2_hist_host)
     return {"obs": obs, "obs_values": hist, "fail": int(c[_CTL_FAIL]), "alpha1_retry_count": int(c[_CTL_RETRY]),
             "alpha2_clip_count": int(c[_CTL_CLIP]), "gamma2_invalid_count": int(c[_CTL_INVALID]),
-            "best_iter": int(c[_CTL_BEST]), "stop_iter": int(c[_CTL_STOP])}
+            "best_iter": int(c[_CTL_BEST]), "stop_iter": int(c[_CTL_STOP]),
+            "alpha1_mean": float(sum(a1) / len(a1)) if a1 else 0.0,
+            "alpha2_mean": float(sum(a2) / len(a2)) if a2 else 0.0}
 
 
 def _e8_host_loop(*, Wr, hat0, B, n, nb, R, iters, cfg, obs, em_active, mmse, map_state, err_of, opV, opVh, S, Y_u,
-                  tmpBR, dev):
+                  tmpBR, dev, best_iterate=True, post_stats=None):
     """The E8P12 VAMP loop with the host deciding between launches (needed for the best-iterate test,
-    mpq/solver.py:1089-1122, which restores the best iterate and stops)."""
+    mpq/solver.py:1089-1122, which restores the best iterate and stops, and for the per-iteration posterior
+    diagnostics of log_stats: post_stats(r1, gamma1_work) -> (entropy, margin) of the accepted posterior)."""
     damping = float(cfg.damping)
     f32 = dict(device=dev, dtype=torch.float32)
     r1 = hat0.clone()
     gamma1 = torch.empty(B, **f32)
     call("mpq_gamma_init", ptr(Wr), ptr(hat0), B, n, Wr.stride(0), float(cfg.gamma_start), ptr(gamma1))
 
-    best_iterate = True
     best_err_mean = float("inf")
     best_iter_idx = -1
     stop_iter_idx = -1
@@ -917,6 +924,7 @@ def _e8_host_loop(*, Wr, hat0, B, n, nb, R, iters, cfg, obs, em_active, mmse, ma
     retry_steps = max(int(cfg.gamma_retry_steps), 0)
     alpha1_retry_count = alpha2_clip_count = gamma2_invalid_count = 0
     obs_values = []
+    a1_values, a2_values, ent_values, mar_values = [], [], [], []
     for it in range(iters):
         rows["g1w"].copy_(gamma1)
         for retry_idx in range(retry_steps + 1):
@@ -939,6 +947,7 @@ def _e8_host_loop(*, Wr, hat0, B, n, nb, R, iters, cfg, obs, em_active, mmse, ma
         if fl[2] > 0 or fl[3] > 0:
             gamma2_invalid_count += 1
             continue
+        it_stats = post_stats(r1, rows["g1w"]) if post_stats is not None else None
         alpha2_clip_count += int(fl[4])
         call("mpq_vamp_r2", ptr(x1), ptr(r1), ptr(r2_prev) if (have_prev and damping < 1.0) else None, ptr(r2),
              ptr(rows["eta1"]), ptr(rows["g1w"]), ptr(rows["g2n"]), B, n, r2.stride(0), damping)
@@ -959,6 +968,11 @@ def _e8_host_loop(*, Wr, hat0, B, n, nb, R, iters, cfg, obs, em_active, mmse, ma
             beta = _log_damp_scalar(max(obs, 1e-12), beta_new, float(cfg.em_obs_precision_damping))
             obs = float(min(max(beta, float(cfg.em_obs_precision_min)), float(cfg.em_obs_precision_max)))
         obs_values.append(obs)
+        a1_values.append(float(rows["a1"].mean()))
+        a2_values.append(float(rows["a2"].mean()))
+        if it_stats is not None:
+            ent_values.append(it_stats[0])
+            mar_values.append(it_stats[1])
         if best_iterate:
             hx, _ = map_state(r1, gamma1)
             cur = float(ops.mean_rows(err_of(hx)).item())
@@ -976,8 +990,11 @@ def _e8_host_loop(*, Wr, hat0, B, n, nb, R, iters, cfg, obs, em_active, mmse, ma
                 reported_iters = it + 1
                 break
 
+    mean = lambda v: float(sum(v) / len(v)) if v else 0.0
+    extra = {"alpha1_mean": mean(a1_values), "alpha2_mean": mean(a2_values), "mean_entropy": mean(ent_values),
+             "mean_margin": mean(mar_values)}
     return (r1, gamma1, obs, obs_values, (alpha1_retry_count, alpha2_clip_count, gamma2_invalid_count), best_err_mean,
-            best_iter_idx, stop_iter_idx, reported_iters)
+            best_iter_idx, stop_iter_idx, reported_iters, extra)
 
 
 @torch.inference_mode()
@@ -1064,7 +1081,8 @@ def solve_e8p12_rankspace_vamp(
     best_iter_idx = -1
     stop_iter_idx = -1
 
-    if not best_iterate:
+    extra: Dict[str, float] = {"mean_entropy": 0.0, "mean_margin": 0.0}
+    if not best_iterate and not log_stats:
         # device-resident loop: one host synchronisation after the iterations instead of one per iteration
         L = E8Layer.__new__(E8Layer)
         L.dev, L.cb, L.R, L.tab, L._gram = dev, cb, R, tab, None
@@ -1077,21 +1095,30 @@ def solve_e8p12_rankspace_vamp(
         e8_vamp_device(st_dev, ctl, L, Wr=Wr, hat0=hat0, center=center, pscale=pscale, tau=tau, Y_u=Y_u, cfg=cfg,
                        em_active=em_active)
         r1, gamma1 = st_dev.r1, st_dev.gamma1
-        cst = vamp_ctl_stats(ctl.cpu().numpy(), st_dev.obs_hist.cpu().tolist(), iters)
+        hist_h = st_dev.hist.cpu().tolist()
+        cst = vamp_ctl_stats(ctl.cpu().numpy(), hist_h[0], iters, hist_h[1], hist_h[2])
         if cst["fail"]:
             raise RuntimeError(f"alpha1 invalid: expected all in ({ALPHA_EPS}, 1-{ALPHA_EPS}).")
         obs = cst["obs"]
         obs_values = cst["obs_values"]
+        extra.update(alpha1_mean=cst["alpha1_mean"], alpha2_mean=cst["alpha2_mean"])
         alpha1_retry_count = cst["alpha1_retry_count"]
         alpha2_clip_count = cst["alpha2_clip_count"]
         gamma2_invalid_count = cst["gamma2_invalid_count"]
         factor = max(float(cfg.gamma_retry_factor), 1.000001)
         retry_steps = max(int(cfg.gamma_retry_steps), 0)
     else:
-        r1, gamma1, obs, obs_values, counts, best_err_mean, best_iter_idx, stop_iter_idx, reported_iters = \
+        from .e8p12 import posterior_stats
+
+        def post_stats(r, g):
+            ps = posterior_stats(r, g, cb, center=center, pscale=pscale, prior_tau=tau,
+                                 blocks_per_chunk=int(cfg.blocks_per_chunk))
+            return ps["entropy"], ps["margin"]
+
+        r1, gamma1, obs, obs_values, counts, best_err_mean, best_iter_idx, stop_iter_idx, reported_iters, extra = \
             _e8_host_loop(Wr=Wr, hat0=hat0, B=B, n=n, nb=nb, R=R, iters=iters, cfg=cfg, obs=obs, em_active=em_active,
                           mmse=mmse, map_state=map_state, err_of=err_of, opV=opV, opVh=opVh, S=S, Y_u=Y_u, tmpBR=tmpBR,
-                          dev=dev)
+                          dev=dev, best_iterate=best_iterate, post_stats=post_stats if log_stats else None)
         alpha1_retry_count, alpha2_clip_count, gamma2_invalid_count = counts
         factor = max(float(cfg.gamma_retry_factor), 1.000001)
         retry_steps = max(int(cfg.gamma_retry_steps), 0)
@@ -1139,6 +1166,18 @@ def solve_e8p12_rankspace_vamp(
             debug_out["r1"] = r1.detach().cpu()
         if not bool(debug_out.get("summary_only", False)):
             debug_out["gamma1"] = gamma1.detach().cpu()
+        if bool(debug_out.get("capture_block_stats", False)):
+            # per-block diagnostics at the VAMP fixed point (mpq/solver.py:96-145)
+            from .e8p12 import posterior_stats, vamp_vector_discrete_mmse_e8p12
+            post = vamp_vector_discrete_mmse_e8p12(r1_blocks=r1.reshape(B, nb, 8), gamma1=gamma1.reshape(B, 1), cb=cb,
+                                                   blocks_per_chunk=int(cfg.blocks_per_chunk),
+                                                   prior_center_blocks=W_blocks if tau > 0.0 else None,
+                                                   prior_scale_blocks=pscale.reshape(B, nb, 1) if pscale is not None
+                                                   else None, prior_tau=tau, prior_tau_scale_mode=mode_scale,
+                                                   return_margin_blocks=True, return_entropy_blocks=True)
+            debug_out["block_stats"] = {"top2_gap": post["margin_blocks"].float().cpu(),
+                                        "entropy": post["entropy_blocks"].float().cpu(),
+                                        "cov_trace": (8.0 * post["var1"].float()).cpu()}
     stats: Dict[str, Any] = {
         "solver": "e8p12_exact_vamp",
         "module": str(module_name),
@@ -1168,5 +1207,12 @@ def solve_e8p12_rankspace_vamp(
         "stop_iter": int(stop_iter_idx),
         "best_rankspace_error_mean": float(best_err_mean) if best_iterate else 0.0,
         "rankspace_error_mean": float(ops.mean_rows(final_err).item()),
+        "alpha1_mean": float(extra.get("alpha1_mean", 0.0)),
+        "alpha2_mean": float(extra.get("alpha2_mean", 0.0)),
+        "mean_entropy": float(extra.get("mean_entropy", 0.0)),
+        "mean_margin": float(extra.get("mean_margin", 0.0)),
+        "compile_prior": bool(getattr(cfg, "compile_prior", True)),
+        "blocks_per_chunk": int(getattr(cfg, "blocks_per_chunk", 16)),
+        "topk_k": int(getattr(cfg, "topk_k", 16)),
     }
     return final_hat, final_idx, final_err, stats

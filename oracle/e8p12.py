@@ -655,3 +655,83 @@ def refine_codebook(*, Wr, Hr, cb, cfg: E8P12VampConfig, block_rows=128, jitter_
         blocks.append(st)
     return {"hatWr": hat, "Qidxs": idx, "rtn_hat": hat0, "rtn_idx": idx0, "V": V, "S": S, "Vs": Vs,
             "obs_precision_final": obs, "block_stats": blocks}
+
+
+def posterior_stats_e8p12(*, r1_blocks, gamma1, cb, prior_center_blocks=None, prior_scale_blocks=None, prior_tau=0.0,
+                          correctly_rounded=False):
+    """Posterior diagnostics of mpq/priors/e8p12.py:815-968 with need_stats (per-block log-partition, entropy and
+    top-2 log-score margin; the components' sign entropies and second-best sign patterns of :292-306).
+
+    Float32 torch CPU arithmetic in the reference's formula order.  correctly_rounded evaluates tanh and the log
+    of |tanh| in float64 and rounds once (the CUDA kernels' choice; on the fixtures' inputs it changes nothing).
+    Returns logZ_blocks, entropy_blocks, margin_blocks (B x nb) and the means entropy, margin."""
+    import torch
+    if correctly_rounded:
+        tanh = lambda x: torch.from_numpy(_cr(np.tanh, x.numpy()))
+        log = lambda x: torch.from_numpy(_cr(np.log, x.numpy()))
+    else:
+        tanh, log = torch.tanh, torch.log
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    B, nb, _ = r1_blocks.shape
+    rw, gw = _fold_prior(r1_blocks, gamma1, prior_center_blocks, prior_scale_blocks, prior_tau)
+    cache = factor_cache(cb)
+    Y = T(rw.reshape(-1, 8))
+    G = T(gw.reshape(-1, 1))
+    N = Y.shape[0]
+    base_abs = T(cache["base_abs"])
+    sqn = T(cache["base_sqnorm"])
+    par = T(cache["base_parity"])
+    even = (par == 0)[None, :]
+    comps, entr, scores = [], [], []
+    for offset in (0.25, -0.25):
+        y = Y - np.float32(offset)
+        a = (G[:, :, None] * y[:, None, :]) * base_abs[None, :, :]
+        const = np.float32(-0.5) * G * ((y * y).sum(dim=1, keepdim=True) + sqn[None, :])
+        logC = torch.logaddexp(a, -a).sum(dim=-1)
+        t = tanh(a).clamp(-1.0 + 1e-7, 1.0 - 1e-7)
+        lpt = log(t.abs().clamp_min(1e-7)).sum(dim=-1)
+        neg = ((t < 0).sum(dim=-1) & 1).bool()
+        pabs = torch.exp(lpt)
+        prod = torch.where(neg, -pabs, pabs)
+        l1me = torch.where(lpt < -LOG2, torch.log1p(-torch.exp(lpt)), torch.log(-torch.expm1(lpt)))
+        lae = torch.logaddexp(torch.zeros_like(lpt), lpt)
+        lzs = torch.where(even, logC + torch.where(neg, l1me, lae) - np.float32(LOG2),
+                          logC + torch.where(neg, lae, l1me) - np.float32(LOG2))
+        pre, acc = [], torch.ones_like(prod)
+        for k in range(8):
+            pre.append(acc)
+            acc = acc * t[:, :, k]
+        de = 1.0 + prod
+        do = 1.0 - prod
+        de = torch.where(de.abs() > 1e-12, de, torch.ones_like(de))
+        do = torch.where(do.abs() > 1e-12, do, torch.ones_like(do))
+        sm = torch.empty_like(t)
+        suf = torch.ones_like(prod)
+        for k in reversed(range(8)):
+            ex = pre[k] * suf
+            sm[:, :, k] = torch.where(even, (t[:, :, k] + ex) / de, (t[:, :, k] - ex) / do)
+            suf = suf * t[:, :, k]
+        sm = torch.nan_to_num(sm, nan=0.0, posinf=0.0, neginf=0.0)
+        sign_ent = torch.where(torch.isfinite(lzs), (lzs - (a * sm).sum(dim=-1)).clamp_min(0.0), torch.zeros_like(lzs))
+        aa = a.abs()
+        sum_abs = aa.sum(dim=-1)
+        min_abs, min_pos = aa.min(dim=-1)
+        second = aa.clone()
+        second.scatter_(-1, min_pos.unsqueeze(-1), float("inf"))
+        min2 = second.min(dim=-1).values
+        mismatch = ((a < 0).sum(dim=-1) & 1) != par[None, :]
+        best_lin = sum_abs - 2.0 * mismatch.to(torch.float32) * min_abs
+        second_lin = torch.where(mismatch, sum_abs - 2.0 * min2, sum_abs - 2.0 * (min_abs + min2))
+        comps.append(const + lzs)
+        entr.append(sign_ent)
+        scores.append(torch.stack([const + best_lin, const + second_lin], dim=-1))
+    lc = torch.stack(comps, dim=1).reshape(N, -1)
+    lz = torch.logsumexp(lc, dim=-1)
+    lw = lc - lz[:, None]
+    w = torch.exp(lw)
+    wlw = torch.where(torch.isfinite(lw), w * lw, torch.zeros_like(lw))
+    ent = -wlw.sum(dim=1) + (w * torch.stack(entr, dim=1).reshape(N, -1)).sum(dim=1)
+    top2 = torch.topk(torch.stack(scores, dim=1).reshape(N, -1), k=2, dim=-1).values
+    margin = top2[:, 0] - top2[:, 1]
+    return {"logZ_blocks": lz.view(B, nb).numpy(), "entropy_blocks": ent.view(B, nb).numpy(),
+            "margin_blocks": margin.view(B, nb).numpy(), "entropy": float(ent.mean()), "margin": float(margin.mean())}

@@ -261,6 +261,37 @@ def gen_e8p12(out):
     np.savez_compressed(out / "e8p12_prior.npz", **cases)
 
 
+def gen_e8p12_stats(out):
+    """The posterior's diagnostics (need_stats): per-block log-partition, entropy and top-2 log-score margin."""
+    from mpq.priors.e8p12 import vamp_vector_discrete_mmse_e8p12, prior_scale_from_center
+    cb = _reference_codebook()
+    g = torch.Generator().manual_seed(33)
+    cases = {}
+    B, nb = 6, 24
+    W = torch.randn(B, nb, 8, generator=g) * 0.8
+    r1 = W + torch.randn(B, nb, 8, generator=g) * 0.3
+    ps = prior_scale_from_center(W, "absmax")
+    gams = {"lo": torch.rand(B, 1, generator=g) * 4 + 0.5, "hi": torch.rand(B, 1, generator=g) * 40 + 10,
+            "snap": torch.full((B, 1), 1500.0)}
+    for name, gam in gams.items():
+        for tau in (0.0, 0.25):
+            post = vamp_vector_discrete_mmse_e8p12(r1_blocks=r1, gamma1=gam, cb=cb, blocks_per_chunk=nb,
+                                                   need_stats=True, prior_center_blocks=W if tau else None,
+                                                   prior_scale_blocks=ps if tau else None, prior_tau=tau,
+                                                   compile_prior=False, return_logZ_blocks=True,
+                                                   return_margin_blocks=True, return_entropy_blocks=True)
+            key = f"{name}_t{int(tau * 100)}"
+            for k in ("logZ_blocks", "margin_blocks", "entropy_blocks", "x1_blocks", "var1"):
+                cases[f"{key}/{k}"] = _np(post[k])
+            cases[f"{key}/entropy"] = np.array(post["entropy"])
+            cases[f"{key}/margin"] = np.array(post["margin"])
+        cases[f"{name}/gamma"] = _np(gam)
+    cases["r1"] = _np(r1)
+    cases["W"] = _np(W)
+    cases["ps"] = _np(ps)
+    np.savez_compressed(out / "e8p12_stats.npz", **cases)
+
+
 def gen_e8p12_layer(out):
     from mpq.adapters.quip_sharp import mpq_refine_codebook
     cb = _reference_codebook()
@@ -512,7 +543,8 @@ def gen_postprocess(out):
 GENERATORS = {"uniform_denoise": gen_uniform_denoise, "linear": gen_linear, "scalar_cd": gen_scalar_cd,
               "scalar_layer": gen_scalar_layer, "rotation": gen_rotation, "e8p12": gen_e8p12,
               "e8p12_layer": gen_e8p12_layer, "block_cd": gen_block_cd, "topk": gen_topk,
-              "postprocess": gen_postprocess, "e8p12_topk_layer": gen_e8p12_topk_layer, "awq": gen_awq}
+              "postprocess": gen_postprocess, "e8p12_topk_layer": gen_e8p12_topk_layer, "awq": gen_awq,
+              "e8p12_stats": gen_e8p12_stats}
 
 
 def main():

@@ -300,3 +300,58 @@ def test_solvers_topk_polish_wrapper(cuda_dev, ocb, pcb):
         cfg=PS.E8P12VampConfig(iters=6, polish_mode="topk_block_cd", topk_k=5), **kw)
     assert torch.equal(idx_a, idx_b) and torch.equal(err_a, err_b)
     assert st["polish_mode"] == "topk_block_cd"
+
+
+@pytest.mark.gpu
+def test_e8p12_posterior_diagnostics_match_reference(cuda_dev, golden_dir, pcb, ocb):
+    """need_stats / return_*_blocks of vamp_vector_discrete_mmse_e8p12 against the reference's own run and the
+    oracle: per-block log-partition, entropy and top-2 margin, and the chunk means."""
+    from mpq_b200 import e8p12 as PE
+    z = np.load(golden_dir / "e8p12_stats.npz")
+    d = lambda a: _t(a, cuda_dev)
+    for name in ("lo", "hi", "snap"):
+        for tau in (0, 25):
+            key = f"{name}_t{tau}"
+            kw = dict(prior_center_blocks=d(z["W"]), prior_scale_blocks=d(z["ps"])) if tau else {}
+            post = PE.vamp_vector_discrete_mmse_e8p12(r1_blocks=d(z["r1"]), gamma1=d(z[f"{name}/gamma"]), cb=pcb,
+                                                      blocks_per_chunk=z["r1"].shape[1], need_stats=True,
+                                                      prior_tau=tau / 100, return_logZ_blocks=True,
+                                                      return_margin_blocks=True, return_entropy_blocks=True, **kw)
+            orc = OE.posterior_stats_e8p12(r1_blocks=z["r1"], gamma1=z[f"{name}/gamma"], cb=ocb,
+                                           prior_center_blocks=z["W"] if tau else None,
+                                           prior_scale_blocks=z["ps"] if tau else None, prior_tau=tau / 100)
+            for k in ("logZ_blocks", "entropy_blocks", "margin_blocks"):
+                got = post[k].cpu().numpy()
+                # Log-partition and margin agree in every block.  The entropy's sign-mean term divides by 1 +- prod
+                # (~1e-6 for components whose |tanh| is near 1), which amplifies the last bit of the float32 sum of
+                # log|tanh| over the 8 coordinates; the kernel and torch add those 8 terms in different orders, so a
+                # few entropy blocks differ.
+                for want, who in ((z[f"{key}/{k}"], "reference"), (orc[k], "oracle")):
+                    close = np.isclose(got, want, rtol=2e-4, atol=2e-4)
+                    assert close.mean() >= (0.95 if k == "entropy_blocks" else 1.0), (key, k, who, close.mean())
+            assert abs(post["margin"] - float(z[f"{key}/margin"])) <= 2e-4 * max(1.0, abs(float(z[f"{key}/margin"])))
+            want = float(z[f"{key}/entropy"])
+            assert abs(post["entropy"] - want) <= 5e-3 * max(1.0, abs(want)), (key, post["entropy"], want)
+
+
+@pytest.mark.gpu
+def test_e8p12_log_stats_loop_matches_device_loop(cuda_dev, ocb, pcb):
+    """log_stats=True runs the host-decided loop with the per-iteration diagnostics; the codes equal the
+    device-resident loop's, and the reference's stats keys are filled."""
+    from mpq_b200 import solver as PS
+    W, H, V, S, Vs = _layer(16, 128, 5)
+    d = lambda a: _t(a, cuda_dev)
+    hat0, _ = OE.rtn_init(W, ocb)
+    cfg = PS.E8P12VampConfig(iters=6, prior_tau=0.25, polish_sweeps=1)
+    outs = []
+    for log_stats in (False, True):
+        outs.append(PS.solve_e8p12_rankspace_vamp(Wr=d(W), hatWr_init=d(hat0), cb=pcb, V=d(V),
+                                                  Vh=d(np.ascontiguousarray(V.T)), S=d(S), Vs=d(Vs), cfg=cfg,
+                                                  log_stats=log_stats))
+    (h0, i0, _, s0), (h1, i1, _, s1) = outs
+    assert torch.equal(i0, i1)
+    assert s0["obs_precision_final"] == pytest.approx(s1["obs_precision_final"], rel=1e-6)
+    assert s0["alpha1_mean"] == pytest.approx(s1["alpha1_mean"], rel=1e-5)
+    assert s0["alpha2_mean"] == pytest.approx(s1["alpha2_mean"], rel=1e-5)
+    assert 0.0 < s1["alpha1_mean"] < 1.0 and 0.0 < s1["alpha2_mean"] < 1.0
+    assert s0["mean_entropy"] == 0.0 and s1["mean_entropy"] > 0.0 and s1["mean_margin"] > 0.0

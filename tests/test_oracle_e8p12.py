@@ -164,3 +164,18 @@ def test_e8p12_layer_case_a_second_block_is_set_by_a_diverging_row(golden_dir, c
     H = g("H")
     l0, l1 = OL.proxy_loss(g("Wr"), base["hatWr"], H), OL.proxy_loss(g("Wr"), pert["hatWr"], H)
     assert abs(l1 - l0) <= 0.005 * l0, (l0, l1)
+
+
+def test_posterior_stats_match_reference(golden_dir, cb):
+    """Posterior diagnostics (need_stats) against the reference run on the same inputs."""
+    z = np.load(golden_dir / "e8p12_stats.npz")
+    for name in ("lo", "hi", "snap"):
+        for tau in (0, 25):
+            key = f"{name}_t{tau}"
+            got = E.posterior_stats_e8p12(r1_blocks=z["r1"], gamma1=z[f"{name}/gamma"], cb=cb,
+                                          prior_center_blocks=z["W"] if tau else None,
+                                          prior_scale_blocks=z["ps"] if tau else None, prior_tau=tau / 100)
+            for k in ("logZ_blocks", "entropy_blocks", "margin_blocks"):
+                np.testing.assert_allclose(got[k], z[f"{key}/{k}"], rtol=1e-4, atol=1e-4, err_msg=f"{key}/{k}")
+            assert abs(got["entropy"] - float(z[f"{key}/entropy"])) <= 1e-4 * max(1.0, abs(float(z[f"{key}/entropy"])))
+            assert abs(got["margin"] - float(z[f"{key}/margin"])) <= 1e-4 * max(1.0, abs(float(z[f"{key}/margin"])))
