@@ -151,3 +151,46 @@ def save_quip_config(out_dir, model, quant_args: Dict) -> None:
                                 "adapter_name": "llama_like_dense_decoder"}})
     torch.save({"quant_args": dict(quant_args), "model_config": cfg, "adapter_name": "llama_like_dense_decoder"},
                os.path.join(out_dir, "config.pt"))
+
+
+def apply_quip_ckpt(model, ckpt_dir, cb=None) -> int:
+    """Write every quantized group of a QUIP# ckpt directory into ``model`` (decoded dense weights) and load the
+    saved layernorms (mpq/quip_generic.py apply_quantized_ckpt_to_model, the step before hfize's save).
+    Returns the number of groups applied."""
+    import os
+    from .codebook import E8P12_codebook
+    from .model import QUIP_GROUPS, _quip_load_group
+    cb = cb or E8P12_codebook()
+    layers = model.model.layers
+    applied = 0
+    with torch.inference_mode():
+        for li, layer in enumerate(layers):
+            for name, mods in QUIP_GROUPS:
+                if os.path.exists(os.path.join(ckpt_dir, f"{li}_{name}.pt")):
+                    _quip_load_group(str(ckpt_dir), f"{li}_{name}", layer, mods, cb, True)
+                    applied += 1
+            ln = os.path.join(ckpt_dir, f"{li}_layernorm.pt")
+            if os.path.exists(ln):
+                payload = torch.load(ln, map_location="cpu", weights_only=False)
+                for key in ("input_layernorm", "post_attention_layernorm"):
+                    w = getattr(layer, key).weight
+                    w.copy_(payload[key].to(device=w.device, dtype=w.dtype))
+    return applied
+
+
+def export_dense_hf_from_ckpt(quantized_path, hf_output_path, model=None, cb=None):
+    """A dense Hugging Face model from a QUIP# ckpt directory (mpq/quip_generic.py:1047-1069): the float model named
+    by ``config.pt`` (or the given ``model``; with no network a local checkpoint or an in-memory model is
+    needed), every group's decoded E8P12 weights applied, then ``save_pretrained``."""
+    import os
+    saved = torch.load(os.path.join(quantized_path, "config.pt"), map_location="cpu", weights_only=False)
+    if model is None:
+        from transformers import AutoModelForCausalLM
+        mc = saved["model_config"]
+        model = AutoModelForCausalLM.from_pretrained(mc._name_or_path, torch_dtype="auto", low_cpu_mem_usage=True,
+                                                     config=mc)
+    n = apply_quip_ckpt(model, quantized_path, cb=cb)
+    if n == 0:
+        raise ValueError(f"no quantized groups found in {quantized_path}")
+    model.save_pretrained(str(hf_output_path), safe_serialization=True)
+    return model

@@ -90,6 +90,7 @@ class ModelQuantConfig:
     keep_codes: bool = False     # gather q_int / scale / zero of every linear to the host
     export_gptq: bool = False    # also pack them into GPTQ v1 tensors (qweight / qzeros / scales / g_idx)
     checkpoint_dir: Optional[str] = None  # per-layer resume state: layer_<i>.pt after each layer; done layers load
+    keep_inputs: bool = False    # keep every linear's solve inputs (float W, its Hessian) on the host (checking)
 
 
 def _world(group=None) -> Tuple[int, int]:
@@ -232,6 +233,7 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
                         secs, st = 0.0, {}
                 with timer("gather"):
                     Qa = gather_rows(Q.to(W.dtype).contiguous(), row_shards(rows, world, 128), group=group)
+                    inputs = {"W": W.float().cpu(), "H": Hs[name].float().cpu()} if cfg.keep_inputs else None
                     W.copy_(Qa)
                     lr = max(r1 - r0, 1)
                     entry = {"rows": rows, "cols": W.shape[1], "rows_local": (r0, r1), "solve_s": secs,
@@ -248,6 +250,8 @@ def quantize_model(model, calib_ids: torch.Tensor, cfg: ModelQuantConfig, *, gro
                         if cfg.export_gptq:
                             from .export import pack_gptq
                             entry["gptq"] = {k: v.cpu() for k, v in pack_gptq(qa, sa, za, g_idx, int(cfg.bits)).items()}
+                    if inputs is not None:
+                        entry["inputs"] = inputs
                     results[full] = entry
             del sums, Hs
         if cfg.checkpoint_dir and rank == 0:
@@ -332,6 +336,7 @@ class QuipModelConfig:
     #                                       layers finish; groups whose file exists are loaded instead of solved
     fingerprint: bool = False    # sha256 of each group's W and H in the ckpt (host hashing: seconds per layer)
     block_rows: int = 128        # the adapter's chained row blocks (mpq/adapters/quip_sharp.py:28)
+    keep_inputs: bool = False    # keep every group's solve inputs (rotated unit-RMS W, rotated H) on the host
     pipelined: bool = False      # set up the next group (rotations, eigendecomposition) while a group is solved
     #                              (same results; on B200 the solve keeps the GPU busy, so this measured no faster)
 
@@ -482,6 +487,8 @@ def quantize_model_quip(model, calib_ids: torch.Tensor, cfg: QuipModelConfig, *,
                 if not cfg.keep_attrs:
                     for k in ("Qidxs", "SU", "SV"):
                         entry.pop(k, None)
+                if cfg.keep_inputs:
+                    entry["inputs"] = {"Wn": Wn.cpu(), "Hr": P["Hr"].cpu()}
                 attrs[key] = entry
                 del P
     finally:

@@ -190,9 +190,9 @@ def quantize(model, output_dir, config: Optional[QuantizationConfig] = None, *, 
         res = quantize_model_quip(m, ids, qcfg, group=group)
         payload["groups"] = res["groups"]
         if resolved.save and rank == 0:
-            from .export import save_quip_config
+            from .export import export_dense_hf_from_ckpt, save_quip_config
             save_quip_config(ckpt, m, asdict(resolved))
-            m.save_pretrained(out / "hf")
+            export_dense_hf_from_ckpt(ckpt, out / "hf", model=m)  # hfize: the dense model from the ckpt
             paths = {"quantized_dir": str(ckpt), "hf_dir": str(out / "hf")}
         payload["artifact_format"] = {"native": "quip_ckpt (unpacked Qidxs)", "hf": "huggingface_dense"}
     else:

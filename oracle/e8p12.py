@@ -623,8 +623,11 @@ def rtn_init(Wr, cb):
     return vals.reshape(m, n).astype(f32), idx.reshape(m, n // 8)
 
 
-def refine_codebook(*, Wr, Hr, cb, cfg: E8P12VampConfig, block_rows=128, jitter_base=1e-6, eigen_floor_scale=1e-6):
-    """mpq/adapters/quip_sharp.py:396-878 for the default recipe (mpq_init=rtn, solver=vamp, block_cd)."""
+def refine_codebook(*, Wr, Hr, cb, cfg: E8P12VampConfig, block_rows=128, jitter_base=1e-6, eigen_floor_scale=1e-6,
+                    max_blocks=None):
+    """mpq/adapters/quip_sharp.py:396-878 for the default recipe (mpq_init=rtn, solver=vamp, block_cd).
+    max_blocks: solve only the first row blocks of the chain (the obs-precision warm start is still the layer's);
+    the other rows keep their RTN codes."""
     from .layer import vamp_hessian_eigen
     m, n = Wr.shape
     hat0, idx0 = rtn_init(Wr, cb)
@@ -644,7 +647,9 @@ def refine_codebook(*, Wr, Hr, cb, cfg: E8P12VampConfig, block_rows=128, jitter_
     idx = idx0.copy()
     blocks = []
     mcache = {}
-    for r0 in range(0, m, block_rows):
+    for bi, r0 in enumerate(range(0, m, block_rows)):
+        if max_blocks is not None and bi >= int(max_blocks):
+            break
         rb = slice(r0, min(r0 + block_rows, m))
         h, i, e, st = solve_e8p12_rankspace_vamp(Wr=Wr[rb], hatWr_init=hat0[rb], cb=cb, V=V, Vh=Vh, S=S, Vs=Vs,
                                                  cfg=cfg, obs_precision_init=obs, metric_cache=mcache)
