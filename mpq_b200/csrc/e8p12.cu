@@ -168,7 +168,7 @@ __device__ __forceinline__ bool stage_abs_patterns(const E8Tab& tab, uint2* s_of
 }
 
 template <bool MMSE>
-__global__ void __launch_bounds__(kWarps * 32, 3)
+__global__ void __launch_bounds__(kWarps * 32, 4)
 k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __restrict__ var_out, int64_t ld_v,
         int* __restrict__ idx_out, int64_t ld_i, float* __restrict__ map_out, int64_t ld_m,
         float* __restrict__ var_rowsum, RowSplit rs) {

@@ -721,9 +721,10 @@ def vamp_ctl_reset(ctl: torch.Tensor) -> None:
     ctl[_CTL_BEST:_CTL_STOP + 1].fill_(-1)
 
 
-def _posterior_chunks(B: int, nb: int, slots: int = 148 * 3) -> int:
-    """Item chunks per row of the posterior launch (CTA slots: 148 SMs x 3 resident CTAs).  Rows alone fill the GPU
-    from about two waves up; below that, the chunk count whose last wave is fullest (>= 32 items per chunk)."""
+def _posterior_chunks(B: int, nb: int, slots: int = 148 * 4) -> int:
+    """Item chunks per row of the posterior launch (CTA slots: 148 SMs x 4 resident CTAs of k_e8p12<1>).  Rows alone
+    fill the GPU from about two waves up; below that, the chunk count whose last wave is fullest (>= 32 items per
+    chunk)."""
     if B <= 0 or B >= 2 * slots:
         return 1
     best, best_eff = 1, 0.0
