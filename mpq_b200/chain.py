@@ -234,7 +234,7 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     L.load(V=V, Vh=Vh, S=S, Vs=Vs)
     pscale_all = (prior_scale_from_center(Wr.reshape(m, nb, 8), mode_scale).reshape(m, nb).contiguous()
                   if tau > 0.0 else None)
-    Y_u_all = ops.mm_nt(Wr, L.opVsT, precision="fp32")  # FP32 FMA chains, all rows at once (rows are independent)
+    Y_u_all = ops.mm_nt(Wr, L.opVsT)  # FP32-faithful split product, all rows at once (rows are independent)
     obs0 = float(cfg.obs_precision) if float(cfg.obs_precision) > 0.0 else float(obs_init)
     vamp_ctl_reset(ctl)
     ctl.view(torch.float64)[0:1].fill_(obs0)

@@ -207,9 +207,9 @@ class _UniformCtx:
         self.opVh = ops.Operand(Vh)      # r2 @ V                ==  r2 @ Vh^T
         self.opVsT = ops.Operand(self.VsT)  # x @ Vs
         self.opVs = ops.Operand(Vs)      # residual_u @ Vs^T
-        # Y_u anchors every residual of the solve; it is computed once with FP32 FMA chains (the tensor
-        # core's FP32 accumulation is ~10x coarser and the greedy CD order is sensitive to it)
-        self.Y_u = ops.mm_nt(W, self.opVsT, precision="fp32")
+        # Y_u anchors every residual of the solve: one FP32-faithful split product (the solve's parity tests at
+        # 4096 columns hold with it; a single-pass TF32 product would not be faithful enough)
+        self.Y_u = ops.mm_nt(W, self.opVsT)
 
     def err(self, x, out=None, tmp=None):
         C = ops.mm_nt(x, self.opVsT, tmp)
@@ -1046,7 +1046,7 @@ def solve_e8p12_rankspace_vamp(
     opV, opVh = ops.Operand(V), ops.Operand(Vh)
     VsT = Vs.t().contiguous()
     opVs, opVsT = ops.Operand(Vs), ops.Operand(VsT)
-    Y_u = ops.mm_nt(Wr, opVsT, precision="fp32")  # computed once with FP32 FMA chains (see _UniformCtx)
+    Y_u = ops.mm_nt(Wr, opVsT)  # FP32-faithful split product, once per solve
     tmpBR = torch.empty(B, R, **f32)
 
     def err_of(x, out=None):
