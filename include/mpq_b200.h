@@ -136,7 +136,10 @@ int mpq_vamp_ctl_round(void* ctl, int* flags, float* gamma1_work, const float* v
 int mpq_vamp_ctl_commit(void* ctl, float* gamma1, const float* gamma1_next, float* gamma2_prev, const float* gamma2,
                         const float* resid_rowsum, const float* trace, int B, int R, int em_active, double em_damping,
                         double em_min, double em_max, double* obs_hist, const float* alpha1, const float* alpha2,
-                        double* alpha1_hist, double* alpha2_hist, int it, void* stream);
+                        double* alpha1_hist, double* alpha2_hist, int it, float* gamma1_work_next, int* flags_next,
+                        void* stream);
+/* gamma1_work_next / flags_next (optional, together): the commit also opens the next iteration (mpq_vamp_ctl_begin's
+ * work), saving a launch per iteration. */
 /* Best-iterate test and state copies of the scalar loop (mpq/solver.py:668-699); decision[0] = 1 improved, 0 stopped
  * (r1, gamma1, obs restored), -1 skipped. */
 int mpq_vamp_ctl_best(void* ctl, const float* err_cur, int B, int n, double* best_mean, double* best_obs,
@@ -147,6 +150,13 @@ int mpq_vamp_rows_ctl(const float* var_rowsum, float* gamma1, float* gamma1_work
                       float* gamma2_new, float* gamma2, const float* gamma2_prev, float* alpha2, float* eta2,
                       float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int B, int n,
                       int n_var, int R, float damping, int final_retry, const void* ctl, void* stream);
+/* mpq_vamp_rows_ctl and the end of the retry round (mpq_vamp_ctl_round) in one launch: the last row CTA to finish
+ * takes the round's decision.  counter: caller-owned device word, zero before the first launch and left at zero. */
+int mpq_vamp_rows_round_ctl(const float* var_rowsum, float* gamma1, float* gamma1_work, float* alpha1, float* eta1,
+                            float* gamma2_new, float* gamma2, const float* gamma2_prev, float* alpha2, float* eta2,
+                            float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int B,
+                            int n, int n_var, int R, float damping, int final_retry, void* ctl, float factor,
+                            unsigned* counter, void* stream);
 int mpq_vamp_r2_ctl(const float* x1, const float* r1, const float* r2_prev, float* r2, const float* eta1,
                     const float* gamma1_work, const float* gamma2_new, int B, int n, int64_t ld, float damping,
                     const void* ctl, void* stream);

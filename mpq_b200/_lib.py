@@ -83,9 +83,10 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_vamp_ctl_size": (),
     "mpq_vamp_ctl_begin": (P, P, P, I, P, P),
     "mpq_vamp_ctl_round": (P, P, P, P, I, I, F, I, P),
-    "mpq_vamp_ctl_commit": (P, P, P, P, P, P, P, I, I, I, D, D, D, P, P, P, P, P, I, P),
+    "mpq_vamp_ctl_commit": (P, P, P, P, P, P, P, I, I, I, D, D, D, P, P, P, P, P, I, P, P, P),
     "mpq_vamp_ctl_best": (P, P, I, I, P, P, P, P, P, P, P, P, P, P, P, L, I, P, P),
     "mpq_vamp_rows_ctl": (P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, F, I, P, P),
+    "mpq_vamp_rows_round_ctl": (P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, F, I, P, F, P, P),
     "mpq_vamp_r2_ctl": (P, P, P, P, P, P, P, I, I, L, F, P, P),
     "mpq_linear_epilogue_ctl": (P, P, P, P, I, I, L, P, P, P, P),
     "mpq_vamp_r1_ctl": (P, P, P, P, P, P, I, I, L, F, P, P, P),

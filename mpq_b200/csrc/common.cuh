@@ -41,6 +41,39 @@ struct VampCtl {
 };
 static_assert(sizeof(VampCtl) == 64, "VampCtl layout");
 
+// End of a retry round of the device-controlled VAMP iteration (mpq/solver.py:575-596), by one thread: all alpha1
+// valid -> close the round; last round -> record a non-finite alpha1 and close; otherwise count the invalid rows and
+// rescale their work precision (divide where alpha1 <= eps, multiply where alpha1 >= 1 - eps) for the next round.
+// When the round closes, the invalid-gamma2 test (:598-604) decides whether the iteration continues.  `flags` is read
+// through volatile loads: the row CTAs set it with atomics before the caller observed their arrival.
+__device__ inline void ctl_round_serial(VampCtl* ctl, int* flags, float* g1w, const float* var_rowsum, int B,
+                                        int n_var, float factor, int final_round) {
+  if (!ctl->active) return;
+  volatile int* vf = flags;
+  const int f0 = vf[0];
+  if (f0 == 0 || final_round) {
+    if (f0 != 0 && vf[1] > 0) ctl->fail = 1;
+    ctl->active = 0;
+    if (vf[2] > 0 || vf[3] > 0) {
+      ctl->gamma2_invalid_count += 1;
+      ctl->skip = 1;
+    } else {
+      ctl->alpha2_clip_count += vf[4];
+    }
+    return;
+  }
+  ctl->alpha1_retry_count += f0;
+  for (int i = 0; i < 8; ++i) vf[i] = 0;
+  const volatile float* vv = var_rowsum;
+  for (int b = 0; b < B; ++b) {
+    float g = g1w[b];
+    const float a = __fmul_rn(g, __fdiv_rn(vv[b], (float)n_var));
+    if (a <= 1e-7f) g = __fdiv_rn(g, factor);
+    if (a >= 0.99999988079071044921875f) g = __fmul_rn(g, factor);
+    g1w[b] = fmaxf(g, 1e-12f);
+  }
+}
+
 inline int launch_status(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

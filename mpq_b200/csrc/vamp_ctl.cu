@@ -19,6 +19,20 @@ namespace mpq {
 constexpr float kAlphaEpsC = 1e-7f;
 constexpr float kOneMinusAlphaEpsC = 0.99999988079071044921875f;
 
+// Start of an iteration by one CTA (k_ctl_begin's work, also done at the end of the previous commit).
+__device__ inline void ctl_begin_body(VampCtl* ctl, const float* __restrict__ gamma1, float* __restrict__ g1w, int B,
+                                      int* __restrict__ flags) {
+  const bool stopped = ctl->stopped != 0;
+  if (!stopped)
+    for (int b = threadIdx.x; b < B; b += blockDim.x) g1w[b] = gamma1[b];
+  __syncthreads();  // every thread has read `stopped` before thread 0 changes the block
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 8; ++i) flags[i] = 0;
+    ctl->active = stopped ? 0 : 1;
+    ctl->skip = stopped ? 1 : 0;
+  }
+}
+
 // Start of an iteration: gamma1_work = gamma1, flags cleared, the retry round opened unless the loop stopped.
 __global__ void k_ctl_begin(VampCtl* ctl, const float* __restrict__ gamma1, float* __restrict__ g1w, int B,
                             int* __restrict__ flags) {
@@ -81,7 +95,8 @@ __global__ void __launch_bounds__(1024) k_ctl_commit(VampCtl* ctl, float* __rest
                                                      double em_damping, double em_min, double em_max,
                                                      double* __restrict__ obs_hist, const float* __restrict__ a1,
                                                      const float* __restrict__ a2, double* __restrict__ a1_hist,
-                                                     double* __restrict__ a2_hist, int it) {
+                                                     double* __restrict__ a2_hist, int it,
+                                                     float* __restrict__ g1w_next, int* __restrict__ flags_next) {
   __shared__ float red[32];
   if (ctl->skip) {
     if (threadIdx.x == 0) {
@@ -90,6 +105,7 @@ __global__ void __launch_bounds__(1024) k_ctl_commit(VampCtl* ctl, float* __rest
       if (a1_hist) a1_hist[it] = nan;
       if (a2_hist) a2_hist[it] = nan;
     }
+    if (g1w_next) ctl_begin_body(ctl, gamma1, g1w_next, B, flags_next);
     return;
   }
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
@@ -134,6 +150,10 @@ __global__ void __launch_bounds__(1024) k_ctl_commit(VampCtl* ctl, float* __rest
     ctl->have_prev = 1;
     ctl->committed += 1;
     if (obs_hist) obs_hist[it] = obs;
+  }
+  if (g1w_next) {
+    __syncthreads();  // gamma1 of every row and the control block updated
+    ctl_begin_body(ctl, gamma1, g1w_next, B, flags_next);
   }
 }
 
@@ -230,16 +250,19 @@ MPQ_API int mpq_vamp_ctl_commit(void* ctl, float* gamma1, const float* gamma1_ne
                                 const float* gamma2, const float* resid_rowsum, const float* trace, int B, int R,
                                 int em_active, double em_damping, double em_min, double em_max, double* obs_hist,
                                 const float* alpha1, const float* alpha2, double* alpha1_hist, double* alpha2_hist,
-                                int it, void* stream) {
+                                int it, float* gamma1_work_next, int* flags_next, void* stream) {
   MPQ_CHECK_ARG(ctl, "mpq_vamp_ctl_commit: null pointer");
   MPQ_CHECK_ARG(B == 0 || (gamma1 && gamma1_next && gamma2_prev && gamma2 && resid_rowsum && trace),
                 "mpq_vamp_ctl_commit: null pointer");
+  MPQ_CHECK_ARG((gamma1_work_next == nullptr) == (flags_next == nullptr),
+                "mpq_vamp_ctl_commit: the next iteration's gamma1_work and flags go together");
   MPQ_CHECK_ARG((alpha1_hist == nullptr) == (alpha2_hist == nullptr) &&
                     (alpha1_hist == nullptr || B == 0 || (alpha1 && alpha2)),
                 "mpq_vamp_ctl_commit: alpha histories need both rows and both outputs");
   k_ctl_commit<<<1, 1024, 0, (cudaStream_t)stream>>>(static_cast<VampCtl*>(ctl), gamma1, gamma1_next, gamma2_prev,
                                                      gamma2, resid_rowsum, trace, B, R, em_active, em_damping, em_min,
-                                                     em_max, obs_hist, alpha1, alpha2, alpha1_hist, alpha2_hist, it);
+                                                     em_max, obs_hist, alpha1, alpha2, alpha1_hist, alpha2_hist, it,
+                                                     gamma1_work_next, flags_next);
   return launch_status("mpq_vamp_ctl_commit");
 }
 

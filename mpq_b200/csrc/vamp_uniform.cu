@@ -48,9 +48,17 @@ constexpr int kRowThreads = 128;
 
 // ctl (optional): device-side control -- the launch does nothing unless a retry round is open, obs is read from the
 // control block, and gamma2_prev is used only once an iteration has been committed.
+// Optional fused end of the retry round: the last row CTA to finish takes the round's decision (ctl_round_serial).
+struct RoundCtl {
+  VampCtl* ctl;          // the control block (writable)
+  unsigned* counter;     // arrival counter, zero between launches
+  float factor;
+  int n_var;
+};
+
 __global__ void __launch_bounds__(kRowThreads) k_vamp_rows(RowState st, const float* __restrict__ S, int B, int n,
                                                           int n_var, int R, float obs, float damping, int final_retry,
-                                                          const VampCtl* __restrict__ ctl) {
+                                                          const VampCtl* __restrict__ ctl, RoundCtl rc) {
   __shared__ float red[2][kRowThreads / 32];
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -116,6 +124,14 @@ __global__ void __launch_bounds__(kRowThreads) k_vamp_rows(RowState st, const fl
   if (!precision_valid(g2n)) atomicAdd(&st.flags[2], 1);
   if (!precision_valid(g2)) atomicAdd(&st.flags[3], 1);
   if (!alpha_valid(a2_raw)) atomicAdd(&st.flags[4], 1);
+  if (rc.counter) {
+    __threadfence();  // this row's flags and outputs before its arrival
+    if (atomicAdd(rc.counter, 1u) == (unsigned)(B - 1)) {
+      __threadfence();
+      ctl_round_serial(rc.ctl, st.flags, st.gamma1_work, st.var_rowsum, B, rc.n_var, rc.factor, final_retry);
+      *rc.counter = 0u;
+    }
+  }
 }
 
 // gamma retry (mpq/solver.py:593-596): divide/multiply the work precision of invalid rows.
@@ -403,7 +419,8 @@ MPQ_API int mpq_vamp_rows(const float* var_rowsum, float* gamma1, float* gamma1_
   RowState st{var_rowsum, gamma1, gamma1_work, alpha1, eta1, gamma2_new, gamma2, gamma2_prev,
               alpha2, eta2, gamma1_new, gamma1_next, trace, flags};
   MPQ_CHECK_ARG(n_var >= 1, "mpq_vamp_rows: n_var must be >= 1");
-  k_vamp_rows<<<B, kRowThreads, 0, (cudaStream_t)stream>>>(st, S, B, n, n_var, R, obs, damping, final_retry, nullptr);
+  k_vamp_rows<<<B, kRowThreads, 0, (cudaStream_t)stream>>>(st, S, B, n, n_var, R, obs, damping, final_retry, nullptr,
+                                                            RoundCtl{});
   return launch_status("mpq_vamp_rows");
 }
 
@@ -421,8 +438,29 @@ MPQ_API int mpq_vamp_rows_ctl(const float* var_rowsum, float* gamma1, float* gam
   RowState st{var_rowsum, gamma1, gamma1_work, alpha1, eta1, gamma2_new, gamma2, damping < 1.f ? gamma2_prev : nullptr,
               alpha2, eta2, gamma1_new, gamma1_next, trace, flags};
   k_vamp_rows<<<B, kRowThreads, 0, (cudaStream_t)stream>>>(st, S, B, n, n_var, R, 0.f, damping, final_retry,
-                                                            static_cast<const VampCtl*>(ctl));
+                                                            static_cast<const VampCtl*>(ctl), RoundCtl{});
   return launch_status("mpq_vamp_rows_ctl");
+}
+
+// mpq_vamp_rows_ctl followed by the end of the retry round (mpq_vamp_ctl_round), taken by the last row CTA to
+// finish: one launch per round.  counter: caller-owned device word, zero before the first launch (every launch
+// leaves it at zero).
+MPQ_API int mpq_vamp_rows_round_ctl(const float* var_rowsum, float* gamma1, float* gamma1_work, float* alpha1,
+                                    float* eta1, float* gamma2_new, float* gamma2, const float* gamma2_prev,
+                                    float* alpha2, float* eta2, float* gamma1_new, float* gamma1_next, float* trace,
+                                    int* flags, const float* S, int B, int n, int n_var, int R, float damping,
+                                    int final_retry, void* ctl, float factor, unsigned* counter, void* stream) {
+  MPQ_CHECK_ARG(var_rowsum && gamma1 && gamma1_work && alpha1 && eta1 && gamma2_new && gamma2 && gamma2_prev &&
+                    alpha2 && eta2 && gamma1_new && gamma1_next && trace && flags && S && ctl && counter,
+                "mpq_vamp_rows_round_ctl: null pointer");
+  MPQ_CHECK_ARG(n_var >= 1, "mpq_vamp_rows_round_ctl: n_var must be >= 1");
+  if (B == 0) return MPQ_OK;
+  RowState st{var_rowsum, gamma1, gamma1_work, alpha1, eta1, gamma2_new, gamma2, damping < 1.f ? gamma2_prev : nullptr,
+              alpha2, eta2, gamma1_new, gamma1_next, trace, flags};
+  RoundCtl rc{static_cast<VampCtl*>(ctl), counter, factor, n_var};
+  k_vamp_rows<<<B, kRowThreads, 0, (cudaStream_t)stream>>>(st, S, B, n, n_var, R, 0.f, damping, final_retry,
+                                                            static_cast<const VampCtl*>(ctl), rc);
+  return launch_status("mpq_vamp_rows_round_ctl");
 }
 
 MPQ_API int mpq_gamma_retry(float* gamma1_work, const float* var_rowsum, int B, int n, float factor, void* stream) {

@@ -801,6 +801,7 @@ class E8VampState:
         self.rows = {k: torch.empty(B, **f32) for k in ("var", "g1w", "a1", "eta1", "g2n", "g2", "g2p", "a2", "eta2",
                                                           "g1n", "g1next", "trace", "resid")}
         self.flags = torch.zeros(8, device=device, dtype=torch.int32)
+        self.round_counter = torch.zeros(1, device=device, dtype=torch.int32)  # the fused row stage's arrivals
         # per iteration: obs, mean alpha1, mean alpha2 (NaN for skipped iterations)
         self.hist = torch.empty(3, max(iters, 1), device=device, dtype=torch.float64)
         self.obs_hist, self.a1_hist, self.a2_hist = self.hist[0], self.hist[1], self.hist[2]
@@ -832,8 +833,10 @@ def e8_vamp_device(st: E8VampState, ctl: torch.Tensor, L: E8Layer, *, Wr, hat0, 
     st.r1.copy_(hat0)
     call("mpq_gamma_init", ptr(Wr), ptr(hat0), B, n, Wr.stride(0), float(cfg.gamma_start), ptr(st.gamma1))
     tabs = L.tab_ptrs()
-    for it in range(max(int(cfg.iters), 0)):
-        call("mpq_vamp_ctl_begin", c, ptr(st.gamma1), ptr(rows["g1w"]), B, ptr(flags))
+    iters = max(int(cfg.iters), 0)
+    for it in range(iters):
+        if it == 0:  # later iterations are opened by the previous commit
+            call("mpq_vamp_ctl_begin", c, ptr(st.gamma1), ptr(rows["g1w"]), B, ptr(flags))
         for rnd in range(retry_steps + 1):
             final = int(rnd >= retry_steps)
             # retry rounds usually do nothing (the device skips them): only the first round's launch is timed
@@ -844,11 +847,10 @@ def e8_vamp_device(st: E8VampState, ctl: torch.Tensor, L: E8Layer, *, Wr, hat0, 
             trace.end_timing("e8p12_mmse" if rnd == 0 else "e8p12_mmse_retry", tok,
                              4.0 * B * n * (3 if center is not None else 2) + 8.0 * B
                              + (4.0 * B * nb if pscale is not None else 0.0))
-            call("mpq_vamp_rows_ctl", ptr(rows["var"]), ptr(st.gamma1), ptr(rows["g1w"]), ptr(rows["a1"]),
+            call("mpq_vamp_rows_round_ctl", ptr(rows["var"]), ptr(st.gamma1), ptr(rows["g1w"]), ptr(rows["a1"]),
                  ptr(rows["eta1"]), ptr(rows["g2n"]), ptr(rows["g2"]), ptr(rows["g2p"]), ptr(rows["a2"]),
                  ptr(rows["eta2"]), ptr(rows["g1n"]), ptr(rows["g1next"]), ptr(rows["trace"]), ptr(flags), ptr(L.S), B,
-                 n, nb, R, damping, final, c)
-            call("mpq_vamp_ctl_round", c, ptr(flags), ptr(rows["g1w"]), ptr(rows["var"]), B, nb, factor, final)
+                 n, nb, R, damping, final, c, factor, ptr(st.round_counter))
         # r2 and its fp16 split -> P = r2 V (partial planes) -> linear epilogue (adds the planes, writes u split)
         # -> D = u V^T (partial planes) -> r1 update (adds the planes)
         call("mpq_vamp_r2_split_ctl", ptr(st.x1), ptr(st.r1), ptr(st.r2_prev), ptr(st.r2), ptr(rows["eta1"]),
@@ -872,7 +874,8 @@ def e8_vamp_device(st: E8VampState, ctl: torch.Tensor, L: E8Layer, *, Wr, hat0, 
         call("mpq_vamp_ctl_commit", c, ptr(st.gamma1), ptr(rows["g1next"]), ptr(rows["g2p"]), ptr(rows["g2"]),
              ptr(rows["resid"]), ptr(rows["trace"]), B, R, int(em_active), float(cfg.em_obs_precision_damping),
              float(cfg.em_obs_precision_min), float(cfg.em_obs_precision_max), ptr(st.obs_hist), ptr(rows["a1"]),
-             ptr(rows["a2"]), ptr(st.a1_hist), ptr(st.a2_hist), it)
+             ptr(rows["a2"]), ptr(st.a1_hist), ptr(st.a2_hist), it,
+             ptr(rows["g1w"]) if it + 1 < iters else None, ptr(flags) if it + 1 < iters else None)
 
 
 def vamp_ctl_stats(ctl_host, obs_hist_host, iters: int, a1_hist_host=None, a2_hist_host=None) -> Dict[str, Any]:
