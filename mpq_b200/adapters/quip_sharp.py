@@ -77,6 +77,18 @@ class _Surrogate:
         call("mpq_row_dot", ptr(dH), dH.stride(0), ptr(d), d.stride(0), W.shape[0], W.shape[1], ptr(out))
         return out
 
+    def chunk_means_dev(self, W, hat, block_rows) -> torch.Tensor:
+        """chunk_means without the read-back: float64 device tensor [chunk means..., overall mean]."""
+        m = W.shape[0]
+        if m == 0:
+            return torch.zeros(1, device=W.device, dtype=torch.float64)
+        s = self.rows(W, hat).double()
+        nfull = m // block_rows
+        parts = [s[:nfull * block_rows].reshape(nfull, block_rows).mean(1)] if nfull else []
+        if m % block_rows:
+            parts.append(s[nfull * block_rows:].mean().reshape(1))
+        return torch.cat(parts + [s.mean().reshape(1)])
+
     def chunk_means(self, W, hat, block_rows) -> Tuple[float, List[float]]:
         """Per-row surrogates of all rows in one product (rows are independent), then the means of the block_rows
         chunks and of all rows, read back together."""
@@ -178,16 +190,16 @@ def mpq_refine_codebook(
         zeros = torch.zeros_like(du)
         e = torch.empty(m, device=device, dtype=torch.float32)
         call("mpq_row_sqerr", ptr(du), ptr(zeros), m, R, du.stride(0), zeros.stride(0), ptr(e))
-        sum_sq = float(e.double().sum().item())
-        obs_precision = 1.0 / float(max(sum_sq / max(m * R, 1), 1e-12))
+        # kept on the device (float64, the reference's Python float arithmetic): read back with the statistics
+        obs_precision = 1.0 / torch.clamp(e.double().sum() / float(max(m * R, 1)), min=1e-12)
     vamp_cfg = _build_vamp_cfg(args, polish_mode=polish_mode)
     sur = _Surrogate(Hr)
-    exact_ldlq, exact_ldlq_chunks = sur.chunk_means(Wr, hatWr0.to(device=device, dtype=torch.float32).contiguous(),
-                                                    block_rows)
+    # the surrogate audits (:97-122) stay on the device until the end: one read-back per layer
+    ldlq_t = sur.chunk_means_dev(Wr, hatWr0.to(device=device, dtype=torch.float32).contiguous(), block_rows)
     final_hat = hat_init.clone()
     final_idx = idx_init.clone()
-    exact_before, exact_before_chunks = sur.chunk_means(Wr, hat_init, block_rows)
-    obs_block = float(obs_precision)
+    before_t = sur.chunk_means_dev(Wr, hat_init, block_rows)
+    obs_block = obs_precision
     gamma_sum, gamma_count, changed, changed_total = 0.0, 0, 0, 0
     stats_chunk: Dict[str, Any] = {}
     if chain_supported(vamp_cfg):
@@ -214,7 +226,7 @@ def mpq_refine_codebook(
             dbg: Dict[str, Any] = {"summary_only": True}
             hat_c, idx_c, _err, stats_chunk = solve_e8p12_rankspace_vamp(
                 Wr=Wr[rb], hatWr_init=final_hat[rb], cb=cb, V=V, Vh=Vh, S=S, Vs=Vs, cfg=vamp_cfg,
-                module_name=module_name, obs_precision_init=obs_block, log_stats=False, debug_out=dbg)
+                module_name=module_name, obs_precision_init=float(obs_block), log_stats=False, debug_out=dbg)
             final_hat[rb] = hat_c
             final_idx[rb] = idx_c
             if bool(vamp_cfg.em_obs_precision) and float(vamp_cfg.obs_precision) <= 0.0:
@@ -223,7 +235,19 @@ def mpq_refine_codebook(
             gamma_count += int(dbg.get("gamma1_count", 0))
             changed += int(dbg.get("changed_count", 0))
             changed_total += int(dbg.get("changed_total", 0))
-    exact_after, exact_after_chunks = sur.chunk_means(Wr, final_hat, block_rows)
+    after_t = sur.chunk_means_dev(Wr, final_hat, block_rows)
+    k = int(ldlq_t.numel())
+    host = torch.cat([ldlq_t, before_t, after_t, torch.as_tensor(obs_precision, device=device,
+                                                                 dtype=torch.float64).reshape(1)]).cpu().tolist()
+    split = lambda v: (float(v[-1]), [float(x) for x in v[:-1]])
+    exact_ldlq, exact_ldlq_chunks = split(host[:k])
+    exact_before, exact_before_chunks = split(host[k:2 * k])
+    exact_after, exact_after_chunks = split(host[2 * k:3 * k])
+    obs_precision = float(host[-1])
+    if not torch.is_tensor(obs_block):
+        obs_block = float(obs_block)
+    else:
+        obs_block = obs_precision
     violations, max_delta, max_ratio = 0, 0.0, 0.0
     for ld, mp in zip(exact_ldlq_chunks, exact_after_chunks):
         if mp > ld + 1e-8:

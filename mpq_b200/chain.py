@@ -197,7 +197,7 @@ _WARM: set = set()  # devices whose kernels have run once in this process (launc
 
 @torch.inference_mode()
 def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.Tensor, Vh: torch.Tensor,
-                      S: torch.Tensor, Vs: torch.Tensor, cfg: E8P12VampConfig, block_rows: int, obs_init: float,
+                      S: torch.Tensor, Vs: torch.Tensor, cfg: E8P12VampConfig, block_rows: int, obs_init,
                       polish_streams: int = 6, graphs: Optional[bool] = None,
                       after_enqueue: Optional[Callable[[], None]] = None
                       ) -> Tuple[torch.Tensor, torch.Tensor, List[Dict[str, Any]]]:
@@ -235,9 +235,13 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     pscale_all = (prior_scale_from_center(Wr.reshape(m, nb, 8), mode_scale).reshape(m, nb).contiguous()
                   if tau > 0.0 else None)
     Y_u_all = ops.mm_nt(Wr, L.opVsT)  # FP32-faithful split product, all rows at once (rows are independent)
-    obs0 = float(cfg.obs_precision) if float(cfg.obs_precision) > 0.0 else float(obs_init)
+    fixed_obs = float(cfg.obs_precision) > 0.0
+    obs0 = float(cfg.obs_precision) if fixed_obs else obs_init
     vamp_ctl_reset(ctl)
-    ctl.view(torch.float64)[0:1].fill_(obs0)
+    if torch.is_tensor(obs0):  # the warm start computed on the device (no host read)
+        ctl.view(torch.float64)[0:1].copy_(obs0.reshape(1).to(torch.float64))
+    else:
+        ctl.view(torch.float64)[0:1].fill_(float(obs0))
     final_hat = torch.empty_like(Wr)
     final_idx = torch.empty(m, nb, device=dev, dtype=torch.int64)
     starts = list(range(0, m, B))
@@ -276,8 +280,8 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
                 cs.capture()
             if bi > 0:
                 vamp_ctl_reset(ctl)
-                if float(cfg.obs_precision) > 0.0:
-                    ctl.view(torch.float64)[0:1].fill_(obs0)
+                if fixed_obs:
+                    ctl.view(torch.float64)[0:1].fill_(float(obs0))
             vb.W.copy_(Wr[rb])
             vb.hat0.copy_(hat_init[rb])
             vb.Y.copy_(Y_u_all[rb])
