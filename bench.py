@@ -86,10 +86,9 @@ def parse():
     ap.add_argument("--hess-dtype", default="bf16", choices=["bf16", "f32"])
     ap.add_argument("--schedule", default="auto", choices=["auto", "serial", "pipelined"],
                     help="e8p12: 'serial' sets up each step (rotations, eigendecomposition) before solving it; "
-                         "'pipelined' sets up step k+N on a worker stream while step k is solved and, with N ranks, "
-                         "computes each step's eigendecomposition on one rank and copies it to the others; 'auto' is "
-                         "pipelined with more than one GPU, serial on one (one GPU is busy through the solve, so the "
-                         "overlap gains nothing there)")
+                         "'pipelined' (= 'auto') sets up step k+N on a worker stream once step k's VAMP chain is done, "
+                         "beside its last polish work, and with N ranks computes each step's eigendecomposition on one "
+                         "rank and copies it to the others")
     ap.add_argument("--polish-mode", default="block_cd", choices=["block_cd", "topk_block_cd"],
                     help="layer workloads: the polish recipe (block_cd is the reference's default)")
     a = ap.parse_args()
@@ -381,7 +380,7 @@ def run_mpq(args):
         block_rows = min(args.block_rows if args.block_rows > 0 else 128, rows_per)
     else:
         block_rows = min(args.block_rows, rows_per) if args.block_rows > 0 else 0
-    pipelined = args.schedule == "pipelined" or (args.schedule == "auto" and world > 1)
+    pipelined = args.schedule != "serial"
     if args.workload == "e8p12":
         wl = E8Workload(dev, block_rows, SU, SV, (r0, r1), polish_mode=args.polish_mode, rank=rank, world=world,
                         pipelined=pipelined)
@@ -453,7 +452,7 @@ def run_mpq(args):
     H_host = H.cpu().pin_memory()
     h2d = W_host.numel() * 4 + H_host.numel() * 4
     d2h = 0
-    n_e2e = max(1, min(args.steps, 3))
+    n_e2e = max(1, args.steps)  # as many steps as the timed region (a pipelined schedule drains once per region)
     if hasattr(wl, "queue"):
         wl.queue(k, W_host, H_host)  # as in the timed region: the first step's set-up was queued by the step before
     if world > 1:
@@ -499,7 +498,7 @@ def run_mpq(args):
             result["schedule"] = ("serial: each step's layer set-up (rotations, fp64 eigendecomposition), then its solve"
                                   if not pipelined else
                                   "pipelined: the layer set-up of step k+N (rotations, fp64 eigendecomposition) runs on "
-                                  "a low-priority worker stream while step k is solved; with N ranks the "
+                                  "a low-priority worker stream after step k's VAMP chain, beside its polish; with N ranks the "
                                   "eigendecomposition of step k runs on rank k mod N and the others copy it over NVLink; "
                                   "the set-ups queued by the timed steps finish inside the timed region")
         if not args.no_cpu_baseline and world == 1:

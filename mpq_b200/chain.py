@@ -204,7 +204,8 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
     """Solve all rows of one E8P12 layer as the reference's serial chain of `block_rows`-row blocks.  graphs=False
     launches every kernel from the host (the same kernels and arguments as the graphs; per-launch timing works);
     None means the module default (use_graphs).  after_enqueue() runs once every block is enqueued, while the
-    device works through them (e.g. to start the next layer's set-up without competing for the host thread).
+    device works through them, with the VAMP stream current (e.g. to start the next layer's set-up after the VAMP
+    chain, beside the last polish work, without competing for the host thread).
 
     Returns (hatWr (m, n), Qidxs int64 (m, n/8), per-block stats in the keys of solve_e8p12_rankspace_vamp plus
     the adapter's mechanism sums)."""
@@ -306,14 +307,16 @@ def e8p12_layer_chain(*, Wr: torch.Tensor, hat_init: torch.Tensor, cb, V: torch.
                 final_idx[rb].copy_(pb.idx_out)
                 b_pol[bi].copy_(pb.stats)
                 b_trace[bi].copy_(pb.trace)
+        if after_enqueue is not None:
+            # called with the VAMP stream current: work it orders after the caller's stream (such as the next
+            # layer's set-up) waits for the VAMP chain only, and overlaps the last blocks' polish
+            after_enqueue()
     main.wait_stream(vs)
     for pb in cs.polish + ([tail[1]] if tail is not None else []):
         main.wait_stream(pb.stream)
     if not graphs or cs.vamp.graph is None:
         _WARM.add(dev.index)
     t_enq = time.perf_counter()
-    if after_enqueue is not None:
-        after_enqueue()
     ops.check_status(dev)  # synchronises: every block has finished
     last_timing.update(enqueue_s=t_enq - t_start, total_s=time.perf_counter() - t_start, blocks=float(nblk))
     ctl_h, hist_h, obs_in_h = b_ctl.cpu().numpy(), b_hist.cpu().tolist(), b_obs_in.cpu().tolist()
