@@ -353,6 +353,13 @@ int mpq_gram_gain(const float* rhs, int64_t ld, int B, int nb, const float* meta
 /* chunk operands for blocks order[c0:c0+Kb] (Kb <= 16): VsJ 128 x R, VsJT R x 128, Hsub 128 x 128 of Hf = Vs Vs^T. */
 int mpq_gram_gather(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order, int c0,
                     int Kb, float* VsJ, float* VsJT, float* Hsub, void* stream);
+/* mpq_gram_gather with the chunk's rows of Vs gathered from Vs's row-scaled fp16 split (vs_hi / vs_lo with leading
+ * dimension ld16, vs_inv = 1 / row scale) into j_hi / j_lo / j_inv: the split of a row depends on that row alone,
+ * so the product with the gathered split equals the product with the split of the gathered rows. */
+int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order, int c0,
+                          int Kb, const void* vs_hi, const void* vs_lo, int64_t ld16, const float* vs_inv,
+                          void* j_hi, void* j_lo, int64_t ldj16, float* j_inv, float* VsJT, float* Hsub,
+                          void* stream);
 /* Sequential block decisions of one chunk per row: target = x + rhs Ginv, exact first-minimum gram search,
  * accept test, x / idx / residual-norm updates, accepted steps delta (B x 128).  Replaces the block loop of
  * mpq/polish/block_cd.py:534-547 with _cd_gram_step_impl :212-246. */

@@ -187,20 +187,33 @@ __global__ void __launch_bounds__(256) k_gram_gain(const float* __restrict__ rhs
 
 // Chunk operands for the blocks order[c0 : c0 + Kb]:  VsJ (128 x R) = rows of Vs for the chunk's columns,
 // VsJT (R x 128) its transpose, Hsub (128 x 128) = Hf[cols, cols] with Hf = Vs Vs^T.
+// Pre-split rows of Vs (its row-scaled fp16 split: hi, lo, 1/scale) gathered like VsJ: the split of a row depends on
+// that row only, so the gathered split equals the split of the gathered rows.
+struct SplitRows {
+  const unsigned short* hi; const unsigned short* lo; int64_t ld; const float* inv;  // Vs's split (n rows)
+  unsigned short* hiJ; unsigned short* loJ; int64_t ldJ; float* invJ;                // chunk rows (128)
+};
+
 __global__ void __launch_bounds__(256) k_gram_gather(const float* __restrict__ Vs, int64_t ldv, int R,
                                                      const float* __restrict__ Hf, int64_t ldh,
                                                      const int* __restrict__ order, int c0, int Kb,
                                                      float* __restrict__ VsJ, float* __restrict__ VsJT,
-                                                     float* __restrict__ Hsub) {
+                                                     float* __restrict__ Hsub, SplitRows sp) {
   __shared__ float tile[32][33];
   const int r0 = blockIdx.x * 32, k0 = blockIdx.y * 32;  // k: chunk column 0..127
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   for (int kk = ty; kk < 32; kk += 8) {
     const int k = k0 + kk, r = r0 + tx;
     float v = 0.f;
-    if (k < Kb * 8 && r < R) v = Vs[(int64_t)(order[c0 + k / 8] * 8 + (k & 7)) * ldv + r];
+    const int64_t row = k < Kb * 8 ? (int64_t)(order[c0 + k / 8] * 8 + (k & 7)) : -1;
+    if (row >= 0 && r < R) v = Vs[row * ldv + r];
     tile[kk][tx] = v;
-    if (r < R) VsJ[(int64_t)k * R + r] = v;
+    if (VsJ && r < R) VsJ[(int64_t)k * R + r] = v;
+    if (sp.hiJ && row >= 0 && r < R) {
+      sp.hiJ[(int64_t)k * sp.ldJ + r] = sp.hi[row * sp.ld + r];
+      sp.loJ[(int64_t)k * sp.ldJ + r] = sp.lo[row * sp.ld + r];
+      if (r == 0) sp.invJ[k] = sp.inv[row];
+    }
   }
   __syncthreads();
   for (int rr = ty; rr < 32; rr += 8) {
@@ -640,8 +653,27 @@ MPQ_API int mpq_gram_gather(const float* Vs, int64_t ldv, int R, const float* Hf
   MPQ_CHECK_ARG(Vs && Hf && order && VsJ && VsJT && Hsub, "mpq_gram_gather: null pointer");
   MPQ_CHECK_ARG(Kb >= 1 && Kb <= kChunkBlocks, "mpq_gram_gather: Kb must be in [1, %d]", kChunkBlocks);
   dim3 grid((R + 31) / 32, kChunkCols / 32);
-  k_gram_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, VsJ, VsJT, Hsub);
+  k_gram_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, VsJ, VsJT, Hsub,
+                                                        SplitRows{});
   return launch_status("mpq_gram_gather");
+}
+
+// mpq_gram_gather with the chunk's rows of Vs taken from Vs's row-scaled fp16 split (vs_hi / vs_lo, leading
+// dimension ld16, vs_inv) into j_hi / j_lo (ldj16) / j_inv instead of fp32 VsJ: the product with them needs no
+// split of its own.
+MPQ_API int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order,
+                                  int c0, int Kb, const void* vs_hi, const void* vs_lo, int64_t ld16,
+                                  const float* vs_inv, void* j_hi, void* j_lo, int64_t ldj16, float* j_inv,
+                                  float* VsJT, float* Hsub, void* stream) {
+  MPQ_CHECK_ARG(Vs && Hf && order && vs_hi && vs_lo && vs_inv && j_hi && j_lo && j_inv && VsJT && Hsub,
+                "mpq_gram_gather_split: null pointer");
+  MPQ_CHECK_ARG(Kb >= 1 && Kb <= kChunkBlocks, "mpq_gram_gather_split: Kb must be in [1, %d]", kChunkBlocks);
+  MPQ_CHECK_ARG(ld16 >= R && ldj16 >= R, "mpq_gram_gather_split: fp16 leading dimensions below R");
+  dim3 grid((R + 31) / 32, kChunkCols / 32);
+  SplitRows sp{static_cast<const unsigned short*>(vs_hi), static_cast<const unsigned short*>(vs_lo), ld16, vs_inv,
+               static_cast<unsigned short*>(j_hi), static_cast<unsigned short*>(j_lo), ldj16, j_inv};
+  k_gram_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, nullptr, VsJT, Hsub, sp);
+  return launch_status("mpq_gram_gather_split");
 }
 
 MPQ_API int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* Hsub, const float* meta,

@@ -235,6 +235,12 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
     order = torch.empty(nb, device=dev, dtype=torch.int32)
     VsJ = torch.empty(128, R, device=dev, dtype=torch.float32)
     VsJT = torch.empty(R, 128, device=dev, dtype=torch.float32)
+    # the chunk's rows of Vs come pre-split from the layer's split of Vs (no split per chunk)
+    vs16 = opVs.f16 if (opVs is not None and opVs.f16 is not None and ops.gemm_precision() == "f16x3") else None
+    if vs16 is not None:
+        hiJ = torch.empty(128, vs16[0].shape[1], device=dev, dtype=torch.float16)
+        loJ = torch.empty_like(hiJ)
+        invJ = torch.empty(128, device=dev, dtype=torch.float32)
     Hsub = torch.empty(128, 128, device=dev, dtype=torch.float32)
     rhsJ = torch.empty(B, 128, device=dev, dtype=torch.float32)
     delta = torch.empty(B, 128, device=dev, dtype=torch.float32)
@@ -260,9 +266,15 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
         for c0 in range(0, nb, 16):
             Kb = min(16, nb - c0)
             kc = 8 * Kb
-            call("mpq_gram_gather", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb, ptr(VsJ),
-                 ptr(VsJT), ptr(Hsub))
-            ops.mm_nt(res_u, VsJ[:kc], out=rhsJ[:, :kc])
+            if vs16 is not None:
+                call("mpq_gram_gather_split", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb,
+                     ptr(vs16[0]), ptr(vs16[1]), vs16[0].stride(0), ptr(vs16[2]), ptr(hiJ), ptr(loJ), hiJ.stride(0),
+                     ptr(invJ), ptr(VsJT), ptr(Hsub))
+                ops.mm_nt(res_u, ops.Operand.presplit(VsJ[:kc], (hiJ[:kc], loJ[:kc], invJ[:kc])), out=rhsJ[:, :kc])
+            else:
+                call("mpq_gram_gather", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb, ptr(VsJ),
+                     ptr(VsJT), ptr(Hsub))
+                ops.mm_nt(res_u, VsJ[:kc], out=rhsJ[:, :kc])
             if n_cand:
                 call("mpq_gram_chunk_topk", ptr(x_work), x_work.stride(0), ptr(rhsJ), rhsJ.stride(0), ptr(Hsub),
                      ptr(meta), ptr(order), c0, Kb, ptr(topk_vals), ptr(topk_idx), n_cand, nb, ptr(res_norm), ptr(idx),

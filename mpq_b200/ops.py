@@ -165,6 +165,13 @@ class Operand:
         elif self.precision == "f16x3" and t.dim() == 2 and t.dtype == torch.float32:
             self.f16 = split_f16(t)
 
+    @classmethod
+    def presplit(cls, full: torch.Tensor, f16) -> "Operand":
+        """An f16x3 operand whose row-scaled split (hi, lo, inv) is already made (``full`` gives the shape only)."""
+        op = cls.__new__(cls)
+        op.full, op.precision, op.hi, op.lo, op.f16 = full, "f16x3", None, None, tuple(f16)
+        return op
+
     def reload(self, t: torch.Tensor) -> None:
         """Copy new values (same shape) into this operand's buffers and re-split them in place: products captured in a
         CUDA graph against this operand see the new matrix."""
