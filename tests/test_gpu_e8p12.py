@@ -355,3 +355,27 @@ def test_e8p12_log_stats_loop_matches_device_loop(cuda_dev, ocb, pcb):
     assert s0["alpha2_mean"] == pytest.approx(s1["alpha2_mean"], rel=1e-5)
     assert 0.0 < s1["alpha1_mean"] < 1.0 and 0.0 < s1["alpha2_mean"] < 1.0
     assert s0["mean_entropy"] == 0.0 and s1["mean_entropy"] > 0.0 and s1["mean_margin"] > 0.0
+
+
+@pytest.mark.gpu
+def test_chain_with_ragged_tail_block_matches_oracle(cuda_dev, ocb, pcb):
+    """The chained solve with a last block of fewer rows (200 rows = 128 + 72; the tail block runs eagerly with its own
+    buffers) against the oracle's chain on the same inputs: VAMP-stage codes and the full solve's proxy loss."""
+    import types
+    from mpq_b200.adapters.quip_sharp import mpq_refine_codebook
+    W, H, V, S, Vs = _layer(200, 256, 9)
+    for sweeps in (0, 2):
+        args = types.SimpleNamespace(mpq_init="rtn", mpq_iters=8, mpq_prior_tau=0.25, mpq_polish_sweeps=sweeps,
+                                     mpq_block_rows=128, quant_solver="vamp",
+                                     quant_polish_mode="block_cd" if sweeps else "none", mpq_polish_metric="gram")
+        Wd = _t(W, cuda_dev)
+        hat, idx, st = mpq_refine_codebook(Wd, _t(H, cuda_dev), Wd, torch.zeros(200, 32, dtype=torch.int64,
+                                                                             device=cuda_dev), pcb, args)
+        ref = OE.refine_codebook(Wr=W, Hr=H, cb=ocb, block_rows=128,
+                                 cfg=OE.E8P12VampConfig(iters=8, prior_tau=0.25, polish_sweeps=sweeps))
+        agree = (idx.cpu().numpy() == ref["Qidxs"]).mean()
+        l, rl = OL.proxy_loss(W, hat.cpu().numpy(), H), OL.proxy_loss(W, ref["hatWr"], H)
+        if sweeps == 0:
+            assert agree >= 0.999, agree
+            assert abs(st["obs_precision_final"] - ref["obs_precision_final"]) <= 1e-4 * ref["obs_precision_final"]
+        assert abs(l - rl) <= 0.005 * rl, (sweeps, l, rl, agree)
