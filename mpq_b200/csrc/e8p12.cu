@@ -93,13 +93,47 @@ __device__ __forceinline__ void fold_item(const E8Args& a, int b, int k, float y
 
 constexpr int kWarps = 8;  // items in flight per CTA (one warp each)
 
+// 4-byte asynchronous global -> shared copies (cp.async, cached at L1), one commit group per call site.
+__device__ __forceinline__ void async_copy4(float* dst, const float* src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
 // Per-item table of the per-(branch, coordinate k, magnitude m) values, entry e = 3 k + m.  Signs are
 // canonical (a value that is not < 0 has its sign bit clear), so the XOR of sign bits is the parity of
 // the reference's (x < 0) tests.
 struct ItemTab {
   float2 am[2][24];  // {a, T}: a = (g (y_k - off)) |b| with |b| = 1/2, 3/2, 5/2; T = |a| + log1p(exp(-2|a|))
   float4 pt[2][24];  // {T, t, lt, |b|}: t = tanh(a) clamped to +-(1 - 2^-23), lt = log(max(|t|, 1e-7))
+  float tb[24][2];   // {T of branch 0, T of branch 1} per entry: the bound pass reads both branches in one load
 };
+
+// Folded message of one item with the work spread over the warp (the posterior kernel): lane l holds
+// coordinate l & 7 of r1 (yv) and of the prior centre (cv), every lane the item's prior scale (sv, when given)
+// and the row's precision g1.  The same float32 operations as fold_item per coordinate, so the folded y and the
+// precision are bit-identical.  Every group of 8 lanes holds the item's 8 coordinates (lane l: coordinate
+// l & 7); returns the lane's coordinate of the folded y.
+__device__ __forceinline__ float fold_item_lanes(const E8Args& a, bool prior, float yv, float cv, float sv, float g1,
+                                                 float& g) {
+  float yl = yv;
+  g = g1;
+  if (prior) {
+    // max |c| over the block (fmaxf is exact in any order; a NaN entry is skipped as in the sequential scan)
+    float sc = fmaxf(0.f, fabsf(cv));
+    #pragma unroll
+    for (int o = 4; o > 0; o >>= 1) sc = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, o));
+    if (a.pscale) sc = sv;
+    sc = fmaxf(sc, 1e-12f);
+    const float t = fmul(fmaxf(a.prior_tau, 1e-12f), sc);
+    const float pp = fdiv(1.f, fmul(t, t));
+    const float gw = fadd(g1, pp);
+    yl = fdiv(fadd(fmul(g1, yv), fmul(pp, cv)), gw);
+    g = gw;
+  }
+  return yl;
+}
 
 __device__ __forceinline__ float canon_sign(float x) { return x < 0.f ? x : fabsf(x); }
 __device__ __forceinline__ unsigned sign_bit(float x) { return __float_as_uint(x) >> 31; }
@@ -180,6 +214,7 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
   __shared__ unsigned short s_list[MMSE ? kWarps : 1][512];
   __shared__ float s_ub[MMSE ? kWarps : 1][512];
   __shared__ float s_var[kWarps];
+  __shared__ float s_stage[kWarps][17];
   __shared__ int s_bad;
   if (rs.active && *rs.active == 0) return;  // device-side control: this launch is not needed
   const bool bad = stage_abs_patterns(tab, s_off, s_sqn, s_par, &s_bad);
@@ -189,9 +224,31 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
   const int k0 = (int)((int64_t)a.nb * blockIdx.y / gridDim.y), k1 = (int)((int64_t)a.nb * (blockIdx.y + 1) / gridDim.y);
   ItemTab& T = s_tab[warp];
   float vacc = 0.f;
+  // The next item's r1 (lanes 0-7), prior centre (lanes 8-15) and prior scale (lane 16) are copied into the
+  // warp's staging slot with asynchronous copies while the current item is scored, so their latency is hidden
+  // behind the item's arithmetic without holding registers.
+  const bool prior = a.prior_tau > 0.f && a.center;
+  float* stage = s_stage[warp];
+  if ((lane >= 8 && lane < 16 && !prior) || (lane == 16 && !(prior && a.pscale))) stage[lane] = 0.f;
+  auto prefetch = [&](int kn) {
+    if (kn < k1) {
+      const float* src = nullptr;
+      if (lane < 8) src = a.r1 + b * a.ld_r1 + kn * 8 + lane;
+      else if (lane < 16 && prior) src = a.center + b * a.ld_c + kn * 8 + (lane - 8);
+      else if (lane == 16 && prior && a.pscale) src = a.pscale + b * a.ld_s + kn;
+      if (src) async_copy4(stage + lane, src);
+    }
+    async_commit();
+  };
+  prefetch(k0 + warp);
   for (int k = k0 + warp; k < k1; k += kWarps) {
-    float y[8], g, g1;
-    fold_item(a, b, k, y, g, g1);
+    async_wait_all();
+    __syncwarp();
+    const float yv = stage[lane & 7], cv = stage[8 + (lane & 7)], sv = stage[16];
+    __syncwarp();
+    prefetch(k + kWarps);
+    float g;
+    const float yl = fold_item_lanes(a, prior, yv, cv, sv, a.fixed_gamma > 0.f ? a.fixed_gamma : a.gamma[b], g);
     if (bad) {  // base_abs is not an E8P12 abs table: poison the outputs
       if (lane == 0 && idx_out) idx_out[b * ld_i + k] = -1;
       if (lane < 8) {
@@ -205,23 +262,22 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
       continue;
     }
     const float ng = fmul(-0.5f, g);
-    float ynorm[2];
+    float ynorm[2] = {0.f, 0.f};
     #pragma unroll
-    for (int br = 0; br < 2; ++br) {
-      const float off = br ? -0.25f : 0.25f;
-      float yn = 0.f;
-      #pragma unroll
-      for (int i = 0; i < 8; ++i) yn = fadd(yn, fmul(fsub(y[i], off), fsub(y[i], off)));
-      ynorm[br] = yn;
+    for (int i = 0; i < 8; ++i) {
+      const float yi = __shfl_sync(0xffffffffu, yl, i);
+      ynorm[0] = fadd(ynorm[0], fmul(fsub(yi, 0.25f), fsub(yi, 0.25f)));
+      ynorm[1] = fadd(ynorm[1], fmul(fsub(yi, -0.25f), fsub(yi, -0.25f)));
     }
+    // the coordinates of the lane's table entries e = lane and e = lane + 32 (coordinate (e mod 24) / 3)
+    const float yk_a = __shfl_sync(0xffffffffu, yl, (lane < 24 ? lane : lane - 24) / 3);
+    const float yk_b = __shfl_sync(0xffffffffu, yl, min((lane + 8) / 3, 7));
     // ---- per-item table ----
     __syncwarp();
     #pragma unroll 1
     for (int e = lane; e < 48; e += 32) {
-      const int br = e / 24, r = e - br * 24, kk = r / 3, m = r - kk * 3;
-      float yk = y[0];
-      #pragma unroll
-      for (int i = 1; i < 8; ++i) yk = (kk == i) ? y[i] : yk;
+      const int br = e / 24, r = e - br * 24, m = r % 3;
+      const float yk = e < 32 ? yk_a : yk_b;
       const float off = br ? -0.25f : 0.25f;
       const float mag = 0.5f + (float)m;
       const float av = fmul(fmul(g, fsub(yk, off)), mag);
@@ -237,6 +293,7 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
         T.pt[br][r] = make_float4(Tv, canon_sign(ti), (float)log((double)fmaxf(fabsf(ti), 1e-7f)), mag);
       }
       T.am[br][r] = make_float2(canon_sign(av), Tv);
+      T.tb[r][br] = Tv;
     }
     __syncwarp();
     // Lane's components c = 32 j + lane = (branch c >> 8, abs c & 255), the reference's component order.
@@ -322,14 +379,14 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
       for (int j = 0; j < 8; ++j) {
         const int ai = (j << 5) | lane;
         const uint2 of = s_off[ai];
-        const char* base = reinterpret_cast<const char*>(T.am[0]);
+        const char* base = reinterpret_cast<const char*>(T.tb);  // 8-byte entries, as T.am[br]
         float l0 = 0.f, l1 = 0.f;
         #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const unsigned byte = __byte_perm(kk < 4 ? of.x : of.y, 0u, 0x4440u + (kk & 3));
-          const float2* e = reinterpret_cast<const float2*>(base + byte);
-          l0 = fadd(l0, e->y);
-          l1 = fadd(l1, (e + 24)->y);  // the same coordinate and magnitude in branch 1
+          const float2 v = *reinterpret_cast<const float2*>(base + byte);  // T of both branches
+          l0 = fadd(l0, v.x);
+          l1 = fadd(l1, v.y);
         }
         const float sq = s_sqn[ai];
         const float ub0 = fadd(fmul(ng, fadd(ynorm[0], sq)), l0);
@@ -425,10 +482,27 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
         W = warp_sum(W * scl);
         WOFF = warp_sum(WOFF * scl);
         SEC = warp_sum(SEC * scl);
+        // The eight coordinate sums as a reduce-scatter over the same xor-16, 8, 4, 2, 1 butterfly: at each
+        // stage a lane keeps half of its coordinates and adds its partner's values of them, so lane l ends with
+        // the full sum of coordinate (l >> 2) & 7, bit-identical to a warp_sum of that coordinate.
+        const bool h4 = (lane & 16) != 0, h3 = (lane & 8) != 0, h2 = (lane & 4) != 0;
+        float v4[4], v2[2];
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = MU[j] * scl, hi = MU[j + 4] * scl;
+          v4[j] = (h4 ? hi : lo) + __shfl_xor_sync(0xffffffffu, h4 ? lo : hi, 16);
+        }
+        #pragma unroll
+        for (int j = 0; j < 2; ++j)
+          v2[j] = (h3 ? v4[j + 2] : v4[j]) + __shfl_xor_sync(0xffffffffu, h3 ? v4[j] : v4[j + 2], 8);
+        float v1 = (h2 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, h2 ? v2[0] : v2[1], 4);
+        v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+        const float mown = (v1 + WOFF) / W;  // coordinate (lane >> 2) & 7 of the posterior mean
         float nrm = 0.f;
         #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float mi = (warp_sum(MU[i] * scl) + WOFF) / W;
+          const float mi = __shfl_sync(0xffffffffu, mown, 4 * i);
           nrm += mi * mi;
           mu_l = (lane == i) ? mi : mu_l;
         }
