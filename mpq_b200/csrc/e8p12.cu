@@ -169,7 +169,9 @@ __device__ __forceinline__ void comp_terms(const ItemTab& T, int br, int ai, uin
   const float pabs = __expf(lpt);
   o.prod = negp ? -pabs : pabs;
   const float lae = __logf(1.f + pabs);  // logaddexp(0, lpt), lpt <= 0: 1 + pabs in (1, 2]
-  const float l1me = lpt < -kLn2 ? __logf(1.f - pabs) : __logf(-expm1f(lpt));  // log(1 - exp(lpt))
+  float l1me;  // log(1 - exp(lpt)); a branch, so expm1f runs only for the lanes that need it
+  if (lpt < -kLn2) l1me = __logf(1.f - pabs);
+  else l1me = __logf(-expm1f(lpt));
   const float lop = negp ? l1me : lae;  // log(1 + prod)
   const float lom = negp ? lae : l1me;  // log(1 - prod)
   o.even = parity == 0;
@@ -417,7 +419,7 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
         const float thr = best - kPrune;
         unsigned short* list = s_list[warp];
         int cnt = 0;
-        #pragma unroll 1
+        #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const bool keep = !(s_ub[warp][j * 32 + lane] < thr);
           const unsigned msk = __ballot_sync(0xffffffffu, keep);
