@@ -263,6 +263,14 @@ int mpq_split_tf32_t(const void* x, int dtype, int64_t ldx, int tokens, int n, f
  * activations (see mpq_syrk_tc). */
 int mpq_syrk_bf16(int n, int K, float alpha, const void* A, int64_t lda, float beta, float* C, int64_t ldc, int mirror,
                   int* status, void* stream);
+/* The whole-K forms of mpq_syrk_bf16 / mpq_syrk_tc in one launch (the same H += X^T X accumulation): the tensor core
+ * accumulates `chunk` columns of K at a time (a multiple of 64 for bf16, of 32 for fp32) and each chunk is added,
+ * round to nearest, into a running sum held in tensor memory; C is read (beta != 0, lower triangle) and written once
+ * per tile, every entry also at its mirror (exactly symmetric). */
+int mpq_syrk_bf16_acc(int n, int K, float alpha, const void* A, int64_t lda, float beta, float* C, int64_t ldc,
+                      int chunk, int* status, void* stream);
+int mpq_syrk_tc_acc(int nreg, int n, int K, float alpha, const float* const* A, const float* const* B, int64_t lda,
+                    float beta, float* C, int64_t ldc, int chunk, int* status, void* stream);
 /* out[j,t] = X[t,j] for bf16 activations X (T x n): the K-major operand of mpq_syrk_bf16. */
 int mpq_transpose_bf16(const void* x, int64_t ldx, int tokens, int n, void* out, int64_t ldo, void* stream);
 /* out[j] = beta out[j] + alpha sum_t X[t,j] (the QUIP# hook's running sum of inputs, mpq/quip_generic.py:906-918). */

@@ -71,6 +71,8 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_split_tf32_t": (P, I, L, I, I, P, P, L, P),
     "mpq_col_sum": (P, I, L, I, I, F, F, P, P),
     "mpq_syrk_bf16": (I, I, F, P, L, F, P, L, I, P, P),
+    "mpq_syrk_bf16_acc": (I, I, F, P, L, F, P, L, I, P, P),
+    "mpq_syrk_tc_acc": (I, I, I, F, P, P, L, F, P, L, I, P, P),
     "mpq_transpose_bf16": (P, L, I, I, P, L, P),
     "mpq_cd_target": (P, L, P, L, I, I, P, P, P, L, P),
     "mpq_pack_bits": (P, L, L, I, I, I, I, P, L, P),

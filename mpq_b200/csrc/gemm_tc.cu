@@ -348,6 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // epilogue of one tile overlap the MMAs of the next.  Roles as above; acc_full[b] is committed by the MMA thread when
 // buffer b holds a finished tile, acc_empty[b] collects one arrival per epilogue warp when it has been drained.
 // Symmetric products enumerate only the tiles holding entries col <= row.
+//
+// Chunked accumulation (ckb > 0, no split-K): the tensor core's FP32 accumulator does not round to nearest, so a
+// long K extent is cut into chunks of ckb k-blocks.  Each chunk is accumulated in TMEM columns [0, BN) and the
+// epilogue warps add it, round to nearest, into a running sum held in TMEM columns [BN, 2 BN); the tile is written
+// to C once, after its last chunk.  The MMAs of chunk q + 1 wait only for the epilogue to have read chunk q.
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
@@ -359,6 +364,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -407,7 +423,8 @@ template <int BN, int STAGES, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc_pt(const __grid_constant__ Maps maps, int nreg, int M, int N, int K, float alpha, float beta,
                  float* __restrict__ C, int64_t ldc, int* __restrict__ status, int sym, const float* __restrict__ sa,
-                 const float* __restrict__ sb, int mt, int nt, int ntiles, int splits, float* __restrict__ ws) {
+                 const float* __restrict__ sb, int mt, int nt, int ntiles, int splits, float* __restrict__ ws,
+                 int ckb) {
   constexpr bool B16 = KIND != 0;
   constexpr uint32_t kStageA = BM * 128;
   constexpr uint32_t kStageB = BN * 128;
@@ -483,27 +500,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int g = 0, i = 0;
+      int g = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
-        const int b = i & 1;
-        const uint32_t use = (uint32_t)(i >> 1);
-        if (*abort_flag || !mbar_wait(&acc_empty[b], (use & 1u) ^ 1u)) {
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t dacc = tmem + (uint32_t)(b * BN);
-        int kb0, kb1;
-        split_range(t % splits, splits, total_kb, kb0, kb1);
+      // k-blocks [kb0, kb1) into the accumulator at dacc (the first MMA overwrites it); false on a timed-out wait
+      auto issue = [&](int kb0, int kb1, uint32_t dacc) -> bool {
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
           if (*abort_flag || !mbar_wait(&full[s], ph)) {
             *abort_flag = 1;
-            ok = false;
-            break;
+            return false;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t a_addr = smem_u32(sA + s * kStageA);
@@ -533,10 +539,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                            smem_u32(&empty[s]))
                        : "memory");
         }
-        if (!ok) break;
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                         smem_u32(&acc_full[b]))
-                     : "memory");
+        return true;
+      };
+      if (ckb > 0) {
+        // chunked accumulation: every chunk of every tile goes to the accumulator in columns [0, BN)
+        int u = 0;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+          for (int cs = 0; cs < total_kb; cs += ckb, ++u) {
+            if (*abort_flag || !mbar_wait(&acc_empty[0], ((uint32_t)u & 1u) ^ 1u)) {
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (!(ok = issue(cs, min(cs + ckb, total_kb), tmem))) break;
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_u32(&acc_full[0]))
+                         : "memory");
+          }
+        }
+      } else {
+        int i = 0;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
+          const int b = i & 1;
+          const uint32_t use = (uint32_t)(i >> 1);
+          if (*abort_flag || !mbar_wait(&acc_empty[b], (use & 1u) ^ 1u)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          int kb0, kb1;
+          split_range(t % splits, splits, total_kb, kb0, kb1);
+          if (!(ok = issue(kb0, kb1, tmem + (uint32_t)(b * BN)))) break;
+          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                           smem_u32(&acc_full[b]))
+                       : "memory");
+        }
       }
       // every MMA this thread issued has retired before teardown (bounded)
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -544,6 +583,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                    : "memory");
       mbar_wait(drain_bar, 0);
       if (!ok) atomicCAS(status, 0, 3);
+    }
+  } else if (ckb > 0) {
+    // chunked epilogue: fold each chunk into the running sum (TMEM columns [BN, 2 BN)), then write the tile
+    const int quad = warp & 3;
+    const uint32_t lanes = (uint32_t)(quad * 32) << 16;
+    const int nq = (total_kb + ckb - 1) / ckb;
+    int u = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int q = 0; q < nq; ++q, ++u) {
+        if (*abort_flag) { ok = false; break; }
+        if (!mbar_wait(&acc_full[0], (uint32_t)u & 1u)) {
+          *abort_flag = 1;
+          atomicCAS(status, 0, 4);
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        #pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lanes + (uint32_t)c0, v);
+          if (q > 0) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lanes + (uint32_t)(BN + c0), r);
+            #pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(r[e]) + __uint_as_float(v[e]));
+          }
+          tmem_st32(tmem + lanes + (uint32_t)(BN + c0), v);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[0]);  // the accumulator may take the next chunk
+      }
+      if (!ok) break;
+      int mb, nb;
+      tile_coords<BN>(t, mt, nt, sym, mb, nb);
+      const int row = mb * BM + quad * 32 + lane;
+      #pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lanes + (uint32_t)(BN + c0), v);
+        store_chunk(v, row, nb * BN, c0, M, N, alpha, beta, C, ldc, sym, sa, sb);
+      }
     }
   } else {
     // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
@@ -649,7 +733,7 @@ static int num_sms() {
 template <int BN, int STAGES, int KIND>
 static int launch_pt(const Maps& maps, int nreg, int M, int N, int K, float alpha, float beta, float* C, int64_t ldc,
                      int* status, cudaStream_t stream, int sym = 0, const float* sa = nullptr, const float* sb = nullptr,
-                     int splits = 1, float* ws = nullptr, bool reduce = true) {
+                     int splits = 1, float* ws = nullptr, bool reduce = true, int ckb = 0) {
   const size_t smem = 1024 + (size_t)STAGES * (BM + BN) * 128 + 256;
   const int ast = smem_opt_in((const void*)k_gemm_tc_pt<BN, STAGES, KIND>, smem, "mpq_gemm_tc (persistent)");
   if (ast) return ast;
@@ -662,10 +746,11 @@ static int launch_pt(const Maps& maps, int nreg, int M, int N, int K, float alph
   }
   if (ntiles == 0) return MPQ_OK;
   if (splits < 1 || !ws) splits = 1;
+  if (ckb > 0) splits = 1;  // chunked accumulation keeps each tile's whole K extent in one CTA
   const int64_t units = ntiles * splits;
   const int grid = (int)std::min<int64_t>(units, num_sms());
   k_gemm_tc_pt<BN, STAGES, KIND><<<grid, kThreads, smem, stream>>>(maps, nreg, M, N, K, alpha, beta, C, ldc, status,
-                                                                    sym, sa, sb, mt, nt, (int)units, splits, ws);
+                                                                    sym, sa, sb, mt, nt, (int)units, splits, ws, ckb);
   int st = launch_status("mpq_gemm_tc (persistent)");
   if (st || splits == 1 || !reduce) return st;
   const int64_t total = (int64_t)M * N;
@@ -751,6 +836,57 @@ MPQ_API int mpq_syrk_bf16(int n, int K, float alpha, const void* A, int64_t lda,
   st = tc::make_map(&maps.b[0], A, n, K, lda, 256, 1);
   if (st) return st;
   return tc::launch_pt<256, 4, 1>(maps, 1, n, n, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, mirror ? 1 : 2);
+}
+
+// Whole-K symmetric accumulation of a bf16 operand in one launch, C = alpha A A^T + beta C, exactly symmetric: the
+// K extent is accumulated by the tensor core in chunks of `chunk` columns (a multiple of 64) that are added, round
+// to nearest, into a running sum kept in TMEM; C is read (beta != 0, lower triangle) and written once per tile.
+MPQ_API int mpq_syrk_bf16_acc(int n, int K, float alpha, const void* A, int64_t lda, float beta, float* C,
+                              int64_t ldc, int chunk, int* status, void* stream) {
+  MPQ_CHECK_ARG(n >= 0 && K >= 1, "mpq_syrk_bf16_acc: bad shape");
+  MPQ_CHECK_ARG(chunk >= 64 && chunk % 64 == 0, "mpq_syrk_bf16_acc: chunk must be a positive multiple of 64");
+  if (n == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(A && C && status, "mpq_syrk_bf16_acc: null pointer");
+  MPQ_CHECK_ARG(lda % 8 == 0 && lda >= K && ldc >= n, "mpq_syrk_bf16_acc: lda must be a multiple of 8 and >= K, ldc >= n");
+  MPQ_CHECK_ARG(((uintptr_t)A & 15) == 0, "mpq_syrk_bf16_acc: A must be 16-byte aligned");
+  int st = tc::get_encoder();
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  st = tc::make_map(&maps.a[0], A, n, K, lda, tc::BM, 1);
+  if (st) return st;
+  st = tc::make_map(&maps.b[0], A, n, K, lda, 256, 1);
+  if (st) return st;
+  return tc::launch_pt<256, 4, 1>(maps, 1, n, n, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 1, nullptr,
+                                  nullptr, 1, nullptr, true, chunk / 64);
+}
+
+// Whole-K symmetric accumulation of fp32 operands (the 3xTF32 split, as mpq_syrk_tc) in one launch: the regions'
+// K extents are concatenated and accumulated in chunks of `chunk` columns (a multiple of 32) added, round to
+// nearest, into a running sum in TMEM; C is read and written once per tile, exactly symmetric.
+MPQ_API int mpq_syrk_tc_acc(int nreg, int n, int K, float alpha, const float* const* A, const float* const* B,
+                            int64_t lda, float beta, float* C, int64_t ldc, int chunk, int* status, void* stream) {
+  MPQ_CHECK_ARG(nreg >= 1 && nreg <= 3, "mpq_syrk_tc_acc: nreg must be 1..3");
+  MPQ_CHECK_ARG(n >= 0 && K >= 1, "mpq_syrk_tc_acc: bad shape");
+  MPQ_CHECK_ARG(chunk >= 32 && chunk % 32 == 0, "mpq_syrk_tc_acc: chunk must be a positive multiple of 32");
+  if (n == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(A && B && C && status, "mpq_syrk_tc_acc: null pointer");
+  MPQ_CHECK_ARG(lda % 4 == 0 && lda >= K && ldc >= n, "mpq_syrk_tc_acc: lda must be a multiple of 4 and >= K, ldc >= n");
+  int st = tc::get_encoder();
+  if (st) return st;
+  tc::Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  for (int r = 0; r < nreg; ++r) {
+    MPQ_CHECK_ARG(A[r] && B[r], "mpq_syrk_tc_acc: null operand %d", r);
+    MPQ_CHECK_ARG(((uintptr_t)A[r] & 15) == 0 && ((uintptr_t)B[r] & 15) == 0,
+                  "mpq_syrk_tc_acc: operands must be 16-byte aligned");
+    st = tc::make_map(&maps.a[r], A[r], n, K, lda, tc::BM);
+    if (st) return st;
+    st = tc::make_map(&maps.b[r], B[r], n, K, lda, 256);
+    if (st) return st;
+  }
+  return tc::launch_pt<256, 4, 0>(maps, nreg, n, n, K, alpha, beta, C, ldc, status, (cudaStream_t)stream, 1, nullptr,
+                                  nullptr, 1, nullptr, true, chunk / 32);
 }
 
 // FP32-faithful product on the fp16 tensor cores: C = alpha sum_{(a,b) in (hi,hi),(hi,lo),(lo,hi)} diag(sa) A_a B_b^T diag(sb)

@@ -51,9 +51,10 @@ _split_cache: dict = {}
 _bf16_cache: dict = {}
 
 # The tensor core's FP32 accumulator does not round to nearest (its error grows with the K extent of one
-# product: 1.7e-5 relative low after 4100 tokens).  Each symmetric product covers at most CHUNK_TOKENS
-# tokens and the chunks are combined by the epilogue's round-to-nearest C = beta C + alpha P, which keeps
-# H within a few 1e-6 of an FP32 FMA product.
+# accumulation: 1.7e-5 relative low after 4100 tokens).  The symmetric product accumulates at most CHUNK_TOKENS
+# tokens at a time in tensor memory and adds the chunks, round to nearest, into a running sum kept there (one
+# launch over all tokens, H read and written once per tile), which keeps H within a few 1e-6 of an FP32 FMA
+# product.
 CHUNK_TOKENS = 1024
 
 
@@ -80,27 +81,19 @@ def accumulate_xtx(H: torch.Tensor, x: torch.Tensor, *, alpha: float = 1.0, beta
             XT = _bf16_cache[key] = torch.empty(n, ld, device=H.device, dtype=torch.bfloat16)
         ld = XT.stride(0)
         call("mpq_transpose_bf16", ptr(X), X.stride(0), T, n, ptr(XT), ld)
-        for t0 in range(0, T, CHUNK_TOKENS):
-            kc = min(CHUNK_TOKENS, T - t0)
-            last = t0 + CHUNK_TOKENS >= T
-            call("mpq_syrk_bf16", n, kc, float(alpha), ptr(XT[:, t0:]), ld, float(beta) if t0 == 0 else 1.0, ptr(H),
-                 H.stride(0), 1 if last else 0, st)
+        call("mpq_syrk_bf16_acc", n, T, float(alpha), ptr(XT), ld, float(beta), ptr(H), H.stride(0), CHUNK_TOKENS, st)
         return H
     sp = _split_cache.setdefault(key, _Split())
     hi, lo, ld = sp.get(n, T, H.device, need_lo=(dtype == 0))
     call("mpq_split_tf32_t", ptr(X), dtype, X.stride(0), T, n, ptr(hi), ptr(lo), ld)
-    for t0 in range(0, T, CHUNK_TOKENS):  # hi/lo columns t0.. are the chunk's tokens (16-byte aligned)
-        kc = min(CHUNK_TOKENS, T - t0)
-        h = hi[:, t0:]
-        if dtype == 0:
-            l = lo[:, t0:]
-            As, Bs = [h, h, l], [h, l, h]
-        else:
-            As, Bs = [h], [h]
-        arrA = (_ct.c_void_p * 3)(*[t.data_ptr() for t in As])
-        arrB = (_ct.c_void_p * 3)(*[t.data_ptr() for t in Bs])
-        call("mpq_syrk_tc", len(As), n, kc, float(alpha), arrA, arrB, ld, float(beta) if t0 == 0 else 1.0, ptr(H),
-             H.stride(0), st)
+    if dtype == 0:
+        As, Bs = [hi, hi, lo], [hi, lo, hi]
+    else:
+        As, Bs = [hi], [hi]
+    arrA = (_ct.c_void_p * 3)(*[t.data_ptr() for t in As])
+    arrB = (_ct.c_void_p * 3)(*[t.data_ptr() for t in Bs])
+    call("mpq_syrk_tc_acc", len(As), n, T, float(alpha), arrA, arrB, ld, float(beta), ptr(H), H.stride(0),
+         CHUNK_TOKENS, st)
     return H
 
 

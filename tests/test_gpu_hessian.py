@@ -66,3 +66,52 @@ def test_xtx_bf16_single_product_is_exact_products(cuda_dev):
     scale = (X.double().abs().T @ X.double().abs() / T).max().item()
     assert (H.cpu().double() - want).abs().max().item() <= 1e-5 * scale
     assert torch.equal(H, H.T)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n,T,chunk", [(300, 5000, 1024), (256, 5000, 64), (520, 1100, 128)])
+def test_xtx_chunked_running_sum(cuda_dev, dtype, n, T, chunk):
+    """One launch over all tokens: chunks of `chunk` tokens accumulated on the tensor core and added, round to
+    nearest, into the running sum kept in tensor memory (many chunks per tile, ragged token and row counts,
+    beta != 0 reading the lower triangle); exactly symmetric and within FP32 accumulation of fp64."""
+    import ctypes
+    from mpq_b200._lib import call, ptr
+    X = _batches(11 + n, [(T,)], n, dtype)[0].to(cuda_dev)
+    g = torch.Generator().manual_seed(3)
+    H0 = torch.randn(n, n, generator=g)
+    H0 = (H0 + H0.T).to(cuda_dev)
+    H = H0.clone()
+    alpha, beta = 1.0 / T, 0.5
+    st = torch.zeros(1, dtype=torch.int32, device=cuda_dev)  # the launch's own status word (0: no wait timed out)
+    if dtype == torch.bfloat16:
+        ld = (T + 7) // 8 * 8
+        XT = torch.zeros(n, ld, device=cuda_dev, dtype=torch.bfloat16)
+        XT[:, :T] = X.T
+        call("mpq_syrk_bf16_acc", n, T, alpha, ptr(XT), ld, beta, ptr(H), H.stride(0), chunk, ptr(st))
+    else:
+        ld = (T + 3) // 4 * 4
+        hi = torch.zeros(n, ld, device=cuda_dev)
+        lo = torch.zeros(n, ld, device=cuda_dev)
+        call("mpq_split_tf32_t", ptr(X), 0, X.stride(0), T, n, ptr(hi), ptr(lo), ld)
+        arrA = (ctypes.c_void_p * 3)(hi.data_ptr(), hi.data_ptr(), lo.data_ptr())
+        arrB = (ctypes.c_void_p * 3)(hi.data_ptr(), lo.data_ptr(), hi.data_ptr())
+        call("mpq_syrk_tc_acc", 3, n, T, alpha, arrA, arrB, ld, beta, ptr(H), H.stride(0), chunk, ptr(st))
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    Xd = X.double().cpu()
+    want = beta * H0.double().cpu() + alpha * (Xd.T @ Xd)
+    scale = (Xd.abs().T @ Xd.abs() * alpha).max().item() + beta * H0.abs().max().item()
+    assert torch.equal(H, H.T)
+    assert (H.cpu().double() - want).abs().max().item() <= 1e-5 * scale
+
+
+@pytest.mark.gpu
+def test_xtx_chunked_rejects_bad_chunk(cuda_dev):
+    from mpq_b200._lib import call, ptr
+    n, T = 128, 256
+    XT = torch.zeros(n, T, device=cuda_dev, dtype=torch.bfloat16)
+    H = torch.zeros(n, n, device=cuda_dev)
+    st = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    with pytest.raises(RuntimeError):
+        call("mpq_syrk_bf16_acc", n, T, 1.0, ptr(XT), T, 0.0, ptr(H), n, 96, ptr(st))
