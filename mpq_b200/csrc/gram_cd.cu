@@ -350,23 +350,41 @@ __device__ int gram_search_warp(const E8Small& e8, const float t[8], const float
     }
     // the 128 codewords (a<<8)|s with parity(s) = br; their sign pattern relative to the offset comes
     // from the codebook's sign table, and the coordinates whose sign differs from y's cost 4|y_k||b_k|.
+    // Bounds first (lane: raw sign bytes s = 2 m + bit0, m = 4 lane + u, bit0 giving parity br); then one round
+    // in which every lane scores its smallest-bound codeword exactly; then the warp's best so far prunes the
+    // rest.  Whatever the order, every codeword whose bound is within the margin of the final best is scored
+    // exactly, so the result is the first minimum of the exact scores.
+    float dEu[4];
+    int u1 = 0;
     #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      // enumerate the 128 raw sign bytes of this branch: s = 2*m + bit0, bit0 chosen to give parity br
       const int m = lane * 4 + u;  // 0..127
       const int hi7 = m << 1;
-      int par7 = 0;
-      #pragma unroll
-      for (int k = 1; k < 8; ++k) par7 ^= (hi7 >> k) & 1;
-      const int s = hi7 | (par7 ^ br);
+      const int s = hi7 | ((__popc(hi7) & 1) ^ br);
       const int real = __ldg(e8.sign_id + ((a << 8) | s));
       const int diff = real ^ sgn;
       float dE = base;
       #pragma unroll
       for (int k = 0; k < 8; ++k)
         if (diff & (1 << k)) dE += w[k];
-      if (lam * dE > best + marg) continue;
-      const int c = (a << 8) | s;
+      dEu[u] = dE;
+      if (dE < dEu[u1]) u1 = u;
+    }
+    auto code_of = [&](int u) {
+      const int hi7 = (lane * 4 + u) << 1;
+      return (a << 8) | hi7 | ((__popc(hi7) & 1) ^ br);
+    };
+    if (!(lam * dEu[u1] > best + marg)) {
+      const int c = code_of(u1);
+      const float sc = exact_score(e8.grid, c, L, tl, tn);
+      ++count;
+      if (better(sc, c, best, best_c)) { best = sc; best_c = c; }
+    }
+    warp_argmin(best, best_c);
+    #pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (u == u1 || lam * dEu[u] > best + marg) continue;
+      const int c = code_of(u);
       const float sc = exact_score(e8.grid, c, L, tl, tn);
       ++count;
       if (better(sc, c, best, best_c)) { best = sc; best_c = c; }
