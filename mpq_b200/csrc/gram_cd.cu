@@ -278,12 +278,15 @@ __device__ int gram_search_warp(const E8Small& e8, const float t[8], const float
                                 int* n_exact) {
   const int lane = threadIdx.x & 31;
   float tl[8], tn = 0.f;
-  #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  {
+    // tl = t L (L lower): lane l computes coordinate l & 7 in the same order (k = j .. 7), then broadcast
+    const int j = lane & 7;
     float s = 0.f;
     #pragma unroll
-    for (int k = j; k < 8; ++k) s = fadd(s, fmul(t[k], L[k * 8 + j]));
-    tl[j] = s;
+    for (int k = 0; k < 8; ++k)
+      if (k >= j) s = fadd(s, fmul(t[k], L[k * 8 + j]));
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) tl[q] = __shfl_sync(0xffffffffu, s, q);
   }
   #pragma unroll
   for (int j = 0; j < 8; ++j) tn = fadd(tn, fmul(tl[j], tl[j]));
@@ -540,25 +543,33 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
     v1 = __ldg(reinterpret_cast<const float4*>(cp + 4));
   };
   if (reg_cand && lane < a.kc) load_cand(0, cv0, cv1);
+  // Per-block 8 x 8 algebra is spread over the lanes (lane l: coordinate l & 7, each sum in the sequential order)
+  // and broadcast.  The next block's current decision is loaded a block ahead (a decision only writes its own
+  // block).
+  const int jl = lane & 7;
+  float xb_next = a.Kb > 0 ? a.x[b * a.ldx + a.order[a.c0] * 8 + jl] : 0.f;
   for (int p = 0; p < a.Kb; ++p) {
     const int blk = a.order[a.c0 + p];
     const float* m = s_meta + p * kMeta;
     const float* G = m;
     const float* L = m + 64;
     const float* Gi = m + 128;
+    const float xb_l = xb_next;
+    if (p + 1 < a.Kb) xb_next = a.x[b * a.ldx + a.order[a.c0 + p + 1] * 8 + jl];
     float xb[8], r[8], t[8];
     #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      xb[j] = a.x[b * a.ldx + blk * 8 + j];
+      xb[j] = __shfl_sync(0xffffffffu, xb_l, j);
       r[j] = rh[p * 8 + j];
     }
     // target = x_blk + rhs @ ginv
-    #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    {
       float s = 0.f;
       #pragma unroll
-      for (int i = 0; i < 8; ++i) s = fadd(s, fmul(r[i], Gi[i * 8 + j]));
-      t[j] = fadd(xb[j], s);
+      for (int i = 0; i < 8; ++i) s = fadd(s, fmul(r[i], Gi[i * 8 + jl]));
+      const float tj = fadd(xb_l, s);
+      #pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] = __shfl_sync(0xffffffffu, tj, j);
     }
     int c;
     const float* gv;
@@ -590,12 +601,13 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
       d[j] = fsub(__ldg(gv + j), xb[j]);
       cross = fadd(cross, fmul(r[j], d[j]));
     }
-    #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    {
+      // (d G)_j on lane j & 7, then dn = sum_j (d G)_j d_j in order
       float s = 0.f;
       #pragma unroll
-      for (int i = 0; i < 8; ++i) s = fadd(s, fmul(d[i], G[i * 8 + j]));
-      dn = fadd(dn, fmul(s, d[j]));
+      for (int i = 0; i < 8; ++i) s = fadd(s, fmul(d[i], G[i * 8 + jl]));
+      #pragma unroll
+      for (int j = 0; j < 8; ++j) dn = fadd(dn, fmul(__shfl_sync(0xffffffffu, s, j), d[j]));
     }
     dn = fmaxf(dn, 0.f);
     const float cand = fmaxf(fsub(fadd(res, dn), fmul(2.f, cross)), 0.f);
