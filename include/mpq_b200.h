@@ -363,11 +363,13 @@ int mpq_gram_gather(const float* Vs, int64_t ldv, int R, const float* Hf, int64_
                     int Kb, float* VsJ, float* VsJT, float* Hsub, void* stream);
 /* mpq_gram_gather with the chunk's rows of Vs gathered from Vs's row-scaled fp16 split (vs_hi / vs_lo with leading
  * dimension ld16, vs_inv = 1 / row scale) into j_hi / j_lo / j_inv: the split of a row depends on that row alone,
- * so the product with the gathered split equals the product with the split of the gathered rows. */
+ * so the product with the gathered split equals the product with the split of the gathered rows.  With t_hi
+ * (optional; t_lo, leading dimension ldt16 >= 8 Kb, t_inv) it also writes the split of VsJT[:, :8 Kb], equal to
+ * mpq_split_f16 of that matrix. */
 int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order, int c0,
                           int Kb, const void* vs_hi, const void* vs_lo, int64_t ld16, const float* vs_inv,
                           void* j_hi, void* j_lo, int64_t ldj16, float* j_inv, float* VsJT, float* Hsub,
-                          void* stream);
+                          void* t_hi, void* t_lo, int64_t ldt16, float* t_inv, void* stream);
 /* Sequential block decisions of one chunk per row: target = x + rhs Ginv, exact first-minimum gram search,
  * accept test, x / idx / residual-norm updates, accepted steps delta (B x 128).  Replaces the block loop of
  * mpq/polish/block_cd.py:534-547 with _cd_gram_step_impl :212-246. */
@@ -375,6 +377,15 @@ int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const f
                    const int* order, int c0, int Kb, const float* base_abs, const int* base_parity, const float* grid,
                    const uint8_t* sign_id, float* res, int* idx, int64_t ldi, float* delta, int* accepted,
                    long long* evals, int B, float accept_tol, void* stream);
+/* mpq_gram_chunk reading the rhs product as `splits` split-K partial planes (plane s at rhs + s * plane, leading
+ * dimension ldr, added in plane order as the split-K reduction does) and also writing the row-scaled fp16 split of
+ * delta[:, :8 Kb] (d_hi / d_lo, leading dimension ldd; d_inv) exactly as mpq_split_f16 would: the chunk's products
+ * need no reduction or split launch of their own (same block loop, mpq/polish/block_cd.py:332-625). */
+int mpq_gram_chunk_planes(float* x, int64_t ldx, const float* rhs, int64_t ldr, int splits, int64_t plane,
+                          const float* Hsub, const float* meta, const int* order, int c0, int Kb,
+                          const float* base_abs, const int* base_parity, const float* grid, const uint8_t* sign_id,
+                          float* res, int* idx, int64_t ldi, float* delta, void* d_hi, void* d_lo, int64_t ldd,
+                          float* d_inv, int* accepted, long long* evals, int B, float accept_tol, void* stream);
 /* mpq_gram_chunk over each block's kc precomputed candidates (cand B x nb x kc x 8, 16-byte aligned; cand_idx
  * B x nb x kc codebook indices): first minimum of the metric distance.  Replaces the top-k block step
  * mpq/polish/block_cd.py:137-172 (_topk_gram_step_impl) with E8P12TopKProvider :768-860. */

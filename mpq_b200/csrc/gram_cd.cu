@@ -192,6 +192,7 @@ __global__ void __launch_bounds__(256) k_gram_gain(const float* __restrict__ rhs
 struct SplitRows {
   const unsigned short* hi; const unsigned short* lo; int64_t ld; const float* inv;  // Vs's split (n rows)
   unsigned short* hiJ; unsigned short* loJ; int64_t ldJ; float* invJ;                // chunk rows (128)
+  unsigned short* hiT; unsigned short* loT; int64_t ldT; float* invT;                // VsJT's own split (R rows)
 };
 
 __global__ void __launch_bounds__(256) k_gram_gather(const float* __restrict__ Vs, int64_t ldv, int R,
@@ -199,34 +200,58 @@ __global__ void __launch_bounds__(256) k_gram_gather(const float* __restrict__ V
                                                      const int* __restrict__ order, int c0, int Kb,
                                                      float* __restrict__ VsJ, float* __restrict__ VsJT,
                                                      float* __restrict__ Hsub, SplitRows sp) {
+  // CTA (x, y): rows r0 .. r0 + 31 of VsJT and the chunk columns k0 = 32 y, 32 (y + gridDim.y), ...; with the
+  // split of VsJT requested the grid has one column of CTAs, so each CTA holds its rows' 128 columns (tileT) and
+  // splits them as k_split_f16 splits the rows of VsJT[:, :8 Kb] (the zero columns beyond do not change a row's
+  // maximum).
   __shared__ float tile[32][33];
-  const int r0 = blockIdx.x * 32, k0 = blockIdx.y * 32;  // k: chunk column 0..127
+  __shared__ float tileT[32][kChunkCols + 1];
+  const int r0 = blockIdx.x * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int kk = ty; kk < 32; kk += 8) {
-    const int k = k0 + kk, r = r0 + tx;
-    float v = 0.f;
-    const int64_t row = k < Kb * 8 ? (int64_t)(order[c0 + k / 8] * 8 + (k & 7)) : -1;
-    if (row >= 0 && r < R) v = Vs[row * ldv + r];
-    tile[kk][tx] = v;
-    if (VsJ && r < R) VsJ[(int64_t)k * R + r] = v;
-    if (sp.hiJ && row >= 0 && r < R) {
-      sp.hiJ[(int64_t)k * sp.ldJ + r] = sp.hi[row * sp.ld + r];
-      sp.loJ[(int64_t)k * sp.ldJ + r] = sp.lo[row * sp.ld + r];
-      if (r == 0) sp.invJ[k] = sp.inv[row];
+  for (int k0 = blockIdx.y * 32; k0 < kChunkCols; k0 += gridDim.y * 32) {
+    for (int kk = ty; kk < 32; kk += 8) {
+      const int k = k0 + kk, r = r0 + tx;
+      float v = 0.f;
+      const int64_t row = k < Kb * 8 ? (int64_t)(order[c0 + k / 8] * 8 + (k & 7)) : -1;
+      if (row >= 0 && r < R) v = Vs[row * ldv + r];
+      tile[kk][tx] = v;
+      if (VsJ && r < R) VsJ[(int64_t)k * R + r] = v;
+      if (sp.hiJ && row >= 0 && r < R) {
+        sp.hiJ[(int64_t)k * sp.ldJ + r] = sp.hi[row * sp.ld + r];
+        sp.loJ[(int64_t)k * sp.ldJ + r] = sp.lo[row * sp.ld + r];
+        if (r == 0) sp.invJ[k] = sp.inv[row];
+      }
+    }
+    __syncthreads();
+    for (int rr = ty; rr < 32; rr += 8) {
+      const int r = r0 + rr, k = k0 + tx;
+      if (r < R) VsJT[(int64_t)r * kChunkCols + k] = tile[tx][rr];
+      if (sp.hiT) tileT[rr][k] = tile[tx][rr];
+    }
+    __syncthreads();
+    if (blockIdx.x == 0) {
+      for (int i = threadIdx.x; i < 32 * kChunkCols; i += blockDim.x) {
+        const int k = k0 + i / kChunkCols, l = i % kChunkCols;
+        float v = 0.f;
+        if (k < Kb * 8 && l < Kb * 8)
+          v = Hf[(int64_t)(order[c0 + k / 8] * 8 + (k & 7)) * ldh + order[c0 + l / 8] * 8 + (l & 7)];
+        Hsub[k * kChunkCols + l] = v;
+      }
     }
   }
-  __syncthreads();
-  for (int rr = ty; rr < 32; rr += 8) {
-    const int r = r0 + rr, k = k0 + tx;
-    if (r < R) VsJT[(int64_t)r * kChunkCols + k] = tile[tx][rr];
-  }
-  if (blockIdx.x == 0) {
-    for (int i = threadIdx.x; i < 32 * kChunkCols; i += blockDim.x) {
-      const int k = k0 + i / kChunkCols, l = i % kChunkCols;
-      float v = 0.f;
-      if (k < Kb * 8 && l < Kb * 8)
-        v = Hf[(int64_t)(order[c0 + k / 8] * 8 + (k & 7)) * ldh + order[c0 + l / 8] * 8 + (l & 7)];
-      Hsub[k * kChunkCols + l] = v;
+  if (sp.hiT) {
+    for (int rr = ty; rr < 32; rr += 8) {  // one warp per row of VsJT
+      const int r = r0 + rr;
+      if (r >= R) continue;
+      float mx = 0.f;
+      for (int k = tx; k < Kb * 8; k += 32) mx = fmaxf(mx, fabsf(tileT[rr][k]));
+      #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sc, inv;
+      split_f16_scale(mx, sc, inv);
+      for (int k = tx; k < Kb * 8; k += 32)
+        split_f16_store(tileT[rr][k], sc, sp.hiT + (int64_t)r * sp.ldT + k, sp.loT + (int64_t)r * sp.ldT + k);
+      if (tx == 0) sp.invT[r] = inv;
     }
   }
 }
@@ -429,6 +454,11 @@ struct GramChunkArgs {
   int B; float accept_tol;
   // top-k candidate mode: per (row, block) kc codewords (values B x nb x kc x 8, indices B x nb x kc)
   const float* cand; const int* cand_idx; int kc; int nb;
+  // rhs_splits > 0: rhs holds the split-K partial planes of the rhs product (plane s at rhs + s * rhs_plane,
+  // leading dimension ldr), added in plane order as the split-K reduction adds them
+  int rhs_splits; int64_t rhs_plane;
+  // optional: the row-scaled fp16 split of delta[:, :8 Kb] (as mpq_split_f16), for the residual update product
+  unsigned short* dhi; unsigned short* dlo; int64_t ldd; float* dinv;
 };
 
 // Top-k candidate choice of one block (mpq/polish/block_cd.py:137-172 _topk_gram_step_impl): metric distance
@@ -528,7 +558,15 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
   const int b = blockIdx.x * 8 + warp;
   if (b >= a.B) return;
   float* rh = s_rhs + warp * kChunkCols;
-  for (int i = lane; i < kChunkCols; i += 32) rh[i] = i < a.Kb * 8 ? a.rhs[b * a.ldr + i] : 0.f;
+  for (int i = lane; i < kChunkCols; i += 32) {
+    float v = 0.f;
+    if (i < a.Kb * 8) {
+      const int64_t o = (int64_t)b * a.ldr + i;
+      v = a.rhs[o];
+      for (int sp = 1; sp < a.rhs_splits; ++sp) v += a.rhs[sp * a.rhs_plane + o];
+    }
+    rh[i] = v;
+  }
   __syncwarp();
   E8Small e8{s_abs, s_par, a.grid, a.sign_id};
   float res = a.res[b];
@@ -631,6 +669,19 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
     __syncwarp();
   }
   for (int i = a.Kb * 8 + lane; i < kChunkCols; i += 32) a.delta[(int64_t)b * kChunkCols + i] = 0.f;
+  if (a.dhi) {
+    __syncwarp();  // the warp's delta stores above are visible to its lanes
+    const float* dr = a.delta + (int64_t)b * kChunkCols;
+    float mx = 0.f;
+    for (int i = lane; i < a.Kb * 8; i += 32) mx = fmaxf(mx, fabsf(dr[i]));
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sc, inv;
+    split_f16_scale(mx, sc, inv);
+    for (int i = lane; i < a.Kb * 8; i += 32)
+      split_f16_store(dr[i], sc, a.dhi + (int64_t)b * a.ldd + i, a.dlo + (int64_t)b * a.ldd + i);
+    if (lane == 0) a.dinv[b] = inv;
+  }
   if (lane == 0) {
     a.res[b] = res;
     if (acc_n) atomicAdd(a.accepted, acc_n);
@@ -690,18 +741,22 @@ MPQ_API int mpq_gram_gather(const float* Vs, int64_t ldv, int R, const float* Hf
 
 // mpq_gram_gather with the chunk's rows of Vs taken from Vs's row-scaled fp16 split (vs_hi / vs_lo, leading
 // dimension ld16, vs_inv) into j_hi / j_lo (ldj16) / j_inv instead of fp32 VsJ: the product with them needs no
-// split of its own.
+// split of its own.  With t_hi (optional; t_lo, ldt16 >= 8 Kb, t_inv) the split of VsJT[:, :8 Kb] is written
+// too, equal to mpq_split_f16 of that matrix.
 MPQ_API int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order,
                                   int c0, int Kb, const void* vs_hi, const void* vs_lo, int64_t ld16,
                                   const float* vs_inv, void* j_hi, void* j_lo, int64_t ldj16, float* j_inv,
-                                  float* VsJT, float* Hsub, void* stream) {
+                                  float* VsJT, float* Hsub, void* t_hi, void* t_lo, int64_t ldt16, float* t_inv,
+                                  void* stream) {
   MPQ_CHECK_ARG(Vs && Hf && order && vs_hi && vs_lo && vs_inv && j_hi && j_lo && j_inv && VsJT && Hsub,
                 "mpq_gram_gather_split: null pointer");
   MPQ_CHECK_ARG(Kb >= 1 && Kb <= kChunkBlocks, "mpq_gram_gather_split: Kb must be in [1, %d]", kChunkBlocks);
   MPQ_CHECK_ARG(ld16 >= R && ldj16 >= R, "mpq_gram_gather_split: fp16 leading dimensions below R");
-  dim3 grid((R + 31) / 32, kChunkCols / 32);
+  MPQ_CHECK_ARG(!t_hi || (t_lo && t_inv && ldt16 >= 8 * Kb), "mpq_gram_gather_split: bad VsJT split buffers");
+  dim3 grid((R + 31) / 32, t_hi ? 1 : kChunkCols / 32);
   SplitRows sp{static_cast<const unsigned short*>(vs_hi), static_cast<const unsigned short*>(vs_lo), ld16, vs_inv,
-               static_cast<unsigned short*>(j_hi), static_cast<unsigned short*>(j_lo), ldj16, j_inv};
+               static_cast<unsigned short*>(j_hi), static_cast<unsigned short*>(j_lo), ldj16, j_inv,
+               static_cast<unsigned short*>(t_hi), static_cast<unsigned short*>(t_lo), ldt16, t_inv};
   k_gram_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, nullptr, VsJT, Hsub, sp);
   return launch_status("mpq_gram_gather_split");
 }
@@ -725,6 +780,36 @@ MPQ_API int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr,
   }
   k_gram_chunk<false><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
   return launch_status("mpq_gram_chunk");
+}
+
+// mpq_gram_chunk reading the rhs product as `splits` split-K partial planes (plane s at rhs + s * plane, leading
+// dimension ldr, added in plane order as the split-K reduction adds them) and writing the row-scaled fp16 split of
+// delta[:, :8 Kb] (d_hi / d_lo, leading dimension ldd >= 8 Kb, multiple of 8; d_inv), equal to mpq_split_f16 of it:
+// the chunk's two products then need neither a reduction nor a split launch of their own.
+MPQ_API int mpq_gram_chunk_planes(float* x, int64_t ldx, const float* rhs, int64_t ldr, int splits, int64_t plane,
+                                  const float* Hsub, const float* meta, const int* order, int c0, int Kb,
+                                  const float* base_abs, const int* base_parity, const float* grid,
+                                  const uint8_t* sign_id, float* res, int* idx, int64_t ldi, float* delta, void* d_hi,
+                                  void* d_lo, int64_t ldd, float* d_inv, int* accepted, long long* evals, int B,
+                                  float accept_tol, void* stream) {
+  MPQ_CHECK_ARG(Kb >= 1 && Kb <= kChunkBlocks, "mpq_gram_chunk_planes: Kb must be in [1, %d]", kChunkBlocks);
+  MPQ_CHECK_ARG(splits >= 1 && ldr >= 8 * Kb && plane >= (int64_t)B * ldr, "mpq_gram_chunk_planes: bad plane layout");
+  if (B == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(x && rhs && Hsub && meta && order && base_abs && base_parity && grid && sign_id && res && idx && delta &&
+                    accepted && d_hi && d_lo && d_inv,
+                "mpq_gram_chunk_planes: null pointer");
+  MPQ_CHECK_ARG(ldd >= 8 * Kb, "mpq_gram_chunk_planes: ldd below 8 Kb");
+  MPQ_CHECK_ARG(((uintptr_t)grid & 15) == 0, "mpq_gram_chunk_planes: grid must be 16-byte aligned");
+  GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, base_abs, base_parity, grid, sign_id, res, idx, ldi,
+                  delta, accepted, evals, B, accept_tol, nullptr, nullptr, 0, 0, splits, plane,
+                  static_cast<unsigned short*>(d_hi), static_cast<unsigned short*>(d_lo), ldd, d_inv};
+  const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
+  {
+    const int ast = smem_opt_in((const void*)k_gram_chunk<false>, smem, "mpq_gram_chunk_planes");
+    if (ast) return ast;
+  }
+  k_gram_chunk<false><<<(B + 7) / 8, 256, smem, (cudaStream_t)stream>>>(a);
+  return launch_status("mpq_gram_chunk_planes");
 }
 
 MPQ_API int mpq_gram_chunk_topk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* Hsub,

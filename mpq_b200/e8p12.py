@@ -241,6 +241,22 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
         hiJ = torch.empty(128, vs16[0].shape[1], device=dev, dtype=torch.float16)
         loJ = torch.empty_like(hiJ)
         invJ = torch.empty(128, device=dev, dtype=torch.float32)
+        # Per chunk: the gather writes the split of VsJT and the chunk kernel the split of delta and sums the rhs
+        # product's split-K planes, so the chunk's two products take their operands as they are (the same splits
+        # and sums that mm_nt's split and reduction launches would produce, bit for bit).
+        hiT = torch.empty(R, 128, device=dev, dtype=torch.float16)
+        loT = torch.empty_like(hiT)
+        invT = torch.empty(R, device=dev, dtype=torch.float32)
+        dhi = torch.empty(B, 128, device=dev, dtype=torch.float16)
+        dlo = torch.empty_like(dhi)
+        dinv = torch.empty(B, device=dev, dtype=torch.float32)
+        ld16 = (R + 7) // 8 * 8
+        rhi = torch.empty(B, ld16, device=dev, dtype=torch.float16)
+        rlo = torch.empty_like(rhi)
+        rinv = torch.empty(B, device=dev, dtype=torch.float32)
+        rsplits = ops.splitk_for(B, 128, R, ops.num_sms(dev)) if B else 1
+        planes = torch.empty(max(rsplits, 1) * B * 128, device=dev, dtype=torch.float32)
+        st_word = ops.status_word(dev)
     Hsub = torch.empty(128, 128, device=dev, dtype=torch.float32)
     rhsJ = torch.empty(B, 128, device=dev, dtype=torch.float32)
     delta = torch.empty(B, 128, device=dev, dtype=torch.float32)
@@ -266,10 +282,26 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
         for c0 in range(0, nb, 16):
             Kb = min(16, nb - c0)
             kc = 8 * Kb
+            if vs16 is not None and not n_cand:
+                call("mpq_gram_gather_split", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb,
+                     ptr(vs16[0]), ptr(vs16[1]), vs16[0].stride(0), ptr(vs16[2]), ptr(hiJ), ptr(loJ), hiJ.stride(0),
+                     ptr(invJ), ptr(VsJT), ptr(Hsub), ptr(hiT), ptr(loT), hiT.stride(0), ptr(invT))
+                ops.split_f16(res_u, (rhi, rlo, rinv))
+                spl = min(ops.splitk_for(B, kc, R, ops.num_sms(dev)), rsplits) if B else 1
+                call("mpq_gemm_f16x3_parts", B, kc, R, ptr(rhi), ptr(rlo), rhi.stride(0), ptr(rinv), ptr(hiJ),
+                     ptr(loJ), hiJ.stride(0), ptr(invJ), spl, ptr(planes), planes.numel(), ptr(st_word))
+                call("mpq_gram_chunk_planes", ptr(x_work), x_work.stride(0), ptr(planes), kc, spl, B * kc,
+                     ptr(Hsub), ptr(meta), ptr(order), c0, Kb, ptr(t["base_abs"]), ptr(t["base_parity"]),
+                     ptr(t["grid"]), ptr(t["sign_id"]), ptr(res_norm), ptr(idx), idx.stride(0), ptr(delta), ptr(dhi),
+                     ptr(dlo), dhi.stride(0), ptr(dinv), ptr(accepted), ptr(evals), B, float(accept_tol))
+                ops.mm_nt(ops.Operand.presplit(delta[:, :kc], (dhi[:, :kc], dlo[:, :kc], dinv)),
+                          ops.Operand.presplit(VsJT[:, :kc], (hiT[:, :kc], loT[:, :kc], invT)),
+                          out=res_u, alpha=-1.0, beta=1.0)
+                continue
             if vs16 is not None:
                 call("mpq_gram_gather_split", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb,
                      ptr(vs16[0]), ptr(vs16[1]), vs16[0].stride(0), ptr(vs16[2]), ptr(hiJ), ptr(loJ), hiJ.stride(0),
-                     ptr(invJ), ptr(VsJT), ptr(Hsub))
+                     ptr(invJ), ptr(VsJT), ptr(Hsub), None, None, 0, None)
                 ops.mm_nt(res_u, ops.Operand.presplit(VsJ[:kc], (hiJ[:kc], loJ[:kc], invJ[:kc])), out=rhsJ[:, :kc])
             else:
                 call("mpq_gram_gather", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb, ptr(VsJ),

@@ -289,7 +289,12 @@ def splitk_for(M: int, N: int, K: int, sms: int) -> int:
 
 def mm_nt(A: torch.Tensor, B, out: Optional[torch.Tensor] = None, *, alpha: float = 1.0, beta: float = 0.0,
           precision: Optional[str] = None) -> torch.Tensor:
-    """C = alpha * A @ B^T + beta * C on the tensor cores.  B: Operand or (N x K) tensor."""
+    """C = alpha * A @ B^T + beta * C on the tensor cores.  B: Operand or (N x K) tensor; A: (M x K) tensor, or an
+    Operand whose f16x3 split is already made (Operand.presplit)."""
+    A_split = None
+    if isinstance(A, Operand):
+        A_split = A.f16
+        A = A.full
     if not isinstance(B, Operand):
         B = Operand(B, precision)
     prec = precision or B.precision
@@ -301,8 +306,8 @@ def mm_nt(A: torch.Tensor, B, out: Optional[torch.Tensor] = None, *, alpha: floa
         out = torch.empty(M, N, device=A.device, dtype=torch.float32)
     if prec == "f16x3" and B.f16 is None:
         B = Operand(B.full, "f16x3")
-    if prec == "f16x3" and A.dtype == torch.float32 and A.stride(-1) == 1:
-        Ah, Al, Ai = _scratch_split16(A)
+    if prec == "f16x3" and A.dtype == torch.float32 and (A_split is not None or A.stride(-1) == 1):
+        Ah, Al, Ai = A_split if A_split is not None else _scratch_split16(A)
         Bh, Bl, Bi = B.f16
         st = status_word(A.device)
         splits = splitk_for(M, N, K, num_sms(A.device)) if M and N else 1
