@@ -229,14 +229,13 @@ __global__ void __launch_bounds__(256) k_gram_gather(const float* __restrict__ V
       if (sp.hiT) tileT[rr][k] = tile[tx][rr];
     }
     __syncthreads();
-    if (blockIdx.x == 0) {
-      for (int i = threadIdx.x; i < 32 * kChunkCols; i += blockDim.x) {
-        const int k = k0 + i / kChunkCols, l = i % kChunkCols;
-        float v = 0.f;
-        if (k < Kb * 8 && l < Kb * 8)
-          v = Hf[(int64_t)(order[c0 + k / 8] * 8 + (k & 7)) * ldh + order[c0 + l / 8] * 8 + (l & 7)];
-        Hsub[k * kChunkCols + l] = v;
-      }
+    // Hsub rows k0 .. k0 + 31 spread over the CTAs of the grid's first row (one row of 128 entries per warp step)
+    for (int i = blockIdx.x * 256 + threadIdx.x; i < 32 * kChunkCols; i += gridDim.x * 256) {
+      const int k = k0 + i / kChunkCols, l = i % kChunkCols;
+      float v = 0.f;
+      if (k < Kb * 8 && l < Kb * 8)
+        v = Hf[(int64_t)(order[c0 + k / 8] * 8 + (k & 7)) * ldh + order[c0 + l / 8] * 8 + (l & 7)];
+      Hsub[k * kChunkCols + l] = v;
     }
   }
   if (sp.hiT) {
