@@ -365,7 +365,7 @@ int mpq_gram_gather(const float* Vs, int64_t ldv, int R, const float* Hf, int64_
  * dimension ld16, vs_inv = 1 / row scale) into j_hi / j_lo / j_inv: the split of a row depends on that row alone,
  * so the product with the gathered split equals the product with the split of the gathered rows.  With t_hi
  * (optional; t_lo, leading dimension ldt16 >= 8 Kb, t_inv) it also writes the split of VsJT[:, :8 Kb], equal to
- * mpq_split_f16 of that matrix. */
+ * mpq_split_f16 of that matrix, and VsJT itself only when it is not NULL. */
 int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order, int c0,
                           int Kb, const void* vs_hi, const void* vs_lo, int64_t ld16, const float* vs_inv,
                           void* j_hi, void* j_lo, int64_t ldj16, float* j_inv, float* VsJT, float* Hsub,

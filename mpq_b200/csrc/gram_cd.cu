@@ -434,6 +434,77 @@ __device__ int gram_search_warp(const E8Small& e8, const float t[8], const float
   return best_c;
 }
 
+// The fused path's gather (mpq_gram_gather_split with the split of VsJT requested): CTA x copies the fp16 split
+// row k = x of the chunk (16-byte vectors), transposes and splits rows r = 32 x .. 32 x + 31 of VsJT[:, :8 Kb]
+// (128 chunk columns held in shared memory; VsJT itself is written only when asked for), and gathers its share of
+// Hsub.  The same values as k_gram_gather, with fewer and wider memory operations.
+__global__ void __launch_bounds__(256) k_gram_gather_fused(const float* __restrict__ Vs, int64_t ldv, int R,
+                                                           const float* __restrict__ Hf, int64_t ldh,
+                                                           const int* __restrict__ order, int c0, int Kb,
+                                                           float* __restrict__ VsJT, float* __restrict__ Hsub,
+                                                           SplitRows sp) {
+  __shared__ float tileT[32][kChunkCols + 1];
+  __shared__ int s_row[kChunkCols];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int kc = Kb * 8;
+  for (int k = threadIdx.x; k < kChunkCols; k += blockDim.x) s_row[k] = k < kc ? order[c0 + k / 8] * 8 + (k & 7) : -1;
+  __syncthreads();
+  // (1) split rows of the chunk: row k = blockIdx.x, blockIdx.x + gridDim.x, ... (R halves = R / 8 vectors)
+  if ((R & 7) == 0 && ((sp.ld | sp.ldJ) & 7) == 0) {
+    for (int k = blockIdx.x; k < kc; k += gridDim.x) {
+      const int64_t row = s_row[k];
+      const int4* shi = reinterpret_cast<const int4*>(sp.hi + row * sp.ld);
+      const int4* slo = reinterpret_cast<const int4*>(sp.lo + row * sp.ld);
+      int4* dhi = reinterpret_cast<int4*>(sp.hiJ + (int64_t)k * sp.ldJ);
+      int4* dlo = reinterpret_cast<int4*>(sp.loJ + (int64_t)k * sp.ldJ);
+      for (int v = threadIdx.x; v < R / 8; v += blockDim.x) {
+        dhi[v] = shi[v];
+        dlo[v] = slo[v];
+      }
+      if (threadIdx.x == 0) sp.invJ[k] = sp.inv[row];
+    }
+  } else {
+    for (int k = blockIdx.x; k < kc; k += gridDim.x) {
+      const int64_t row = s_row[k];
+      for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        sp.hiJ[(int64_t)k * sp.ldJ + r] = sp.hi[row * sp.ld + r];
+        sp.loJ[(int64_t)k * sp.ldJ + r] = sp.lo[row * sp.ld + r];
+      }
+      if (threadIdx.x == 0) sp.invJ[k] = sp.inv[row];
+    }
+  }
+  // (2) rows r0 .. r0 + 31 of VsJT (warp ty reads chunk columns k = ty, ty + 8, ...; lane = r)
+  for (int r0 = blockIdx.x * 32; r0 < R; r0 += gridDim.x * 32) {
+    const int r = r0 + tx;
+    for (int k = ty; k < kChunkCols; k += 8) {
+      const int64_t row = s_row[k];
+      tileT[tx][k] = (row >= 0 && r < R) ? Vs[row * ldv + r] : 0.f;
+    }
+    __syncthreads();
+    for (int rr = ty; rr < 32; rr += 8) {  // one warp per row of VsJT
+      const int rw = r0 + rr;
+      if (rw >= R) continue;
+      float mx = 0.f;
+      for (int k = tx; k < kc; k += 32) mx = fmaxf(mx, fabsf(tileT[rr][k]));
+      #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sc, inv;
+      split_f16_scale(mx, sc, inv);
+      for (int k = tx; k < kc; k += 32)
+        split_f16_store(tileT[rr][k], sc, sp.hiT + (int64_t)rw * sp.ldT + k, sp.loT + (int64_t)rw * sp.ldT + k);
+      if (tx == 0) sp.invT[rw] = inv;
+      if (VsJT)
+        for (int k = tx; k < kChunkCols; k += 32) VsJT[(int64_t)rw * kChunkCols + k] = tileT[rr][k];
+    }
+    __syncthreads();
+  }
+  // (3) Hsub (128 x 128), spread over the grid
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kChunkCols * kChunkCols; i += gridDim.x * blockDim.x) {
+    const int k = i / kChunkCols, l = i % kChunkCols;
+    Hsub[i] = (k < kc && l < kc) ? Hf[(int64_t)s_row[k] * ldh + s_row[l]] : 0.f;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // chunk of greedy block decisions (one warp per row)
 // ---------------------------------------------------------------------------------------------
@@ -747,7 +818,7 @@ MPQ_API int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const flo
                                   const float* vs_inv, void* j_hi, void* j_lo, int64_t ldj16, float* j_inv,
                                   float* VsJT, float* Hsub, void* t_hi, void* t_lo, int64_t ldt16, float* t_inv,
                                   void* stream) {
-  MPQ_CHECK_ARG(Vs && Hf && order && vs_hi && vs_lo && vs_inv && j_hi && j_lo && j_inv && VsJT && Hsub,
+  MPQ_CHECK_ARG(Vs && Hf && order && vs_hi && vs_lo && vs_inv && j_hi && j_lo && j_inv && (VsJT || t_hi) && Hsub,
                 "mpq_gram_gather_split: null pointer");
   MPQ_CHECK_ARG(Kb >= 1 && Kb <= kChunkBlocks, "mpq_gram_gather_split: Kb must be in [1, %d]", kChunkBlocks);
   MPQ_CHECK_ARG(ld16 >= R && ldj16 >= R, "mpq_gram_gather_split: fp16 leading dimensions below R");
@@ -756,7 +827,12 @@ MPQ_API int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const flo
   SplitRows sp{static_cast<const unsigned short*>(vs_hi), static_cast<const unsigned short*>(vs_lo), ld16, vs_inv,
                static_cast<unsigned short*>(j_hi), static_cast<unsigned short*>(j_lo), ldj16, j_inv,
                static_cast<unsigned short*>(t_hi), static_cast<unsigned short*>(t_lo), ldt16, t_inv};
-  k_gram_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, nullptr, VsJT, Hsub, sp);
+  if (t_hi) {
+    const int nblk = (R + 31) / 32 > 8 * Kb ? (R + 31) / 32 : 8 * Kb;
+    k_gram_gather_fused<<<nblk, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, VsJT, Hsub, sp);
+  } else {
+    k_gram_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, nullptr, VsJT, Hsub, sp);
+  }
   return launch_status("mpq_gram_gather_split");
 }
 

@@ -285,7 +285,7 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
             if vs16 is not None and not n_cand:
                 call("mpq_gram_gather_split", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb,
                      ptr(vs16[0]), ptr(vs16[1]), vs16[0].stride(0), ptr(vs16[2]), ptr(hiJ), ptr(loJ), hiJ.stride(0),
-                     ptr(invJ), ptr(VsJT), ptr(Hsub), ptr(hiT), ptr(loT), hiT.stride(0), ptr(invT))
+                     ptr(invJ), None, ptr(Hsub), ptr(hiT), ptr(loT), hiT.stride(0), ptr(invT))
                 ops.split_f16(res_u, (rhi, rlo, rinv))
                 spl = min(ops.splitk_for(B, kc, R, ops.num_sms(dev)), rsplits) if B else 1
                 call("mpq_gemm_f16x3_parts", B, kc, R, ptr(rhi), ptr(rlo), rhi.stride(0), ptr(rinv), ptr(hiJ),
