@@ -981,12 +981,18 @@ MPQ_API int mpq_gemm_f16x3_parts(int M, int N, int K, const void* a_hi, const vo
   memset(&maps, 0, sizeof(maps));
   const void* As[3] = {a_hi, a_hi, a_lo};
   const void* Bs[3] = {b_hi, b_lo, b_hi};
+  // N <= 128 (a polish chunk's 128 columns): 128-wide tiles, so no MMA or B load is spent on padding (every output
+  // element's k-order, and so its value, is the same as with 256-wide tiles)
+  const int bn = N <= 128 ? 128 : 256;
   for (int r = 0; r < 3; ++r) {
     st = tc::make_map(&maps.a[r], As[r], M, K, lda, tc::BM, 2);
     if (st) return st;
-    st = tc::make_map(&maps.b[r], Bs[r], N, K, ldb, 256, 2);
+    st = tc::make_map(&maps.b[r], Bs[r], N, K, ldb, bn, 2);
     if (st) return st;
   }
+  if (bn == 128)
+    return tc::launch_pt<128, 4, 2>(maps, 3, M, N, K, 1.f, 0.f, ws, N, status, (cudaStream_t)stream, 0, sa, sb, splits,
+                                    splits > 1 ? ws : nullptr, false);
   return tc::launch_pt<256, 4, 2>(maps, 3, M, N, K, 1.f, 0.f, ws, N, status, (cudaStream_t)stream, 0, sa, sb, splits,
                                   splits > 1 ? ws : nullptr, false);
 }

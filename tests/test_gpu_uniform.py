@@ -204,6 +204,38 @@ def test_gemm_splitk_matches_single_pass(cuda_dev, M, N, K):
     assert torch.equal(outs[1], outs[2])  # fixed reduction order
 
 
+@pytest.mark.parametrize("N", [128, 100, 40])
+def test_gemm_parts_narrow_tiles_match_splitk(cuda_dev, N):
+    """Split-K partial planes of a narrow product (N <= 128 runs on 128-wide tiles) added in plane order equal the
+    split-K product's own reduction (256-wide tiles) bit for bit: the tile width does not change any element."""
+    from mpq_b200 import ops
+    from mpq_b200._lib import call, ptr
+    M, K, splits = 128, 4096, 24
+    g = torch.Generator(device="cpu").manual_seed(N)
+    A = torch.randn(M, K, generator=g).to(cuda_dev)
+    Bt = (torch.randn(N, K, generator=g) * torch.exp(torch.randn(N, 1, generator=g))).to(cuda_dev)
+    Ah, Al, Ai = ops.split_f16(A)
+    Bh, Bl, Bi = ops.Operand(Bt, "f16x3").f16
+    st = ops.status_word(cuda_dev)
+    C = torch.zeros(M, N, device=cuda_dev)
+    ws = torch.empty(splits * M * N, device=cuda_dev)
+    call("mpq_gemm_f16x3_splitk", M, N, K, 1.0, ptr(Ah), ptr(Al), Ah.stride(0), ptr(Ai), ptr(Bh), ptr(Bl),
+         Bh.stride(0), ptr(Bi), 0.0, ptr(C), C.stride(0), splits, ptr(ws), ws.numel(), ptr(st))
+    planes = torch.empty(splits * M * N, device=cuda_dev)
+    call("mpq_gemm_f16x3_parts", M, N, K, ptr(Ah), ptr(Al), Ah.stride(0), ptr(Ai), ptr(Bh), ptr(Bl), Bh.stride(0),
+         ptr(Bi), splits, ptr(planes), planes.numel(), ptr(st))
+    torch.cuda.synchronize()
+    ops.check_status(cuda_dev)
+    P = planes.view(splits, M, N)
+    acc = P[0].clone()
+    for s_ in range(1, splits):
+        acc = acc + P[s_]
+    assert torch.equal(acc, C)
+    ref = A.double() @ Bt.double().T
+    scale = (A.double().abs() @ Bt.double().abs().T).max().item()
+    assert (C.double() - ref).abs().max().item() <= 1e-5 * scale
+
+
 def test_gemm_f16x3_wide_dynamic_range(cuda_dev):
     """f16x3 on rows whose entries span 2^20 (log-uniform magnitudes, as Vs rows under log-normal channel scales
     and small eigenvalues): every entry within 1e-5 of its own |A||B|^T scale plus the split's absolute floor
