@@ -370,6 +370,15 @@ int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const float* Hf, 
                           int Kb, const void* vs_hi, const void* vs_lo, int64_t ld16, const float* vs_inv,
                           void* j_hi, void* j_lo, int64_t ldj16, float* j_inv, float* VsJT, float* Hsub,
                           void* t_hi, void* t_lo, int64_t ldt16, float* t_inv, void* stream);
+/* Every chunk of one sweep in one launch: the block order is fixed for the sweep (mpq/polish/block_cd.py:286-306,
+ * sorted once per sweep) and the gathered operands depend only on Vs, Hf and that order.  Chunk c = 0 .. ceil(nb/16)-1
+ * receives what mpq_gram_gather_split with t_hi writes for c0 = 16 c, in chunk-major slices: j_hi / j_lo + 128 c ldj16,
+ * j_inv + 128 c, Hsub + 16384 c, t_hi / t_lo + R c ldt16 (ldt16 >= 128), t_inv + R c.  Replaces the per-chunk
+ * gathers of the greedy block loop, mpq/polish/block_cd.py:534-547. */
+int mpq_gram_gather_sweep(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order, int nb,
+                          const void* vs_hi, const void* vs_lo, int64_t ld16, const float* vs_inv, void* j_hi,
+                          void* j_lo, int64_t ldj16, float* j_inv, float* Hsub, void* t_hi, void* t_lo, int64_t ldt16,
+                          float* t_inv, void* stream);
 /* Sequential block decisions of one chunk per row: target = x + rhs Ginv, exact first-minimum gram search,
  * accept test, x / idx / residual-norm updates, accepted steps delta (B x 128).  Replaces the block loop of
  * mpq/polish/block_cd.py:534-547 with _cd_gram_step_impl :212-246. */

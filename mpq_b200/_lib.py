@@ -41,6 +41,7 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_gram_gain": (P, L, I, I, P, P, P),
     "mpq_gram_gather": (P, L, I, P, L, P, I, I, P, P, P, P),
     "mpq_gram_gather_split": (P, L, I, P, L, P, I, I, P, P, L, P, P, P, L, P, P, P, P, P, L, P, P),
+    "mpq_gram_gather_sweep": (P, L, I, P, L, P, I, P, P, L, P, P, P, L, P, P, P, P, L, P, P),
     "mpq_gram_chunk_planes": (P, L, P, L, I, L, P, P, P, I, I, P, P, P, P, P, P, L, P, P, P, L, P, P, P, I, F, P),
     "mpq_gram_chunk": (P, L, P, L, P, P, P, I, I, P, P, P, P, P, P, L, P, P, P, I, F, P),
     "mpq_gram_search": (P, I, P, F, F, P, P, P, P, P, P),

@@ -1016,6 +1016,43 @@ __global__ void k_split_f16(const float* __restrict__ x, int64_t ldx, int rows, 
                     reinterpret_cast<unsigned short*>(lo + (int64_t)warp * ldo + c));
   if (lane == 0) inv_scale[warp] = inv;
 }
+
+// The same split with one CTA per row, 16-byte loads and 8-byte stores of four halves (rows whose length, leading
+// dimensions and base addresses allow it): a few hundred rows fill the GPU instead of a few dozen warps.  The row
+// maximum is order independent, so every output equals k_split_f16's.
+__global__ void __launch_bounds__(256) k_split_f16_v4(const float* __restrict__ x, int64_t ldx, int cols,
+                                                      __half* __restrict__ hi, __half* __restrict__ lo, int64_t ldo,
+                                                      float* __restrict__ inv_scale) {
+  __shared__ float red[8];
+  const int row = blockIdx.x, nv = cols >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)row * ldx);
+  float mx = 0.f;
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+    const float4 q = xr[v];
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
+  }
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+  #pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  float s, inv;
+  split_f16_scale(mx, s, inv);
+  uint2* hr = reinterpret_cast<uint2*>(hi + (int64_t)row * ldo);
+  uint2* lr = reinterpret_cast<uint2*>(lo + (int64_t)row * ldo);
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+    const float4 q = xr[v];
+    const float e[4] = {q.x, q.y, q.z, q.w};
+    unsigned short h[4], l[4];
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) split_f16_store(e[i], s, &h[i], &l[i]);
+    hr[v] = make_uint2(h[0] | ((unsigned)h[1] << 16), h[2] | ((unsigned)h[3] << 16));
+    lr[v] = make_uint2(l[0] | ((unsigned)l[1] << 16), l[2] | ((unsigned)l[3] << 16));
+  }
+  if (threadIdx.x == 0) inv_scale[row] = inv;
+}
 }  // namespace mpq
 
 MPQ_API int mpq_split_f16(const float* x, int64_t ldx, int rows, int cols, void* hi, void* lo, int64_t ldo,
@@ -1023,6 +1060,12 @@ MPQ_API int mpq_split_f16(const float* x, int64_t ldx, int rows, int cols, void*
   MPQ_CHECK_ARG(rows >= 0 && cols >= 0 && ldo >= cols && ldx >= cols, "mpq_split_f16: bad shape");
   if (rows == 0 || cols == 0) return MPQ_OK;
   MPQ_CHECK_ARG(x && hi && lo && inv_scale, "mpq_split_f16: null pointer");
+  const bool v4 = (cols & 3) == 0 && (ldx & 3) == 0 && (ldo & 3) == 0 && ((uintptr_t)x & 15) == 0 &&
+                  ((uintptr_t)hi & 7) == 0 && ((uintptr_t)lo & 7) == 0;
+  if (v4) {
+    k_split_f16_v4<<<rows, 256, 0, (cudaStream_t)stream>>>(x, ldx, cols, (__half*)hi, (__half*)lo, ldo, inv_scale);
+    return launch_status("mpq_split_f16");
+  }
   const int warps_per_block = 8;
   k_split_f16<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, (cudaStream_t)stream>>>(
       x, ldx, rows, cols, (__half*)hi, (__half*)lo, ldo, inv_scale);

@@ -23,6 +23,11 @@ namespace mpq {
 
 constexpr int kChunkBlocks = 16;
 constexpr int kChunkCols = kChunkBlocks * 8;
+// The chunk kernel reads only the strict upper block triangle of Hsub (rows of block p, columns of the later blocks):
+// block row p is kept as 8 rows of width 128 - 8 (p + 1), starting at hs_tri_off(p).
+constexpr int kHsTri = 8 * 8 * (kChunkBlocks * (kChunkBlocks - 1) / 2);
+__host__ __device__ constexpr int hs_tri_off(int p) { return 960 * p - 32 * p * (p - 1); }
+static_assert(hs_tri_off(kChunkBlocks) == kHsTri, "triangle layout");
 
 // ---------------------------------------------------------------------------------------------
 // per-block metadata
@@ -438,14 +443,29 @@ __device__ int gram_search_warp(const E8Small& e8, const float t[8], const float
 // row k = x of the chunk (16-byte vectors), transposes and splits rows r = 32 x .. 32 x + 31 of VsJT[:, :8 Kb]
 // (128 chunk columns held in shared memory; VsJT itself is written only when asked for), and gathers its share of
 // Hsub.  The same values as k_gram_gather, with fewer and wider memory operations.
+// Sweep mode (nb_sweep > 0): CTA row y gathers chunk y of the sweep (blocks order[16 y ..], Kb = min(16, nb - 16 y))
+// into its own slice of each output (chunk-major: 128 rows of hiJ / loJ / invJ, R rows of hiT / loT / invT, one
+// 128 x 128 Hsub), with exactly the per-chunk launch's arithmetic.
 __global__ void __launch_bounds__(256) k_gram_gather_fused(const float* __restrict__ Vs, int64_t ldv, int R,
                                                            const float* __restrict__ Hf, int64_t ldh,
                                                            const int* __restrict__ order, int c0, int Kb,
                                                            float* __restrict__ VsJT, float* __restrict__ Hsub,
-                                                           SplitRows sp) {
+                                                           SplitRows sp, int nb_sweep) {
   __shared__ float tileT[32][kChunkCols + 1];
   __shared__ int s_row[kChunkCols];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  if (nb_sweep > 0) {
+    const int ch = blockIdx.y;
+    c0 = ch * kChunkBlocks;
+    Kb = min(kChunkBlocks, nb_sweep - c0);
+    sp.hiJ += (int64_t)ch * kChunkCols * sp.ldJ;
+    sp.loJ += (int64_t)ch * kChunkCols * sp.ldJ;
+    sp.invJ += (int64_t)ch * kChunkCols;
+    sp.hiT += (int64_t)ch * R * sp.ldT;
+    sp.loT += (int64_t)ch * R * sp.ldT;
+    sp.invT += (int64_t)ch * R;
+    Hsub += (int64_t)ch * kChunkCols * kChunkCols;
+  }
   const int kc = Kb * 8;
   for (int k = threadIdx.x; k < kChunkCols; k += blockDim.x) s_row[k] = k < kc ? order[c0 + k / 8] * 8 + (k & 7) : -1;
   __syncthreads();
@@ -611,12 +631,15 @@ __device__ __forceinline__ int topk_pick_reg(const float t[8], const float* L, f
 template <bool TOPK>
 __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
   extern __shared__ float sm[];
-  float* Hs = sm;                                    // 128 x 128
-  float* s_abs = Hs + kChunkCols * kChunkCols;       // 256 x 8
+  float* Hs = sm;                                    // strict upper block triangle of the 128 x 128 Hsub
+  float* s_abs = Hs + kHsTri;                        // 256 x 8
   int* s_par = reinterpret_cast<int*>(s_abs + 2048); // 256
   float* s_meta = reinterpret_cast<float*>(s_par + 256);  // 16 x kMeta
   float* s_rhs = s_meta + kChunkBlocks * kMeta;      // 8 warps x 128
-  for (int i = threadIdx.x; i < kChunkCols * kChunkCols; i += blockDim.x) Hs[i] = a.Hsub[i];
+  for (int i = threadIdx.x; i < kChunkCols * kChunkCols; i += blockDim.x) {
+    const int k = i / kChunkCols, l = i % kChunkCols, p = k >> 3, c0 = (p + 1) * 8;
+    if (l >= c0) Hs[hs_tri_off(p) + (k & 7) * (kChunkCols - c0) + (l - c0)] = a.Hsub[i];
+  }
   if constexpr (!TOPK) {
     for (int i = threadIdx.x; i < 2048; i += blockDim.x) s_abs[i] = a.base_abs[i];
     for (int i = threadIdx.x; i < 256; i += blockDim.x) s_par[i] = a.base_parity[i];
@@ -726,11 +749,13 @@ __global__ void __launch_bounds__(256) k_gram_chunk(GramChunkArgs a) {
       if (lane < 8) a.x[b * a.ldx + blk * 8 + lane] = __ldg(gv + lane);
       if (lane == 0) a.idx[b * a.ldi + blk] = c;
       // later blocks of the chunk see this step: rhs_q -= d @ Hsub[p-block, q-block]
+      const int cb = (p + 1) * 8, wp = kChunkCols - cb;
+      const float* hp = Hs + hs_tri_off(p);  // hp[i * wp + col - cb] = Hsub[p * 8 + i][col] for col >= cb
       for (int col = lane; col < a.Kb * 8; col += 32) {
-        if (col >= (p + 1) * 8) {
+        if (col >= cb) {
           float s = 0.f;
           #pragma unroll
-          for (int i = 0; i < 8; ++i) s = fadd(s, fmul(d[i], Hs[(p * 8 + i) * kChunkCols + col]));
+          for (int i = 0; i < 8; ++i) s = fadd(s, fmul(d[i], hp[i * wp + (col - cb)]));
           rh[col] = fsub(rh[col], s);
         }
       }
@@ -829,11 +854,37 @@ MPQ_API int mpq_gram_gather_split(const float* Vs, int64_t ldv, int R, const flo
                static_cast<unsigned short*>(t_hi), static_cast<unsigned short*>(t_lo), ldt16, t_inv};
   if (t_hi) {
     const int nblk = (R + 31) / 32 > 8 * Kb ? (R + 31) / 32 : 8 * Kb;
-    k_gram_gather_fused<<<nblk, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, VsJT, Hsub, sp);
+    k_gram_gather_fused<<<nblk, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, VsJT, Hsub, sp,
+                                                                0);
   } else {
     k_gram_gather<<<grid, 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, c0, Kb, nullptr, VsJT, Hsub, sp);
   }
   return launch_status("mpq_gram_gather_split");
+}
+
+// Every chunk of one sweep gathered in one launch (the block order is fixed for the whole sweep, and the gathered
+// values depend only on Vs, Hf and the order): chunk c = 0 .. ceil(nb / 16) - 1 gets what mpq_gram_gather_split
+// with t_hi would write for c0 = 16 c, at j_hi / j_lo + 128 c ldj16, j_inv + 128 c, Hsub + 16384 c,
+// t_hi / t_lo + R c ldt16 (ldt16 >= 128) and t_inv + R c.
+MPQ_API int mpq_gram_gather_sweep(const float* Vs, int64_t ldv, int R, const float* Hf, int64_t ldh, const int* order,
+                                  int nb, const void* vs_hi, const void* vs_lo, int64_t ld16, const float* vs_inv,
+                                  void* j_hi, void* j_lo, int64_t ldj16, float* j_inv, float* Hsub, void* t_hi,
+                                  void* t_lo, int64_t ldt16, float* t_inv, void* stream) {
+  MPQ_CHECK_ARG(R >= 0 && nb >= 0, "mpq_gram_gather_sweep: negative size");
+  if (R == 0 || nb == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(Vs && Hf && order && vs_hi && vs_lo && vs_inv && j_hi && j_lo && j_inv && Hsub && t_hi && t_lo && t_inv,
+                "mpq_gram_gather_sweep: null pointer");
+  MPQ_CHECK_ARG(ld16 >= R && ldj16 >= R, "mpq_gram_gather_sweep: fp16 leading dimensions below R");
+  MPQ_CHECK_ARG(ldt16 >= kChunkCols, "mpq_gram_gather_sweep: ldt16 must be at least %d", kChunkCols);
+  const int nchunks = (nb + kChunkBlocks - 1) / kChunkBlocks;
+  MPQ_CHECK_ARG(nchunks <= 65535, "mpq_gram_gather_sweep: too many chunks");
+  SplitRows sp{static_cast<const unsigned short*>(vs_hi), static_cast<const unsigned short*>(vs_lo), ld16, vs_inv,
+               static_cast<unsigned short*>(j_hi), static_cast<unsigned short*>(j_lo), ldj16, j_inv,
+               static_cast<unsigned short*>(t_hi), static_cast<unsigned short*>(t_lo), ldt16, t_inv};
+  const int nblk = (R + 31) / 32 > kChunkCols ? (R + 31) / 32 : kChunkCols;
+  k_gram_gather_fused<<<dim3(nblk, nchunks), 256, 0, (cudaStream_t)stream>>>(Vs, ldv, R, Hf, ldh, order, 0,
+                                                                             kChunkBlocks, nullptr, Hsub, sp, nb);
+  return launch_status("mpq_gram_gather_sweep");
 }
 
 MPQ_API int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr, const float* Hsub, const float* meta,
@@ -848,7 +899,7 @@ MPQ_API int mpq_gram_chunk(float* x, int64_t ldx, const float* rhs, int64_t ldr,
   if (B == 0) return MPQ_OK;
   GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, base_abs, base_parity, grid, sign_id, res, idx, ldi,
                   delta, accepted, evals, B, accept_tol, nullptr, nullptr, 0, 0};
-  const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
+  const size_t smem = (size_t)(kHsTri + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
   {
     const int ast = smem_opt_in((const void*)k_gram_chunk<false>, smem, "mpq_gram_chunk");
     if (ast) return ast;
@@ -878,7 +929,7 @@ MPQ_API int mpq_gram_chunk_planes(float* x, int64_t ldx, const float* rhs, int64
   GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, base_abs, base_parity, grid, sign_id, res, idx, ldi,
                   delta, accepted, evals, B, accept_tol, nullptr, nullptr, 0, 0, splits, plane,
                   static_cast<unsigned short*>(d_hi), static_cast<unsigned short*>(d_lo), ldd, d_inv};
-  const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
+  const size_t smem = (size_t)(kHsTri + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
   {
     const int ast = smem_opt_in((const void*)k_gram_chunk<false>, smem, "mpq_gram_chunk_planes");
     if (ast) return ast;
@@ -899,7 +950,7 @@ MPQ_API int mpq_gram_chunk_topk(float* x, int64_t ldx, const float* rhs, int64_t
   MPQ_CHECK_ARG(((uintptr_t)cand & 15) == 0, "mpq_gram_chunk_topk: candidates must be 16-byte aligned");
   GramChunkArgs a{x, ldx, rhs, ldr, Hsub, meta, order, c0, Kb, nullptr, nullptr, nullptr, nullptr, res, idx, ldi,
                   delta, accepted, evals, B, accept_tol, cand, cand_idx, kc, nb};
-  const size_t smem = (size_t)(kChunkCols * kChunkCols + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
+  const size_t smem = (size_t)(kHsTri + 2048 + 256 + kChunkBlocks * kMeta + 8 * kChunkCols) * 4;
   {
     const int ast = smem_opt_in((const void*)k_gram_chunk<true>, smem, "mpq_gram_chunk_topk");
     if (ast) return ast;

@@ -237,6 +237,7 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
     VsJT = torch.empty(R, 128, device=dev, dtype=torch.float32)
     # the chunk's rows of Vs come pre-split from the layer's split of Vs (no split per chunk)
     vs16 = opVs.f16 if (opVs is not None and opVs.f16 is not None and ops.gemm_precision() == "f16x3") else None
+    topk_vals_given = topk_vals is not None
     if vs16 is not None:
         hiJ = torch.empty(128, vs16[0].shape[1], device=dev, dtype=torch.float16)
         loJ = torch.empty_like(hiJ)
@@ -244,9 +245,6 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
         # Per chunk: the gather writes the split of VsJT and the chunk kernel the split of delta and sums the rhs
         # product's split-K planes, so the chunk's two products take their operands as they are (the same splits
         # and sums that mm_nt's split and reduction launches would produce, bit for bit).
-        hiT = torch.empty(R, 128, device=dev, dtype=torch.float16)
-        loT = torch.empty_like(hiT)
-        invT = torch.empty(R, device=dev, dtype=torch.float32)
         dhi = torch.empty(B, 128, device=dev, dtype=torch.float16)
         dlo = torch.empty_like(dhi)
         dinv = torch.empty(B, device=dev, dtype=torch.float32)
@@ -257,6 +255,18 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
         rsplits = ops.splitk_for(B, 128, R, ops.num_sms(dev)) if B else 1
         planes = torch.empty(max(rsplits, 1) * B * 128, device=dev, dtype=torch.float32)
         st_word = ops.status_word(dev)
+        if not topk_vals_given:
+            # The block order is fixed for a whole sweep, so one launch per sweep gathers every chunk's operands
+            # (chunk-major slices of these buffers: Vs rows' split, VsJT's split, Hsub) instead of one small
+            # launch per chunk.
+            nch = (nb + 15) // 16
+            hiJa = torch.empty(nch, 128, hiJ.shape[1], device=dev, dtype=torch.float16)
+            loJa = torch.empty_like(hiJa)
+            invJa = torch.empty(nch, 128, device=dev, dtype=torch.float32)
+            hiTa = torch.empty(nch, R, 128, device=dev, dtype=torch.float16)
+            loTa = torch.empty_like(hiTa)
+            invTa = torch.empty(nch, R, device=dev, dtype=torch.float32)
+            Hsuba = torch.empty(nch, 128, 128, device=dev, dtype=torch.float32)
     Hsub = torch.empty(128, 128, device=dev, dtype=torch.float32)
     rhsJ = torch.empty(B, 128, device=dev, dtype=torch.float32)
     delta = torch.empty(B, 128, device=dev, dtype=torch.float32)
@@ -279,23 +289,27 @@ def gram_block_cd(*, x: torch.Tensor, Y_u: torch.Tensor, Vs: torch.Tensor, cb, s
         call("mpq_gram_gain", ptr(rhs_all), rhs_all.stride(0), B, nb, ptr(meta), ptr(gain))
         del rhs_all
         call("mpq_argsort_desc", ptr(gain), nb, ptr(order))
+        fused = vs16 is not None and not n_cand
+        if fused:
+            call("mpq_gram_gather_sweep", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), nb,
+                 ptr(vs16[0]), ptr(vs16[1]), vs16[0].stride(0), ptr(vs16[2]), ptr(hiJa), ptr(loJa), hiJa.stride(1),
+                 ptr(invJa), ptr(Hsuba), ptr(hiTa), ptr(loTa), hiTa.stride(1), ptr(invTa))
         for c0 in range(0, nb, 16):
             Kb = min(16, nb - c0)
             kc = 8 * Kb
-            if vs16 is not None and not n_cand:
-                call("mpq_gram_gather_split", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb,
-                     ptr(vs16[0]), ptr(vs16[1]), vs16[0].stride(0), ptr(vs16[2]), ptr(hiJ), ptr(loJ), hiJ.stride(0),
-                     ptr(invJ), None, ptr(Hsub), ptr(hiT), ptr(loT), hiT.stride(0), ptr(invT))
+            if fused:
+                ci = c0 // 16
+                hJ, lJ, iJ, hT, lT, iT = hiJa[ci], loJa[ci], invJa[ci], hiTa[ci], loTa[ci], invTa[ci]
                 ops.split_f16(res_u, (rhi, rlo, rinv))
                 spl = min(ops.splitk_for(B, kc, R, ops.num_sms(dev)), rsplits) if B else 1
-                call("mpq_gemm_f16x3_parts", B, kc, R, ptr(rhi), ptr(rlo), rhi.stride(0), ptr(rinv), ptr(hiJ),
-                     ptr(loJ), hiJ.stride(0), ptr(invJ), spl, ptr(planes), planes.numel(), ptr(st_word))
+                call("mpq_gemm_f16x3_parts", B, kc, R, ptr(rhi), ptr(rlo), rhi.stride(0), ptr(rinv), ptr(hJ),
+                     ptr(lJ), hJ.stride(0), ptr(iJ), spl, ptr(planes), planes.numel(), ptr(st_word))
                 call("mpq_gram_chunk_planes", ptr(x_work), x_work.stride(0), ptr(planes), kc, spl, B * kc,
-                     ptr(Hsub), ptr(meta), ptr(order), c0, Kb, ptr(t["base_abs"]), ptr(t["base_parity"]),
+                     ptr(Hsuba[ci]), ptr(meta), ptr(order), c0, Kb, ptr(t["base_abs"]), ptr(t["base_parity"]),
                      ptr(t["grid"]), ptr(t["sign_id"]), ptr(res_norm), ptr(idx), idx.stride(0), ptr(delta), ptr(dhi),
                      ptr(dlo), dhi.stride(0), ptr(dinv), ptr(accepted), ptr(evals), B, float(accept_tol))
                 ops.mm_nt(ops.Operand.presplit(delta[:, :kc], (dhi[:, :kc], dlo[:, :kc], dinv)),
-                          ops.Operand.presplit(VsJT[:, :kc], (hiT[:, :kc], loT[:, :kc], invT)),
+                          ops.Operand.presplit(VsJT[:, :kc], (hT[:, :kc], lT[:, :kc], iT)),
                           out=res_u, alpha=-1.0, beta=1.0)
                 continue
             if vs16 is not None:

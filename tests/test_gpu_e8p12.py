@@ -179,6 +179,52 @@ def test_gram_block_cd_matches_oracle(cuda_dev, ocb, pcb):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("n,R", [(392, 256), (136, 100)])
+def test_gram_gather_sweep_equals_per_chunk_gathers(cuda_dev, n, R):
+    """One launch per sweep (mpq_gram_gather_sweep) writes, for every chunk, bit for bit what the per-chunk gather
+    (mpq_gram_gather_split with the VsJT split) writes: ragged last chunk (nb = 49, 17), R with and without the
+    16-byte vector path (256, 100)."""
+    from mpq_b200 import ops
+    from mpq_b200._lib import call, ptr
+    g = torch.Generator(device="cpu").manual_seed(n + R)
+    nb = n // 8
+    # rows with a wide dynamic range, as Vs under log-normal channel scales
+    Vs = (torch.randn(n, R, generator=g) * torch.exp(2.0 * torch.randn(n, 1, generator=g))).to(cuda_dev)
+    Hf = torch.randn(n, n, generator=g).to(cuda_dev)
+    order = torch.randperm(nb, generator=g).to(torch.int32).to(cuda_dev)
+    hi, lo, inv = ops.split_f16(Vs)
+    nch = (nb + 15) // 16
+    hiJa = torch.full((nch, 128, hi.shape[1]), 7.0, device=cuda_dev, dtype=torch.float16)
+    loJa, invJa = torch.full_like(hiJa, 7.0), torch.full((nch, 128), 7.0, device=cuda_dev)
+    hiTa = torch.full((nch, R, 128), 7.0, device=cuda_dev, dtype=torch.float16)
+    loTa, invTa = torch.full_like(hiTa, 7.0), torch.full((nch, R), 7.0, device=cuda_dev)
+    Hsuba = torch.full((nch, 128, 128), 7.0, device=cuda_dev)
+    call("mpq_gram_gather_sweep", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), nb, ptr(hi), ptr(lo),
+         hi.stride(0), ptr(inv), ptr(hiJa), ptr(loJa), hiJa.stride(1), ptr(invJa), ptr(Hsuba), ptr(hiTa), ptr(loTa),
+         hiTa.stride(1), ptr(invTa))
+    for ci, c0 in enumerate(range(0, nb, 16)):
+        Kb = min(16, nb - c0)
+        kc = 8 * Kb
+        hiJ = torch.zeros(128, hi.shape[1], device=cuda_dev, dtype=torch.float16)
+        loJ, invJ = torch.zeros_like(hiJ), torch.zeros(128, device=cuda_dev)
+        hiT = torch.zeros(R, 128, device=cuda_dev, dtype=torch.float16)
+        loT, invT = torch.zeros_like(hiT), torch.zeros(R, device=cuda_dev)
+        Hsub = torch.zeros(128, 128, device=cuda_dev)
+        call("mpq_gram_gather_split", ptr(Vs), Vs.stride(0), R, ptr(Hf), Hf.stride(0), ptr(order), c0, Kb, ptr(hi),
+             ptr(lo), hi.stride(0), ptr(inv), ptr(hiJ), ptr(loJ), hiJ.stride(0), ptr(invJ), None, ptr(Hsub), ptr(hiT),
+             ptr(loT), hiT.stride(0), ptr(invT))
+        torch.cuda.synchronize()
+        for got, want in ((hiJa[ci, :kc, :R], hiJ[:kc, :R]), (loJa[ci, :kc, :R], loJ[:kc, :R]), (hiTa[ci][:, :kc], hiT[:, :kc]),
+                          (loTa[ci][:, :kc], loT[:, :kc])):
+            assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (ci, kc)
+        assert torch.equal(invJa[ci, :kc], invJ[:kc]) and torch.equal(invTa[ci], invT), ci
+        assert torch.equal(Hsuba[ci], Hsub), ci
+        # the gathered rows are the order's blocks of Vs
+        rows = (order[c0:c0 + Kb].long()[:, None] * 8 + torch.arange(8, device=cuda_dev)).reshape(-1)
+        assert torch.equal(hiJa[ci, :kc, :R], hi[rows, :R])
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("m,n,iters", [(32, 256, 16), (16, 128, 8)])
 def test_solve_e8p12_matches_oracle(cuda_dev, ocb, pcb, m, n, iters):
     from mpq_b200 import solver as PS

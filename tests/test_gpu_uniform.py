@@ -236,6 +236,29 @@ def test_gemm_parts_narrow_tiles_match_splitk(cuda_dev, N):
     assert (C.double() - ref).abs().max().item() <= 1e-5 * scale
 
 
+@pytest.mark.parametrize("rows,cols,ldx", [(128, 4096, 4096), (37, 100, 104), (5, 98, 98), (300, 4100, 4100)])
+def test_split_f16_bits_match_definition(cuda_dev, rows, cols, ldx):
+    """mpq_split_f16 (16-byte path for rows of 4k floats at 4k-aligned strides, the warp-per-row path otherwise) bit
+    for bit against its definition: s = 2^(15 - e) with max|row| < 2^e, hi = fp16_rn(x s), lo = fp16_rn(x s - hi),
+    inverse scale 2^(e - 15); zero rows and rows spanning 2^±6 magnitudes included."""
+    from mpq_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(rows + cols)
+    base = torch.randn(rows, ldx, generator=g) * torch.exp(3.0 * torch.randn(rows, 1, generator=g))
+    base[0] = 0.0
+    x = base.to(cuda_dev)[:, :cols]
+    hi, lo, inv = ops.split_f16(x)
+    torch.cuda.synchronize()
+    mx = x.abs().amax(1)
+    e = torch.where(mx > 0, torch.frexp(mx).exponent, torch.zeros_like(mx, dtype=torch.int32))
+    one = torch.ones_like(mx)
+    y = x * torch.ldexp(one, 15 - e)[:, None]
+    h = y.half()
+    lo_want = (y - h.float()).half()
+    assert torch.equal(hi[:, :cols].view(torch.int16), h.view(torch.int16))
+    assert torch.equal(lo[:, :cols].view(torch.int16), lo_want.view(torch.int16))
+    assert torch.equal(inv, torch.ldexp(one, e - 15))
+
+
 def test_gemm_f16x3_wide_dynamic_range(cuda_dev):
     """f16x3 on rows whose entries span 2^20 (log-uniform magnitudes, as Vs rows under log-normal channel scales
     and small eigenvalues): every entry within 1e-5 of its own |A||B|^T scale plus the split's absolute floor
