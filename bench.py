@@ -324,6 +324,12 @@ class E8Workload:
                        "wscale": P["wscale"], "changed_fraction": st["mechanism"]["cleanup_changed_fraction"],
                        "block_rows": st["block_rows"], "chain_host_s": dict(chain.last_timing)}
 
+    def settle(self):
+        """Wait for the set-ups queued so far to complete (their results stay queued for their steps)."""
+        if self.pipe is not None:
+            for j in self.pipe.keys():
+                self.pipe.wait(j)
+
     def finish(self, k):
         """Wait for the set-ups still queued (their work belongs to the steps that queued them) and drop them;
         returns the next step index (dropped steps' indices are not reused)."""
@@ -461,6 +467,10 @@ def run_mpq(args):
     if hasattr(wl, "queue"):
         for j in range(world):  # as in the timed region: each step's set-up queued N steps ahead
             wl.queue(k + j, W_host, H_host)
+        # The set-ups queued here belong to the steps before the region (as the warm-up's do for the device-timed
+        # region): they complete before the clock starts, and every timed step carries the one it queues for a
+        # later step (finished inside the region by finish()).
+        wl.settle()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()

@@ -81,6 +81,11 @@ class SetupPipeline:
                 t.record_stream(cur)
         return out
 
+    def wait(self, key: Hashable) -> None:
+        """Block until the set-up has run and its device work has completed; its result stays queued for get()."""
+        _, ev = self._pending[key].result()
+        ev.synchronize()
+
     def drain(self) -> None:
         """Wait for every queued set-up; the caller's stream then waits for their device work.  Results are
         dropped."""

@@ -102,3 +102,19 @@ def test_quip_walk_pipelined_matches_serial(cuda_dev):
         assert torch.equal(g0[key]["Qidxs"], g1[key]["Qidxs"]), key
     for name in w0:
         assert torch.equal(w0[name], w1[name]), name
+
+
+def test_wait_completes_a_setup_and_keeps_it_queued(cuda_dev):
+    """wait(key) blocks until the set-up's device work is done; the result stays queued and get() returns it."""
+    from mpq_b200.pipeline import SetupPipeline
+    (W, H, SU, SV), = _layers(cuda_dev, 1)
+    with SetupPipeline(cuda_dev) as pipe:
+        pipe.submit(7, _setup, W, H, SU, SV, eigen=True)
+        pipe.wait(7)
+        assert pipe.pending(7) and pipe.keys() == [7]
+        P = pipe.get(7)
+        assert not pipe.pending(7)
+    want = _setup(W, H, SU, SV, eigen=True)
+    torch.cuda.synchronize()
+    assert torch.equal(P["Wn"], want["Wn"]) and torch.equal(P["Hr"], want["Hr"])
+    assert torch.equal(P["eig"][0], want["eig"][0])
