@@ -317,6 +317,19 @@ int mpq_e8p12_mmse_rows(const float* r1, int64_t ld_r1, const float* center, int
                         const float* base_sqnorm, const int* base_parity, const int* idx_lut, const float* grid,
                         float* x1_out, int64_t ld_x, float* var_rowsum, int chunks, void* work, const int* active,
                         void* stream);
+/* mpq_e8p12_mmse_rows with the retry round's row stage fused behind it: the CTA that completes a row's variance sum
+ * runs that row's alpha1 / gamma2 / alpha2 / gamma1 algebra (mpq/solver.py:559-631, as mpq_vamp_rows_round_ctl with
+ * gamma1_work = gamma and n_var = nb), and the last row to finish takes the retry round's decision
+ * (mpq/solver.py:575-604).  One launch per retry round instead of two; the same arithmetic. */
+int mpq_e8p12_mmse_rows_round_ctl(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c, const float* pscale,
+                                  int64_t ld_s, const float* gamma, float prior_tau, int B, int nb,
+                                  const float* base_abs, const float* base_sqnorm, const int* base_parity,
+                                  const int* idx_lut, const float* grid, float* x1_out, int64_t ld_x, float* var_rowsum,
+                                  int chunks, void* work, const int* active, float* gamma1, float* alpha1, float* eta1,
+                                  float* gamma2_new, float* gamma2, const float* gamma2_prev, float* alpha2, float* eta2,
+                                  float* gamma1_new, float* gamma1_next, float* trace, int* flags, const float* S, int n,
+                                  int R, float damping, int final_retry, void* ctl, float factor, unsigned* counter,
+                                  void* stream);
 /* MAP codeword (bit-exact first maximum); fixed_gamma > 0 with prior_tau <= 0 is the nearest codeword (RTN).
  * Replaces mpq/priors/e8p12.py:541-631 (vamp_vector_map_e8p12, _branch_factorized_map :367-449) and the
  * nearest-codeword cb.quantize of mpq/adapters/quip_sharp.py:212-241. */

@@ -32,6 +32,8 @@ SIGNATURES: Dict[str, Tuple[Any, ...]] = {
     "mpq_block_hadamard": (P, L, P, L, I, I, I, P, I, P),
     "mpq_e8p12_mmse": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, L, P, L, P, L, P, P),
     "mpq_e8p12_mmse_rows": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, I, P, P, P),
+    "mpq_e8p12_mmse_rows_round_ctl": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, L, P, I, P, P,
+                                      P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, F, I, P, F, P, P),
     "mpq_e8p12_map": (P, L, P, L, P, L, P, F, F, I, I, P, P, P, P, P, P, L, P, L, P),
     "mpq_e8p12_stats": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, P, P, P, L, P),
     "mpq_e8p12_topk": (P, L, P, L, P, L, P, F, I, I, P, P, P, P, P, I, P, P, P, P),

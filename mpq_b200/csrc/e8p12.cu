@@ -30,6 +30,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "vamp_rows.cuh"
 
 namespace mpq {
 
@@ -203,11 +204,25 @@ __device__ __forceinline__ bool stage_abs_patterns(const E8Tab& tab, uint2* s_of
   return *s_bad != 0;
 }
 
+// Optional row stage fused behind the posterior (on = 1): the CTA that completes row b's variance sum runs the
+// VAMP row stage of row b (vamp_row_stage, threads 0 .. kRowThreads - 1), so a retry round is one launch instead of
+// a posterior launch and a row-stage launch.
+struct RowsFuse {
+  int on;
+  RowState st;
+  const float* S;
+  int n, n_var, R;
+  float damping;
+  int final_retry;
+  const VampCtl* ctl;
+  RoundCtl rc;
+};
+
 template <bool MMSE>
 __global__ void __launch_bounds__(kWarps * 32, 4)
 k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __restrict__ var_out, int64_t ld_v,
         int* __restrict__ idx_out, int64_t ld_i, float* __restrict__ map_out, int64_t ld_m,
-        float* __restrict__ var_rowsum, RowSplit rs) {
+        float* __restrict__ var_rowsum, RowSplit rs, RowsFuse fz) {
   // s_off[ai]: byte k of the pair = 8 * (3 k + m_k), the offset of coordinate k's float2 entry
   __shared__ uint2 s_off[256];
   __shared__ float s_sqn[256];
@@ -518,11 +533,14 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
     }
   }
   if constexpr (MMSE) {
+    __shared__ int s_last;
+    __shared__ float s_red[2][kRowThreads / 32];
     if (lane == 0) s_var[warp] = vacc;
     __syncthreads();
     if (threadIdx.x == 0 && var_rowsum) {
       float tsum = 0.f;
       for (int w = 0; w < kWarps; ++w) tsum += s_var[w];
+      int last = 1;
       if (gridDim.y == 1) {
         var_rowsum[b] = tsum;
       } else {
@@ -530,7 +548,8 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
         rs.part[(int64_t)b * gridDim.y + blockIdx.y] = tsum;
         __threadfence();
         const unsigned prev = atomicAdd(&rs.counters[b], 1u);
-        if (prev == gridDim.y - 1) {
+        last = prev == gridDim.y - 1;
+        if (last) {
           __threadfence();
           float t = 0.f;
           for (unsigned c = 0; c < gridDim.y; ++c) t += __ldcg(&rs.part[(int64_t)b * gridDim.y + c]);
@@ -538,6 +557,13 @@ k_e8p12(E8Args a, E8Tab tab, float* __restrict__ x1_out, int64_t ld_x, float* __
           rs.counters[b] = 0u;  // ready for the next launch
         }
       }
+      s_last = last;
+    }
+    if (fz.on) {
+      __syncthreads();  // s_last and thread 0's var_rowsum[b] store, for the row stage's threads
+      if (s_last && threadIdx.x < kRowThreads)
+        vamp_row_stage<true>(fz.st, fz.S, b, a.B, fz.n, fz.n_var, fz.R, 0.f, fz.damping, fz.final_retry, fz.ctl,
+                             fz.rc, s_red);
     }
   }
 }
@@ -914,7 +940,7 @@ MPQ_API int mpq_e8p12_mmse(const float* r1, int64_t ld_r1, const float* center, 
   E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
   E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
   k_e8p12<true><<<dim3(B, 1), kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, var_out, ld_v, idx_out, ld_i,
-                                                                      map_out, ld_m, var_rowsum, RowSplit{});
+                                                                      map_out, ld_m, var_rowsum, RowSplit{}, RowsFuse{});
   return launch_status("mpq_e8p12_mmse");
 }
 
@@ -939,8 +965,45 @@ MPQ_API int mpq_e8p12_mmse_rows(const float* r1, int64_t ld_r1, const float* cen
   RowSplit rs{static_cast<float*>(work), work ? reinterpret_cast<unsigned*>(static_cast<float*>(work) + (int64_t)B * chunks)
                                               : nullptr, active};
   k_e8p12<true><<<dim3(B, chunks), kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, nullptr, 0, nullptr, 0,
-                                                                           nullptr, 0, var_rowsum, rs);
+                                                                           nullptr, 0, var_rowsum, rs, RowsFuse{});
   return launch_status("mpq_e8p12_mmse_rows");
+}
+
+// mpq_e8p12_mmse_rows with the retry round's row stage fused behind it (mpq_vamp_rows_round_ctl's arguments after
+// `active`): the CTA that completes a row's variance sum runs that row's stage, and the last row to finish takes the
+// round's decision.  One launch per retry round instead of two, with the same arithmetic.
+MPQ_API int mpq_e8p12_mmse_rows_round_ctl(const float* r1, int64_t ld_r1, const float* center, int64_t ld_c,
+                                          const float* pscale, int64_t ld_s, const float* gamma, float prior_tau, int B,
+                                          int nb, const float* base_abs, const float* base_sqnorm,
+                                          const int* base_parity, const int* idx_lut, const float* grid, float* x1_out,
+                                          int64_t ld_x, float* var_rowsum, int chunks, void* work, const int* active,
+                                          float* gamma1, float* alpha1, float* eta1, float* gamma2_new, float* gamma2,
+                                          const float* gamma2_prev, float* alpha2, float* eta2, float* gamma1_new,
+                                          float* gamma1_next, float* trace, int* flags, const float* S, int n, int R,
+                                          float damping, int final_retry, void* ctl, float factor, unsigned* counter,
+                                          void* stream) {
+  int st = e8_check(r1, B, nb, base_abs, base_sqnorm, base_parity, idx_lut, grid);
+  if (st) return st;
+  if (B == 0 || nb == 0) return MPQ_OK;
+  MPQ_CHECK_ARG(gamma && x1_out && var_rowsum, "mpq_e8p12_mmse_rows_round_ctl: gamma, x1_out and var_rowsum are required");
+  MPQ_CHECK_ARG(chunks >= 1 && chunks <= nb && chunks <= 1024,
+                "mpq_e8p12_mmse_rows_round_ctl: chunks must be in [1, min(nb, 1024)]");
+  MPQ_CHECK_ARG(chunks == 1 || work, "mpq_e8p12_mmse_rows_round_ctl: work buffer required for chunks > 1");
+  MPQ_CHECK_ARG(gamma1 && alpha1 && eta1 && gamma2_new && gamma2 && gamma2_prev && alpha2 && eta2 && gamma1_new &&
+                    gamma1_next && trace && flags && S && ctl && counter,
+                "mpq_e8p12_mmse_rows_round_ctl: null pointer");
+  E8Args a{r1, ld_r1, center, ld_c, pscale, ld_s, gamma, prior_tau, 0.f, B, nb};
+  E8Tab t{base_abs, base_sqnorm, base_parity, idx_lut, grid};
+  RowSplit rs{static_cast<float*>(work), work ? reinterpret_cast<unsigned*>(static_cast<float*>(work) + (int64_t)B * chunks)
+                                              : nullptr, active};
+  // gamma1_work of the row stage is the posterior's own precision vector
+  RowState rst{var_rowsum, gamma1, const_cast<float*>(gamma), alpha1, eta1, gamma2_new, gamma2,
+               damping < 1.f ? gamma2_prev : nullptr, alpha2, eta2, gamma1_new, gamma1_next, trace, flags};
+  RowsFuse fz{1, rst, S, n, nb, R, damping, final_retry, static_cast<const VampCtl*>(ctl),
+              RoundCtl{static_cast<VampCtl*>(ctl), counter, factor, nb}};
+  k_e8p12<true><<<dim3(B, chunks), kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, x1_out, ld_x, nullptr, 0, nullptr, 0,
+                                                                           nullptr, 0, var_rowsum, rs, fz);
+  return launch_status("mpq_e8p12_mmse_rows_round_ctl");
 }
 
 // Posterior diagnostics per item (B x nb outputs with leading dimension ld): log-partition, entropy, margin.
@@ -976,7 +1039,7 @@ MPQ_API int mpq_e8p12_map(const float* r1, int64_t ld_r1, const float* center, i
   // MAP only: no per-row reduction, so rows split freely into chunks of 64 items (enough CTAs for small row counts)
   const int chunks = std::max(1, std::min(nb / 64, (1776 + B - 1) / B));
   k_e8p12<false><<<dim3(B, chunks), kWarps * 32, 0, (cudaStream_t)stream>>>(a, t, nullptr, 0, nullptr, 0, idx_out, ld_i,
-                                                                            map_out, ld_m, nullptr, RowSplit{});
+                                                                            map_out, ld_m, nullptr, RowSplit{}, RowsFuse{});
   return launch_status("mpq_e8p12_map");
 }
 

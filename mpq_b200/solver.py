@@ -840,17 +840,19 @@ def e8_vamp_device(st: E8VampState, ctl: torch.Tensor, L: E8Layer, *, Wr, hat0, 
         for rnd in range(retry_steps + 1):
             final = int(rnd >= retry_steps)
             # retry rounds usually do nothing (the device skips them): only the first round's launch is timed
+            # the posterior with the round's row stage fused behind it (the CTA completing a row's variance sum runs
+            # that row's stage; the last row takes the round's decision)
             tok = trace.begin_timing("e8p12_mmse" if rnd == 0 else "e8p12_mmse_retry")
-            call("mpq_e8p12_mmse_rows", ptr(st.r1), st.r1.stride(0), ptr(center), center.stride(0) if center is not None else 0,
-                 ptr(pscale), pscale.stride(0) if pscale is not None else 0, ptr(rows["g1w"]), tau, B, nb, *tabs,
-                 ptr(st.x1), st.x1.stride(0), ptr(rows["var"]), st.chunks, ptr(st.work), c + 8)
+            call("mpq_e8p12_mmse_rows_round_ctl", ptr(st.r1), st.r1.stride(0), ptr(center),
+                 center.stride(0) if center is not None else 0, ptr(pscale),
+                 pscale.stride(0) if pscale is not None else 0, ptr(rows["g1w"]), tau, B, nb, *tabs, ptr(st.x1),
+                 st.x1.stride(0), ptr(rows["var"]), st.chunks, ptr(st.work), c + 8, ptr(st.gamma1), ptr(rows["a1"]),
+                 ptr(rows["eta1"]), ptr(rows["g2n"]), ptr(rows["g2"]), ptr(rows["g2p"]), ptr(rows["a2"]),
+                 ptr(rows["eta2"]), ptr(rows["g1n"]), ptr(rows["g1next"]), ptr(rows["trace"]), ptr(flags), ptr(L.S), n,
+                 R, damping, final, c, factor, ptr(st.round_counter))
             trace.end_timing("e8p12_mmse" if rnd == 0 else "e8p12_mmse_retry", tok,
                              4.0 * B * n * (3 if center is not None else 2) + 8.0 * B
                              + (4.0 * B * nb if pscale is not None else 0.0))
-            call("mpq_vamp_rows_round_ctl", ptr(rows["var"]), ptr(st.gamma1), ptr(rows["g1w"]), ptr(rows["a1"]),
-                 ptr(rows["eta1"]), ptr(rows["g2n"]), ptr(rows["g2"]), ptr(rows["g2p"]), ptr(rows["a2"]),
-                 ptr(rows["eta2"]), ptr(rows["g1n"]), ptr(rows["g1next"]), ptr(rows["trace"]), ptr(flags), ptr(L.S), B,
-                 n, nb, R, damping, final, c, factor, ptr(st.round_counter))
         # r2 and its fp16 split -> P = r2 V (partial planes) -> linear epilogue (adds the planes, writes u split)
         # -> D = u V^T (partial planes) -> r1 update (adds the planes)
         call("mpq_vamp_r2_split_ctl", ptr(st.x1), ptr(st.r1), ptr(st.r2_prev), ptr(st.r2), ptr(rows["eta1"]),
